@@ -1,0 +1,219 @@
+"""TEST INFRASTRUCTURE — ctypes front-end for the two CPU oracles (see ``oracle/__init__.py``)."""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+from dataclasses import dataclass, field
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REF_SO = os.path.join(HERE, "_ref", "libref_runner.so")
+PORT_SO = os.path.join(HERE, "_build", "libmoe_oracle.so")
+
+# ggml type ids (third_party/llama/ggml/include/ggml.h:390-432)
+F32, F16, Q5_0, Q8_0, Q4_K, Q8_K, IQ4_NL, IQ2_S = 0, 1, 6, 8, 12, 15, 20, 22
+
+
+class _Layer(C.Structure):
+    _fields_ = [
+        ("d_model", C.c_int32), ("n_ff", C.c_int32), ("n_expert", C.c_int32), ("top_k", C.c_int32),
+        ("n_tokens", C.c_int32),
+        ("x", C.c_void_p), ("w_router", C.c_void_p), ("b_router", C.c_void_p),
+        ("n_slots", C.c_int32), ("exp_slot", C.c_void_p), ("slot_exp", C.c_void_p), ("slot_state", C.c_void_p),
+        ("hot_type_gu", C.c_int32), ("hot_type_down", C.c_int32),
+        ("hot_gu", C.c_void_p), ("hot_down", C.c_void_p), ("s_hot", C.c_void_p),
+        ("cold_type_gu", C.c_int32), ("cold_type_down", C.c_int32),
+        ("cold_gu", C.c_void_p), ("cold_down", C.c_void_p), ("s_cold", C.c_void_p),
+        ("n_threads", C.c_int32),
+    ]
+
+
+class _LayerOut(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in ("logits", "probs", "ids", "weights", "gate_up", "act", "down", "out")]
+
+
+def _ptr(a):
+    return None if a is None else a.ctypes.data
+
+
+@dataclass
+class LayerSpec:
+    """Host-side (numpy) description of one MoE layer; mirrors ``oracle_layer``."""
+    d_model: int
+    n_ff: int
+    n_expert: int
+    top_k: int
+    x: np.ndarray                       # f32 [T, d_model]
+    w_router: np.ndarray                # f32 [E, d_model]
+    b_router: np.ndarray | None = None  # f32 [E]
+    n_slots: int = 0
+    exp_slot: np.ndarray | None = None  # i32 [E]
+    slot_exp: np.ndarray | None = None  # i32 [K]
+    slot_state: np.ndarray | None = None  # i32 [K]
+    hot_type_gu: int = Q4_K
+    hot_type_down: int = Q5_0
+    hot_gu: np.ndarray | None = None    # u8 [K, 2*n_ff, row]
+    hot_down: np.ndarray | None = None  # u8 [K, d_model, row]
+    s_hot: np.ndarray | None = None
+    cold_type_gu: int = IQ2_S
+    cold_type_down: int = IQ4_NL
+    cold_gu: np.ndarray | None = None   # u8 [E, 2*n_ff, row]
+    cold_down: np.ndarray | None = None
+    s_cold: np.ndarray | None = None
+    keep: list = field(default_factory=list)
+
+    @property
+    def n_tokens(self) -> int:
+        return int(self.x.shape[0])
+
+    def to_c(self, n_threads: int = 1) -> _Layer:
+        L = _Layer()
+        L.d_model, L.n_ff, L.n_expert, L.top_k = self.d_model, self.n_ff, self.n_expert, self.top_k
+        L.n_tokens = self.n_tokens
+        arrs = dict(
+            x=np.ascontiguousarray(self.x, np.float32),
+            w_router=np.ascontiguousarray(self.w_router, np.float32),
+            b_router=None if self.b_router is None else np.ascontiguousarray(self.b_router, np.float32),
+            exp_slot=None if self.exp_slot is None else np.ascontiguousarray(self.exp_slot, np.int32),
+            slot_exp=None if self.slot_exp is None else np.ascontiguousarray(self.slot_exp, np.int32),
+            slot_state=None if self.slot_state is None else np.ascontiguousarray(self.slot_state, np.int32),
+            hot_gu=None if self.hot_gu is None else np.ascontiguousarray(self.hot_gu),
+            hot_down=None if self.hot_down is None else np.ascontiguousarray(self.hot_down),
+            s_hot=None if self.s_hot is None else np.ascontiguousarray(self.s_hot, np.float32),
+            cold_gu=None if self.cold_gu is None else np.ascontiguousarray(self.cold_gu),
+            cold_down=None if self.cold_down is None else np.ascontiguousarray(self.cold_down),
+            s_cold=None if self.s_cold is None else np.ascontiguousarray(self.s_cold, np.float32),
+        )
+        self.keep = list(arrs.values())
+        for k, v in arrs.items():
+            setattr(L, k, _ptr(v))
+        L.n_slots = self.n_slots
+        L.hot_type_gu, L.hot_type_down = self.hot_type_gu, self.hot_type_down
+        L.cold_type_gu, L.cold_type_down = self.cold_type_gu, self.cold_type_down
+        L.n_threads = n_threads
+        return L
+
+
+class _Oracle:
+    prefix = ""
+
+    def __init__(self, so: str):
+        self.lib = C.CDLL(so)
+        p = self.prefix
+        f = self._fn
+        self._row_size = f(p + "row_size", C.c_size_t, [C.c_int32, C.c_int64])
+        self._deq = f(p + "dequantize_row", None, [C.c_int32, C.c_void_p, C.c_void_p, C.c_int64])
+        self._qact = f(p + "quantize_act", None, [C.c_int32, C.c_void_p, C.c_void_p, C.c_int64])
+        self._vdt = f(p + "vec_dot_type", C.c_int32, [C.c_int32])
+        self._vdot = f(p + "vec_dot", C.c_float, [C.c_int32, C.c_int64, C.c_void_p, C.c_void_p])
+        self._layer = f(p + "moe_layer", C.c_int, [C.POINTER(_Layer), C.POINTER(_LayerOut)])
+
+    def _fn(self, name, res, args):
+        fn = getattr(self.lib, name)
+        fn.restype = res
+        fn.argtypes = args
+        return fn
+
+    def row_size(self, t: int, n: int) -> int:
+        return int(self._row_size(t, n))
+
+    def dequantize(self, t: int, data: np.ndarray, n: int) -> np.ndarray:
+        data = np.ascontiguousarray(data)
+        out = np.empty(n, np.float32)
+        self._deq(t, data.ctypes.data, out.ctypes.data, n)
+        return out
+
+    def vec_dot_type(self, wtype: int) -> int:
+        return int(self._vdt(wtype))
+
+    def quantize_act(self, vdt: int, x: np.ndarray) -> np.ndarray:
+        x = np.ascontiguousarray(x, np.float32)
+        out = np.zeros(self.row_size(vdt, x.size), np.uint8)
+        self._qact(vdt, x.ctypes.data, out.ctypes.data, x.size)
+        return out
+
+    def vec_dot(self, wtype: int, n: int, w_row: np.ndarray, xq: np.ndarray) -> float:
+        return float(self._vdot(wtype, n, np.ascontiguousarray(w_row).ctypes.data,
+                                np.ascontiguousarray(xq).ctypes.data))
+
+    def moe_layer(self, spec: LayerSpec, n_threads: int = 1, want=("logits", "probs", "ids", "weights",
+                                                                     "gate_up", "act", "down")) -> dict:
+        T, E, k, d, nff = spec.n_tokens, spec.n_expert, spec.top_k, spec.d_model, spec.n_ff
+        shapes = dict(logits=((T, E), np.float32), probs=((T, E), np.float32), ids=((T, k), np.int32),
+                      weights=((T, k), np.float32), gate_up=((T * k, 2 * nff), np.float32),
+                      act=((T * k, nff), np.float32), down=((T * k, d), np.float32), out=((T, d), np.float32))
+        res = {n: np.zeros(*shapes[n]) for n in list(want) + ["out"]}
+        o = _LayerOut()
+        for n, a in res.items():
+            setattr(o, n, a.ctypes.data)
+        L = spec.to_c(n_threads)
+        rc = self._layer(C.byref(L), C.byref(o))
+        if rc != 1:
+            raise RuntimeError(f"{type(self).__name__}.moe_layer failed ({rc})")
+        return res
+
+
+class Ref(_Oracle):
+    """The reference's ggml-cpu path, built from the reference sources (oracle/_ref)."""
+    prefix = "ref_"
+
+    def __init__(self):
+        super().__init__(REF_SO)
+        self._quant = self._fn("ref_quantize", C.c_size_t, [C.c_int32, C.c_void_p, C.c_void_p, C.c_int64, C.c_int64])
+        self._gelu = self._fn("ref_gelu_table", C.c_uint16, [C.c_uint16])
+        self.lib.ref_init()
+
+    def quantize(self, t: int, w: np.ndarray) -> np.ndarray:
+        """Reference quantiser ggml_quantize_chunk (ggml.c:7761) over rows of ``w`` (f32 [..., n])."""
+        w = np.ascontiguousarray(w, np.float32)
+        n = w.shape[-1]
+        nrow = w.size // n
+        out = np.zeros(nrow * self.row_size(t, n), np.uint8)
+        self._quant(t, w.ctypes.data, out.ctypes.data, nrow, n)
+        return out.reshape(*w.shape[:-1], self.row_size(t, n))
+
+    def gelu_table(self) -> np.ndarray:
+        return np.array([self._gelu(h) for h in range(1 << 16)], np.uint16)
+
+
+class Port(_Oracle):
+    """This repository's plain-C restatement of the path (oracle/moe_oracle.c)."""
+    prefix = "oracle_"
+
+    def __init__(self):
+        if not os.path.exists(PORT_SO):
+            build_port()
+        super().__init__(PORT_SO)
+        self._topk = self._fn("oracle_topk", None, [C.c_void_p, C.c_int32, C.c_int32, C.c_void_p])
+        self._gelu = self._fn("oracle_gelu_table", C.c_uint16, [C.c_uint16])
+        self._geglu = self._fn("oracle_geglu", None, [C.c_int64, C.c_void_p, C.c_void_p, C.c_void_p])
+
+    def topk(self, v: np.ndarray, k: int) -> np.ndarray:
+        v = np.ascontiguousarray(v, np.float32)
+        out = np.zeros(k, np.int32)
+        self._topk(v.ctypes.data, v.size, k, out.ctypes.data)
+        return out
+
+    def gelu_table(self) -> np.ndarray:
+        return np.array([self._gelu(h) for h in range(1 << 16)], np.uint16)
+
+    def geglu(self, gate: np.ndarray, up: np.ndarray) -> np.ndarray:
+        gate = np.ascontiguousarray(gate, np.float32)
+        up = np.ascontiguousarray(up, np.float32)
+        out = np.empty_like(gate)
+        self._geglu(gate.size, out.ctypes.data, gate.ctypes.data, up.ctypes.data)
+        return out
+
+
+def ref_available() -> bool:
+    return os.path.exists(REF_SO)
+
+
+def port_available() -> bool:
+    return os.path.exists(PORT_SO)
+
+
+def build_port() -> None:
+    subprocess.run(["make", "-s", "-C", HERE, "port"], check=True)
