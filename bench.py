@@ -1,0 +1,320 @@
+"""Benchmark of the B200 MoE-FFN layer (router -> dispatch -> grouped gate_up -> GeGLU -> down ->
+combine) on the configurations of BASELINE.json.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config NAME] [--impl ours|reference]
+
+One JSON line on rank 0. A "step" is one layer forward over the config's tokens. `value` is
+layer-tokens/s summed over ranks, device-timed with CUDA events on the launching stream (inputs
+resident in HBM, L2 flushed between steps with a 256 MiB write that is not timed). `e2e` is the
+same metric through the public API with the step's input copied from pinned host memory and the
+output read back inside the timed region. Decode configs do not shard: at N > 1 every rank runs
+an independent replica (weak scaling). `--impl reference` times the reference's own CPU
+implementation (ggml-cpu built from the reference sources, oracle/_ref) on this host's cores.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+DEFAULT_CONFIG = "decode_t4_mixed"
+METRIC = "moe_layer_tokens_per_s"
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=200)
+    p.add_argument("--warmup", type=int, default=20)
+    p.add_argument("--config", default=DEFAULT_CONFIG)
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--no-graph", action="store_true", help="launch eagerly instead of replaying a CUDA graph")
+    p.add_argument("--cpu-sample-s", type=float, default=15.0, help="CPU baseline budget (seconds)")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def dist_env():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
+
+
+class Clocks:
+    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(2)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, 1590.0, "fallback"
+
+
+def reference_spec(host, x):
+    from oracle import LayerSpec
+    exp_slot, slot_exp, slot_state = host.residency()
+    K = host.n_slots
+    return LayerSpec(host.d_model, host.n_ff, host.n_expert, host.top_k, x=x, w_router=host.w_router,
+                     b_router=host.b_router, n_slots=K, exp_slot=exp_slot if K else None,
+                     slot_exp=slot_exp if K else None, slot_state=slot_state if K else None, hot_gu=host.hot_gu,
+                     hot_down=host.hot_down, s_hot=host.s_hot, cold_gu=host.cold_gu, cold_down=host.cold_down,
+                     s_cold=host.s_cold)
+
+
+def time_reference(host, x, warmup, steps, budget_s, n_threads=None):
+    """The reference CPU path (oracle/_ref: the ggml-cpu MUL_MAT_ID graph of build_moe_ffn) on this
+    host's cores: `warmup` untimed forwards, then up to `steps` timed ones within `budget_s`."""
+    from oracle import Ref, ref_available
+    if not ref_available():
+        return None
+    r = Ref()
+    spec = reference_spec(host, x)
+    nt = n_threads or os.cpu_count() or 1
+    for _ in range(max(1, warmup)):
+        r.moe_layer(spec, n_threads=nt, want=())
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while len(times) < max(1, steps) and (len(times) < 2 or time.perf_counter() < t_end):
+        t0 = time.perf_counter()
+        r.moe_layer(spec, n_threads=nt, want=())
+        times.append(time.perf_counter() - t0)
+    value = x.shape[0] * len(times) / sum(times)
+    return {"value": value, "unit": "tokens/s", "cores": nt, "kind": "reference",
+            "sample": f"{len(times)} layer forwards of {x.shape[0]} tokens each, ggml-cpu O1 graph built from the "
+                      f"reference sources, {nt} threads", "ms_per_forward": 1e3 * sum(times) / len(times)}
+
+
+def run_reference(args):
+    rank, _, world = dist_env()
+    if rank != 0:
+        return 0
+    from llapis_b200 import workload
+    cfg = workload.CONFIGS[args.config]
+    host = workload.build_layer(cfg)
+    x = workload.make_input(cfg)
+    cb = time_reference(host, x, args.warmup, args.steps, budget_s=120.0)
+    if cb is None:
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref (reference ggml-cpu build) missing"}))
+        return 0
+    v = cb["value"]
+    line = {"metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": cb["ms_per_forward"], "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "q8 int dot / f32", "data": "synthetic (seeded)",
+            "config": {"workload": cfg.name, "n_tokens": cfg.n_tokens, "layers": 1},
+            "impl": "reference", "cpu_baseline": cb,
+            "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+    return 0
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch
+    import torch.distributed as dist
+
+    from llapis_b200 import capi, workload
+    from llapis_b200.layer import MoELayer
+
+    rank, local, world = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+
+    cfg = workload.CONFIGS[args.config]
+    host = workload.build_layer(cfg)
+    layer = MoELayer(host, dev)
+    x_host = workload.make_input(cfg)
+    T = x_host.shape[0]
+    x = torch.from_numpy(x_host).to(dev)
+    out = torch.empty_like(x)
+    s = torch.cuda.Stream(dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)   # > 126 MB L2
+
+    # routing of this workload (for the algorithmic byte count)
+    ids = torch.empty((T, host.top_k), dtype=torch.int32, device=dev)
+    with torch.cuda.stream(s):
+        layer(x, out, aux={"ids": ids}, stream=s)
+    s.synchronize()
+    alg_bytes = workload.algorithmic_bytes(host, ids.cpu().numpy(), T)
+    launches_per_step = 4 * ((T + 15) // 16)
+
+    graph = None
+    if not args.no_graph:
+        layer.workspace(T)
+        with torch.cuda.stream(s):
+            for _ in range(3):
+                layer(x, out, stream=s)
+        s.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            layer(x, out, stream=s)
+        s.synchronize()
+
+    def step():
+        if graph is not None:
+            graph.replay()
+        else:
+            layer(x, out, stream=s)
+
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    with torch.cuda.stream(s):
+        for _ in range(args.warmup):
+            flush.zero_()
+            step()
+    s.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with Clocks(local) as clk:
+        # keep the GPU under this load until the sampler has a few readings (untimed)
+        t_load = time.perf_counter()
+        while len(clk.lines) < 3 and time.perf_counter() - t_load < 3.0:
+            with torch.cuda.stream(s):
+                for _ in range(50):
+                    flush.zero_()
+                    step()
+            s.synchronize()
+        with torch.cuda.stream(s):
+            for i in range(args.steps):
+                flush.zero_()
+                ev[i][0].record(s)
+                step()
+                ev[i][1].record(s)
+        s.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+    times_ms = [a.elapsed_time(b) for a, b in ev]
+    dev_ms = float(sum(times_ms))
+
+    # end to end through the public API: pinned host input -> layer -> host output, per step
+    x_pin = torch.from_numpy(x_host).pin_memory()
+    o_pin = torch.empty_like(x_pin).pin_memory()
+    ev2 = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    x_e = torch.empty_like(x)
+    o_e = torch.empty_like(x)
+    with torch.cuda.stream(s):
+        for i in range(args.warmup + args.steps):
+            flush.zero_()
+            if i >= args.warmup:
+                ev2[i - args.warmup][0].record(s)
+            x_e.copy_(x_pin, non_blocking=True)
+            layer(x_e, o_e, stream=s)
+            o_pin.copy_(o_e, non_blocking=True)
+            if i >= args.warmup:
+                ev2[i - args.warmup][1].record(s)
+    s.synchronize()
+    e2e_ms = float(sum(a.elapsed_time(b) for a, b in ev2))
+    err = layer.device_error()
+
+    tot = torch.tensor([dev_ms, e2e_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(tot, op=dist.ReduceOp.MAX)
+    dev_ms, e2e_ms = tot.tolist()
+    tokens = T * args.steps * world
+    value = tokens / (dev_ms / 1e3)
+    e2e = tokens / (e2e_ms / 1e3)
+    hbm, _, peak_kind = measured_peaks()
+    avg_ms = dev_ms / args.steps
+    achieved_gbs = alg_bytes / (avg_ms / 1e3) / 1e9
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = time_reference(host, x_host, 1, 1000, args.cpu_sample_s)
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": avg_ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "q8 int dot / f32",
+            "data": "synthetic (seeded N(0,0.02) weights quantised to ggml formats, N(0,1) activations)",
+            "config": {"workload": cfg.name, "n_tokens": T, "layers": 1, "d_model": cfg.d_model,
+                       "n_expert": cfg.n_expert, "top_k": cfg.top_k, "hot_experts": len(cfg.hot),
+                       "parallelism": f"replicas{world}" if world > 1 else "single",
+                       "l2": "flushed between steps (256 MiB write, not timed)",
+                       "cuda_graph": graph is not None, "unique_experts": int(np.unique(ids.cpu().numpy()).size)},
+            "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": int(x_host.nbytes),
+                    "d2h_bytes_per_step": int(x_host.nbytes)},
+            "gpu_launches": launches_per_step * args.steps,
+            "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": hbm, "unit": "GB/s",
+                         "frac": achieved_gbs / hbm, "traffic": None, "peak_kind": peak_kind,
+                         "scope": "whole layer forward (4 PDL-chained kernels), algorithmic bytes "
+                                  f"{alg_bytes} per step"},
+            "cpu_baseline": cpu,
+            "clocks": clk.summary(),
+            "device_error": err,
+        }
+        print(json.dumps(line))
+    if world > 1:
+        del graph
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

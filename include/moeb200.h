@@ -1,0 +1,135 @@
+/*
+ * moeb200.h — B200-native entry points of the MoE-FFN hot path (libmoeb200.so).
+ *
+ * The Gemma-4 MoE FFN layer as LLapis computes it through GGML_OP_MOE_DUAL / GGML_OP_MUL_MAT_ID
+ * (third_party/llama/src/llama-graph.cpp:1507-1851, gemma4.cpp:409-425):
+ *   router logits (f32) [+ bias] -> softmax -> top-k (value desc, lowest index on ties)
+ *   -> normalised weights -> per-expert dispatch (histogram, exclusive scan, stable permutation)
+ *   -> grouped gate_up with on-the-fly Q4_K / IQ2_S dequantisation (activations as Q8_K)
+ *   -> GeGLU (ggml-cpu fp16-table GELU) -> down projection (Q5_0 / IQ4_NL, activations as Q8_0)
+ *   -> per-expert down scale -> routing-weighted, slot-ordered combine.
+ * Two precision classes live in HBM, selected per routed pair by the moe_dual residency mirror:
+ * a pair is hot iff 0 <= exp_slot[e] < n_slots, slot_state[slot] == 2 and slot_exp[slot] == e
+ * (moert/cuda/ffn_moe.cu:101-104); hot pairs read the hot pool at `slot`, cold pairs the cold
+ * pool at `e`.
+ *
+ * Conventions: device pointers unless stated; ggml layouts (a weight pool is
+ * [slots][rows][row bytes], activations are [tokens][features] f32 rows); `stream` is a
+ * cudaStream_t passed as void*. Every entry returns 0 on success or a negative MOEB_E* code;
+ * moeb_last_error() gives the message. Nothing falls back to the CPU: without a usable sm_100
+ * device every compute entry fails with MOEB_ENODEV.
+ */
+#ifndef MOEB200_H
+#define MOEB200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+    MOEB_OK = 0,
+    MOEB_EINVAL = -1,    /* bad argument or shape                                    */
+    MOEB_ENODEV = -2,    /* no sm_100 device / CUDA unavailable                      */
+    MOEB_ECUDA = -3,     /* a CUDA runtime call failed                               */
+    MOEB_ESPACE = -4,    /* workspace too small                                      */
+    MOEB_EDEVICE = -5,   /* a kernel reported an error (bounded wait gave up, bad id) */
+    MOEB_ETYPE = -6,     /* weight type not supported on this path                   */
+};
+
+/* ggml type ids accepted as weight types (third_party/llama/ggml/include/ggml.h:390-432) */
+enum { MOEB_T_Q5_0 = 6, MOEB_T_Q4_K = 12, MOEB_T_IQ4_NL = 20, MOEB_T_IQ2_S = 22 };
+
+/* One HBM-resident precision class: merged gate_up [n][2*n_ff rows][row(d_model)] and
+ * down [n][d_model rows][row(n_ff)], each in ggml block layout. */
+typedef struct moeb_pool {
+    int32_t     type_gu;     /* MOEB_T_Q4_K or MOEB_T_IQ2_S                  */
+    int32_t     type_down;   /* MOEB_T_Q5_0 or MOEB_T_IQ4_NL                 */
+    int32_t     n;           /* experts (cold pool) or slots (hot pool)      */
+    int32_t     _pad;
+    const void *w_gu;
+    const void *w_down;
+    const float *s_down;     /* f32 [n] down scale (ffn_down_exps_s) or NULL */
+} moeb_pool;
+
+/* One MoE layer (replaces the per-layer tensors build_moe_ffn reads). */
+typedef struct moeb_layer {
+    int32_t        d_model, n_ff, n_expert, top_k;
+    const float   *w_router;   /* f32 [n_expert][d_model] (ffn_gate_inp)                */
+    const float   *b_router;   /* f32 [n_expert] added to the logits, or NULL           */
+    moeb_pool      hot;        /* n = slot count K (may be 0)                           */
+    moeb_pool      cold;       /* n = n_expert (may be 0 when every expert is hot)      */
+    const int32_t *exp_slot;   /* i32 [n_expert] (NULL when hot.n == 0)                 */
+    const int32_t *slot_exp;   /* i32 [K]                                               */
+    const int32_t *slot_state; /* i32 [K], 2 = READY                                    */
+} moeb_layer;
+
+/* Optional per-call outputs for inspection / parity (any pointer may be NULL). */
+typedef struct moeb_layer_aux {
+    float   *logits;     /* f32 [T][n_expert] router logits (+ bias)                          */
+    int32_t *ids;        /* i32 [T][top_k] selected experts, (value desc, index asc)          */
+    float   *weights;    /* f32 [T][top_k] normalised routing weights                         */
+    int32_t *counts;     /* i32 [n_expert] routed pairs per expert (histogram)                */
+    int32_t *offsets;    /* i32 [n_expert + 1] exclusive scan of counts                       */
+    int32_t *perm;       /* i32 [T*top_k] pair indices p = t*top_k + j grouped by expert, stable */
+    float   *gate_up;    /* f32 [T*top_k][2*n_ff] raw gate_up per routed pair                 */
+    float   *down;       /* f32 [T*top_k][d_model] scaled down output per routed pair         */
+} moeb_layer_aux;
+
+/* Library and device setup. moeb_init loads the format tables into the current device (once per
+ * device; also done lazily by the first compute call on a device). */
+int         moeb_init(void);
+const char *moeb_last_error(void);
+const char *moeb_version(void);
+/* Reads and clears the device error word (bit 1: a bounded wait gave up; 2: expert id out of
+ * range; 4: a capacity limit was exceeded). */
+int32_t     moeb_device_error(void *stream);
+
+/* Workspace bytes moeb_layer_forward needs for n_tokens tokens. */
+size_t moeb_layer_workspace_size(const moeb_layer *L, int32_t n_tokens);
+
+/* One whole MoE layer, router to combine (new; the graph-level unit the benchmark measures).
+ * x: f32 [n_tokens][d_model]; out: f32 [n_tokens][d_model]. The workspace must stay untouched
+ * until the stream reaches the end of the call. Kernels are chained with programmatic dependent
+ * launch; the call is stream-ordered and capturable in a CUDA graph. */
+int moeb_layer_forward(const moeb_layer *L, const float *x, int32_t n_tokens, float *out,
+                       const moeb_layer_aux *aux, void *workspace, size_t workspace_bytes, void *stream);
+
+/* Binds the weight pools that moert_ffn_moe(il, kind) reads (the reference trampoline lends its
+ * w_hot / w_cold tensors through the mm vtable instead, moe-dual.cu:74-94). hot/cold: device
+ * pools in ggml layout [n][d_out][row(d_in)] of type hot_type / cold_type. */
+int moeb_bind_pools(int32_t il, int32_t kind, const void *w_hot, int32_t hot_type, int32_t n_hot,
+                    const void *w_cold, int32_t cold_type, int32_t n_cold);
+
+/* Router epilogue alone: softmax / top-k / weights over given logits f32 [T][n_expert]
+ * (the index-parity check feeds the reference's logits through this). */
+int moeb_router_topk(const float *logits, int32_t n_tokens, int32_t n_expert, int32_t top_k,
+                     int32_t *ids, float *weights, void *stream);
+
+/* Dispatch alone: ids i32 [T][top_k] -> counts [n_expert], offsets [n_expert+1], perm [T*top_k]
+ * (histogram, exclusive scan, stable permutation; mmid.cu:28 / ggml-cpu.c:1613-1626). */
+int moeb_dispatch(const int32_t *ids, int32_t n_tokens, int32_t top_k, int32_t n_expert,
+                  int32_t *counts, int32_t *offsets, int32_t *perm, void *stream);
+
+/* Weight dequantisation to f32 rows (bit-exact with ggml's dequantize_row_*). */
+int moeb_dequantize(int32_t type, const void *src, float *dst, int64_t n_rows, int64_t n_per_row, void *stream);
+
+/* Activation quantisation of f32 rows to the vec_dot type of `wtype` (Q8_K for Q4_K/IQ2_S, Q8_0
+ * for Q5_0/IQ4_NL), bit-exact with ggml-cpu on x86. */
+int moeb_quantize_act(int32_t wtype, const float *x, void *dst, int64_t n_rows, int64_t n_per_row, void *stream);
+
+/* ---- host-side weight quantiser (CPU, multi-threaded) ----
+ * Restates ggml_quantize_chunk without an importance matrix (third_party/llama/ggml/src/ggml.c:7761)
+ * for the four expert types; output bytes are identical to the reference quantiser's. src: host
+ * f32 [nrow][n_per_row]; dst: host. n_threads <= 0 uses every online CPU. Returns bytes written,
+ * or 0 on a bad type/shape. */
+size_t moeb_quantize_weights(int32_t type, const float *src, void *dst, int64_t nrow, int64_t n_per_row,
+                             int32_t n_threads);
+size_t moeb_row_size(int32_t type, int64_t n_per_row);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

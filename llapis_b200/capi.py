@@ -1,0 +1,107 @@
+"""ctypes binding of libmoeb200.so (include/moeb200.h, include/moert_cuda.h).
+
+The library is the product: every compute entry runs sm_100a kernels and fails loudly (MoebError)
+when it cannot — there is no CPU fallback anywhere in this package.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+from . import build as _build
+
+# ggml type ids (third_party/llama/ggml/include/ggml.h:390-432)
+Q5_0, Q4_K, IQ4_NL, IQ2_S, Q8_0, Q8_K = 6, 12, 20, 22, 8, 15
+
+ERRORS = {0: "OK", -1: "EINVAL", -2: "ENODEV", -3: "ECUDA", -4: "ESPACE", -5: "EDEVICE", -6: "ETYPE"}
+
+
+class MoebError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"moeb error {ERRORS.get(code, code)}: {msg}")
+        self.code = code
+
+
+class Pool(C.Structure):
+    _fields_ = [("type_gu", C.c_int32), ("type_down", C.c_int32), ("n", C.c_int32), ("_pad", C.c_int32),
+                ("w_gu", C.c_void_p), ("w_down", C.c_void_p), ("s_down", C.c_void_p)]
+
+
+class Layer(C.Structure):
+    _fields_ = [("d_model", C.c_int32), ("n_ff", C.c_int32), ("n_expert", C.c_int32), ("top_k", C.c_int32),
+                ("w_router", C.c_void_p), ("b_router", C.c_void_p), ("hot", Pool), ("cold", Pool),
+                ("exp_slot", C.c_void_p), ("slot_exp", C.c_void_p), ("slot_state", C.c_void_p)]
+
+
+class LayerAux(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in ("logits", "ids", "weights", "counts", "offsets", "perm", "gate_up", "down")]
+
+
+_lib = None
+
+# name -> (restype, argtypes); every symbol include/*.h declares
+SIGNATURES = {
+    "moeb_init": (C.c_int, []),
+    "moeb_last_error": (C.c_char_p, []),
+    "moeb_version": (C.c_char_p, []),
+    "moeb_device_error": (C.c_int32, [C.c_void_p]),
+    "moeb_layer_workspace_size": (C.c_size_t, [C.POINTER(Layer), C.c_int32]),
+    "moeb_layer_forward": (C.c_int, [C.POINTER(Layer), C.c_void_p, C.c_int32, C.c_void_p, C.POINTER(LayerAux),
+                                     C.c_void_p, C.c_size_t, C.c_void_p]),
+    "moeb_bind_pools": (C.c_int, [C.c_int32, C.c_int32, C.c_void_p, C.c_int32, C.c_int32, C.c_void_p, C.c_int32,
+                                  C.c_int32]),
+    "moeb_router_topk": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "moeb_dispatch": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p,
+                                C.c_void_p]),
+    "moeb_dequantize": (C.c_int, [C.c_int32, C.c_void_p, C.c_void_p, C.c_int64, C.c_int64, C.c_void_p]),
+    "moeb_quantize_act": (C.c_int, [C.c_int32, C.c_void_p, C.c_void_p, C.c_int64, C.c_int64, C.c_void_p]),
+    "moeb_quantize_weights": (C.c_size_t, [C.c_int32, C.c_void_p, C.c_void_p, C.c_int64, C.c_int64, C.c_int32]),
+    "moeb_row_size": (C.c_size_t, [C.c_int32, C.c_int64]),
+    "moert_cuda_configure": (None, [C.c_void_p]),
+    "moert_ffn_moe": (None, [C.c_void_p, C.c_void_p]),
+    "moert_cuda_route_counts_enable": (C.c_int32, [C.c_int32, C.c_int32]),
+    "moert_cuda_route_counts_fetch": (C.c_int32, [C.c_void_p, C.c_int32]),
+    "moert_cuda_host_register_pinned": (C.c_int32, [C.c_void_p, C.c_uint64]),
+    "moert_cuda_host_unregister": (None, [C.c_void_p]),
+    "moert_cuda_host_register_mapped": (C.c_int32, [C.c_void_p, C.c_uint64]),
+    "moert_cuda_host_map": (C.c_void_p, [C.c_void_p, C.c_uint64]),
+    "moert_cuda_stats_get": (None, [C.c_void_p]),
+    "moert_cuda_dir_init": (C.c_int32, [C.c_int32, C.c_int32, C.c_int32]),
+    "moert_cuda_dir_async": (C.c_int32, [C.c_void_p, C.c_void_p, C.c_uint64]),
+    "moert_cuda_dir_mark": (C.c_int64, []),
+    "moert_cuda_dir_poll": (C.c_int64, [C.c_int32]),
+    "moert_cuda_publish_h2d": (C.c_int32, [C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "moert_cuda_dir_stats_get": (None, [C.c_void_p]),
+    "moert_cuda_dir_gate": (C.c_int64, [C.c_int32, C.c_int64]),
+    "moert_cuda_set_hot_table": (None, [C.c_int32, C.c_int32, C.c_void_p, C.c_int32, C.c_int32]),
+}
+
+
+def lib(build_if_missing: bool = True) -> C.CDLL:
+    """Loads libmoeb200.so (building it in-tree first when the sources changed)."""
+    global _lib
+    if _lib is None:
+        path = _build.LIB
+        if build_if_missing:
+            try:
+                path = _build.build()
+            except (RuntimeError, OSError) as exc:
+                if not os.path.exists(path):
+                    raise MoebError(-2, f"libmoeb200.so is not built and cannot be built: {exc}") from exc
+        if not os.path.exists(path):
+            raise MoebError(-2, f"{path} missing: run `python -m llapis_b200.build`")
+        _lib = C.CDLL(path)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(_lib, name)
+            fn.restype = res
+            fn.argtypes = args
+    return _lib
+
+
+def check(code: int) -> None:
+    if code != 0:
+        raise MoebError(code, lib().moeb_last_error().decode())
+
+
+def row_size(wtype: int, n: int) -> int:
+    return int(lib().moeb_row_size(wtype, n))

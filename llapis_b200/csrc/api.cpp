@@ -1,0 +1,563 @@
+// Host side of libmoeb200.so: the C-ABI entry points declared in include/moeb200.h and the
+// moert island ABI of include/moert_cuda.h. Validates arguments, carves workspaces, keeps the
+// per-device state (format tables, GELU table, SM count) and launches the sm_100a kernels.
+// There is no CPU fallback: without a compute-capability-10 device every compute entry returns
+// MOEB_ENODEV (moert_ffn_moe, whose ABI returns nothing, prints and aborts like the reference).
+#include "moeb200.h"
+#include "moert_cuda.h"
+#include "params.h"
+
+#include <cuda_runtime.h>
+#include <immintrin.h>
+
+#include <atomic>
+#include <chrono>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+using namespace moeb;
+
+namespace {
+
+thread_local std::string g_msg;
+
+int fail(int code, const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_msg = buf;
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char *what) {
+    return fail(MOEB_ECUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+// ---------------------------------------------------------------- per-device state
+constexpr int kMaxDevices = 64;
+struct DeviceState {
+    bool ready = false;
+    int n_sms = 0;
+};
+std::mutex g_mu;
+DeviceState g_dev[kMaxDevices];
+
+// ggml-cpu's GELU table (ggml-cpu.c:3784-3793): f16(gelu_tanh(f32(h))) for every f16 bit pattern,
+// with gelu_tanh evaluated in ggml's operation order (ggml-cpu/vec.h:963-970). This file is built
+// with -ffp-contract=off and the conversions are the F16C instructions ggml uses on x86.
+void make_gelu_table(std::vector<uint16_t> &t) {
+    t.resize(1u << 16);
+    const float c = 0.79788456080286535587989211986876f, a = 0.044715f;
+    for (uint32_t h = 0; h < (1u << 16); ++h) {
+        const float x = _cvtsh_ss((unsigned short)h);
+        const float g = 0.5f * x * (1.0f + tanhf(c * x * (1.0f + a * x * x)));
+        t[h] = _cvtss_sh(g, 0);
+    }
+}
+
+// Makes the current device ready (tables uploaded); returns MOEB_OK or an error code.
+int ensure_device(int *n_sms_out = nullptr) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return fail(MOEB_ENODEV, "no CUDA device: %s", cudaGetErrorString(e));
+    if (dev < 0 || dev >= kMaxDevices) return fail(MOEB_ENODEV, "device index %d out of range", dev);
+    std::lock_guard<std::mutex> lk(g_mu);
+    DeviceState &st = g_dev[dev];
+    if (!st.ready) {
+        cudaDeviceProp prop;
+        e = cudaGetDeviceProperties(&prop, dev);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceProperties");
+        if (prop.major != 10)
+            return fail(MOEB_ENODEV, "device %d is sm_%d%d; this library is built for sm_100a only", dev, prop.major,
+                        prop.minor);
+        std::vector<uint16_t> tab;
+        make_gelu_table(tab);
+        e = upload_gelu_table(tab.data(), 0);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(0);
+        if (e != cudaSuccess) return cuda_fail(e, "GELU table upload");
+        st.n_sms = prop.multiProcessorCount;
+        st.ready = true;
+    }
+    if (n_sms_out) *n_sms_out = st.n_sms;
+    return MOEB_OK;
+}
+
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+int check_pool(const moeb_pool &pl, int d_model, int n_ff, const char *name) {
+    if (pl.n <= 0) return MOEB_OK;
+    if (pl.type_gu != MOEB_T_Q4_K && pl.type_gu != MOEB_T_IQ2_S)
+        return fail(MOEB_ETYPE, "%s pool: gate_up type %d unsupported (Q4_K=12, IQ2_S=22)", name, pl.type_gu);
+    if (pl.type_down != MOEB_T_Q5_0 && pl.type_down != MOEB_T_IQ4_NL)
+        return fail(MOEB_ETYPE, "%s pool: down type %d unsupported (Q5_0=6, IQ4_NL=20)", name, pl.type_down);
+    if (!pl.w_gu || !pl.w_down) return fail(MOEB_EINVAL, "%s pool: null weight pointer", name);
+    if (!aligned16(pl.w_gu) || !aligned16(pl.w_down))
+        return fail(MOEB_EINVAL, "%s pool: weight bases must be 16-byte aligned", name);
+    if ((2LL * n_ff * row_bytes(pl.type_gu, d_model)) % 16 || ((long long)d_model * row_bytes(pl.type_down, n_ff)) % 16)
+        return fail(MOEB_EINVAL, "%s pool: expert stride is not a multiple of 16 bytes", name);
+    return MOEB_OK;
+}
+
+int check_layer(const moeb_layer *L) {
+    if (!L) return fail(MOEB_EINVAL, "null layer");
+    if (L->d_model <= 0 || L->d_model % QK_K) return fail(MOEB_EINVAL, "d_model %d must be a multiple of 256", L->d_model);
+    if (L->n_ff <= 0 || L->n_ff % 32) return fail(MOEB_EINVAL, "n_ff %d must be a multiple of 32", L->n_ff);
+    if (L->n_expert <= 0 || L->n_expert % 32 || L->n_expert > kMaxE)
+        return fail(MOEB_EINVAL, "n_expert %d must be a multiple of 32 and <= %d", L->n_expert, kMaxE);
+    if (L->top_k <= 0 || L->top_k > kMaxTopK || L->top_k > L->n_expert)
+        return fail(MOEB_EINVAL, "top_k %d out of range (1..%d)", L->top_k, kMaxTopK);
+    if (!L->w_router) return fail(MOEB_EINVAL, "null router weights");
+    if (L->hot.n > 0 && (!L->exp_slot || !L->slot_exp || !L->slot_state))
+        return fail(MOEB_EINVAL, "hot pool given without the residency mirror (exp_slot/slot_exp/slot_state)");
+    if (L->hot.n <= 0 && L->cold.n <= 0) return fail(MOEB_EINVAL, "no expert pool");
+    if (L->cold.n > 0 && L->cold.n < L->n_expert)
+        return fail(MOEB_EINVAL, "cold pool holds %d experts, layer has %d", L->cold.n, L->n_expert);
+    int rc = check_pool(L->hot, L->d_model, L->n_ff, "hot");
+    if (rc) return rc;
+    return check_pool(L->cold, L->d_model, L->n_ff, "cold");
+}
+
+// workspace carve for one chunk of up to kMaxDecodeT tokens
+struct LayerWs {
+    float *logits;
+    uint8_t *xq;
+    float *h, *y;
+    int32_t *ids, *cnt, *off, *perm;
+    float *w;
+    size_t bytes;
+};
+
+LayerWs carve(const moeb_layer *L, int T, uint8_t *base) {
+    LayerWs w{};
+    const int P = T * L->top_k;
+    size_t o = 0;
+    auto take = [&](size_t n) { size_t at = o; o = align_up(o + n, 256); return base ? base + at : nullptr; };
+    w.logits = (float *)take(sizeof(float) * T * L->n_expert);
+    w.xq = take((size_t)T * xq_stride_bytes(L->d_model));
+    w.h = (float *)take(sizeof(float) * P * 2 * L->n_ff);
+    w.y = (float *)take(sizeof(float) * P * L->d_model);
+    w.ids = (int32_t *)take(sizeof(int32_t) * P);
+    w.w = (float *)take(sizeof(float) * P);
+    w.cnt = (int32_t *)take(sizeof(int32_t) * L->n_expert);
+    w.off = (int32_t *)take(sizeof(int32_t) * (L->n_expert + 1));
+    w.perm = (int32_t *)take(sizeof(int32_t) * P);
+    w.bytes = o;
+    return w;
+}
+
+PoolView pool_view(const moeb_pool &pl, bool gate_up) {
+    PoolView v{};
+    v.w = (const uint8_t *)(gate_up ? pl.w_gu : pl.w_down);
+    v.type = gate_up ? pl.type_gu : pl.type_down;
+    v.n = pl.n;
+    v.scale = gate_up ? nullptr : pl.s_down;
+    v.ptrs = nullptr;
+    return v;
+}
+
+}  // namespace
+
+// ================================================================= moeb200.h
+extern "C" int moeb_init(void) { return ensure_device(); }
+
+extern "C" const char *moeb_last_error(void) { return g_msg.c_str(); }
+
+extern "C" const char *moeb_version(void) { return "moeb200 0.1 (sm_100a)"; }
+
+extern "C" int32_t moeb_device_error(void *stream) {
+    int32_t v = 0;
+    if (ensure_device() != MOEB_OK) return MOEB_ENODEV;
+    cudaError_t e = read_and_clear_error(&v, (cudaStream_t)stream);
+    if (e != cudaSuccess) return cuda_fail(e, "read device error word");
+    return v;
+}
+
+extern "C" size_t moeb_layer_workspace_size(const moeb_layer *L, int32_t n_tokens) {
+    if (!L || n_tokens <= 0) return 0;
+    const int T = n_tokens < kMaxDecodeT ? n_tokens : kMaxDecodeT;
+    return carve(L, T, nullptr).bytes;
+}
+
+extern "C" int moeb_layer_forward(const moeb_layer *L, const float *x, int32_t n_tokens, float *out,
+                                  const moeb_layer_aux *aux, void *workspace, size_t workspace_bytes, void *stream) {
+    int rc = check_layer(L);
+    if (rc) return rc;
+    if (n_tokens < 0) return fail(MOEB_EINVAL, "n_tokens %d < 0", n_tokens);
+    if (n_tokens == 0) return MOEB_OK;
+    if (!x || !out) return fail(MOEB_EINVAL, "null x / out");
+    if (!aligned16(x) || !aligned16(out) || !aligned16(L->w_router))
+        return fail(MOEB_EINVAL, "x, out and router weights must be 16-byte aligned");
+    int n_sms = 0;
+    rc = ensure_device(&n_sms);
+    if (rc) return rc;
+    const size_t need = moeb_layer_workspace_size(L, n_tokens);
+    if (!workspace || workspace_bytes < need)
+        return fail(MOEB_ESPACE, "workspace of %zu bytes, %zu needed", workspace_bytes, need);
+    if (!aligned16(workspace)) return fail(MOEB_EINVAL, "workspace must be 16-byte aligned");
+    cudaStream_t s = (cudaStream_t)stream;
+    const int d = L->d_model, k = L->top_k, E = L->n_expert;
+    const Residency res = {L->hot.n, L->exp_slot, L->slot_exp, L->slot_state};
+
+    // tokens are independent: longer batches run as consecutive chunks of the decode path
+    for (int t0 = 0; t0 < n_tokens; t0 += kMaxDecodeT) {
+        const int T = n_tokens - t0 < kMaxDecodeT ? n_tokens - t0 : kMaxDecodeT;
+        const int P = T * k;
+        LayerWs w = carve(L, T, (uint8_t *)workspace);
+
+        RouterParams rp{};
+        rp.w_router = L->w_router;
+        rp.b_router = L->b_router;
+        rp.x = x + (size_t)t0 * d;
+        rp.T = T;
+        rp.E = E;
+        rp.d = d;
+        rp.logits = w.logits;
+        rp.xq = w.xq;
+        rp.xq_stride = xq_stride_bytes(d);
+        cudaError_t e = launch_router(rp, s, false);
+        if (e != cudaSuccess) return cuda_fail(e, "router launch");
+
+        GemvParams g{};
+        g.route = {w.logits, nullptr, 0, T, E, k};
+        g.res = res;
+        g.hot = pool_view(L->hot, true);
+        g.cold = pool_view(L->cold, true);
+        g.d_in = d;
+        g.d_out = 2 * L->n_ff;
+        g.xq = w.xq;
+        g.xq_stride = xq_stride_bytes(d);
+        g.kind = 0;
+        g.y = w.h;
+        g.ids_out = w.ids;
+        g.w_out = w.w;
+        g.cnt_out = w.cnt;
+        g.off_out = w.off;
+        g.perm_out = w.perm;
+        e = launch_gemv(g, s, true, n_sms);
+        if (e != cudaSuccess) return cuda_fail(e, "gate_up launch");
+
+        GemvParams dn{};
+        dn.route = g.route;
+        dn.res = res;
+        dn.hot = pool_view(L->hot, false);
+        dn.cold = pool_view(L->cold, false);
+        dn.d_in = L->n_ff;
+        dn.d_out = d;
+        dn.h = w.h;
+        dn.kind = 1;
+        dn.y = w.y;
+        dn.apply_scale = 1;
+        e = launch_gemv(dn, s, true, n_sms);
+        if (e != cudaSuccess) return cuda_fail(e, "down launch");
+
+        CombineParams cp{};
+        cp.y = w.y;
+        cp.w = w.w;
+        cp.T = T;
+        cp.k = k;
+        cp.d = d;
+        cp.out = out + (size_t)t0 * d;
+        e = launch_combine(cp, s, true);
+        if (e != cudaSuccess) return cuda_fail(e, "combine launch");
+
+        if (aux) {
+            struct Cp { void *dst; const void *src; size_t n; } cps[] = {
+                {aux->logits ? aux->logits + (size_t)t0 * E : nullptr, w.logits, sizeof(float) * T * E},
+                {aux->ids ? aux->ids + (size_t)t0 * k : nullptr, w.ids, sizeof(int32_t) * P},
+                {aux->weights ? aux->weights + (size_t)t0 * k : nullptr, w.w, sizeof(float) * P},
+                {aux->gate_up ? aux->gate_up + (size_t)t0 * k * 2 * L->n_ff : nullptr, w.h, sizeof(float) * P * 2 * L->n_ff},
+                {aux->down ? aux->down + (size_t)t0 * k * d : nullptr, w.y, sizeof(float) * P * d},
+            };
+            for (auto &c : cps) {
+                if (!c.dst) continue;
+                e = cudaMemcpyAsync(c.dst, c.src, c.n, cudaMemcpyDeviceToDevice, s);
+                if (e != cudaSuccess) return cuda_fail(e, "aux copy");
+            }
+            // the dispatch outputs describe one chunk; they are reported for single-chunk calls
+            if (n_tokens <= kMaxDecodeT) {
+                if (aux->counts) e = cudaMemcpyAsync(aux->counts, w.cnt, sizeof(int32_t) * E, cudaMemcpyDeviceToDevice, s);
+                if (e == cudaSuccess && aux->offsets)
+                    e = cudaMemcpyAsync(aux->offsets, w.off, sizeof(int32_t) * (E + 1), cudaMemcpyDeviceToDevice, s);
+                if (e == cudaSuccess && aux->perm)
+                    e = cudaMemcpyAsync(aux->perm, w.perm, sizeof(int32_t) * P, cudaMemcpyDeviceToDevice, s);
+                if (e != cudaSuccess) return cuda_fail(e, "aux copy");
+            }
+        }
+    }
+    return MOEB_OK;
+}
+
+extern "C" int moeb_router_topk(const float *logits, int32_t n_tokens, int32_t n_expert, int32_t top_k, int32_t *ids,
+                                float *weights, void *stream) {
+    if (!logits || n_tokens <= 0 || n_expert <= 0 || n_expert % 32 || n_expert > kMaxE || top_k <= 0 ||
+        top_k > kMaxTopK || top_k > n_expert)
+        return fail(MOEB_EINVAL, "moeb_router_topk: bad shape T=%d E=%d k=%d", n_tokens, n_expert, top_k);
+    int rc = ensure_device();
+    if (rc) return rc;
+    for (int t0 = 0; t0 < n_tokens; t0 += kMaxDecodeT) {
+        const int T = n_tokens - t0 < kMaxDecodeT ? n_tokens - t0 : kMaxDecodeT;
+        RouteSrc r = {logits + (size_t)t0 * n_expert, nullptr, 0, T, n_expert, top_k};
+        cudaError_t e = launch_route_only(r, ids ? ids + (size_t)t0 * top_k : nullptr,
+                                          weights ? weights + (size_t)t0 * top_k : nullptr, nullptr, nullptr, nullptr,
+                                          (cudaStream_t)stream);
+        if (e != cudaSuccess) return cuda_fail(e, "route launch");
+    }
+    return MOEB_OK;
+}
+
+extern "C" int moeb_dispatch(const int32_t *ids, int32_t n_tokens, int32_t top_k, int32_t n_expert, int32_t *counts,
+                             int32_t *offsets, int32_t *perm, void *stream) {
+    if (!ids || n_tokens <= 0 || n_tokens > kMaxDecodeT || n_expert <= 0 || n_expert % 32 || n_expert > kMaxE ||
+        top_k <= 0 || top_k > kMaxTopK)
+        return fail(MOEB_EINVAL, "moeb_dispatch: bad shape T=%d E=%d k=%d (T <= %d on this path)", n_tokens, n_expert,
+                    top_k, kMaxDecodeT);
+    int rc = ensure_device();
+    if (rc) return rc;
+    RouteSrc r = {nullptr, ids, top_k, n_tokens, n_expert, top_k};
+    cudaError_t e = launch_route_only(r, nullptr, nullptr, counts, offsets, perm, (cudaStream_t)stream);
+    if (e != cudaSuccess) return cuda_fail(e, "dispatch launch");
+    return MOEB_OK;
+}
+
+extern "C" int moeb_dequantize(int32_t type, const void *src, float *dst, int64_t n_rows, int64_t n_per_row, void *stream) {
+    if (type != MOEB_T_Q4_K && type != MOEB_T_IQ2_S && type != MOEB_T_Q5_0 && type != MOEB_T_IQ4_NL)
+        return fail(MOEB_ETYPE, "moeb_dequantize: type %d unsupported", type);
+    const int blk = (type == MOEB_T_Q4_K || type == MOEB_T_IQ2_S) ? QK_K : QK32;
+    if (!src || !dst || n_rows <= 0 || n_per_row <= 0 || n_per_row % blk)
+        return fail(MOEB_EINVAL, "moeb_dequantize: bad shape");
+    int rc = ensure_device();
+    if (rc) return rc;
+    cudaError_t e = launch_dequant(type, src, dst, n_rows, n_per_row, (cudaStream_t)stream);
+    return e == cudaSuccess ? MOEB_OK : cuda_fail(e, "dequant launch");
+}
+
+extern "C" int moeb_quantize_act(int32_t wtype, const float *x, void *dst, int64_t n_rows, int64_t n_per_row,
+                                 void *stream) {
+    int32_t vdt;
+    if (wtype == MOEB_T_Q4_K || wtype == MOEB_T_IQ2_S) vdt = T_Q8_K;
+    else if (wtype == MOEB_T_Q5_0 || wtype == MOEB_T_IQ4_NL) vdt = T_Q8_0;
+    else return fail(MOEB_ETYPE, "moeb_quantize_act: weight type %d unsupported", wtype);
+    if (!x || !dst || n_rows <= 0 || n_per_row <= 0 || n_per_row % (vdt == T_Q8_K ? QK_K : QK32))
+        return fail(MOEB_EINVAL, "moeb_quantize_act: bad shape");
+    int rc = ensure_device();
+    if (rc) return rc;
+    cudaError_t e = launch_quant_act(vdt, x, dst, n_rows, n_per_row, (cudaStream_t)stream);
+    return e == cudaSuccess ? MOEB_OK : cuda_fail(e, "quant launch");
+}
+
+extern "C" size_t moeb_row_size(int32_t type, int64_t n_per_row) { return (size_t)row_bytes(type, n_per_row); }
+
+// ================================================================= moert_cuda.h
+namespace {
+
+moert_cuda_config g_cfg = {1, 0, 0, 3, 0, 0, 0, 0, 0};
+
+struct Binding {
+    const void *w_hot = nullptr, *w_cold = nullptr;
+    int32_t hot_type = 0, cold_type = 0, n_hot = 0, n_cold = 0;
+    const void *const *hot_table = nullptr;
+    int32_t hot_table_n = 0, hot_table_type = 0;
+};
+constexpr int kMaxLayers = 128;
+Binding g_bind[kMaxLayers][2];
+
+struct RouteCounters {
+    int32_t *dev = nullptr;
+    int32_t nl = 0, ne = 0;
+} g_rc;
+
+std::atomic<long long> g_fires{0}, g_op_ns{0};
+
+[[noreturn]] void island_abort(const char *what) {
+    fprintf(stderr, "moert_ffn_moe: %s\n", what);
+    abort();
+}
+
+}  // namespace
+
+extern "C" void moert_cuda_configure(const moert_cuda_config *cfg) {
+    if (cfg) g_cfg = *cfg;
+}
+
+extern "C" int moeb_bind_pools(int32_t il, int32_t kind, const void *w_hot, int32_t hot_type, int32_t n_hot,
+                               const void *w_cold, int32_t cold_type, int32_t n_cold) {
+    if (il < 0 || il >= kMaxLayers || kind < 0 || kind > 1) return fail(MOEB_EINVAL, "bind: il/kind out of range");
+    Binding &b = g_bind[il][kind];
+    b.w_hot = w_hot;
+    b.hot_type = hot_type;
+    b.n_hot = n_hot;
+    b.w_cold = w_cold;
+    b.cold_type = cold_type;
+    b.n_cold = n_cold;
+    return MOEB_OK;
+}
+
+extern "C" void moert_ffn_moe(const moert_ffn_moe_args *a, const moert_ffn_moe_host *h) {
+    const auto t_start = std::chrono::steady_clock::now();
+    if (!a) island_abort("null args");
+    if (a->planc_mode != 0) island_abort("only planc_mode 0 (device-resident cold pool) is served on B200");
+    if (a->kind != 0 && a->kind != 1) island_abort("kind must be 0 (gate_up) or 1 (down)");
+    if (a->il < 0 || a->il >= kMaxLayers) island_abort("layer index out of range");
+    int n_sms = 0;
+    if (ensure_device(&n_sms) != MOEB_OK) island_abort(g_msg.c_str());
+    const Binding &b = g_bind[a->il][a->kind];
+    cudaStream_t s = (cudaStream_t)a->stream;
+    const int kind = a->kind, k = a->n_used, T = a->n_tokens;
+    if (k <= 0 || k > kMaxTopK || T <= 0) island_abort("n_used / n_tokens out of range");
+    if (a->n_expert <= 0 || a->n_expert > kMaxE || a->n_expert % 32) island_abort("n_expert must be a multiple of 32, <= 256");
+    const int blk = kind == 0 ? QK_K : QK32;
+    if (a->d_in % blk || a->d_out % kGroupRows) island_abort("d_in / d_out not supported");
+
+    PoolView hot{}, cold{};
+    hot.w = (const uint8_t *)b.w_hot;
+    hot.type = b.hot_type;
+    hot.n = b.n_hot;
+    hot.scale = kind == 1 ? (const float *)a->s_hot : nullptr;
+    if (b.hot_table && b.hot_table_n == a->k) { hot.ptrs = b.hot_table; hot.type = b.hot_table_type; }
+    cold.w = (const uint8_t *)b.w_cold;
+    cold.type = a->cold_type_tag;
+    cold.n = a->n_expert;
+    cold.scale = kind == 1 ? (const float *)a->s_cold : nullptr;
+    if (!cold.w && a->has_w_cold) island_abort("cold pool not bound (moeb_bind_pools)");
+    const Residency res = {a->k, (const int32_t *)a->exp_slot, (const int32_t *)a->slot_exp, (const int32_t *)a->slot_state};
+
+    int32_t *rc_counts = nullptr, *rc_hits = nullptr;
+    if (g_rc.dev && kind == 0 && a->il < g_rc.nl && a->n_expert == g_rc.ne) {
+        rc_counts = g_rc.dev + (size_t)a->il * g_rc.ne;
+        rc_hits = g_rc.dev + (size_t)g_rc.nl * g_rc.ne + (size_t)a->il * 2;
+    }
+
+    // scratch from the caller's pool (strict LIFO): the Q8_K activations of gate_up
+    void *scratch = nullptr;
+    const int xs = xq_stride_bytes(a->d_in);
+    if (kind == 0) {
+        if (!h || !h->pool_alloc) island_abort("gate_up needs the host pool for activation scratch");
+        scratch = h->pool_alloc(h->user, (uint64_t)xs * (T < kMaxDecodeT ? T : kMaxDecodeT) + 256);
+    }
+    const int32_t *ids = (const int32_t *)a->ids;
+    const float *cur = (const float *)a->cur;
+    float *dst = (float *)a->dst;
+    for (int t0 = 0; t0 < T; t0 += kMaxDecodeT) {
+        const int Tc = T - t0 < kMaxDecodeT ? T - t0 : kMaxDecodeT;
+        GemvParams g{};
+        g.route = {nullptr, ids + (size_t)t0 * a->ids_s1, a->ids_s1, Tc, a->n_expert, k};
+        g.res = res;
+        g.hot = hot;
+        g.cold = cold;
+        g.d_in = a->d_in;
+        g.d_out = a->d_out;
+        g.y = dst + (size_t)t0 * k * a->d_out;
+        g.rc_counts = rc_counts;
+        g.rc_hits = rc_hits;
+        cudaError_t e;
+        if (kind == 0) {
+            // gate_up: one shared activation column per token (cur is [d_in, 1, T])
+            e = launch_quant_q8k(cur + (size_t)t0 * a->d_in, (uint8_t *)scratch, Tc, a->d_in, xs, s);
+            if (e != cudaSuccess) island_abort(cudaGetErrorString(e));
+            g.kind = 0;
+            g.xq = (const uint8_t *)scratch;
+            g.xq_stride = xs;
+        } else {
+            // down: one activation column per routed pair (cur is [d_in, n_used, T])
+            g.kind = 2;
+            g.a = cur + (size_t)t0 * k * a->d_in;
+            g.a_per_pair = 1;
+            g.apply_scale = 1;
+        }
+        e = launch_gemv(g, s, false, n_sms);
+        if (e != cudaSuccess) island_abort(cudaGetErrorString(e));
+    }
+    if (scratch) h->pool_free(h->user, scratch);
+    g_fires++;
+    g_op_ns += std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now() - t_start).count();
+}
+
+extern "C" int32_t moert_cuda_route_counts_enable(int32_t n_layers, int32_t n_expert) {
+    if (n_layers <= 0 || n_expert <= 0) return 0;
+    if (ensure_device() != MOEB_OK) return 0;
+    if (g_rc.dev) { cudaFree(g_rc.dev); g_rc.dev = nullptr; }
+    const size_t n = (size_t)n_layers * n_expert + (size_t)n_layers * 2;
+    if (cudaMalloc(&g_rc.dev, n * sizeof(int32_t)) != cudaSuccess) { g_rc.dev = nullptr; return 0; }
+    if (cudaMemset(g_rc.dev, 0, n * sizeof(int32_t)) != cudaSuccess) return 0;
+    g_rc.nl = n_layers;
+    g_rc.ne = n_expert;
+    return 1;
+}
+
+extern "C" int32_t moert_cuda_route_counts_fetch(int32_t *dst, int32_t reset) {
+    if (!g_rc.dev || !dst) return 0;
+    const size_t n = (size_t)g_rc.nl * g_rc.ne + (size_t)g_rc.nl * 2;
+    if (cudaMemcpy(dst, g_rc.dev, n * sizeof(int32_t), cudaMemcpyDeviceToHost) != cudaSuccess) return 0;
+    if (reset && cudaMemset(g_rc.dev, 0, n * sizeof(int32_t)) != cudaSuccess) return 0;
+    return 1;
+}
+
+extern "C" int32_t moert_cuda_host_register_pinned(void *base, uint64_t size) {
+    if (!base || !size) return 0;
+    cudaError_t e = cudaHostRegister(base, size, cudaHostRegisterDefault);
+    if (e == cudaErrorHostMemoryAlreadyRegistered) { cudaGetLastError(); return 1; }
+    return e == cudaSuccess ? 1 : (cudaGetLastError(), 0);
+}
+
+extern "C" void moert_cuda_host_unregister(void *base) {
+    if (base && cudaHostUnregister(base) != cudaSuccess) cudaGetLastError();
+}
+
+extern "C" int32_t moert_cuda_host_register_mapped(void *base, uint64_t size) {
+    if (!base || !size) return 0;
+    cudaError_t e = cudaHostRegister(base, size, cudaHostRegisterMapped);
+    if (e == cudaErrorHostMemoryAlreadyRegistered) { cudaGetLastError(); return 1; }
+    return e == cudaSuccess ? 1 : (cudaGetLastError(), 0);
+}
+
+extern "C" void *moert_cuda_host_map(void *base, uint64_t size) {
+    if (!moert_cuda_host_register_mapped(base, size)) return nullptr;
+    void *dev = nullptr;
+    if (cudaHostGetDevicePointer(&dev, base, 0) != cudaSuccess) { cudaGetLastError(); return nullptr; }
+    return dev;
+}
+
+extern "C" void moert_cuda_stats_get(moert_cuda_stats *out) {
+    if (!out) return;
+    memset(out, 0, sizeof *out);
+    out->fires = g_fires.load();
+    out->op_host_ns = g_op_ns.load();
+}
+
+// The transfer director moves experts between host RAM and VRAM slots; on B200 both classes are
+// HBM-resident, so the asynchronous transport is refused (0) and callers copy themselves, which
+// is the reference contract for a refused copy (cuda.h:248-250).
+extern "C" int32_t moert_cuda_dir_init(int32_t, int32_t, int32_t) { return 0; }
+extern "C" int32_t moert_cuda_dir_async(void *, const void *, uint64_t) { return 0; }
+extern "C" int64_t moert_cuda_dir_mark(void) { return 0; }
+extern "C" int64_t moert_cuda_dir_poll(int32_t) { return 0; }
+extern "C" void moert_cuda_dir_stats_get(moert_cuda_dir_stats *out) {
+    if (out) memset(out, 0, sizeof *out);
+}
+extern "C" int64_t moert_cuda_dir_gate(int32_t, int64_t) { return 0; }
+
+// Residency publication: n synchronous host -> device copies (cuda.h:258-260).
+extern "C" int32_t moert_cuda_publish_h2d(int32_t n, void *const *dsts, const void *const *srcs, const uint64_t *sizes) {
+    if (n < 0 || (n > 0 && (!dsts || !srcs || !sizes))) return 0;
+    for (int32_t i = 0; i < n; ++i)
+        if (cudaMemcpy(dsts[i], srcs[i], sizes[i], cudaMemcpyHostToDevice) != cudaSuccess) return 0;
+    return 1;
+}
+
+extern "C" void moert_cuda_set_hot_table(int32_t il, int32_t kind, const void *const *dev_ptrs, int32_t n, int32_t type_tag) {
+    if (il < 0 || il >= kMaxLayers || kind < 0 || kind > 1) return;
+    Binding &b = g_bind[il][kind];
+    b.hot_table = n > 0 ? dev_ptrs : nullptr;
+    b.hot_table_n = n > 0 ? n : 0;
+    b.hot_table_type = type_tag;
+}

@@ -1,0 +1,119 @@
+// Device-only helpers for the B200 MoE-FFN path (included by kernels.cu alone): half conversions, the
+// format tables, inline-PTX wrappers for mbarrier / bulk copies / programmatic dependent launch,
+// and the device error word that bounded waits report into.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "ggml_tables.inc"
+#include "params.h"
+
+namespace moeb {
+
+// ---------------------------------------------------------------- format tables (device copies)
+// All device code of the library is one translation unit (kernels.cu includes the kernel
+// headers), so these module-scope variables are defined here, once.
+// IQ2_S codebook (1024 rows x 8 magnitudes) and IQ4_NL levels: format constants of ggml's blocks.
+__device__ uint64_t g_iq2s_grid[MOE_IQ2S_GRID_ROWS] = MOE_IQ2S_GRID_INIT;
+__device__ int8_t g_iq4nl[16] = MOE_IQ4NL_VALUES_INIT;
+// ggml-cpu's fp16 GELU table (gelu_tanh rounded to f16, indexed by the f16 bit pattern of the
+// gate value); filled from the host once per device.
+__device__ uint16_t g_gelu_f16[1 << 16];
+// Error word: bounded waits that give up OR their code in here and return.
+__device__ int32_t g_error;
+
+enum : int32_t { ERR_MBAR_TIMEOUT = 1, ERR_BAD_EXPERT = 2, ERR_CAPACITY = 4 };
+
+// ---------------------------------------------------------------- small device helpers
+__device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
+__device__ __forceinline__ uint16_t f2h_rn(float f) { return __half_as_ushort(__float2half_rn(f)); }
+
+__device__ __forceinline__ uint16_t ld_u16(const uint8_t *p) {
+    return (uint16_t)p[0] | ((uint16_t)p[1] << 8);
+}
+__device__ __forceinline__ uint32_t ld_u32_unaligned(const uint8_t *p) {
+    return (uint32_t)p[0] | ((uint32_t)p[1] << 8) | ((uint32_t)p[2] << 16) | ((uint32_t)p[3] << 24);
+}
+// 4 bytes at a 2-byte aligned shared address
+__device__ __forceinline__ uint32_t ld_u32_a2(const uint8_t *p) {
+    const uint16_t *q = reinterpret_cast<const uint16_t *>(p);
+    return (uint32_t)q[0] | ((uint32_t)q[1] << 16);
+}
+
+__device__ __forceinline__ int dp4a(int a, int b, int c) { return __dp4a(a, b, c); }
+
+// byte-wise mask 0xff for each set bit of the low 4 bits of s
+__device__ __forceinline__ uint32_t sign_bytes4(uint32_t s) {
+    return ((s * 0x00204081u) & 0x01010101u) * 0xffu;
+}
+
+// ---------------------------------------------------------------- mbarrier + bulk copy (PTX)
+__device__ __forceinline__ uint32_t smem_addr(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+                 : "memory");
+}
+
+// one bulk copy global -> shared, completion signalled on `bar` (addresses and size 16-byte aligned)
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait on an mbarrier phase. Returns false (and records ERR_MBAR_TIMEOUT) if the phase
+// did not complete within the iteration limit; each try_wait itself suspends for a
+// hardware-chosen interval, so the limit bounds the wait to well under a second.
+constexpr uint32_t kWaitLimit = 1u << 22;
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+    for (uint32_t i = 0; i < kWaitLimit; ++i)
+        if (mbar_try_wait(bar, parity)) return true;
+    atomicOr(&g_error, ERR_MBAR_TIMEOUT);
+    return false;
+}
+
+// ---------------------------------------------------------------- programmatic dependent launch
+// wait: block until the upstream grid has completed and its memory is visible.
+// launch_dependents: allow the downstream grid to start its pre-wait prologue.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+}  // namespace moeb

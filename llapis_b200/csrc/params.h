@@ -1,0 +1,137 @@
+// Kernel parameter blocks, shape helpers and launcher declarations shared by the device
+// translation unit (kernels.cu) and the host-side C-ABI (api.cpp). Host-safe: no device code.
+#pragma once
+
+#include <cuda_runtime_api.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __CUDACC__
+#define MOEB_HD __host__ __device__
+#else
+#define MOEB_HD
+#endif
+
+namespace moeb {
+
+// ggml type ids (third_party/llama/ggml/include/ggml.h:390-432); they travel through the moert
+// ABI as opaque "type tags".
+enum : int32_t {
+    T_F32 = 0, T_F16 = 1, T_Q5_0 = 6, T_Q8_0 = 8, T_Q4_K = 12, T_Q8_K = 15, T_IQ4_NL = 20, T_IQ2_S = 22,
+};
+
+constexpr int QK_K = 256;
+constexpr int QK32 = 32;
+constexpr int B_Q4_K = 144;    // d f16 | dmin f16 | scales[12] | qs[128]
+constexpr int B_IQ2_S = 82;    // d f16 | qs[32] | signs[32] | qh[8] | scales[8]
+constexpr int B_Q5_0 = 22;     // d f16 | qh[4] | qs[16]
+constexpr int B_IQ4_NL = 18;   // d f16 | qs[16]
+constexpr int B_Q8_K = 292;    // d f32 | qs[256] | bsums[16] i16
+constexpr int B_Q8_0 = 34;     // d f16 | qs[32]
+
+MOEB_HD inline int64_t row_bytes(int32_t type, int64_t n) {
+    switch (type) {
+        case T_F32:    return n * 4;
+        case T_F16:    return n * 2;
+        case T_Q4_K:   return n / QK_K * B_Q4_K;
+        case T_IQ2_S:  return n / QK_K * B_IQ2_S;
+        case T_Q5_0:   return n / QK32 * B_Q5_0;
+        case T_IQ4_NL: return n / QK32 * B_IQ4_NL;
+        case T_Q8_K:   return n / QK_K * B_Q8_K;
+        case T_Q8_0:   return n / QK32 * B_Q8_0;
+        default:       return 0;
+    }
+}
+
+constexpr int kThreads = 256;            // 8 warps per CTA
+constexpr int kWarps = kThreads / 32;
+constexpr int kMaxDecodeT = 16;          // tokens per call on the GEMV path
+constexpr int kMaxE = 256;               // experts per layer (multiple of 32)
+constexpr int kMaxTopK = 16;
+constexpr int kMaxPairs = kMaxDecodeT * kMaxTopK;
+constexpr int kTokChunk = 4;             // tokens dotted per pass over a decoded weight row
+constexpr int kGroupRows = 8;            // work-split granularity (16-byte aligned for all types)
+
+// Residency classes of a routed pair (moert/cuda/ffn_moe.cu:101-104).
+struct Residency {
+    int32_t n_slots;
+    const int32_t *exp_slot, *slot_exp, *slot_state;
+};
+
+// One precision class of a projection: pool base, type, rows, and the per-entry down scale.
+struct PoolView {
+    const uint8_t *w;     // [n][rows][row_bytes]
+    int32_t type;
+    int32_t n;
+    const float *scale;   // [n] or nullptr
+    const void *const *ptrs;   // optional device table: entry i at ptrs[i] instead of w + i*stride
+};
+
+// Routing source for the in-CTA dispatch: either logits (softmax/top-k in the CTA) or given ids.
+struct RouteSrc {
+    const float *logits;    // [T][E] or nullptr
+    const int32_t *ids;     // [T][ids_s1] or nullptr (when logits == nullptr)
+    int32_t ids_s1;
+    int32_t T, E, k;
+};
+
+// gate_up / down grouped GEMV problem.
+struct GemvParams {
+    RouteSrc route;
+    Residency res;
+    PoolView hot, cold;
+    int32_t d_in, d_out;
+    // activations
+    const uint8_t *xq;       // gate_up: Q8_K rows [T][xq_stride] (per token)
+    int32_t xq_stride;
+    const float *h;          // down (from_h): f32 [P][2*d_in] gate_up outputs -> GeGLU -> Q8_0
+    const float *a;          // down (plain): f32 [P][d_in] activations (or [n_cols][d_in] with a_per_pair=0)
+    int32_t a_per_pair;
+    int32_t kind;            // 0 gate_up (Q8_K from xq), 1 down from h, 2 down from a
+    float *y;                // [P][d_out]
+    int32_t apply_scale;
+    // routing outputs for inspection (written by CTA 0 when non-null)
+    int32_t *ids_out;
+    float *w_out;
+    int32_t *cnt_out, *off_out, *perm_out;
+    // device routing counters (moert_cuda_route_counts_*): [E] routed pairs, [2] hot/cold pairs
+    int32_t *rc_counts, *rc_hits;
+};
+
+struct RouterParams {
+    const float *w_router;   // [E][d]
+    const float *b_router;   // [E] or nullptr
+    const float *x;          // [T][d]
+    int32_t T, E, d;
+    float *logits;           // [T][E]
+    uint8_t *xq;             // [T][xq_stride] Q8_K (nullptr: skip)
+    int32_t xq_stride;
+};
+
+struct CombineParams {
+    const float *y;          // [P][d]
+    const float *w;          // [T][k]
+    int32_t T, k, d;
+    float *out;              // [T][d]
+};
+
+MOEB_HD inline int xq_stride_bytes(int d) { return (int)(((d / QK_K) * B_Q8_K + 15) / 16 * 16); }
+// Q8_0 activation row in shared memory: qs[nb][32] | d[nb] f32 | qsum[nb] i32
+MOEB_HD inline int q80_stride(int d_in) { return ((d_in / 32) * 40 + 15) / 16 * 16; }
+
+// host-side launch helpers (decode.cu); `pdl` chains the launch to the previous kernel in the stream
+cudaError_t launch_router(const RouterParams &p, cudaStream_t s, bool pdl);
+cudaError_t launch_gemv(const GemvParams &p, cudaStream_t s, bool pdl, int n_sms);
+cudaError_t launch_combine(const CombineParams &p, cudaStream_t s, bool pdl);
+cudaError_t launch_quant_q8k(const float *x, uint8_t *dst, int rows, int d, int stride, cudaStream_t s);
+size_t gemv_smem_bytes(int kind, int d_in, int T);
+// standalone pieces behind the moeb_* inspection entry points
+cudaError_t launch_route_only(const RouteSrc &r, int32_t *ids, float *w, int32_t *cnt, int32_t *off, int32_t *perm,
+                              cudaStream_t s);
+cudaError_t launch_dequant(int32_t type, const void *src, float *dst, int64_t rows, int64_t n, cudaStream_t s);
+cudaError_t launch_quant_act(int32_t vdt, const float *x, void *dst, int64_t rows, int64_t n, cudaStream_t s);
+// device state: format tables, GELU table upload, error word
+cudaError_t upload_gelu_table(const uint16_t *host_table, cudaStream_t s);
+cudaError_t read_and_clear_error(int32_t *out, cudaStream_t s);
+
+}  // namespace moeb

@@ -1,0 +1,140 @@
+"""Host-side MoE layer over libmoeb200.so: the HBM-resident precision classes, the residency mirror
+and one call per layer forward (moeb_layer_forward), mirroring what LLapis's build_moe_ffn +
+moe_dual hook compute for one Gemma-4 MoE layer (third_party/llama/src/llama-graph.cpp:1507-1851).
+
+PyTorch provides device memory and streams only; all compute is the library's sm_100a kernels.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import capi
+from .capi import IQ2_S, IQ4_NL, Q4_K, Q5_0
+
+READY = 2  # moert_slot_state READY (moert/include/moert/policy.h:46)
+
+
+@dataclass
+class HostLayer:
+    """Quantised weights of one layer in host memory (ggml layouts)."""
+    d_model: int
+    n_ff: int
+    n_expert: int
+    top_k: int
+    w_router: np.ndarray                  # f32 [E, d]
+    b_router: np.ndarray | None           # f32 [E]
+    hot_ids: np.ndarray                   # i32 [K] experts held by the hot class, slot order
+    hot_gu: np.ndarray | None             # u8 [K, 2nff, row]
+    hot_down: np.ndarray | None           # u8 [K, d, row]
+    cold_gu: np.ndarray | None            # u8 [E, 2nff, row]
+    cold_down: np.ndarray | None
+    hot_type_gu: int = Q4_K
+    hot_type_down: int = Q5_0
+    cold_type_gu: int = IQ2_S
+    cold_type_down: int = IQ4_NL
+    s_hot: np.ndarray | None = None       # f32 [K]
+    s_cold: np.ndarray | None = None      # f32 [E]
+
+    @property
+    def n_slots(self) -> int:
+        return int(len(self.hot_ids))
+
+    def residency(self):
+        """exp_slot / slot_exp / slot_state of the moe_dual mirror for this layout."""
+        exp_slot = np.full(self.n_expert, -1, np.int32)
+        exp_slot[self.hot_ids] = np.arange(self.n_slots, dtype=np.int32)
+        return exp_slot, self.hot_ids.astype(np.int32), np.full(self.n_slots, READY, np.int32)
+
+    def hot_mask(self) -> np.ndarray:
+        m = np.zeros(self.n_expert, bool)
+        m[self.hot_ids] = True
+        return m
+
+    def expert_bytes(self, e: int) -> int:
+        """Weight bytes a forward reads for expert e (gate_up + down of its class)."""
+        if self.hot_mask()[e]:
+            return (2 * self.n_ff * capi.row_size(self.hot_type_gu, self.d_model)
+                    + self.d_model * capi.row_size(self.hot_type_down, self.n_ff))
+        return (2 * self.n_ff * capi.row_size(self.cold_type_gu, self.d_model)
+                + self.d_model * capi.row_size(self.cold_type_down, self.n_ff))
+
+
+def _dev(a, device):
+    return None if a is None else torch.from_numpy(np.ascontiguousarray(a)).to(device)
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+class MoELayer:
+    """One MoE layer resident on a CUDA device."""
+
+    def __init__(self, host: HostLayer, device: str | torch.device = "cuda"):
+        self.host = host
+        self.device = torch.device(device)
+        capi.lib()
+        with torch.cuda.device(self.device):
+            capi.check(capi.lib().moeb_init())
+        h = host
+        exp_slot, slot_exp, slot_state = h.residency()
+        self.t = dict(
+            w_router=_dev(h.w_router.astype(np.float32), self.device),
+            b_router=_dev(None if h.b_router is None else h.b_router.astype(np.float32), self.device),
+            hot_gu=_dev(h.hot_gu, self.device), hot_down=_dev(h.hot_down, self.device),
+            cold_gu=_dev(h.cold_gu, self.device), cold_down=_dev(h.cold_down, self.device),
+            s_hot=_dev(h.s_hot, self.device), s_cold=_dev(h.s_cold, self.device),
+            exp_slot=_dev(exp_slot, self.device) if h.n_slots else None,
+            slot_exp=_dev(slot_exp, self.device) if h.n_slots else None,
+            slot_state=_dev(slot_state, self.device) if h.n_slots else None,
+        )
+        t = self.t
+        L = capi.Layer()
+        L.d_model, L.n_ff, L.n_expert, L.top_k = h.d_model, h.n_ff, h.n_expert, h.top_k
+        L.w_router, L.b_router = _ptr(t["w_router"]), _ptr(t["b_router"])
+        L.hot = capi.Pool(h.hot_type_gu, h.hot_type_down, h.n_slots if h.hot_gu is not None else 0, 0,
+                          _ptr(t["hot_gu"]), _ptr(t["hot_down"]), _ptr(t["s_hot"]))
+        L.cold = capi.Pool(h.cold_type_gu, h.cold_type_down, h.n_expert if h.cold_gu is not None else 0, 0,
+                           _ptr(t["cold_gu"]), _ptr(t["cold_down"]), _ptr(t["s_cold"]))
+        L.exp_slot, L.slot_exp, L.slot_state = _ptr(t["exp_slot"]), _ptr(t["slot_exp"]), _ptr(t["slot_state"])
+        self.c = L
+        self._ws = None
+
+    def workspace_bytes(self, n_tokens: int) -> int:
+        return int(capi.lib().moeb_layer_workspace_size(C.byref(self.c), n_tokens))
+
+    def workspace(self, n_tokens: int) -> torch.Tensor:
+        need = self.workspace_bytes(n_tokens)
+        if self._ws is None or self._ws.numel() < need:
+            self._ws = torch.empty(need, dtype=torch.uint8, device=self.device)
+        return self._ws
+
+    def forward(self, x: torch.Tensor, out: torch.Tensor | None = None, aux: dict | None = None,
+                stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+        """x: f32 [T, d_model] on the layer's device. aux: optional dict of preallocated device tensors
+        among logits [T,E], ids [T,k] i32, weights [T,k], counts [E], offsets [E+1], perm [T*k],
+        gate_up [T*k, 2nff], down [T*k, d]."""
+        assert x.dtype == torch.float32 and x.is_contiguous() and x.device == self.device
+        T = x.shape[0]
+        if out is None:
+            out = torch.empty_like(x)
+        ws = self.workspace(T)
+        s = stream if stream is not None else torch.cuda.current_stream(self.device)
+        a = None
+        if aux:
+            a = capi.LayerAux(*[_ptr(aux.get(n)) for n, _ in capi.LayerAux._fields_])
+        rc = capi.lib().moeb_layer_forward(C.byref(self.c), x.data_ptr(), T, out.data_ptr(),
+                                           C.byref(a) if a is not None else None, ws.data_ptr(), ws.numel(),
+                                           s.cuda_stream)
+        capi.check(rc)
+        return out
+
+    __call__ = forward
+
+    def device_error(self) -> int:
+        s = torch.cuda.current_stream(self.device)
+        return int(capi.lib().moeb_device_error(s.cuda_stream))

@@ -1,0 +1,101 @@
+"""CPU: the restated oracle is pinned against the reference's golden fixtures (and against the
+reference build itself when oracle/_ref is present)."""
+import numpy as np
+import pytest
+
+from conftest import assert_layer_close, host_layer, near_tie_tokens, sha, spec_of
+from oracle.oracle import IQ2_S, IQ4_NL, Q4_K, Q5_0, Q8_0, Q8_K
+
+
+def test_tables_match_reference(golden, port):
+    import ctypes as C
+    port.lib.oracle_iq2s_grid.restype = C.POINTER(C.c_uint64)
+    port.lib.oracle_iq4nl_values.restype = C.POINTER(C.c_int8)
+    grid = np.ctypeslib.as_array(port.lib.oracle_iq2s_grid(), shape=(1024,))
+    kv = np.ctypeslib.as_array(port.lib.oracle_iq4nl_values(), shape=(16,))
+    assert np.array_equal(grid, golden["iq2s_grid"])
+    assert np.array_equal(kv, golden["iq4nl_values"])
+
+
+@pytest.mark.parametrize("t,n", [(Q4_K, 512), (IQ2_S, 512), (Q5_0, 64), (IQ4_NL, 64)])
+def test_dequant_bit_exact(golden, port, t, n):
+    src, want = golden[f"deq_{t}_src"], golden[f"deq_{t}_f32"]
+    for i in range(len(src)):
+        got = port.dequantize(t, src[i], n)
+        assert np.array_equal(got.view(np.uint32), want[i].view(np.uint32)), f"row {i}"
+
+
+@pytest.mark.parametrize("vdt", [Q8_K, Q8_0])
+def test_activation_quant_bit_exact(golden, port, vdt):
+    x, want = golden[f"act_{vdt}_x"], golden[f"act_{vdt}_q"]
+    for i in range(len(x)):
+        assert np.array_equal(port.quantize_act(vdt, x[i]), want[i]), f"row {i}"
+
+
+def test_gelu_table(golden, port):
+    t = port.gelu_table()
+    t[np.isnan(t.view(np.float16))] = 0x7E00      # NaN payloads carry no meaning
+    assert sha(t) == str(golden["gelu_table_sha"])
+
+
+def test_topk_ties_lowest_index(port):
+    v = np.array([0.5, 0.9, 0.9, 0.1, 0.9, 0.2], np.float32)
+    assert port.topk(v, 4).tolist() == [1, 2, 4, 0]
+
+
+def test_geglu_branches(port):
+    g = np.array([-20, -10, -9.99, 0.0, 1.0, 9.99, 10, 30], np.float32)
+    u = np.full_like(g, 2.0)
+    y = port.geglu(g, u)
+    assert y[0] == 0 and y[1] == 0
+    assert y[6] == 20 and y[7] == 60
+    assert abs(y[4] - 2 * 0.8413) < 2e-3
+
+
+def test_mini_layer_matches_reference_fixture(golden, port):
+    host = host_layer("mini_mixed")
+    for n in ("hot_gu", "hot_down", "cold_gu", "cold_down"):
+        assert sha(getattr(host, n)) == str(golden[f"mini_sha_{n}"]), f"quantised {n} differs from the reference quantiser"
+    res = port.moe_layer(spec_of(host, golden["mini_x"]))
+    assert np.array_equal(res["ids"], golden["mini_ids"])
+    np.testing.assert_allclose(res["logits"], golden["mini_logits"], rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(res["weights"], golden["mini_weights"], rtol=1e-5, atol=1e-7)
+    assert_layer_close(res["gate_up"], golden["mini_gate_up"], tol=1e-5)
+    assert_layer_close(res["down"], golden["mini_down"], tol=1e-4)
+    assert_layer_close(res["out"], golden["mini_out"], tol=1e-4)
+
+
+@pytest.mark.parametrize("name", ["decode_t4_mixed"])
+def test_real_shape_layer_matches_reference_fixture(golden, port, name):
+    host = host_layer(name)
+    for n in ("hot_gu", "hot_down", "cold_gu", "cold_down"):
+        want = str(golden[f"{name}_sha_{n}"])
+        got = sha(getattr(host, n)) if getattr(host, n) is not None else ""
+        assert got == want, f"quantised {n} differs from the reference quantiser"
+    x = golden[f"{name}_x"]
+    res = port.moe_layer(spec_of(host, x), want=("logits", "ids", "weights"))
+    ties = set(near_tie_tokens(golden[f"{name}_logits"], host.top_k).tolist())
+    for t in range(x.shape[0]):
+        if t not in ties:
+            assert np.array_equal(res["ids"][t], golden[f"{name}_ids"][t]), f"token {t}"
+    assert_layer_close(res["out"], golden[f"{name}_out"], tol=1e-4)
+
+
+def test_port_vs_reference_random_layers(ref, port):
+    """Fresh seeded layers through both oracles (needs oracle/_ref)."""
+    from oracle import LayerSpec
+    rng = np.random.default_rng(5)
+    d, nff, E, k, K = 512, 64, 32, 4, 5
+    wg = rng.normal(0, 0.02, (E, 2 * nff, d)).astype(np.float32)
+    wd = rng.normal(0, 0.02, (E, d, nff)).astype(np.float32)
+    spec = LayerSpec(d, nff, E, k, x=rng.normal(0, 1, (6, d)).astype(np.float32),
+                     w_router=rng.normal(0, 0.02, (E, d)).astype(np.float32),
+                     n_slots=K, exp_slot=np.full(E, -1, np.int32), slot_exp=np.arange(K, dtype=np.int32), slot_state=np.array([2, 2, 1, 2, 2], np.int32),
+                     hot_gu=ref.quantize(Q4_K, wg[:K]), hot_down=ref.quantize(Q5_0, wd[:K]),
+                     cold_gu=ref.quantize(IQ2_S, wg), cold_down=ref.quantize(IQ4_NL, wd),
+                     s_cold=rng.uniform(0.5, 2, E).astype(np.float32), s_hot=rng.uniform(0.5, 2, K).astype(np.float32))
+    spec.exp_slot = np.full(E, -1, np.int32)
+    spec.exp_slot[:K] = np.arange(K)          # slot 2 is FILLING: expert 2 stays cold
+    a, b = ref.moe_layer(spec, n_threads=4), port.moe_layer(spec)
+    assert np.array_equal(a["ids"], b["ids"])
+    assert_layer_close(b["out"], a["out"], tol=1e-4)
