@@ -28,7 +28,29 @@ enum : int32_t { ERR_MBAR_TIMEOUT = 1, ERR_BAD_EXPERT = 2, ERR_CAPACITY = 4 };
 
 // ---------------------------------------------------------------- small device helpers
 __device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
-__device__ __forceinline__ uint16_t f2h_rn(float f) { return __half_as_ushort(__float2half_rn(f)); }
+// binary32 -> binary16, round to nearest even, in integer arithmetic (the bit pattern is used as a
+// table index and as stored block bytes, so it is built explicitly rather than through a half type)
+__device__ __forceinline__ uint16_t f2h_rn(float f) {
+    const uint32_t x = __float_as_uint(f);
+    const uint32_t sign = (x >> 16) & 0x8000u;
+    const uint32_t ax = x & 0x7fffffffu;
+    if (ax >= 0x7f800000u) return (uint16_t)(sign | (ax == 0x7f800000u ? 0x7c00u : (0x7e00u | ((ax >> 13) & 0x1ffu))));
+    if (ax >= 0x477ff000u) return (uint16_t)(sign | 0x7c00u);       // rounds to >= 65520: infinity
+    if (ax < 0x38800000u) {                                          // subnormal half (unit 2^-24) or zero
+        const uint32_t e = ax >> 23;
+        if (e < 102u) return (uint16_t)sign;
+        const uint32_t m = (ax & 0x7fffffu) | 0x800000u;
+        const uint32_t sh = 126u - e;                                // 14..24
+        uint32_t q = m >> sh;
+        const uint32_t rem = m & ((1u << sh) - 1u), half = 1u << (sh - 1u);
+        if (rem > half || (rem == half && (q & 1u))) ++q;
+        return (uint16_t)(sign | q);
+    }
+    uint32_t h = (((ax >> 23) - 112u) << 10) | ((ax >> 13) & 0x3ffu);
+    const uint32_t rem = ax & 0x1fffu;
+    if (rem > 0x1000u || (rem == 0x1000u && (h & 1u))) ++h;         // carries into the exponent as needed
+    return (uint16_t)(sign | h);
+}
 
 __device__ __forceinline__ uint16_t ld_u16(const uint8_t *p) {
     return (uint16_t)p[0] | ((uint16_t)p[1] << 8);

@@ -204,7 +204,7 @@ __device__ void route_tokens(const RouteSrc &r, RouteSmem &rs, int tid) {
 // ggml-cpu's mul_mat_id, ggml-cpu.c:1613-1626), plus the unique-expert list with each expert's
 // precision class and cumulative weight bytes for the work split.
 __device__ void dispatch_pairs(const RouteSrc &r, const Residency &res, const PoolView &hot, const PoolView &cold,
-                               int d_in, int d_out, RouteSmem &rs, int tid) {
+                               int d_in, int d_out, RouteSmem &rs, int tid, bool check_pools) {
     const int P = r.T * r.k;
     for (int e = tid; e < r.E; e += kThreads) rs.cnt[e] = 0;
     __syncthreads();
@@ -230,8 +230,7 @@ __device__ void dispatch_pairs(const RouteSrc &r, const Residency &res, const Po
             }
             if (e < r.E) rs.off[e] = base + incl - c;
             base += __shfl_sync(0xffffffffu, incl, 31);
-            const bool has = c > 0;
-            const unsigned m = __ballot_sync(0xffffffffu, has);
+            bool has = c > 0;
             long long cost = 0;
             int cls = 1, widx = e;
             if (has) {
@@ -239,8 +238,17 @@ __device__ void dispatch_pairs(const RouteSrc &r, const Residency &res, const Po
                     const int s = res.exp_slot[e];
                     if (s >= 0 && s < res.n_slots && res.slot_state[s] == 2 && res.slot_exp[s] == e) { cls = 0; widx = s; }
                 }
-                cost = (long long)d_out * row_bytes(cls == 0 ? hot.type : cold.type, d_in);
+                const PoolView &pv = cls == 0 ? hot : cold;
+                // an expert whose class pool is absent (or whose table entry is not 16-byte aligned)
+                // is reported and left out of the work split instead of being read
+                const bool ok = !check_pools ||
+                                (pv.ptrs ? ((reinterpret_cast<uintptr_t>(pv.ptrs[widx]) & 15u) == 0 && pv.ptrs[widx])
+                                         : (pv.w != nullptr && widx < pv.n));
+                if (!ok) { atomicOr(&g_error, ERR_BAD_EXPERT); has = false; }
+                cost = (long long)d_out * row_bytes(pv.type, d_in);
             }
+            const unsigned m = __ballot_sync(0xffffffffu, has);
+            if (!has) cost = 0;
             long long cincl = cost;
 #pragma unroll
             for (int o = 1; o < 32; o <<= 1) {
@@ -582,7 +590,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(GemvParams p) {
     // ---- routing and dispatch (every CTA, identical results)
     route_tokens(p.route, rs, tid);
     __syncthreads();
-    dispatch_pairs(p.route, p.res, p.hot, p.cold, p.d_in, p.d_out, rs, tid);
+    dispatch_pairs(p.route, p.res, p.hot, p.cold, p.d_in, p.d_out, rs, tid, true);
     const int T = p.route.T, k = p.route.k, P = T * k;
     if (blockIdx.x == 0) {
         for (int i = tid; i < P; i += kThreads) {
@@ -648,7 +656,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(GemvParams p) {
     for (int f = g0; f < g1;) {
         const StagePlan st = next_stage(f, g1, gpe, stage_groups);
         const int e = rs.uexp[st.u], cls = rs.ucls[st.u], widx = rs.uwidx[st.u];
-        const int po = rs.off[e], n = rs.cnt[e];
+        const int po = rs.off[e];
+        int n = rs.cnt[e];
+        if (p.kind != 0 && n > T) {
+            // the down activation buffer holds one pair per token of an expert; an expert repeated
+            // within a token's routes is reported and its extra pairs are not computed
+            if (tid == 0) atomicOr(&g_error, ERR_CAPACITY);
+            n = T;
+        }
         if (p.kind != 0 && st.u != cur_u) {
             // Q8_0 activations of this expert's routed pairs: slot i <- pair perm[po + i]
             for (int item = warp; item < n * nb; item += kWarps) {
@@ -794,7 +809,7 @@ __global__ void __launch_bounds__(kThreads, 1) route_only_kernel(RouteSrc r, int
     __syncthreads();
     const Residency none = {0, nullptr, nullptr, nullptr};
     const PoolView pv = {nullptr, T_Q4_K, 0, nullptr};
-    dispatch_pairs(r, none, pv, pv, QK_K, kGroupRows, rs, tid);
+    dispatch_pairs(r, none, pv, pv, QK_K, kGroupRows, rs, tid, false);
     const int P = r.T * r.k;
     for (int i = tid; i < P; i += kThreads) {
         if (ids) ids[i] = rs.ids[i];
@@ -899,7 +914,7 @@ __global__ void __launch_bounds__(kThreads) quant_act_kernel(int32_t vdt, const 
             __syncwarp();
             uint8_t *blk = out + b * B_Q8_0;
             blk[2 + lane] = (uint8_t)qs[warp][lane];
-            if (lane == 0) { const uint16_t h = f2h_rn(dd[warp]); blk[0] = h & 0xff; blk[1] = h >> 8; }
+            if (lane == 0) *reinterpret_cast<uint16_t *>(blk) = f2h_rn(dd[warp]);   // blocks sit at even offsets
             __syncwarp();
         }
     }

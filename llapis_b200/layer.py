@@ -77,6 +77,8 @@ class MoELayer:
     def __init__(self, host: HostLayer, device: str | torch.device = "cuda"):
         self.host = host
         self.device = torch.device(device)
+        if self.device.index is None:
+            self.device = torch.device(self.device.type, torch.cuda.current_device())
         capi.lib()
         with torch.cuda.device(self.device):
             capi.check(capi.lib().moeb_init())
