@@ -97,6 +97,29 @@ size_t moeb_layer_workspace_size(const moeb_layer *L, int32_t n_tokens);
 int moeb_layer_forward(const moeb_layer *L, const float *x, int32_t n_tokens, float *out,
                        const moeb_layer_aux *aux, void *workspace, size_t workspace_bytes, void *stream);
 
+/* Allocation-free variant of moeb_layer_forward. No counterpart in the reference.
+ *
+ * For callers that cannot allocate device memory where they call the layer: hosts whose own
+ * memory manager has reserved all of HBM up front and forbids stray allocations (an inference
+ * server carving the device into its own pools), plug-ins loaded into such a process that must not
+ * disturb its allocator, and latency-critical paths that cannot afford cudaMalloc's implicit
+ * device synchronisation. The caller passes only inputs and outputs; the workspace lives in a
+ * library-owned static device array of MOEB_STATIC_SCRATCH_BYTES, held by every GPU that loads
+ * the library until the process exits. It allocates no device memory and calls no allocating
+ * library routine.
+ *
+ * Limits and rules:
+ *  - a layer whose workspace (moeb_layer_workspace_size, which tops out at one 16-token chunk)
+ *    exceeds MOEB_STATIC_SCRATCH_BYTES is rejected with MOEB_ESPACE (the Gemma-4 26B-A4B layer
+ *    needs about 2.2 MB, for any n_tokens);
+ *  - the first call on a device does one-time set-up there (format tables, the device address of
+ *    the static array); make that first call before any stream capture on that device;
+ *  - all calls share the one array per device and it keeps the last call's contents: calls that
+ *    overlap on the GPU (different streams, or different host threads, on the same device) race.
+ *    Nothing in it needs clearing between calls; every byte a forward reads it writes first. */
+#define MOEB_STATIC_SCRATCH_BYTES (4u << 20)
+int moeb_layer_forward_static(const moeb_layer *L, const float *x, int32_t n_tokens, float *out, void *stream);
+
 /* Binds the weight pools that moert_ffn_moe(il, kind) reads (the reference trampoline lends its
  * w_hot / w_cold tensors through the mm vtable instead, moe-dual.cu:74-94). hot/cold: device
  * pools in ggml layout [n][d_out][row(d_in)] of type hot_type / cold_type. */

@@ -48,6 +48,7 @@ SIGNATURES = {
     "moeb_layer_workspace_size": (C.c_size_t, [C.POINTER(Layer), C.c_int32]),
     "moeb_layer_forward": (C.c_int, [C.POINTER(Layer), C.c_void_p, C.c_int32, C.c_void_p, C.POINTER(LayerAux),
                                      C.c_void_p, C.c_size_t, C.c_void_p]),
+    "moeb_layer_forward_static": (C.c_int, [C.POINTER(Layer), C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p]),
     "moeb_bind_pools": (C.c_int, [C.c_int32, C.c_int32, C.c_void_p, C.c_int32, C.c_int32, C.c_void_p, C.c_int32,
                                   C.c_int32]),
     "moeb_router_topk": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p]),

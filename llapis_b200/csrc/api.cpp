@@ -167,6 +167,16 @@ PoolView pool_view(const moeb_pool &pl, bool gate_up) {
 
 }  // namespace
 
+int moeb::set_last_error(int code, const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_msg = buf;
+    return code;
+}
+
 // ================================================================= moeb200.h
 extern "C" int moeb_init(void) { return ensure_device(); }
 

@@ -18,6 +18,9 @@
 #include "common.cuh"
 
 #include <algorithm>
+#include <mutex>
+
+#include "moeb200.h"
 
 namespace moeb {
 
@@ -1003,4 +1006,48 @@ cudaError_t read_and_clear_error(int32_t *out, cudaStream_t s) {
     return cudaStreamSynchronize(s);
 }
 
+
+// ------------------------------------------------------------------ allocation-free layer entry
+// moeb_layer_forward_static(): the whole-layer forward with its workspace in this module-scope
+// array instead of caller memory, for hosts that cannot allocate device memory on the call path
+// (see include/moeb200.h). Every device that loads the library holds this array until exit.
+static __device__ __align__(256) uint8_t g_static_scratch[MOEB_STATIC_SCRATCH_BYTES];
+
+namespace {
+std::mutex g_static_mu;
+void *g_static_addr[64];   // device address of g_static_scratch, per device, resolved once
+}  // namespace
+
 }  // namespace moeb
+
+extern "C" int moeb_layer_forward_static(const moeb_layer *L, const float *x, int32_t n_tokens, float *out,
+                                         void *stream) {
+    using namespace moeb;
+    const size_t need = moeb_layer_workspace_size(L, n_tokens);
+    if (n_tokens > 0 && need > MOEB_STATIC_SCRATCH_BYTES)
+        return set_last_error(MOEB_ESPACE, "moeb_layer_forward_static: this layer needs a %zu-byte workspace; the "
+                                           "static scratch holds %u bytes (use moeb_layer_forward)",
+                              need, (unsigned)MOEB_STATIC_SCRATCH_BYTES);
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess || dev < 0 || dev >= 64)
+        return set_last_error(MOEB_ENODEV, "moeb_layer_forward_static: no usable CUDA device");
+    void *scratch = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(g_static_mu);
+        if (!g_static_addr[dev]) {
+            // In host code g_static_scratch names a host-side shadow, not device memory: the kernels
+            // need the device address, looked up once per device with that device current.
+            void *p = nullptr;
+            e = cudaGetSymbolAddress(&p, g_static_scratch);
+            if (e != cudaSuccess || !p)
+                return set_last_error(MOEB_ECUDA, "moeb_layer_forward_static: cudaGetSymbolAddress failed: %s",
+                                      cudaGetErrorString(e));
+            g_static_addr[dev] = p;
+        }
+        scratch = g_static_addr[dev];
+    }
+    // Every byte of the workspace the forward reads is written earlier in the same forward, so the
+    // previous call's contents need no clearing.
+    return moeb_layer_forward(L, x, n_tokens, out, nullptr, scratch, MOEB_STATIC_SCRATCH_BYTES, stream);
+}

@@ -133,5 +133,7 @@ cudaError_t launch_quant_act(int32_t vdt, const float *x, void *dst, int64_t row
 // device state: format tables, GELU table upload, error word
 cudaError_t upload_gelu_table(const uint16_t *host_table, cudaStream_t s);
 cudaError_t read_and_clear_error(int32_t *out, cudaStream_t s);
+// records the message moeb_last_error() returns; returns `code`
+int set_last_error(int code, const char *fmt, ...);
 
 }  // namespace moeb
