@@ -109,9 +109,9 @@ int moeb_layer_forward(const moeb_layer *L, const float *x, int32_t n_tokens, fl
  * library routine.
  *
  * Limits and rules:
- *  - a layer whose workspace (moeb_layer_workspace_size, which tops out at one 16-token chunk)
+ *  - a layer whose workspace (moeb_layer_workspace_size, which tops out at one 8-token chunk)
  *    exceeds MOEB_STATIC_SCRATCH_BYTES is rejected with MOEB_ESPACE (the Gemma-4 26B-A4B layer
- *    needs about 2.2 MB, for any n_tokens);
+ *    needs about 1.1 MB, for any n_tokens);
  *  - the first call on a device does one-time set-up there (format tables, the device address of
  *    the static array); make that first call before any stream capture on that device;
  *  - all calls share the one array per device and it keeps the last call's contents: calls that

@@ -122,18 +122,22 @@ int check_layer(const moeb_layer *L) {
     if (L->hot.n <= 0 && L->cold.n <= 0) return fail(MOEB_EINVAL, "no expert pool");
     if (L->cold.n > 0 && L->cold.n < L->n_expert)
         return fail(MOEB_EINVAL, "cold pool holds %d experts, layer has %d", L->cold.n, L->n_expert);
+    if (fused_smem_bytes(L->d_model, L->n_ff) > 227 * 1024)
+        return fail(MOEB_EINVAL, "layer shape d_model=%d n_ff=%d needs more shared memory than an SM has", L->d_model,
+                    L->n_ff);
     int rc = check_pool(L->hot, L->d_model, L->n_ff, "hot");
     if (rc) return rc;
     return check_pool(L->cold, L->d_model, L->n_ff, "cold");
 }
 
-// workspace carve for one chunk of up to kMaxDecodeT tokens
+// workspace carve for one chunk of up to kFusedTokens tokens
 struct LayerWs {
     float *logits;
     uint8_t *xq;
     float *h, *y;
     int32_t *ids, *cnt, *off, *perm;
     float *w;
+    uint32_t *sync;
     size_t bytes;
 };
 
@@ -151,6 +155,7 @@ LayerWs carve(const moeb_layer *L, int T, uint8_t *base) {
     w.cnt = (int32_t *)take(sizeof(int32_t) * L->n_expert);
     w.off = (int32_t *)take(sizeof(int32_t) * (L->n_expert + 1));
     w.perm = (int32_t *)take(sizeof(int32_t) * P);
+    w.sync = (uint32_t *)take(sizeof(uint32_t) * fused_sync_words(T, L->d_model));
     w.bytes = o;
     return w;
 }
@@ -194,7 +199,7 @@ extern "C" int32_t moeb_device_error(void *stream) {
 
 extern "C" size_t moeb_layer_workspace_size(const moeb_layer *L, int32_t n_tokens) {
     if (!L || n_tokens <= 0) return 0;
-    const int T = n_tokens < kMaxDecodeT ? n_tokens : kMaxDecodeT;
+    const int T = n_tokens < kFusedTokens ? n_tokens : kFusedTokens;
     return carve(L, T, nullptr).bytes;
 }
 
@@ -218,67 +223,39 @@ extern "C" int moeb_layer_forward(const moeb_layer *L, const float *x, int32_t n
     const int d = L->d_model, k = L->top_k, E = L->n_expert;
     const Residency res = {L->hot.n, L->exp_slot, L->slot_exp, L->slot_state};
 
-    // tokens are independent: longer batches run as consecutive chunks of the decode path
-    for (int t0 = 0; t0 < n_tokens; t0 += kMaxDecodeT) {
-        const int T = n_tokens - t0 < kMaxDecodeT ? n_tokens - t0 : kMaxDecodeT;
+    // tokens are independent: longer batches run as consecutive chunks of the fused decode kernel
+    for (int t0 = 0; t0 < n_tokens; t0 += kFusedTokens) {
+        const int T = n_tokens - t0 < kFusedTokens ? n_tokens - t0 : kFusedTokens;
         const int P = T * k;
         LayerWs w = carve(L, T, (uint8_t *)workspace);
-
-        RouterParams rp{};
-        rp.w_router = L->w_router;
-        rp.b_router = L->b_router;
-        rp.x = x + (size_t)t0 * d;
-        rp.T = T;
-        rp.E = E;
-        rp.d = d;
-        rp.logits = w.logits;
-        rp.xq = w.xq;
-        rp.xq_stride = xq_stride_bytes(d);
-        cudaError_t e = launch_router(rp, s, false);
-        if (e != cudaSuccess) return cuda_fail(e, "router launch");
-
-        GemvParams g{};
-        g.route = {w.logits, nullptr, 0, T, E, k};
-        g.res = res;
-        g.hot = pool_view(L->hot, true);
-        g.cold = pool_view(L->cold, true);
-        g.d_in = d;
-        g.d_out = 2 * L->n_ff;
-        g.xq = w.xq;
-        g.xq_stride = xq_stride_bytes(d);
-        g.kind = 0;
-        g.y = w.h;
-        g.ids_out = w.ids;
-        g.w_out = w.w;
-        g.cnt_out = w.cnt;
-        g.off_out = w.off;
-        g.perm_out = w.perm;
-        e = launch_gemv(g, s, true, n_sms);
-        if (e != cudaSuccess) return cuda_fail(e, "gate_up launch");
-
-        GemvParams dn{};
-        dn.route = g.route;
-        dn.res = res;
-        dn.hot = pool_view(L->hot, false);
-        dn.cold = pool_view(L->cold, false);
-        dn.d_in = L->n_ff;
-        dn.d_out = d;
-        dn.h = w.h;
-        dn.kind = 1;
-        dn.y = w.y;
-        dn.apply_scale = 1;
-        e = launch_gemv(dn, s, true, n_sms);
-        if (e != cudaSuccess) return cuda_fail(e, "down launch");
-
-        CombineParams cp{};
-        cp.y = w.y;
-        cp.w = w.w;
-        cp.T = T;
-        cp.k = k;
-        cp.d = d;
-        cp.out = out + (size_t)t0 * d;
-        e = launch_combine(cp, s, true);
-        if (e != cudaSuccess) return cuda_fail(e, "combine launch");
+        FusedArgs f{};
+        f.w_router = L->w_router;
+        f.b_router = L->b_router;
+        f.x = x + (size_t)t0 * d;
+        f.T = T;
+        f.E = E;
+        f.d = d;
+        f.k = k;
+        f.nff = L->n_ff;
+        f.res = res;
+        f.hot_gu = pool_view(L->hot, true);
+        f.cold_gu = pool_view(L->cold, true);
+        f.hot_dn = pool_view(L->hot, false);
+        f.cold_dn = pool_view(L->cold, false);
+        f.logits = w.logits;
+        f.xq = w.xq;
+        f.xq_stride = xq_stride_bytes(d);
+        f.h = w.h;
+        f.y = w.y;
+        f.out = out + (size_t)t0 * d;
+        f.ids_out = w.ids;
+        f.w_out = w.w;
+        f.cnt_out = w.cnt;
+        f.off_out = w.off;
+        f.perm_out = w.perm;
+        f.sync = w.sync;
+        cudaError_t e = launch_fused(f, s, n_sms);
+        if (e != cudaSuccess) return cuda_fail(e, "fused decode layer launch");
 
         if (aux) {
             struct Cp { void *dst; const void *src; size_t n; } cps[] = {
@@ -294,7 +271,7 @@ extern "C" int moeb_layer_forward(const moeb_layer *L, const float *x, int32_t n
                 if (e != cudaSuccess) return cuda_fail(e, "aux copy");
             }
             // the dispatch outputs describe one chunk; they are reported for single-chunk calls
-            if (n_tokens <= kMaxDecodeT) {
+            if (n_tokens <= kFusedTokens) {
                 if (aux->counts) e = cudaMemcpyAsync(aux->counts, w.cnt, sizeof(int32_t) * E, cudaMemcpyDeviceToDevice, s);
                 if (e == cudaSuccess && aux->offsets)
                     e = cudaMemcpyAsync(aux->offsets, w.off, sizeof(int32_t) * (E + 1), cudaMemcpyDeviceToDevice, s);

@@ -1,20 +1,14 @@
-// Decode-size MoE layer kernels for sm_100a.
+// MoE-FFN layer kernels for sm_100a (the library's single device translation unit).
 //
-//   router_kernel   : router logits (f32 GEMV, one CTA per expert, fixed reduction order) + bias,
-//                     and the Q8_K quantisation of every token (extra CTAs).
-//   gemv_kernel     : grouped GEMV over the routed experts for one projection. Every CTA redoes
-//                     the routing (softmax / top-k / weights) and the dispatch (histogram, exclusive
-//                     scan, stable permutation) in shared memory from the logits, splits the routed
-//                     experts' weight bytes evenly over the grid, streams its share HBM -> shared
-//                     memory with bulk async copies (multi-stage mbarrier ring), and decodes the
-//                     quantised blocks in registers into integer dp4a dot products with per-block
-//                     float scaling — the same integer work as ggml-cpu's vec_dot kernels.
-//                     kind 0: gate_up (Q4_K / IQ2_S weights, Q8_K activations).
-//                     kind 1: down, activations = GeGLU(gate_up) quantised to Q8_0 in the prologue.
-//                     kind 2: down, activations given (the moert per-kind ABI).
-//   combine_kernel  : routing-weighted sum over the top-k slots in slot order.
-// Kernels are chained with programmatic dependent launch: the down GEMV starts streaming its
-// weights while the gate_up GEMV is still running, and only then waits for the gate_up outputs.
+//   fused_decode_kernel : the whole layer for up to 8 tokens in ONE persistent cooperative launch:
+//                         router logits, routing (softmax / top-k / weights) and dispatch
+//                         (histogram, exclusive scan, stable permutation), then the grouped
+//                         gate_up and down GEMVs streamed HBM -> shared memory by bulk async copies
+//                         and decoded in registers into integer dp4a dot products (the integer work
+//                         of ggml-cpu's vec_dot kernels), and the slot-ordered combine.
+//   gemv_kernel         : one projection of the moert per-kind ABI (moert_ffn_moe): the same
+//                         grouped GEMV with routes given by the caller.
+//   route_only / dequant / quant_act kernels : the inspection entry points of moeb200.h.
 #include "common.cuh"
 
 #include <algorithm>
@@ -82,59 +76,6 @@ __device__ void q8k_superblock_warp(const float *x, int8_t *qs, float *d_out, in
     if (lane == 0) *d_out = __fdiv_rn(1.f, iscale);
 }
 
-// ------------------------------------------------------------------ router
-__global__ void __launch_bounds__(kThreads) router_kernel(RouterParams p) {
-    // let the dependent GEMV grid start its table prologue while the router runs
-    pdl_launch_dependents();
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int b = blockIdx.x;
-    if (b < p.E) {
-        __shared__ float red[kMaxDecodeT][kWarps];
-        const int n4 = p.d / 4;
-        const float4 *w4 = reinterpret_cast<const float4 *>(p.w_router + (size_t)b * p.d);
-        float part[kMaxDecodeT];
-#pragma unroll
-        for (int t = 0; t < kMaxDecodeT; ++t) part[t] = 0.f;
-        for (int i = tid; i < n4; i += kThreads) {
-            const float4 w = __ldg(w4 + i);
-#pragma unroll
-            for (int t = 0; t < kMaxDecodeT; ++t) {
-                if (t < p.T) {
-                    const float4 xv = reinterpret_cast<const float4 *>(p.x + (size_t)t * p.d)[i];
-                    part[t] = fmaf(w.x, xv.x, part[t]);
-                    part[t] = fmaf(w.y, xv.y, part[t]);
-                    part[t] = fmaf(w.z, xv.z, part[t]);
-                    part[t] = fmaf(w.w, xv.w, part[t]);
-                }
-            }
-        }
-#pragma unroll
-        for (int t = 0; t < kMaxDecodeT; ++t) {
-            if (t < p.T) {
-                const float s = warp_sum(part[t]);
-                if (lane == 0) red[t][warp] = s;
-            }
-        }
-        __syncthreads();
-        if (tid < p.T) {
-            float s = 0.f;
-#pragma unroll
-            for (int w = 0; w < kWarps; ++w) s += red[tid][w];
-            if (p.b_router) s = __fadd_rn(s, p.b_router[b]);
-            p.logits[(size_t)tid * p.E + b] = s;
-        }
-    } else if (p.xq) {
-        const int t = b - p.E;
-        const int nsb = p.d / QK_K;
-        uint8_t *row = p.xq + (size_t)t * p.xq_stride;
-        int8_t *qs = reinterpret_cast<int8_t *>(row);
-        float *dd = reinterpret_cast<float *>(row + nsb * 256);
-        int16_t *bs = reinterpret_cast<int16_t *>(row + nsb * 256 + nsb * 4);
-        for (int sb = warp; sb < nsb; sb += kWarps)
-            q8k_superblock_warp(p.x + (size_t)t * p.d + sb * 256, qs + sb * 256, dd + sb, bs + sb * 16, lane);
-    }
-}
-
 // ------------------------------------------------------------------ routing + dispatch in a CTA
 struct RouteSmem {
     int32_t ids[kMaxPairs];
@@ -155,10 +96,10 @@ __device__ __forceinline__ bool better(float v, int i, float bv, int bi) {
 
 // softmax -> top-k (value desc, index asc) -> normalised weights, one warp per token
 // (llama-graph.cpp:1553-1648; the reference's argsort is unstable, so ties go to the lowest id).
-__device__ void route_tokens(const RouteSrc &r, RouteSmem &rs, int tid) {
+__device__ void route_tokens(const RouteSrc &r, RouteSmem &rs, int tid, int nwarps) {
     const int lane = tid & 31, warp = tid >> 5;
     const int per = r.E / 32;
-    for (int t = warp; t < r.T; t += kWarps) {
+    for (int t = warp; t < r.T; t += nwarps) {
         if (r.logits) {
             float v[kMaxE / 32];
 #pragma unroll
@@ -207,11 +148,11 @@ __device__ void route_tokens(const RouteSrc &r, RouteSmem &rs, int tid) {
 // ggml-cpu's mul_mat_id, ggml-cpu.c:1613-1626), plus the unique-expert list with each expert's
 // precision class and cumulative weight bytes for the work split.
 __device__ void dispatch_pairs(const RouteSrc &r, const Residency &res, const PoolView &hot, const PoolView &cold,
-                               int d_in, int d_out, RouteSmem &rs, int tid, bool check_pools) {
+                               int d_in, int d_out, RouteSmem &rs, int tid, int nthreads, bool check_pools) {
     const int P = r.T * r.k;
-    for (int e = tid; e < r.E; e += kThreads) rs.cnt[e] = 0;
+    for (int e = tid; e < r.E; e += nthreads) rs.cnt[e] = 0;
     __syncthreads();
-    for (int p = tid; p < P; p += kThreads) {
+    for (int p = tid; p < P; p += nthreads) {
         int e = rs.ids[p];
         if (e < 0 || e >= r.E) { atomicOr(&g_error, ERR_BAD_EXPERT); e = 0; rs.ids[p] = 0; }
         atomicAdd(&rs.cnt[e], 1);
@@ -276,7 +217,7 @@ __device__ void dispatch_pairs(const RouteSrc &r, const Residency &res, const Po
     }
     __syncthreads();
     // stable rank of each pair within its expert (P <= 256: quadratic is cheaper than a sort)
-    for (int p = tid; p < P; p += kThreads) {
+    for (int p = tid; p < P; p += nthreads) {
         const int e = rs.ids[p];
         int rank = 0;
         for (int q = 0; q < p; ++q) rank += rs.ids[q] == e;
@@ -285,158 +226,166 @@ __device__ void dispatch_pairs(const RouteSrc &r, const Residency &res, const Po
     __syncthreads();
 }
 
-// ------------------------------------------------------------------ per-format row dot products
-// Each returns, for one lane, its partial contribution to rows' dot products with up to
-// kTokChunk activation columns; the caller sums the lanes that share a row.
+// ------------------------------------------------------------------ shared-memory word access
+// Quantised blocks sit in shared memory at 2-byte aligned addresses (902-, 82-, 22- and 18-byte
+// strides). Runs of 32-bit words are read with aligned 32-bit loads and realigned with a funnel
+// shift; stage buffers carry 16 bytes of padding so the extra word read at the end stays inside.
+template <int N>
+__device__ __forceinline__ void lds_words_a2(const uint8_t *p, uint32_t (&w)[N]) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+    const uint32_t *base = reinterpret_cast<const uint32_t *>(a & ~uintptr_t(3));
+    const uint32_t sh = (uint32_t)(a & 2u) * 8u;   // 0 or 16
+    uint32_t raw[N + 1];
+#pragma unroll
+    for (int i = 0; i <= N; ++i) raw[i] = base[i];
+#pragma unroll
+    for (int i = 0; i < N; ++i) w[i] = __funnelshift_r(raw[i], raw[i + 1], sh);
+}
 
-// IQ2_S x Q8_K: lane owns 32-value sub-block j of every super-block (8 lanes per row).
-// Integer part per sub-block: ls0*sum(l=0,1) + ls1*sum(l=2,3) with ls = 1 + 2*nibble; float:
-// (d_w * d_x) per super-block; the caller scales the total by 0.125 (ggml-cpu/quants.c:947-990).
-__device__ __forceinline__ void dot_iq2s_lane(const uint8_t *row, int nsb, int j, const uint64_t *grid,
-                                              const uint8_t *act, int act_stride, const int *tok, int ntok,
-                                              float *acc) {
+__device__ __forceinline__ uint32_t byte_of(uint32_t w, int i) { return (w >> (8 * i)) & 0xffu; }
+
+// per-token activation rows in shared memory (pointers hoisted out of the block loops)
+struct ActQ8K {           // Q8_K row split as qs[nsb][256] | d[nsb] f32 | bsums[nsb][16] i16
+    const int8_t *qs;
+    const float *d;
+    const int16_t *bs;
+};
+struct ActQ80 {           // Q8_0 row split as qs[nb][32] | d[nb] f32 | qsum[nb] i32
+    const int8_t *qs;
+    const float *d;
+    const int *qsum;
+};
+
+// ------------------------------------------------------------------ per-format row dot products
+// Each lane accumulates its share of a row's dot products with NT activation columns; the lanes
+// sharing a row are summed by the caller. Integer work per block equals ggml-cpu's vec_dot kernels
+// (ggml-cpu/quants.c:314, :645, :947, :1203); only the float summation order differs.
+
+// IQ2_S x Q8_K, lane = 32-value sub-block j of every super-block (8 lanes per row):
+// sum over the 4 groups of 8 of (signed codebook magnitude * q8), scaled ls0 / ls1 = 1 + 2*nibble,
+// times d_w * d_x per super-block; the caller multiplies the total by 0.125.
+template <int NT>
+__device__ __forceinline__ void iq2s_lane(const uint8_t *row, int nsb, int j, const uint64_t *grid,
+                                          const ActQ8K (&x)[NT], float (&acc)[NT]) {
+#pragma unroll 1
     for (int sb = 0; sb < nsb; ++sb) {
         const uint8_t *blk = row + sb * B_IQ2_S;
-        const float dw = h2f(ld_u16(blk));
-        const uint32_t qs4 = ld_u32_a2(blk + 2 + 4 * j);
-        const uint32_t sg4 = ld_u32_a2(blk + 34 + 4 * j);
-        const uint32_t qh = blk[66 + j];
-        const uint32_t sc = blk[74 + j];
+        const float dw = h2f(*reinterpret_cast<const uint16_t *>(blk));
+        uint32_t qs4[1], sg4[1];
+        lds_words_a2<1>(blk + 2 + 4 * j, qs4);
+        lds_words_a2<1>(blk + 34 + 4 * j, sg4);
+        const uint32_t qh = blk[66 + j], sc = blk[74 + j];
         int wv[8];
 #pragma unroll
         for (int l = 0; l < 4; ++l) {
-            const uint32_t gi = ((qs4 >> (8 * l)) & 0xffu) | (((qh >> (2 * l)) & 3u) << 8);
+            const uint32_t gi = byte_of(qs4[0], l) | (((qh >> (2 * l)) & 3u) << 8);
             const uint64_t g = grid[gi];
-            const uint32_t s = (sg4 >> (8 * l)) & 0xffu;
+            const uint32_t s = byte_of(sg4[0], l);
             const uint32_t c0 = ((s & 15u) * 0x00204081u) & 0x01010101u;
             const uint32_t c1 = ((s >> 4) * 0x00204081u) & 0x01010101u;
-            // negate the flagged bytes: (w ^ 0xff) + 1 == -w, and magnitudes >= 8 never carry
+            // negate flagged bytes: (w ^ 0xff) + 1 == -w; magnitudes are >= 8, so nothing carries
             wv[2 * l] = (int)(((uint32_t)g ^ (c0 * 0xffu)) + c0);
             wv[2 * l + 1] = (int)(((uint32_t)(g >> 32) ^ (c1 * 0xffu)) + c1);
         }
         const int ls0 = 1 + 2 * (int)(sc & 15u), ls1 = 1 + 2 * (int)(sc >> 4);
 #pragma unroll
-        for (int c = 0; c < kTokChunk; ++c) {
-            if (c < ntok) {
-                const Q8KView xv = q8k_view(act + (size_t)tok[c] * act_stride, nsb);
-                const int4 *q = reinterpret_cast<const int4 *>(xv.qs + sb * 256 + 32 * j);
-                const int4 qa = q[0], qb = q[1];
-                int s0 = dp4a(wv[0], qa.x, 0);
-                s0 = dp4a(wv[1], qa.y, s0);
-                s0 = dp4a(wv[2], qa.z, s0);
-                s0 = dp4a(wv[3], qa.w, s0);
-                int s1 = dp4a(wv[4], qb.x, 0);
-                s1 = dp4a(wv[5], qb.y, s1);
-                s1 = dp4a(wv[6], qb.z, s1);
-                s1 = dp4a(wv[7], qb.w, s1);
-                acc[c] += (dw * xv.d[sb]) * (float)(ls0 * s0 + ls1 * s1);
-            }
+        for (int t = 0; t < NT; ++t) {
+            const int4 *q = reinterpret_cast<const int4 *>(x[t].qs + sb * 256 + 32 * j);
+            const int4 qa = q[0], qb = q[1];
+            int s0 = dp4a(wv[0], qa.x, 0);
+            s0 = dp4a(wv[1], qa.y, s0);
+            s0 = dp4a(wv[2], qa.z, s0);
+            s0 = dp4a(wv[3], qa.w, s0);
+            int s1 = dp4a(wv[4], qb.x, 0);
+            s1 = dp4a(wv[5], qb.y, s1);
+            s1 = dp4a(wv[6], qb.z, s1);
+            s1 = dp4a(wv[7], qb.w, s1);
+            acc[t] = fmaf(dw * x[t].d[sb], (float)(ls0 * s0 + ls1 * s1), acc[t]);
         }
     }
 }
 
-// Q4_K x Q8_K: lane owns sub-block j (32 values) of every super-block (8 lanes per row).
-// main = s_j * sum(q4 * q8), min = m_j * (bsum[2j] + bsum[2j+1]);
-// float (d_w d_x) main - (dmin_w d_x) min (ggml-cpu/quants.c:645-715).
-__device__ __forceinline__ void dot_q4k_lane(const uint8_t *row, int nsb, int j, const uint8_t *act, int act_stride,
-                                             const int *tok, int ntok, float *acc) {
+// Q4_K x Q8_K, lane = sub-block j (8 lanes per row): s_j * sum(q4 * q8) and m_j * (bsum pair),
+// combined as (d_w d_x) main - (dmin_w d_x) min per super-block. Q4_K rows are 16-byte aligned.
+template <int NT>
+__device__ __forceinline__ void q4k_lane(const uint8_t *row, int nsb, int j, const ActQ8K (&x)[NT],
+                                         float (&acc)[NT]) {
+    const int jj = 8 * (j & 3), hi = j >> 2, sh = 4 * (j & 1), qoff = 16 + 32 * (j >> 1);
+#pragma unroll 1
     for (int sb = 0; sb < nsb; ++sb) {
         const uint8_t *blk = row + sb * B_Q4_K;
-        const uint32_t dm = *reinterpret_cast<const uint32_t *>(blk);
-        const float dw = h2f((uint16_t)(dm & 0xffffu)), dmin = h2f((uint16_t)(dm >> 16));
-        const uint8_t *sc = blk + 4;
-        int s, m;
-        if (j < 4) {
-            s = sc[j] & 63;
-            m = sc[j + 4] & 63;
-        } else {
-            s = (sc[j + 4] & 0x0f) | ((sc[j - 4] >> 6) << 4);
-            m = (sc[j + 4] >> 4) | ((sc[j] >> 6) << 4);
-        }
-        const int4 *qp = reinterpret_cast<const int4 *>(blk + 16 + 32 * (j >> 1));
+        const uint4 hdr = *reinterpret_cast<const uint4 *>(blk);   // d, dmin | scales[12]
+        const float dw = h2f((uint16_t)(hdr.x & 0xffffu)), dmin = h2f((uint16_t)(hdr.x >> 16));
+        // 6-bit scale and min of sub-block j (get_scale_min_k4, ggml-quants.c:822)
+        const int s = hi ? (int)(((hdr.w >> jj) & 0xfu) | (((hdr.y >> (jj + 6)) & 3u) << 4)) : (int)((hdr.y >> jj) & 63u);
+        const int m = hi ? (int)(((hdr.w >> (jj + 4)) & 0xfu) | (((hdr.z >> (jj + 6)) & 3u) << 4))
+                         : (int)((hdr.z >> jj) & 63u);
+        const int4 *qp = reinterpret_cast<const int4 *>(blk + qoff);
         const int4 qa = qp[0], qb = qp[1];
-        const int sh = 4 * (j & 1);
         int wv[8];
         wv[0] = (qa.x >> sh) & 0x0f0f0f0f; wv[1] = (qa.y >> sh) & 0x0f0f0f0f;
         wv[2] = (qa.z >> sh) & 0x0f0f0f0f; wv[3] = (qa.w >> sh) & 0x0f0f0f0f;
         wv[4] = (qb.x >> sh) & 0x0f0f0f0f; wv[5] = (qb.y >> sh) & 0x0f0f0f0f;
         wv[6] = (qb.z >> sh) & 0x0f0f0f0f; wv[7] = (qb.w >> sh) & 0x0f0f0f0f;
 #pragma unroll
-        for (int c = 0; c < kTokChunk; ++c) {
-            if (c < ntok) {
-                const Q8KView xv = q8k_view(act + (size_t)tok[c] * act_stride, nsb);
-                const int4 *q = reinterpret_cast<const int4 *>(xv.qs + sb * 256 + 32 * j);
-                const int4 xa = q[0], xb = q[1];
-                int d = dp4a(wv[0], xa.x, 0);
-                d = dp4a(wv[1], xa.y, d);
-                d = dp4a(wv[2], xa.z, d);
-                d = dp4a(wv[3], xa.w, d);
-                d = dp4a(wv[4], xb.x, d);
-                d = dp4a(wv[5], xb.y, d);
-                d = dp4a(wv[6], xb.z, d);
-                d = dp4a(wv[7], xb.w, d);
-                const int bsum = xv.bs[sb * 16 + 2 * j] + xv.bs[sb * 16 + 2 * j + 1];
-                const float dx = xv.d[sb];
-                acc[c] += (dw * dx) * (float)(s * d);
-                acc[c] -= (dmin * dx) * (float)(m * bsum);
-            }
+        for (int t = 0; t < NT; ++t) {
+            const int4 *q = reinterpret_cast<const int4 *>(x[t].qs + sb * 256 + 32 * j);
+            const int4 xa = q[0], xb = q[1];
+            int d = dp4a(wv[0], xa.x, 0);
+            d = dp4a(wv[1], xa.y, d);
+            d = dp4a(wv[2], xa.z, d);
+            d = dp4a(wv[3], xa.w, d);
+            d = dp4a(wv[4], xb.x, d);
+            d = dp4a(wv[5], xb.y, d);
+            d = dp4a(wv[6], xb.z, d);
+            d = dp4a(wv[7], xb.w, d);
+            const uint32_t bp = *reinterpret_cast<const uint32_t *>(x[t].bs + sb * 16 + 2 * j);
+            const int bsum = (int)(int16_t)(bp & 0xffffu) + (int)(int16_t)(bp >> 16);
+            const float dx = x[t].d[sb];
+            acc[t] = fmaf(dw * dx, (float)(s * d), acc[t]);
+            acc[t] = fmaf(-(dmin * dx), (float)(m * bsum), acc[t]);
         }
     }
 }
 
-// Q8_0 activations in shared memory: qs[nb][32] int8 | d[nb] f32 (f16 value widened) | qsum[nb] i32
-struct Q80View {
-    const int8_t *qs;
-    const float *d;
-    const int *qsum;
-};
-__device__ __forceinline__ Q80View q80_view(const uint8_t *row, int nb) {
-    Q80View v;
-    v.qs = reinterpret_cast<const int8_t *>(row);
-    v.d = reinterpret_cast<const float *>(row + nb * 32);
-    v.qsum = reinterpret_cast<const int *>(row + nb * 36);
-    return v;
-}
-
-// Q5_0 x Q8_0: lane owns half of a row's 32-blocks. value = (nibble | hbit << 4) - 16, so
-// dot = sum(u * q) - 16 * sum(q); float d_w * d_x per block (ggml-cpu/quants.c:314-352).
-__device__ __forceinline__ void dot_q5_0_lane(const uint8_t *row, int b0, int b1, const uint8_t *act, int act_stride,
-                                              int nb, const int *col, int ntok, float *acc) {
+// Q5_0 x Q8_0, lane = half of a row's 32-blocks: value = (nibble | hbit << 4) - 16, so
+// dot = sum(u * q) - 16 * sum(q); d_w * d_x per block.
+template <int NT>
+__device__ __forceinline__ void q5_0_lane(const uint8_t *row, int b0, int b1, const ActQ80 (&x)[NT], float (&acc)[NT]) {
+#pragma unroll 1
     for (int b = b0; b < b1; ++b) {
         const uint8_t *blk = row + b * B_Q5_0;
-        const float dw = h2f(ld_u16(blk));
-        const uint32_t qh = ld_u32_a2(blk + 2);
+        const float dw = h2f(*reinterpret_cast<const uint16_t *>(blk));
+        uint32_t w[5];                                  // qh | qs[0..15]
+        lds_words_a2<5>(blk + 2, w);
+        const uint32_t qh = w[0];
         int wlo[4], whi[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-            const uint32_t q = ld_u32_a2(blk + 6 + 4 * i);
             const uint32_t hl = (((qh >> (4 * i)) & 15u) * 0x00204081u) & 0x01010101u;
             const uint32_t hh = (((qh >> (16 + 4 * i)) & 15u) * 0x00204081u) & 0x01010101u;
-            wlo[i] = (int)((q & 0x0f0f0f0fu) | (hl << 4));
-            whi[i] = (int)(((q >> 4) & 0x0f0f0f0fu) | (hh << 4));
+            wlo[i] = (int)((w[1 + i] & 0x0f0f0f0fu) | (hl << 4));
+            whi[i] = (int)(((w[1 + i] >> 4) & 0x0f0f0f0fu) | (hh << 4));
         }
 #pragma unroll
-        for (int c = 0; c < kTokChunk; ++c) {
-            if (c < ntok) {
-                const Q80View xv = q80_view(act + (size_t)col[c] * act_stride, nb);
-                const int4 *q = reinterpret_cast<const int4 *>(xv.qs + 32 * b);
-                const int4 xa = q[0], xb = q[1];
-                int s = dp4a(wlo[0], xa.x, 0);
-                s = dp4a(wlo[1], xa.y, s);
-                s = dp4a(wlo[2], xa.z, s);
-                s = dp4a(wlo[3], xa.w, s);
-                s = dp4a(whi[0], xb.x, s);
-                s = dp4a(whi[1], xb.y, s);
-                s = dp4a(whi[2], xb.z, s);
-                s = dp4a(whi[3], xb.w, s);
-                s -= 16 * xv.qsum[b];
-                acc[c] += (dw * xv.d[b]) * (float)s;
-            }
+        for (int t = 0; t < NT; ++t) {
+            const int4 *q = reinterpret_cast<const int4 *>(x[t].qs + 32 * b);
+            const int4 xa = q[0], xb = q[1];
+            int s = dp4a(wlo[0], xa.x, 0);
+            s = dp4a(wlo[1], xa.y, s);
+            s = dp4a(wlo[2], xa.z, s);
+            s = dp4a(wlo[3], xa.w, s);
+            s = dp4a(whi[0], xb.x, s);
+            s = dp4a(whi[1], xb.y, s);
+            s = dp4a(whi[2], xb.z, s);
+            s = dp4a(whi[3], xb.w, s);
+            s -= 16 * x[t].qsum[b];
+            acc[t] = fmaf(dw * x[t].d[b], (float)s, acc[t]);
         }
     }
 }
 
-// 4 table lookups (IQ4_NL levels) for the 4 low nibbles of the bytes of `w`
+// 4 IQ4_NL level lookups for the low nibbles of the 4 bytes of w (levels packed in t0..t3)
 __device__ __forceinline__ int iq4nl_lookup4(uint32_t w, uint32_t t0, uint32_t t1, uint32_t t2, uint32_t t3) {
     const uint32_t x = w & 0x0f0f0f0fu;
     const uint32_t y = x | (x >> 4);
@@ -447,35 +396,35 @@ __device__ __forceinline__ int iq4nl_lookup4(uint32_t w, uint32_t t0, uint32_t t
     return (int)((lo & ~m) | (hi & m));
 }
 
-// IQ4_NL x Q8_0 (ggml-cpu/quants.c:1203-1227)
-__device__ __forceinline__ void dot_iq4nl_lane(const uint8_t *row, int b0, int b1, const uint8_t *act, int act_stride,
-                                               int nb, const int *col, int ntok, const uint32_t *kv, float *acc) {
+// IQ4_NL x Q8_0, lane = half of a row's 32-blocks
+template <int NT>
+__device__ __forceinline__ void iq4nl_lane(const uint8_t *row, int b0, int b1, const ActQ80 (&x)[NT],
+                                           const uint32_t (&kv)[4], float (&acc)[NT]) {
+#pragma unroll 1
     for (int b = b0; b < b1; ++b) {
         const uint8_t *blk = row + b * B_IQ4_NL;
-        const float dw = h2f(ld_u16(blk));
+        const float dw = h2f(*reinterpret_cast<const uint16_t *>(blk));
+        uint32_t w[4];
+        lds_words_a2<4>(blk + 2, w);
         int wlo[4], whi[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-            const uint32_t q = ld_u32_a2(blk + 2 + 4 * i);
-            wlo[i] = iq4nl_lookup4(q, kv[0], kv[1], kv[2], kv[3]);
-            whi[i] = iq4nl_lookup4(q >> 4, kv[0], kv[1], kv[2], kv[3]);
+            wlo[i] = iq4nl_lookup4(w[i], kv[0], kv[1], kv[2], kv[3]);
+            whi[i] = iq4nl_lookup4(w[i] >> 4, kv[0], kv[1], kv[2], kv[3]);
         }
 #pragma unroll
-        for (int c = 0; c < kTokChunk; ++c) {
-            if (c < ntok) {
-                const Q80View xv = q80_view(act + (size_t)col[c] * act_stride, nb);
-                const int4 *q = reinterpret_cast<const int4 *>(xv.qs + 32 * b);
-                const int4 xa = q[0], xb = q[1];
-                int s = dp4a(wlo[0], xa.x, 0);
-                s = dp4a(wlo[1], xa.y, s);
-                s = dp4a(wlo[2], xa.z, s);
-                s = dp4a(wlo[3], xa.w, s);
-                s = dp4a(whi[0], xb.x, s);
-                s = dp4a(whi[1], xb.y, s);
-                s = dp4a(whi[2], xb.z, s);
-                s = dp4a(whi[3], xb.w, s);
-                acc[c] += (xv.d[b] * dw) * (float)s;
-            }
+        for (int t = 0; t < NT; ++t) {
+            const int4 *q = reinterpret_cast<const int4 *>(x[t].qs + 32 * b);
+            const int4 xa = q[0], xb = q[1];
+            int s = dp4a(wlo[0], xa.x, 0);
+            s = dp4a(wlo[1], xa.y, s);
+            s = dp4a(wlo[2], xa.z, s);
+            s = dp4a(wlo[3], xa.w, s);
+            s = dp4a(whi[0], xb.x, s);
+            s = dp4a(whi[1], xb.y, s);
+            s = dp4a(whi[2], xb.z, s);
+            s = dp4a(whi[3], xb.w, s);
+            acc[t] = fmaf(x[t].d[b] * dw, (float)s, acc[t]);
         }
     }
 }
@@ -503,26 +452,44 @@ __device__ __forceinline__ float geglu1(float g, float u) {
 }
 
 // ------------------------------------------------------------------ the grouped GEMV
-constexpr int kStages = 3;
-constexpr int kGuStageRows = 32;     // 8 lanes per row, 4 rows per warp, 8 warps
-constexpr int kDnStageRows = 128;    // 2 lanes per row, 16 rows per warp, 8 warps
+// One CTA per SM: a producer warp streams stages of weight rows HBM -> shared memory with bulk
+// copies; 16 consumer warps in 4 groups take every 4th stage. Each stage slot has a `full`
+// barrier (copy landed) and an `empty` barrier (its group's 4 warps are done), so groups never
+// wait for one another, only for data.
+constexpr int kConsumerWarps = 16;
+constexpr int kGroups = 4;
+constexpr int kWarpsPerGroup = kConsumerWarps / kGroups;
+constexpr int kGemvThreads = (kConsumerWarps + 1) * 32;
+constexpr int kSlots = 6;
+constexpr int kGuStageRows = kWarpsPerGroup * 4;    // 8 lanes per row, 4 rows per warp
+constexpr int kDnStageRows = kWarpsPerGroup * 16;   // 2 lanes per row, 16 rows per warp
 
-struct StagePlan {
-    int u, row0, nrows;
+struct GemvSmem {
+    int route, bars, grid, act, stage, stage_cap, total;
 };
-
-// the next stage from flat group f (8-row groups; every unique expert has gpe groups)
-__device__ __forceinline__ StagePlan next_stage(int f, int g1, int gpe, int stage_groups) {
-    StagePlan s;
-    s.u = f / gpe;
-    const int lg = f - s.u * gpe;
-    int n = min(stage_groups, min(g1 - f, gpe - lg));
-    s.row0 = lg * kGroupRows;
-    s.nrows = n * kGroupRows;
-    return s;
+__host__ __device__ inline GemvSmem gemv_layout(int kind, int d_in, int T) {
+    GemvSmem L;
+    int o = 0;
+    L.route = o; o += (int)((sizeof(RouteSmem) + 127) / 128 * 128);
+    L.bars = o;  o += (2 * kSlots * 8 + 127) / 128 * 128;
+    L.grid = o;  o += kind == 0 ? MOE_IQ2S_GRID_ROWS * 8 : 0;
+    L.act = o;   o += kind == 0 ? T * xq_stride_bytes(d_in) : 2 * T * q80_stride(d_in);
+    o = (o + 127) / 128 * 128;
+    L.stage = o;
+    const int rows = kind == 0 ? kGuStageRows : kDnStageRows;
+    const int rb = kind == 0 ? (int)row_bytes(T_Q4_K, d_in) : (int)row_bytes(T_Q5_0, d_in);
+    L.stage_cap = (rows * rb + 16 + 127) / 128 * 128;
+    o += kSlots * L.stage_cap;
+    L.total = o;
+    return L;
 }
 
-// flat group index of byte position `pos` in the unique-expert cost prefix
+__device__ __forceinline__ const uint8_t *pool_entry(const PoolView &pv, int widx, int d_out, int d_in) {
+    if (pv.ptrs) return reinterpret_cast<const uint8_t *>(pv.ptrs[widx]);
+    return pv.w + (size_t)widx * d_out * row_bytes(pv.type, d_in);
+}
+
+// flat group index (8-row groups; every unique expert has gpe groups) of byte position `pos`
 __device__ __forceinline__ int group_at(const RouteSmem &rs, long long pos, int gpe) {
     const int U = rs.n_unique;
     if (pos >= rs.upre[U]) return U * gpe;
@@ -535,73 +502,146 @@ __device__ __forceinline__ int group_at(const RouteSmem &rs, long long pos, int 
     return lo * gpe + (int)((pos - rs.upre[lo]) / per);
 }
 
-
-// Shared-memory layout of gemv_kernel (identical on host and device).
-struct GemvSmem {
-    int route, bars, grid, act, stage, stage_cap, total;
+// Stages never cross an expert and sit on a per-expert grid of `sg` groups, so stage s of the CTA
+// range [g0, g1) is computable from s alone.
+struct StagePlan {
+    int u, row0, nrows;
 };
-__host__ __device__ inline GemvSmem gemv_layout(int kind, int d_in, int T) {
-    GemvSmem L;
-    int o = 0;
-    L.route = o; o += (int)((sizeof(RouteSmem) + 127) / 128 * 128);
-    L.bars = o;  o += 128;
-    L.grid = o;  o += kind == 0 ? MOE_IQ2S_GRID_ROWS * 8 : 0;
-    L.act = o;   o += (kind == 0 ? T * xq_stride_bytes(d_in) : T * q80_stride(d_in) + 16);
-    o = (o + 127) / 128 * 128;
-    L.stage = o;
-    L.stage_cap = kind == 0 ? kGuStageRows * (int)row_bytes(T_Q4_K, d_in) : kDnStageRows * (int)row_bytes(T_Q5_0, d_in);
-    L.stage_cap = (L.stage_cap + 127) / 128 * 128;
-    o += kStages * L.stage_cap;
-    L.total = o;
-    return L;
+__device__ __forceinline__ int stage_of(int g, int gpe, int spe, int sg) { return (g / gpe) * spe + (g % gpe) / sg; }
+__device__ __forceinline__ StagePlan stage_plan(int s, int g0, int g1, int gpe, int spe, int sg) {
+    StagePlan p;
+    p.u = s / spe;
+    const int k = s - p.u * spe;
+    const int base = p.u * gpe;
+    const int lo = max(base + k * sg, g0);
+    const int hi = min(min(base + (k + 1) * sg, base + gpe), g1);
+    p.row0 = (lo - base) * kGroupRows;
+    p.nrows = (hi - lo) * kGroupRows;
+    return p;
 }
 
-__device__ __forceinline__ const uint8_t *pool_entry(const PoolView &pv, int widx, int d_out, int d_in) {
-    if (pv.ptrs) return reinterpret_cast<const uint8_t *>(pv.ptrs[widx]);
-    return pv.w + (size_t)widx * d_out * row_bytes(pv.type, d_in);
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+__device__ __forceinline__ void consumer_sync() {
+    asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
 }
 
-__global__ void __launch_bounds__(kThreads, 1) gemv_kernel(GemvParams p) {
+template <int NT>
+__device__ __forceinline__ void gu_rows(const uint8_t *row, int nsb, int j, int type, const uint64_t *grid,
+                                        const uint8_t *act, int xs, const int *tok, float (&out)[4]) {
+    ActQ8K x[NT];
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+        const uint8_t *a = act + (size_t)tok[t] * xs;
+        x[t].qs = reinterpret_cast<const int8_t *>(a);
+        x[t].d = reinterpret_cast<const float *>(a + nsb * 256);
+        x[t].bs = reinterpret_cast<const int16_t *>(a + nsb * 256 + nsb * 4);
+    }
+    float acc[NT];
+#pragma unroll
+    for (int t = 0; t < NT; ++t) acc[t] = 0.f;
+    if (type == T_IQ2_S) {
+        iq2s_lane<NT>(row, nsb, j, grid, x, acc);
+#pragma unroll
+        for (int t = 0; t < NT; ++t) acc[t] *= 0.125f;
+    } else {
+        q4k_lane<NT>(row, nsb, j, x, acc);
+    }
+#pragma unroll
+    for (int t = 0; t < NT; ++t) out[t] = acc[t];
+}
+
+template <int NT>
+__device__ __forceinline__ void dn_rows(const uint8_t *row, int b0, int b1, int nb, int type, const uint32_t (&kv)[4],
+                                        const uint8_t *act, int as, int slot0, int nt, float (&out)[4]) {
+    ActQ80 x[NT];
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+        const uint8_t *a = act + (size_t)(slot0 + (t < nt ? t : 0)) * as;   // missing columns repeat column 0
+        x[t].qs = reinterpret_cast<const int8_t *>(a);
+        x[t].d = reinterpret_cast<const float *>(a + nb * 32);
+        x[t].qsum = reinterpret_cast<const int *>(a + nb * 36);
+    }
+    float acc[NT];
+#pragma unroll
+    for (int t = 0; t < NT; ++t) acc[t] = 0.f;
+    if (type == T_Q5_0) q5_0_lane<NT>(row, b0, b1, x, acc);
+    else iq4nl_lane<NT>(row, b0, b1, x, kv, acc);
+#pragma unroll
+    for (int t = 0; t < NT; ++t) out[t] = acc[t];
+}
+
+#ifdef MOEB_TRACE
+__device__ unsigned long long g_trace[2][512][8];
+__device__ __forceinline__ unsigned long long gtime() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+#define TRACE(i) do { if ((threadIdx.x & 31) == 0 && blockIdx.x < 512) g_trace[p.kind == 0 ? 0 : 1][blockIdx.x][i] = gtime(); } while (0)
+#define FTRACE(i) do { if ((threadIdx.x & 31) == 0 && blockIdx.x < 512) g_ftrace[blockIdx.x][i] = clock64(); } while (0)
+__device__ unsigned long long g_ftrace[512][16];
+__device__ unsigned long long g_strace[512][64][3];   // per stage of warp 0: start, data ready, done
+#else
+#define TRACE(i) do { } while (0)
+#define FTRACE(i) do { } while (0)
+#endif
+#ifdef MOEB_TRACE
+#define STRACE(it, k) do { if (warp == 0 && lane == 0 && blockIdx.x < 512 && (it) < 64) g_strace[blockIdx.x][(it)][k] = clock64(); } while (0)
+#else
+#define STRACE(it, k) do { } while (0)
+#endif
+
+__global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(GemvParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const GemvSmem L = gemv_layout(p.kind == 0 ? 0 : 1, p.d_in, p.route.T);
     RouteSmem &rs = *reinterpret_cast<RouteSmem *>(smem + L.route);
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bars);
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.bars);
+    uint64_t *empty = full + kSlots;
     uint64_t *grid = reinterpret_cast<uint64_t *>(smem + L.grid);
     uint8_t *act = smem + L.act;
     uint8_t *stage = smem + L.stage;
 
     // ---- prologue independent of upstream results
     if (tid == 0) {
-        for (int s = 0; s < kStages; ++s) mbar_init(&bars[s], 1);
+        for (int s = 0; s < kSlots; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kWarpsPerGroup);
+        }
         fence_mbar_init();
     }
     if (p.kind == 0)
-        for (int i = tid; i < MOE_IQ2S_GRID_ROWS; i += kThreads) grid[i] = g_iq2s_grid[i];
+        for (int i = tid; i < MOE_IQ2S_GRID_ROWS; i += kGemvThreads) grid[i] = g_iq2s_grid[i];
     uint32_t kv[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i)
         kv[i] = (uint32_t)(uint8_t)g_iq4nl[4 * i] | ((uint32_t)(uint8_t)g_iq4nl[4 * i + 1] << 8) |
                 ((uint32_t)(uint8_t)g_iq4nl[4 * i + 2] << 16) | ((uint32_t)(uint8_t)g_iq4nl[4 * i + 3] << 24);
 
-    // gate_up reads the router's logits and Q8_K activations: wait for the router grid. The down
-    // projection's routing inputs were complete before the gate_up grid got past its own wait, so it
-    // routes and starts streaming weights first and waits for the gate_up outputs later.
+    // gate_up reads the router's logits and activations: wait for the router grid. The down
+    // projection's routing inputs were complete before the gate_up grid got past its own wait, so
+    // it routes and starts streaming weights first and waits for the gate_up outputs later.
+    if (warp == 0) TRACE(0);
     if (p.kind == 0) pdl_wait();
     __syncthreads();
+    if (warp == 0) TRACE(1);
 
     // ---- routing and dispatch (every CTA, identical results)
-    route_tokens(p.route, rs, tid);
+    route_tokens(p.route, rs, tid, kGemvThreads / 32);
     __syncthreads();
-    dispatch_pairs(p.route, p.res, p.hot, p.cold, p.d_in, p.d_out, rs, tid, true);
+    if (warp == 0) TRACE(2);
+    dispatch_pairs(p.route, p.res, p.hot, p.cold, p.d_in, p.d_out, rs, tid, kGemvThreads, true);
+    if (warp == 0) TRACE(3);
     const int T = p.route.T, k = p.route.k, P = T * k;
     if (blockIdx.x == 0) {
-        for (int i = tid; i < P; i += kThreads) {
+        for (int i = tid; i < P; i += kGemvThreads) {
             if (p.ids_out) p.ids_out[i] = rs.ids[i];
             if (p.w_out) p.w_out[i] = rs.w[i];
             if (p.perm_out) p.perm_out[i] = rs.perm[i];
         }
-        for (int e = tid; e <= p.route.E; e += kThreads) {
+        for (int e = tid; e <= p.route.E; e += kGemvThreads) {
             if (p.cnt_out && e < p.route.E) p.cnt_out[e] = rs.cnt[e];
             if (p.off_out) p.off_out[e] = rs.off[e];
             if (p.rc_counts && e < p.route.E && rs.cnt[e]) atomicAdd(&p.rc_counts[e], rs.cnt[e]);
@@ -613,63 +653,52 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(GemvParams p) {
     }
     pdl_launch_dependents();
 
-    // ---- this CTA's share of the routed experts' weight bytes, in 8-row groups
+    // ---- this CTA's share of the routed experts' weight bytes, in 8-row groups and stages
     const int gpe = p.d_out / kGroupRows;
+    const int sg = (p.kind == 0 ? kGuStageRows : kDnStageRows) / kGroupRows;
+    const int spe = (gpe + sg - 1) / sg;
     const long long total = rs.upre[rs.n_unique];
     const long long s0 = total * blockIdx.x / gridDim.x, s1 = total * (blockIdx.x + 1) / gridDim.x;
     const int g0 = group_at(rs, s0, gpe), g1 = group_at(rs, s1, gpe);
-    const int stage_groups = (p.kind == 0 ? kGuStageRows : kDnStageRows) / kGroupRows;
+    if (g0 >= g1) return;   // no barrier below involves a CTA without work
+    const int S0 = stage_of(g0, gpe, spe, sg);
+    const int n_st = stage_of(g1 - 1, gpe, spe, sg) - S0 + 1;
 
-    auto stage_src = [&](const StagePlan &st, int &bytes) -> const uint8_t * {
-        const int cls = rs.ucls[st.u];
-        const PoolView &pv = cls == 0 ? p.hot : p.cold;
-        const int rb = (int)row_bytes(pv.type, p.d_in);
-        bytes = st.nrows * rb;
-        return pool_entry(pv, rs.uwidx[st.u], p.d_out, p.d_in) + (size_t)st.row0 * rb;
-    };
-
-    int f_issue = g0, issued = 0;
-    if (tid == 0) {
-        for (int s = 0; s < kStages && f_issue < g1; ++s) {
-            const StagePlan st = next_stage(f_issue, g1, gpe, stage_groups);
-            int bytes;
-            const uint8_t *src = stage_src(st, bytes);
-            mbar_expect_tx(&bars[s], (uint32_t)bytes);
-            bulk_g2s(stage + s * L.stage_cap, src, (uint32_t)bytes, &bars[s]);
-            f_issue += st.nrows / kGroupRows;
-            ++issued;
+    if (warp == kConsumerWarps) {
+        // ---- producer: one lane streams the stages through the slot ring
+        if (lane == 0) {
+            TRACE(4);
+            for (int it = 0; it < n_st; ++it) {
+                const int slot = it % kSlots;
+                if (it >= kSlots && !mbar_wait(&empty[slot], (uint32_t)(((it / kSlots) - 1) & 1))) break;
+                const StagePlan st = stage_plan(S0 + it, g0, g1, gpe, spe, sg);
+                const PoolView &pv = rs.ucls[st.u] == 0 ? p.hot : p.cold;
+                const int rb = (int)row_bytes(pv.type, p.d_in);
+                const uint32_t bytes = (uint32_t)(st.nrows * rb);
+                mbar_expect_tx(&full[slot], bytes);
+                bulk_g2s(stage + slot * L.stage_cap,
+                         pool_entry(pv, rs.uwidx[st.u], p.d_out, p.d_in) + (size_t)st.row0 * rb, bytes, &full[slot]);
+            }
         }
+        return;
     }
 
-    // ---- activations
+    // ---- consumers: activations for this CTA's experts
+    const int nsb = p.d_in / QK_K, nb = p.d_in / QK32;
+    const int u_first = g0 / gpe;
     if (p.kind == 0) {
         const int n16 = T * p.xq_stride / 16;
         const int4 *src = reinterpret_cast<const int4 *>(p.xq);
         int4 *dst = reinterpret_cast<int4 *>(act);
-        for (int i = tid; i < n16; i += kThreads) dst[i] = src[i];
-    } else if (p.kind == 1) {
-        pdl_wait();   // gate_up outputs
-    }
-    __syncthreads();
-
-    const int nsb = p.d_in / QK_K, nb = p.d_in / QK32;
-    const int a_stride = p.kind == 0 ? p.xq_stride : q80_stride(p.d_in);
-    int cur_u = -1, it = 0;
-    bool ok = true;
-    for (int f = g0; f < g1;) {
-        const StagePlan st = next_stage(f, g1, gpe, stage_groups);
-        const int e = rs.uexp[st.u], cls = rs.ucls[st.u], widx = rs.uwidx[st.u];
-        const int po = rs.off[e];
-        int n = rs.cnt[e];
-        if (p.kind != 0 && n > T) {
-            // the down activation buffer holds one pair per token of an expert; an expert repeated
-            // within a token's routes is reported and its extra pairs are not computed
-            if (tid == 0) atomicOr(&g_error, ERR_CAPACITY);
-            n = T;
-        }
-        if (p.kind != 0 && st.u != cur_u) {
-            // Q8_0 activations of this expert's routed pairs: slot i <- pair perm[po + i]
-            for (int item = warp; item < n * nb; item += kWarps) {
+        for (int i = tid; i < n16; i += kConsumerWarps * 32) dst[i] = src[i];
+    } else {
+        if (p.kind == 1) pdl_wait();   // gate_up outputs
+        const int as = q80_stride(p.d_in);
+        const int u_last = (g1 - 1) / gpe;
+        if (u_last - u_first > 1 && tid == 0) atomicOr(&g_error, ERR_CAPACITY);
+        for (int u = u_first; u <= min(u_last, u_first + 1); ++u) {
+            const int e = rs.uexp[u], po = rs.off[e], n = min(rs.cnt[e], T);
+            for (int item = warp; item < n * nb; item += kConsumerWarps) {
                 const int i = item / nb, b = item - i * nb;
                 const int pair = rs.perm[po + i];
                 float v;
@@ -679,120 +708,736 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(GemvParams p) {
                 } else {
                     v = p.a[(size_t)(p.a_per_pair ? pair : pair / k) * p.d_in + 32 * b + lane];
                 }
-                uint8_t *row = act + (size_t)i * a_stride;
+                uint8_t *row = act + (size_t)((u - u_first) * T + i) * as;
                 q80_block_warp(v, reinterpret_cast<int8_t *>(row) + 32 * b, reinterpret_cast<float *>(row + nb * 32) + b,
                                reinterpret_cast<int *>(row + nb * 36) + b, lane);
             }
-            cur_u = st.u;
-            __syncthreads();
         }
-        const int buf = it % kStages;
-        const uint32_t parity = (uint32_t)((it / kStages) & 1);
-        if (!mbar_wait(&bars[buf], parity)) { ok = false; break; }
-        const uint8_t *sb = stage + buf * L.stage_cap;
+    }
+    consumer_sync();
+    if (warp == 0) TRACE(5);
+
+    // ---- consumers: stages
+    const int grp = warp / kWarpsPerGroup, wg = warp % kWarpsPerGroup;
+    const int xs = p.xq_stride, as = q80_stride(p.d_in);
+    for (int it = grp; it < n_st; it += kGroups) {
+        const int slot = it % kSlots;
+        if (!mbar_wait(&full[slot], (uint32_t)((it / kSlots) & 1))) break;
+        const StagePlan st = stage_plan(S0 + it, g0, g1, gpe, spe, sg);
+        const int e = rs.uexp[st.u], cls = rs.ucls[st.u], widx = rs.uwidx[st.u];
+        const int po = rs.off[e];
         const PoolView &pv = cls == 0 ? p.hot : p.cold;
         const int rb = (int)row_bytes(pv.type, p.d_in);
+        const uint8_t *sbuf = stage + slot * L.stage_cap;
         if (p.kind == 0) {
-            const int j = lane & 7, rsub = lane >> 3;
-            for (int r0 = warp * 4; r0 < st.nrows; r0 += kWarps * 4) {
-                const int r = r0 + rsub;
-                const uint8_t *row = sb + (size_t)r * rb;
+            const int n = rs.cnt[e];
+            const int j = lane & 7, r = wg * 4 + (lane >> 3);
+            if (wg * 4 < st.nrows) {
+                const uint8_t *row = sbuf + (size_t)r * rb;
                 for (int c0 = 0; c0 < n; c0 += kTokChunk) {
-                    const int ntok = min(kTokChunk, n - c0);
+                    const int nt = min(kTokChunk, n - c0);
                     int tok[kTokChunk], pair[kTokChunk];
 #pragma unroll
                     for (int c = 0; c < kTokChunk; ++c) {
-                        pair[c] = c < ntok ? rs.perm[po + c0 + c] : 0;
+                        pair[c] = rs.perm[po + c0 + (c < nt ? c : 0)];
                         tok[c] = pair[c] / k;
                     }
-                    float acc[kTokChunk] = {0.f, 0.f, 0.f, 0.f};
-                    if (pv.type == T_IQ2_S) dot_iq2s_lane(row, nsb, j, grid, act, a_stride, tok, ntok, acc);
-                    else dot_q4k_lane(row, nsb, j, act, a_stride, tok, ntok, acc);
-                    const float post = pv.type == T_IQ2_S ? 0.125f : 1.0f;
+                    float v[4] = {0.f, 0.f, 0.f, 0.f};
+                    if (nt == 1) gu_rows<1>(row, nsb, j, pv.type, grid, act, xs, tok, v);
+                    else gu_rows<4>(row, nsb, j, pv.type, grid, act, xs, tok, v);
 #pragma unroll
                     for (int c = 0; c < kTokChunk; ++c) {
-                        float v = acc[c];
-                        v += __shfl_xor_sync(0xffffffffu, v, 1);
-                        v += __shfl_xor_sync(0xffffffffu, v, 2);
-                        v += __shfl_xor_sync(0xffffffffu, v, 4);
-                        if (j == 0 && c < ntok) p.y[(size_t)pair[c] * p.d_out + st.row0 + r] = v * post;
+                        float s = v[c];
+                        s += __shfl_xor_sync(0xffffffffu, s, 1);
+                        s += __shfl_xor_sync(0xffffffffu, s, 2);
+                        s += __shfl_xor_sync(0xffffffffu, s, 4);
+                        if (j == 0 && c < nt) p.y[(size_t)pair[c] * p.d_out + st.row0 + r] = s;
                     }
                 }
             }
         } else {
-            const int half = lane & 1, rsub = lane >> 1;
-            const int bmid = (nb + 1) / 2;
-            const int b0 = half ? bmid : 0, b1 = half ? nb : bmid;
-            const float *scale = pv.scale;
-            for (int r0 = warp * 16; r0 < st.nrows; r0 += kWarps * 16) {
-                const int r = r0 + rsub;
-                const bool valid = r < st.nrows;
-                const uint8_t *row = sb + (size_t)(valid ? r : 0) * rb;
+            int n = rs.cnt[e];
+            if (n > T) {
+                // the activation buffer holds one pair per token of an expert; an expert repeated
+                // within a token's routes is reported and its extra pairs are not computed
+                if (lane == 0) atomicOr(&g_error, ERR_CAPACITY);
+                n = T;
+            }
+            const int half = lane & 1, r = wg * 16 + (lane >> 1);
+            const int bmid = (nb + 1) / 2, b0 = half ? bmid : 0, b1 = half ? nb : bmid;
+            const bool valid = r < st.nrows;
+            const int slot0 = (st.u - u_first) * T;
+            if (wg * 16 < st.nrows) {
+                const uint8_t *row = sbuf + (size_t)(valid ? r : 0) * rb;
                 for (int c0 = 0; c0 < n; c0 += kTokChunk) {
-                    const int ntok = valid ? min(kTokChunk, n - c0) : 0;
-                    int col[kTokChunk];
-#pragma unroll
-                    for (int c = 0; c < kTokChunk; ++c) col[c] = c0 + c;
-                    float acc[kTokChunk] = {0.f, 0.f, 0.f, 0.f};
-                    if (pv.type == T_Q5_0) dot_q5_0_lane(row, b0, b1, act, a_stride, nb, col, ntok, acc);
-                    else dot_iq4nl_lane(row, b0, b1, act, a_stride, nb, col, ntok, kv, acc);
+                    const int nt = min(kTokChunk, n - c0);
+                    float v[4] = {0.f, 0.f, 0.f, 0.f};
+                    if (nt == 1) dn_rows<1>(row, b0, b1, nb, pv.type, kv, act, as, slot0 + c0, nt, v);
+                    else dn_rows<4>(row, b0, b1, nb, pv.type, kv, act, as, slot0 + c0, nt, v);
 #pragma unroll
                     for (int c = 0; c < kTokChunk; ++c) {
-                        float v = acc[c];
-                        v += __shfl_xor_sync(0xffffffffu, v, 1);
-                        if (half == 0 && c < ntok) {
+                        float s = v[c];
+                        s += __shfl_xor_sync(0xffffffffu, s, 1);
+                        if (half == 0 && valid && c < nt) {
                             const int pair = rs.perm[po + c0 + c];
-                            if (p.apply_scale && scale) v = __fmul_rn(v, scale[widx]);
-                            p.y[(size_t)pair * p.d_out + st.row0 + r] = v;
+                            if (p.apply_scale && pv.scale) s = __fmul_rn(s, pv.scale[widx]);
+                            p.y[(size_t)pair * p.d_out + st.row0 + r] = s;
                         }
                     }
                 }
             }
         }
-        __syncthreads();   // every warp is done with this stage buffer
-        if (tid == 0 && f_issue < g1) {
-            const StagePlan nx = next_stage(f_issue, g1, gpe, stage_groups);
-            int bytes;
-            const uint8_t *src = stage_src(nx, bytes);
-            mbar_expect_tx(&bars[buf], (uint32_t)bytes);
-            bulk_g2s(stage + buf * L.stage_cap, src, (uint32_t)bytes, &bars[buf]);
-            f_issue += nx.nrows / kGroupRows;
-            ++issued;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);
+        if (warp == 0 && it == 0) TRACE(6);
+    }
+    if (warp == 0) TRACE(7);
+}
+
+// ------------------------------------------------------------------ fused decode layer
+// The whole layer for up to kFusedMaxT tokens in ONE persistent cooperative kernel (one CTA per
+// SM), phases separated by bounded grid barriers:
+//   A  router logits (one CTA per expert, fixed-order reduction) + bias; Q8_K of every token;
+//      every CTA also loads the residency class of every expert and the IQ2_S codebook
+//   -- grid barrier 1 --
+//   B  every CTA: softmax / top-k / weights and the dispatch (histogram, scan, stable
+//      permutation), then its byte-balanced share of the routed experts' gate_up AND down rows;
+//      the producer warp streams the gate_up stages and then, without a break, the down stages
+//      through one ring of shared-memory slots
+//   C  consumers: gate_up stages -> h (global)
+//   -- grid barrier 2 (consumers; the producer keeps streaming down weights meanwhile) --
+//   D  consumers: GeGLU + Q8_0 of this CTA's down experts' pairs, then the down stages -> y
+//   -- grid barrier 3 --
+//   E  every CTA combines a slice of the outputs: out = sum_j w_j * y_j in slot order.
+constexpr int kFusedMaxT = 8;
+constexpr int kFusedMaxP = kFusedMaxT * kMaxTopK;
+static_assert(kFusedMaxT == kFusedTokens, "host and device chunk sizes differ");
+constexpr int kFSlots = 5;
+constexpr uint32_t kGridWaitLimit = 1u << 24;   // x >= 32 ns sleeps: bounded well under a second
+
+enum : int32_t { ERR_GRID_TIMEOUT = 8 };
+
+// Grid barrier state (per device, zero at load): arrivals of the current barrier and its
+// generation. The last arriver resets the count before it bumps the generation, so the next
+// barrier always starts from zero; launches of the fused kernel cannot overlap (each fills every
+// SM), so one pair serves all of them.
+__device__ unsigned int g_bar_count;
+__device__ unsigned int g_bar_gen;
+
+__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// One thread per CTA: arrive, then wait (bounded) until every CTA of the grid has arrived.
+__device__ __noinline__ bool grid_barrier_thread(unsigned nblocks) {
+    const unsigned gen = ld_acquire_u32(&g_bar_gen);
+    __threadfence();
+    if (atomicAdd(&g_bar_count, 1u) == nblocks - 1) {
+        atomicExch(&g_bar_count, 0u);
+        __threadfence();
+        atomicAdd(&g_bar_gen, 1u);
+        return true;
+    }
+    for (uint32_t i = 0; i < kGridWaitLimit; ++i) {
+        if (ld_acquire_u32(&g_bar_gen) != gen) {
+            __threadfence();
+            return true;
         }
-        f += st.nrows / kGroupRows;
-        ++it;
+        if (i >= 256) __nanosleep(32);
     }
-    if (!ok && tid == 0) {
-        // a wait gave up: drain this CTA's copies still in flight (bounded) before leaving
-        for (int i = it; i < issued; ++i) mbar_wait(&bars[i % kStages], (uint32_t)((i / kStages) & 1));
-    }
+    atomicOr(&g_error, ERR_GRID_TIMEOUT);
+    return false;
 }
 
-// ------------------------------------------------------------------ combine
-// out[t] = w[t][0]*y[t*k] + w[t][1]*y[t*k+1] + ...: products rounded, then added in slot order
-// (ggml_mul then the view-add chain, llama-graph.cpp:1814-1848).
-__global__ void __launch_bounds__(kThreads) combine_kernel(CombineParams p) {
-    pdl_wait();
-    const int t = blockIdx.y;
-    const int i4 = blockIdx.x * kThreads + threadIdx.x;
-    if (i4 * 4 >= p.d) return;
-    float wj[kMaxTopK];
-    for (int j = 0; j < p.k; ++j) wj[j] = p.w[t * p.k + j];
-    const float4 *y4 = reinterpret_cast<const float4 *>(p.y);
-    const int d4 = p.d / 4;
-    float4 acc = y4[(size_t)(t * p.k) * d4 + i4];
-    acc.x = __fmul_rn(acc.x, wj[0]); acc.y = __fmul_rn(acc.y, wj[0]);
-    acc.z = __fmul_rn(acc.z, wj[0]); acc.w = __fmul_rn(acc.w, wj[0]);
-    for (int j = 1; j < p.k; ++j) {
-        const float4 v = y4[(size_t)(t * p.k + j) * d4 + i4];
-        acc.x = __fadd_rn(acc.x, __fmul_rn(v.x, wj[j]));
-        acc.y = __fadd_rn(acc.y, __fmul_rn(v.y, wj[j]));
-        acc.z = __fadd_rn(acc.z, __fmul_rn(v.z, wj[j]));
-        acc.w = __fadd_rn(acc.w, __fmul_rn(v.w, wj[j]));
-    }
-    reinterpret_cast<float4 *>(p.out)[(size_t)t * d4 + i4] = acc;
+struct FusedParams {
+    const float *w_router, *b_router, *x;
+    int32_t T, E, d, k, nff;
+    Residency res;
+    PoolView hot_gu, cold_gu, hot_dn, cold_dn;
+    float *logits;
+    uint8_t *xq;
+    int32_t xq_stride;
+    float *h, *y, *out;
+    int32_t *ids_out, *cnt_out, *off_out, *perm_out;
+    float *w_out;
+    // completion counters, zeroed in phase A: gate_up rows done per unique expert [kFusedMaxP],
+    // then down rows done per (token, 64-row block) [T][ceil(d / 64)]
+    uint32_t *sync;
+};
+
+struct FusedRoute {
+    int32_t ids[kFusedMaxP];
+    float w[kFusedMaxP];
+    int32_t cnt[kMaxE];
+    int32_t off[kMaxE + 1];
+    int32_t perm[kFusedMaxP];
+    int32_t ecls[kMaxE], ewidx[kMaxE];   // residency class / pool index of every expert
+    int32_t n_unique;
+    int32_t uexp[kFusedMaxP], ucls[kFusedMaxP], uwidx[kFusedMaxP];
+    uint32_t upre_gu[kFusedMaxP + 1], upre_dn[kFusedMaxP + 1];   // cumulative work units (see fused_dispatch)
+    float red[kFusedMaxT][kConsumerWarps + 1];
+    float rmax[kFusedMaxT], rinv[kFusedMaxT];
+};
+
+struct FusedSmem {
+    int route, bars, grid, xact, dact, slots, slot_cap, total;
+};
+__host__ __device__ inline FusedSmem fused_layout(int d, int nff) {
+    FusedSmem L;
+    int o = 0;
+    L.route = o; o += (int)((sizeof(FusedRoute) + 127) / 128 * 128);
+    L.bars = o;  o += (2 * kFSlots * 8 + 127) / 128 * 128;
+    L.grid = o;  o += MOE_IQ2S_GRID_ROWS * 8;
+    L.xact = o;  o += kFusedMaxT * xq_stride_bytes(d);
+    L.dact = o;  o += 2 * kFusedMaxT * q80_stride(nff);
+    o = (o + 127) / 128 * 128;
+    L.slots = o;
+    const int gu = kGuStageRows * (int)row_bytes(T_Q4_K, d), dn = kDnStageRows * (int)row_bytes(T_Q5_0, nff);
+    L.slot_cap = ((gu > dn ? gu : dn) + 16 + 127) / 128 * 128;
+    o += kFSlots * L.slot_cap;
+    L.total = o;
+    return L;
 }
 
+// flat 8-row group of position `pos` in a cost prefix (16-byte units; every unique expert has gpe
+// groups of equal cost)
+__device__ __noinline__ int group_at_pre(const uint32_t *pre, int U, uint32_t pos, int gpe) {
+    if (pos >= pre[U]) return U * gpe;
+    int lo = 0, hi = U - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (pre[mid] <= pos) lo = mid; else hi = mid - 1;
+    }
+    const uint32_t per = (pre[lo + 1] - pre[lo]) / (uint32_t)gpe;
+    return lo * gpe + (int)((pos - pre[lo]) / per);
+}
+
+// Routing of the fused kernel: softmax, top-k and normalised weights for every token, from the
+// logits in global memory. The top-k is a parallel rank: thread (t, e) counts the experts that
+// beat e under (value desc, index asc); experts of rank < k land at slot `rank`.
+__device__ void fused_route(const FusedParams &p, FusedRoute &rs, float *lg, int tid) {
+    const int T = p.T, E = p.E, k = p.k, lane = tid & 31, warp = tid >> 5;
+    for (int i = tid; i < T * E; i += kGemvThreads) lg[i] = __ldcg(p.logits + i);
+    __syncthreads();
+    for (int t = warp; t < T; t += kGemvThreads / 32) {
+        float mx = -INFINITY;
+        for (int e = lane; e < E; e += 32) mx = fmaxf(mx, lg[t * E + e]);
+        mx = warp_max(mx);
+        float s = 0.f;
+        for (int e = lane; e < E; e += 32) s += expf(lg[t * E + e] - mx);
+        s = warp_sum(s);
+        if (lane == 0) { rs.rmax[t] = mx; rs.rinv[t] = 1.f / s; }
+    }
+    __syncthreads();
+    for (int i = tid; i < T * E; i += kGemvThreads) {
+        const int t = i / E, e = i - t * E;
+        const float v = lg[i];
+        const float *row = lg + t * E;
+        int rank = 0;
+#pragma unroll 4
+        for (int q = 0; q < E; ++q) rank += better(row[q], q, v, e);
+        if (rank < k) {
+            rs.ids[t * k + rank] = e;
+            rs.w[t * k + rank] = __fmul_rn(expf(v - rs.rmax[t]), rs.rinv[t]);
+        }
+    }
+    __syncthreads();
+    for (int t = warp; t < T; t += kGemvThreads / 32) {
+        // weights / max(sum, 6.1e-5) with the sum taken in slot order (llama-graph.cpp:1640-1648)
+        const float mine = lane < k ? rs.w[t * k + lane] : 0.f;
+        float psum = 0.f;
+        for (int j = 0; j < k; ++j) psum = __fadd_rn(psum, __shfl_sync(0xffffffffu, mine, j));
+        psum = fmaxf(psum, 6.103515625e-5f);
+        if (lane < k) rs.w[t * k + lane] = __fdiv_rn(mine, psum);
+    }
+    __syncthreads();
+}
+
+// histogram, exclusive scan, stable permutation and the unique-expert list with both
+// projections' cumulative weight bytes. One warp scans: lane l owns experts [l*per, (l+1)*per).
+__device__ void fused_dispatch(const FusedParams &p, FusedRoute &rs, int tid, int nthreads) {
+    const int P = p.T * p.k, E = p.E;
+    for (int e = tid; e < E; e += nthreads) rs.cnt[e] = 0;
+    __syncthreads();
+    for (int i = tid; i < P; i += nthreads) {
+        int e = rs.ids[i];
+        if (e < 0 || e >= E) { atomicOr(&g_error, ERR_BAD_EXPERT); e = 0; rs.ids[i] = 0; }
+        atomicAdd(&rs.cnt[e], 1);
+    }
+    __syncthreads();
+    if (tid < 32) {
+        const int lane = tid, per = E / 32, e0 = lane * per;
+        const int gpe_gu = 2 * p.nff / kGroupRows, gpe_dn = p.d / kGroupRows;
+        // work of an expert with n routed tokens, in units that weigh the HBM bytes a CTA streams
+        // against the instructions its consumer warps issue (about 3 instructions per byte per SM at
+        // the measured bandwidth), rounded to a multiple of the expert's 8-row groups
+        auto cost = [&](bool gu, int type, int n) -> uint32_t {
+            // per 8-row group: bytes and lane instructions (decode + per-column dot work)
+            uint32_t bytes, instr;
+            if (gu) {
+                const uint32_t dec = type == T_IQ2_S ? 70u : 24u;
+                bytes = 8u * (uint32_t)(p.d / QK_K) * (type == T_IQ2_S ? (uint32_t)B_IQ2_S : (uint32_t)B_Q4_K);
+                instr = 8u * 8u * (uint32_t)(p.d / QK_K) * (dec + 16u * (uint32_t)n);
+            } else {
+                const uint32_t dec = type == T_IQ4_NL ? 45u : 25u;
+                bytes = 8u * (uint32_t)(p.nff / QK32) * (type == T_IQ4_NL ? (uint32_t)B_IQ4_NL : (uint32_t)B_Q5_0);
+                instr = 8u * (uint32_t)(p.nff / QK32) * (dec + 12u * (uint32_t)n);
+            }
+            return (3u * bytes + instr) / 64u * (uint32_t)(gu ? gpe_gu : gpe_dn);
+        };
+        int c_sum = 0, u_sum = 0;
+        uint32_t gsum = 0, dsum = 0;
+#pragma unroll 1
+        for (int i = 0; i < per; ++i) {
+            const int e = e0 + i, c = rs.cnt[e];
+            c_sum += c;
+            const bool has = c > 0 && rs.ecls[e] >= 0;
+            if (c > 0 && rs.ecls[e] < 0) atomicOr(&g_error, ERR_BAD_EXPERT);   // its class pool is absent
+            if (has) {
+                const bool hot = rs.ecls[e] == 0;
+                ++u_sum;
+                gsum += cost(true, hot ? p.hot_gu.type : p.cold_gu.type, c);
+                dsum += cost(false, hot ? p.hot_dn.type : p.cold_dn.type, c);
+            }
+        }
+        int c_in = c_sum, u_in = u_sum;
+        uint32_t g_in = gsum, d_in = dsum;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int a0 = __shfl_up_sync(0xffffffffu, c_in, o), a1 = __shfl_up_sync(0xffffffffu, u_in, o);
+            const uint32_t a2 = __shfl_up_sync(0xffffffffu, g_in, o), a3 = __shfl_up_sync(0xffffffffu, d_in, o);
+            if (lane >= o) { c_in += a0; u_in += a1; g_in += a2; d_in += a3; }
+        }
+        int c_base = c_in - c_sum, u = u_in - u_sum;
+        uint32_t gb = g_in - gsum, db = d_in - dsum;
+#pragma unroll 1
+        for (int i = 0; i < per; ++i) {
+            const int e = e0 + i, c = rs.cnt[e];
+            rs.off[e] = c_base;
+            c_base += c;
+            if (c > 0 && rs.ecls[e] >= 0) {
+                const bool hot = rs.ecls[e] == 0;
+                gb += cost(true, hot ? p.hot_gu.type : p.cold_gu.type, c);
+                db += cost(false, hot ? p.hot_dn.type : p.cold_dn.type, c);
+                rs.uexp[u] = e;
+                rs.ucls[u] = rs.ecls[e];
+                rs.uwidx[u] = rs.ewidx[e];
+                rs.upre_gu[u + 1] = gb;
+                rs.upre_dn[u + 1] = db;
+                ++u;
+            }
+        }
+        if (lane == 31) {
+            rs.off[E] = c_in;
+            rs.n_unique = u_in;
+            rs.upre_gu[0] = 0;
+            rs.upre_dn[0] = 0;
+        }
+    }
+    __syncthreads();
+    for (int i = tid; i < P; i += nthreads) {
+        const int e = rs.ids[i];
+        int rank = 0;
+        for (int q = 0; q < i; ++q) rank += rs.ids[q] == e;
+        rs.perm[rs.off[e] + rank] = i;
+    }
+    __syncthreads();
+}
+
+__global__ void __launch_bounds__(kGemvThreads, 1) fused_decode_kernel(FusedParams p) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int G = gridDim.x, T = p.T, k = p.k, E = p.E, d = p.d, nff = p.nff, P = T * k;
+    const FusedSmem L = fused_layout(d, nff);
+    FusedRoute &rs = *reinterpret_cast<FusedRoute *>(smem + L.route);
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.bars);
+    uint64_t *empty = full + kFSlots;
+    uint64_t *grid = reinterpret_cast<uint64_t *>(smem + L.grid);
+    uint8_t *xact = smem + L.xact;
+    uint8_t *dact = smem + L.dact;
+    uint8_t *slots = smem + L.slots;
+
+    // ================= phase A
+    if (warp == 0) FTRACE(0);
+    const int nrb = (d + 63) / 64;
+    if (blockIdx.x == 0)
+        for (int i = tid; i < kFusedMaxP + T * nrb; i += kGemvThreads) p.sync[i] = 0u;
+    if (tid == 0) {
+        for (int s = 0; s < kFSlots; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kWarpsPerGroup);
+        }
+        fence_mbar_init();
+    }
+    if (warp == kConsumerWarps) {
+        // the producer warp is idle until phase B: residency classes and the IQ2_S codebook.
+        // Loads are batched into registers before any shared-memory store, so they overlap.
+        constexpr int kPer = kMaxE / 32;
+        int slot[kPer], st[kPer], se[kPer];
+#pragma unroll
+        for (int i = 0; i < kPer; ++i) {
+            const int e = lane + 32 * i;
+            slot[i] = (e < E && p.res.n_slots > 0 && p.res.exp_slot) ? __ldg(p.res.exp_slot + e) : -1;
+        }
+#pragma unroll
+        for (int i = 0; i < kPer; ++i) {
+            const bool in = slot[i] >= 0 && slot[i] < p.res.n_slots;
+            st[i] = in ? __ldg(p.res.slot_state + slot[i]) : 0;
+            se[i] = in ? __ldg(p.res.slot_exp + slot[i]) : -1;
+        }
+        uint64_t g[MOE_IQ2S_GRID_ROWS / 32];
+#pragma unroll
+        for (int i = 0; i < MOE_IQ2S_GRID_ROWS / 32; ++i) g[i] = g_iq2s_grid[lane + 32 * i];
+#pragma unroll
+        for (int i = 0; i < kPer; ++i) {
+            const int e = lane + 32 * i;
+            if (e >= E) continue;
+            // residency class of expert e (moert/cuda/ffn_moe.cu:101-104): 0 hot (slot), 1 cold, -1 no pool
+            int cls = 1, widx = e;
+            if (slot[i] >= 0 && slot[i] < p.res.n_slots && st[i] == 2 && se[i] == e) { cls = 0; widx = slot[i]; }
+            const PoolView &pv = cls == 0 ? p.hot_gu : p.cold_gu;
+            const PoolView &pd = cls == 0 ? p.hot_dn : p.cold_dn;
+            if (pv.w == nullptr || pd.w == nullptr || widx >= pv.n) cls = -1;
+            rs.ecls[e] = cls;
+            rs.ewidx[e] = widx;
+        }
+#pragma unroll
+        for (int i = 0; i < MOE_IQ2S_GRID_ROWS / 32; ++i) grid[lane + 32 * i] = g[i];
+    }
+    for (int unit = blockIdx.x; unit < E + T; unit += G) {
+        if (unit < E) {
+            // logits[t][unit] = W[unit] . x[t] (+ bias): every thread a strided share, then warp and
+            // CTA reductions in a fixed order
+            const int n4 = d / 4;
+            const float4 *w4 = reinterpret_cast<const float4 *>(p.w_router + (size_t)unit * d);
+            float part[kFusedMaxT];
+#pragma unroll
+            for (int t = 0; t < kFusedMaxT; ++t) part[t] = 0.f;
+            for (int i = tid; i < n4; i += kGemvThreads) {
+                const float4 w = __ldg(w4 + i);
+#pragma unroll
+                for (int t = 0; t < kFusedMaxT; ++t) {
+                    if (t < T) {
+                        const float4 xv = __ldg(reinterpret_cast<const float4 *>(p.x + (size_t)t * d) + i);
+                        part[t] = fmaf(w.x, xv.x, part[t]);
+                        part[t] = fmaf(w.y, xv.y, part[t]);
+                        part[t] = fmaf(w.z, xv.z, part[t]);
+                        part[t] = fmaf(w.w, xv.w, part[t]);
+                    }
+                }
+            }
+#pragma unroll
+            for (int t = 0; t < kFusedMaxT; ++t) {
+                if (t < T) {
+                    const float s = warp_sum(part[t]);
+                    if (lane == 0) rs.red[t][warp] = s;
+                }
+            }
+            __syncthreads();
+            if (tid < T) {
+                float s = 0.f;
+                for (int w = 0; w < kConsumerWarps + 1; ++w) s += rs.red[tid][w];
+                if (p.b_router) s = __fadd_rn(s, p.b_router[unit]);
+                p.logits[(size_t)tid * E + unit] = s;
+            }
+            __syncthreads();
+        } else {
+            const int t = unit - E, nsb = d / QK_K;
+            uint8_t *row = p.xq + (size_t)t * p.xq_stride;
+            for (int sb = warp; sb < nsb; sb += kGemvThreads / 32)
+                q8k_superblock_warp(p.x + (size_t)t * d + sb * 256, reinterpret_cast<int8_t *>(row) + sb * 256,
+                                    reinterpret_cast<float *>(row + nsb * 256) + sb,
+                                    reinterpret_cast<int16_t *>(row + nsb * 256 + nsb * 4) + sb * 16, lane);
+        }
+    }
+    __syncthreads();
+    if (warp == 0) FTRACE(1);
+    if (tid == 0) grid_barrier_thread(G);
+    __syncthreads();
+    if (warp == 0) FTRACE(2);
+
+    // ================= phase B: routing and the work split
+    fused_route(p, rs, reinterpret_cast<float *>(slots), tid);   // the slot ring is free until the producer starts
+    __syncthreads();
+    if (warp == 0) FTRACE(3);
+    fused_dispatch(p, rs, tid, kGemvThreads);
+    if (warp == 0) FTRACE(4);
+#ifdef MOEB_TRACE
+    fused_dispatch(p, rs, tid, kGemvThreads);   // second, warm pass (trace builds only)
+    if (warp == 0) FTRACE(15);
+#endif
+    if (blockIdx.x == 0) {
+        for (int i = tid; i < P; i += kGemvThreads) {
+            if (p.ids_out) p.ids_out[i] = rs.ids[i];
+            if (p.w_out) p.w_out[i] = rs.w[i];
+            if (p.perm_out) p.perm_out[i] = rs.perm[i];
+        }
+        for (int e = tid; e <= E; e += kGemvThreads) {
+            if (p.cnt_out && e < E) p.cnt_out[e] = rs.cnt[e];
+            if (p.off_out) p.off_out[e] = rs.off[e];
+        }
+    }
+    const int U = rs.n_unique;
+    const int gpe_gu = 2 * nff / kGroupRows, sg_gu = kGuStageRows / kGroupRows, spe_gu = (gpe_gu + sg_gu - 1) / sg_gu;
+    const int gpe_dn = d / kGroupRows, sg_dn = kDnStageRows / kGroupRows, spe_dn = (gpe_dn + sg_dn - 1) / sg_dn;
+    // work-balanced share of each projection (totals stay below 2^32 / G units)
+    const uint32_t tgu = rs.upre_gu[U], tdn = rs.upre_dn[U];
+    const int g0 = group_at_pre(rs.upre_gu, U, tgu * blockIdx.x / G, gpe_gu);
+    const int g1 = group_at_pre(rs.upre_gu, U, tgu * (blockIdx.x + 1) / G, gpe_gu);
+    const int h0 = group_at_pre(rs.upre_dn, U, tdn * blockIdx.x / G, gpe_dn);
+    const int h1 = group_at_pre(rs.upre_dn, U, tdn * (blockIdx.x + 1) / G, gpe_dn);
+    const int Sg = g1 > g0 ? stage_of(g0, gpe_gu, spe_gu, sg_gu) : 0;
+    const int n_gu = g1 > g0 ? stage_of(g1 - 1, gpe_gu, spe_gu, sg_gu) - Sg + 1 : 0;
+    const int Sd = h1 > h0 ? stage_of(h0, gpe_dn, spe_dn, sg_dn) : 0;
+    const int n_dn = h1 > h0 ? stage_of(h1 - 1, gpe_dn, spe_dn, sg_dn) - Sd + 1 : 0;
+    if (warp == 0) FTRACE(12);
+
+    auto plan = [&](int it, bool &is_gu) -> StagePlan {
+        is_gu = it < n_gu;
+        return is_gu ? stage_plan(Sg + it, g0, g1, gpe_gu, spe_gu, sg_gu)
+                     : stage_plan(Sd + (it - n_gu), h0, h1, gpe_dn, spe_dn, sg_dn);
+    };
+
+    if (warp == kConsumerWarps) {
+        // ================= producer: gate_up stages, then down stages, through one slot ring
+        if (lane == 0) {
+            for (int it = 0; it < n_gu + n_dn; ++it) {
+                const int slot = it % kFSlots;
+                if (it >= kFSlots && !mbar_wait(&empty[slot], (uint32_t)(((it / kFSlots) - 1) & 1))) break;
+                bool is_gu;
+                const StagePlan st = plan(it, is_gu);
+                const bool hot = rs.ucls[st.u] == 0;
+                const PoolView &pv = is_gu ? (hot ? p.hot_gu : p.cold_gu) : (hot ? p.hot_dn : p.cold_dn);
+                const int d_in = is_gu ? d : nff, d_out = is_gu ? 2 * nff : d;
+                const int rb = (int)row_bytes(pv.type, d_in);
+                const uint32_t bytes = (uint32_t)(st.nrows * rb);
+                mbar_expect_tx(&full[slot], bytes);
+                bulk_g2s(slots + slot * L.slot_cap, pool_entry(pv, rs.uwidx[st.u], d_out, d_in) + (size_t)st.row0 * rb,
+                         bytes, &full[slot]);
+            }
+        }
+    } else {
+        // ================= consumers
+        const int nsb = d / QK_K, nb = nff / QK32;
+        const int xs = p.xq_stride, as = q80_stride(nff);
+        const int grp = warp / kWarpsPerGroup, wg = warp % kWarpsPerGroup;
+        uint32_t kv[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            kv[i] = (uint32_t)(uint8_t)g_iq4nl[4 * i] | ((uint32_t)(uint8_t)g_iq4nl[4 * i + 1] << 8) |
+                    ((uint32_t)(uint8_t)g_iq4nl[4 * i + 2] << 16) | ((uint32_t)(uint8_t)g_iq4nl[4 * i + 3] << 24);
+        if (warp == 0) FTRACE(13);
+        {
+            const int n16 = T * xs / 16;
+            const int4 *src = reinterpret_cast<const int4 *>(p.xq);
+            int4 *dst = reinterpret_cast<int4 *>(xact);
+            for (int i = tid; i < n16; i += kConsumerWarps * 32) dst[i] = __ldcg(src + i);
+        }
+        if (warp == 0) FTRACE(14);
+        consumer_sync();
+        if (warp == 0) FTRACE(5);
+        bool ok = true;
+        // ---- phase C: gate_up
+        for (int it = grp; it < n_gu; it += kGroups) {
+            const int slot = it % kFSlots;
+            STRACE(it, 0);
+            if (ok && !mbar_wait(&full[slot], (uint32_t)((it / kFSlots) & 1))) ok = false;
+            STRACE(it, 1);
+            bool is_gu;
+            const StagePlan st = plan(it, is_gu);
+            const int e = rs.uexp[st.u];
+            const bool hot = rs.ucls[st.u] == 0;
+            const int type = hot ? p.hot_gu.type : p.cold_gu.type;
+            const int rb = (int)row_bytes(type, d);
+            const int po = rs.off[e], n = rs.cnt[e];
+            const int j = lane & 7, r = wg * 4 + (lane >> 3);
+            if (ok && wg * 4 < st.nrows) {
+                const uint8_t *row = slots + slot * L.slot_cap + (size_t)r * rb;
+                for (int c0 = 0; c0 < n; c0 += kTokChunk) {
+                    const int nt = min(kTokChunk, n - c0);
+                    int tok[kTokChunk], pair[kTokChunk];
+#pragma unroll
+                    for (int c = 0; c < kTokChunk; ++c) {
+                        pair[c] = rs.perm[po + c0 + (c < nt ? c : 0)];
+                        tok[c] = pair[c] / k;
+                    }
+                    float v[4] = {0.f, 0.f, 0.f, 0.f};
+                    // one- and four-column bodies only (short code); missing columns repeat column 0
+                    if (nt == 1) gu_rows<1>(row, nsb, j, type, grid, xact, xs, tok, v);
+                    else gu_rows<4>(row, nsb, j, type, grid, xact, xs, tok, v);
+#pragma unroll
+                    for (int c = 0; c < kTokChunk; ++c) {
+                        float s = v[c];
+                        s += __shfl_xor_sync(0xffffffffu, s, 1);
+                        s += __shfl_xor_sync(0xffffffffu, s, 2);
+                        s += __shfl_xor_sync(0xffffffffu, s, 4);
+                        if (j == 0 && c < nt) p.h[(size_t)pair[c] * 2 * nff + st.row0 + r] = s;
+                    }
+                }
+            }
+            __syncwarp();
+            STRACE(it, 2);
+            if (lane == 0) mbar_arrive(&empty[slot]);
+        }
+        consumer_sync();
+        if (tid == 0 && g1 > g0) {
+            // publish this CTA's gate_up rows: one fence, one count per expert of its range
+            __threadfence();
+            for (int u = g0 / gpe_gu; u <= (g1 - 1) / gpe_gu; ++u) {
+                const int lo = max(g0, u * gpe_gu), hi = min(g1, (u + 1) * gpe_gu);
+                atomicAdd(&p.sync[u], (uint32_t)((hi - lo) * kGroupRows));
+            }
+        }
+        if (warp == 0) FTRACE(6);
+
+        // ---- phase D: down activations for this CTA's experts (<= 2), then the down stages
+        const int u_first = h1 > h0 ? h0 / gpe_dn : 0;
+        const int u_last = h1 > h0 ? (h1 - 1) / gpe_dn : -1;
+        if (u_last - u_first > 1 && tid == 0) atomicOr(&g_error, ERR_CAPACITY);
+        if (tid == 0) {
+            // every gate_up row of this CTA's down experts has been written (bounded wait)
+            for (int u = u_first; u <= min(u_last, u_first + 1); ++u) {
+                uint32_t i = 0;
+                while (ld_acquire_u32(&p.sync[u]) < (uint32_t)(2 * nff)) {
+                    if (++i >= kGridWaitLimit) { atomicOr(&g_error, ERR_GRID_TIMEOUT); break; }
+                    if (i >= 256) __nanosleep(32);
+                }
+            }
+            __threadfence();
+        }
+        consumer_sync();
+        if (warp == 0) FTRACE(7);
+        for (int u = u_first; u <= min(u_last, u_first + 1); ++u) {
+            const int e = rs.uexp[u], po = rs.off[e], n = min(rs.cnt[e], T);
+            const int n_items = n * nb;
+            for (int base = warp; base < n_items; base += 4 * kConsumerWarps) {
+                // four items' loads in flight before any of them is quantised
+                float g[4], v[4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const int item = base + q * kConsumerWarps;
+                    g[q] = v[q] = 0.f;
+                    if (item < n_items) {
+                        const int i = item / nb, b = item - i * nb;
+                        const float *hp = p.h + (size_t)rs.perm[po + i] * 2 * nff + 32 * b + lane;
+                        g[q] = __ldcg(hp);
+                        v[q] = __ldcg(hp + nff);
+                    }
+                }
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const int item = base + q * kConsumerWarps;
+                    if (item < n_items) {
+                        const int i = item / nb, b = item - i * nb;
+                        uint8_t *row = dact + (size_t)((u - u_first) * T + i) * as;
+                        q80_block_warp(geglu1(g[q], v[q]), reinterpret_cast<int8_t *>(row) + 32 * b,
+                                       reinterpret_cast<float *>(row + nb * 32) + b, reinterpret_cast<int *>(row + nb * 36) + b,
+                                       lane);
+                    }
+                }
+            }
+        }
+        consumer_sync();
+        if (warp == 0) FTRACE(8);
+        // down stages: the unified sequence continues at it = n_gu; groups keep their residue
+        for (int it = n_gu + grp; it < n_gu + n_dn; it += kGroups) {
+            const int slot = it % kFSlots;
+            if (ok && !mbar_wait(&full[slot], (uint32_t)((it / kFSlots) & 1))) ok = false;
+            bool is_gu;
+            const StagePlan st = plan(it, is_gu);
+            const int e = rs.uexp[st.u], widx = rs.uwidx[st.u];
+            const bool hot = rs.ucls[st.u] == 0;
+            const PoolView &pv = hot ? p.hot_dn : p.cold_dn;
+            const int rb = (int)row_bytes(pv.type, nff);
+            const int po = rs.off[e];
+            int n = rs.cnt[e];
+            if (n > T) {
+                if (lane == 0) atomicOr(&g_error, ERR_CAPACITY);
+                n = T;
+            }
+            const int half = lane & 1, r = wg * 16 + (lane >> 1);
+            const int bmid = (nb + 1) / 2, b0 = half ? bmid : 0, b1 = half ? nb : bmid;
+            const bool valid = r < st.nrows;
+            const int slot0 = (st.u - u_first) * T;
+            if (ok && wg * 16 < st.nrows) {
+                const uint8_t *row = slots + slot * L.slot_cap + (size_t)(valid ? r : 0) * rb;
+                for (int c0 = 0; c0 < n; c0 += kTokChunk) {
+                    const int nt = min(kTokChunk, n - c0);
+                    float v[4] = {0.f, 0.f, 0.f, 0.f};
+                    if (nt == 1) dn_rows<1>(row, b0, b1, nb, pv.type, kv, dact, as, slot0 + c0, nt, v);
+                    else dn_rows<4>(row, b0, b1, nb, pv.type, kv, dact, as, slot0 + c0, nt, v);
+#pragma unroll
+                    for (int c = 0; c < kTokChunk; ++c) {
+                        float s = v[c];
+                        s += __shfl_xor_sync(0xffffffffu, s, 1);
+                        if (half == 0 && valid && c < nt) {
+                            const int pair = rs.perm[po + c0 + c];
+                            if (pv.scale) s = __fmul_rn(s, pv.scale[widx]);
+                            p.y[(size_t)pair * d + st.row0 + r] = s;
+                        }
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+        }
+        // ---- phase E: publish this CTA's down rows per (token, 64-row block); the CTA whose
+        // count completes a block combines it: out[t] = sum_j w_j * y[t*k + j], products rounded,
+        // then added in slot order (ggml_mul + the view-add chain, llama-graph.cpp:1814-1848)
+        consumer_sync();
+        int *todo = reinterpret_cast<int *>(dact);   // the activations are no longer needed
+        if (tid == 0) {
+            todo[0] = 0;
+            __threadfence();
+        }
+        consumer_sync();
+        if (h1 > h0) {
+            // one (pair, block) item per thread, so the counting atomics travel together; each
+            // counting thread fences first, which orders the whole CTA's y rows (made visible to it
+            // by the barrier above) before its count
+            __threadfence();
+            int items = 0;
+            for (int u = h0 / gpe_dn; u <= (h1 - 1) / gpe_dn; ++u) {
+                const int lo = max(h0, u * gpe_dn) * kGroupRows - u * d, hi = min(h1, (u + 1) * gpe_dn) * kGroupRows - u * d;
+                const int e = rs.uexp[u], po = rs.off[e], n = min(rs.cnt[e], T);
+                const int rb0 = lo / 64, rb1 = (hi - 1) / 64;
+                for (int c = 0; c < n; ++c)
+                    for (int rb = rb0; rb <= rb1; ++rb, ++items) {
+                        if (items % (kConsumerWarps * 32) != tid) continue;
+                        const int rows = min(hi, (rb + 1) * 64) - max(lo, rb * 64);
+                        const int t = rs.perm[po + c] / k;
+                        const uint32_t before = atomicAdd(&p.sync[kFusedMaxP + t * nrb + rb], (uint32_t)rows);
+                        if (before + rows == (uint32_t)(k * min(64, d - rb * 64))) {
+                            const int at = atomicAdd(&todo[0], 1);
+                            todo[1 + 2 * at] = t;
+                            todo[2 + 2 * at] = rb;
+                        }
+                    }
+            }
+        }
+        consumer_sync();
+        const int n_todo = todo[0];
+        if (n_todo > 0) {
+            if (tid == 0) __threadfence();
+            consumer_sync();
+            for (int q = warp; q < n_todo; q += kConsumerWarps) {
+                const int t = todo[1 + 2 * q], rb = todo[2 + 2 * q];
+                for (int rr = lane; rr < min(64, d - rb * 64); rr += 32) {
+                    const int row = rb * 64 + rr;
+                    float acc = __fmul_rn(__ldcg(p.y + (size_t)(t * k) * d + row), rs.w[t * k]);
+                    for (int j = 1; j < k; ++j)
+                        acc = __fadd_rn(acc, __fmul_rn(__ldcg(p.y + (size_t)(t * k + j) * d + row), rs.w[t * k + j]));
+                    p.out[(size_t)t * d + row] = acc;
+                }
+            }
+        }
+    }
+    if (warp == 0) FTRACE(9);
+}
+
+// ------------------------------------------------------------------ Q8_K activations for the per-kind path
 __global__ void __launch_bounds__(kThreads) quant_q8k_kernel(const float *x, uint8_t *dst, int d, int stride) {
     const int t = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int nsb = d / QK_K;
@@ -808,11 +1453,11 @@ __global__ void __launch_bounds__(kThreads, 1) route_only_kernel(RouteSrc r, int
                                                                  int32_t *off, int32_t *perm) {
     __shared__ RouteSmem rs;
     const int tid = threadIdx.x;
-    route_tokens(r, rs, tid);
+    route_tokens(r, rs, tid, kThreads / 32);
     __syncthreads();
     const Residency none = {0, nullptr, nullptr, nullptr};
-    const PoolView pv = {nullptr, T_Q4_K, 0, nullptr};
-    dispatch_pairs(r, none, pv, pv, QK_K, kGroupRows, rs, tid, false);
+    const PoolView pv = {nullptr, T_Q4_K, 0, nullptr, nullptr};
+    dispatch_pairs(r, none, pv, pv, QK_K, kGroupRows, rs, tid, kThreads, false);
     const int P = r.T * r.k;
     for (int i = tid; i < P; i += kThreads) {
         if (ids) ids[i] = rs.ids[i];
@@ -939,12 +1584,6 @@ static cudaError_t launch_ex(const void *fn, dim3 grid, dim3 block, size_t smem,
     return cudaLaunchKernelExC(&cfg, fn, args);
 }
 
-cudaError_t launch_router(const RouterParams &p, cudaStream_t s, bool pdl) {
-    RouterParams q = p;
-    void *args[] = {&q};
-    return launch_ex((const void *)router_kernel, dim3(p.E + (p.xq ? p.T : 0)), dim3(kThreads), 0, s, pdl, args);
-}
-
 size_t gemv_smem_bytes(int kind, int d_in, int T) { return (size_t)gemv_layout(kind == 0 ? 0 : 1, d_in, T).total; }
 
 cudaError_t launch_gemv(const GemvParams &p, cudaStream_t s, bool pdl, int n_sms) {
@@ -958,15 +1597,41 @@ cudaError_t launch_gemv(const GemvParams &p, cudaStream_t s, bool pdl, int n_sms
     }
     GemvParams q = p;
     void *args[] = {&q};
-    return launch_ex((const void *)gemv_kernel, dim3(n_sms), dim3(kThreads), smem, s, pdl, args);
+    return launch_ex((const void *)gemv_kernel, dim3(n_sms), dim3(kGemvThreads), smem, s, pdl, args);
 }
 
-cudaError_t launch_combine(const CombineParams &p, cudaStream_t s, bool pdl) {
-    CombineParams q = p;
-    void *args[] = {&q};
-    const int d4 = p.d / 4;
-    return launch_ex((const void *)combine_kernel, dim3((d4 + kThreads - 1) / kThreads, p.T), dim3(kThreads), 0, s,
-                     pdl, args);
+size_t fused_smem_bytes(int d, int nff) { return (size_t)fused_layout(d, nff).total; }
+
+cudaError_t launch_fused(const FusedArgs &a, cudaStream_t s, int n_sms) {
+    FusedParams p{};
+    p.w_router = a.w_router; p.b_router = a.b_router; p.x = a.x;
+    p.T = a.T; p.E = a.E; p.d = a.d; p.k = a.k; p.nff = a.nff;
+    p.res = a.res;
+    p.hot_gu = a.hot_gu; p.cold_gu = a.cold_gu; p.hot_dn = a.hot_dn; p.cold_dn = a.cold_dn;
+    p.logits = a.logits; p.xq = a.xq; p.xq_stride = a.xq_stride;
+    p.h = a.h; p.y = a.y; p.out = a.out;
+    p.ids_out = a.ids_out; p.w_out = a.w_out; p.cnt_out = a.cnt_out; p.off_out = a.off_out; p.perm_out = a.perm_out;
+    p.sync = a.sync;
+    const size_t smem = fused_smem_bytes(a.d, a.nff);
+    static bool attr_set = false;
+    if (!attr_set) {
+        cudaError_t e = cudaFuncSetAttribute((const void *)fused_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             227 * 1024);
+        if (e != cudaSuccess) return e;
+        attr_set = true;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(n_sms);
+    cfg.blockDim = dim3(kGemvThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;   // the grid barriers need every CTA resident
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    void *args[] = {&p};
+    return cudaLaunchKernelExC(&cfg, (const void *)fused_decode_kernel, args);
 }
 
 cudaError_t launch_quant_q8k(const float *x, uint8_t *dst, int rows, int d, int stride, cudaStream_t s) {
@@ -1019,6 +1684,15 @@ void *g_static_addr[64];   // device address of g_static_scratch, per device, re
 }  // namespace
 
 }  // namespace moeb
+
+#ifdef MOEB_TRACE
+extern "C" int moeb_trace_read(void *host, size_t bytes) {
+    return cudaMemcpyFromSymbol(host, moeb::g_ftrace, bytes) == cudaSuccess ? 0 : -3;
+}
+extern "C" int moeb_strace_read(void *host, size_t bytes) {
+    return cudaMemcpyFromSymbol(host, moeb::g_strace, bytes) == cudaSuccess ? 0 : -3;
+}
+#endif
 
 extern "C" int moeb_layer_forward_static(const moeb_layer *L, const float *x, int32_t n_tokens, float *out,
                                          void *stream) {

@@ -98,33 +98,33 @@ struct GemvParams {
     int32_t *rc_counts, *rc_hits;
 };
 
-struct RouterParams {
-    const float *w_router;   // [E][d]
-    const float *b_router;   // [E] or nullptr
-    const float *x;          // [T][d]
-    int32_t T, E, d;
-    float *logits;           // [T][E]
-    uint8_t *xq;             // [T][xq_stride] Q8_K (nullptr: skip)
+// the fused decode layer (one cooperative launch per chunk of <= kFusedTokens tokens)
+constexpr int kFusedTokens = 8;
+struct FusedArgs {
+    const float *w_router, *b_router, *x;
+    int32_t T, E, d, k, nff;
+    Residency res;
+    PoolView hot_gu, cold_gu, hot_dn, cold_dn;
+    float *logits;
+    uint8_t *xq;
     int32_t xq_stride;
+    float *h, *y, *out;
+    int32_t *ids_out, *cnt_out, *off_out, *perm_out;
+    float *w_out;
+    uint32_t *sync;          // fused_sync_words(T, d) zero-initialised-by-the-kernel counters
 };
-
-struct CombineParams {
-    const float *y;          // [P][d]
-    const float *w;          // [T][k]
-    int32_t T, k, d;
-    float *out;              // [T][d]
-};
+MOEB_HD inline int fused_sync_words(int T, int d) { return kFusedTokens * kMaxTopK + T * ((d + 63) / 64); }
 
 MOEB_HD inline int xq_stride_bytes(int d) { return (int)(((d / QK_K) * B_Q8_K + 15) / 16 * 16); }
 // Q8_0 activation row in shared memory: qs[nb][32] | d[nb] f32 | qsum[nb] i32
 MOEB_HD inline int q80_stride(int d_in) { return ((d_in / 32) * 40 + 15) / 16 * 16; }
 
 // host-side launch helpers (decode.cu); `pdl` chains the launch to the previous kernel in the stream
-cudaError_t launch_router(const RouterParams &p, cudaStream_t s, bool pdl);
 cudaError_t launch_gemv(const GemvParams &p, cudaStream_t s, bool pdl, int n_sms);
-cudaError_t launch_combine(const CombineParams &p, cudaStream_t s, bool pdl);
 cudaError_t launch_quant_q8k(const float *x, uint8_t *dst, int rows, int d, int stride, cudaStream_t s);
 size_t gemv_smem_bytes(int kind, int d_in, int T);
+cudaError_t launch_fused(const FusedArgs &a, cudaStream_t s, int n_sms);
+size_t fused_smem_bytes(int d, int nff);
 // standalone pieces behind the moeb_* inspection entry points
 cudaError_t launch_route_only(const RouteSrc &r, int32_t *ids, float *w, int32_t *cnt, int32_t *off, int32_t *perm,
                               cudaStream_t s);

@@ -32,7 +32,7 @@ def test_static_scratch_entry_matches_workspace_entry():
     host = host_layer("decode_t4_mixed")
     layer = MoELayer(host)
     cfg = workload.CONFIGS["decode_t4_mixed"]
-    # two calls in a row, different inputs and token counts (the second is two 16-token chunks)
+    # two calls in a row, different inputs and token counts (the second runs as three 8-token chunks)
     for T, seed in ((4, 101), (20, 102)):
         x = torch.from_numpy(workload.make_input(cfg, n_tokens=T, stream=seed)).cuda()
         got = _forward_static(layer, x)
