@@ -111,6 +111,17 @@ def measured_peaks():
         return 6650.0, 1590.0, "fallback"
 
 
+def measured_traffic(workload_name):
+    """dram__bytes_read.sum + dram__bytes_write.sum of one launch of the dominant kernel, from the
+    ncu capture summarised in profiles/ (None when no capture of this workload is committed)."""
+    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "profiles", "traffic.json")
+    try:
+        with open(path) as f:
+            return json.load(f).get(workload_name)
+    except (OSError, ValueError):
+        return None
+
+
 def reference_spec(host, x):
     from oracle import LayerSpec
     exp_slot, slot_exp, slot_state = host.residency()
@@ -152,7 +163,7 @@ def run_reference(args):
     from llapis_b200 import workload
     cfg = workload.CONFIGS[args.config]
     host = workload.build_layer(cfg)
-    x = workload.make_input(cfg)
+    x = workload.make_input(cfg)[:256]   # bounded sample: at most 256 tokens per step (tokens/s is per token)
     cb = time_reference(host, x, args.warmup, args.steps, budget_s=120.0)
     if cb is None:
         print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref (reference ggml-cpu build) missing"}))
@@ -161,7 +172,8 @@ def run_reference(args):
     line = {"metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": cb["ms_per_forward"], "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "q8 int dot / f32", "data": "synthetic (seeded)",
-            "config": {"workload": cfg.name, "n_tokens": cfg.n_tokens, "layers": 1},
+            "config": {"workload": cfg.name, "n_tokens": cfg.n_tokens, "layers": 1,
+                       "sample_tokens_per_step": int(x.shape[0])},
             "impl": "reference", "cpu_baseline": cb,
             "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line))
@@ -202,7 +214,7 @@ def main():
         layer(x, out, aux={"ids": ids}, stream=s)
     s.synchronize()
     alg_bytes = workload.algorithmic_bytes(host, ids.cpu().numpy(), T)
-    launches_per_step = 4 * ((T + 15) // 16)
+    launches_per_step = layer.launches(T)
 
     graph = None
     if not args.no_graph:
@@ -271,6 +283,24 @@ def main():
                 ev2[i - args.warmup][1].record(s)
     s.synchronize()
     e2e_ms = float(sum(a.elapsed_time(b) for a, b in ev2))
+
+    # prefill path: per-kernel CUDA-event durations on the launching stream (separate eager pass)
+    prefill = layer.prefill_path(T)
+    kernels_ms = None
+    if prefill:
+        lib = capi.lib()
+        names = ("router", "topk", "dispatch", "actq", "gate_up", "down", "combine")
+        acc = np.zeros(len(names))
+        buf = (C.c_float * len(names))()
+        lib.moeb_prefill_profile(1)
+        with torch.cuda.stream(s):
+            for i in range(args.steps):
+                flush.zero_()
+                layer(x, out, stream=s)
+                capi.check(lib.moeb_prefill_profile_read(buf, len(names)))
+                acc += np.array(buf[:])
+        lib.moeb_prefill_profile(0)
+        kernels_ms = dict(zip(names, (acc / args.steps).tolist()))
     err = layer.device_error()
 
     tot = torch.tensor([dev_ms, e2e_ms], dtype=torch.float64, device=dev)
@@ -280,31 +310,53 @@ def main():
     tokens = T * args.steps * world
     value = tokens / (dev_ms / 1e3)
     e2e = tokens / (e2e_ms / 1e3)
-    hbm, _, peak_kind = measured_peaks()
+    hbm, tflops_peak, peak_kind = measured_peaks()
     avg_ms = dev_ms / args.steps
     achieved_gbs = alg_bytes / (avg_ms / 1e3) / 1e9
+    if prefill:
+        P = T * host.top_k
+        kflops = {"gate_up": 2 * P * 2 * host.n_ff * host.d_model, "down": 2 * P * host.d_model * host.n_ff}
+        top = max(kernels_ms, key=kernels_ms.get)
+        if top in kflops:
+            ach = kflops[top] / (kernels_ms[top] / 1e3) / 1e12
+            roofline = {"bound": "tensor", "achieved": ach, "peak": tflops_peak, "unit": "TFLOP/s",
+                        "frac": ach / tflops_peak, "traffic": measured_traffic(f"{cfg.name}:{top}"),
+                        "peak_kind": f"{peak_kind} dense bf16 (burst); the kernel issues kind::f16 MMAs",
+                        "kernel": top, "kernel_ms": kernels_ms[top],
+                        "scope": f"pf_{top}_kernel, algorithmic FLOPs {kflops[top]} per launch "
+                                 f"(2 x pairs x rows x K), CUDA events on the launching stream"}
+        else:
+            roofline = {"bound": "hbm", "achieved": None, "peak": hbm, "unit": "GB/s", "frac": None,
+                        "traffic": None, "kernel": top, "kernel_ms": kernels_ms[top]}
+        roofline["layer_tflops"] = workload.layer_flops(host, T) / (avg_ms / 1e3) / 1e12
+        roofline["kernels_ms"] = kernels_ms
+    else:
+        roofline = {"bound": "hbm", "achieved": achieved_gbs, "peak": hbm, "unit": "GB/s",
+                    "frac": achieved_gbs / hbm, "traffic": measured_traffic(cfg.name), "peak_kind": peak_kind,
+                    "scope": "whole layer forward (one cooperative fused kernel per 8-token chunk), "
+                             f"algorithmic bytes {alg_bytes} per step"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = time_reference(host, x_host, 1, 1000, args.cpu_sample_s)
+        # a bounded sample: at most 256 tokens of the batch (the CPU cost per token is flat in T)
+        cpu = time_reference(host, x_host[:256], 1, 1000, args.cpu_sample_s)
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": avg_ms, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "q8 int dot / f32",
+            "vs_baseline": None,
+            "dtype": "int8 x q4/q5 integer dots on fp16-exact tcgen05 MMAs / f32" if prefill else "q8 int dot / f32",
             "data": "synthetic (seeded N(0,0.02) weights quantised to ggml formats, N(0,1) activations)",
             "config": {"workload": cfg.name, "n_tokens": T, "layers": 1, "d_model": cfg.d_model,
                        "n_expert": cfg.n_expert, "top_k": cfg.top_k, "hot_experts": len(cfg.hot),
                        "parallelism": f"replicas{world}" if world > 1 else "single",
                        "l2": "flushed between steps (256 MiB write, not timed)",
+                       "path": "prefill (tcgen05 grouped GEMMs)" if prefill else "decode (fused GEMV kernel)",
                        "cuda_graph": graph is not None, "unique_experts": int(np.unique(ids.cpu().numpy()).size)},
             "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": int(x_host.nbytes),
                     "d2h_bytes_per_step": int(x_host.nbytes)},
             "gpu_launches": launches_per_step * args.steps,
-            "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": hbm, "unit": "GB/s",
-                         "frac": achieved_gbs / hbm, "traffic": None, "peak_kind": peak_kind,
-                         "scope": "whole layer forward (4 PDL-chained kernels), algorithmic bytes "
-                                  f"{alg_bytes} per step"},
+            "roofline": roofline,
             "cpu_baseline": cpu,
             "clocks": clk.summary(),
             "device_error": err,

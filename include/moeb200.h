@@ -87,15 +87,35 @@ const char *moeb_version(void);
  * range; 4: a capacity limit was exceeded). */
 int32_t     moeb_device_error(void *stream);
 
-/* Workspace bytes moeb_layer_forward needs for n_tokens tokens. */
+/* Workspace bytes moeb_layer_forward needs for n_tokens tokens (the decode path needs one 8-token
+ * chunk's worth for any n_tokens; the prefill path grows with n_tokens, dominated by the f32 down
+ * outputs of every routed pair: n_tokens * top_k * d_model * 4 bytes). */
 size_t moeb_layer_workspace_size(const moeb_layer *L, int32_t n_tokens);
 
 /* One whole MoE layer, router to combine (new; the graph-level unit the benchmark measures).
  * x: f32 [n_tokens][d_model]; out: f32 [n_tokens][d_model]. The workspace must stay untouched
  * until the stream reaches the end of the call. Kernels are chained with programmatic dependent
- * launch; the call is stream-ordered and capturable in a CUDA graph. */
+ * launch; the call is stream-ordered and capturable in a CUDA graph.
+ * Batches below the prefill threshold run the decode path (one fused cooperative kernel per
+ * 8 tokens, integer dot-product GEMVs); larger ones the prefill path (grouped GEMMs on the
+ * tcgen05 tensor cores). Both reproduce the reference's integer block dot products. */
 int moeb_layer_forward(const moeb_layer *L, const float *x, int32_t n_tokens, float *out,
                        const moeb_layer_aux *aux, void *workspace, size_t workspace_bytes, void *stream);
+
+/* Sets the smallest batch that moeb_layer_forward runs on the prefill path (default 64; values
+ * <= 0 leave it unchanged) and returns the previous value. Process-wide. No counterpart in the
+ * reference (its ggml-cuda backend picks mul_mat_vec_q or mul_mat_q by batch size internally,
+ * ggml-cuda.cu). Layers whose shape the prefill kernels do not cover (n_ff not a multiple of 64,
+ * d_model not a multiple of 128, d_model > 4096 or n_ff > 1024) always take the decode path. */
+int32_t moeb_set_prefill_min_tokens(int32_t n_tokens);
+
+/* Profiling of the prefill path (no counterpart in the reference): while enabled, every prefill
+ * forward on the current device records CUDA events around its seven kernels (router, top-k,
+ * dispatch, activation quantisation, gate_up, down, combine) on the caller's stream. Events
+ * between kernels keep them from overlapping, so use it on a separate measurement pass.
+ * moeb_prefill_profile_read waits for the last profiled call and writes up to n durations (ms). */
+int moeb_prefill_profile(int32_t enable);
+int moeb_prefill_profile_read(float *ms, int32_t n);
 
 /* Allocation-free variant of moeb_layer_forward. No counterpart in the reference.
  *
@@ -109,9 +129,9 @@ int moeb_layer_forward(const moeb_layer *L, const float *x, int32_t n_tokens, fl
  * library routine.
  *
  * Limits and rules:
- *  - a layer whose workspace (moeb_layer_workspace_size, which tops out at one 8-token chunk)
- *    exceeds MOEB_STATIC_SCRATCH_BYTES is rejected with MOEB_ESPACE (the Gemma-4 26B-A4B layer
- *    needs about 1.1 MB, for any n_tokens);
+ *  - it always runs the decode path (chunks of 8 tokens), whose workspace is one chunk's worth
+ *    for any n_tokens; a layer whose chunk workspace exceeds MOEB_STATIC_SCRATCH_BYTES is
+ *    rejected with MOEB_ESPACE (the Gemma-4 26B-A4B layer needs about 1.1 MB);
  *  - the first call on a device does one-time set-up there (format tables, the device address of
  *    the static array); make that first call before any stream capture on that device;
  *  - all calls share the one array per device and it keeps the last call's contents: calls that

@@ -160,6 +160,52 @@ LayerWs carve(const moeb_layer *L, int T, uint8_t *base) {
     return w;
 }
 
+// prefill path workspace (whole call at once)
+struct PrefillWs {
+    float *logits, *w, *xd, *ad, *y;
+    int32_t *ids, *cnt, *off, *perm, *pos, *n_tiles;
+    PfTile *tiles;
+    int8_t *xq8, *a8;
+    int16_t *xbs;
+    size_t bytes;
+};
+
+PrefillWs carve_prefill(const moeb_layer *L, int T, uint8_t *base) {
+    PrefillWs w{};
+    const size_t P = (size_t)T * L->top_k, E = L->n_expert, d = L->d_model, nff = L->n_ff, nsb = d / QK_K;
+    size_t o = 0;
+    auto take = [&](size_t n) { size_t at = o; o = align_up(o + n, 256); return base ? base + at : nullptr; };
+    w.logits = (float *)take(sizeof(float) * T * E);
+    w.ids = (int32_t *)take(sizeof(int32_t) * P);
+    w.w = (float *)take(sizeof(float) * P);
+    w.cnt = (int32_t *)take(sizeof(int32_t) * E);
+    w.off = (int32_t *)take(sizeof(int32_t) * (E + 1));
+    w.perm = (int32_t *)take(sizeof(int32_t) * P);
+    w.pos = (int32_t *)take(sizeof(int32_t) * P);
+    w.n_tiles = (int32_t *)take(16);
+    w.tiles = (PfTile *)take(sizeof(PfTile) * prefill_max_tiles((int)P, (int)E));
+    w.xq8 = (int8_t *)take((size_t)T * d);
+    w.xd = (float *)take(sizeof(float) * T * nsb);
+    w.xbs = (int16_t *)take(sizeof(int16_t) * T * nsb * 16);
+    w.a8 = (int8_t *)take(P * nff);
+    w.ad = (float *)take(sizeof(float) * P * (nff / 32));
+    w.y = (float *)take(sizeof(float) * P * d);
+    w.bytes = o;
+    return w;
+}
+
+// Batches of at least this many tokens take the prefill path (when the shape allows it).
+std::atomic<int32_t> g_prefill_min{64};
+
+bool prefill_shape_ok(const moeb_layer *L) {
+    return L->n_ff % 64 == 0 && L->d_model % 128 == 0 && L->d_model / QK_K <= kPrefillMaxSb &&
+           L->n_ff / 32 <= kPrefillMaxBlk;
+}
+
+bool use_prefill(const moeb_layer *L, int32_t n_tokens) {
+    return n_tokens >= g_prefill_min.load() && prefill_shape_ok(L);
+}
+
 PoolView pool_view(const moeb_pool &pl, bool gate_up) {
     PoolView v{};
     v.w = (const uint8_t *)(gate_up ? pl.w_gu : pl.w_down);
@@ -197,14 +243,42 @@ extern "C" int32_t moeb_device_error(void *stream) {
     return v;
 }
 
-extern "C" size_t moeb_layer_workspace_size(const moeb_layer *L, int32_t n_tokens) {
+size_t moeb::chunk_workspace_size(const moeb_layer *L, int32_t n_tokens) {
     if (!L || n_tokens <= 0) return 0;
     const int T = n_tokens < kFusedTokens ? n_tokens : kFusedTokens;
     return carve(L, T, nullptr).bytes;
 }
 
-extern "C" int moeb_layer_forward(const moeb_layer *L, const float *x, int32_t n_tokens, float *out,
-                                  const moeb_layer_aux *aux, void *workspace, size_t workspace_bytes, void *stream) {
+extern "C" size_t moeb_layer_workspace_size(const moeb_layer *L, int32_t n_tokens) {
+    if (!L || n_tokens <= 0) return 0;
+    if (use_prefill(L, n_tokens)) return carve_prefill(L, n_tokens, nullptr).bytes;
+    return chunk_workspace_size(L, n_tokens);
+}
+
+extern "C" int moeb_prefill_profile(int32_t enable) {
+    prefill_profile_enable(enable != 0);
+    return MOEB_OK;
+}
+
+extern "C" int moeb_prefill_profile_read(float *ms, int32_t n) {
+    if (!ms || n <= 0) return fail(MOEB_EINVAL, "moeb_prefill_profile_read: null or empty output");
+    if (prefill_profile_read(ms, n) != 0)
+        return fail(MOEB_EINVAL, "no profiled prefill call on this device (moeb_prefill_profile(1) first)");
+    return MOEB_OK;
+}
+
+extern "C" int32_t moeb_set_prefill_min_tokens(int32_t n_tokens) {
+    const int32_t prev = g_prefill_min.load();
+    if (n_tokens > 0) g_prefill_min.store(n_tokens);
+    return prev;
+}
+
+static int forward_chunks(const moeb_layer *L, const float *x, int32_t n_tokens, float *out,
+                          const moeb_layer_aux *aux, void *workspace, cudaStream_t s, int n_sms);
+
+// argument checks shared by both paths of the layer forward
+static int check_forward(const moeb_layer *L, const float *x, int32_t n_tokens, float *out, void *workspace,
+                         size_t workspace_bytes, size_t need, int *n_sms) {
     int rc = check_layer(L);
     if (rc) return rc;
     if (n_tokens < 0) return fail(MOEB_EINVAL, "n_tokens %d < 0", n_tokens);
@@ -212,14 +286,80 @@ extern "C" int moeb_layer_forward(const moeb_layer *L, const float *x, int32_t n
     if (!x || !out) return fail(MOEB_EINVAL, "null x / out");
     if (!aligned16(x) || !aligned16(out) || !aligned16(L->w_router))
         return fail(MOEB_EINVAL, "x, out and router weights must be 16-byte aligned");
-    int n_sms = 0;
-    rc = ensure_device(&n_sms);
+    rc = ensure_device(n_sms);
     if (rc) return rc;
-    const size_t need = moeb_layer_workspace_size(L, n_tokens);
     if (!workspace || workspace_bytes < need)
         return fail(MOEB_ESPACE, "workspace of %zu bytes, %zu needed", workspace_bytes, need);
     if (!aligned16(workspace)) return fail(MOEB_EINVAL, "workspace must be 16-byte aligned");
-    cudaStream_t s = (cudaStream_t)stream;
+    return MOEB_OK;
+}
+
+// The prefill path: seven PDL-chained kernels, the expert matmuls on tcgen05 tensor cores.
+static int forward_prefill(const moeb_layer *L, const float *x, int32_t T, float *out, const moeb_layer_aux *aux,
+                           void *workspace, cudaStream_t s, int n_sms) {
+    const int d = L->d_model, k = L->top_k, E = L->n_expert, P = T * k;
+    PrefillWs w = carve_prefill(L, T, (uint8_t *)workspace);
+    PrefillArgs a{};
+    a.w_router = L->w_router;
+    a.b_router = L->b_router;
+    a.x = x;
+    a.T = T; a.E = E; a.d = d; a.k = k; a.nff = L->n_ff;
+    a.res = {L->hot.n, L->exp_slot, L->slot_exp, L->slot_state};
+    a.hot_gu = pool_view(L->hot, true);
+    a.cold_gu = pool_view(L->cold, true);
+    a.hot_dn = pool_view(L->hot, false);
+    a.cold_dn = pool_view(L->cold, false);
+    a.logits = w.logits; a.ids = w.ids; a.w = w.w;
+    a.cnt = w.cnt; a.off = w.off; a.perm = w.perm; a.pos = w.pos;
+    a.tiles = w.tiles; a.n_tiles = w.n_tiles;
+    a.xq8 = w.xq8; a.xd = w.xd; a.xbs = w.xbs;
+    a.a8 = w.a8; a.ad = w.ad;
+    a.h = aux ? aux->gate_up : nullptr;
+    a.y = w.y;
+    a.out = out;
+    a.y_pairs = aux ? aux->down : nullptr;
+    cudaError_t e = launch_prefill(a, s, n_sms);
+    if (e != cudaSuccess) return MOEB_ECUDA;   // launch_prefill recorded the failing kernel
+    if (aux) {
+        struct Cp { void *dst; const void *src; size_t n; } cps[] = {
+            {aux->logits, w.logits, sizeof(float) * T * E},
+            {aux->ids, w.ids, sizeof(int32_t) * P},
+            {aux->weights, w.w, sizeof(float) * P},
+            {aux->counts, w.cnt, sizeof(int32_t) * E},
+            {aux->offsets, w.off, sizeof(int32_t) * (E + 1)},
+            {aux->perm, w.perm, sizeof(int32_t) * P},
+        };
+        for (auto &c : cps) {
+            if (!c.dst) continue;
+            e = cudaMemcpyAsync(c.dst, c.src, c.n, cudaMemcpyDeviceToDevice, s);
+            if (e != cudaSuccess) return cuda_fail(e, "aux copy");
+        }
+    }
+    return MOEB_OK;
+}
+
+extern "C" int moeb_layer_forward(const moeb_layer *L, const float *x, int32_t n_tokens, float *out,
+                                  const moeb_layer_aux *aux, void *workspace, size_t workspace_bytes, void *stream) {
+    int n_sms = 0;
+    int rc = check_forward(L, x, n_tokens, out, workspace, workspace_bytes,
+                           L ? moeb_layer_workspace_size(L, n_tokens) : 0, &n_sms);
+    if (rc || n_tokens == 0) return rc;
+    if (use_prefill(L, n_tokens))
+        return forward_prefill(L, x, n_tokens, out, aux, workspace, (cudaStream_t)stream, n_sms);
+    return forward_chunks(L, x, n_tokens, out, aux, workspace, (cudaStream_t)stream, n_sms);
+}
+
+int moeb::layer_forward_chunked(const moeb_layer *L, const float *x, int32_t n_tokens, float *out, void *workspace,
+                                size_t workspace_bytes, void *stream) {
+    int n_sms = 0;
+    int rc = check_forward(L, x, n_tokens, out, workspace, workspace_bytes, chunk_workspace_size(L, n_tokens), &n_sms);
+    if (rc || n_tokens == 0) return rc;
+    return forward_chunks(L, x, n_tokens, out, nullptr, workspace, (cudaStream_t)stream, n_sms);
+}
+
+// The decode path: one fused cooperative kernel per chunk of up to kFusedTokens tokens.
+static int forward_chunks(const moeb_layer *L, const float *x, int32_t n_tokens, float *out, const moeb_layer_aux *aux,
+                          void *workspace, cudaStream_t s, int n_sms) {
     const int d = L->d_model, k = L->top_k, E = L->n_expert;
     const Residency res = {L->hot.n, L->exp_slot, L->slot_exp, L->slot_state};
 

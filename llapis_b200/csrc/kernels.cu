@@ -12,6 +12,7 @@
 #include "common.cuh"
 
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 
 #include "moeb200.h"
@@ -1437,6 +1438,12 @@ __global__ void __launch_bounds__(kGemvThreads, 1) fused_decode_kernel(FusedPara
     if (warp == 0) FTRACE(9);
 }
 
+}  // namespace moeb
+
+#include "prefill.cuh"
+
+namespace moeb {
+
 // ------------------------------------------------------------------ Q8_K activations for the per-kind path
 __global__ void __launch_bounds__(kThreads) quant_q8k_kernel(const float *x, uint8_t *dst, int d, int stride) {
     const int t = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -1634,6 +1641,154 @@ cudaError_t launch_fused(const FusedArgs &a, cudaStream_t s, int n_sms) {
     return cudaLaunchKernelExC(&cfg, (const void *)fused_decode_kernel, args);
 }
 
+// Opt-in to more than 48 KB of dynamic shared memory, once per device and kernel.
+static cudaError_t smem_optin(const void *fn, size_t bytes, unsigned *done_mask, int bit) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 32) return cudaErrorInvalidDevice;
+    static std::mutex mu;
+    std::lock_guard<std::mutex> lk(mu);
+    if (done_mask[dev] & (1u << bit)) return cudaSuccess;
+    e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    if (e == cudaSuccess) done_mask[dev] |= 1u << bit;
+    return e;
+}
+
+// Optional per-kernel CUDA events around the seven prefill launches (moeb_prefill_profile).
+namespace {
+struct PfProfile {
+    cudaEvent_t ev[kPrefillKernels + 1] = {};
+    bool recorded = false;
+};
+std::atomic<bool> g_pf_prof_on{false};
+std::mutex g_pf_prof_mu;
+PfProfile g_pf_prof[32];
+}  // namespace
+
+static cudaError_t prof_mark(cudaStream_t s, int i) {
+    if (!g_pf_prof_on.load(std::memory_order_relaxed)) return cudaSuccess;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess || dev < 0 || dev >= 32) return e;
+    std::lock_guard<std::mutex> lk(g_pf_prof_mu);
+    PfProfile &pp = g_pf_prof[dev];
+    if (!pp.ev[i]) {
+        e = cudaEventCreate(&pp.ev[i]);
+        if (e != cudaSuccess) return e;
+    }
+    if (i == kPrefillKernels) pp.recorded = true;
+    return cudaEventRecord(pp.ev[i], s);
+}
+
+int prefill_profile_read(float *ms, int n) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 32) return -1;
+    std::lock_guard<std::mutex> lk(g_pf_prof_mu);
+    PfProfile &pp = g_pf_prof[dev];
+    if (!pp.recorded) return -1;
+    if (cudaEventSynchronize(pp.ev[kPrefillKernels]) != cudaSuccess) return -1;
+    for (int i = 0; i < n && i < kPrefillKernels; ++i)
+        if (cudaEventElapsedTime(&ms[i], pp.ev[i], pp.ev[i + 1]) != cudaSuccess) return -1;
+    return 0;
+}
+
+void prefill_profile_enable(bool on) { g_pf_prof_on.store(on); }
+
+// launch_ex that, on failure, records which kernel failed and its compiled resource needs
+static cudaError_t pf_launch(const char *name, const void *fn, dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                             bool pdl, void **args) {
+    cudaError_t e = launch_ex(fn, grid, block, smem, s, pdl, args);
+    if (e != cudaSuccess) {
+        cudaFuncAttributes fa{};
+        cudaFuncGetAttributes(&fa, fn);
+        set_last_error(MOEB_ECUDA, "%s launch (grid %u, block %u, dynamic smem %zu): %s [regs %d, max threads %d, "
+                                   "static smem %zu, max dynamic smem %d]",
+                       name, grid.x * grid.y, block.x, smem, cudaGetErrorString(e), fa.numRegs, fa.maxThreadsPerBlock,
+                       fa.sharedSizeBytes, fa.maxDynamicSharedSizeBytes);
+    }
+    return e;
+}
+
+cudaError_t launch_prefill(const PrefillArgs &a, cudaStream_t s, int n_sms) {
+    static unsigned optin[32];
+    cudaError_t e = smem_optin((const void *)pf_gate_up_kernel, sizeof(GuSmem), optin, 0);
+    if (e == cudaSuccess) e = smem_optin((const void *)pf_down_kernel, sizeof(DnSmem), optin, 1);
+    if (e != cudaSuccess) return e;
+    const int T = a.T, E = a.E, d = a.d, k = a.k;
+    int mark = 0;
+    if ((e = prof_mark(s, mark++)) != cudaSuccess) return e;
+    {
+        const float *W = a.w_router, *b = a.b_router, *x = a.x;
+        float *lg = a.logits;
+        int t = T, ne = E, dd = d;
+        void *args[] = {&W, &b, &x, &lg, &t, &ne, &dd};
+        e = pf_launch("pf_router_kernel", (const void *)pf_router_kernel, dim3((T + kRtTok - 1) / kRtTok, (E + kRtExp - 1) / kRtExp),
+                      dim3(256), 0, s, true, args);
+        if (e != cudaSuccess) return e;
+        if ((e = prof_mark(s, mark++)) != cudaSuccess) return e;
+    }
+    {
+        const float *lg = a.logits;
+        int32_t *ids = a.ids;
+        float *w = a.w;
+        int t = T, ne = E, kk = k;
+        void *args[] = {&lg, &ids, &w, &t, &ne, &kk};
+        e = pf_launch("pf_topk_kernel", (const void *)pf_topk_kernel, dim3((T + 7) / 8), dim3(256), 0, s, true, args);
+        if (e != cudaSuccess) return e;
+        if ((e = prof_mark(s, mark++)) != cudaSuccess) return e;
+    }
+    {
+        PfDispatchParams dp{};
+        dp.ids = a.ids; dp.T = T; dp.E = E; dp.k = k;
+        dp.res = a.res;
+        dp.hot_n = a.hot_gu.w ? a.hot_gu.n : 0;
+        dp.cold_n = a.cold_gu.w ? a.cold_gu.n : 0;
+        dp.cnt = a.cnt; dp.off = a.off; dp.perm = a.perm; dp.pos = a.pos;
+        dp.tiles = a.tiles; dp.n_tiles = a.n_tiles;
+        void *args[] = {&dp};
+        e = pf_launch("pf_dispatch_kernel", (const void *)pf_dispatch_kernel, dim3(1), dim3(1024), 0, s, true, args);
+        if (e != cudaSuccess) return e;
+        if ((e = prof_mark(s, mark++)) != cudaSuccess) return e;
+    }
+    {
+        const float *x = a.x;
+        int8_t *q = a.xq8;
+        float *xd = a.xd;
+        int16_t *bs = a.xbs;
+        int t = T, dd = d;
+        void *args[] = {&x, &q, &xd, &bs, &t, &dd};
+        e = pf_launch("pf_actq_kernel", (const void *)pf_actq_kernel, dim3((T * (d / QK_K) + 7) / 8), dim3(256), 0, s, true, args);
+        if (e != cudaSuccess) return e;
+        if ((e = prof_mark(s, mark++)) != cudaSuccess) return e;
+    }
+    PfParams p{};
+    p.T = T; p.E = E; p.d = d; p.k = k; p.nff = a.nff;
+    p.gu[0] = a.hot_gu; p.gu[1] = a.cold_gu; p.dn[0] = a.hot_dn; p.dn[1] = a.cold_dn;
+    p.perm = a.perm; p.tiles = a.tiles; p.n_tiles = a.n_tiles;
+    p.xq8 = a.xq8; p.xd = a.xd; p.xbs = a.xbs;
+    p.a8 = a.a8; p.ad = a.ad; p.h = a.h; p.y = a.y;
+    {
+        void *args[] = {&p};
+        e = pf_launch("pf_gate_up_kernel", (const void *)pf_gate_up_kernel, dim3(n_sms), dim3(kPfThreads), sizeof(GuSmem), s, true, args);
+        if (e != cudaSuccess) return e;
+        if ((e = prof_mark(s, mark++)) != cudaSuccess) return e;
+        e = pf_launch("pf_down_kernel", (const void *)pf_down_kernel, dim3(n_sms), dim3(kPfThreads), sizeof(DnSmem), s, true, args);
+        if (e != cudaSuccess) return e;
+        if ((e = prof_mark(s, mark++)) != cudaSuccess) return e;
+    }
+    {
+        const float *y = a.y, *w = a.w;
+        const int32_t *pos = a.pos;
+        float *out = a.out, *yp = a.y_pairs;
+        int t = T, kk = k, dd = d;
+        void *args[] = {&y, &pos, &w, &out, &yp, &t, &kk, &dd};
+        e = pf_launch("pf_combine_kernel", (const void *)pf_combine_kernel, dim3(T), dim3(256), 0, s, true, args);
+        if (e != cudaSuccess) return e;
+    }
+    return prof_mark(s, mark++);
+}
+
 cudaError_t launch_quant_q8k(const float *x, uint8_t *dst, int rows, int d, int stride, cudaStream_t s) {
     quant_q8k_kernel<<<rows, kThreads, 0, s>>>(x, dst, d, stride);
     return cudaGetLastError();
@@ -1692,12 +1847,15 @@ extern "C" int moeb_trace_read(void *host, size_t bytes) {
 extern "C" int moeb_strace_read(void *host, size_t bytes) {
     return cudaMemcpyFromSymbol(host, moeb::g_strace, bytes) == cudaSuccess ? 0 : -3;
 }
+extern "C" int moeb_ptrace_read(void *host, size_t bytes) {
+    return cudaMemcpyFromSymbol(host, moeb::g_ptrace, bytes) == cudaSuccess ? 0 : -3;
+}
 #endif
 
 extern "C" int moeb_layer_forward_static(const moeb_layer *L, const float *x, int32_t n_tokens, float *out,
                                          void *stream) {
     using namespace moeb;
-    const size_t need = moeb_layer_workspace_size(L, n_tokens);
+    const size_t need = chunk_workspace_size(L, n_tokens);
     if (n_tokens > 0 && need > MOEB_STATIC_SCRATCH_BYTES)
         return set_last_error(MOEB_ESPACE, "moeb_layer_forward_static: this layer needs a %zu-byte workspace; the "
                                            "static scratch holds %u bytes (use moeb_layer_forward)",
@@ -1723,5 +1881,5 @@ extern "C" int moeb_layer_forward_static(const moeb_layer *L, const float *x, in
     }
     // Every byte of the workspace the forward reads is written earlier in the same forward, so the
     // previous call's contents need no clearing.
-    return moeb_layer_forward(L, x, n_tokens, out, nullptr, scratch, MOEB_STATIC_SCRATCH_BYTES, stream);
+    return layer_forward_chunked(L, x, n_tokens, out, scratch, MOEB_STATIC_SCRATCH_BYTES, stream);
 }

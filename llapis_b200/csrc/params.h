@@ -115,6 +115,46 @@ struct FusedArgs {
 };
 MOEB_HD inline int fused_sync_words(int T, int d) { return kFusedTokens * kMaxTopK + T * ((d + 63) / 64); }
 
+// the prefill path (tcgen05 grouped GEMMs; prefill.cuh)
+constexpr int kPrefillTile = 128;        // routed pairs per expert tile (MMA N)
+constexpr int kPrefillMaxSb = 16;        // d_model <= 4096
+constexpr int kPrefillMaxBlk = 32;       // n_ff <= 1024
+// One expert tile: up to kPrefillTile consecutive slots of the expert-sorted pair order.
+struct PfTile {
+    int32_t cls;     // 0 hot pool, 1 cold pool
+    int32_t widx;    // entry of that pool (slot or expert)
+    int32_t slot0;   // first slot
+    int32_t n;       // pairs
+};
+MOEB_HD inline int prefill_max_tiles(int P, int E) { return P / kPrefillTile + E + 1; }
+struct PrefillArgs {
+    const float *w_router, *b_router, *x;
+    int32_t T, E, d, k, nff;
+    Residency res;
+    PoolView hot_gu, cold_gu, hot_dn, cold_dn;
+    float *logits;              // [T][E]
+    int32_t *ids;               // [T][k]
+    float *w;                   // [T][k]
+    int32_t *cnt, *off;         // [E], [E + 1]
+    int32_t *perm, *pos;        // [P] slot -> pair, pair -> slot (-1: expert without a pool)
+    PfTile *tiles;              // [prefill_max_tiles]
+    int32_t *n_tiles;
+    int8_t *xq8;                // [T][d]
+    float *xd;                  // [T][d / 256]
+    int16_t *xbs;               // [T][d / 256][16]
+    int8_t *a8;                 // [P][nff]
+    float *ad;                  // [P][nff / 32]
+    float *h;                   // optional [P][2 nff] gate_up outputs, pair order
+    float *y;                   // [P][d] down outputs, slot order
+    float *out;                 // [T][d]
+    float *y_pairs;             // optional [P][d] down outputs, pair order
+};
+cudaError_t launch_prefill(const PrefillArgs &a, cudaStream_t s, int n_sms);
+// router, top-k, dispatch, activation quantisation, gate_up, down, combine
+constexpr int kPrefillKernels = 7;
+void prefill_profile_enable(bool on);
+int prefill_profile_read(float *ms, int n);
+
 MOEB_HD inline int xq_stride_bytes(int d) { return (int)(((d / QK_K) * B_Q8_K + 15) / 16 * 16); }
 // Q8_0 activation row in shared memory: qs[nb][32] | d[nb] f32 | qsum[nb] i32
 MOEB_HD inline int q80_stride(int d_in) { return ((d_in / 32) * 40 + 15) / 16 * 16; }
@@ -133,6 +173,14 @@ cudaError_t launch_quant_act(int32_t vdt, const float *x, void *dst, int64_t row
 // device state: format tables, GELU table upload, error word
 cudaError_t upload_gelu_table(const uint16_t *host_table, cudaStream_t s);
 cudaError_t read_and_clear_error(int32_t *out, cudaStream_t s);
+// the decode-chunk path of the layer forward with its own (one-chunk) workspace bound; the
+// allocation-free entry uses it for every batch size
+}  // namespace moeb
+struct moeb_layer;
+namespace moeb {
+size_t chunk_workspace_size(const moeb_layer *L, int32_t n_tokens);
+int layer_forward_chunked(const moeb_layer *L, const float *x, int32_t n_tokens, float *out, void *workspace,
+                          size_t workspace_bytes, void *stream);
 // records the message moeb_last_error() returns; returns `code`
 int set_last_error(int code, const char *fmt, ...);
 

@@ -1,0 +1,1101 @@
+// Prefill path of the MoE-FFN layer: the same layer as the fused decode kernel, for batches large
+// enough that every routed expert sees many tokens. Seven kernels chained with programmatic
+// dependent launch:
+//
+//   pf_router_kernel   : router logits, f32 GEMM (ggml mul_mat of ffn_gate_inp, gemma4.cpp:403)
+//   pf_topk_kernel     : softmax -> top-k (value desc, index asc) -> normalised weights
+//                        (llama-graph.cpp:1553-1648), one warp per token
+//   pf_dispatch_kernel : histogram, exclusive scan and stable permutation of the routed pairs
+//                        (ggml-cpu.c:1613-1626 grouping; mmid.cu:28 on the GPU) plus the per-expert
+//                        tile list the grouped GEMMs walk
+//   pf_actq_kernel     : Q8_K quantisation of every token (quantize_row_q8_K, x86/quants.c:505)
+//   pf_gate_up_kernel  : tcgen05 grouped GEMM, gate_up of every tile, fused GeGLU (fp16-table GELU,
+//                        vec.h:1414) and Q8_0 quantisation of its output (x86/quants.c:302)
+//   pf_down_kernel     : tcgen05 grouped GEMM, down projection, per-expert down scale
+//   pf_combine_kernel  : out[t] = sum_j w[t,j] * y[t,j] in j order (llama-graph.cpp:1814-1848)
+//
+// Integer-exact tensor-core formulation. ggml-cpu computes the expert matmuls as integer block
+// dot products scaled per block (ggml_vec_dot_q4_K_q8_K, x86/quants.c:1900; _iq2_s_q8_K :2937;
+// _q5_0_q8_0; _iq4_nl_q8_0). The MMAs here reproduce the integer sums exactly with kind::f16
+// operands that are small integers (exactly representable in fp16) and fp32 accumulation, and
+// apply the per-block float scales in the epilogue ("promotion"):
+//   gate_up Q4_K : A = sc_j * q (<= 945), B = q8; one accumulator per 256-value super-block,
+//                  promoted with d_w * d_x. The min term sum_j m_j * bsum_j goes through one extra
+//                  K=16 MMA into a second accumulator: A = [64 m_j | m_j], B = [bsum_j >> 6 |
+//                  bsum_j & 63], promoted with dmin_w * d_x.
+//   gate_up IQ2_S: A = ls * (+-grid) (<= 1333), B = q8, promoted with d_w * d_x / 8.
+//   down Q5_0    : A = q - 16, B = q8 (Q8_0 of the GeGLU output); promoted per 32-block.
+//   down IQ4_NL  : A = kvalues_iq4nl[q], B = q8; promoted per 32-block.
+// Converter warps build the fp16 operand tiles in shared memory (canonical no-swizzle K-major
+// layout: 8-row x 16-byte core matrices), one thread issues the MMAs, accumulators live in TMEM
+// (double- or quadruple-buffered so the MMAs of the next block overlap the promotion of the last),
+// and epilogue warps read them back with tcgen05.ld.
+#pragma once
+
+namespace moeb {
+
+// ---------------------------------------------------------------- tcgen05 / UMMA wrappers
+// Shared-memory matrix descriptor (sm100 UMMA): start address, leading byte offset (distance of
+// the next core matrix along K), stride byte offset (distance of the next 8-row group), version 1,
+// no swizzle.
+__device__ __forceinline__ uint64_t umma_sdesc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+    return (uint64_t)((saddr >> 4) & 0x3fffu) | ((uint64_t)((lbo >> 4) & 0x3fffu) << 16) |
+           ((uint64_t)((sbo >> 4) & 0x3fffu) << 32) | (1ull << 46);
+}
+// Instruction descriptor of kind::f16: fp16 A and B (K-major), fp32 D, shape M x N.
+__device__ __forceinline__ uint32_t umma_idesc_f16(int M, int N) {
+    return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+__device__ __forceinline__ void umma_f16(uint32_t dtmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accum) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(dtmem),
+        "l"(a), "l"(b), "r"(idesc), "r"(accum)
+        : "memory");
+}
+// arrive on `bar` once every MMA this thread issued so far has completed
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_alloc_warp(uint32_t *dst, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(dst)), "r"(ncols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_warp(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+// generic-proxy shared-memory writes -> visible to the tensor core (async proxy)
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+#define MOEB_R16(a) "=r"(a[0]), "=r"(a[1]), "=r"(a[2]), "=r"(a[3]), "=r"(a[4]), "=r"(a[5]), "=r"(a[6]), "=r"(a[7]), \
+    "=r"(a[8]), "=r"(a[9]), "=r"(a[10]), "=r"(a[11]), "=r"(a[12]), "=r"(a[13]), "=r"(a[14]), "=r"(a[15])
+#define MOEB_RW16(a) "+r"(a[0]), "+r"(a[1]), "+r"(a[2]), "+r"(a[3]), "+r"(a[4]), "+r"(a[5]), "+r"(a[6]), "+r"(a[7]), \
+    "+r"(a[8]), "+r"(a[9]), "+r"(a[10]), "+r"(a[11]), "+r"(a[12]), "+r"(a[13]), "+r"(a[14]), "+r"(a[15])
+#define MOEB_LD16 "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+
+// 16 consecutive accumulator columns of this thread's TMEM lane (the wait is tied to the
+// registers so no use of them can be scheduled before it)
+__device__ __forceinline__ void tmem_ld16(uint32_t ta, float (&va)[16]) {
+    uint32_t a[16];
+    asm volatile(MOEB_LD16 : MOEB_R16(a) : "r"(ta));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" : MOEB_RW16(a)::"memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) va[i] = __uint_as_float(a[i]);
+}
+__device__ __forceinline__ void tmem_ld16x2(uint32_t ta, uint32_t tb, float (&va)[16], float (&vb)[16]) {
+    uint32_t a[16], b[16];
+    asm volatile(MOEB_LD16 : MOEB_R16(a) : "r"(ta));
+    asm volatile(MOEB_LD16 : MOEB_R16(b) : "r"(tb));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" : MOEB_RW16(a), MOEB_RW16(b)::"memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) { va[i] = __uint_as_float(a[i]); vb[i] = __uint_as_float(b[i]); }
+}
+
+// Instrumented builds only (-DMOEB_TRACE): SM-clock stamps of CTA 0's converter warp 0, MMA thread
+// and first epilogue warp, per pipeline step.
+#ifdef MOEB_TRACE
+__device__ unsigned long long g_ptrace[2][3][96][3];
+#define PTRACE(k, role, idx, f) \
+    if (blockIdx.x == 0 && (idx) < 96) g_ptrace[k][role][idx][f] = clock64();
+#else
+#define PTRACE(k, role, idx, f)
+#endif
+
+// ---------------------------------------------------------------- shapes of the tensor-core kernels
+constexpr int kPfN = kPrefillTile;    // routed pairs per expert tile = MMA N (accumulator columns)
+constexpr int kPfM = 128;             // weight rows per work unit = MMA M (TMEM lanes)
+constexpr int kPfConvWarps = 4;       // thread i builds A row i (a weight row) and B row i (a pair)
+constexpr int kPfMmaWarp = kPfConvWarps;
+constexpr int kPfEpiWarp0 = kPfConvWarps + 1;
+constexpr int kPfEpiWarps = 8;        // two per TMEM lane quadrant, one per half of the columns
+// 13 warps: at most 4 share an SM sub-partition's 16K registers, so a thread may hold 128
+constexpr int kPfThreads = (kPfConvWarps + 1 + kPfEpiWarps) * 32;
+// gate_up: a stage is half a super-block, 128 values (+ 16 min-term columns in the first half of
+// a Q4_K super-block): 18 core columns of 8 values
+constexpr int kGuKc = 18;
+constexpr int kGuTileBytes = kPfM * kGuKc * 16;
+constexpr int kGuStages = 2;
+constexpr int kGegluBatch = 8;        // GELU-table lookups a warp keeps in flight
+// down: a stage is two 32-blocks (8 core columns); four accumulator buffers of 128 columns
+constexpr int kDnKc = 8;
+constexpr int kDnTileBytes = kPfM * kDnKc * 16;
+constexpr int kDnStages = 6;
+constexpr int kDnAccBufs = 4;
+static_assert(kPfN == 128 && kPfM == 128, "TMEM budget below assumes 128 x 128 tiles");
+
+// byte offset of core row (r, c) of a canonical K-major tile with kc core columns per 8-row group
+__device__ __forceinline__ uint32_t canon_off(int r, int c, int kc) {
+    return (uint32_t)((((r >> 3) * kc + c) << 7) + ((r & 7) << 4));
+}
+
+struct GuSmem {
+    uint8_t a[kGuStages][kGuTileBytes];
+    uint8_t b[kGuStages][kGuTileBytes];
+    float xg[kPfN][64];                 // gate and up results of a unit, for the GeGLU step
+    float xu[kPfN][64];
+    float dxs[kPrefillMaxSb][kPfN];     // Q8_K scale of each tile column, per super-block
+    uint64_t full[kGuStages], empty[kGuStages], accfull[2], accempty[2], done, epibar;
+    uint32_t tmem;
+    int32_t abort;
+};
+struct DnSmem {
+    uint8_t a[kDnStages][kDnTileBytes];
+    uint8_t b[kDnStages][kDnTileBytes];
+    float dxs[kPrefillMaxBlk][kPfN];    // Q8_0 scale of each tile column, per 32-block
+    uint64_t full[kDnStages], empty[kDnStages], accfull[kDnAccBufs], accempty[kDnAccBufs], done, epibar;
+    uint32_t tmem;
+    int32_t abort;
+};
+
+// Bounded mbarrier wait that also gives up once another role of the CTA has given up.
+__device__ __forceinline__ bool pf_wait(uint64_t *bar, uint32_t parity, volatile int32_t *abort) {
+    for (uint32_t i = 0; i < kWaitLimit; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 255u) == 255u && *abort) return false;
+    }
+    atomicOr(&g_error, ERR_MBAR_TIMEOUT);
+    *abort = 1;
+    return false;
+}
+// the abort flag as one value for the whole warp (loop conditions must not split a warp)
+__device__ __forceinline__ bool warp_aborted(volatile int32_t *abort) { return __any_sync(0xffffffffu, *abort != 0); }
+// The same wait taken by every lane of a warp, with one outcome for the whole warp (so that a
+// warp never splits before a .sync.aligned instruction).
+__device__ __forceinline__ bool pf_wait_warp(uint64_t *bar, uint32_t parity, volatile int32_t *abort) {
+    return __all_sync(0xffffffffu, pf_wait(bar, parity, abort));
+}
+// Barrier of the epilogue warps on an mbarrier (count kPfEpiWarps): bounded, unlike bar.sync, so a
+// warp that gave up cannot leave the others waiting for good.
+__device__ __forceinline__ bool epi_barrier(uint64_t *bar, uint32_t &phase, volatile int32_t *abort) {
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) mbar_arrive(bar);
+    const bool ok = pf_wait_warp(bar, phase & 1u, abort);
+    ++phase;
+    return ok;
+}
+
+// ---------------------------------------------------------------- fp16 operand builders
+__device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
+__device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2 *>(&u); }
+// four small unsigned byte values (one per byte of t) times s, as two fp16 pairs. 0x64XX is the
+// fp16 1024 + XX, so (1024 + v) * s - 1024 * s = v * s, exact while v * s < 2048 and
+// (1024 + v) * s < 65504.
+__device__ __forceinline__ void scale4(uint32_t t, __half2 s2, __half2 ns2, uint32_t &o01, uint32_t &o23) {
+    o01 = h2u(__hfma2(u2h(__byte_perm(t, 0x64646464u, 0x5140)), s2, ns2));
+    o23 = h2u(__hfma2(u2h(__byte_perm(t, 0x64646464u, 0x5342)), s2, ns2));
+}
+// four signed bytes as two fp16 pairs (exact): (1024 + (v ^ 0x80)) - 1152 = v
+__device__ __forceinline__ void s8x4_h(uint32_t w, uint32_t &o01, uint32_t &o23) {
+    const uint32_t u = w ^ 0x80808080u;
+    const __half2 off = u2h(0xe480e480u);   // (-1152, -1152)
+    o01 = h2u(__hadd2(u2h(__byte_perm(u, 0x64646464u, 0x5140)), off));
+    o23 = h2u(__hadd2(u2h(__byte_perm(u, 0x64646464u, 0x5342)), off));
+}
+// four unsigned bytes < 32 minus 16, as two fp16 pairs (exact): (1024 + u) - 1040
+__device__ __forceinline__ void u5x4_h(uint32_t t, uint32_t &o01, uint32_t &o23) {
+    const __half2 off = u2h(0xe410e410u);   // (-1040, -1040)
+    o01 = h2u(__hadd2(u2h(__byte_perm(t, 0x64646464u, 0x5140)), off));
+    o23 = h2u(__hadd2(u2h(__byte_perm(t, 0x64646464u, 0x5342)), off));
+}
+__device__ __forceinline__ uint32_t pack_h2i(int a, int b) {
+    return h2u(__floats2half2_rn((float)a, (float)b));   // exact for the small integers used here
+}
+__device__ __forceinline__ void sts128(uint8_t *p, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    *reinterpret_cast<uint4 *>(p) = make_uint4(a, b, c, d);
+}
+
+// 6-bit scale and min of sub-block j of a Q4_K super-block (get_scale_min_k4, ggml-quants.c:822)
+__device__ __forceinline__ void q4k_scale_min(int j, const uint8_t *q, int &sc, int &m) {
+    if (j < 4) {
+        sc = q[j] & 63;
+        m = q[j + 4] & 63;
+    } else {
+        sc = (q[j + 4] & 0xF) | ((q[j - 4] >> 6) << 4);
+        m = (q[j + 4] >> 4) | ((q[j] >> 6) << 4);
+    }
+}
+
+// Raw bytes of one gate_up stage, loaded into registers ahead of their conversion (read-only
+// global loads, so they may be issued before the shared-memory stores of the previous step).
+struct GuARaw {
+    uint4 v[5];   // Q4_K: header (d, dmin, scales) + the 64 qs bytes of this half;
+                  // IQ2_S: grid bytes, sign bytes, qh and scale words of this half (11 words)
+};
+struct GuBRaw {
+    uint4 v[8];   // 128 q8 values
+    uint4 bs[2];  // the 16 bsums of the super-block (first half of a Q4_K super-block only)
+};
+
+__device__ __forceinline__ void gu_a_load(const uint8_t *blk, int h, bool q4, GuARaw &a) {
+    if (q4) {
+        a.v[0] = __ldg(reinterpret_cast<const uint4 *>(blk));
+#pragma unroll
+        for (int i = 0; i < 4; ++i) a.v[1 + i] = __ldg(reinterpret_cast<const uint4 *>(blk + 16 + 64 * h + 16 * i));
+    } else {   // 2-byte aligned block: 16-bit loads
+        const unsigned short *b16 = reinterpret_cast<const unsigned short *>(blk);
+        uint32_t w[11];
+#pragma unroll
+        for (int ii = 0; ii < 4; ++ii) {
+            w[ii] = (uint32_t)__ldg(b16 + 1 + 8 * h + 2 * ii) | ((uint32_t)__ldg(b16 + 2 + 8 * h + 2 * ii) << 16);
+            w[4 + ii] = (uint32_t)__ldg(b16 + 17 + 8 * h + 2 * ii) | ((uint32_t)__ldg(b16 + 18 + 8 * h + 2 * ii) << 16);
+        }
+        w[8] = (uint32_t)__ldg(b16 + 33 + 2 * h) | ((uint32_t)__ldg(b16 + 34 + 2 * h) << 16);
+        w[9] = (uint32_t)__ldg(b16 + 37 + 2 * h) | ((uint32_t)__ldg(b16 + 38 + 2 * h) << 16);
+        w[10] = 0;
+        a.v[0] = make_uint4(w[0], w[1], w[2], w[3]);
+        a.v[1] = make_uint4(w[4], w[5], w[6], w[7]);
+        a.v[2] = make_uint4(w[8], w[9], w[10], 0u);
+    }
+}
+
+// A rows of one gate_up stage (half `h` of a super-block), Q4_K: sc_j * q, then (h == 0) the
+// min-term columns [64 m_0..7 | m_0..7]
+__device__ __forceinline__ void gu_a_q4k(const GuARaw &a, int h, uint8_t *tile, int r) {
+    const uint4 hdr = a.v[0];
+    uint8_t sc12[12];
+    *reinterpret_cast<uint32_t *>(sc12 + 0) = hdr.y;
+    *reinterpret_cast<uint32_t *>(sc12 + 4) = hdr.z;
+    *reinterpret_cast<uint32_t *>(sc12 + 8) = hdr.w;
+    uint32_t W[16];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        W[4 * i] = a.v[1 + i].x; W[4 * i + 1] = a.v[1 + i].y; W[4 * i + 2] = a.v[1 + i].z; W[4 * i + 3] = a.v[1 + i].w;
+    }
+#pragma unroll
+    for (int ii = 0; ii < 2; ++ii) {
+        int slo, mlo, shi, mhi;
+        q4k_scale_min(4 * h + 2 * ii, sc12, slo, mlo);
+        q4k_scale_min(4 * h + 2 * ii + 1, sc12, shi, mhi);
+        const __half2 s2l = __float2half2_rn((float)slo), ns2l = __float2half2_rn(-1024.f * slo);
+        const __half2 s2h = __float2half2_rn((float)shi), ns2h = __float2half2_rn(-1024.f * shi);
+#pragma unroll
+        for (int cq = 0; cq < 4; ++cq) {
+            const uint32_t w0 = W[8 * ii + 2 * cq], w1 = W[8 * ii + 2 * cq + 1];
+            uint32_t o0, o1, o2, o3;
+            scale4(w0 & 0x0f0f0f0fu, s2l, ns2l, o0, o1);
+            scale4(w1 & 0x0f0f0f0fu, s2l, ns2l, o2, o3);
+            sts128(tile + canon_off(r, 8 * ii + cq, kGuKc), o0, o1, o2, o3);
+            scale4((w0 >> 4) & 0x0f0f0f0fu, s2h, ns2h, o0, o1);
+            scale4((w1 >> 4) & 0x0f0f0f0fu, s2h, ns2h, o2, o3);
+            sts128(tile + canon_off(r, 8 * ii + 4 + cq, kGuKc), o0, o1, o2, o3);
+        }
+    }
+    if (h == 0) {
+        int m[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) { int sc; q4k_scale_min(j, sc12, sc, m[j]); }
+        sts128(tile + canon_off(r, 16, kGuKc), pack_h2i(64 * m[0], 64 * m[1]), pack_h2i(64 * m[2], 64 * m[3]),
+               pack_h2i(64 * m[4], 64 * m[5]), pack_h2i(64 * m[6], 64 * m[7]));
+        sts128(tile + canon_off(r, 17, kGuKc), pack_h2i(m[0], m[1]), pack_h2i(m[2], m[3]), pack_h2i(m[4], m[5]),
+               pack_h2i(m[6], m[7]));
+    }
+}
+
+// A rows of one gate_up stage, IQ2_S (dequantize_row_iq2_s, ggml-quants.c:2471): ls * (+-grid)
+// with ls = 2 * scale_nibble + 1; the d / 8 factor goes to the epilogue.
+__device__ __forceinline__ void gu_a_iq2s(const GuARaw &a, uint8_t *tile, int r) {
+    const uint32_t g[4] = {a.v[0].x, a.v[0].y, a.v[0].z, a.v[0].w};
+    const uint32_t sg[4] = {a.v[1].x, a.v[1].y, a.v[1].z, a.v[1].w};
+    const uint32_t qh = a.v[2].x, scb = a.v[2].y;
+#pragma unroll
+    for (int ii = 0; ii < 4; ++ii) {
+        const uint32_t qhb = (qh >> (8 * ii)) & 0xffu, sc = (scb >> (8 * ii)) & 0xffu;
+#pragma unroll
+        for (int l = 0; l < 4; ++l) {
+            const uint32_t idx = ((g[ii] >> (8 * l)) & 0xffu) | (((qhb >> (2 * l)) & 3u) << 8);
+            const uint64_t grid = g_iq2s_grid[idx];
+            const int ls = 2 * (int)((sc >> (4 * (l >> 1))) & 0xfu) + 1;
+            const __half2 s2 = __float2half2_rn((float)ls), ns2 = __float2half2_rn(-1024.f * ls);
+            uint32_t o0, o1, o2, o3;
+            scale4((uint32_t)grid, s2, ns2, o0, o1);
+            scale4((uint32_t)(grid >> 32), s2, ns2, o2, o3);
+            const uint32_t s8 = (sg[ii] >> (8 * l)) & 0xffu;
+            o0 ^= ((s8 & 1u) << 15) | ((s8 & 2u) << 30);
+            o1 ^= ((s8 & 4u) << 13) | ((s8 & 8u) << 28);
+            o2 ^= ((s8 & 16u) << 11) | ((s8 & 32u) << 26);
+            o3 ^= ((s8 & 64u) << 9) | ((s8 & 128u) << 24);
+            sts128(tile + canon_off(r, 4 * ii + l, kGuKc), o0, o1, o2, o3);
+        }
+    }
+}
+
+__device__ __forceinline__ void gu_b_load(const int8_t *q8, const int16_t *bs16, bool ext, GuBRaw &b) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) b.v[i] = __ldg(reinterpret_cast<const uint4 *>(q8 + 16 * i));
+    if (ext) {
+        b.bs[0] = __ldg(reinterpret_cast<const uint4 *>(bs16));
+        b.bs[1] = __ldg(reinterpret_cast<const uint4 *>(bs16 + 8));
+    }
+}
+
+// B rows of one gate_up stage: 128 q8 values of one pair's token (+ the min-term columns
+// [bsum_j >> 6 | bsum_j & 63] of the first half of a Q4_K super-block)
+__device__ __forceinline__ void gu_b(const GuBRaw &b, bool ext, uint8_t *tile, int c) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        uint32_t o0, o1, o2, o3;
+        s8x4_h(b.v[i].x, o0, o1);
+        s8x4_h(b.v[i].y, o2, o3);
+        sts128(tile + canon_off(c, 2 * i, kGuKc), o0, o1, o2, o3);
+        s8x4_h(b.v[i].z, o0, o1);
+        s8x4_h(b.v[i].w, o2, o3);
+        sts128(tile + canon_off(c, 2 * i + 1, kGuKc), o0, o1, o2, o3);
+    }
+    if (ext) {
+        const uint32_t w[8] = {b.bs[0].x, b.bs[0].y, b.bs[0].z, b.bs[0].w, b.bs[1].x, b.bs[1].y, b.bs[1].z, b.bs[1].w};
+        int hi[8], lo[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int sm = (int)(int16_t)(w[j] & 0xffffu) + (int)(int16_t)(w[j] >> 16);   // bsums 2j, 2j+1
+            hi[j] = sm >> 6;     // floor division: sm = 64 * hi + lo, lo in [0, 63]
+            lo[j] = sm & 63;
+        }
+        sts128(tile + canon_off(c, 16, kGuKc), pack_h2i(hi[0], hi[1]), pack_h2i(hi[2], hi[3]), pack_h2i(hi[4], hi[5]),
+               pack_h2i(hi[6], hi[7]));
+        sts128(tile + canon_off(c, 17, kGuKc), pack_h2i(lo[0], lo[1]), pack_h2i(lo[2], lo[3]), pack_h2i(lo[4], lo[5]),
+               pack_h2i(lo[6], lo[7]));
+    }
+}
+
+// Raw bytes of one down stage: two Q5_0 blocks (11 words) or two IQ4_NL blocks (9 words) of a
+// weight row, 4-byte aligned (44- and 36-byte stages of 484- and 396-byte rows)
+struct DnARaw {
+    uint32_t w[11];
+};
+__device__ __forceinline__ void dn_a_load(const uint8_t *src, bool q5, DnARaw &a) {
+    const unsigned int *w = reinterpret_cast<const unsigned int *>(src);
+#pragma unroll
+    for (int i = 0; i < 9; ++i) a.w[i] = __ldg(w + i);
+    a.w[9] = q5 ? __ldg(w + 9) : 0u;
+    a.w[10] = q5 ? __ldg(w + 10) : 0u;
+}
+
+// A rows of one down stage, Q5_0 (dequantize_row_q5_0, ggml-quants.c:442): q - 16 with
+// q = nibble | high bit << 4
+__device__ __forceinline__ void dn_a_q5_0(const DnARaw &a, uint8_t *tile, int r) {
+#pragma unroll
+    for (int bi = 0; bi < 2; ++bi) {
+        uint32_t qh, qs[4];
+        if (bi == 0) {   // d bytes 0-1, qh 2-5, qs 6-21
+            qh = __funnelshift_r(a.w[0], a.w[1], 16);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) qs[i] = __funnelshift_r(a.w[1 + i], a.w[2 + i], 16);
+        } else {         // d bytes 22-23, qh 24-27, qs 28-43
+            qh = a.w[6];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) qs[i] = a.w[7 + i];
+        }
+#pragma unroll
+        for (int cq = 0; cq < 4; ++cq) {
+            // values 8cq .. 8cq+7: low nibbles of qs bytes for cq < 2, high nibbles of bytes 8(cq-2).. for cq >= 2
+            const uint32_t a0 = cq < 2 ? qs[2 * cq] : qs[2 * (cq - 2)] >> 4;
+            const uint32_t a1 = cq < 2 ? qs[2 * cq + 1] : qs[2 * (cq - 2) + 1] >> 4;
+            const uint32_t hb = (qh >> (8 * cq)) & 0xffu;
+            const uint32_t t0 = (a0 & 0x0f0f0f0fu) | ((((hb & 0xfu) * 0x00204081u) & 0x01010101u) << 4);
+            const uint32_t t1 = (a1 & 0x0f0f0f0fu) | ((((hb >> 4) * 0x00204081u) & 0x01010101u) << 4);
+            uint32_t o0, o1, o2, o3;
+            u5x4_h(t0, o0, o1);
+            u5x4_h(t1, o2, o3);
+            sts128(tile + canon_off(r, 4 * bi + cq, kDnKc), o0, o1, o2, o3);
+        }
+    }
+}
+
+// A rows of one down stage, IQ4_NL (dequantize_row_iq4_nl, ggml-quants.c:2653): kvalues[q]
+__device__ __forceinline__ void dn_a_iq4nl(const DnARaw &a, const uint32_t (&kv)[4], uint8_t *tile, int r) {
+#pragma unroll
+    for (int bi = 0; bi < 2; ++bi) {
+        uint32_t qs[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) qs[i] = bi == 0 ? __funnelshift_r(a.w[i], a.w[i + 1], 16) : a.w[5 + i];
+#pragma unroll
+        for (int cq = 0; cq < 4; ++cq) {
+            const uint32_t a0 = cq < 2 ? qs[2 * cq] : qs[2 * (cq - 2)] >> 4;
+            const uint32_t a1 = cq < 2 ? qs[2 * cq + 1] : qs[2 * (cq - 2) + 1] >> 4;
+            uint32_t o0, o1, o2, o3;
+            s8x4_h((uint32_t)iq4nl_lookup4(a0, kv[0], kv[1], kv[2], kv[3]), o0, o1);
+            s8x4_h((uint32_t)iq4nl_lookup4(a1, kv[0], kv[1], kv[2], kv[3]), o2, o3);
+            sts128(tile + canon_off(r, 4 * bi + cq, kDnKc), o0, o1, o2, o3);
+        }
+    }
+}
+
+// B rows of one down stage: 64 Q8_0 values of one pair
+__device__ __forceinline__ void dn_b_load(const int8_t *q8, uint4 (&v)[4]) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = __ldg(reinterpret_cast<const uint4 *>(q8 + 16 * i));
+}
+__device__ __forceinline__ void dn_b(const uint4 (&v)[4], uint8_t *tile, int c) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        uint32_t o0, o1, o2, o3;
+        s8x4_h(v[i].x, o0, o1);
+        s8x4_h(v[i].y, o2, o3);
+        sts128(tile + canon_off(c, 2 * i, kDnKc), o0, o1, o2, o3);
+        s8x4_h(v[i].z, o0, o1);
+        s8x4_h(v[i].w, o2, o3);
+        sts128(tile + canon_off(c, 2 * i + 1, kDnKc), o0, o1, o2, o3);
+    }
+}
+
+struct PfParams {
+    int32_t T, E, d, k, nff;
+    PoolView gu[2], dn[2];            // [0] hot, [1] cold
+    const int32_t *perm;              // [P] slot -> pair (t*k + j)
+    const PfTile *tiles;
+    const int32_t *n_tiles;
+    const int8_t *xq8;                // [T][d] Q8_K values
+    const float *xd;                  // [T][d/256] Q8_K scales
+    const int16_t *xbs;               // [T][d/256][16] Q8_K bsums
+    int8_t *a8;                       // [P slots][nff] Q8_0 values of the GeGLU output
+    float *ad;                        // [P slots][nff/32] Q8_0 scales
+    float *h;                         // optional [P pairs][2 nff] gate_up outputs
+    float *y;                         // [P slots][d] down outputs (scaled)
+};
+
+__device__ __forceinline__ const uint8_t *tile_rows(const PoolView &pv, int widx, int rows, int d_in) {
+    return pool_entry(pv, widx, rows, d_in);
+}
+
+// ---------------------------------------------------------------- gate_up grouped GEMM
+// Work unit (tile, mb): the pairs of one expert tile against 64 gate rows [64 mb, 64 mb + 64) and
+// the matching 64 up rows, so GeGLU pairs sit in the same CTA. Persistent: CTA b takes units
+// b, b + grid, ...; the 11 units of a tile run side by side, sharing its activations in L2.
+__global__ void __launch_bounds__(kPfThreads, 1) pf_gate_up_kernel(PfParams p) {
+    extern __shared__ __align__(1024) uint8_t pf_smem[];
+    GuSmem &S = *reinterpret_cast<GuSmem *>(pf_smem);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (tid == 0) {
+        for (int s = 0; s < kGuStages; ++s) { mbar_init(&S.full[s], kPfConvWarps); mbar_init(&S.empty[s], 1); }
+        for (int b = 0; b < 2; ++b) { mbar_init(&S.accfull[b], 1); mbar_init(&S.accempty[b], kPfEpiWarps); }
+        mbar_init(&S.done, 1);
+        mbar_init(&S.epibar, kPfEpiWarps);
+        S.abort = 0;
+        fence_mbar_init();
+    }
+    if (warp == kPfMmaWarp) tmem_alloc_warp(&S.tmem, 512);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = S.tmem;
+    volatile int32_t *abort = &S.abort;
+    pdl_wait();
+    const int nsb = p.d / QK_K, n_mb = p.nff / 64, k = p.k;
+    const int units = *p.n_tiles * n_mb;
+    const int gu_rows = 2 * p.nff;
+
+    if (warp < kPfConvWarps) {
+        // ------------------------------------------------ converters
+        // Software-pipelined: the B loads of a stage fly while its A rows convert, and the A loads
+        // of the next stage while its B rows convert.
+        int it = 0;
+        GuARaw ar;
+        GuBRaw br;
+        for (int u = blockIdx.x; u < units && !warp_aborted(abort); u += gridDim.x) {
+            const int ti = u / n_mb, mb = u - ti * n_mb;
+            const PfTile tl = p.tiles[ti];
+            const PoolView &pv = p.gu[tl.cls];
+            const bool q4 = pv.type == T_Q4_K;
+            const int bsz = q4 ? B_Q4_K : B_IQ2_S;
+            const int rb = (int)row_bytes(pv.type, p.d);
+            const uint8_t *rows = tile_rows(pv, tl.widx, gu_rows, p.d);
+            const int r = tid, c = tid;        // A row and B row of this thread
+            const int wr = r < 64 ? 64 * mb + r : p.nff + 64 * mb + (r - 64);
+            const uint8_t *arow = rows + (size_t)wr * rb;
+            const int8_t *xrow = nullptr;
+            const int16_t *xbs = nullptr;
+            if (c < tl.n) {
+                const int t = p.perm[tl.slot0 + c] / k;
+                xrow = p.xq8 + (size_t)t * p.d;
+                xbs = p.xbs + (size_t)t * nsb * 16;
+            }
+            gu_a_load(arow, 0, q4, ar);
+            bool ok = true;
+            for (int sb = 0; sb < nsb && ok; ++sb) {
+                for (int h = 0; h < 2; ++h, ++it) {
+                    const int s = it & 1;
+                    if (xrow) gu_b_load(xrow + sb * QK_K + h * 128, xbs + sb * 16, q4 && h == 0, br);
+                    if (tid == 0) PTRACE(0, 0, it, 0);
+                    if (it >= kGuStages && !pf_wait_warp(&S.empty[s], ((it >> 1) & 1) ^ 1, abort)) { ok = false; break; }
+                    if (tid == 0) PTRACE(0, 0, it, 1);
+                    if (q4) gu_a_q4k(ar, h, S.a[s], r);
+                    else gu_a_iq2s(ar, S.a[s], r);
+                    const int nsb_ = sb + h;           // the next stage: (sb, 1) or (sb + 1, 0)
+                    if (nsb_ < nsb) gu_a_load(arow + nsb_ * bsz, h ^ 1, q4, ar);
+                    if (xrow) gu_b(br, q4 && h == 0, S.b[s], c);
+                    if (tid == 0) PTRACE(0, 0, it, 2);
+                    fence_async_smem();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&S.full[s]);
+                }
+            }
+            if (!ok) break;
+        }
+    } else if (warp == kPfMmaWarp) {
+        // ------------------------------------------------ MMA issue (one thread)
+        if (lane == 0) {
+            int it = 0, sbc = 0;
+            const uint32_t sbo = kGuKc * 128;
+            for (int u = blockIdx.x; u < units && !*abort; u += gridDim.x) {
+                const PfTile tl = p.tiles[u / n_mb];
+                const bool q4 = p.gu[tl.cls].type == T_Q4_K;
+                const int N = (tl.n + 15) & ~15;
+                const uint32_t idesc = umma_idesc_f16(kPfM, N);
+                for (int sb = 0; sb < nsb && !*abort; ++sb, ++sbc) {
+                    const int b = sbc & 1;
+                    if (sbc >= 2 && !pf_wait(&S.accempty[b], ((sbc >> 1) & 1) ^ 1, abort)) break;
+                    tc_fence_after();
+                    const uint32_t dmain = tmem + (uint32_t)(b * 256), dmin = dmain + 128;
+                    for (int h = 0; h < 2; ++h, ++it) {
+                        const int s = it & 1;
+                        PTRACE(0, 1, it, 0);
+                        if (!pf_wait(&S.full[s], (it >> 1) & 1, abort)) break;
+                        PTRACE(0, 1, it, 1);
+                        tc_fence_after();
+                        const uint32_t a0 = smem_addr(S.a[s]), b0 = smem_addr(S.b[s]);
+#pragma unroll
+                        for (int ks = 0; ks < 8; ++ks)
+                            umma_f16(dmain, umma_sdesc(a0 + ks * 256, 128, sbo), umma_sdesc(b0 + ks * 256, 128, sbo), idesc,
+                                     (h | ks) != 0);
+                        if (h == 0 && q4)
+                            umma_f16(dmin, umma_sdesc(a0 + 8 * 256, 128, sbo), umma_sdesc(b0 + 8 * 256, 128, sbo), idesc, 0);
+                        umma_commit(&S.empty[s]);
+                        PTRACE(0, 1, it, 2);
+                    }
+                    umma_commit(&S.accfull[b]);
+                }
+            }
+            umma_commit(&S.done);
+            mbar_wait(&S.done, 0);   // issued MMAs always complete; TMEM is freed only after them
+        }
+        __syncwarp();
+    } else {
+        // ------------------------------------------------ epilogue: promotion, GeGLU, Q8_0
+        const int ew = warp - kPfEpiWarp0, et = tid - kPfEpiWarp0 * 32;
+        const int q = warp & 3, ch = ew >> 2;
+        const int r = 32 * q + lane;
+        const int nb32 = p.nff / 32;
+        int sbc = 0;
+        uint32_t eph = 0;
+        for (int u = blockIdx.x; u < units && !warp_aborted(abort); u += gridDim.x) {
+            const int ti = u / n_mb, mb = u - ti * n_mb;
+            const PfTile tl = p.tiles[ti];
+            const PoolView &pv = p.gu[tl.cls];
+            const bool q4 = pv.type == T_Q4_K;
+            const int rb = (int)row_bytes(pv.type, p.d);
+            const int N = (tl.n + 15) & ~15;
+            const int wr = r < 64 ? 64 * mb + r : p.nff + 64 * mb + (r - 64);
+            const uint8_t *arow = tile_rows(pv, tl.widx, gu_rows, p.d) + (size_t)wr * rb;
+            for (int i = et; i < tl.n * nsb; i += kPfEpiWarps * 32) {
+                const int c = i / nsb, sb = i - c * nsb;
+                S.dxs[sb][c] = p.xd[(size_t)(p.perm[tl.slot0 + c] / k) * nsb + sb];
+            }
+            if (!epi_barrier(&S.epibar, eph, abort)) break;
+            float acc[64];
+#pragma unroll
+            for (int i = 0; i < 64; ++i) acc[i] = 0.f;
+            for (int sb = 0; sb < nsb; ++sb, ++sbc) {
+                float dw, dmn = 0.f;
+                if (q4) {
+                    const uint32_t hd = *reinterpret_cast<const uint32_t *>(arow + sb * B_Q4_K);
+                    dw = h2f((uint16_t)(hd & 0xffffu));
+                    dmn = h2f((uint16_t)(hd >> 16));
+                } else {
+                    dw = 0.125f * h2f(*reinterpret_cast<const uint16_t *>(arow + sb * B_IQ2_S));
+                }
+                const int b = sbc & 1;
+                if (et == 0) PTRACE(0, 2, sbc, 0);
+                if (!pf_wait_warp(&S.accfull[b], (sbc >> 1) & 1, abort)) break;
+                if (et == 0) PTRACE(0, 2, sbc, 1);
+                tc_fence_after();
+                const uint32_t tb = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(b * 256);
+#pragma unroll
+                for (int cc = 0; cc < 4; ++cc) {
+                    const int col = 64 * ch + 16 * cc;
+                    if (col < N) {
+                        float vm[16], vn[16];
+                        if (q4) {
+                            tmem_ld16x2(tb + col, tb + 128 + col, vm, vn);
+#pragma unroll
+                            for (int i = 0; i < 16; ++i)
+                                acc[16 * cc + i] = fmaf(S.dxs[sb][col + i], fmaf(-dmn, vn[i], dw * vm[i]), acc[16 * cc + i]);
+                        } else {
+                            tmem_ld16(tb + col, vm);
+#pragma unroll
+                            for (int i = 0; i < 16; ++i)
+                                acc[16 * cc + i] = fmaf(S.dxs[sb][col + i], dw * vm[i], acc[16 * cc + i]);
+                        }
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&S.accempty[b]);
+                if (et == 0) PTRACE(0, 2, sbc, 2);
+            }
+            if (warp_aborted(abort)) break;
+            // GeGLU and Q8_0 over all epilogue warps: gate (lanes 0-63) and up (lanes 64-127) rows
+            // go to shared memory, then each warp takes (pair, 32-output block) items, lane = output
+            if (r < 64) {
+#pragma unroll
+                for (int i = 0; i < 64; ++i)
+                    if (64 * ch + i < tl.n) S.xg[64 * ch + i][r] = acc[i];
+            } else {
+#pragma unroll
+                for (int i = 0; i < 64; ++i)
+                    if (64 * ch + i < tl.n) S.xu[64 * ch + i][r - 64] = acc[i];
+            }
+            if (!epi_barrier(&S.epibar, eph, abort)) break;
+            const int items = 2 * tl.n;
+            for (int i0 = ew * kGegluBatch; i0 < items; i0 += kPfEpiWarps * kGegluBatch) {
+                float g[kGegluBatch], uu[kGegluBatch];
+                uint16_t tv[kGegluBatch];
+#pragma unroll
+                for (int j = 0; j < kGegluBatch; ++j) {
+                    const int item = i0 + j < items ? i0 + j : items - 1;
+                    g[j] = S.xg[item >> 1][32 * (item & 1) + lane];
+                    uu[j] = S.xu[item >> 1][32 * (item & 1) + lane];
+                }
+#pragma unroll
+                for (int j = 0; j < kGegluBatch; ++j) tv[j] = g_gelu_f16[f2h_rn(g[j])];   // loads in flight together
+#pragma unroll
+                for (int j = 0; j < kGegluBatch; ++j) {
+                    const int item = i0 + j;
+                    if (item >= items) break;        // warp-uniform
+                    const int col = item >> 1, blk = item & 1, slot = tl.slot0 + col;
+                    // geglu1 (ggml-cpu vec.h:1414): 0 below -10, g * u above 10, else table(g) * u
+                    const float a = g[j] <= -10.0f ? 0.0f : (g[j] >= 10.0f ? __fmul_rn(g[j], uu[j]) : __fmul_rn(h2f(tv[j]), uu[j]));
+                    const float amax = warp_max(fabsf(a));
+                    const float dd = h2f(f2h_rn(__fdiv_rn(amax, 127.f)));
+                    const float id = amax != 0.f ? __fdiv_rn(127.f, amax) : 0.f;
+                    p.a8[(size_t)slot * p.nff + 64 * mb + 32 * blk + lane] = (int8_t)__float2int_rn(__fmul_rn(a, id));
+                    if (lane == 0) p.ad[(size_t)slot * nb32 + 2 * mb + blk] = dd;
+                    if (p.h) {
+                        float *hp = p.h + (size_t)p.perm[slot] * 2 * p.nff;
+                        hp[64 * mb + 32 * blk + lane] = g[j];
+                        hp[p.nff + 64 * mb + 32 * blk + lane] = uu[j];
+                    }
+                }
+            }
+            if (!epi_barrier(&S.epibar, eph, abort)) break;
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == kPfMmaWarp) {
+        tc_fence_after();
+        tmem_dealloc_warp(tmem, 512);
+    }
+}
+
+// ---------------------------------------------------------------- down grouped GEMM
+// Work unit (tile, mb): the pairs of one expert tile against down rows [128 mb, 128 mb + 128).
+__global__ void __launch_bounds__(kPfThreads, 1) pf_down_kernel(PfParams p) {
+    extern __shared__ __align__(1024) uint8_t pf_smem[];
+    DnSmem &S = *reinterpret_cast<DnSmem *>(pf_smem);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (tid == 0) {
+        for (int s = 0; s < kDnStages; ++s) { mbar_init(&S.full[s], kPfConvWarps); mbar_init(&S.empty[s], 1); }
+        for (int b = 0; b < kDnAccBufs; ++b) { mbar_init(&S.accfull[b], 1); mbar_init(&S.accempty[b], kPfEpiWarps); }
+        mbar_init(&S.done, 1);
+        mbar_init(&S.epibar, kPfEpiWarps);
+        S.abort = 0;
+        fence_mbar_init();
+    }
+    if (warp == kPfMmaWarp) tmem_alloc_warp(&S.tmem, 512);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = S.tmem;
+    volatile int32_t *abort = &S.abort;
+    pdl_wait();
+    const int n_mb = p.d / kPfM, nblk = p.nff / QK32, nst = nblk / 2;
+    const int units = *p.n_tiles * n_mb;
+
+    if (warp < kPfConvWarps) {
+        uint32_t kv[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            kv[i] = (uint32_t)(uint8_t)g_iq4nl[4 * i] | ((uint32_t)(uint8_t)g_iq4nl[4 * i + 1] << 8) |
+                    ((uint32_t)(uint8_t)g_iq4nl[4 * i + 2] << 16) | ((uint32_t)(uint8_t)g_iq4nl[4 * i + 3] << 24);
+        int it = 0;
+        DnARaw ar;
+        uint4 br[4];
+        for (int u = blockIdx.x; u < units && !warp_aborted(abort); u += gridDim.x) {
+            const int ti = u / n_mb, mb = u - ti * n_mb;
+            const PfTile tl = p.tiles[ti];
+            const PoolView &pv = p.dn[tl.cls];
+            const bool q5 = pv.type == T_Q5_0;
+            const int rb = (int)row_bytes(pv.type, p.nff);
+            const int r = tid, c = tid;
+            const uint8_t *arow = tile_rows(pv, tl.widx, p.d, p.nff) + (size_t)(kPfM * mb + r) * rb;
+            const int8_t *brow = c < tl.n ? p.a8 + (size_t)(tl.slot0 + c) * p.nff : nullptr;
+            const int sbytes = q5 ? 2 * B_Q5_0 : 2 * B_IQ4_NL;
+            dn_a_load(arow, q5, ar);
+            for (int st = 0; st < nst; ++st, ++it) {
+                const int s = it % kDnStages;
+                if (brow) dn_b_load(brow + 64 * st, br);
+                if (it >= kDnStages && !pf_wait_warp(&S.empty[s], ((it / kDnStages) - 1) & 1, abort)) break;
+                if (q5) dn_a_q5_0(ar, S.a[s], r);
+                else dn_a_iq4nl(ar, kv, S.a[s], r);
+                if (st + 1 < nst) dn_a_load(arow + (st + 1) * sbytes, q5, ar);
+                if (brow) dn_b(br, S.b[s], c);
+                fence_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&S.full[s]);
+            }
+        }
+    } else if (warp == kPfMmaWarp) {
+        if (lane == 0) {
+            int it = 0, ac = 0;
+            const uint32_t sbo = kDnKc * 128;
+            for (int u = blockIdx.x; u < units && !*abort; u += gridDim.x) {
+                const PfTile tl = p.tiles[u / n_mb];
+                const int N = (tl.n + 15) & ~15;
+                const uint32_t idesc = umma_idesc_f16(kPfM, N);
+                for (int st = 0; st < nst && !*abort; ++st, ++it) {
+                    const int s = it % kDnStages;
+                    if (!pf_wait(&S.full[s], (it / kDnStages) & 1, abort)) break;
+                    tc_fence_after();
+                    const uint32_t a0 = smem_addr(S.a[s]), b0 = smem_addr(S.b[s]);
+                    for (int bi = 0; bi < 2; ++bi, ++ac) {
+                        const int b = ac % kDnAccBufs;
+                        if (ac >= kDnAccBufs && !pf_wait(&S.accempty[b], ((ac / kDnAccBufs) - 1) & 1, abort)) break;
+                        tc_fence_after();
+                        const uint32_t dt = tmem + (uint32_t)(b * 128);
+#pragma unroll
+                        for (int ks = 0; ks < 2; ++ks) {
+                            const uint32_t off = (uint32_t)((4 * bi + 2 * ks) * 128);
+                            umma_f16(dt, umma_sdesc(a0 + off, 128, sbo), umma_sdesc(b0 + off, 128, sbo), idesc, ks);
+                        }
+                        umma_commit(&S.accfull[b]);
+                    }
+                    umma_commit(&S.empty[s]);
+                }
+            }
+            umma_commit(&S.done);
+            mbar_wait(&S.done, 0);   // issued MMAs always complete; TMEM is freed only after them
+        }
+        __syncwarp();
+    } else {
+        const int ew = warp - kPfEpiWarp0, et = tid - kPfEpiWarp0 * 32;
+        const int q = warp & 3, ch = ew >> 2;
+        const int r = 32 * q + lane;
+        int ac = 0;
+        uint32_t eph = 0;
+        for (int u = blockIdx.x; u < units && !warp_aborted(abort); u += gridDim.x) {
+            const int ti = u / n_mb, mb = u - ti * n_mb;
+            const PfTile tl = p.tiles[ti];
+            const PoolView &pv = p.dn[tl.cls];
+            const int bsz = pv.type == T_Q5_0 ? B_Q5_0 : B_IQ4_NL;
+            const int rb = (int)row_bytes(pv.type, p.nff);
+            const int N = (tl.n + 15) & ~15;
+            const uint8_t *arow = tile_rows(pv, tl.widx, p.d, p.nff) + (size_t)(kPfM * mb + r) * rb;
+            for (int i = et; i < tl.n * nblk; i += kPfEpiWarps * 32) {
+                const int c = i / nblk, bk = i - c * nblk;
+                S.dxs[bk][c] = p.ad[(size_t)(tl.slot0 + c) * nblk + bk];
+            }
+            if (!epi_barrier(&S.epibar, eph, abort)) break;
+            float acc[64];
+#pragma unroll
+            for (int i = 0; i < 64; ++i) acc[i] = 0.f;
+            for (int bk = 0; bk < nblk; ++bk, ++ac) {
+                const float dw = h2f(*reinterpret_cast<const uint16_t *>(arow + bk * bsz));
+                const int b = ac % kDnAccBufs;
+                if (!pf_wait_warp(&S.accfull[b], (ac / kDnAccBufs) & 1, abort)) break;
+                tc_fence_after();
+                const uint32_t tb = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(b * 128);
+#pragma unroll
+                for (int cc = 0; cc < 4; ++cc) {
+                    const int col = 64 * ch + 16 * cc;
+                    if (col < N) {
+                        float v[16];
+                        tmem_ld16(tb + col, v);
+#pragma unroll
+                        for (int i = 0; i < 16; ++i)
+                            acc[16 * cc + i] = fmaf(dw * S.dxs[bk][col + i], v[i], acc[16 * cc + i]);
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&S.accempty[b]);
+            }
+            if (warp_aborted(abort)) break;
+            const float sc = pv.scale ? pv.scale[tl.widx] : 1.f;
+#pragma unroll
+            for (int i = 0; i < 64; ++i) {
+                const int col = 64 * ch + i;
+                if (col < tl.n) {
+                    const float v = pv.scale ? __fmul_rn(acc[i], sc) : acc[i];
+                    p.y[(size_t)(tl.slot0 + col) * p.d + kPfM * mb + r] = v;
+                }
+            }
+            if (!epi_barrier(&S.epibar, eph, abort)) break;
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == kPfMmaWarp) {
+        tc_fence_after();
+        tmem_dealloc_warp(tmem, 512);
+    }
+}
+
+// ---------------------------------------------------------------- router, routing, dispatch, act quant
+constexpr int kRtTok = 16, kRtExp = 128, kRtK = 32;
+
+// logits[t][e] = sum_k W[e][k] x[t][k] (+ b[e]); CTA: 16 tokens x 128 experts, 256 threads of
+// 4 experts x 2 tokens each; one fp32 accumulator per output, k ascending.
+__global__ void __launch_bounds__(256) pf_router_kernel(const float *W, const float *bias, const float *x, float *logits,
+                                                        int T, int E, int d) {
+    __shared__ __align__(16) float ws[kRtK][kRtExp + 4];
+    __shared__ __align__(16) float xs[kRtK][kRtTok + 4];
+    pdl_wait();
+    pdl_launch_dependents();
+    const int t0 = blockIdx.x * kRtTok, e0 = blockIdx.y * kRtExp, tid = threadIdx.x;
+    const int eg = tid & 31, tg = tid >> 5;
+    float acc[4][2];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[i][0] = acc[i][1] = 0.f;
+    for (int k0 = 0; k0 < d; k0 += kRtK) {
+#pragma unroll
+        for (int i = 0; i < (kRtExp * kRtK / 4) / 256; ++i) {
+            const int idx = tid + 256 * i, e = idx >> 3, f = idx & 7;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (e0 + e < E) v = *reinterpret_cast<const float4 *>(W + (size_t)(e0 + e) * d + k0 + 4 * f);
+            ws[4 * f][e] = v.x; ws[4 * f + 1][e] = v.y; ws[4 * f + 2][e] = v.z; ws[4 * f + 3][e] = v.w;
+        }
+        if (tid < kRtTok * kRtK / 4) {
+            const int t = tid >> 3, f = tid & 7;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (t0 + t < T) v = *reinterpret_cast<const float4 *>(x + (size_t)(t0 + t) * d + k0 + 4 * f);
+            xs[4 * f][t] = v.x; xs[4 * f + 1][t] = v.y; xs[4 * f + 2][t] = v.z; xs[4 * f + 3][t] = v.w;
+        }
+        __syncthreads();
+#pragma unroll 8
+        for (int kk = 0; kk < kRtK; ++kk) {
+            const float4 wv = *reinterpret_cast<const float4 *>(&ws[kk][4 * eg]);
+            const float2 xv = *reinterpret_cast<const float2 *>(&xs[kk][2 * tg]);
+            acc[0][0] = fmaf(wv.x, xv.x, acc[0][0]); acc[0][1] = fmaf(wv.x, xv.y, acc[0][1]);
+            acc[1][0] = fmaf(wv.y, xv.x, acc[1][0]); acc[1][1] = fmaf(wv.y, xv.y, acc[1][1]);
+            acc[2][0] = fmaf(wv.z, xv.x, acc[2][0]); acc[2][1] = fmaf(wv.z, xv.y, acc[2][1]);
+            acc[3][0] = fmaf(wv.w, xv.x, acc[3][0]); acc[3][1] = fmaf(wv.w, xv.y, acc[3][1]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int e = e0 + 4 * eg + i;
+        if (e >= E) continue;
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const int t = t0 + 2 * tg + j;
+            if (t < T) logits[(size_t)t * E + e] = bias ? __fadd_rn(acc[i][j], bias[e]) : acc[i][j];
+        }
+    }
+}
+
+// softmax -> top-k -> normalised weights, one warp per token (same arithmetic as route_tokens)
+__global__ void __launch_bounds__(256) pf_topk_kernel(const float *logits, int32_t *ids, float *wts, int T, int E,
+                                                      int k) {
+    pdl_wait();
+    pdl_launch_dependents();
+    const int lane = threadIdx.x & 31;
+    const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (t >= T) return;
+    const int per = E / 32;
+    float v[kMaxE / 32];
+#pragma unroll
+    for (int i = 0; i < kMaxE / 32; ++i) v[i] = i < per ? logits[(size_t)t * E + lane + 32 * i] : -INFINITY;
+    float mx = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < kMaxE / 32; ++i) mx = fmaxf(mx, v[i]);
+    mx = warp_max(mx);
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < kMaxE / 32; ++i) if (i < per) s += expf(v[i] - mx);
+    s = warp_sum(s);
+    const float inv = 1.f / s;
+    uint32_t taken = 0;
+    float psum = 0.f, mine = 0.f;
+    int myid = 0;
+    for (int j = 0; j < k; ++j) {
+        float bv = -INFINITY;
+        int bi = 0x7fffffff;
+#pragma unroll
+        for (int i = 0; i < kMaxE / 32; ++i) {
+            const int e = lane + 32 * i;
+            if (i < per && !((taken >> i) & 1u) && better(v[i], e, bv, bi)) { bv = v[i]; bi = e; }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
+        }
+        if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+        const float pj = __fmul_rn(expf(bv - mx), inv);
+        psum = __fadd_rn(psum, pj);
+        if (lane == j) { myid = bi; mine = pj; }
+    }
+    psum = fmaxf(psum, 6.103515625e-5f);
+    if (lane < k) {
+        ids[(size_t)t * k + lane] = myid;
+        wts[(size_t)t * k + lane] = __fdiv_rn(mine, psum);
+    }
+}
+
+struct PfDispatchParams {
+    const int32_t *ids;
+    int32_t T, E, k;
+    Residency res;
+    int32_t hot_n, cold_n;     // pool sizes (0 = class absent)
+    int32_t *cnt, *off, *perm, *pos;
+    PfTile *tiles;
+    int32_t *n_tiles;
+};
+
+// One CTA of 1024 threads. Warp w owns the contiguous pair range [w*per, (w+1)*per); counting
+// and placement walk it 32 pairs at a time in pair order, so the permutation is stable.
+__global__ void __launch_bounds__(1024, 1) pf_dispatch_kernel(PfDispatchParams p) {
+    __shared__ int32_t wcnt[32][kMaxE];
+    __shared__ int32_t cnt[kMaxE], off[kMaxE + 1], tpre[kMaxE + 1], cls[kMaxE], widx[kMaxE];
+    pdl_wait();
+    pdl_launch_dependents();
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int P = p.T * p.k, E = p.E;
+    for (int i = tid; i < 32 * kMaxE; i += 1024) (&wcnt[0][0])[i] = 0;
+    __syncthreads();
+    const int per = (P + 31) / 32;
+    const int lo = min(P, warp * per), hi = min(P, lo + per);
+    const unsigned lt = (1u << lane) - 1u;
+    for (int base = lo; base < hi; base += 32) {
+        const int pi = base + lane;
+        const bool v = pi < hi;
+        int e = v ? p.ids[pi] : -1;
+        if (v && (e < 0 || e >= E)) { atomicOr(&g_error, ERR_BAD_EXPERT); e = 0; }
+        const unsigned act = __ballot_sync(0xffffffffu, v);
+        const unsigned peers = __match_any_sync(0xffffffffu, e) & act;
+        if (v && (peers & lt) == 0) wcnt[warp][e] += __popc(peers);
+        __syncwarp();
+    }
+    __syncthreads();
+    if (tid < E) {
+        int c = 0;
+        for (int w = 0; w < 32; ++w) c += wcnt[w][tid];
+        cnt[tid] = c;
+        int cl = -1, wi = tid;
+        if (c > 0) {
+            if (p.res.n_slots > 0 && p.res.exp_slot) {
+                const int s = p.res.exp_slot[tid];
+                if (s >= 0 && s < p.res.n_slots && p.res.slot_state[s] == 2 && p.res.slot_exp[s] == tid) { cl = 0; wi = s; }
+            }
+            if (cl < 0 && tid < p.cold_n) cl = 1;
+            if (cl == 0 && wi >= p.hot_n) cl = -1;
+            if (cl < 0) atomicOr(&g_error, ERR_BAD_EXPERT);
+        }
+        cls[tid] = cl;
+        widx[tid] = wi;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        int base = 0, tb = 0;
+        for (int e0 = 0; e0 < E; e0 += 32) {
+            const int e = e0 + lane;
+            const int c = e < E ? cnt[e] : 0;
+            const int nt = (e < E && cls[e] >= 0) ? (c + kPfN - 1) / kPfN : 0;
+            int ic = c, it = nt;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int a = __shfl_up_sync(0xffffffffu, ic, o), b = __shfl_up_sync(0xffffffffu, it, o);
+                if (lane >= o) { ic += a; it += b; }
+            }
+            if (e < E) { off[e] = base + ic - c; tpre[e] = tb + it - nt; }
+            base += __shfl_sync(0xffffffffu, ic, 31);
+            tb += __shfl_sync(0xffffffffu, it, 31);
+        }
+        if (lane == 0) { off[E] = base; tpre[E] = tb; }
+    }
+    __syncthreads();
+    if (tid < E) {
+        int run = off[tid];
+        for (int w = 0; w < 32; ++w) { const int c = wcnt[w][tid]; wcnt[w][tid] = run; run += c; }
+        const int c = cnt[tid], nt = tpre[tid + 1] - tpre[tid];
+        if (nt > 0) {
+            const int bsz = c / nt, rem = c - bsz * nt;
+            int s0 = off[tid];
+            for (int i = 0; i < nt; ++i) {
+                const int n = bsz + (i < rem ? 1 : 0);
+                PfTile tl;
+                tl.cls = cls[tid]; tl.widx = widx[tid]; tl.slot0 = s0; tl.n = n;
+                p.tiles[tpre[tid] + i] = tl;
+                s0 += n;
+            }
+        }
+        if (p.cnt) p.cnt[tid] = c;
+        if (p.off) p.off[tid] = off[tid];
+    }
+    if (tid == 0) {
+        *p.n_tiles = tpre[E];
+        if (p.off) p.off[E] = off[E];
+    }
+    __syncthreads();
+    for (int base = lo; base < hi; base += 32) {
+        const int pi = base + lane;
+        const bool v = pi < hi;
+        int e = v ? p.ids[pi] : -1;
+        if (v && (e < 0 || e >= E)) e = 0;
+        const unsigned act = __ballot_sync(0xffffffffu, v);
+        const unsigned peers = __match_any_sync(0xffffffffu, e) & act;
+        const int b0 = v ? wcnt[warp][e] : 0;
+        __syncwarp();
+        if (v) {
+            const int at = b0 + __popc(peers & lt);
+            p.perm[at] = pi;
+            p.pos[pi] = cls[e] >= 0 ? at : -1;
+            if ((peers & lt) == 0) wcnt[warp][e] = b0 + __popc(peers);
+        }
+        __syncwarp();
+    }
+}
+
+// Q8_K quantisation of every token: one warp per (token, super-block)
+__global__ void __launch_bounds__(256) pf_actq_kernel(const float *x, int8_t *xq8, float *xd, int16_t *xbs, int T,
+                                                      int d) {
+    pdl_wait();
+    pdl_launch_dependents();
+    const int nsb = d / QK_K;
+    const int item = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (item >= T * nsb) return;
+    const int t = item / nsb, sb = item - t * nsb;
+    q8k_superblock_warp(x + (size_t)t * d + sb * QK_K, xq8 + (size_t)t * d + sb * QK_K, xd + item, xbs + (size_t)item * 16,
+                        lane);
+}
+
+// out[t] = ((w0 y0 + w1 y1) + w2 y2) + ...: products rounded, then added in slot order, as the
+// reference's mul + add chain does; optionally copies y to pair order.
+__global__ void __launch_bounds__(256) pf_combine_kernel(const float *y, const int32_t *pos, const float *w, float *out,
+                                                         float *y_pairs, int T, int k, int d) {
+    pdl_wait();
+    pdl_launch_dependents();
+    const int t = blockIdx.x;
+    for (int c = 4 * threadIdx.x; c < d; c += 4 * blockDim.x) {
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int j = 0; j < k; ++j) {
+            const int sl = pos[(size_t)t * k + j];
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (sl >= 0) v = *reinterpret_cast<const float4 *>(y + (size_t)sl * d + c);
+            const float wj = w[(size_t)t * k + j];
+            const float4 pr = make_float4(__fmul_rn(wj, v.x), __fmul_rn(wj, v.y), __fmul_rn(wj, v.z), __fmul_rn(wj, v.w));
+            if (j == 0) acc = pr;
+            else acc = make_float4(__fadd_rn(acc.x, pr.x), __fadd_rn(acc.y, pr.y), __fadd_rn(acc.z, pr.z), __fadd_rn(acc.w, pr.w));
+            if (y_pairs) *reinterpret_cast<float4 *>(y_pairs + ((size_t)t * k + j) * d + c) = v;
+        }
+        *reinterpret_cast<float4 *>(out + (size_t)t * d + c) = acc;
+    }
+}
+
+}  // namespace moeb

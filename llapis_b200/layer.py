@@ -106,6 +106,19 @@ class MoELayer:
         self.c = L
         self._ws = None
 
+    def prefill_path(self, n_tokens: int) -> bool:
+        """Whether moeb_layer_forward runs n_tokens on the prefill (tensor-core GEMM) path."""
+        h = self.host
+        shape_ok = h.n_ff % 64 == 0 and h.d_model % 128 == 0 and h.d_model // 256 <= 16 and h.n_ff // 32 <= 32
+        return shape_ok and n_tokens >= int(capi.lib().moeb_set_prefill_min_tokens(0))
+
+    def launches(self, n_tokens: int) -> int:
+        """Kernels one forward of n_tokens launches: seven on the prefill path, else one cooperative
+        fused kernel per 8-token chunk."""
+        if n_tokens <= 0:
+            return 0
+        return 7 if self.prefill_path(n_tokens) else (n_tokens + 7) // 8
+
     def workspace_bytes(self, n_tokens: int) -> int:
         return int(capi.lib().moeb_layer_workspace_size(C.byref(self.c), n_tokens))
 

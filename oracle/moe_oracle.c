@@ -431,7 +431,8 @@ int oracle_moe_layer(const oracle_layer *L, oracle_layer_out *o) {
         for (int e = 0; e < E; ++e) { prob[e] = expf(logit[e] - mx); sum += prob[e]; }
         const float inv = (float)(1.0 / sum);
         for (int e = 0; e < E; ++e) prob[e] *= inv;
-        oracle_topk(prob, E, k, ids);
+        if (L->ids_in) memcpy(ids, L->ids_in + (size_t)t * k, sizeof(int32_t) * k);
+        else oracle_topk(prob, E, k, ids);
         /* weights: get_rows, sum_rows (double), clamp, div (llama-graph.cpp:1626-1648) */
         double ws = 0.0;
         for (int j = 0; j < k; ++j) { w[j] = prob[ids[j]]; ws += w[j]; }
@@ -457,8 +458,12 @@ int oracle_moe_layer(const oracle_layer *L, oracle_layer_out *o) {
             wgu += (size_t)widx * 2 * nff * rgu;
             wdn += (size_t)widx * d * rdn;
             /* gate_up: x quantised to the weight type's vec_dot_type (ggml-cpu.c:1581-1610) */
-            oracle_quantize_act(oracle_vec_dot_type(tgu), xt, xq, d);
-            for (int r = 0; r < 2 * nff; ++r) h[r] = oracle_vec_dot(tgu, d, wgu + (size_t)r * rgu, xq);
+            if (L->gate_up_in) {
+                memcpy(h, L->gate_up_in + (size_t)p * 2 * nff, sizeof(float) * 2 * nff);
+            } else {
+                oracle_quantize_act(oracle_vec_dot_type(tgu), xt, xq, d);
+                for (int r = 0; r < 2 * nff; ++r) h[r] = oracle_vec_dot(tgu, d, wgu + (size_t)r * rgu, xq);
+            }
             oracle_geglu(nff, a, h, h + nff);
             oracle_quantize_act(oracle_vec_dot_type(tdn), a, aq, nff);
             const float sc = hot ? (L->s_hot ? L->s_hot[slot] : 1.f) : (L->s_cold ? L->s_cold[e] : 1.f);

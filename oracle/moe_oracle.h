@@ -50,6 +50,13 @@ typedef struct oracle_layer {
     const void    *cold_down;  /* [n_expert][d_model rows][row bytes]                   */
     const float   *s_cold;     /* [n_expert] down scale or NULL                         */
     int32_t        n_threads;
+    /* Conditional-parity inputs (port oracle only; the reference runner ignores them): when set,
+     * the routed experts (ids_in, [n_tokens][top_k]) and/or the raw gate_up outputs of every
+     * routed pair (gate_up_in, [n_tokens*top_k][2*n_ff], pair order) are taken as given instead
+     * of being computed, so the later stages can be checked on exactly the inputs a tested
+     * implementation fed them. */
+    const int32_t *ids_in;
+    const float   *gate_up_in;
 } oracle_layer;
 
 typedef struct oracle_layer_out {

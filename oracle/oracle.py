@@ -27,6 +27,7 @@ class _Layer(C.Structure):
         ("cold_type_gu", C.c_int32), ("cold_type_down", C.c_int32),
         ("cold_gu", C.c_void_p), ("cold_down", C.c_void_p), ("s_cold", C.c_void_p),
         ("n_threads", C.c_int32),
+        ("ids_in", C.c_void_p), ("gate_up_in", C.c_void_p),
     ]
 
 
@@ -62,6 +63,8 @@ class LayerSpec:
     cold_gu: np.ndarray | None = None   # u8 [E, 2*n_ff, row]
     cold_down: np.ndarray | None = None
     s_cold: np.ndarray | None = None
+    ids_in: np.ndarray | None = None      # i32 [T, k]: routing taken as given (port oracle only)
+    gate_up_in: np.ndarray | None = None  # f32 [T*k, 2*n_ff]: gate_up taken as given (port oracle only)
     keep: list = field(default_factory=list)
 
     @property
@@ -85,6 +88,8 @@ class LayerSpec:
             cold_gu=None if self.cold_gu is None else np.ascontiguousarray(self.cold_gu),
             cold_down=None if self.cold_down is None else np.ascontiguousarray(self.cold_down),
             s_cold=None if self.s_cold is None else np.ascontiguousarray(self.s_cold, np.float32),
+            ids_in=None if self.ids_in is None else np.ascontiguousarray(self.ids_in, np.int32),
+            gate_up_in=None if self.gate_up_in is None else np.ascontiguousarray(self.gate_up_in, np.float32),
         )
         self.keep = list(arrs.values())
         for k, v in arrs.items():
