@@ -1,0 +1,116 @@
+"""The C-ABI library without a GPU: it loads, exports every symbol the public headers declare (and
+capi.py binds exactly those), its moert structs have the reference's layout, and argument
+validation and the host-side helpers work on a CPU-only machine."""
+import ctypes as C
+import json
+import os
+import re
+import sys
+
+import numpy as np
+import pytest
+
+from conftest import ROOT
+
+sys.path.insert(0, os.path.join(ROOT, "tests", "golden"))
+import abi_layout  # noqa: E402
+
+HEADERS = [os.path.join(ROOT, "include", h) for h in ("moeb200.h", "moert_cuda.h")]
+
+
+def declared_functions():
+    names = set()
+    for h in HEADERS:
+        src = re.sub(r"/\*.*?\*/", "", open(h).read(), flags=re.S)
+        src = re.sub(r"#define[^\n]*", "", src)
+        for m in re.finditer(r"\b((?:moeb|moert)_\w+)\s*\(", src):
+            # declarations only: skip the names of function-pointer typedefs, `(*name)(`
+            if re.search(r"\(\s*\*\s*$", src[max(0, m.start() - 8):m.start()]):
+                continue
+            names.add(m.group(1))
+    # inline helpers defined in the header, not exported
+    return {n for n in names if n != "moert_cuda_config_defaults"}
+
+
+def test_library_exports_every_declared_symbol(lib):
+    names = declared_functions()
+    assert len(names) >= 30
+    missing = [n for n in sorted(names) if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_capi_binds_exactly_the_declared_symbols():
+    from llapis_b200 import capi
+    assert set(capi.SIGNATURES) == declared_functions()
+
+
+def test_moert_struct_layouts_match_reference():
+    want = json.load(open(os.path.join(ROOT, "tests", "golden", "moert_abi_layout.json")))
+    assert abi_layout.ours() == want
+
+
+def test_python_struct_mirrors_match_c(lib):
+    from llapis_b200 import capi
+    # moeb_pool: 4 x i32 + 3 pointers; moeb_layer: 4 x i32, 2 pointers, 2 pools, 3 pointers
+    assert C.sizeof(capi.Pool) == 16 + 3 * 8
+    assert C.sizeof(capi.Layer) == 16 + 2 * 8 + 2 * C.sizeof(capi.Pool) + 3 * 8
+    assert C.sizeof(capi.LayerAux) == 8 * 8
+
+
+def test_row_sizes(lib):
+    from llapis_b200 import capi
+    assert capi.row_size(capi.Q4_K, 2816) == 11 * 144
+    assert capi.row_size(capi.IQ2_S, 2816) == 11 * 82
+    assert capi.row_size(capi.Q5_0, 704) == 22 * 22
+    assert capi.row_size(capi.IQ4_NL, 704) == 22 * 18
+
+
+def test_argument_validation_without_device(lib):
+    from llapis_b200 import capi
+    assert lib.moeb_layer_forward(None, None, 1, None, None, None, 0, None) == -1      # null layer
+    L = capi.Layer()
+    L.d_model, L.n_ff, L.n_expert, L.top_k = 100, 64, 32, 4                              # d % 256 != 0
+    assert lib.moeb_layer_forward(C.byref(L), None, 1, None, None, None, 0, None) == -1
+    assert "d_model" in lib.moeb_last_error().decode()
+    assert lib.moeb_router_topk(None, 1, 32, 4, None, None, None) == -1
+    assert lib.moeb_layer_workspace_size(None, 8) == 0
+    prev = lib.moeb_set_prefill_min_tokens(0)
+    assert prev > 0 and lib.moeb_set_prefill_min_tokens(0) == prev
+
+
+def test_no_device_means_enodev(lib):
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    assert lib.moeb_init() == -2
+
+
+def test_workspace_sizes_by_path(lib):
+    """Decode workspace is one 8-token chunk for any T; the prefill workspace grows with T."""
+    from llapis_b200 import capi
+    L = capi.Layer()
+    L.d_model, L.n_ff, L.n_expert, L.top_k = 2816, 704, 128, 8
+    prev = lib.moeb_set_prefill_min_tokens(1 << 30)
+    try:
+        a, b = lib.moeb_layer_workspace_size(C.byref(L), 8), lib.moeb_layer_workspace_size(C.byref(L), 4096)
+        assert a == b and 1_000_000 < a < 1_200_000
+        lib.moeb_set_prefill_min_tokens(64)
+        p = lib.moeb_layer_workspace_size(C.byref(L), 2048)
+        assert p > 2048 * 8 * 2816 * 4          # the f32 down outputs of every pair
+        assert lib.moeb_layer_workspace_size(C.byref(L), 32) == a   # below the threshold: decode
+    finally:
+        lib.moeb_set_prefill_min_tokens(prev)
+
+
+def test_host_quantiser_matches_reference_quantiser(ref):
+    """The library's weight quantiser (moeb_quantize_weights) is byte-identical to
+    ggml_quantize_chunk of the reference build, for every type the pools use."""
+    from llapis_b200 import capi
+    rng = np.random.default_rng(3)
+    for t, n in ((capi.Q4_K, 512), (capi.IQ2_S, 512), (capi.Q5_0, 128), (capi.IQ4_NL, 128)):
+        w = (rng.standard_normal((4, n)) * 0.02).astype(np.float32)
+        rs = capi.row_size(t, n)
+        ours = np.zeros(4 * rs, np.uint8)
+        got = capi.lib().moeb_quantize_weights(t, w.ctypes.data, ours.ctypes.data, 4, n, 1)
+        assert got == 4 * rs
+        assert np.array_equal(ours, ref.quantize(t, w).reshape(-1)), t
