@@ -289,7 +289,7 @@ def main():
     kernels_ms = None
     if prefill:
         lib = capi.lib()
-        names = ("router", "topk", "dispatch", "actq", "gate_up", "down", "combine")
+        names = ("router", "topk", "dispatch", "actq", "gather", "gate_up", "geglu", "down", "combine")
         acc = np.zeros(len(names))
         buf = (C.c_float * len(names))()
         lib.moeb_prefill_profile(1)

@@ -84,7 +84,8 @@ int         moeb_init(void);
 const char *moeb_last_error(void);
 const char *moeb_version(void);
 /* Reads and clears the device error word (bit 1: a bounded wait gave up; 2: expert id out of
- * range; 4: a capacity limit was exceeded). */
+ * range; 4: a capacity limit was exceeded; 16: a GeGLU output beyond the fp16 operand range of
+ * the prefill down GEMM, |value| > 65504). */
 int32_t     moeb_device_error(void *stream);
 
 /* Workspace bytes moeb_layer_forward needs for n_tokens tokens (the decode path needs one 8-token
@@ -110,8 +111,9 @@ int moeb_layer_forward(const moeb_layer *L, const float *x, int32_t n_tokens, fl
 int32_t moeb_set_prefill_min_tokens(int32_t n_tokens);
 
 /* Profiling of the prefill path (no counterpart in the reference): while enabled, every prefill
- * forward on the current device records CUDA events around its seven kernels (router, top-k,
- * dispatch, activation quantisation, gate_up, down, combine) on the caller's stream. Events
+ * forward on the current device records CUDA events around its nine kernels (router, top-k,
+ * dispatch, activation quantisation, operand gather, gate_up, GeGLU, down, combine) on the
+ * caller's stream. Events
  * between kernels keep them from overlapping, so use it on a separate measurement pass.
  * moeb_prefill_profile_read waits for the last profiled call and writes up to n durations (ms). */
 int moeb_prefill_profile(int32_t enable);

@@ -165,8 +165,11 @@ struct PrefillWs {
     float *logits, *w, *xd, *ad, *y;
     int32_t *ids, *cnt, *off, *perm, *pos, *n_tiles;
     PfTile *tiles;
-    int8_t *xq8, *a8;
+    int8_t *xq8;
     int16_t *xbs;
+    uint8_t *bimg, *dimg;
+    float *dxt, *hbuf;
+    int max_tiles;
     size_t bytes;
 };
 
@@ -183,12 +186,16 @@ PrefillWs carve_prefill(const moeb_layer *L, int T, uint8_t *base) {
     w.perm = (int32_t *)take(sizeof(int32_t) * P);
     w.pos = (int32_t *)take(sizeof(int32_t) * P);
     w.n_tiles = (int32_t *)take(16);
-    w.tiles = (PfTile *)take(sizeof(PfTile) * prefill_max_tiles((int)P, (int)E));
+    w.max_tiles = prefill_max_tiles((int)P, (int)E);
+    w.tiles = (PfTile *)take(sizeof(PfTile) * w.max_tiles);
     w.xq8 = (int8_t *)take((size_t)T * d);
     w.xd = (float *)take(sizeof(float) * T * nsb);
     w.xbs = (int16_t *)take(sizeof(int16_t) * T * nsb * 16);
-    w.a8 = (int8_t *)take(P * nff);
-    w.ad = (float *)take(sizeof(float) * P * (nff / 32));
+    const size_t mt = (size_t)w.max_tiles;
+    w.bimg = (uint8_t *)take(mt * nsb * 2 * kPfGuImageBytes);
+    w.dxt = (float *)take(sizeof(float) * mt * nsb * kPrefillTile);
+    w.hbuf = (float *)take(sizeof(float) * P * 2 * nff);
+    w.dimg = (uint8_t *)take(mt * (nff / 64) * 2 * kPfDnImageBytes);
     w.y = (float *)take(sizeof(float) * P * d);
     w.bytes = o;
     return w;
@@ -294,7 +301,7 @@ static int check_forward(const moeb_layer *L, const float *x, int32_t n_tokens, 
     return MOEB_OK;
 }
 
-// The prefill path: seven PDL-chained kernels, the expert matmuls on tcgen05 tensor cores.
+// The prefill path: nine PDL-chained kernels, the expert matmuls on tcgen05 tensor cores.
 static int forward_prefill(const moeb_layer *L, const float *x, int32_t T, float *out, const moeb_layer_aux *aux,
                            void *workspace, cudaStream_t s, int n_sms) {
     const int d = L->d_model, k = L->top_k, E = L->n_expert, P = T * k;
@@ -313,7 +320,7 @@ static int forward_prefill(const moeb_layer *L, const float *x, int32_t T, float
     a.cnt = w.cnt; a.off = w.off; a.perm = w.perm; a.pos = w.pos;
     a.tiles = w.tiles; a.n_tiles = w.n_tiles;
     a.xq8 = w.xq8; a.xd = w.xd; a.xbs = w.xbs;
-    a.a8 = w.a8; a.ad = w.ad;
+    a.bimg = w.bimg; a.dxt = w.dxt; a.hbuf = w.hbuf; a.dimg = w.dimg; a.max_tiles = w.max_tiles;
     a.h = aux ? aux->gate_up : nullptr;
     a.y = w.y;
     a.out = out;

@@ -24,7 +24,8 @@ __device__ uint16_t g_gelu_f16[1 << 16];
 // Error word: bounded waits that give up OR their code in here and return.
 __device__ int32_t g_error;
 
-enum : int32_t { ERR_MBAR_TIMEOUT = 1, ERR_BAD_EXPERT = 2, ERR_CAPACITY = 4 };
+// ERR_RANGE: a value outside the fp16 range of a tensor-core operand (prefill down input > 65504)
+enum : int32_t { ERR_MBAR_TIMEOUT = 1, ERR_BAD_EXPERT = 2, ERR_CAPACITY = 4, ERR_RANGE = 16 };
 
 // ---------------------------------------------------------------- small device helpers
 __device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }

@@ -1655,7 +1655,7 @@ static cudaError_t smem_optin(const void *fn, size_t bytes, unsigned *done_mask,
     return e;
 }
 
-// Optional per-kernel CUDA events around the seven prefill launches (moeb_prefill_profile).
+// Optional per-kernel CUDA events around the nine prefill launches (moeb_prefill_profile).
 namespace {
 struct PfProfile {
     cudaEvent_t ev[kPrefillKernels + 1] = {};
@@ -1767,13 +1767,24 @@ cudaError_t launch_prefill(const PrefillArgs &a, cudaStream_t s, int n_sms) {
     p.gu[0] = a.hot_gu; p.gu[1] = a.cold_gu; p.dn[0] = a.hot_dn; p.dn[1] = a.cold_dn;
     p.perm = a.perm; p.tiles = a.tiles; p.n_tiles = a.n_tiles;
     p.xq8 = a.xq8; p.xd = a.xd; p.xbs = a.xbs;
-    p.a8 = a.a8; p.ad = a.ad; p.h = a.h; p.y = a.y;
+    p.bimg = a.bimg; p.dxt = a.dxt; p.hbuf = a.hbuf; p.dimg = a.dimg; p.h = a.h; p.y = a.y;
+    {
+        void *args[] = {&p};
+        e = pf_launch("pf_gather_kernel", (const void *)pf_gather_kernel, dim3(a.max_tiles, d / QK_K), dim3(256), 0, s,
+                      true, args);
+        if (e != cudaSuccess) return e;
+        if ((e = prof_mark(s, mark++)) != cudaSuccess) return e;
+    }
     {
         void *args[] = {&p};
         e = pf_launch("pf_gate_up_kernel", (const void *)pf_gate_up_kernel, dim3(n_sms), dim3(kPfThreads), sizeof(GuSmem), s, true, args);
         if (e != cudaSuccess) return e;
         if ((e = prof_mark(s, mark++)) != cudaSuccess) return e;
-        e = pf_launch("pf_down_kernel", (const void *)pf_down_kernel, dim3(n_sms), dim3(kPfThreads), sizeof(DnSmem), s, true, args);
+        e = pf_launch("pf_geglu_kernel", (const void *)pf_geglu_kernel, dim3(a.max_tiles, a.nff / 32), dim3(256), 0, s,
+                      true, args);
+        if (e != cudaSuccess) return e;
+        if ((e = prof_mark(s, mark++)) != cudaSuccess) return e;
+        e = pf_launch("pf_down_kernel", (const void *)pf_down_kernel, dim3(n_sms), dim3(kDnThreads), sizeof(DnSmem), s, true, args);
         if (e != cudaSuccess) return e;
         if ((e = prof_mark(s, mark++)) != cudaSuccess) return e;
     }
@@ -1849,6 +1860,9 @@ extern "C" int moeb_strace_read(void *host, size_t bytes) {
 }
 extern "C" int moeb_ptrace_read(void *host, size_t bytes) {
     return cudaMemcpyFromSymbol(host, moeb::g_ptrace, bytes) == cudaSuccess ? 0 : -3;
+}
+extern "C" int moeb_utrace_read(void *host, size_t bytes) {
+    return cudaMemcpyFromSymbol(host, moeb::g_utrace, bytes) == cudaSuccess ? 0 : -3;
 }
 #endif
 

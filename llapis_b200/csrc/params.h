@@ -127,6 +127,11 @@ struct PfTile {
     int32_t n;       // pairs
 };
 MOEB_HD inline int prefill_max_tiles(int P, int E) { return P / kPrefillTile + E + 1; }
+// fp16 operand images of one tile in the tensor cores' canonical layout: 128 rows x 18 core
+// columns (128 values + 16 min-term columns) per half super-block for gate_up, 128 rows x 8 core
+// columns (two 32-blocks) per down stage; 16 bytes per core row
+constexpr int kPfGuImageBytes = kPrefillTile * 18 * 16;
+constexpr int kPfDnImageBytes = kPrefillTile * 8 * 16;
 struct PrefillArgs {
     const float *w_router, *b_router, *x;
     int32_t T, E, d, k, nff;
@@ -142,16 +147,19 @@ struct PrefillArgs {
     int8_t *xq8;                // [T][d]
     float *xd;                  // [T][d / 256]
     int16_t *xbs;               // [T][d / 256][16]
-    int8_t *a8;                 // [P][nff]
-    float *ad;                  // [P][nff / 32]
+    uint8_t *bimg;              // [max_tiles][d / 256][2][kPfGuImageBytes] gate_up B operand images
+    float *dxt;                 // [max_tiles][d / 256][kPrefillTile] Q8_K scales per tile row
+    float *hbuf;                // [P][2 nff] gate_up outputs, slot order
+    uint8_t *dimg;              // [max_tiles][nff / 64][2][kPfDnImageBytes] down B operand images (hi, lo)
+    int32_t max_tiles;
     float *h;                   // optional [P][2 nff] gate_up outputs, pair order
     float *y;                   // [P][d] down outputs, slot order
     float *out;                 // [T][d]
     float *y_pairs;             // optional [P][d] down outputs, pair order
 };
 cudaError_t launch_prefill(const PrefillArgs &a, cudaStream_t s, int n_sms);
-// router, top-k, dispatch, activation quantisation, gate_up, down, combine
-constexpr int kPrefillKernels = 7;
+// router, top-k, dispatch, activation quantisation, gather, gate_up, GeGLU, down, combine
+constexpr int kPrefillKernels = 9;
 void prefill_profile_enable(bool on);
 int prefill_profile_read(float *ms, int n);
 

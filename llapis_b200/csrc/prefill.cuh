@@ -9,8 +9,10 @@
 //                        (ggml-cpu.c:1613-1626 grouping; mmid.cu:28 on the GPU) plus the per-expert
 //                        tile list the grouped GEMMs walk
 //   pf_actq_kernel     : Q8_K quantisation of every token (quantize_row_q8_K, x86/quants.c:505)
-//   pf_gate_up_kernel  : tcgen05 grouped GEMM, gate_up of every tile, fused GeGLU (fp16-table GELU,
-//                        vec.h:1414) and Q8_0 quantisation of its output (x86/quants.c:302)
+//   pf_gather_kernel   : per expert tile, the tokens' Q8_K values as fp16 operand images
+//   pf_gate_up_kernel  : tcgen05 grouped GEMM, gate_up of every tile (f32 rows, slot order)
+//   pf_geglu_kernel    : GeGLU (fp16-table GELU, vec.h:1414) and Q8_0 quantisation of its output
+//                        (x86/quants.c:302) into the down kernel's fp16 operand images
 //   pf_down_kernel     : tcgen05 grouped GEMM, down projection, per-expert down scale
 //   pf_combine_kernel  : out[t] = sum_j w[t,j] * y[t,j] in j order (llama-graph.cpp:1814-1848)
 //
@@ -24,9 +26,12 @@
 //                  K=16 MMA into a second accumulator: A = [64 m_j | m_j], B = [bsum_j >> 6 |
 //                  bsum_j & 63], promoted with dmin_w * d_x.
 //   gate_up IQ2_S: A = ls * (+-grid) (<= 1333), B = q8, promoted with d_w * d_x / 8.
-//   down Q5_0    : A = q - 16, B = q8 (Q8_0 of the GeGLU output); promoted per 32-block.
-//   down IQ4_NL  : A = kvalues_iq4nl[q], B = q8; promoted per 32-block.
-// Converter warps build the fp16 operand tiles in shared memory (canonical no-swizzle K-major
+//   down Q5_0    : A = q - 16; B = d_x * q8 (the Q8_0 GeGLU output, dequantised) split exactly
+//                  into fp16 hi + lo, two MMAs per K step; promoted per 32-block with d_w.
+//   down IQ4_NL  : A = kvalues_iq4nl[q], B as for Q5_0.
+// Converter warps build the fp16 weight (A) tiles in shared memory; the activation (B) tiles are
+// fp16 images in HBM (written by pf_gather_kernel for gate_up, by the gate_up epilogue for down)
+// fetched with one bulk copy per stage. Converter warps build the A tiles (canonical no-swizzle K-major
 // layout: 8-row x 16-byte core matrices), one thread issues the MMAs, accumulators live in TMEM
 // (double- or quadruple-buffered so the MMAs of the next block overlap the promotion of the last),
 // and epilogue warps read them back with tcgen05.ld.
@@ -99,10 +104,14 @@ __device__ __forceinline__ void tmem_ld16x2(uint32_t ta, uint32_t tb, float (&va
 // and first epilogue warp, per pipeline step.
 #ifdef MOEB_TRACE
 __device__ unsigned long long g_ptrace[2][3][96][3];
+__device__ unsigned long long g_utrace[32][16];
 #define PTRACE(k, role, idx, f) \
     if (blockIdx.x == 0 && (idx) < 96) g_ptrace[k][role][idx][f] = clock64();
+#define UTRACE(u, f) \
+    if (blockIdx.x == 0 && (u) < 32) g_utrace[u][f] = clock64();
 #else
 #define PTRACE(k, role, idx, f)
+#define UTRACE(u, f)
 #endif
 
 // ---------------------------------------------------------------- shapes of the tensor-core kernels
@@ -118,12 +127,17 @@ constexpr int kPfThreads = (kPfConvWarps + 1 + kPfEpiWarps) * 32;
 // a Q4_K super-block): 18 core columns of 8 values
 constexpr int kGuKc = 18;
 constexpr int kGuTileBytes = kPfM * kGuKc * 16;
-constexpr int kGuStages = 2;
-constexpr int kGegluBatch = 8;        // GELU-table lookups a warp keeps in flight
+constexpr int kGuStages = 3;
+constexpr int kGegluBatch = 8;        // GeGLU items a warp reduces together
+constexpr int kGegluItems = 2 * kPrefillTile / 8;   // items per epilogue warp: 2 blocks x 128 pairs / 8 warps
 // down: a stage is two 32-blocks (8 core columns); four accumulator buffers of 128 columns
 constexpr int kDnKc = 8;
 constexpr int kDnTileBytes = kPfM * kDnKc * 16;
-constexpr int kDnStages = 6;
+constexpr int kDnStages = 4;
+// down: 16 epilogue warps, four per TMEM lane quadrant, 32 columns each (one TMEM round trip per
+// 32-block); 21 warps leave 80 registers a thread
+constexpr int kDnEpiWarps = 16;
+constexpr int kDnThreads = (kPfConvWarps + 1 + kDnEpiWarps) * 32;
 constexpr int kDnAccBufs = 4;
 static_assert(kPfN == 128 && kPfM == 128, "TMEM budget below assumes 128 x 128 tiles");
 
@@ -135,8 +149,6 @@ __device__ __forceinline__ uint32_t canon_off(int r, int c, int kc) {
 struct GuSmem {
     uint8_t a[kGuStages][kGuTileBytes];
     uint8_t b[kGuStages][kGuTileBytes];
-    float xg[kPfN][64];                 // gate and up results of a unit, for the GeGLU step
-    float xu[kPfN][64];
     float dxs[kPrefillMaxSb][kPfN];     // Q8_K scale of each tile column, per super-block
     uint64_t full[kGuStages], empty[kGuStages], accfull[2], accempty[2], done, epibar;
     uint32_t tmem;
@@ -144,8 +156,7 @@ struct GuSmem {
 };
 struct DnSmem {
     uint8_t a[kDnStages][kDnTileBytes];
-    uint8_t b[kDnStages][kDnTileBytes];
-    float dxs[kPrefillMaxBlk][kPfN];    // Q8_0 scale of each tile column, per 32-block
+    uint8_t b[kDnStages][2 * kDnTileBytes];   // hi and lo halves of dx * q8
     uint64_t full[kDnStages], empty[kDnStages], accfull[kDnAccBufs], accempty[kDnAccBufs], done, epibar;
     uint32_t tmem;
     int32_t abort;
@@ -224,10 +235,6 @@ __device__ __forceinline__ void q4k_scale_min(int j, const uint8_t *q, int &sc, 
 struct GuARaw {
     uint4 v[5];   // Q4_K: header (d, dmin, scales) + the 64 qs bytes of this half;
                   // IQ2_S: grid bytes, sign bytes, qh and scale words of this half (11 words)
-};
-struct GuBRaw {
-    uint4 v[8];   // 128 q8 values
-    uint4 bs[2];  // the 16 bsums of the super-block (first half of a Q4_K super-block only)
 };
 
 __device__ __forceinline__ void gu_a_load(const uint8_t *blk, int h, bool q4, GuARaw &a) {
@@ -323,43 +330,6 @@ __device__ __forceinline__ void gu_a_iq2s(const GuARaw &a, uint8_t *tile, int r)
     }
 }
 
-__device__ __forceinline__ void gu_b_load(const int8_t *q8, const int16_t *bs16, bool ext, GuBRaw &b) {
-#pragma unroll
-    for (int i = 0; i < 8; ++i) b.v[i] = __ldg(reinterpret_cast<const uint4 *>(q8 + 16 * i));
-    if (ext) {
-        b.bs[0] = __ldg(reinterpret_cast<const uint4 *>(bs16));
-        b.bs[1] = __ldg(reinterpret_cast<const uint4 *>(bs16 + 8));
-    }
-}
-
-// B rows of one gate_up stage: 128 q8 values of one pair's token (+ the min-term columns
-// [bsum_j >> 6 | bsum_j & 63] of the first half of a Q4_K super-block)
-__device__ __forceinline__ void gu_b(const GuBRaw &b, bool ext, uint8_t *tile, int c) {
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        uint32_t o0, o1, o2, o3;
-        s8x4_h(b.v[i].x, o0, o1);
-        s8x4_h(b.v[i].y, o2, o3);
-        sts128(tile + canon_off(c, 2 * i, kGuKc), o0, o1, o2, o3);
-        s8x4_h(b.v[i].z, o0, o1);
-        s8x4_h(b.v[i].w, o2, o3);
-        sts128(tile + canon_off(c, 2 * i + 1, kGuKc), o0, o1, o2, o3);
-    }
-    if (ext) {
-        const uint32_t w[8] = {b.bs[0].x, b.bs[0].y, b.bs[0].z, b.bs[0].w, b.bs[1].x, b.bs[1].y, b.bs[1].z, b.bs[1].w};
-        int hi[8], lo[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const int sm = (int)(int16_t)(w[j] & 0xffffu) + (int)(int16_t)(w[j] >> 16);   // bsums 2j, 2j+1
-            hi[j] = sm >> 6;     // floor division: sm = 64 * hi + lo, lo in [0, 63]
-            lo[j] = sm & 63;
-        }
-        sts128(tile + canon_off(c, 16, kGuKc), pack_h2i(hi[0], hi[1]), pack_h2i(hi[2], hi[3]), pack_h2i(hi[4], hi[5]),
-               pack_h2i(hi[6], hi[7]));
-        sts128(tile + canon_off(c, 17, kGuKc), pack_h2i(lo[0], lo[1]), pack_h2i(lo[2], lo[3]), pack_h2i(lo[4], lo[5]),
-               pack_h2i(lo[6], lo[7]));
-    }
-}
 
 // Raw bytes of one down stage: two Q5_0 blocks (11 words) or two IQ4_NL blocks (9 words) of a
 // weight row, 4-byte aligned (44- and 36-byte stages of 484- and 396-byte rows)
@@ -424,23 +394,6 @@ __device__ __forceinline__ void dn_a_iq4nl(const DnARaw &a, const uint32_t (&kv)
     }
 }
 
-// B rows of one down stage: 64 Q8_0 values of one pair
-__device__ __forceinline__ void dn_b_load(const int8_t *q8, uint4 (&v)[4]) {
-#pragma unroll
-    for (int i = 0; i < 4; ++i) v[i] = __ldg(reinterpret_cast<const uint4 *>(q8 + 16 * i));
-}
-__device__ __forceinline__ void dn_b(const uint4 (&v)[4], uint8_t *tile, int c) {
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        uint32_t o0, o1, o2, o3;
-        s8x4_h(v[i].x, o0, o1);
-        s8x4_h(v[i].y, o2, o3);
-        sts128(tile + canon_off(c, 2 * i, kDnKc), o0, o1, o2, o3);
-        s8x4_h(v[i].z, o0, o1);
-        s8x4_h(v[i].w, o2, o3);
-        sts128(tile + canon_off(c, 2 * i + 1, kDnKc), o0, o1, o2, o3);
-    }
-}
 
 struct PfParams {
     int32_t T, E, d, k, nff;
@@ -451,8 +404,11 @@ struct PfParams {
     const int8_t *xq8;                // [T][d] Q8_K values
     const float *xd;                  // [T][d/256] Q8_K scales
     const int16_t *xbs;               // [T][d/256][16] Q8_K bsums
-    int8_t *a8;                       // [P slots][nff] Q8_0 values of the GeGLU output
-    float *ad;                        // [P slots][nff/32] Q8_0 scales
+    uint8_t *bimg;                    // gate_up B operand images, [tile][sb][half][kPfGuImageBytes]
+    float *dxt;                       // [tile][sb][128] Q8_K scale of each tile row
+    float *hbuf;                      // [slot][2 n_ff] gate_up outputs, f32
+    uint8_t *dimg;                    // down B operand images, [tile][stage][kPfDnImageBytes]
+
     float *h;                         // optional [P pairs][2 nff] gate_up outputs
     float *y;                         // [P slots][d] down outputs (scaled)
 };
@@ -470,7 +426,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gate_up_kernel(PfParams p) {
     GuSmem &S = *reinterpret_cast<GuSmem *>(pf_smem);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (tid == 0) {
-        for (int s = 0; s < kGuStages; ++s) { mbar_init(&S.full[s], kPfConvWarps); mbar_init(&S.empty[s], 1); }
+        for (int s = 0; s < kGuStages; ++s) { mbar_init(&S.full[s], kPfConvWarps + 1); mbar_init(&S.empty[s], 1); }
         for (int b = 0; b < 2; ++b) { mbar_init(&S.accfull[b], 1); mbar_init(&S.accempty[b], kPfEpiWarps); }
         mbar_init(&S.done, 1);
         mbar_init(&S.epibar, kPfEpiWarps);
@@ -484,17 +440,17 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gate_up_kernel(PfParams p) {
     const uint32_t tmem = S.tmem;
     volatile int32_t *abort = &S.abort;
     pdl_wait();
-    const int nsb = p.d / QK_K, n_mb = p.nff / 64, k = p.k;
+    const int nsb = p.d / QK_K, n_mb = p.nff / 64;
     const int units = *p.n_tiles * n_mb;
     const int gu_rows = 2 * p.nff;
 
     if (warp < kPfConvWarps) {
         // ------------------------------------------------ converters
-        // Software-pipelined: the B loads of a stage fly while its A rows convert, and the A loads
-        // of the next stage while its B rows convert.
+        // Thread i expands weight row i; thread 0 also fetches the stage's B operand image (built by
+        // pf_gather_kernel) with one bulk copy. Software-pipelined: the raw rows of a stage are
+        // loaded two stages ahead (one register buffer per half super-block).
         int it = 0;
-        GuARaw ar;
-        GuBRaw br;
+        GuARaw ar0, ar1;
         for (int u = blockIdx.x; u < units && !warp_aborted(abort); u += gridDim.x) {
             const int ti = u / n_mb, mb = u - ti * n_mb;
             const PfTile tl = p.tiles[ti];
@@ -502,31 +458,29 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gate_up_kernel(PfParams p) {
             const bool q4 = pv.type == T_Q4_K;
             const int bsz = q4 ? B_Q4_K : B_IQ2_S;
             const int rb = (int)row_bytes(pv.type, p.d);
-            const uint8_t *rows = tile_rows(pv, tl.widx, gu_rows, p.d);
-            const int r = tid, c = tid;        // A row and B row of this thread
+            const uint32_t bbytes = (uint32_t)(((tl.n + 15) & ~15) / 8) * (kGuKc * 128);
+            const uint8_t *bsrc = p.bimg + (size_t)ti * nsb * 2 * kPfGuImageBytes;
+            const int r = tid;
             const int wr = r < 64 ? 64 * mb + r : p.nff + 64 * mb + (r - 64);
-            const uint8_t *arow = rows + (size_t)wr * rb;
-            const int8_t *xrow = nullptr;
-            const int16_t *xbs = nullptr;
-            if (c < tl.n) {
-                const int t = p.perm[tl.slot0 + c] / k;
-                xrow = p.xq8 + (size_t)t * p.d;
-                xbs = p.xbs + (size_t)t * nsb * 16;
-            }
-            gu_a_load(arow, 0, q4, ar);
+            const uint8_t *arow = tile_rows(pv, tl.widx, gu_rows, p.d) + (size_t)wr * rb;
+            gu_a_load(arow, 0, q4, ar0);
+            gu_a_load(arow, 1, q4, ar1);
             bool ok = true;
             for (int sb = 0; sb < nsb && ok; ++sb) {
+#pragma unroll
                 for (int h = 0; h < 2; ++h, ++it) {
-                    const int s = it & 1;
-                    if (xrow) gu_b_load(xrow + sb * QK_K + h * 128, xbs + sb * 16, q4 && h == 0, br);
+                    const int s = it % kGuStages;
                     if (tid == 0) PTRACE(0, 0, it, 0);
-                    if (it >= kGuStages && !pf_wait_warp(&S.empty[s], ((it >> 1) & 1) ^ 1, abort)) { ok = false; break; }
-                    if (tid == 0) PTRACE(0, 0, it, 1);
+                    if (it >= kGuStages && !pf_wait_warp(&S.empty[s], ((it / kGuStages) - 1) & 1, abort)) { ok = false; break; }
+                    if (tid == 0) {
+                        PTRACE(0, 0, it, 1);
+                        mbar_expect_tx(&S.full[s], bbytes);
+                        bulk_g2s(S.b[s], bsrc + (size_t)(2 * sb + h) * kPfGuImageBytes, bbytes, &S.full[s]);
+                    }
+                    GuARaw &ar = h == 0 ? ar0 : ar1;
                     if (q4) gu_a_q4k(ar, h, S.a[s], r);
                     else gu_a_iq2s(ar, S.a[s], r);
-                    const int nsb_ = sb + h;           // the next stage: (sb, 1) or (sb + 1, 0)
-                    if (nsb_ < nsb) gu_a_load(arow + nsb_ * bsz, h ^ 1, q4, ar);
-                    if (xrow) gu_b(br, q4 && h == 0, S.b[s], c);
+                    if (sb + 1 < nsb) gu_a_load(arow + (sb + 1) * bsz, h, q4, ar);   // two stages ahead
                     if (tid == 0) PTRACE(0, 0, it, 2);
                     fence_async_smem();
                     __syncwarp();
@@ -551,9 +505,9 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gate_up_kernel(PfParams p) {
                     tc_fence_after();
                     const uint32_t dmain = tmem + (uint32_t)(b * 256), dmin = dmain + 128;
                     for (int h = 0; h < 2; ++h, ++it) {
-                        const int s = it & 1;
+                        const int s = it % kGuStages;
                         PTRACE(0, 1, it, 0);
-                        if (!pf_wait(&S.full[s], (it >> 1) & 1, abort)) break;
+                        if (!pf_wait(&S.full[s], (it / kGuStages) & 1, abort)) break;
                         PTRACE(0, 1, it, 1);
                         tc_fence_after();
                         const uint32_t a0 = smem_addr(S.a[s]), b0 = smem_addr(S.b[s]);
@@ -578,10 +532,9 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gate_up_kernel(PfParams p) {
         const int ew = warp - kPfEpiWarp0, et = tid - kPfEpiWarp0 * 32;
         const int q = warp & 3, ch = ew >> 2;
         const int r = 32 * q + lane;
-        const int nb32 = p.nff / 32;
-        int sbc = 0;
+        int sbc = 0, ucount = 0;
         uint32_t eph = 0;
-        for (int u = blockIdx.x; u < units && !warp_aborted(abort); u += gridDim.x) {
+        for (int u = blockIdx.x; u < units && !warp_aborted(abort); u += gridDim.x, ++ucount) {
             const int ti = u / n_mb, mb = u - ti * n_mb;
             const PfTile tl = p.tiles[ti];
             const PoolView &pv = p.gu[tl.cls];
@@ -590,11 +543,10 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gate_up_kernel(PfParams p) {
             const int N = (tl.n + 15) & ~15;
             const int wr = r < 64 ? 64 * mb + r : p.nff + 64 * mb + (r - 64);
             const uint8_t *arow = tile_rows(pv, tl.widx, gu_rows, p.d) + (size_t)wr * rb;
-            for (int i = et; i < tl.n * nsb; i += kPfEpiWarps * 32) {
-                const int c = i / nsb, sb = i - c * nsb;
-                S.dxs[sb][c] = p.xd[(size_t)(p.perm[tl.slot0 + c] / k) * nsb + sb];
-            }
+            for (int i = et; i < nsb * kPfN; i += kPfEpiWarps * 32)
+                (&S.dxs[0][0])[i] = p.dxt[(size_t)ti * nsb * kPfN + i];
             if (!epi_barrier(&S.epibar, eph, abort)) break;
+            if (et == 0) UTRACE(ucount, 0);
             float acc[64];
 #pragma unroll
             for (int i = 0; i < 64; ++i) acc[i] = 0.f;
@@ -637,50 +589,19 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gate_up_kernel(PfParams p) {
                 if (et == 0) PTRACE(0, 2, sbc, 2);
             }
             if (warp_aborted(abort)) break;
-            // GeGLU and Q8_0 over all epilogue warps: gate (lanes 0-63) and up (lanes 64-127) rows
-            // go to shared memory, then each warp takes (pair, 32-output block) items, lane = output
-            if (r < 64) {
+            if (et == 0) UTRACE(ucount, 1);
+            // the unit's 64 gate and 64 up rows for every pair of the tile, f32, slot order
+            // ([slot][2 n_ff]); lanes write consecutive rows
+            {
+                const int wr = r < 64 ? 64 * mb + r : p.nff + 64 * mb + (r - 64);
+                float *hb = p.hbuf + (size_t)tl.slot0 * 2 * p.nff + wr;
 #pragma unroll
                 for (int i = 0; i < 64; ++i)
-                    if (64 * ch + i < tl.n) S.xg[64 * ch + i][r] = acc[i];
-            } else {
-#pragma unroll
-                for (int i = 0; i < 64; ++i)
-                    if (64 * ch + i < tl.n) S.xu[64 * ch + i][r - 64] = acc[i];
+                    if (64 * ch + i < tl.n) hb[(size_t)(64 * ch + i) * 2 * p.nff] = acc[i];
             }
+            if (et == 0) UTRACE(ucount, 3);
             if (!epi_barrier(&S.epibar, eph, abort)) break;
-            const int items = 2 * tl.n;
-            for (int i0 = ew * kGegluBatch; i0 < items; i0 += kPfEpiWarps * kGegluBatch) {
-                float g[kGegluBatch], uu[kGegluBatch];
-                uint16_t tv[kGegluBatch];
-#pragma unroll
-                for (int j = 0; j < kGegluBatch; ++j) {
-                    const int item = i0 + j < items ? i0 + j : items - 1;
-                    g[j] = S.xg[item >> 1][32 * (item & 1) + lane];
-                    uu[j] = S.xu[item >> 1][32 * (item & 1) + lane];
-                }
-#pragma unroll
-                for (int j = 0; j < kGegluBatch; ++j) tv[j] = g_gelu_f16[f2h_rn(g[j])];   // loads in flight together
-#pragma unroll
-                for (int j = 0; j < kGegluBatch; ++j) {
-                    const int item = i0 + j;
-                    if (item >= items) break;        // warp-uniform
-                    const int col = item >> 1, blk = item & 1, slot = tl.slot0 + col;
-                    // geglu1 (ggml-cpu vec.h:1414): 0 below -10, g * u above 10, else table(g) * u
-                    const float a = g[j] <= -10.0f ? 0.0f : (g[j] >= 10.0f ? __fmul_rn(g[j], uu[j]) : __fmul_rn(h2f(tv[j]), uu[j]));
-                    const float amax = warp_max(fabsf(a));
-                    const float dd = h2f(f2h_rn(__fdiv_rn(amax, 127.f)));
-                    const float id = amax != 0.f ? __fdiv_rn(127.f, amax) : 0.f;
-                    p.a8[(size_t)slot * p.nff + 64 * mb + 32 * blk + lane] = (int8_t)__float2int_rn(__fmul_rn(a, id));
-                    if (lane == 0) p.ad[(size_t)slot * nb32 + 2 * mb + blk] = dd;
-                    if (p.h) {
-                        float *hp = p.h + (size_t)p.perm[slot] * 2 * p.nff;
-                        hp[64 * mb + 32 * blk + lane] = g[j];
-                        hp[p.nff + 64 * mb + 32 * blk + lane] = uu[j];
-                    }
-                }
-            }
-            if (!epi_barrier(&S.epibar, eph, abort)) break;
+            if (et == 0) UTRACE(ucount, 4);
         }
     }
     tc_fence_before();
@@ -693,15 +614,15 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gate_up_kernel(PfParams p) {
 
 // ---------------------------------------------------------------- down grouped GEMM
 // Work unit (tile, mb): the pairs of one expert tile against down rows [128 mb, 128 mb + 128).
-__global__ void __launch_bounds__(kPfThreads, 1) pf_down_kernel(PfParams p) {
+__global__ void __launch_bounds__(kDnThreads, 1) pf_down_kernel(PfParams p) {
     extern __shared__ __align__(1024) uint8_t pf_smem[];
     DnSmem &S = *reinterpret_cast<DnSmem *>(pf_smem);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (tid == 0) {
-        for (int s = 0; s < kDnStages; ++s) { mbar_init(&S.full[s], kPfConvWarps); mbar_init(&S.empty[s], 1); }
-        for (int b = 0; b < kDnAccBufs; ++b) { mbar_init(&S.accfull[b], 1); mbar_init(&S.accempty[b], kPfEpiWarps); }
+        for (int s = 0; s < kDnStages; ++s) { mbar_init(&S.full[s], kPfConvWarps + 1); mbar_init(&S.empty[s], 1); }
+        for (int b = 0; b < kDnAccBufs; ++b) { mbar_init(&S.accfull[b], 1); mbar_init(&S.accempty[b], kDnEpiWarps); }
         mbar_init(&S.done, 1);
-        mbar_init(&S.epibar, kPfEpiWarps);
+        mbar_init(&S.epibar, kDnEpiWarps);
         S.abort = 0;
         fence_mbar_init();
     }
@@ -722,30 +643,45 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_down_kernel(PfParams p) {
             kv[i] = (uint32_t)(uint8_t)g_iq4nl[4 * i] | ((uint32_t)(uint8_t)g_iq4nl[4 * i + 1] << 8) |
                     ((uint32_t)(uint8_t)g_iq4nl[4 * i + 2] << 16) | ((uint32_t)(uint8_t)g_iq4nl[4 * i + 3] << 24);
         int it = 0;
-        DnARaw ar;
-        uint4 br[4];
+        DnARaw ar0, ar1;
         for (int u = blockIdx.x; u < units && !warp_aborted(abort); u += gridDim.x) {
             const int ti = u / n_mb, mb = u - ti * n_mb;
             const PfTile tl = p.tiles[ti];
             const PoolView &pv = p.dn[tl.cls];
             const bool q5 = pv.type == T_Q5_0;
             const int rb = (int)row_bytes(pv.type, p.nff);
-            const int r = tid, c = tid;
+            const int r = tid;
             const uint8_t *arow = tile_rows(pv, tl.widx, p.d, p.nff) + (size_t)(kPfM * mb + r) * rb;
-            const int8_t *brow = c < tl.n ? p.a8 + (size_t)(tl.slot0 + c) * p.nff : nullptr;
+            const uint32_t bbytes = (uint32_t)(((tl.n + 15) & ~15) / 8) * (kDnKc * 128);
+            const uint8_t *bsrc = p.dimg + (size_t)ti * nst * 2 * kPfDnImageBytes;
             const int sbytes = q5 ? 2 * B_Q5_0 : 2 * B_IQ4_NL;
-            dn_a_load(arow, q5, ar);
-            for (int st = 0; st < nst; ++st, ++it) {
-                const int s = it % kDnStages;
-                if (brow) dn_b_load(brow + 64 * st, br);
-                if (it >= kDnStages && !pf_wait_warp(&S.empty[s], ((it / kDnStages) - 1) & 1, abort)) break;
-                if (q5) dn_a_q5_0(ar, S.a[s], r);
-                else dn_a_iq4nl(ar, kv, S.a[s], r);
-                if (st + 1 < nst) dn_a_load(arow + (st + 1) * sbytes, q5, ar);
-                if (brow) dn_b(br, S.b[s], c);
-                fence_async_smem();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&S.full[s]);
+            dn_a_load(arow, q5, ar0);
+            if (nst > 1) dn_a_load(arow + sbytes, q5, ar1);
+            for (int st0 = 0; st0 < nst; st0 += 2) {
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    const int st = st0 + e;
+                    if (st >= nst) break;
+                    const int s = it % kDnStages;
+                    if (tid == 0) PTRACE(1, 0, it, 0);
+                    if (it >= kDnStages && !pf_wait_warp(&S.empty[s], ((it / kDnStages) - 1) & 1, abort)) { st0 = nst; break; }
+                    if (tid == 0) {
+                        PTRACE(1, 0, it, 1);
+                        mbar_expect_tx(&S.full[s], 2 * bbytes);
+                        bulk_g2s(S.b[s], bsrc + (size_t)st * 2 * kPfDnImageBytes, bbytes, &S.full[s]);
+                        bulk_g2s(S.b[s] + kDnTileBytes, bsrc + (size_t)st * 2 * kPfDnImageBytes + kPfDnImageBytes, bbytes,
+                                 &S.full[s]);
+                    }
+                    DnARaw &ar = e == 0 ? ar0 : ar1;
+                    if (q5) dn_a_q5_0(ar, S.a[s], r);
+                    else dn_a_iq4nl(ar, kv, S.a[s], r);
+                    if (st + 2 < nst) dn_a_load(arow + (st + 2) * sbytes, q5, ar);   // two stages ahead
+                    if (tid == 0) PTRACE(1, 0, it, 2);
+                    fence_async_smem();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&S.full[s]);
+                    ++it;
+                }
             }
         }
     } else if (warp == kPfMmaWarp) {
@@ -758,7 +694,9 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_down_kernel(PfParams p) {
                 const uint32_t idesc = umma_idesc_f16(kPfM, N);
                 for (int st = 0; st < nst && !*abort; ++st, ++it) {
                     const int s = it % kDnStages;
+                    PTRACE(1, 1, it, 0);
                     if (!pf_wait(&S.full[s], (it / kDnStages) & 1, abort)) break;
+                    PTRACE(1, 1, it, 1);
                     tc_fence_after();
                     const uint32_t a0 = smem_addr(S.a[s]), b0 = smem_addr(S.b[s]);
                     for (int bi = 0; bi < 2; ++bi, ++ac) {
@@ -769,11 +707,14 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_down_kernel(PfParams p) {
 #pragma unroll
                         for (int ks = 0; ks < 2; ++ks) {
                             const uint32_t off = (uint32_t)((4 * bi + 2 * ks) * 128);
-                            umma_f16(dt, umma_sdesc(a0 + off, 128, sbo), umma_sdesc(b0 + off, 128, sbo), idesc, ks);
+                            const uint64_t da = umma_sdesc(a0 + off, 128, sbo);
+                            umma_f16(dt, da, umma_sdesc(b0 + off, 128, sbo), idesc, ks);                    // dx*q8 hi
+                            umma_f16(dt, da, umma_sdesc(b0 + kDnTileBytes + off, 128, sbo), idesc, 1u);      // dx*q8 lo
                         }
                         umma_commit(&S.accfull[b]);
                     }
                     umma_commit(&S.empty[s]);
+                    PTRACE(1, 1, it, 2);
                 }
             }
             umma_commit(&S.done);
@@ -781,9 +722,11 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_down_kernel(PfParams p) {
         }
         __syncwarp();
     } else {
-        const int ew = warp - kPfEpiWarp0, et = tid - kPfEpiWarp0 * 32;
-        const int q = warp & 3, ch = ew >> 2;
-        const int r = 32 * q + lane;
+        // epilogue: warp -> (lane quadrant q, column quarter cq); promotion per 32-block by the
+        // row's d_w (the activation scale is already in the operand)
+        const int ew = warp - kPfEpiWarp0;
+        const int q = warp & 3, cq = ew >> 2;
+        const int r = 32 * q + lane, c0 = 32 * cq;
         int ac = 0;
         uint32_t eph = 0;
         for (int u = blockIdx.x; u < units && !warp_aborted(abort); u += gridDim.x) {
@@ -793,45 +736,44 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_down_kernel(PfParams p) {
             const int bsz = pv.type == T_Q5_0 ? B_Q5_0 : B_IQ4_NL;
             const int rb = (int)row_bytes(pv.type, p.nff);
             const int N = (tl.n + 15) & ~15;
-            const uint8_t *arow = tile_rows(pv, tl.widx, p.d, p.nff) + (size_t)(kPfM * mb + r) * rb;
-            for (int i = et; i < tl.n * nblk; i += kPfEpiWarps * 32) {
-                const int c = i / nblk, bk = i - c * nblk;
-                S.dxs[bk][c] = p.ad[(size_t)(tl.slot0 + c) * nblk + bk];
-            }
-            if (!epi_barrier(&S.epibar, eph, abort)) break;
-            float acc[64];
+            const uint16_t *dwp = reinterpret_cast<const uint16_t *>(tile_rows(pv, tl.widx, p.d, p.nff) +
+                                                                     (size_t)(kPfM * mb + r) * rb);
+            float acc[32];
 #pragma unroll
-            for (int i = 0; i < 64; ++i) acc[i] = 0.f;
+            for (int i = 0; i < 32; ++i) acc[i] = 0.f;
+            uint16_t dw_next = __ldg(reinterpret_cast<const unsigned short *>(dwp));
             for (int bk = 0; bk < nblk; ++bk, ++ac) {
-                const float dw = h2f(*reinterpret_cast<const uint16_t *>(arow + bk * bsz));
+                const float dw = h2f(dw_next);
+                if (bk + 1 < nblk) dw_next = __ldg(reinterpret_cast<const unsigned short *>(dwp) + (bk + 1) * (bsz / 2));
                 const int b = ac % kDnAccBufs;
+                if (ew == 0 && lane == 0) PTRACE(1, 2, ac, 0);
                 if (!pf_wait_warp(&S.accfull[b], (ac / kDnAccBufs) & 1, abort)) break;
+                if (ew == 0 && lane == 0) PTRACE(1, 2, ac, 1);
                 tc_fence_after();
-                const uint32_t tb = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(b * 128);
+                const uint32_t tb = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(b * 128 + c0);
+                if (c0 < N) {
+                    float v[32];
+                    if (c0 + 16 < N) {
+                        tmem_ld16x2(tb, tb + 16, *reinterpret_cast<float(*)[16]>(&v[0]), *reinterpret_cast<float(*)[16]>(&v[16]));
 #pragma unroll
-                for (int cc = 0; cc < 4; ++cc) {
-                    const int col = 64 * ch + 16 * cc;
-                    if (col < N) {
-                        float v[16];
-                        tmem_ld16(tb + col, v);
+                        for (int i = 0; i < 32; ++i) acc[i] = fmaf(dw, v[i], acc[i]);
+                    } else {
+                        tmem_ld16(tb, *reinterpret_cast<float(*)[16]>(&v[0]));
 #pragma unroll
-                        for (int i = 0; i < 16; ++i)
-                            acc[16 * cc + i] = fmaf(dw * S.dxs[bk][col + i], v[i], acc[16 * cc + i]);
+                        for (int i = 0; i < 16; ++i) acc[i] = fmaf(dw, v[i], acc[i]);
                     }
                 }
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&S.accempty[b]);
+                if (ew == 0 && lane == 0) PTRACE(1, 2, ac, 2);
             }
             if (warp_aborted(abort)) break;
             const float sc = pv.scale ? pv.scale[tl.widx] : 1.f;
 #pragma unroll
-            for (int i = 0; i < 64; ++i) {
-                const int col = 64 * ch + i;
-                if (col < tl.n) {
-                    const float v = pv.scale ? __fmul_rn(acc[i], sc) : acc[i];
-                    p.y[(size_t)(tl.slot0 + col) * p.d + kPfM * mb + r] = v;
-                }
+            for (int i = 0; i < 32; ++i) {
+                const int col = c0 + i;
+                if (col < tl.n) p.y[(size_t)(tl.slot0 + col) * p.d + kPfM * mb + r] = pv.scale ? __fmul_rn(acc[i], sc) : acc[i];
             }
             if (!epi_barrier(&S.epibar, eph, abort)) break;
         }
@@ -841,6 +783,130 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_down_kernel(PfParams p) {
     if (warp == kPfMmaWarp) {
         tc_fence_after();
         tmem_dealloc_warp(tmem, 512);
+    }
+}
+
+// ---------------------------------------------------------------- GeGLU + Q8_0 -> down operand images
+// CTA per (tile, 32-output block); warp per tile row (pair), lane = output: a = geglu1(g, u) with
+// ggml-cpu's fp16-table GELU (vec.h:1414), Q8_0 of the 32 values (AVX2 quantize_row_q8_0
+// semantics), written as fp16 into the tile's down operand image, the scale into the tile's
+// per-row table. A kernel of its own: the table lookups are random, and here the table stays
+// in L2 instead of being evicted by the weight stream of the GEMMs.
+constexpr int kGegluRows = 4;   // pairs a warp keeps in flight
+__global__ void __launch_bounds__(256) pf_geglu_kernel(PfParams p) {
+    pdl_wait();
+    pdl_launch_dependents();
+    const int ti = blockIdx.x, blk = blockIdx.y;
+    if (ti >= *p.n_tiles) return;
+    const PfTile tl = p.tiles[ti];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nff = p.nff;
+    const int st = blk >> 1, kcol = 4 * (blk & 1) + (lane >> 3);
+    uint8_t *dimg = p.dimg + ((size_t)ti * (nff / 64) + st) * 2 * kPfDnImageBytes;
+    for (int c0 = warp * kGegluRows; c0 < tl.n; c0 += 8 * kGegluRows) {
+        float g[kGegluRows], u[kGegluRows];
+        uint16_t tv[kGegluRows];
+#pragma unroll
+        for (int j = 0; j < kGegluRows; ++j) {
+            const int c = min(c0 + j, tl.n - 1);
+            const float *hr = p.hbuf + (size_t)(tl.slot0 + c) * 2 * nff + 32 * blk + lane;
+            g[j] = hr[0];
+            u[j] = hr[nff];
+        }
+#pragma unroll
+        for (int j = 0; j < kGegluRows; ++j) tv[j] = g_gelu_f16[f2h_rn(g[j])];
+        float a[kGegluRows], m[kGegluRows];
+#pragma unroll
+        for (int j = 0; j < kGegluRows; ++j) {
+            a[j] = g[j] <= -10.0f ? 0.0f : (g[j] >= 10.0f ? __fmul_rn(g[j], u[j]) : __fmul_rn(h2f(tv[j]), u[j]));
+            m[j] = fabsf(a[j]);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+            for (int j = 0; j < kGegluRows; ++j) m[j] = fmaxf(m[j], __shfl_xor_sync(0xffffffffu, m[j], o));
+#pragma unroll
+        for (int j = 0; j < kGegluRows; ++j) {
+            const int c = c0 + j;
+            if (c >= tl.n) break;   // warp-uniform
+            const float dd = h2f(f2h_rn(__fdiv_rn(m[j], 127.f)));
+            const float id = m[j] != 0.f ? __fdiv_rn(127.f, m[j]) : 0.f;
+            // the down operand is dx * q8 (exact in f32: an fp16 scale times a 7-bit integer), split
+            // into fp16 hi + lo, both exact: the value and its parts are multiples of 2^-24 with at
+            // most 18 significant bits
+            const float v = __fmul_rn(dd, (float)__float2int_rn(__fmul_rn(a[j], id)));
+            if (fabsf(v) > 65504.f) atomicOr(&g_error, ERR_RANGE);
+            const __half hi = __float2half_rn(v);
+            const __half lo = __float2half_rn(__fsub_rn(v, __half2float(hi)));
+            const uint32_t off = canon_off(c, kcol, kDnKc) + 2 * (lane & 7);
+            *reinterpret_cast<__half *>(dimg + off) = hi;
+            *reinterpret_cast<__half *>(dimg + kPfDnImageBytes + off) = lo;
+            if (p.h) {
+                float *hp = p.h + (size_t)p.perm[tl.slot0 + c] * 2 * nff + 32 * blk + lane;
+                hp[0] = g[j];
+                hp[nff] = u[j];
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------- gate_up B operand images
+// One CTA per (tile, super-block), thread = (tile row c, half h): the q8 values of the row's token
+// as fp16 in the canonical layout of a gate_up stage, the min-term columns [bsum_j >> 6 |
+// bsum_j & 63] in the first half, and the row's Q8_K scale. Rows n..N-1 (padding up to the
+// MMA's N) are zero. Each image is read by the tile's n_ff / 64 gate_up work units.
+__global__ void __launch_bounds__(256) pf_gather_kernel(PfParams p) {
+    pdl_wait();
+    pdl_launch_dependents();
+    const int ti = blockIdx.x, sb = blockIdx.y;
+    if (ti >= *p.n_tiles) return;
+    const PfTile tl = p.tiles[ti];
+    const int N = (tl.n + 15) & ~15, nsb = p.d / QK_K;
+    const int c = threadIdx.x >> 1, h = threadIdx.x & 1;
+    if (c >= N) return;
+    uint8_t *img = p.bimg + ((size_t)(ti * nsb + sb) * 2 + h) * kPfGuImageBytes;
+    float *dxt = p.dxt + ((size_t)ti * nsb + sb) * kPfN;
+    if (c >= tl.n) {
+        const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+        for (int col = 0; col < kGuKc; ++col) *reinterpret_cast<uint4 *>(img + canon_off(c, col, kGuKc)) = z;
+        if (h == 0) dxt[c] = 0.f;
+        return;
+    }
+    const int t = p.perm[tl.slot0 + c] / p.k;
+    const int8_t *q8 = p.xq8 + (size_t)t * p.d + sb * QK_K + h * 128;
+    uint4 v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = __ldg(reinterpret_cast<const uint4 *>(q8 + 16 * i));
+    uint4 b0 = make_uint4(0u, 0u, 0u, 0u), b1 = b0;
+    const int16_t *bs16 = p.xbs + ((size_t)t * nsb + sb) * 16;
+    if (h == 0) {
+        b0 = __ldg(reinterpret_cast<const uint4 *>(bs16));
+        b1 = __ldg(reinterpret_cast<const uint4 *>(bs16 + 8));
+        dxt[c] = p.xd[(size_t)t * nsb + sb];
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        uint32_t o0, o1, o2, o3;
+        s8x4_h(v[i].x, o0, o1);
+        s8x4_h(v[i].y, o2, o3);
+        *reinterpret_cast<uint4 *>(img + canon_off(c, 2 * i, kGuKc)) = make_uint4(o0, o1, o2, o3);
+        s8x4_h(v[i].z, o0, o1);
+        s8x4_h(v[i].w, o2, o3);
+        *reinterpret_cast<uint4 *>(img + canon_off(c, 2 * i + 1, kGuKc)) = make_uint4(o0, o1, o2, o3);
+    }
+    if (h == 0) {
+        const uint32_t w[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+        int hi[8], lo[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int sm = (int)(int16_t)(w[j] & 0xffffu) + (int)(int16_t)(w[j] >> 16);   // bsums 2j, 2j+1
+            hi[j] = sm >> 6;     // floor division: sm = 64 * hi + lo, lo in [0, 63]
+            lo[j] = sm & 63;
+        }
+        *reinterpret_cast<uint4 *>(img + canon_off(c, 16, kGuKc)) =
+            make_uint4(pack_h2i(hi[0], hi[1]), pack_h2i(hi[2], hi[3]), pack_h2i(hi[4], hi[5]), pack_h2i(hi[6], hi[7]));
+        *reinterpret_cast<uint4 *>(img + canon_off(c, 17, kGuKc)) =
+            make_uint4(pack_h2i(lo[0], lo[1]), pack_h2i(lo[2], lo[3]), pack_h2i(lo[4], lo[5]), pack_h2i(lo[6], lo[7]));
     }
 }
 

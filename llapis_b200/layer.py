@@ -113,11 +113,11 @@ class MoELayer:
         return shape_ok and n_tokens >= int(capi.lib().moeb_set_prefill_min_tokens(0))
 
     def launches(self, n_tokens: int) -> int:
-        """Kernels one forward of n_tokens launches: seven on the prefill path, else one cooperative
+        """Kernels one forward of n_tokens launches: nine on the prefill path, else one cooperative
         fused kernel per 8-token chunk."""
         if n_tokens <= 0:
             return 0
-        return 7 if self.prefill_path(n_tokens) else (n_tokens + 7) // 8
+        return 9 if self.prefill_path(n_tokens) else (n_tokens + 7) // 8
 
     def workspace_bytes(self, n_tokens: int) -> int:
         return int(capi.lib().moeb_layer_workspace_size(C.byref(self.c), n_tokens))

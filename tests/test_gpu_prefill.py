@@ -24,7 +24,7 @@ def test_prefill_mini_vs_reference_fixture(golden, prefill_from):
     prefill_from(1)
     host = host_layer("mini_mixed")
     out, aux, layer = run_layer(host, golden["mini_x"])
-    assert layer.launches(golden["mini_x"].shape[0]) == 7
+    assert layer.launches(golden["mini_x"].shape[0]) == 9
     assert np.array_equal(aux["ids"], golden["mini_ids"])
     np.testing.assert_allclose(aux["logits"], golden["mini_logits"], rtol=1e-5, atol=1e-6)
     np.testing.assert_allclose(aux["weights"], golden["mini_weights"], rtol=1e-5, atol=1e-7)
@@ -47,7 +47,7 @@ def q80_flips(port, want_act, cond_act):
             if not np.array_equal(port.quantize_act(Q8_0, want_act[i]), port.quantize_act(Q8_0, cond_act[i]))]
 
 
-def check_stages(port, host, x, out, aux, tokens=None):
+def check_stages(port, host, x, out, aux, tokens=None, dispatch=True):
     """Stage by stage against the oracle port, on `tokens` (default all) of a forward of x:
       1. routing (ids, counts, stable permutation over the whole batch) exact for tokens without
          a near tie;
@@ -60,9 +60,10 @@ def check_stages(port, host, x, out, aux, tokens=None):
          output by up to a few 1e-3 of RMS at n_ff = 704, ~2% at the mini shape's n_ff = 64).
     Returns (end-to-end max-abs / rms, near-tie tokens, flip tokens)."""
     T, k = x.shape[0], host.top_k
-    flat = aux["ids"].reshape(-1)
-    assert np.array_equal(aux["counts"], np.bincount(flat, minlength=host.n_expert))
-    assert np.array_equal(aux["perm"], np.argsort(flat, kind="stable"))
+    if dispatch:   # the whole batch's dispatch (the decode path reports it for one-chunk calls only)
+        flat = aux["ids"].reshape(-1)
+        assert np.array_equal(aux["counts"], np.bincount(flat, minlength=host.n_expert))
+        assert np.array_equal(aux["perm"], np.argsort(flat, kind="stable"))
     tok = np.arange(T) if tokens is None else np.asarray(tokens)
     pr = (tok[:, None] * k + np.arange(k)[None, :]).reshape(-1)
     xs = np.ascontiguousarray(x[tok])
@@ -95,7 +96,7 @@ def test_layer_paths_vs_port_oracle(port, prefill_from, path, name, T):
     x = workload.make_input(workload.CONFIGS[name], n_tokens=T, stream=T + 1)
     out, aux, layer = run_layer(host, x, aux_names=("logits", "ids", "gate_up", "down", "counts", "perm"))
     assert layer.prefill_path(T) == (path == "prefill")
-    rel, nt, nf = check_stages(port, host, x, out, aux)
+    rel, nt, nf = check_stages(port, host, x, out, aux, dispatch=path == "prefill" or T <= 8)
     print(f"{path} {name} T={T}: max-abs / rms = {rel:.2e}; near-tie tokens {nt}, Q8_0-flip tokens {nf}")
 
 
@@ -111,7 +112,7 @@ def test_prefill_full_size(port, prefill_from):
     prefill_from(1)
     out, aux, layer = run_layer(host, x, aux_names=("logits", "ids", "gate_up", "down", "counts", "offsets",
                                                     "perm"))
-    assert layer.launches(T) == 7
+    assert layer.launches(T) == 9
     counts = np.bincount(aux["ids"].reshape(-1), minlength=host.n_expert)
     assert np.array_equal(aux["offsets"], np.concatenate([[0], np.cumsum(counts)]))
     assert counts.max() > 128, "the workload should put more than one tile on some expert"
