@@ -180,10 +180,150 @@ def run_reference(args):
     return 0
 
 
+def local_shard(host, rank, world):
+    """This rank's experts of a layer whose experts all sit in the hot class (expert-parallel)."""
+    import dataclasses
+    from llapis_b200.ep import local_experts
+    mine = local_experts(rank, host.n_expert, world)
+    assert host.n_slots == host.n_expert and np.array_equal(host.hot_ids, np.arange(host.n_expert))
+    return dataclasses.replace(host, hot_ids=mine, hot_gu=host.hot_gu[mine], hot_down=host.hot_down[mine],
+                               s_hot=host.s_hot[mine], cold_gu=None, cold_down=None, s_cold=None)
+
+
+def run_ep(args, cfg):
+    """Expert-parallel prefill: experts sharded over the ranks, tokens split
+    T/G per rank, NCCL all-to-all dispatch and combine (llapis_b200/ep.py); strong scaling."""
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    from llapis_b200 import capi, workload
+    from llapis_b200.ep import EPMoE
+    from llapis_b200.layer import MoELayer
+
+    rank, local, world = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    else:
+        dist.init_process_group("nccl", init_method="tcp://127.0.0.1:%d" % _free_port(), rank=0, world_size=1,
+                                timeout=timedelta(seconds=300), device_id=dev)
+    host = workload.build_layer(cfg)
+    layer = MoELayer(local_shard(host, rank, world), dev)
+    x_all = workload.make_input(cfg)
+    T = x_all.shape[0]
+    assert T % world == 0
+    x_host = x_all[rank * (T // world):(rank + 1) * (T // world)]
+    x = torch.from_numpy(x_host).to(dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    ep = EPMoE.from_layer(layer, group=None)
+    s = torch.cuda.current_stream(dev)
+
+    def timed(fn, steps):
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        for i in range(steps):
+            flush.zero_()
+            ev[i][0].record(s)
+            fn()
+            ev[i][1].record(s)
+        torch.cuda.synchronize()
+        return float(sum(a.elapsed_time(b) for a, b in ev))
+
+    for _ in range(args.warmup):
+        ep(x)
+    torch.cuda.synchronize()
+    dist.barrier()
+    with Clocks(local) as clk:
+        # keep the GPU loaded while the sampler takes its first readings: a FIXED number of steps,
+        # the same on every rank (each step holds collectives, so ranks must take the same count)
+        for _ in range(160):
+            ep(x)
+        torch.cuda.synchronize()
+        dev_ms = timed(lambda: ep(x), args.steps)
+    dist.barrier()
+    # compute-only: the same local expert work on the rows this rank received, without communication
+    recv_probe = {}
+
+    def experts_only():
+        layer.forward_routed(recv_probe["x"], recv_probe["ids"], recv_probe["w"])
+
+    orig = ep.experts_fn
+    ep.experts_fn = lambda rx, ri, rw: (recv_probe.update(x=rx, ids=ri, w=rw), orig(rx, ri, rw))[1]
+    ep(x)
+    torch.cuda.synchronize()
+    ep.experts_fn = orig
+    comp_ms = timed(experts_only, args.steps) if recv_probe["x"].shape[0] else 0.0
+    # kernel profile of this rank's expert half
+    lib = capi.lib()
+    names = ("router", "topk", "dispatch", "actq", "gather", "gate_up", "geglu", "down", "combine")
+    buf = (C.c_float * len(names))()
+    lib.moeb_prefill_profile(1)
+    experts_only()
+    capi.check(lib.moeb_prefill_profile_read(buf, len(names)))
+    lib.moeb_prefill_profile(0)
+    kernels_ms = dict(zip(names, buf[:]))
+    # end to end: pinned host shard in, result out
+    x_pin = torch.from_numpy(x_host).pin_memory()
+    o_pin = torch.empty_like(x_pin).pin_memory()
+
+    def e2e_step():
+        xe = x_pin.to(dev, non_blocking=True)
+        o_pin.copy_(ep(xe), non_blocking=True)
+
+    e2e_ms = timed(e2e_step, args.steps)
+    tot = torch.tensor([dev_ms, comp_ms, e2e_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(tot, op=dist.ReduceOp.MAX)
+    dev_ms, comp_ms, e2e_ms = tot.tolist()
+    hbm, tflops_peak, peak_kind = measured_peaks()
+    avg_ms = dev_ms / args.steps
+    flops = workload.layer_flops(host, T)
+    ach = flops / (avg_ms / 1e3) / 1e12
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": T * args.steps / (dev_ms / 1e3), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": avg_ms, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None,
+            "dtype": "int8 x q4/q5 integer dots on fp16-exact tcgen05 MMAs / f32",
+            "data": "synthetic (seeded N(0,0.02) weights quantised to ggml formats, bf16-valued N(0,1) activations)",
+            "config": {"workload": cfg.name, "n_tokens": T, "layers": 1, "d_model": cfg.d_model,
+                       "n_expert": cfg.n_expert, "top_k": cfg.top_k, "parallelism": f"ep{world}",
+                       "experts_per_gpu": cfg.n_expert // world, "tokens_per_gpu": T // world,
+                       "l2": "flushed between steps (256 MiB write, not timed)", "cuda_graph": False},
+            "e2e": {"value": T * args.steps / (e2e_ms / 1e3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": int(x_host.nbytes) * world, "d2h_bytes_per_step": int(x_host.nbytes) * world},
+            # per step: router + top-k, then the seven kernels of the routed expert half
+            "gpu_launches": 9 * args.steps,
+            "roofline": {"bound": "tensor", "achieved": ach, "peak": tflops_peak * world, "unit": "TFLOP/s",
+                         "frac": ach / (tflops_peak * world), "traffic": None,
+                         "peak_kind": f"{peak_kind} dense bf16 (burst) x {world} GPUs",
+                         "scope": "whole job: layer FLOPs / step time",
+                         "rank0_kernels_ms": kernels_ms},
+            "exposed_comm_ms": avg_ms - comp_ms / args.steps, "compute_only_ms": comp_ms / args.steps,
+            "cpu_baseline": None,
+            "clocks": clk.summary(),
+            "device_error": layer.device_error(),
+        }
+        print(json.dumps(line))
+    dist.destroy_process_group()
+    return 0
+
+
+def _free_port():
+    import socket
+    with socket.socket() as sk:
+        sk.bind(("127.0.0.1", 0))
+        return sk.getsockname()[1]
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
+    from llapis_b200 import workload as _wl
+    if args.config.startswith("ep_"):
+        return run_ep(args, _wl.CONFIGS[args.config])
 
     import torch
     import torch.distributed as dist

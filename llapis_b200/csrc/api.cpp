@@ -345,6 +345,65 @@ static int forward_prefill(const moeb_layer *L, const float *x, int32_t T, float
     return MOEB_OK;
 }
 
+extern "C" int moeb_layer_route(const moeb_layer *L, const float *x, int32_t n_tokens, float *logits, int32_t *ids,
+                                float *weights, void *stream) {
+    int rc = check_layer(L);
+    if (rc) return rc;
+    if (n_tokens < 0) return fail(MOEB_EINVAL, "n_tokens %d < 0", n_tokens);
+    if (n_tokens == 0) return MOEB_OK;
+    if (!x || !logits || !ids || !weights) return fail(MOEB_EINVAL, "moeb_layer_route: null x / logits / ids / weights");
+    if (!aligned16(x) || !aligned16(L->w_router)) return fail(MOEB_EINVAL, "x and router weights must be 16-byte aligned");
+    rc = ensure_device();
+    if (rc) return rc;
+    cudaError_t e = launch_route(L->w_router, L->b_router, x, n_tokens, L->n_expert, L->d_model, L->top_k, logits, ids,
+                                 weights, (cudaStream_t)stream);
+    if (e != cudaSuccess) return cuda_fail(e, "route launch");
+    return MOEB_OK;
+}
+
+extern "C" size_t moeb_routed_workspace_size(const moeb_layer *L, int32_t n_rows) {
+    if (!L || n_rows <= 0) return 0;
+    return carve_prefill(L, n_rows, nullptr).bytes;
+}
+
+extern "C" int moeb_layer_forward_routed(const moeb_layer *L, const float *x, int32_t n_rows, const int32_t *ids,
+                                         const float *weights, float *out, void *workspace, size_t workspace_bytes,
+                                         void *stream) {
+    int n_sms = 0;
+    int rc = check_forward(L, x, n_rows, out, workspace, workspace_bytes, L ? moeb_routed_workspace_size(L, n_rows) : 0,
+                           &n_sms);
+    if (rc || n_rows == 0) return rc;
+    if (!prefill_shape_ok(L))
+        return fail(MOEB_EINVAL, "moeb_layer_forward_routed: n_ff must be a multiple of 64, d_model of 128, d_model <= "
+                                 "4096 and n_ff <= 1024");
+    if (!ids || !weights) return fail(MOEB_EINVAL, "moeb_layer_forward_routed: null ids / weights");
+    const int d = L->d_model, k = L->top_k, E = L->n_expert;
+    PrefillWs w = carve_prefill(L, n_rows, (uint8_t *)workspace);
+    PrefillArgs a{};
+    a.w_router = L->w_router;
+    a.b_router = L->b_router;
+    a.x = x;
+    a.T = n_rows; a.E = E; a.d = d; a.k = k; a.nff = L->n_ff;
+    a.res = {L->hot.n, L->exp_slot, L->slot_exp, L->slot_state};
+    a.hot_gu = pool_view(L->hot, true);
+    a.cold_gu = pool_view(L->cold, true);
+    a.hot_dn = pool_view(L->hot, false);
+    a.cold_dn = pool_view(L->cold, false);
+    a.logits = w.logits;
+    a.ids = const_cast<int32_t *>(ids);       // read only when routed
+    a.w = const_cast<float *>(weights);
+    a.cnt = w.cnt; a.off = w.off; a.perm = w.perm; a.pos = w.pos;
+    a.tiles = w.tiles; a.n_tiles = w.n_tiles;
+    a.xq8 = w.xq8; a.xd = w.xd; a.xbs = w.xbs;
+    a.bimg = w.bimg; a.dxt = w.dxt; a.hbuf = w.hbuf; a.dimg = w.dimg; a.max_tiles = w.max_tiles;
+    a.y = w.y;
+    a.out = out;
+    a.routed = 1;
+    cudaError_t e = launch_prefill(a, (cudaStream_t)stream, n_sms);
+    if (e != cudaSuccess) return MOEB_ECUDA;
+    return MOEB_OK;
+}
+
 extern "C" int moeb_layer_forward(const moeb_layer *L, const float *x, int32_t n_tokens, float *out,
                                   const moeb_layer_aux *aux, void *workspace, size_t workspace_bytes, void *stream) {
     int n_sms = 0;

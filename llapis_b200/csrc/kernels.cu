@@ -1718,24 +1718,29 @@ cudaError_t launch_prefill(const PrefillArgs &a, cudaStream_t s, int n_sms) {
     const int T = a.T, E = a.E, d = a.d, k = a.k;
     int mark = 0;
     if ((e = prof_mark(s, mark++)) != cudaSuccess) return e;
-    {
-        const float *W = a.w_router, *b = a.b_router, *x = a.x;
-        float *lg = a.logits;
-        int t = T, ne = E, dd = d;
-        void *args[] = {&W, &b, &x, &lg, &t, &ne, &dd};
-        e = pf_launch("pf_router_kernel", (const void *)pf_router_kernel, dim3((T + kRtTok - 1) / kRtTok, (E + kRtExp - 1) / kRtExp),
-                      dim3(256), 0, s, true, args);
-        if (e != cudaSuccess) return e;
+    if (!a.routed) {
+        {
+            const float *W = a.w_router, *b = a.b_router, *x = a.x;
+            float *lg = a.logits;
+            int t = T, ne = E, dd = d;
+            void *args[] = {&W, &b, &x, &lg, &t, &ne, &dd};
+            e = pf_launch("pf_router_kernel", (const void *)pf_router_kernel, dim3((T + kRtTok - 1) / kRtTok, (E + kRtExp - 1) / kRtExp),
+                          dim3(256), 0, s, true, args);
+            if (e != cudaSuccess) return e;
+            if ((e = prof_mark(s, mark++)) != cudaSuccess) return e;
+        }
+        {
+            const float *lg = a.logits;
+            int32_t *ids = a.ids;
+            float *w = a.w;
+            int t = T, ne = E, kk = k;
+            void *args[] = {&lg, &ids, &w, &t, &ne, &kk};
+            e = pf_launch("pf_topk_kernel", (const void *)pf_topk_kernel, dim3((T + 7) / 8), dim3(256), 0, s, true, args);
+            if (e != cudaSuccess) return e;
+            if ((e = prof_mark(s, mark++)) != cudaSuccess) return e;
+        }
+    } else {   // routing given: the router and top-k slots of the profile read zero
         if ((e = prof_mark(s, mark++)) != cudaSuccess) return e;
-    }
-    {
-        const float *lg = a.logits;
-        int32_t *ids = a.ids;
-        float *w = a.w;
-        int t = T, ne = E, kk = k;
-        void *args[] = {&lg, &ids, &w, &t, &ne, &kk};
-        e = pf_launch("pf_topk_kernel", (const void *)pf_topk_kernel, dim3((T + 7) / 8), dim3(256), 0, s, true, args);
-        if (e != cudaSuccess) return e;
         if ((e = prof_mark(s, mark++)) != cudaSuccess) return e;
     }
     {
@@ -1798,6 +1803,18 @@ cudaError_t launch_prefill(const PrefillArgs &a, cudaStream_t s, int n_sms) {
         if (e != cudaSuccess) return e;
     }
     return prof_mark(s, mark++);
+}
+
+cudaError_t launch_route(const float *w_router, const float *b_router, const float *x, int T, int E, int d, int k,
+                         float *logits, int32_t *ids, float *w, cudaStream_t s) {
+    int t = T, ne = E, dd = d, kk = k;
+    const float *lgc = logits;
+    void *a1[] = {&w_router, &b_router, &x, &logits, &t, &ne, &dd};
+    cudaError_t e = pf_launch("pf_router_kernel", (const void *)pf_router_kernel,
+                              dim3((T + kRtTok - 1) / kRtTok, (E + kRtExp - 1) / kRtExp), dim3(256), 0, s, true, a1);
+    if (e != cudaSuccess) return e;
+    void *a2[] = {&lgc, &ids, &w, &t, &ne, &kk};
+    return pf_launch("pf_topk_kernel", (const void *)pf_topk_kernel, dim3((T + 7) / 8), dim3(256), 0, s, true, a2);
 }
 
 cudaError_t launch_quant_q8k(const float *x, uint8_t *dst, int rows, int d, int stride, cudaStream_t s) {

@@ -156,7 +156,11 @@ struct PrefillArgs {
     float *y;                   // [P][d] down outputs, slot order
     float *out;                 // [T][d]
     float *y_pairs;             // optional [P][d] down outputs, pair order
+    int32_t routed;             // 1: ids / w are given (the router and top-k kernels are skipped)
 };
+// router logits + softmax/top-k/weights only (the first two prefill kernels)
+cudaError_t launch_route(const float *w_router, const float *b_router, const float *x, int T, int E, int d, int k,
+                         float *logits, int32_t *ids, float *w, cudaStream_t s);
 cudaError_t launch_prefill(const PrefillArgs &a, cudaStream_t s, int n_sms);
 // router, top-k, dispatch, activation quantisation, gather, gate_up, GeGLU, down, combine
 constexpr int kPrefillKernels = 9;

@@ -1040,9 +1040,9 @@ __global__ void __launch_bounds__(1024, 1) pf_dispatch_kernel(PfDispatchParams p
     const unsigned lt = (1u << lane) - 1u;
     for (int base = lo; base < hi; base += 32) {
         const int pi = base + lane;
-        const bool v = pi < hi;
-        int e = v ? p.ids[pi] : -1;
-        if (v && (e < 0 || e >= E)) { atomicOr(&g_error, ERR_BAD_EXPERT); e = 0; }
+        int e = pi < hi ? p.ids[pi] : -1;
+        if (e >= E) { atomicOr(&g_error, ERR_BAD_EXPERT); e = 0; }
+        const bool v = e >= 0;            // a negative id is an absent pair (expert-parallel partial routing)
         const unsigned act = __ballot_sync(0xffffffffu, v);
         const unsigned peers = __match_any_sync(0xffffffffu, e) & act;
         if (v && (peers & lt) == 0) wcnt[warp][e] += __popc(peers);
@@ -1111,9 +1111,9 @@ __global__ void __launch_bounds__(1024, 1) pf_dispatch_kernel(PfDispatchParams p
     __syncthreads();
     for (int base = lo; base < hi; base += 32) {
         const int pi = base + lane;
-        const bool v = pi < hi;
-        int e = v ? p.ids[pi] : -1;
-        if (v && (e < 0 || e >= E)) e = 0;
+        int e = pi < hi ? p.ids[pi] : -1;
+        if (e >= E) e = 0;
+        const bool v = e >= 0;
         const unsigned act = __ballot_sync(0xffffffffu, v);
         const unsigned peers = __match_any_sync(0xffffffffu, e) & act;
         const int b0 = v ? wcnt[warp][e] : 0;
@@ -1123,6 +1123,8 @@ __global__ void __launch_bounds__(1024, 1) pf_dispatch_kernel(PfDispatchParams p
             p.perm[at] = pi;
             p.pos[pi] = cls[e] >= 0 ? at : -1;
             if ((peers & lt) == 0) wcnt[warp][e] = b0 + __popc(peers);
+        } else if (pi < hi) {
+            p.pos[pi] = -1;
         }
         __syncwarp();
     }

@@ -150,6 +150,38 @@ class MoELayer:
 
     __call__ = forward
 
+    def route(self, x: torch.Tensor, stream: torch.cuda.Stream | None = None):
+        """Router logits, top-k ids and normalised weights of x (moeb_layer_route)."""
+        assert x.dtype == torch.float32 and x.is_contiguous() and x.device == self.device
+        T, h = x.shape[0], self.host
+        logits = torch.empty((T, h.n_expert), dtype=torch.float32, device=self.device)
+        ids = torch.empty((T, h.top_k), dtype=torch.int32, device=self.device)
+        w = torch.empty((T, h.top_k), dtype=torch.float32, device=self.device)
+        s = stream if stream is not None else torch.cuda.current_stream(self.device)
+        capi.check(capi.lib().moeb_layer_route(C.byref(self.c), x.data_ptr(), T, logits.data_ptr(), ids.data_ptr(),
+                                               w.data_ptr(), s.cuda_stream))
+        return logits, ids, w
+
+    def forward_routed(self, x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None,
+                       stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+        """The expert half on given routing (moeb_layer_forward_routed): ids [n, k] i32 with -1 for
+        experts held elsewhere, w [n, k] f32."""
+        assert x.dtype == torch.float32 and x.is_contiguous() and x.device == self.device
+        assert ids.dtype == torch.int32 and w.dtype == torch.float32 and ids.is_contiguous() and w.is_contiguous()
+        n = x.shape[0]
+        if out is None:
+            out = torch.empty_like(x)
+        if n == 0:
+            return out
+        need = int(capi.lib().moeb_routed_workspace_size(C.byref(self.c), n))
+        if self._ws is None or self._ws.numel() < need:
+            self._ws = torch.empty(need, dtype=torch.uint8, device=self.device)
+        s = stream if stream is not None else torch.cuda.current_stream(self.device)
+        capi.check(capi.lib().moeb_layer_forward_routed(C.byref(self.c), x.data_ptr(), n, ids.data_ptr(), w.data_ptr(),
+                                                        out.data_ptr(), self._ws.data_ptr(), self._ws.numel(),
+                                                        s.cuda_stream))
+        return out
+
     def device_error(self) -> int:
         s = torch.cuda.current_stream(self.device)
         return int(capi.lib().moeb_device_error(s.cuda_stream))
