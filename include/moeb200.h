@@ -106,13 +106,16 @@ int moeb_layer_forward(const moeb_layer *L, const float *x, int32_t n_tokens, fl
 /* The two halves of the layer, for expert-parallel hosts (new; the reference runs the router and
  * the expert matmuls as separate graph nodes, llama-graph.cpp:1530-1613 and :1689-1848).
  *  moeb_layer_route: router logits (f32 [n_tokens][n_expert], caller memory), top-k ids
- *    (i32 [n_tokens][top_k]) and normalised weights (f32 [n_tokens][top_k]).
+ *    (i32 [n_tokens][top_k]) and normalised weights (f32 [n_tokens][top_k]). With a workspace of
+ *    moeb_route_workspace_size bytes the logits GEMM splits K four ways (more CTAs for the same
+ *    tokens, partial sums added in order); with workspace NULL it runs in one part.
  *  moeb_layer_forward_routed: the expert half for rows whose routing is given: out[r] =
  *    sum_j weights[r][j] * down(GeGLU(gate_up(x[r]))) over the slots j with ids[r][j] >= 0, in
  *    slot order; negative ids mark experts that live elsewhere. Runs the prefill kernels for any
  *    n_rows >= 1 (the layer needs the prefill shapes); workspace from moeb_routed_workspace_size. */
 int    moeb_layer_route(const moeb_layer *L, const float *x, int32_t n_tokens, float *logits, int32_t *ids,
-                        float *weights, void *stream);
+                        float *weights, void *workspace, size_t workspace_bytes, void *stream);
+size_t moeb_route_workspace_size(const moeb_layer *L, int32_t n_tokens);
 size_t moeb_routed_workspace_size(const moeb_layer *L, int32_t n_rows);
 int    moeb_layer_forward_routed(const moeb_layer *L, const float *x, int32_t n_rows, const int32_t *ids,
                                  const float *weights, float *out, void *workspace, size_t workspace_bytes,

@@ -162,7 +162,7 @@ LayerWs carve(const moeb_layer *L, int T, uint8_t *base) {
 
 // prefill path workspace (whole call at once)
 struct PrefillWs {
-    float *logits, *w, *xd, *ad, *y;
+    float *logits, *rpart, *w, *xd, *ad, *y;
     int32_t *ids, *cnt, *off, *perm, *pos, *n_tiles;
     PfTile *tiles;
     int8_t *xq8;
@@ -179,6 +179,7 @@ PrefillWs carve_prefill(const moeb_layer *L, int T, uint8_t *base) {
     size_t o = 0;
     auto take = [&](size_t n) { size_t at = o; o = align_up(o + n, 256); return base ? base + at : nullptr; };
     w.logits = (float *)take(sizeof(float) * T * E);
+    w.rpart = (float *)take(sizeof(float) * 4 * T * E);
     w.ids = (int32_t *)take(sizeof(int32_t) * P);
     w.w = (float *)take(sizeof(float) * P);
     w.cnt = (int32_t *)take(sizeof(int32_t) * E);
@@ -316,7 +317,7 @@ static int forward_prefill(const moeb_layer *L, const float *x, int32_t T, float
     a.cold_gu = pool_view(L->cold, true);
     a.hot_dn = pool_view(L->hot, false);
     a.cold_dn = pool_view(L->cold, false);
-    a.logits = w.logits; a.ids = w.ids; a.w = w.w;
+    a.logits = w.logits; a.rpart = w.rpart; a.ids = w.ids; a.w = w.w;
     a.cnt = w.cnt; a.off = w.off; a.perm = w.perm; a.pos = w.pos;
     a.tiles = w.tiles; a.n_tiles = w.n_tiles;
     a.xq8 = w.xq8; a.xd = w.xd; a.xbs = w.xbs;
@@ -345,8 +346,13 @@ static int forward_prefill(const moeb_layer *L, const float *x, int32_t T, float
     return MOEB_OK;
 }
 
+extern "C" size_t moeb_route_workspace_size(const moeb_layer *L, int32_t n_tokens) {
+    if (!L || n_tokens <= 0) return 0;
+    return sizeof(float) * 4 * (size_t)n_tokens * L->n_expert;
+}
+
 extern "C" int moeb_layer_route(const moeb_layer *L, const float *x, int32_t n_tokens, float *logits, int32_t *ids,
-                                float *weights, void *stream) {
+                                float *weights, void *workspace, size_t workspace_bytes, void *stream) {
     int rc = check_layer(L);
     if (rc) return rc;
     if (n_tokens < 0) return fail(MOEB_EINVAL, "n_tokens %d < 0", n_tokens);
@@ -355,8 +361,16 @@ extern "C" int moeb_layer_route(const moeb_layer *L, const float *x, int32_t n_t
     if (!aligned16(x) || !aligned16(L->w_router)) return fail(MOEB_EINVAL, "x and router weights must be 16-byte aligned");
     rc = ensure_device();
     if (rc) return rc;
-    cudaError_t e = launch_route(L->w_router, L->b_router, x, n_tokens, L->n_expert, L->d_model, L->top_k, logits, ids,
-                                 weights, (cudaStream_t)stream);
+    float *part = nullptr;
+    if (workspace) {
+        if (workspace_bytes < moeb_route_workspace_size(L, n_tokens) || !aligned16(workspace))
+            return fail(MOEB_ESPACE, "moeb_layer_route: workspace of %zu bytes (16-byte aligned) < %zu", workspace_bytes,
+                        moeb_route_workspace_size(L, n_tokens));
+        if (L->d_model % 128) return fail(MOEB_EINVAL, "moeb_layer_route: a split router needs d_model %% 128 == 0");
+        part = (float *)workspace;
+    }
+    cudaError_t e = launch_route(L->w_router, L->b_router, x, n_tokens, L->n_expert, L->d_model, L->top_k, part, logits,
+                                 ids, weights, (cudaStream_t)stream);
     if (e != cudaSuccess) return cuda_fail(e, "route launch");
     return MOEB_OK;
 }

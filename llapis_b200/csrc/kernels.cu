@@ -1720,21 +1720,22 @@ cudaError_t launch_prefill(const PrefillArgs &a, cudaStream_t s, int n_sms) {
     if ((e = prof_mark(s, mark++)) != cudaSuccess) return e;
     if (!a.routed) {
         {
-            const float *W = a.w_router, *b = a.b_router, *x = a.x;
-            float *lg = a.logits;
-            int t = T, ne = E, dd = d;
-            void *args[] = {&W, &b, &x, &lg, &t, &ne, &dd};
-            e = pf_launch("pf_router_kernel", (const void *)pf_router_kernel, dim3((T + kRtTok - 1) / kRtTok, (E + kRtExp - 1) / kRtExp),
-                          dim3(256), 0, s, true, args);
+            const float *W = a.w_router, *x = a.x;
+            float *part = a.rpart;
+            int t = T, ne = E, dd = d, ns = kRtSplit;
+            void *args[] = {&W, &x, &part, &t, &ne, &dd, &ns};
+            e = pf_launch("pf_router_kernel", (const void *)pf_router_kernel,
+                          dim3((T + kRtTok - 1) / kRtTok, kRtSplit, (E + kRtExp - 1) / kRtExp), dim3(256), 0, s, true, args);
             if (e != cudaSuccess) return e;
             if ((e = prof_mark(s, mark++)) != cudaSuccess) return e;
         }
         {
-            const float *lg = a.logits;
+            const float *part = a.rpart, *b = a.b_router;
+            float *lg = a.logits;
             int32_t *ids = a.ids;
             float *w = a.w;
-            int t = T, ne = E, kk = k;
-            void *args[] = {&lg, &ids, &w, &t, &ne, &kk};
+            int t = T, ne = E, kk = k, ns = kRtSplit;
+            void *args[] = {&part, &b, &lg, &ids, &w, &t, &ne, &kk, &ns};
             e = pf_launch("pf_topk_kernel", (const void *)pf_topk_kernel, dim3((T + 7) / 8), dim3(256), 0, s, true, args);
             if (e != cudaSuccess) return e;
             if ((e = prof_mark(s, mark++)) != cudaSuccess) return e;
@@ -1806,14 +1807,17 @@ cudaError_t launch_prefill(const PrefillArgs &a, cudaStream_t s, int n_sms) {
 }
 
 cudaError_t launch_route(const float *w_router, const float *b_router, const float *x, int T, int E, int d, int k,
-                         float *logits, int32_t *ids, float *w, cudaStream_t s) {
-    int t = T, ne = E, dd = d, kk = k;
-    const float *lgc = logits;
-    void *a1[] = {&w_router, &b_router, &x, &logits, &t, &ne, &dd};
+                         float *part, float *logits, int32_t *ids, float *w, cudaStream_t s) {
+    // with `part` the K split is four-way into it; without, one part straight into the logits
+    // buffer, which the top-k kernel completes in place (bias)
+    int t = T, ne = E, dd = d, kk = k, ns = part ? kRtSplit : 1;
+    float *dst = part ? part : logits;
+    void *a1[] = {&w_router, &x, &dst, &t, &ne, &dd, &ns};
     cudaError_t e = pf_launch("pf_router_kernel", (const void *)pf_router_kernel,
-                              dim3((T + kRtTok - 1) / kRtTok, (E + kRtExp - 1) / kRtExp), dim3(256), 0, s, true, a1);
+                              dim3((T + kRtTok - 1) / kRtTok, ns, (E + kRtExp - 1) / kRtExp), dim3(256), 0, s, true, a1);
     if (e != cudaSuccess) return e;
-    void *a2[] = {&lgc, &ids, &w, &t, &ne, &kk};
+    const float *pc = dst;
+    void *a2[] = {&pc, &b_router, &logits, &ids, &w, &t, &ne, &kk, &ns};
     return pf_launch("pf_topk_kernel", (const void *)pf_topk_kernel, dim3((T + 7) / 8), dim3(256), 0, s, true, a2);
 }
 

@@ -138,6 +138,7 @@ struct PrefillArgs {
     Residency res;
     PoolView hot_gu, cold_gu, hot_dn, cold_dn;
     float *logits;              // [T][E]
+    float *rpart;               // [4][T][E] router partial sums (the four K quarters)
     int32_t *ids;               // [T][k]
     float *w;                   // [T][k]
     int32_t *cnt, *off;         // [E], [E + 1]
@@ -160,7 +161,7 @@ struct PrefillArgs {
 };
 // router logits + softmax/top-k/weights only (the first two prefill kernels)
 cudaError_t launch_route(const float *w_router, const float *b_router, const float *x, int T, int E, int d, int k,
-                         float *logits, int32_t *ids, float *w, cudaStream_t s);
+                         float *part, float *logits, int32_t *ids, float *w, cudaStream_t s);
 cudaError_t launch_prefill(const PrefillArgs &a, cudaStream_t s, int n_sms);
 // router, top-k, dispatch, activation quantisation, gather, gate_up, GeGLU, down, combine
 constexpr int kPrefillKernels = 9;

@@ -911,62 +911,90 @@ __global__ void __launch_bounds__(256) pf_gather_kernel(PfParams p) {
 }
 
 // ---------------------------------------------------------------- router, routing, dispatch, act quant
-constexpr int kRtTok = 16, kRtExp = 128, kRtK = 32;
-
-// logits[t][e] = sum_k W[e][k] x[t][k] (+ b[e]); CTA: 16 tokens x 128 experts, 256 threads of
-// 4 experts x 2 tokens each; one fp32 accumulator per output, k ascending.
-__global__ void __launch_bounds__(256) pf_router_kernel(const float *W, const float *bias, const float *x, float *logits,
-                                                        int T, int E, int d) {
-    __shared__ __align__(16) float ws[kRtK][kRtExp + 4];
-    __shared__ __align__(16) float xs[kRtK][kRtTok + 4];
+// Router logits, f32 SIMT GEMM (no tensor cores: the logits decide the routing, so they keep f32
+// products; the reference's ggml mul_mat is f32 too). CTA: 64 tokens x 128 experts x one quarter
+// of K, 256 threads of 8 experts x 4 tokens; K in chunks of 32 staged k-major in shared memory,
+// the next chunk prefetched into registers. The nsplit K parts land in part[nsplit][T][E] and
+// the top-k kernel adds them in order (deterministic); with nsplit = 1, part may be the logits
+// buffer itself (the top-k kernel completes it in place).
+constexpr int kRtTok = 64, kRtExp = 128, kRtK = 32, kRtSplit = 4;
+__global__ void __launch_bounds__(256) pf_router_kernel(const float *W, const float *x, float *part, int T, int E,
+                                                        int d, int nsplit) {
+    __shared__ __align__(16) float ws[kRtK][kRtExp];
+    __shared__ __align__(16) float xs[kRtK][kRtTok];
     pdl_wait();
     pdl_launch_dependents();
-    const int t0 = blockIdx.x * kRtTok, e0 = blockIdx.y * kRtExp, tid = threadIdx.x;
-    const int eg = tid & 31, tg = tid >> 5;
-    float acc[4][2];
+    const int t0 = blockIdx.x * kRtTok, e0 = blockIdx.z * kRtExp, split = blockIdx.y, tid = threadIdx.x;
+    const int kq = d / nsplit, kbeg = split * kq, nch = kq / kRtK;
+    const int eg = tid & 15, tg = tid >> 4;           // experts 8eg..8eg+7, tokens 4tg..4tg+3
+    float acc[8][4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) acc[i][0] = acc[i][1] = 0.f;
-    for (int k0 = 0; k0 < d; k0 += kRtK) {
+    for (int i = 0; i < 8; ++i)
 #pragma unroll
-        for (int i = 0; i < (kRtExp * kRtK / 4) / 256; ++i) {
-            const int idx = tid + 256 * i, e = idx >> 3, f = idx & 7;
-            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (e0 + e < E) v = *reinterpret_cast<const float4 *>(W + (size_t)(e0 + e) * d + k0 + 4 * f);
-            ws[4 * f][e] = v.x; ws[4 * f + 1][e] = v.y; ws[4 * f + 2][e] = v.z; ws[4 * f + 3][e] = v.w;
+        for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+    // global -> register staging: W rows (e fastest across threads) and x rows
+    float4 wr[4], xr[2];
+    auto load = [&](int k0) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int idx = tid + 256 * i, e = idx & 127, qd = idx >> 7;
+            wr[i] = e0 + e < E ? __ldg(reinterpret_cast<const float4 *>(W + (size_t)(e0 + e) * d + k0 + 4 * qd))
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
         }
-        if (tid < kRtTok * kRtK / 4) {
-            const int t = tid >> 3, f = tid & 7;
-            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (t0 + t < T) v = *reinterpret_cast<const float4 *>(x + (size_t)(t0 + t) * d + k0 + 4 * f);
-            xs[4 * f][t] = v.x; xs[4 * f + 1][t] = v.y; xs[4 * f + 2][t] = v.z; xs[4 * f + 3][t] = v.w;
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const int idx = tid + 256 * i, t = idx & 63, qd = idx >> 6;
+            xr[i] = t0 + t < T ? __ldg(reinterpret_cast<const float4 *>(x + (size_t)(t0 + t) * d + k0 + 4 * qd))
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
         }
+    };
+    auto store = [&]() {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int idx = tid + 256 * i, e = idx & 127, qd = idx >> 7;
+            ws[4 * qd][e] = wr[i].x; ws[4 * qd + 1][e] = wr[i].y; ws[4 * qd + 2][e] = wr[i].z; ws[4 * qd + 3][e] = wr[i].w;
+        }
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const int idx = tid + 256 * i, t = idx & 63, qd = idx >> 6;
+            xs[4 * qd][t] = xr[i].x; xs[4 * qd + 1][t] = xr[i].y; xs[4 * qd + 2][t] = xr[i].z; xs[4 * qd + 3][t] = xr[i].w;
+        }
+    };
+    load(kbeg);
+    for (int c = 0; c < nch; ++c) {
+        store();
         __syncthreads();
+        if (c + 1 < nch) load(kbeg + (c + 1) * kRtK);
 #pragma unroll 8
         for (int kk = 0; kk < kRtK; ++kk) {
-            const float4 wv = *reinterpret_cast<const float4 *>(&ws[kk][4 * eg]);
-            const float2 xv = *reinterpret_cast<const float2 *>(&xs[kk][2 * tg]);
-            acc[0][0] = fmaf(wv.x, xv.x, acc[0][0]); acc[0][1] = fmaf(wv.x, xv.y, acc[0][1]);
-            acc[1][0] = fmaf(wv.y, xv.x, acc[1][0]); acc[1][1] = fmaf(wv.y, xv.y, acc[1][1]);
-            acc[2][0] = fmaf(wv.z, xv.x, acc[2][0]); acc[2][1] = fmaf(wv.z, xv.y, acc[2][1]);
-            acc[3][0] = fmaf(wv.w, xv.x, acc[3][0]); acc[3][1] = fmaf(wv.w, xv.y, acc[3][1]);
+            const float4 wa = *reinterpret_cast<const float4 *>(&ws[kk][8 * eg]);
+            const float4 wb = *reinterpret_cast<const float4 *>(&ws[kk][8 * eg + 4]);
+            const float4 xv = *reinterpret_cast<const float4 *>(&xs[kk][4 * tg]);
+            const float wv[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+            const float xx[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(wv[i], xx[j], acc[i][j]);
         }
         __syncthreads();
     }
+    float *pp = part + (size_t)split * T * E;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const int e = e0 + 4 * eg + i;
-        if (e >= E) continue;
+    for (int j = 0; j < 4; ++j) {
+        const int t = t0 + 4 * tg + j;
+        if (t >= T) continue;
 #pragma unroll
-        for (int j = 0; j < 2; ++j) {
-            const int t = t0 + 2 * tg + j;
-            if (t < T) logits[(size_t)t * E + e] = bias ? __fadd_rn(acc[i][j], bias[e]) : acc[i][j];
+        for (int i = 0; i < 8; ++i) {
+            const int e = e0 + 8 * eg + i;
+            if (e < E) pp[(size_t)t * E + e] = acc[i][j];
         }
     }
 }
 
 // softmax -> top-k -> normalised weights, one warp per token (same arithmetic as route_tokens)
-__global__ void __launch_bounds__(256) pf_topk_kernel(const float *logits, int32_t *ids, float *wts, int T, int E,
-                                                      int k) {
+__global__ void __launch_bounds__(256) pf_topk_kernel(const float *part, const float *bias, float *logits, int32_t *ids,
+                                                      float *wts, int T, int E, int k, int nsplit) {
     pdl_wait();
     pdl_launch_dependents();
     const int lane = threadIdx.x & 31;
@@ -975,7 +1003,19 @@ __global__ void __launch_bounds__(256) pf_topk_kernel(const float *logits, int32
     const int per = E / 32;
     float v[kMaxE / 32];
 #pragma unroll
-    for (int i = 0; i < kMaxE / 32; ++i) v[i] = i < per ? logits[(size_t)t * E + lane + 32 * i] : -INFINITY;
+    for (int i = 0; i < kMaxE / 32; ++i) {
+        v[i] = -INFINITY;
+        if (i < per) {
+            // the router's K quarters added in order, then the bias (ggml_add after the mul_mat)
+            const size_t o = (size_t)t * E + lane + 32 * i;
+            float l = part[o];
+#pragma unroll
+            for (int sp = 1; sp < nsplit; ++sp) l = __fadd_rn(l, part[(size_t)sp * T * E + o]);
+            if (bias) l = __fadd_rn(l, bias[lane + 32 * i]);
+            logits[o] = l;
+            v[i] = l;
+        }
+    }
     float mx = -INFINITY;
 #pragma unroll
     for (int i = 0; i < kMaxE / 32; ++i) mx = fmaxf(mx, v[i]);

@@ -105,6 +105,7 @@ class MoELayer:
         L.exp_slot, L.slot_exp, L.slot_state = _ptr(t["exp_slot"]), _ptr(t["slot_exp"]), _ptr(t["slot_state"])
         self.c = L
         self._ws = None
+        self._rws = None
 
     def prefill_path(self, n_tokens: int) -> bool:
         """Whether moeb_layer_forward runs n_tokens on the prefill (tensor-core GEMM) path."""
@@ -158,8 +159,12 @@ class MoELayer:
         ids = torch.empty((T, h.top_k), dtype=torch.int32, device=self.device)
         w = torch.empty((T, h.top_k), dtype=torch.float32, device=self.device)
         s = stream if stream is not None else torch.cuda.current_stream(self.device)
-        capi.check(capi.lib().moeb_layer_route(C.byref(self.c), x.data_ptr(), T, logits.data_ptr(), ids.data_ptr(),
-                                               w.data_ptr(), s.cuda_stream))
+        lib = capi.lib()
+        need = int(lib.moeb_route_workspace_size(C.byref(self.c), T))
+        if self._rws is None or self._rws.numel() < need:
+            self._rws = torch.empty(need, dtype=torch.uint8, device=self.device)
+        capi.check(lib.moeb_layer_route(C.byref(self.c), x.data_ptr(), T, logits.data_ptr(), ids.data_ptr(),
+                                        w.data_ptr(), self._rws.data_ptr(), self._rws.numel(), s.cuda_stream))
         return logits, ids, w
 
     def forward_routed(self, x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None,

@@ -29,11 +29,10 @@ def test_routed_halves_sum_to_full():
     b = layer.forward_routed(x, torch.where(~odd, ids, -1).contiguous(), w).clone()
     ref = full.cpu().numpy()
     assert_layer_close((a + b).cpu().numpy(), ref, tol=1e-5)
+    # the whole-layer forward routes with the router's K split in four parts (summed in order),
+    # moeb_layer_route in one: logits agree to f32 rounding, outputs to far below the parity bar
     layer_out = layer(x).cpu().numpy()
-    if layer.prefill_path(200):
-        assert np.array_equal(layer_out, ref)   # same kernels, same routing
-    else:
-        assert_layer_close(layer_out, ref, tol=5e-4)
+    assert_layer_close(layer_out, ref, tol=5e-5 if layer.prefill_path(200) else 5e-4)
     none = layer.forward_routed(x, torch.full_like(ids, -1), w)
     assert torch.count_nonzero(none).item() == 0
 
@@ -51,9 +50,6 @@ def test_ep_world1_matches_layer():
         x = torch.from_numpy(workload.make_input(workload.CONFIGS["mini_mixed"], n_tokens=300, stream=8)).cuda()
         out = EPMoE.from_layer(layer)(x)
         want = layer(x)
-        if layer.prefill_path(300):
-            assert torch.equal(out, want)
-        else:
-            assert_layer_close(out.cpu().numpy(), want.cpu().numpy(), tol=5e-4)
+        assert_layer_close(out.cpu().numpy(), want.cpu().numpy(), tol=5e-5 if layer.prefill_path(300) else 5e-4)
     finally:
         dist.destroy_process_group()
