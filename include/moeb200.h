@@ -151,7 +151,7 @@ int moeb_prefill_profile_read(float *ms, int32_t n);
  * Limits and rules:
  *  - it always runs the decode path (chunks of 8 tokens), whose workspace is one chunk's worth
  *    for any n_tokens; a layer whose chunk workspace exceeds MOEB_STATIC_SCRATCH_BYTES is
- *    rejected with MOEB_ESPACE (the Gemma-4 26B-A4B layer needs about 1.1 MB);
+ *    rejected with MOEB_ESPACE (the Gemma-4 26B-A4B layer needs about 2.2 MB);
  *  - the first call on a device does one-time set-up there (format tables, the device address of
  *    the static array); make that first call before any stream capture on that device;
  *  - all calls share the one array per device and it keeps the last call's contents: calls that

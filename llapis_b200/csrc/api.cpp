@@ -148,7 +148,7 @@ LayerWs carve(const moeb_layer *L, int T, uint8_t *base) {
     auto take = [&](size_t n) { size_t at = o; o = align_up(o + n, 256); return base ? base + at : nullptr; };
     w.logits = (float *)take(sizeof(float) * T * L->n_expert);
     w.xq = take((size_t)T * xq_stride_bytes(L->d_model));
-    w.h = (float *)take(sizeof(float) * P * 2 * L->n_ff);
+    w.h = (float *)take(sizeof(float) * 4 * P * 2 * L->n_ff);   // four partial-sum parts
     w.y = (float *)take(sizeof(float) * P * L->d_model);
     w.ids = (int32_t *)take(sizeof(int32_t) * P);
     w.w = (float *)take(sizeof(float) * P);
@@ -482,13 +482,18 @@ static int forward_chunks(const moeb_layer *L, const float *x, int32_t n_tokens,
                 {aux->logits ? aux->logits + (size_t)t0 * E : nullptr, w.logits, sizeof(float) * T * E},
                 {aux->ids ? aux->ids + (size_t)t0 * k : nullptr, w.ids, sizeof(int32_t) * P},
                 {aux->weights ? aux->weights + (size_t)t0 * k : nullptr, w.w, sizeof(float) * P},
-                {aux->gate_up ? aux->gate_up + (size_t)t0 * k * 2 * L->n_ff : nullptr, w.h, sizeof(float) * P * 2 * L->n_ff},
+
                 {aux->down ? aux->down + (size_t)t0 * k * d : nullptr, w.y, sizeof(float) * P * d},
             };
             for (auto &c : cps) {
                 if (!c.dst) continue;
                 e = cudaMemcpyAsync(c.dst, c.src, c.n, cudaMemcpyDeviceToDevice, s);
                 if (e != cudaSuccess) return cuda_fail(e, "aux copy");
+            }
+            if (aux->gate_up) {
+                const size_t n = (size_t)P * 2 * L->n_ff;
+                e = launch_sum4(w.h, n, aux->gate_up + (size_t)t0 * k * 2 * L->n_ff, n, s);
+                if (e != cudaSuccess) return cuda_fail(e, "aux gate_up");
             }
             // the dispatch outputs describe one chunk; they are reported for single-chunk calls
             if (n_tokens <= kFusedTokens) {

@@ -349,6 +349,108 @@ __device__ __forceinline__ void q4k_lane(const uint8_t *row, int nsb, int j, con
     }
 }
 
+// ---------------------------------------------------------------- warp-level int8 MMA helpers
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &d0, uint32_t &d1, uint32_t &d2, uint32_t &d3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(d0), "=r"(d1), "=r"(d2), "=r"(d3)
+                 : "r"(addr)
+                 : "memory");
+}
+__device__ __forceinline__ void ldsm_x2(uint32_t addr, uint32_t &d0, uint32_t &d1) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];" : "=r"(d0), "=r"(d1) : "r"(addr) : "memory");
+}
+// D = A (16x32 s8, row) * B (32x8 s8, col), exact int32
+__device__ __forceinline__ void mma_s8_k32(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                           uint32_t b1) {
+    d[0] = d[1] = d[2] = d[3] = 0;
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void mma_s8_k16(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
+    d[0] = d[1] = d[2] = d[3] = 0;
+    asm("mma.sync.aligned.m16n8k16.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(b0));
+}
+__device__ __forceinline__ int sbyte(uint32_t w, int i) { return (int)((w >> (8 * i)) & 0xffu); }
+__device__ __forceinline__ uint32_t pack_s8x4(int a, int b, int c, int d) {
+    return (uint32_t)(a & 0xff) | ((uint32_t)(b & 0xff) << 8) | ((uint32_t)(c & 0xff) << 16) | ((uint32_t)(d & 0xff) << 24);
+}
+
+// One 16-row x (up to 8) column tile of a Q4_K gate_up stage against the Q8_K activation rows of
+// its pairs, over super-blocks sb0, sb0 + 4, ... (the four warps of a group split a stage's
+// super-blocks). Integer work of ggml_vec_dot_q4_K_q8_K (x86/quants.c:1900) on warp-level int8
+// MMAs: per sub-block j an m16n8k32 gives sum_i q_i * q8_i exactly, scaled by the 6-bit sc_j in
+// int32; the min term sum_j m_j * bsum_j runs as two m16n8k16 (bsum = 64 hi + lo); d_w * d_x and
+// dmin_w * d_x per super-block in f32. Lane (g, c) owns rows g, g + 8 and columns 2c, 2c + 1.
+// stage/_s: the stage's rows (generic / shared address); tok[col]: activation row of each column.
+__device__ __forceinline__ void q4k_tile_mma(const uint8_t *stage, uint32_t stage_s, int rb, int sb0, int nsb,
+                                             const uint8_t *xact, uint32_t xact_s, int xs, const int (&tok)[8], int n,
+                                             float (&out)[4]) {
+    const int lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
+    const int am = lane >> 3;   // ldmatrix.x4 matrix this lane addresses: rows +8 for odd, bytes +16 for 2, 3
+    const uint32_t a_row = stage_s + (uint32_t)(((lane & 7) + 8 * (am & 1)) * rb + 16 * (am >> 1) + 16);
+    const uint32_t b_row = xact_s + (uint32_t)(tok[lane & 7] * xs + 16 * ((lane >> 3) & 1));
+    const bool colv = g < n;
+    const uint8_t *r0 = stage + (size_t)g * rb, *r1 = stage + (size_t)(g + 8) * rb;
+    const uint8_t *xg = xact + (size_t)tok[g] * xs;
+    const float *dxa = reinterpret_cast<const float *>(xact + (size_t)tok[2 * c] * xs + nsb * 256);
+    const float *dxb = reinterpret_cast<const float *>(xact + (size_t)tok[2 * c + 1] * xs + nsb * 256);
+    const int16_t *bsg = reinterpret_cast<const int16_t *>(xg + nsb * 256 + nsb * 4);
+    const uint32_t M = 0x0f0f0f0fu;
+#pragma unroll 1
+    for (int sb = sb0; sb < nsb; sb += 4) {
+        const uint4 h0 = *reinterpret_cast<const uint4 *>(r0 + sb * B_Q4_K);
+        const uint4 h1 = *reinterpret_cast<const uint4 *>(r1 + sb * B_Q4_K);
+        // 6-bit scales / mins of sub-blocks 0-3 and 4-7, four per word (get_scale_min_k4, ggml-quants.c:822)
+        const uint32_t s0l = h0.y & 0x3f3f3f3fu, s0h = (h0.w & M) | ((h0.y >> 2) & 0x30303030u);
+        const uint32_t m0l = h0.z & 0x3f3f3f3fu, m0h = ((h0.w >> 4) & M) | ((h0.z >> 2) & 0x30303030u);
+        const uint32_t s1l = h1.y & 0x3f3f3f3fu, s1h = (h1.w & M) | ((h1.y >> 2) & 0x30303030u);
+        const uint32_t m1l = h1.z & 0x3f3f3f3fu, m1h = ((h1.w >> 4) & M) | ((h1.z >> 2) & 0x30303030u);
+        int as[4] = {0, 0, 0, 0};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {   // 32-byte qs chunk i: sub-block 2i (low nibbles), 2i + 1 (high)
+            uint32_t w0, w1, w2, w3, b0l, b1l, b0h, b1h;
+            ldsm_x4(a_row + (uint32_t)(sb * B_Q4_K + 32 * i), w0, w1, w2, w3);
+            ldsm_x2(b_row + (uint32_t)(sb * 256 + 64 * i), b0l, b1l);
+            ldsm_x2(b_row + (uint32_t)(sb * 256 + 64 * i + 32), b0h, b1h);
+            if (!colv) b0l = b1l = b0h = b1h = 0u;
+            int dl[4], dh[4];
+            mma_s8_k32(dl, w0 & M, w1 & M, w2 & M, w3 & M, b0l, b1l);
+            mma_s8_k32(dh, (w0 >> 4) & M, (w1 >> 4) & M, (w2 >> 4) & M, (w3 >> 4) & M, b0h, b1h);
+            const int jl = 2 * i, jh = 2 * i + 1;
+            const int sl0 = sbyte(jl < 4 ? s0l : s0h, jl & 3), sh0 = sbyte(jh < 4 ? s0l : s0h, jh & 3);
+            const int sl1 = sbyte(jl < 4 ? s1l : s1h, jl & 3), sh1 = sbyte(jh < 4 ? s1l : s1h, jh & 3);
+            as[0] += sl0 * dl[0] + sh0 * dh[0];
+            as[1] += sl0 * dl[1] + sh0 * dh[1];
+            as[2] += sl1 * dl[2] + sh1 * dh[2];
+            as[3] += sl1 * dl[3] + sh1 * dh[3];
+        }
+        // min term: A = [m_0..7 | m_0..7] (rows g, g + 8), B = [bsum_j >> 6 | 0] and [0 | bsum_j & 63]
+        const uint32_t am0 = (c & 1) ? m0h : m0l, am1 = (c & 1) ? m1h : m1l;
+        const int16_t *bq = bsg + sb * 16 + 8 * (c & 1);
+        const uint32_t q01 = *reinterpret_cast<const uint32_t *>(bq), q23 = *reinterpret_cast<const uint32_t *>(bq + 2);
+        const uint32_t q45 = *reinterpret_cast<const uint32_t *>(bq + 4), q67 = *reinterpret_cast<const uint32_t *>(bq + 6);
+        const int p0 = (int)(int16_t)(q01 & 0xffffu) + (int)(int16_t)(q01 >> 16);
+        const int p1 = (int)(int16_t)(q23 & 0xffffu) + (int)(int16_t)(q23 >> 16);
+        const int p2 = (int)(int16_t)(q45 & 0xffffu) + (int)(int16_t)(q45 >> 16);
+        const int p3 = (int)(int16_t)(q67 & 0xffffu) + (int)(int16_t)(q67 >> 16);
+        uint32_t bw = c < 2 ? pack_s8x4(p0 >> 6, p1 >> 6, p2 >> 6, p3 >> 6) : pack_s8x4(p0 & 63, p1 & 63, p2 & 63, p3 & 63);
+        if (!colv) bw = 0u;
+        int d1[4], d2[4];
+        mma_s8_k16(d1, am0, am1, c < 2 ? bw : 0u);
+        mma_s8_k16(d2, am0, am1, c < 2 ? 0u : bw);
+        const float dw0 = h2f((uint16_t)(h0.x & 0xffffu)), dm0 = h2f((uint16_t)(h0.x >> 16));
+        const float dw1 = h2f((uint16_t)(h1.x & 0xffffu)), dm1 = h2f((uint16_t)(h1.x >> 16));
+        const float dxa_ = dxa[sb], dxb_ = dxb[sb];
+        out[0] = fmaf(dxa_, fmaf(-dm0, (float)(64 * d1[0] + d2[0]), dw0 * (float)as[0]), out[0]);
+        out[1] = fmaf(dxb_, fmaf(-dm0, (float)(64 * d1[1] + d2[1]), dw0 * (float)as[1]), out[1]);
+        out[2] = fmaf(dxa_, fmaf(-dm1, (float)(64 * d1[2] + d2[2]), dw1 * (float)as[2]), out[2]);
+        out[3] = fmaf(dxb_, fmaf(-dm1, (float)(64 * d1[3] + d2[3]), dw1 * (float)as[3]), out[3]);
+    }
+}
+
 // Q5_0 x Q8_0, lane = half of a row's 32-blocks: value = (nibble | hbit << 4) - 16, so
 // dot = sum(u * q) - 16 * sum(q); d_w * d_x per block.
 template <int NT>
@@ -1223,6 +1325,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) fused_decode_kernel(FusedPara
         // ================= consumers
         const int nsb = d / QK_K, nb = nff / QK32;
         const int xs = p.xq_stride, as = q80_stride(nff);
+        const size_t hpart = (size_t)T * k * 2 * nff;   // stride of the four gate_up partial-sum parts
         const int grp = warp / kWarpsPerGroup, wg = warp % kWarpsPerGroup;
         uint32_t kv[4];
 #pragma unroll
@@ -1254,7 +1357,26 @@ __global__ void __launch_bounds__(kGemvThreads, 1) fused_decode_kernel(FusedPara
             const int rb = (int)row_bytes(type, d);
             const int po = rs.off[e], n = rs.cnt[e];
             const int j = lane & 7, r = wg * 4 + (lane >> 3);
-            if (ok && wg * 4 < st.nrows) {
+            if (ok && type == T_Q4_K) {
+                // warp-level int8 MMAs: warp wg takes super-blocks wg, wg + 4, ... of all 16 rows and
+                // writes its partial sums to gate_up part wg (the GeGLU step adds the four in order)
+                int tok[8], pair[8];
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                    pair[c] = rs.perm[po + (c < n ? c : 0)];
+                    tok[c] = pair[c] / k;
+                }
+                float v[4] = {0.f, 0.f, 0.f, 0.f};
+                const uint8_t *stage = slots + slot * L.slot_cap;
+                q4k_tile_mma(stage, smem_addr(stage), rb, wg, nsb, xact, smem_addr(xact), xs, tok, n, v);
+                float *hp = p.h + (size_t)wg * hpart;
+                const int g = lane >> 2, cc = lane & 3;
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const int row = g + 8 * (q >> 1), col = 2 * cc + (q & 1);
+                    if (row < st.nrows && col < n) hp[(size_t)pair[col] * 2 * nff + st.row0 + row] = v[q];
+                }
+            } else if (ok && wg * 4 < st.nrows) {
                 const uint8_t *row = slots + slot * L.slot_cap + (size_t)r * rb;
                 for (int c0 = 0; c0 < n; c0 += kTokChunk) {
                     const int nt = min(kTokChunk, n - c0);
@@ -1274,7 +1396,13 @@ __global__ void __launch_bounds__(kGemvThreads, 1) fused_decode_kernel(FusedPara
                         s += __shfl_xor_sync(0xffffffffu, s, 1);
                         s += __shfl_xor_sync(0xffffffffu, s, 2);
                         s += __shfl_xor_sync(0xffffffffu, s, 4);
-                        if (j == 0 && c < nt) p.h[(size_t)pair[c] * 2 * nff + st.row0 + r] = s;
+                        if (j == 0 && c < nt) {
+                            float *hp = p.h + (size_t)pair[c] * 2 * nff + st.row0 + r;
+                            hp[0] = s;
+                            hp[hpart] = 0.f;   // rows not split over the four parts
+                            hp[2 * hpart] = 0.f;
+                            hp[3 * hpart] = 0.f;
+                        }
                     }
                 }
             }
@@ -1323,8 +1451,12 @@ __global__ void __launch_bounds__(kGemvThreads, 1) fused_decode_kernel(FusedPara
                     if (item < n_items) {
                         const int i = item / nb, b = item - i * nb;
                         const float *hp = p.h + (size_t)rs.perm[po + i] * 2 * nff + 32 * b + lane;
-                        g[q] = __ldcg(hp);
-                        v[q] = __ldcg(hp + nff);
+                        // gate_up partial sums of the four super-block quarters, added in order
+                        g[q] = __fadd_rn(__fadd_rn(__fadd_rn(__ldcg(hp), __ldcg(hp + hpart)), __ldcg(hp + 2 * hpart)),
+                                         __ldcg(hp + 3 * hpart));
+                        v[q] = __fadd_rn(__fadd_rn(__fadd_rn(__ldcg(hp + nff), __ldcg(hp + nff + hpart)),
+                                                   __ldcg(hp + nff + 2 * hpart)),
+                                         __ldcg(hp + nff + 3 * hpart));
                     }
                 }
 #pragma unroll
@@ -1819,6 +1951,16 @@ cudaError_t launch_route(const float *w_router, const float *b_router, const flo
     const float *pc = dst;
     void *a2[] = {&pc, &b_router, &logits, &ids, &w, &t, &ne, &kk, &ns};
     return pf_launch("pf_topk_kernel", (const void *)pf_topk_kernel, dim3((T + 7) / 8), dim3(256), 0, s, true, a2);
+}
+
+__global__ void sum4_kernel(const float *h, size_t stride, float *dst, size_t n) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) dst[i] = __fadd_rn(__fadd_rn(__fadd_rn(h[i], h[i + stride]), h[i + 2 * stride]), h[i + 3 * stride]);
+}
+
+cudaError_t launch_sum4(const float *h, size_t stride, float *dst, size_t n, cudaStream_t s) {
+    sum4_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(h, stride, dst, n);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_quant_q8k(const float *x, uint8_t *dst, int rows, int d, int stride, cudaStream_t s) {

@@ -108,7 +108,7 @@ struct FusedArgs {
     float *logits;
     uint8_t *xq;
     int32_t xq_stride;
-    float *h, *y, *out;
+    float *h, *y, *out;         // h: four [T*k][2 nff] partial-sum parts of gate_up
     int32_t *ids_out, *cnt_out, *off_out, *perm_out;
     float *w_out;
     uint32_t *sync;          // fused_sync_words(T, d) zero-initialised-by-the-kernel counters
@@ -177,6 +177,9 @@ cudaError_t launch_gemv(const GemvParams &p, cudaStream_t s, bool pdl, int n_sms
 cudaError_t launch_quant_q8k(const float *x, uint8_t *dst, int rows, int d, int stride, cudaStream_t s);
 size_t gemv_smem_bytes(int kind, int d_in, int T);
 cudaError_t launch_fused(const FusedArgs &a, cudaStream_t s, int n_sms);
+// dst[i] = ((h[i] + h[i + stride]) + h[i + 2 stride]) + h[i + 3 stride]: the fused kernel's gate_up
+// rows are four partial sums (super-block quarters); this adds them for the aux output
+cudaError_t launch_sum4(const float *h, size_t stride, float *dst, size_t n, cudaStream_t s);
 size_t fused_smem_bytes(int d, int nff);
 // standalone pieces behind the moeb_* inspection entry points
 cudaError_t launch_route_only(const RouteSrc &r, int32_t *ids, float *w, int32_t *cnt, int32_t *off, int32_t *perm,
