@@ -137,6 +137,7 @@ struct LayerWs {
     float *h, *y;
     int32_t *ids, *cnt, *off, *perm;
     float *w;
+    uint8_t *qa;
     uint32_t *sync;
     size_t bytes;
 };
@@ -155,7 +156,8 @@ LayerWs carve(const moeb_layer *L, int T, uint8_t *base) {
     w.cnt = (int32_t *)take(sizeof(int32_t) * L->n_expert);
     w.off = (int32_t *)take(sizeof(int32_t) * (L->n_expert + 1));
     w.perm = (int32_t *)take(sizeof(int32_t) * P);
-    w.sync = (uint32_t *)take(sizeof(uint32_t) * fused_sync_words(T, L->d_model));
+    w.qa = take((size_t)P * fused_qa_stride(L->n_ff));
+    w.sync = (uint32_t *)take(sizeof(uint32_t) * fused_sync_words(T, L->d_model, L->n_ff));
     w.bytes = o;
     return w;
 }
@@ -473,6 +475,7 @@ static int forward_chunks(const moeb_layer *L, const float *x, int32_t n_tokens,
         f.cnt_out = w.cnt;
         f.off_out = w.off;
         f.perm_out = w.perm;
+        f.qa = w.qa;
         f.sync = w.sync;
         cudaError_t e = launch_fused(f, s, n_sms);
         if (e != cudaSuccess) return cuda_fail(e, "fused decode layer launch");

@@ -384,19 +384,20 @@ __device__ __forceinline__ uint32_t pack_s8x4(int a, int b, int c, int d) {
 // MMAs: per sub-block j an m16n8k32 gives sum_i q_i * q8_i exactly, scaled by the 6-bit sc_j in
 // int32; the min term sum_j m_j * bsum_j runs as two m16n8k16 (bsum = 64 hi + lo); d_w * d_x and
 // dmin_w * d_x per super-block in f32. Lane (g, c) owns rows g, g + 8 and columns 2c, 2c + 1.
-// stage/_s: the stage's rows (generic / shared address); tok[col]: activation row of each column.
+// stage/_s: the stage's rows (generic / shared address); tok_*: the activation rows of columns
+// lane & 7, g, 2c and 2c + 1.
 __device__ __forceinline__ void q4k_tile_mma(const uint8_t *stage, uint32_t stage_s, int rb, int sb0, int nsb,
-                                             const uint8_t *xact, uint32_t xact_s, int xs, const int (&tok)[8], int n,
-                                             float (&out)[4]) {
+                                             const uint8_t *xact, uint32_t xact_s, int xs, int tok_l7, int tok_g,
+                                             int tok_a, int tok_b, int n, float (&out)[4]) {
     const int lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
     const int am = lane >> 3;   // ldmatrix.x4 matrix this lane addresses: rows +8 for odd, bytes +16 for 2, 3
     const uint32_t a_row = stage_s + (uint32_t)(((lane & 7) + 8 * (am & 1)) * rb + 16 * (am >> 1) + 16);
-    const uint32_t b_row = xact_s + (uint32_t)(tok[lane & 7] * xs + 16 * ((lane >> 3) & 1));
+    const uint32_t b_row = xact_s + (uint32_t)(tok_l7 * xs + 16 * ((lane >> 3) & 1));
     const bool colv = g < n;
     const uint8_t *r0 = stage + (size_t)g * rb, *r1 = stage + (size_t)(g + 8) * rb;
-    const uint8_t *xg = xact + (size_t)tok[g] * xs;
-    const float *dxa = reinterpret_cast<const float *>(xact + (size_t)tok[2 * c] * xs + nsb * 256);
-    const float *dxb = reinterpret_cast<const float *>(xact + (size_t)tok[2 * c + 1] * xs + nsb * 256);
+    const uint8_t *xg = xact + (size_t)tok_g * xs;
+    const float *dxa = reinterpret_cast<const float *>(xact + (size_t)tok_a * xs + nsb * 256);
+    const float *dxb = reinterpret_cast<const float *>(xact + (size_t)tok_b * xs + nsb * 256);
     const int16_t *bsg = reinterpret_cast<const int16_t *>(xg + nsb * 256 + nsb * 4);
     const uint32_t M = 0x0f0f0f0fu;
 #pragma unroll 1
@@ -625,6 +626,10 @@ __device__ __forceinline__ StagePlan stage_plan(int s, int g0, int g1, int gpe, 
 
 __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+// the four warps of consumer group g (named barriers 2 .. 5)
+__device__ __forceinline__ void group_sync(int g) {
+    asm volatile("bar.sync %0, %1;" ::"r"(2 + g), "r"(kWarpsPerGroup * 32) : "memory");
 }
 __device__ __forceinline__ void consumer_sync() {
     asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
@@ -920,12 +925,12 @@ constexpr uint32_t kGridWaitLimit = 1u << 24;   // x >= 32 ns sleeps: bounded we
 
 enum : int32_t { ERR_GRID_TIMEOUT = 8 };
 
-// Grid barrier state (per device, zero at load): arrivals of the current barrier and its
-// generation. The last arriver resets the count before it bumps the generation, so the next
-// barrier always starts from zero; launches of the fused kernel cannot overlap (each fills every
-// SM), so one pair serves all of them.
-__device__ unsigned int g_bar_count;
-__device__ unsigned int g_bar_gen;
+// Grid barrier word (per device, zero at load). Every CTA adds 1 to it except CTA 0, which adds
+// 2^31 - (G - 1): once all G CTAs have arrived the word has gained exactly 2^31, so its top bit has
+// flipped and its low 31 bits are back where they were (zero). No reset step is needed, and
+// consecutive barriers and launches reuse the word; a partial sum never flips the top bit. Launches
+// of the fused kernel cannot overlap (each fills every SM), so one word serves all of them.
+__device__ unsigned int g_bar_word;
 
 __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned *p) {
     unsigned v;
@@ -933,22 +938,18 @@ __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned *p) {
     return v;
 }
 
-// One thread per CTA: arrive, then wait (bounded) until every CTA of the grid has arrived.
-__device__ __noinline__ bool grid_barrier_thread(unsigned nblocks) {
-    const unsigned gen = ld_acquire_u32(&g_bar_gen);
+// One thread per CTA: arrive, then wait (bounded) until the top bit of the word differs from the
+// value this CTA saw at its own arrival.
+__device__ __forceinline__ bool grid_barrier_thread(unsigned nblocks) {
+    const unsigned add = blockIdx.x == 0 ? 0x80000000u - (nblocks - 1u) : 1u;
     __threadfence();
-    if (atomicAdd(&g_bar_count, 1u) == nblocks - 1) {
-        atomicExch(&g_bar_count, 0u);
-        __threadfence();
-        atomicAdd(&g_bar_gen, 1u);
-        return true;
-    }
+    const unsigned old = atomicAdd(&g_bar_word, add);
     for (uint32_t i = 0; i < kGridWaitLimit; ++i) {
-        if (ld_acquire_u32(&g_bar_gen) != gen) {
+        if ((ld_acquire_u32(&g_bar_word) ^ old) & 0x80000000u) {
             __threadfence();
             return true;
         }
-        if (i >= 256) __nanosleep(32);
+        if (i >= 64) __nanosleep(32);
     }
     atomicOr(&g_error, ERR_GRID_TIMEOUT);
     return false;
@@ -965,8 +966,10 @@ struct FusedParams {
     float *h, *y, *out;
     int32_t *ids_out, *cnt_out, *off_out, *perm_out;
     float *w_out;
-    // completion counters, zeroed in phase A: gate_up rows done per unique expert [kFusedMaxP],
-    // then down rows done per (token, 64-row block) [T][ceil(d / 64)]
+    uint8_t *qa;   // down activations (Q8_0 rows of n_ff) in expert-sorted slot order
+    // completion counters, zeroed in phase A: gate_up rows done per (unique expert, 32-row ff block)
+    // [kFusedMaxP][n_ff / 32], finished ff blocks per unique expert [kFusedMaxP], then down rows
+    // done per (token, 64-row block) [T][ceil(d / 64)]
     uint32_t *sync;
 };
 
@@ -980,8 +983,12 @@ struct FusedRoute {
     int32_t n_unique;
     int32_t uexp[kFusedMaxP], ucls[kFusedMaxP], uwidx[kFusedMaxP];
     uint32_t upre_gu[kFusedMaxP + 1], upre_dn[kFusedMaxP + 1];   // cumulative work units (see fused_dispatch)
+    int32_t scan_c[kMaxE / 32], scan_u[kMaxE / 32];
+    uint32_t scan_g[kMaxE / 32], scan_d[kMaxE / 32];
+    int32_t split[4];   // this CTA's gate_up groups [g0, g1) and down groups [h0, h1)
+    int32_t claim_gu, claim_dn;      // next unclaimed gate_up / down stage of this CTA
+    int32_t claim[kGroups][2];       // each group's current claim (double-buffered by iteration)
     float red[kFusedMaxT][kConsumerWarps + 1];
-    float rmax[kFusedMaxT], rinv[kFusedMaxT];
 };
 
 struct FusedSmem {
@@ -991,7 +998,7 @@ __host__ __device__ inline FusedSmem fused_layout(int d, int nff) {
     FusedSmem L;
     int o = 0;
     L.route = o; o += (int)((sizeof(FusedRoute) + 127) / 128 * 128);
-    L.bars = o;  o += (2 * kFSlots * 8 + 127) / 128 * 128;
+    L.bars = o;  o += ((2 * kFSlots + 1) * 8 + 127) / 128 * 128;
     L.grid = o;  o += MOE_IQ2S_GRID_ROWS * 8;
     L.xact = o;  o += kFusedMaxT * xq_stride_bytes(d);
     L.dact = o;  o += 2 * kFusedMaxT * q80_stride(nff);
@@ -1004,64 +1011,96 @@ __host__ __device__ inline FusedSmem fused_layout(int d, int nff) {
     return L;
 }
 
-// flat 8-row group of position `pos` in a cost prefix (16-byte units; every unique expert has gpe
-// groups of equal cost)
-__device__ __noinline__ int group_at_pre(const uint32_t *pre, int U, uint32_t pos, int gpe) {
-    if (pos >= pre[U]) return U * gpe;
-    int lo = 0, hi = U - 1;
-    while (lo < hi) {
-        const int mid = (lo + hi + 1) >> 1;
-        if (pre[mid] <= pos) lo = mid; else hi = mid - 1;
-    }
-    const uint32_t per = (pre[lo + 1] - pre[lo]) / (uint32_t)gpe;
-    return lo * gpe + (int)((pos - pre[lo]) / per);
+// Order key of a routing candidate: the float's bits mapped to an unsigned order (-0 folded into +0,
+// which compares equal to it), so the top-k's (value desc, index asc) becomes max key, then min index.
+__device__ __forceinline__ uint32_t route_key(float v) {
+    const uint32_t b = __float_as_uint(__fadd_rn(v, 0.f));
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
 }
 
-// Routing of the fused kernel: softmax, top-k and normalised weights for every token, from the
-// logits in global memory. The top-k is a parallel rank: thread (t, e) counts the experts that
-// beat e under (value desc, index asc); experts of rank < k land at slot `rank`.
-__device__ void fused_route(const FusedParams &p, FusedRoute &rs, float *lg, int tid) {
-    const int T = p.T, E = p.E, k = p.k, lane = tid & 31, warp = tid >> 5;
-    for (int i = tid; i < T * E; i += kGemvThreads) lg[i] = __ldcg(p.logits + i);
-    __syncthreads();
+// Routing of the fused kernel, one warp per token (llama-graph.cpp:1553-1648): softmax max and sum
+// over the token's logits, then k selection rounds (each a warp max over the lanes' best keys and a
+// warp min over the tied experts' ids, so ties go to the lowest id), then the selected
+// probabilities normalised by their slot-order sum.
+__device__ void fused_route(const FusedParams &p, FusedRoute &rs, int tid) {
+    const int T = p.T, E = p.E, k = p.k, lane = tid & 31, warp = tid >> 5, per = E / 32;
     for (int t = warp; t < T; t += kGemvThreads / 32) {
+        float v[kMaxE / 32];
+#pragma unroll
+        for (int i = 0; i < kMaxE / 32; ++i) v[i] = i < per ? __ldcg(p.logits + (size_t)t * E + lane + 32 * i) : -INFINITY;
         float mx = -INFINITY;
-        for (int e = lane; e < E; e += 32) mx = fmaxf(mx, lg[t * E + e]);
+#pragma unroll
+        for (int i = 0; i < kMaxE / 32; ++i) mx = fmaxf(mx, v[i]);
         mx = warp_max(mx);
-        float s = 0.f;
-        for (int e = lane; e < E; e += 32) s += expf(lg[t * E + e] - mx);
-        s = warp_sum(s);
-        if (lane == 0) { rs.rmax[t] = mx; rs.rinv[t] = 1.f / s; }
-    }
-    __syncthreads();
-    for (int i = tid; i < T * E; i += kGemvThreads) {
-        const int t = i / E, e = i - t * E;
-        const float v = lg[i];
-        const float *row = lg + t * E;
-        int rank = 0;
-#pragma unroll 4
-        for (int q = 0; q < E; ++q) rank += better(row[q], q, v, e);
-        if (rank < k) {
-            rs.ids[t * k + rank] = e;
-            rs.w[t * k + rank] = __fmul_rn(expf(v - rs.rmax[t]), rs.rinv[t]);
+        float sum = 0.f;
+#pragma unroll
+        for (int i = 0; i < kMaxE / 32; ++i) if (i < per) sum += expf(v[i] - mx);
+        sum = warp_sum(sum);
+        const float inv = 1.f / sum;
+        uint32_t key[kMaxE / 32];
+#pragma unroll
+        for (int i = 0; i < kMaxE / 32; ++i) key[i] = i < per ? route_key(v[i]) : 0u;
+        int my_id = 0;
+        float my_v = 0.f;
+        for (int j = 0; j < k; ++j) {
+            uint32_t bk = 0u;
+            int bi = 0;
+#pragma unroll
+            for (int i = 0; i < kMaxE / 32; ++i)
+                if (key[i] > bk) { bk = key[i]; bi = i; }   // strict: the lowest i (lowest id) of a lane's ties
+            const uint32_t kmax = __reduce_max_sync(0xffffffffu, bk);
+            const uint32_t e = __reduce_min_sync(0xffffffffu, bk == kmax ? (uint32_t)(lane + 32 * bi) : 0xffffffffu);
+            if ((int)(e & 31) == lane) {
+#pragma unroll
+                for (int i = 0; i < kMaxE / 32; ++i)
+                    if (i == (int)(e >> 5)) key[i] = 0u;   // taken (every real key is above 0)
+            }
+            const float ve = __shfl_sync(0xffffffffu, v[0], (int)(e & 31));
+            float vs = ve;
+#pragma unroll
+            for (int i = 1; i < kMaxE / 32; ++i) {
+                const float vi = __shfl_sync(0xffffffffu, v[i], (int)(e & 31));
+                if (i == (int)(e >> 5)) vs = vi;
+            }
+            if (lane == j) { my_id = (int)e; my_v = vs; }
+        }
+        // probabilities of the selected experts, normalised by max(sum, 6.1e-5) with the sum taken in
+        // slot order (llama-graph.cpp:1640-1648)
+        const float pj = lane < k ? __fmul_rn(expf(my_v - mx), inv) : 0.f;
+        float psum = 0.f;
+        for (int j = 0; j < k; ++j) psum = __fadd_rn(psum, __shfl_sync(0xffffffffu, pj, j));
+        psum = fmaxf(psum, 6.103515625e-5f);
+        if (lane < k) {
+            rs.ids[t * k + lane] = my_id;
+            rs.w[t * k + lane] = __fdiv_rn(pj, psum);
         }
     }
     __syncthreads();
-    for (int t = warp; t < T; t += kGemvThreads / 32) {
-        // weights / max(sum, 6.1e-5) with the sum taken in slot order (llama-graph.cpp:1640-1648)
-        const float mine = lane < k ? rs.w[t * k + lane] : 0.f;
-        float psum = 0.f;
-        for (int j = 0; j < k; ++j) psum = __fadd_rn(psum, __shfl_sync(0xffffffffu, mine, j));
-        psum = fmaxf(psum, 6.103515625e-5f);
-        if (lane < k) rs.w[t * k + lane] = __fdiv_rn(mine, psum);
-    }
-    __syncthreads();
 }
 
-// histogram, exclusive scan, stable permutation and the unique-expert list with both
-// projections' cumulative weight bytes. One warp scans: lane l owns experts [l*per, (l+1)*per).
+// work of an expert with n routed tokens for the split, in units that weigh the HBM bytes a CTA
+// streams against the instructions its consumer warps issue (about 3 instructions per byte per SM at
+// the measured bandwidth), rounded to a multiple of the expert's 8-row groups
+__device__ __forceinline__ uint32_t fused_cost(const FusedParams &p, bool gu, int type, int n) {
+    uint32_t bytes, instr;
+    if (gu) {
+        const uint32_t dec = type == T_IQ2_S ? 70u : 24u;
+        bytes = 8u * (uint32_t)(p.d / QK_K) * (type == T_IQ2_S ? (uint32_t)B_IQ2_S : (uint32_t)B_Q4_K);
+        instr = 8u * 8u * (uint32_t)(p.d / QK_K) * (dec + 16u * (uint32_t)n);
+    } else {
+        const uint32_t dec = type == T_IQ4_NL ? 45u : 25u;
+        bytes = 8u * (uint32_t)(p.nff / QK32) * (type == T_IQ4_NL ? (uint32_t)B_IQ4_NL : (uint32_t)B_Q5_0);
+        instr = 8u * (uint32_t)(p.nff / QK32) * (dec + 12u * (uint32_t)n);
+    }
+    const int gpe = gu ? 2 * p.nff / kGroupRows : p.d / kGroupRows;
+    return (3u * bytes + instr) / 64u * (uint32_t)gpe;
+}
+
+// Histogram, exclusive scan and stable permutation of the routed pairs (ggml-cpu.c:1613-1626), and
+// the unique-expert list with both projections' cumulative work units. Thread e owns expert e; the
+// scan runs as E/32 warp shuffle scans plus the preceding warps' totals.
 __device__ void fused_dispatch(const FusedParams &p, FusedRoute &rs, int tid, int nthreads) {
-    const int P = p.T * p.k, E = p.E;
+    const int P = p.T * p.k, E = p.E, lane = tid & 31, warp = tid >> 5;
     for (int e = tid; e < E; e += nthreads) rs.cnt[e] = 0;
     __syncthreads();
     for (int i = tid; i < P; i += nthreads) {
@@ -1070,71 +1109,54 @@ __device__ void fused_dispatch(const FusedParams &p, FusedRoute &rs, int tid, in
         atomicAdd(&rs.cnt[e], 1);
     }
     __syncthreads();
-    if (tid < 32) {
-        const int lane = tid, per = E / 32, e0 = lane * per;
-        const int gpe_gu = 2 * p.nff / kGroupRows, gpe_dn = p.d / kGroupRows;
-        // work of an expert with n routed tokens, in units that weigh the HBM bytes a CTA streams
-        // against the instructions its consumer warps issue (about 3 instructions per byte per SM at
-        // the measured bandwidth), rounded to a multiple of the expert's 8-row groups
-        auto cost = [&](bool gu, int type, int n) -> uint32_t {
-            // per 8-row group: bytes and lane instructions (decode + per-column dot work)
-            uint32_t bytes, instr;
-            if (gu) {
-                const uint32_t dec = type == T_IQ2_S ? 70u : 24u;
-                bytes = 8u * (uint32_t)(p.d / QK_K) * (type == T_IQ2_S ? (uint32_t)B_IQ2_S : (uint32_t)B_Q4_K);
-                instr = 8u * 8u * (uint32_t)(p.d / QK_K) * (dec + 16u * (uint32_t)n);
-            } else {
-                const uint32_t dec = type == T_IQ4_NL ? 45u : 25u;
-                bytes = 8u * (uint32_t)(p.nff / QK32) * (type == T_IQ4_NL ? (uint32_t)B_IQ4_NL : (uint32_t)B_Q5_0);
-                instr = 8u * (uint32_t)(p.nff / QK32) * (dec + 12u * (uint32_t)n);
-            }
-            return (3u * bytes + instr) / 64u * (uint32_t)(gu ? gpe_gu : gpe_dn);
-        };
-        int c_sum = 0, u_sum = 0;
-        uint32_t gsum = 0, dsum = 0;
-#pragma unroll 1
-        for (int i = 0; i < per; ++i) {
-            const int e = e0 + i, c = rs.cnt[e];
-            c_sum += c;
-            const bool has = c > 0 && rs.ecls[e] >= 0;
-            if (c > 0 && rs.ecls[e] < 0) atomicOr(&g_error, ERR_BAD_EXPERT);   // its class pool is absent
-            if (has) {
-                const bool hot = rs.ecls[e] == 0;
-                ++u_sum;
-                gsum += cost(true, hot ? p.hot_gu.type : p.cold_gu.type, c);
-                dsum += cost(false, hot ? p.hot_dn.type : p.cold_dn.type, c);
-            }
+    int c = 0, has = 0;
+    uint32_t gc = 0, dc = 0;
+    if (tid < E) {
+        c = rs.cnt[tid];
+        if (c > 0 && rs.ecls[tid] < 0) atomicOr(&g_error, ERR_BAD_EXPERT);   // its class pool is absent
+        if (c > 0 && rs.ecls[tid] >= 0) {
+            const bool hot = rs.ecls[tid] == 0;
+            has = 1;
+            gc = fused_cost(p, true, hot ? p.hot_gu.type : p.cold_gu.type, c);
+            dc = fused_cost(p, false, hot ? p.hot_dn.type : p.cold_dn.type, c);
         }
-        int c_in = c_sum, u_in = u_sum;
-        uint32_t g_in = gsum, d_in = dsum;
+    }
+    int ci = c, ui = has;
+    uint32_t gi = gc, di = dc;
+    if (warp < E / 32) {
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
-            const int a0 = __shfl_up_sync(0xffffffffu, c_in, o), a1 = __shfl_up_sync(0xffffffffu, u_in, o);
-            const uint32_t a2 = __shfl_up_sync(0xffffffffu, g_in, o), a3 = __shfl_up_sync(0xffffffffu, d_in, o);
-            if (lane >= o) { c_in += a0; u_in += a1; g_in += a2; d_in += a3; }
-        }
-        int c_base = c_in - c_sum, u = u_in - u_sum;
-        uint32_t gb = g_in - gsum, db = d_in - dsum;
-#pragma unroll 1
-        for (int i = 0; i < per; ++i) {
-            const int e = e0 + i, c = rs.cnt[e];
-            rs.off[e] = c_base;
-            c_base += c;
-            if (c > 0 && rs.ecls[e] >= 0) {
-                const bool hot = rs.ecls[e] == 0;
-                gb += cost(true, hot ? p.hot_gu.type : p.cold_gu.type, c);
-                db += cost(false, hot ? p.hot_dn.type : p.cold_dn.type, c);
-                rs.uexp[u] = e;
-                rs.ucls[u] = rs.ecls[e];
-                rs.uwidx[u] = rs.ewidx[e];
-                rs.upre_gu[u + 1] = gb;
-                rs.upre_dn[u + 1] = db;
-                ++u;
-            }
+            const int a0 = __shfl_up_sync(0xffffffffu, ci, o), a1 = __shfl_up_sync(0xffffffffu, ui, o);
+            const uint32_t a2 = __shfl_up_sync(0xffffffffu, gi, o), a3 = __shfl_up_sync(0xffffffffu, di, o);
+            if (lane >= o) { ci += a0; ui += a1; gi += a2; di += a3; }
         }
         if (lane == 31) {
-            rs.off[E] = c_in;
-            rs.n_unique = u_in;
+            rs.scan_c[warp] = ci;
+            rs.scan_u[warp] = ui;
+            rs.scan_g[warp] = gi;
+            rs.scan_d[warp] = di;
+        }
+    }
+    __syncthreads();
+    if (tid < E) {
+        for (int w = 0; w < warp; ++w) {
+            ci += rs.scan_c[w];
+            ui += rs.scan_u[w];
+            gi += rs.scan_g[w];
+            di += rs.scan_d[w];
+        }
+        rs.off[tid] = ci - c;
+        if (has) {
+            const int u = ui - 1;
+            rs.uexp[u] = tid;
+            rs.ucls[u] = rs.ecls[tid];
+            rs.uwidx[u] = rs.ewidx[tid];
+            rs.upre_gu[u + 1] = gi;
+            rs.upre_dn[u + 1] = di;
+        }
+        if (tid == E - 1) {
+            rs.off[E] = ci;
+            rs.n_unique = ui;
             rs.upre_gu[0] = 0;
             rs.upre_dn[0] = 0;
         }
@@ -1149,6 +1171,23 @@ __device__ void fused_dispatch(const FusedParams &p, FusedRoute &rs, int tid, in
     __syncthreads();
 }
 
+// The 8-row group at position `pos` of a cumulative work prefix (every unique expert has gpe groups
+// of equal cost), one warp: the unit u with pre[u] <= pos < pre[u + 1] by ballot, 32 units per step.
+__device__ __forceinline__ int group_at_pre_warp(const uint32_t *pre, int U, uint32_t pos, int gpe, int lane) {
+    if (pos >= pre[U]) return U * gpe;
+    int u = 0;
+    for (int u0 = 0; u0 < U; u0 += 32) {
+        const int q = u0 + lane;
+        const unsigned hit = __ballot_sync(0xffffffffu, q < U && pre[q] <= pos && pos < pre[q + 1]);
+        if (hit) {
+            u = u0 + __ffs(hit) - 1;
+            break;
+        }
+    }
+    const uint32_t unit = (pre[u + 1] - pre[u]) / (uint32_t)gpe;
+    return u * gpe + (int)((pos - pre[u]) / unit);
+}
+
 __global__ void __launch_bounds__(kGemvThreads, 1) fused_decode_kernel(FusedParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -1157,6 +1196,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) fused_decode_kernel(FusedPara
     FusedRoute &rs = *reinterpret_cast<FusedRoute *>(smem + L.route);
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.bars);
     uint64_t *empty = full + kFSlots;
+    uint64_t *xbar = empty + kFSlots;   // the Q8_K activation rows landed in xact
     uint64_t *grid = reinterpret_cast<uint64_t *>(smem + L.grid);
     uint8_t *xact = smem + L.xact;
     uint8_t *dact = smem + L.dact;
@@ -1166,12 +1206,19 @@ __global__ void __launch_bounds__(kGemvThreads, 1) fused_decode_kernel(FusedPara
     if (warp == 0) FTRACE(0);
     const int nrb = (d + 63) / 64;
     if (blockIdx.x == 0)
-        for (int i = tid; i < kFusedMaxP + T * nrb; i += kGemvThreads) p.sync[i] = 0u;
+        for (int i = tid; i < kFusedMaxP * (nff / QK32 + 1) + T * nrb; i += kGemvThreads) p.sync[i] = 0u;
+    {
+        // the GELU table (128 KB) into L2 ahead of the GeGLU step: CTA b takes lines b, b + G, ...
+        const char *gt = reinterpret_cast<const char *>(g_gelu_f16);
+        for (int l = blockIdx.x + G * tid; l < (int)(sizeof(g_gelu_f16) / 128); l += G * kGemvThreads)
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(gt + 128 * (size_t)l));
+    }
     if (tid == 0) {
         for (int s = 0; s < kFSlots; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kWarpsPerGroup);
         }
+        mbar_init(xbar, 1);
         fence_mbar_init();
     }
     if (warp == kConsumerWarps) {
@@ -1259,11 +1306,17 @@ __global__ void __launch_bounds__(kGemvThreads, 1) fused_decode_kernel(FusedPara
     if (warp == 0) FTRACE(1);
     if (tid == 0) grid_barrier_thread(G);
     __syncthreads();
+    if (tid == kConsumerWarps * 32) {
+        // every token's Q8_K row (written by other CTAs before the barrier) into xact, in the
+        // background of the routing; the generic-proxy writes are ordered before this async-proxy read
+        asm volatile("fence.proxy.async.global;" ::: "memory");
+        mbar_expect_tx(xbar, (uint32_t)(T * p.xq_stride));
+        bulk_g2s(xact, p.xq, (uint32_t)(T * p.xq_stride), xbar);
+    }
     if (warp == 0) FTRACE(2);
 
     // ================= phase B: routing and the work split
-    fused_route(p, rs, reinterpret_cast<float *>(slots), tid);   // the slot ring is free until the producer starts
-    __syncthreads();
+    fused_route(p, rs, tid);
     if (warp == 0) FTRACE(3);
     fused_dispatch(p, rs, tid, kGemvThreads);
     if (warp == 0) FTRACE(4);
@@ -1282,15 +1335,26 @@ __global__ void __launch_bounds__(kGemvThreads, 1) fused_decode_kernel(FusedPara
             if (p.off_out) p.off_out[e] = rs.off[e];
         }
     }
+    if (warp == 0) FTRACE(13);
     const int U = rs.n_unique;
     const int gpe_gu = 2 * nff / kGroupRows, sg_gu = kGuStageRows / kGroupRows, spe_gu = (gpe_gu + sg_gu - 1) / sg_gu;
     const int gpe_dn = d / kGroupRows, sg_dn = kDnStageRows / kGroupRows, spe_dn = (gpe_dn + sg_dn - 1) / sg_dn;
-    // work-balanced share of each projection (totals stay below 2^32 / G units)
-    const uint32_t tgu = rs.upre_gu[U], tdn = rs.upre_dn[U];
-    const int g0 = group_at_pre(rs.upre_gu, U, tgu * blockIdx.x / G, gpe_gu);
-    const int g1 = group_at_pre(rs.upre_gu, U, tgu * (blockIdx.x + 1) / G, gpe_gu);
-    const int h0 = group_at_pre(rs.upre_dn, U, tdn * blockIdx.x / G, gpe_dn);
-    const int h1 = group_at_pre(rs.upre_dn, U, tdn * (blockIdx.x + 1) / G, gpe_dn);
+    // work-balanced share of each projection (totals stay below 2^32 / G units): warps 0-3 search
+    // the bounds g0, g1 (gate_up) and h0, h1 (down) at once
+    if (warp < 4) {
+        const bool gu = warp < 2;
+        const uint32_t *pre = gu ? rs.upre_gu : rs.upre_dn;
+        const uint32_t pos = pre[U] * (blockIdx.x + (uint32_t)(warp & 1)) / (uint32_t)G;
+        const int g = group_at_pre_warp(pre, U, pos, gu ? gpe_gu : gpe_dn, lane);
+        if (lane == 0) rs.split[warp] = g;
+    }
+    if (tid == 0) {
+        rs.claim_gu = 0;
+        rs.claim_dn = 0;
+    }
+    __syncthreads();
+    const int g0 = rs.split[0], g1 = rs.split[1], h0 = rs.split[2], h1 = rs.split[3];
+    if (warp == 0) FTRACE(14);
     const int Sg = g1 > g0 ? stage_of(g0, gpe_gu, spe_gu, sg_gu) : 0;
     const int n_gu = g1 > g0 ? stage_of(g1 - 1, gpe_gu, spe_gu, sg_gu) - Sg + 1 : 0;
     const int Sd = h1 > h0 ? stage_of(h0, gpe_dn, spe_dn, sg_dn) : 0;
@@ -1326,25 +1390,23 @@ __global__ void __launch_bounds__(kGemvThreads, 1) fused_decode_kernel(FusedPara
         const int nsb = d / QK_K, nb = nff / QK32;
         const int xs = p.xq_stride, as = q80_stride(nff);
         const size_t hpart = (size_t)T * k * 2 * nff;   // stride of the four gate_up partial-sum parts
+        const int qas = fused_qa_stride(nff);
+        uint32_t *blk_cnt = p.sync, *act_cnt = p.sync + kFusedMaxP * nb, *dn_cnt = act_cnt + kFusedMaxP;
         const int grp = warp / kWarpsPerGroup, wg = warp % kWarpsPerGroup;
         uint32_t kv[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i)
             kv[i] = (uint32_t)(uint8_t)g_iq4nl[4 * i] | ((uint32_t)(uint8_t)g_iq4nl[4 * i + 1] << 8) |
                     ((uint32_t)(uint8_t)g_iq4nl[4 * i + 2] << 16) | ((uint32_t)(uint8_t)g_iq4nl[4 * i + 3] << 24);
-        if (warp == 0) FTRACE(13);
-        {
-            const int n16 = T * xs / 16;
-            const int4 *src = reinterpret_cast<const int4 *>(p.xq);
-            int4 *dst = reinterpret_cast<int4 *>(xact);
-            for (int i = tid; i < n16; i += kConsumerWarps * 32) dst[i] = __ldcg(src + i);
-        }
-        if (warp == 0) FTRACE(14);
-        consumer_sync();
+        bool ok = mbar_wait(xbar, 0u);
         if (warp == 0) FTRACE(5);
-        bool ok = true;
-        // ---- phase C: gate_up
-        for (int it = grp; it < n_gu; it += kGroups) {
+        // ---- phase C: gate_up. Groups claim stages in order as they become free (lane 0 of the
+        // group's first warp takes the next index; the group reads it after a group barrier).
+        for (int m = 0;; ++m) {
+            if (wg == 0 && lane == 0) rs.claim[grp][m & 1] = atomicAdd(&rs.claim_gu, 1);
+            group_sync(grp);
+            const int it = rs.claim[grp][m & 1];
+            if (it >= n_gu) break;
             const int slot = it % kFSlots;
             STRACE(it, 0);
             if (ok && !mbar_wait(&full[slot], (uint32_t)((it / kFSlots) & 1))) ok = false;
@@ -1360,21 +1422,19 @@ __global__ void __launch_bounds__(kGemvThreads, 1) fused_decode_kernel(FusedPara
             if (ok && type == T_Q4_K) {
                 // warp-level int8 MMAs: warp wg takes super-blocks wg, wg + 4, ... of all 16 rows and
                 // writes its partial sums to gate_up part wg (the GeGLU step adds the four in order)
-                int tok[8], pair[8];
-#pragma unroll
-                for (int c = 0; c < 8; ++c) {
-                    pair[c] = rs.perm[po + (c < n ? c : 0)];
-                    tok[c] = pair[c] / k;
-                }
+                // pair of column c (missing columns repeat column 0)
+                auto pair_of = [&](int c) { return rs.perm[po + (c < n ? c : 0)]; };
+                const int g = lane >> 2, cc = lane & 3;
+                const int pa = pair_of(2 * cc), pb = pair_of(2 * cc + 1);
                 float v[4] = {0.f, 0.f, 0.f, 0.f};
                 const uint8_t *stage = slots + slot * L.slot_cap;
-                q4k_tile_mma(stage, smem_addr(stage), rb, wg, nsb, xact, smem_addr(xact), xs, tok, n, v);
+                q4k_tile_mma(stage, smem_addr(stage), rb, wg, nsb, xact, smem_addr(xact), xs, pair_of(lane & 7) / k,
+                             pair_of(g) / k, pa / k, pb / k, n, v);
                 float *hp = p.h + (size_t)wg * hpart;
-                const int g = lane >> 2, cc = lane & 3;
 #pragma unroll
                 for (int q = 0; q < 4; ++q) {
                     const int row = g + 8 * (q >> 1), col = 2 * cc + (q & 1);
-                    if (row < st.nrows && col < n) hp[(size_t)pair[col] * 2 * nff + st.row0 + row] = v[q];
+                    if (row < st.nrows && col < n) hp[(size_t)((q & 1) ? pb : pa) * 2 * nff + st.row0 + row] = v[q];
                 }
             } else if (ok && wg * 4 < st.nrows) {
                 const uint8_t *row = slots + slot * L.slot_cap + (size_t)r * rb;
@@ -1411,27 +1471,90 @@ __global__ void __launch_bounds__(kGemvThreads, 1) fused_decode_kernel(FusedPara
             if (lane == 0) mbar_arrive(&empty[slot]);
         }
         consumer_sync();
-        if (tid == 0 && g1 > g0) {
-            // publish this CTA's gate_up rows: one fence, one count per expert of its range
+        if (warp == 0) FTRACE(6);
+        // ---- phase D1: publish this CTA's gate_up rows per (expert, 32-row ff block), one count per
+        // 8-row group; the CTA whose count completes a block's 64 rows (32 gate + 32 up) computes that
+        // block's GeGLU + Q8_0 for every token of the expert into qa, then counts the block as done.
+        // Each counting thread fences first, which orders the whole CTA's h rows (made visible to it by
+        // the barrier above) before its count.
+        int *blk_todo = reinterpret_cast<int *>(dact);   // act items: (u * nb + b) * kFusedMaxT + token
+        const int todo_cap = 2 * kFusedMaxT * as / 4 - 1;
+        if (tid == 0) blk_todo[0] = 0;
+        consumer_sync();
+        for (int gg = g0 + tid; gg < g1; gg += kConsumerWarps * 32) {
+            const int u = gg / gpe_gu, r = (gg - u * gpe_gu) * kGroupRows;
+            const int b = (r < nff ? r : r - nff) / QK32;
             __threadfence();
-            for (int u = g0 / gpe_gu; u <= (g1 - 1) / gpe_gu; ++u) {
-                const int lo = max(g0, u * gpe_gu), hi = min(g1, (u + 1) * gpe_gu);
-                atomicAdd(&p.sync[u], (uint32_t)((hi - lo) * kGroupRows));
+            if (atomicAdd(&blk_cnt[u * nb + b], (uint32_t)kGroupRows) + kGroupRows == 2u * QK32) {
+                const int n = min(rs.cnt[rs.uexp[u]], T);
+                const int at = atomicAdd(&blk_todo[0], n);
+                if (at + n <= todo_cap) {
+                    for (int i = 0; i < n; ++i) blk_todo[1 + at + i] = (u * nb + b) * kFusedMaxT + i;
+                } else {
+                    atomicOr(&g_error, ERR_CAPACITY);
+                }
             }
         }
-        if (warp == 0) FTRACE(6);
+        consumer_sync();
+        const int n_items = min(blk_todo[0], todo_cap);
+        if (n_items > 0) {
+            if (tid == 0) __threadfence();   // every other CTA's rows of these blocks are counted
+            consumer_sync();
+            // two items per warp in flight: both items' partial sums are loaded before either is quantised
+            for (int q0 = warp; q0 < n_items; q0 += 2 * kConsumerWarps) {
+                float g[2], v[2];
+                uint8_t *row[2];
+                int bq[2];
+#pragma unroll
+                for (int h2 = 0; h2 < 2; ++h2) {
+                    const int q = q0 + h2 * kConsumerWarps;
+                    g[h2] = v[h2] = 0.f;
+                    row[h2] = nullptr;
+                    bq[h2] = 0;
+                    if (q < n_items) {
+                        const int item = blk_todo[1 + q], ub = item / kFusedMaxT, i = item - ub * kFusedMaxT;
+                        const int u = ub / nb, b = ub - u * nb, e = rs.uexp[u];
+                        const float *hp = p.h + (size_t)rs.perm[rs.off[e] + i] * 2 * nff + QK32 * b + lane;
+                        // gate_up partial sums of the four super-block quarters, added in order
+                        g[h2] = __fadd_rn(__fadd_rn(__fadd_rn(__ldcg(hp), __ldcg(hp + hpart)), __ldcg(hp + 2 * hpart)),
+                                          __ldcg(hp + 3 * hpart));
+                        v[h2] = __fadd_rn(__fadd_rn(__fadd_rn(__ldcg(hp + nff), __ldcg(hp + nff + hpart)),
+                                                    __ldcg(hp + nff + 2 * hpart)),
+                                          __ldcg(hp + nff + 3 * hpart));
+                        row[h2] = p.qa + (size_t)(rs.off[e] + i) * qas;
+                        bq[h2] = b;
+                    }
+                }
+#pragma unroll
+                for (int h2 = 0; h2 < 2; ++h2) {
+                    if (row[h2] == nullptr) continue;
+                    const int b = bq[h2];
+                    q80_block_warp(geglu1(g[h2], v[h2]), reinterpret_cast<int8_t *>(row[h2]) + QK32 * b,
+                                   reinterpret_cast<float *>(row[h2] + nb * 32) + b,
+                                   reinterpret_cast<int *>(row[h2] + nb * 36) + b, lane);
+                }
+            }
+            consumer_sync();
+            for (int q = tid; q < n_items; q += kConsumerWarps * 32) {
+                const int item = blk_todo[1 + q];
+                if (item % kFusedMaxT == 0) {   // one count per finished block
+                    __threadfence();
+                    atomicAdd(&act_cnt[item / kFusedMaxT / nb], 1u);
+                }
+            }
+        }
 
-        // ---- phase D: down activations for this CTA's experts (<= 2), then the down stages
+        // ---- phase D2: the down activations of this CTA's down experts (<= 2) once all their
+        // blocks are finished (bounded wait), copied into shared memory
         const int u_first = h1 > h0 ? h0 / gpe_dn : 0;
         const int u_last = h1 > h0 ? (h1 - 1) / gpe_dn : -1;
         if (u_last - u_first > 1 && tid == 0) atomicOr(&g_error, ERR_CAPACITY);
         if (tid == 0) {
-            // every gate_up row of this CTA's down experts has been written (bounded wait)
             for (int u = u_first; u <= min(u_last, u_first + 1); ++u) {
                 uint32_t i = 0;
-                while (ld_acquire_u32(&p.sync[u]) < (uint32_t)(2 * nff)) {
+                while (ld_acquire_u32(&act_cnt[u]) < (uint32_t)nb) {
                     if (++i >= kGridWaitLimit) { atomicOr(&g_error, ERR_GRID_TIMEOUT); break; }
-                    if (i >= 256) __nanosleep(32);
+                    if (i >= 64) __nanosleep(32);
                 }
             }
             __threadfence();
@@ -1439,45 +1562,25 @@ __global__ void __launch_bounds__(kGemvThreads, 1) fused_decode_kernel(FusedPara
         consumer_sync();
         if (warp == 0) FTRACE(7);
         for (int u = u_first; u <= min(u_last, u_first + 1); ++u) {
-            const int e = rs.uexp[u], po = rs.off[e], n = min(rs.cnt[e], T);
-            const int n_items = n * nb;
-            for (int base = warp; base < n_items; base += 4 * kConsumerWarps) {
-                // four items' loads in flight before any of them is quantised
-                float g[4], v[4];
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const int item = base + q * kConsumerWarps;
-                    g[q] = v[q] = 0.f;
-                    if (item < n_items) {
-                        const int i = item / nb, b = item - i * nb;
-                        const float *hp = p.h + (size_t)rs.perm[po + i] * 2 * nff + 32 * b + lane;
-                        // gate_up partial sums of the four super-block quarters, added in order
-                        g[q] = __fadd_rn(__fadd_rn(__fadd_rn(__ldcg(hp), __ldcg(hp + hpart)), __ldcg(hp + 2 * hpart)),
-                                         __ldcg(hp + 3 * hpart));
-                        v[q] = __fadd_rn(__fadd_rn(__fadd_rn(__ldcg(hp + nff), __ldcg(hp + nff + hpart)),
-                                                   __ldcg(hp + nff + 2 * hpart)),
-                                         __ldcg(hp + nff + 3 * hpart));
-                    }
-                }
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const int item = base + q * kConsumerWarps;
-                    if (item < n_items) {
-                        const int i = item / nb, b = item - i * nb;
-                        uint8_t *row = dact + (size_t)((u - u_first) * T + i) * as;
-                        q80_block_warp(geglu1(g[q], v[q]), reinterpret_cast<int8_t *>(row) + 32 * b,
-                                       reinterpret_cast<float *>(row + nb * 32) + b, reinterpret_cast<int *>(row + nb * 36) + b,
-                                       lane);
-                    }
-                }
+            const int e = rs.uexp[u], n = min(rs.cnt[e], T), r16 = as / 16;
+            for (int i = tid; i < n * r16; i += kConsumerWarps * 32) {
+                const int row = i / r16, c = i - row * r16;
+                reinterpret_cast<int4 *>(dact + (size_t)((u - u_first) * T + row) * as)[c] =
+                    __ldcg(reinterpret_cast<const int4 *>(p.qa + (size_t)(rs.off[e] + row) * qas) + c);
             }
         }
         consumer_sync();
         if (warp == 0) FTRACE(8);
-        // down stages: the unified sequence continues at it = n_gu; groups keep their residue
-        for (int it = n_gu + grp; it < n_gu + n_dn; it += kGroups) {
+        // the unified sequence continues at it = n_gu; groups keep their residue
+        for (int m = 0;; ++m) {
+            if (wg == 0 && lane == 0) rs.claim[grp][m & 1] = n_gu + atomicAdd(&rs.claim_dn, 1);
+            group_sync(grp);
+            const int it = rs.claim[grp][m & 1];
+            if (it >= n_gu + n_dn) break;
             const int slot = it % kFSlots;
+            STRACE(it, 0);
             if (ok && !mbar_wait(&full[slot], (uint32_t)((it / kFSlots) & 1))) ok = false;
+            STRACE(it, 1);
             bool is_gu;
             const StagePlan st = plan(it, is_gu);
             const int e = rs.uexp[st.u], widx = rs.uwidx[st.u];
@@ -1503,19 +1606,21 @@ __global__ void __launch_bounds__(kGemvThreads, 1) fused_decode_kernel(FusedPara
                     else dn_rows<4>(row, b0, b1, nb, pv.type, kv, dact, as, slot0 + c0, nt, v);
 #pragma unroll
                     for (int c = 0; c < kTokChunk; ++c) {
-                        float s = v[c];
-                        s += __shfl_xor_sync(0xffffffffu, s, 1);
+                        float sum = v[c];
+                        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
                         if (half == 0 && valid && c < nt) {
                             const int pair = rs.perm[po + c0 + c];
-                            if (pv.scale) s = __fmul_rn(s, pv.scale[widx]);
-                            p.y[(size_t)pair * d + st.row0 + r] = s;
+                            if (pv.scale) sum = __fmul_rn(sum, pv.scale[widx]);
+                            p.y[(size_t)pair * d + st.row0 + r] = sum;
                         }
                     }
                 }
             }
             __syncwarp();
+            STRACE(it, 2);
             if (lane == 0) mbar_arrive(&empty[slot]);
         }
+        if (warp == 0) FTRACE(10);
         // ---- phase E: publish this CTA's down rows per (token, 64-row block); the CTA whose
         // count completes a block combines it: out[t] = sum_j w_j * y[t*k + j], products rounded,
         // then added in slot order (ggml_mul + the view-add chain, llama-graph.cpp:1814-1848)
@@ -1541,7 +1646,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) fused_decode_kernel(FusedPara
                         if (items % (kConsumerWarps * 32) != tid) continue;
                         const int rows = min(hi, (rb + 1) * 64) - max(lo, rb * 64);
                         const int t = rs.perm[po + c] / k;
-                        const uint32_t before = atomicAdd(&p.sync[kFusedMaxP + t * nrb + rb], (uint32_t)rows);
+                        const uint32_t before = atomicAdd(&dn_cnt[t * nrb + rb], (uint32_t)rows);
                         if (before + rows == (uint32_t)(k * min(64, d - rb * 64))) {
                             const int at = atomicAdd(&todo[0], 1);
                             todo[1 + 2 * at] = t;
@@ -1551,6 +1656,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) fused_decode_kernel(FusedPara
             }
         }
         consumer_sync();
+        if (warp == 0) FTRACE(11);
         const int n_todo = todo[0];
         if (n_todo > 0) {
             if (tid == 0) __threadfence();
@@ -1750,6 +1856,7 @@ cudaError_t launch_fused(const FusedArgs &a, cudaStream_t s, int n_sms) {
     p.logits = a.logits; p.xq = a.xq; p.xq_stride = a.xq_stride;
     p.h = a.h; p.y = a.y; p.out = a.out;
     p.ids_out = a.ids_out; p.w_out = a.w_out; p.cnt_out = a.cnt_out; p.off_out = a.off_out; p.perm_out = a.perm_out;
+    p.qa = a.qa;
     p.sync = a.sync;
     const size_t smem = fused_smem_bytes(a.d, a.nff);
     static bool attr_set = false;
@@ -1997,6 +2104,13 @@ cudaError_t read_and_clear_error(int32_t *out, cudaStream_t s) {
     const int32_t zero = 0;
     e = cudaMemcpyToSymbolAsync(g_error, &zero, sizeof(int32_t), 0, cudaMemcpyHostToDevice, s);
     if (e != cudaSuccess) return e;
+    if (*out & ERR_GRID_TIMEOUT) {
+        // a CTA gave up a grid barrier: the barrier word may hold a partial count; the launch has
+        // ended (stream order), so start the next one from zero
+        const unsigned zw = 0;
+        e = cudaMemcpyToSymbolAsync(g_bar_word, &zw, sizeof(unsigned), 0, cudaMemcpyHostToDevice, s);
+        if (e != cudaSuccess) return e;
+    }
     return cudaStreamSynchronize(s);
 }
 

@@ -111,9 +111,14 @@ struct FusedArgs {
     float *h, *y, *out;         // h: four [T*k][2 nff] partial-sum parts of gate_up
     int32_t *ids_out, *cnt_out, *off_out, *perm_out;
     float *w_out;
-    uint32_t *sync;          // fused_sync_words(T, d) zero-initialised-by-the-kernel counters
+    uint8_t *qa;             // [T*k][q80 row of n_ff] down activations (Q8_0), expert-sorted slot order
+    uint32_t *sync;          // fused_sync_words(T, d, nff) zero-initialised-by-the-kernel counters
 };
-MOEB_HD inline int fused_sync_words(int T, int d) { return kFusedTokens * kMaxTopK + T * ((d + 63) / 64); }
+// counters: gate_up rows per (unique expert, 32-row ff block), finished blocks per unique expert,
+// down rows per (token, 64-row output block)
+MOEB_HD inline int fused_sync_words(int T, int d, int nff) {
+    return kFusedTokens * kMaxTopK * (nff / 32 + 1) + T * ((d + 63) / 64);
+}
 
 // the prefill path (tcgen05 grouped GEMMs; prefill.cuh)
 constexpr int kPrefillTile = 128;        // routed pairs per expert tile (MMA N)
@@ -171,6 +176,9 @@ int prefill_profile_read(float *ms, int n);
 MOEB_HD inline int xq_stride_bytes(int d) { return (int)(((d / QK_K) * B_Q8_K + 15) / 16 * 16); }
 // Q8_0 activation row in shared memory: qs[nb][32] | d[nb] f32 | qsum[nb] i32
 MOEB_HD inline int q80_stride(int d_in) { return ((d_in / 32) * 40 + 15) / 16 * 16; }
+// rows of the fused kernel's down activations in global memory start on their own 128-byte lines,
+// so a row read through L1 never shares a line with a row another CTA is still writing
+MOEB_HD inline int fused_qa_stride(int nff) { return (q80_stride(nff) + 127) / 128 * 128; }
 
 // host-side launch helpers (decode.cu); `pdl` chains the launch to the previous kernel in the stream
 cudaError_t launch_gemv(const GemvParams &p, cudaStream_t s, bool pdl, int n_sms);
