@@ -128,6 +128,15 @@ int    moeb_layer_forward_routed(const moeb_layer *L, const float *x, int32_t n_
  * d_model not a multiple of 128, d_model > 4096 or n_ff > 1024) always take the decode path. */
 int32_t moeb_set_prefill_min_tokens(int32_t n_tokens);
 
+/* Sets the bound on the mean routed pairs per expert (top_k x n_tokens / n_expert) below which a
+ * batch on the prefill path runs the mid-size kernels instead of the tcgen05 GEMMs (default 48;
+ * values <= 0 leave it unchanged; 1 turns the mid-size kernels off) and returns the previous value.
+ * Process-wide. The mid-size kernels stream each routed expert's rows once and multiply the
+ * weights' own integer codes (warp-level int8 MMAs) by every 8-pair block of its tokens, so their
+ * cost follows the weight bytes, where the tcgen05 path converts every weight element into an
+ * fp16 operand. Layers whose shape they do not cover fall back to the tcgen05 path. */
+int32_t moeb_set_mid_max_pairs(int32_t pairs_per_expert);
+
 /* Profiling of the prefill path (no counterpart in the reference): while enabled, every prefill
  * forward on the current device records CUDA events around its nine kernels (router, top-k,
  * dispatch, activation quantisation, operand gather, gate_up, GeGLU, down, combine) on the

@@ -195,7 +195,9 @@ PrefillWs carve_prefill(const moeb_layer *L, int T, uint8_t *base) {
     w.xd = (float *)take(sizeof(float) * T * nsb);
     w.xbs = (int16_t *)take(sizeof(int16_t) * T * nsb * 16);
     const size_t mt = (size_t)w.max_tiles;
-    w.bimg = (uint8_t *)take(mt * nsb * 2 * kPfGuImageBytes);
+    // the tcgen05 path's gate_up images, or the mid-size path's operand images
+    const size_t pf_img = mt * nsb * 2 * kPfGuImageBytes, md_img = md_image_bytes((int)P, (int)E, (int)d, (int)nff);
+    w.bimg = (uint8_t *)take(pf_img > md_img ? pf_img : md_img);
     w.dxt = (float *)take(sizeof(float) * mt * nsb * kPrefillTile);
     w.hbuf = (float *)take(sizeof(float) * P * 2 * nff);
     w.dimg = (uint8_t *)take(mt * (nff / 64) * 2 * kPfDnImageBytes);
@@ -214,6 +216,15 @@ bool prefill_shape_ok(const moeb_layer *L) {
 
 bool use_prefill(const moeb_layer *L, int32_t n_tokens) {
     return n_tokens >= g_prefill_min.load() && prefill_shape_ok(L);
+}
+
+// Prefill-path batches with fewer routed pairs per expert than this run the mid-size kernels.
+std::atomic<int32_t> g_mid_max{48};
+
+bool use_mid(const moeb_layer *L, int32_t n_rows) {
+    const long long P = (long long)n_rows * L->top_k;
+    const int32_t m = g_mid_max.load();   // 1: off
+    return m > 1 && P < (long long)m * L->n_expert && mid_shape_ok(L->d_model, L->n_ff, (int)P, L->n_expert);
 }
 
 PoolView pool_view(const moeb_pool &pl, bool gate_up) {
@@ -277,6 +288,12 @@ extern "C" int moeb_prefill_profile_read(float *ms, int32_t n) {
     return MOEB_OK;
 }
 
+extern "C" int32_t moeb_set_mid_max_pairs(int32_t pairs_per_expert) {
+    const int32_t prev = g_mid_max.load();
+    if (pairs_per_expert > 0) g_mid_max.store(pairs_per_expert);
+    return prev;
+}
+
 extern "C" int32_t moeb_set_prefill_min_tokens(int32_t n_tokens) {
     const int32_t prev = g_prefill_min.load();
     if (n_tokens > 0) g_prefill_min.store(n_tokens);
@@ -328,6 +345,8 @@ static int forward_prefill(const moeb_layer *L, const float *x, int32_t T, float
     a.y = w.y;
     a.out = out;
     a.y_pairs = aux ? aux->down : nullptr;
+    a.mid = use_mid(L, T) ? 1 : 0;
+    a.md_max_cb = P / 8 + w.max_tiles;
     cudaError_t e = launch_prefill(a, s, n_sms);
     if (e != cudaSuccess) return MOEB_ECUDA;   // launch_prefill recorded the failing kernel
     if (aux) {
@@ -415,6 +434,8 @@ extern "C" int moeb_layer_forward_routed(const moeb_layer *L, const float *x, in
     a.y = w.y;
     a.out = out;
     a.routed = 1;
+    a.mid = use_mid(L, n_rows) ? 1 : 0;
+    a.md_max_cb = n_rows * k / 8 + w.max_tiles;
     cudaError_t e = launch_prefill(a, (cudaStream_t)stream, n_sms);
     if (e != cudaSuccess) return MOEB_ECUDA;
     return MOEB_OK;

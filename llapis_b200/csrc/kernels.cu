@@ -1679,6 +1679,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) fused_decode_kernel(FusedPara
 }  // namespace moeb
 
 #include "prefill.cuh"
+#include "mid.cuh"
 
 namespace moeb {
 
@@ -1949,6 +1950,12 @@ static cudaError_t pf_launch(const char *name, const void *fn, dim3 grid, dim3 b
     return e;
 }
 
+bool mid_shape_ok(int d, int nff, int P, int E) {
+    return d % QK_K == 0 && nff % QK32 == 0 && prefill_max_tiles(P, E) <= kMdMaxTiles &&
+           (P / 8 + prefill_max_tiles(P, E)) / 2 <= kMdMaxUnits && md_layout(0, d, nff).n_slots >= 2 &&
+           md_layout(1, d, nff).n_slots >= 2;
+}
+
 cudaError_t launch_prefill(const PrefillArgs &a, cudaStream_t s, int n_sms) {
     static unsigned optin[32];
     cudaError_t e = smem_optin((const void *)pf_gate_up_kernel, sizeof(GuSmem), optin, 0);
@@ -2007,31 +2014,84 @@ cudaError_t launch_prefill(const PrefillArgs &a, cudaStream_t s, int n_sms) {
         if (e != cudaSuccess) return e;
         if ((e = prof_mark(s, mark++)) != cudaSuccess) return e;
     }
-    PfParams p{};
-    p.T = T; p.E = E; p.d = d; p.k = k; p.nff = a.nff;
-    p.gu[0] = a.hot_gu; p.gu[1] = a.cold_gu; p.dn[0] = a.hot_dn; p.dn[1] = a.cold_dn;
-    p.perm = a.perm; p.tiles = a.tiles; p.n_tiles = a.n_tiles;
-    p.xq8 = a.xq8; p.xd = a.xd; p.xbs = a.xbs;
-    p.bimg = a.bimg; p.dxt = a.dxt; p.hbuf = a.hbuf; p.dimg = a.dimg; p.h = a.h; p.y = a.y;
-    {
-        void *args[] = {&p};
-        e = pf_launch("pf_gather_kernel", (const void *)pf_gather_kernel, dim3(a.max_tiles, d / QK_K), dim3(256), 0, s,
-                      true, args);
+    if (a.mid) {
+        // mid-size batches: operand image, gate_up, GeGLU + Q8_0, down (mid.cuh)
+        const size_t smem_gu = (size_t)md_layout(0, d, a.nff).total, smem_dn = (size_t)md_layout(1, d, a.nff).total;
+        // opt in once at the largest size any layer shape may ask for
+        e = smem_optin((const void *)md_kernel<0>, 227 * 1024, optin, 2);
+        if (e == cudaSuccess) e = smem_optin((const void *)md_kernel<1>, 227 * 1024, optin, 3);
         if (e != cudaSuccess) return e;
-        if ((e = prof_mark(s, mark++)) != cudaSuccess) return e;
-    }
-    {
-        void *args[] = {&p};
-        e = pf_launch("pf_gate_up_kernel", (const void *)pf_gate_up_kernel, dim3(n_sms), dim3(kPfThreads), sizeof(GuSmem), s, true, args);
-        if (e != cudaSuccess) return e;
-        if ((e = prof_mark(s, mark++)) != cudaSuccess) return e;
-        e = pf_launch("pf_geglu_kernel", (const void *)pf_geglu_kernel, dim3(a.max_tiles, a.nff / 32), dim3(256), 0, s,
-                      true, args);
-        if (e != cudaSuccess) return e;
-        if ((e = prof_mark(s, mark++)) != cudaSuccess) return e;
-        e = pf_launch("pf_down_kernel", (const void *)pf_down_kernel, dim3(n_sms), dim3(kDnThreads), sizeof(DnSmem), s, true, args);
-        if (e != cudaSuccess) return e;
-        if ((e = prof_mark(s, mark++)) != cudaSuccess) return e;
+        {
+            const PfTile *tl = a.tiles;
+            const int32_t *nt = a.n_tiles, *perm = a.perm;
+            const int8_t *q = a.xq8;
+            const float *xd = a.xd;
+            const int16_t *bs = a.xbs;
+            uint8_t *img = a.bimg;
+            int kk = k, dd = d;
+            void *args[] = {&tl, &nt, &perm, &q, &xd, &bs, &img, &kk, &dd};
+            e = pf_launch("md_bimg_kernel", (const void *)md_bimg_kernel, dim3(a.md_max_cb, d / QK_K), dim3(256), 0, s,
+                          true, args);
+            if (e != cudaSuccess) return e;
+            if ((e = prof_mark(s, mark++)) != cudaSuccess) return e;
+        }
+        MdParams m{};
+        m.T = T; m.E = E; m.d = d; m.k = k; m.nff = a.nff;
+        m.tiles = a.tiles; m.n_tiles = a.n_tiles; m.perm = a.perm; m.img = a.bimg;
+        m.pv[0] = a.hot_gu; m.pv[1] = a.cold_gu; m.out = a.hbuf;
+        {
+            void *args[] = {&m};
+            e = pf_launch("md_kernel<0>", (const void *)md_kernel<0>, dim3(n_sms), dim3(kMdThreads), smem_gu, s, true, args);
+            if (e != cudaSuccess) return e;
+            if ((e = prof_mark(s, mark++)) != cudaSuccess) return e;
+        }
+        {
+            const PfTile *tl = a.tiles;
+            const int32_t *nt = a.n_tiles, *perm = a.perm;
+            const float *hb = a.hbuf;
+            uint8_t *img = a.bimg;
+            float *hp = a.h;
+            int nf = a.nff;
+            void *args[] = {&tl, &nt, &perm, &hb, &img, &hp, &nf};
+            e = pf_launch("md_act_kernel", (const void *)md_act_kernel, dim3(a.md_max_cb, (a.nff / QK32 + 7) / 8), dim3(256),
+                          0, s, true, args);
+            if (e != cudaSuccess) return e;
+            if ((e = prof_mark(s, mark++)) != cudaSuccess) return e;
+        }
+        m.pv[0] = a.hot_dn; m.pv[1] = a.cold_dn; m.out = a.y;
+        {
+            void *args[] = {&m};
+            e = pf_launch("md_kernel<1>", (const void *)md_kernel<1>, dim3(n_sms), dim3(kMdThreads), smem_dn, s, true, args);
+            if (e != cudaSuccess) return e;
+            if ((e = prof_mark(s, mark++)) != cudaSuccess) return e;
+        }
+    } else {
+        PfParams p{};
+        p.T = T; p.E = E; p.d = d; p.k = k; p.nff = a.nff;
+        p.gu[0] = a.hot_gu; p.gu[1] = a.cold_gu; p.dn[0] = a.hot_dn; p.dn[1] = a.cold_dn;
+        p.perm = a.perm; p.tiles = a.tiles; p.n_tiles = a.n_tiles;
+        p.xq8 = a.xq8; p.xd = a.xd; p.xbs = a.xbs;
+        p.bimg = a.bimg; p.dxt = a.dxt; p.hbuf = a.hbuf; p.dimg = a.dimg; p.h = a.h; p.y = a.y;
+        {
+            void *args[] = {&p};
+            e = pf_launch("pf_gather_kernel", (const void *)pf_gather_kernel, dim3(a.max_tiles, d / QK_K), dim3(256), 0, s,
+                          true, args);
+            if (e != cudaSuccess) return e;
+            if ((e = prof_mark(s, mark++)) != cudaSuccess) return e;
+        }
+        {
+            void *args[] = {&p};
+            e = pf_launch("pf_gate_up_kernel", (const void *)pf_gate_up_kernel, dim3(n_sms), dim3(kPfThreads), sizeof(GuSmem), s, true, args);
+            if (e != cudaSuccess) return e;
+            if ((e = prof_mark(s, mark++)) != cudaSuccess) return e;
+            e = pf_launch("pf_geglu_kernel", (const void *)pf_geglu_kernel, dim3(a.max_tiles, a.nff / 32), dim3(256), 0, s,
+                          true, args);
+            if (e != cudaSuccess) return e;
+            if ((e = prof_mark(s, mark++)) != cudaSuccess) return e;
+            e = pf_launch("pf_down_kernel", (const void *)pf_down_kernel, dim3(n_sms), dim3(kDnThreads), sizeof(DnSmem), s, true, args);
+            if (e != cudaSuccess) return e;
+            if ((e = prof_mark(s, mark++)) != cudaSuccess) return e;
+        }
     }
     {
         const float *y = a.y, *w = a.w;

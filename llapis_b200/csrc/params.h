@@ -163,11 +163,21 @@ struct PrefillArgs {
     float *out;                 // [T][d]
     float *y_pairs;             // optional [P][d] down outputs, pair order
     int32_t routed;             // 1: ids / w are given (the router and top-k kernels are skipped)
+    int32_t mid;                // 1: mid-size path (int8 MMAs on the weight codes; bimg holds its operand images)
+    int32_t md_max_cb;          // mid path: bound on the column blocks (P / 8 + max_tiles)
 };
+// mid path: operand image bytes (one 8-pair column block of gate_up, the larger of the two kinds)
+MOEB_HD inline size_t md_image_bytes(int P, int E, int d, int nff) {
+    const size_t cb = (size_t)(P / 8 + prefill_max_tiles(P, E));
+    const size_t gu = (size_t)(d / 256) * 5 * 512, dn = (size_t)(nff / 32) * 512;
+    return cb * (gu > dn ? gu : dn);
+}
 // router logits + softmax/top-k/weights only (the first two prefill kernels)
 cudaError_t launch_route(const float *w_router, const float *b_router, const float *x, int T, int E, int d, int k,
                          float *part, float *logits, int32_t *ids, float *w, cudaStream_t s);
 cudaError_t launch_prefill(const PrefillArgs &a, cudaStream_t s, int n_sms);
+// whether the mid-size kernels cover this shape (shared memory, tile count) for P routed pairs
+bool mid_shape_ok(int d, int nff, int P, int E);
 // router, top-k, dispatch, activation quantisation, gather, gate_up, GeGLU, down, combine
 constexpr int kPrefillKernels = 9;
 void prefill_profile_enable(bool on);

@@ -113,6 +113,16 @@ class MoELayer:
         shape_ok = h.n_ff % 64 == 0 and h.d_model % 128 == 0 and h.d_model // 256 <= 16 and h.n_ff // 32 <= 32
         return shape_ok and n_tokens >= int(capi.lib().moeb_set_prefill_min_tokens(0))
 
+    def mid_path(self, n_tokens: int) -> bool:
+        """Whether a prefill-path forward of n_tokens runs the mid-size kernels (int8 MMAs on the
+        weight codes) rather than the tcgen05 GEMMs: fewer routed pairs per expert than the
+        library's bound (moeb_set_mid_max_pairs) and a covered shape."""
+        h = self.host
+        P = n_tokens * h.top_k
+        m = int(capi.lib().moeb_set_mid_max_pairs(0))   # 1: off
+        return (self.prefill_path(n_tokens) and m > 1 and P < m * h.n_expert
+                and h.d_model % 256 == 0 and h.n_ff % 32 == 0 and P // 128 + h.n_expert + 1 <= 512)
+
     def launches(self, n_tokens: int) -> int:
         """Kernels one forward of n_tokens launches: nine on the prefill path, else one cooperative
         fused kernel per 8-token chunk."""

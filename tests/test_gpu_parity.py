@@ -123,6 +123,8 @@ def run_layer(host, x, aux_names=("logits", "ids", "weights", "counts", "offsets
     aux = {n: torch.empty(*shapes[n][0], dtype=shapes[n][1], device="cuda") for n in aux_names}
     out = layer(dev(x), aux=aux)
     torch.cuda.synchronize()
+    # every bounded wait ended in time (a timed-out wait would leave its outputs unwritten)
+    assert layer.device_error() == 0
     return out.cpu().numpy(), {n: t.cpu().numpy() for n, t in aux.items()}, layer
 
 

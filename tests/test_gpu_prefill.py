@@ -20,11 +20,24 @@ def prefill_from():
     lib.moeb_set_prefill_min_tokens(prev)
 
 
-def test_prefill_mini_vs_reference_fixture(golden, prefill_from):
+@pytest.fixture
+def gemm():
+    """Selects the prefill path's GEMMs for one test ("mid": int8 MMAs on the weight codes;
+    "tcgen05": the converted-operand tensor-core GEMMs) and restores the threshold afterwards."""
+    lib = capi.lib()
+    prev = lib.moeb_set_mid_max_pairs(0)
+    yield lambda kind: lib.moeb_set_mid_max_pairs(1 << 30 if kind == "mid" else 1)
+    lib.moeb_set_mid_max_pairs(prev)
+
+
+@pytest.mark.parametrize("kind", ["tcgen05", "mid"])
+def test_prefill_mini_vs_reference_fixture(golden, prefill_from, gemm, kind):
     prefill_from(1)
+    gemm(kind)
     host = host_layer("mini_mixed")
     out, aux, layer = run_layer(host, golden["mini_x"])
     assert layer.launches(golden["mini_x"].shape[0]) == 9
+    assert layer.mid_path(golden["mini_x"].shape[0]) == (kind == "mid")
     assert np.array_equal(aux["ids"], golden["mini_ids"])
     np.testing.assert_allclose(aux["logits"], golden["mini_logits"], rtol=1e-5, atol=1e-6)
     np.testing.assert_allclose(aux["weights"], golden["mini_weights"], rtol=1e-5, atol=1e-7)
@@ -36,6 +49,11 @@ def test_prefill_mini_vs_reference_fixture(golden, prefill_from):
     assert_layer_close(aux["gate_up"], golden["mini_gate_up"], tol=1e-5)
     assert_layer_close(aux["down"], golden["mini_down"], tol=TOL)
     assert_layer_close(out, golden["mini_out"], tol=TOL)
+
+
+def host_layer_mid(host, T):
+    m = int(capi.lib().moeb_set_mid_max_pairs(0))
+    return m > 1 and T * host.top_k < m * host.n_expert
 
 
 def q80_flips(port, want_act, cond_act):
@@ -84,19 +102,24 @@ def check_stages(port, host, x, out, aux, tokens=None, dispatch=True):
     return rel, len(ties), len(flips)
 
 
-@pytest.mark.parametrize("path", ["prefill", "decode"])
+@pytest.mark.parametrize("path", ["tcgen05", "mid", "decode"])
 @pytest.mark.parametrize("name,T", [("mini_mixed", 64), ("mini_mixed", 1100), ("decode_t4_mixed", 96),
-                                    ("prefill_t2048_q4k", 160)])
-def test_layer_paths_vs_port_oracle(port, prefill_from, path, name, T):
-    """Both paths, stage by stage (check_stages). mini_mixed at T=1100 puts more than 128 pairs on
-    most experts (several tiles per expert); decode_t4_mixed mixes Q4_K/Q5_0 and IQ2_S/IQ4_NL
-    tiles at the real shapes."""
-    prefill_from(1 if path == "prefill" else 1 << 30)
+                                    ("prefill_t2048_q4k", 160), ("stack30_t256_mixed", 256)])
+def test_layer_paths_vs_port_oracle(port, prefill_from, gemm, path, name, T):
+    """Every path, stage by stage (check_stages). mini_mixed at T=1100 puts more than 128 pairs on
+    most experts (several tiles per expert, 16 column blocks per tile on the mid path);
+    decode_t4_mixed and the stack layer mix Q4_K/Q5_0 and IQ2_S/IQ4_NL tiles at the real shapes."""
+    if path == "decode" and T > 160:
+        pytest.skip("the decode path's share of this batch adds nothing over T=160")
+    prefill_from(1 << 30 if path == "decode" else 1)
+    gemm("mid" if path == "mid" else "tcgen05")
     host = host_layer(name)
     x = workload.make_input(workload.CONFIGS[name], n_tokens=T, stream=T + 1)
     out, aux, layer = run_layer(host, x, aux_names=("logits", "ids", "gate_up", "down", "counts", "perm"))
-    assert layer.prefill_path(T) == (path == "prefill")
-    rel, nt, nf = check_stages(port, host, x, out, aux, dispatch=path == "prefill" or T <= 8)
+    assert layer.prefill_path(T) == (path != "decode")
+    assert layer.mid_path(T) == (path == "mid")
+    tokens = np.arange(0, T, 4) if T >= 256 else None
+    rel, nt, nf = check_stages(port, host, x, out, aux, tokens=tokens, dispatch=path != "decode" or T <= 8)
     print(f"{path} {name} T={T}: max-abs / rms = {rel:.2e}; near-tie tokens {nt}, Q8_0-flip tokens {nf}")
 
 
@@ -110,6 +133,7 @@ def test_prefill_full_size(port, prefill_from):
     x = workload.make_input(workload.CONFIGS[name])
     T = x.shape[0]
     prefill_from(1)
+    assert not host_layer_mid(host, T), "T=2048 (128 pairs per expert) runs the tcgen05 GEMMs by default"
     out, aux, layer = run_layer(host, x, aux_names=("logits", "ids", "gate_up", "down", "counts", "offsets",
                                                     "perm"))
     assert layer.launches(T) == 9
@@ -129,9 +153,12 @@ def test_prefill_full_size(port, prefill_from):
     assert np.array_equal(aux["ids"][same], aux_d["ids"][same])
 
 
-def test_prefill_zero_and_small_batches(prefill_from, port):
-    """T=1 and T=2 on the prefill path (tiles of one pair: MMA N = 16 with 15 padding columns)."""
+@pytest.mark.parametrize("kind", ["tcgen05", "mid"])
+def test_prefill_zero_and_small_batches(prefill_from, gemm, port, kind):
+    """T=1 and T=2 on the prefill path (tiles of one pair: MMA N = 16 with 15 padding columns on
+    the tcgen05 path, one column block with 7 absent pairs on the mid path)."""
     prefill_from(1)
+    gemm(kind)
     host = host_layer("mini_mixed")
     for T in (1, 2):
         x = workload.make_input(workload.CONFIGS["mini_mixed"], n_tokens=T, stream=500 + T)
