@@ -181,7 +181,7 @@ PrefillWs carve_prefill(const moeb_layer *L, int T, uint8_t *base) {
     size_t o = 0;
     auto take = [&](size_t n) { size_t at = o; o = align_up(o + n, 256); return base ? base + at : nullptr; };
     w.logits = (float *)take(sizeof(float) * T * E);
-    w.rpart = (float *)take(sizeof(float) * 4 * T * E);
+    w.rpart = (float *)take(sizeof(float) * router_splits(T, (int)E, (int)d) * T * E);
     w.ids = (int32_t *)take(sizeof(int32_t) * P);
     w.w = (float *)take(sizeof(float) * P);
     w.cnt = (int32_t *)take(sizeof(int32_t) * E);

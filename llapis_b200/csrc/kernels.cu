@@ -1968,10 +1968,10 @@ cudaError_t launch_prefill(const PrefillArgs &a, cudaStream_t s, int n_sms) {
         {
             const float *W = a.w_router, *x = a.x;
             float *part = a.rpart;
-            int t = T, ne = E, dd = d, ns = kRtSplit;
+            int t = T, ne = E, dd = d, ns = router_splits(T, E, d);
             void *args[] = {&W, &x, &part, &t, &ne, &dd, &ns};
             e = pf_launch("pf_router_kernel", (const void *)pf_router_kernel,
-                          dim3((T + kRtTok - 1) / kRtTok, kRtSplit, (E + kRtExp - 1) / kRtExp), dim3(256), 0, s, true, args);
+                          dim3((T + kRtTok - 1) / kRtTok, ns, (E + kRtExp - 1) / kRtExp), dim3(256), 0, s, true, args);
             if (e != cudaSuccess) return e;
             if ((e = prof_mark(s, mark++)) != cudaSuccess) return e;
         }
@@ -1980,7 +1980,7 @@ cudaError_t launch_prefill(const PrefillArgs &a, cudaStream_t s, int n_sms) {
             float *lg = a.logits;
             int32_t *ids = a.ids;
             float *w = a.w;
-            int t = T, ne = E, kk = k, ns = kRtSplit;
+            int t = T, ne = E, kk = k, ns = router_splits(T, E, d);
             void *args[] = {&part, &b, &lg, &ids, &w, &t, &ne, &kk, &ns};
             e = pf_launch("pf_topk_kernel", (const void *)pf_topk_kernel, dim3((T + 7) / 8), dim3(256), 0, s, true, args);
             if (e != cudaSuccess) return e;

@@ -143,7 +143,7 @@ struct PrefillArgs {
     Residency res;
     PoolView hot_gu, cold_gu, hot_dn, cold_dn;
     float *logits;              // [T][E]
-    float *rpart;               // [4][T][E] router partial sums (the four K quarters)
+    float *rpart;               // [router_splits][T][E] router partial sums (one per K part)
     int32_t *ids;               // [T][k]
     float *w;                   // [T][k]
     int32_t *cnt, *off;         // [E], [E + 1]
@@ -166,6 +166,18 @@ struct PrefillArgs {
     int32_t mid;                // 1: mid-size path (int8 MMAs on the weight codes; bimg holds its operand images)
     int32_t md_max_cb;          // mid path: bound on the column blocks (P / 8 + max_tiles)
 };
+// K parts of the prefill router GEMM: the smallest divisor s >= 4 of d / 32 (32-wide K chunks) that
+// gives at least one wave of 64-token x 128-expert CTAs on 148 SMs, at most d / 64 (two chunks per CTA)
+MOEB_HD inline int router_splits(int T, int E, int d) {
+    const int nch = d / 32, tiles = ((T + 63) / 64) * ((E + 127) / 128);
+    int best = 4;
+    for (int s = 4; s <= nch / 2; ++s) {
+        if (nch % s) continue;
+        best = s;
+        if (tiles * s >= 148) break;
+    }
+    return best;
+}
 // mid path: operand image bytes (one 8-pair column block of gate_up, the larger of the two kinds)
 MOEB_HD inline size_t md_image_bytes(int P, int E, int d, int nff) {
     const size_t cb = (size_t)(P / 8 + prefill_max_tiles(P, E));

@@ -1006,7 +1006,7 @@ __global__ void __launch_bounds__(256) pf_topk_kernel(const float *part, const f
     for (int i = 0; i < kMaxE / 32; ++i) {
         v[i] = -INFINITY;
         if (i < per) {
-            // the router's K quarters added in order, then the bias (ggml_add after the mul_mat)
+            // the router's K parts added in order, then the bias (ggml_add after the mul_mat)
             const size_t o = (size_t)t * E + lane + 32 * i;
             float l = part[o];
 #pragma unroll
