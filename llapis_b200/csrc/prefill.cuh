@@ -1078,15 +1078,22 @@ __global__ void __launch_bounds__(1024, 1) pf_dispatch_kernel(PfDispatchParams p
     const int per = (P + 31) / 32;
     const int lo = min(P, warp * per), hi = min(P, lo + per);
     const unsigned lt = (1u << lane) - 1u;
-    for (int base = lo; base < hi; base += 32) {
-        const int pi = base + lane;
-        int e = pi < hi ? p.ids[pi] : -1;
-        if (e >= E) { atomicOr(&g_error, ERR_BAD_EXPERT); e = 0; }
-        const bool v = e >= 0;            // a negative id is an absent pair (expert-parallel partial routing)
-        const unsigned act = __ballot_sync(0xffffffffu, v);
-        const unsigned peers = __match_any_sync(0xffffffffu, e) & act;
-        if (v && (peers & lt) == 0) wcnt[warp][e] += __popc(peers);
-        __syncwarp();
+    // eight 32-pair steps per batch: the ids are loaded before any is counted (latency), then the
+    // steps run in pair order
+    for (int base = lo; base < hi; base += 256) {
+        int ev[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) ev[j] = base + 32 * j + lane < hi ? p.ids[base + 32 * j + lane] : -1;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            int e = ev[j];
+            if (e >= E) { atomicOr(&g_error, ERR_BAD_EXPERT); e = 0; }
+            const bool v = e >= 0;        // a negative id is an absent pair (expert-parallel partial routing)
+            const unsigned act = __ballot_sync(0xffffffffu, v);
+            const unsigned peers = __match_any_sync(0xffffffffu, e) & act;
+            if (v && (peers & lt) == 0) wcnt[warp][e] += __popc(peers);
+            __syncwarp();
+        }
     }
     __syncthreads();
     if (tid < E) {
@@ -1149,24 +1156,30 @@ __global__ void __launch_bounds__(1024, 1) pf_dispatch_kernel(PfDispatchParams p
         if (p.off) p.off[E] = off[E];
     }
     __syncthreads();
-    for (int base = lo; base < hi; base += 32) {
-        const int pi = base + lane;
-        int e = pi < hi ? p.ids[pi] : -1;
-        if (e >= E) e = 0;
-        const bool v = e >= 0;
-        const unsigned act = __ballot_sync(0xffffffffu, v);
-        const unsigned peers = __match_any_sync(0xffffffffu, e) & act;
-        const int b0 = v ? wcnt[warp][e] : 0;
-        __syncwarp();
-        if (v) {
-            const int at = b0 + __popc(peers & lt);
-            p.perm[at] = pi;
-            p.pos[pi] = cls[e] >= 0 ? at : -1;
-            if ((peers & lt) == 0) wcnt[warp][e] = b0 + __popc(peers);
-        } else if (pi < hi) {
-            p.pos[pi] = -1;
+    for (int base = lo; base < hi; base += 256) {
+        int ev[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) ev[j] = base + 32 * j + lane < hi ? p.ids[base + 32 * j + lane] : -1;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int pi = base + 32 * j + lane;
+            int e = ev[j];
+            if (e >= E) e = 0;
+            const bool v = e >= 0;
+            const unsigned act = __ballot_sync(0xffffffffu, v);
+            const unsigned peers = __match_any_sync(0xffffffffu, e) & act;
+            const int b0 = v ? wcnt[warp][e] : 0;
+            __syncwarp();
+            if (v) {
+                const int at = b0 + __popc(peers & lt);
+                p.perm[at] = pi;
+                p.pos[pi] = cls[e] >= 0 ? at : -1;
+                if ((peers & lt) == 0) wcnt[warp][e] = b0 + __popc(peers);
+            } else if (pi < hi) {
+                p.pos[pi] = -1;
+            }
+            __syncwarp();
         }
-        __syncwarp();
     }
 }
 
