@@ -129,13 +129,17 @@ int    moeb_layer_forward_routed(const moeb_layer *L, const float *x, int32_t n_
 int32_t moeb_set_prefill_min_tokens(int32_t n_tokens);
 
 /* Sets the bound on the mean routed pairs per expert (top_k x n_tokens / n_expert) below which a
- * batch on the prefill path runs the mid-size kernels instead of the tcgen05 GEMMs (default 48;
+ * batch on the prefill path runs gate_up on the mid-size kernels instead of the tcgen05 GEMM (default 48;
  * values <= 0 leave it unchanged; 1 turns the mid-size kernels off) and returns the previous value.
  * Process-wide. The mid-size kernels stream each routed expert's rows once and multiply the
  * weights' own integer codes (warp-level int8 MMAs) by every 8-pair block of its tokens, so their
  * cost follows the weight bytes, where the tcgen05 path converts every weight element into an
  * fp16 operand. Layers whose shape they do not cover fall back to the tcgen05 path. */
 int32_t moeb_set_mid_max_pairs(int32_t pairs_per_expert);
+
+/* The same bound for the down projection (default 16): the two projections choose their kernels
+ * independently (both hand over the gate_up rows in the same slot-order buffer). */
+int32_t moeb_set_mid_max_pairs_down(int32_t pairs_per_expert);
 
 /* Profiling of the prefill path (no counterpart in the reference): while enabled, every prefill
  * forward on the current device records CUDA events around its nine kernels (router, top-k,

@@ -51,6 +51,7 @@ SIGNATURES = {
     "moeb_layer_forward_static": (C.c_int, [C.POINTER(Layer), C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p]),
     "moeb_set_prefill_min_tokens": (C.c_int32, [C.c_int32]),
     "moeb_set_mid_max_pairs": (C.c_int32, [C.c_int32]),
+    "moeb_set_mid_max_pairs_down": (C.c_int32, [C.c_int32]),
     "moeb_layer_route": (C.c_int, [C.POINTER(Layer), C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p,
                                    C.c_void_p, C.c_size_t, C.c_void_p]),
     "moeb_route_workspace_size": (C.c_size_t, [C.POINTER(Layer), C.c_int32]),

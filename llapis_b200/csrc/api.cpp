@@ -218,13 +218,16 @@ bool use_prefill(const moeb_layer *L, int32_t n_tokens) {
     return n_tokens >= g_prefill_min.load() && prefill_shape_ok(L);
 }
 
-// Prefill-path batches with fewer routed pairs per expert than this run the mid-size kernels.
-std::atomic<int32_t> g_mid_max{48};
+// Prefill-path batches with fewer routed pairs per expert than these run a projection on the
+// mid-size kernels (gate_up, down). Measured: gate_up on the mid-size kernel wins up to ~48 pairs
+// per expert; the down kernel re-streams a tile's weight rows once per 4-block chunk, which loses
+// to the tcgen05 down on skewed routing already at 16 (one stack layer: 178 vs 152 us).
+std::atomic<int32_t> g_mid_max[2] = {{48}, {16}};
 
-bool use_mid(const moeb_layer *L, int32_t n_rows) {
+bool use_mid(const moeb_layer *L, int32_t n_rows, int kind) {
     const long long P = (long long)n_rows * L->top_k;
-    const int32_t m = g_mid_max.load();   // 1: off
-    return m > 1 && P < (long long)m * L->n_expert && mid_shape_ok(L->d_model, L->n_ff, (int)P, L->n_expert);
+    const int32_t m = g_mid_max[kind].load();   // 1: off
+    return m > 1 && P < (long long)m * L->n_expert && mid_shape_ok(kind, L->d_model, L->n_ff, (int)P, L->n_expert);
 }
 
 PoolView pool_view(const moeb_pool &pl, bool gate_up) {
@@ -289,8 +292,14 @@ extern "C" int moeb_prefill_profile_read(float *ms, int32_t n) {
 }
 
 extern "C" int32_t moeb_set_mid_max_pairs(int32_t pairs_per_expert) {
-    const int32_t prev = g_mid_max.load();
-    if (pairs_per_expert > 0) g_mid_max.store(pairs_per_expert);
+    const int32_t prev = g_mid_max[0].load();
+    if (pairs_per_expert > 0) g_mid_max[0].store(pairs_per_expert);
+    return prev;
+}
+
+extern "C" int32_t moeb_set_mid_max_pairs_down(int32_t pairs_per_expert) {
+    const int32_t prev = g_mid_max[1].load();
+    if (pairs_per_expert > 0) g_mid_max[1].store(pairs_per_expert);
     return prev;
 }
 
@@ -345,7 +354,8 @@ static int forward_prefill(const moeb_layer *L, const float *x, int32_t T, float
     a.y = w.y;
     a.out = out;
     a.y_pairs = aux ? aux->down : nullptr;
-    a.mid = use_mid(L, T) ? 1 : 0;
+    a.mid_gu = use_mid(L, T, 0) ? 1 : 0;
+    a.mid_dn = use_mid(L, T, 1) ? 1 : 0;
     a.md_max_cb = P / 8 + w.max_tiles;
     cudaError_t e = launch_prefill(a, s, n_sms);
     if (e != cudaSuccess) return MOEB_ECUDA;   // launch_prefill recorded the failing kernel
@@ -434,7 +444,8 @@ extern "C" int moeb_layer_forward_routed(const moeb_layer *L, const float *x, in
     a.y = w.y;
     a.out = out;
     a.routed = 1;
-    a.mid = use_mid(L, n_rows) ? 1 : 0;
+    a.mid_gu = use_mid(L, n_rows, 0) ? 1 : 0;
+    a.mid_dn = use_mid(L, n_rows, 1) ? 1 : 0;
     a.md_max_cb = n_rows * k / 8 + w.max_tiles;
     cudaError_t e = launch_prefill(a, (cudaStream_t)stream, n_sms);
     if (e != cudaSuccess) return MOEB_ECUDA;

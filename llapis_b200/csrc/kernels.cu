@@ -1950,10 +1950,10 @@ static cudaError_t pf_launch(const char *name, const void *fn, dim3 grid, dim3 b
     return e;
 }
 
-bool mid_shape_ok(int d, int nff, int P, int E) {
-    return d % QK_K == 0 && nff % QK32 == 0 && prefill_max_tiles(P, E) <= kMdMaxTiles &&
-           (P / 8 + prefill_max_tiles(P, E)) / 2 <= kMdMaxUnits && md_layout(0, d, nff).n_slots >= 2 &&
-           md_layout(1, d, nff).n_slots >= 2;
+bool mid_shape_ok(int kind, int d, int nff, int P, int E) {
+    const int tiles = prefill_max_tiles(P, E);
+    return d % QK_K == 0 && nff % QK32 == 0 && tiles <= kMdMaxTiles &&
+           P / (8 * md_chunk(kind)) + tiles <= kMdMaxUnits && md_layout(kind, d, nff).n_slots >= 2;
 }
 
 cudaError_t launch_prefill(const PrefillArgs &a, cudaStream_t s, int n_sms) {
@@ -2014,13 +2014,25 @@ cudaError_t launch_prefill(const PrefillArgs &a, cudaStream_t s, int n_sms) {
         if (e != cudaSuccess) return e;
         if ((e = prof_mark(s, mark++)) != cudaSuccess) return e;
     }
-    if (a.mid) {
-        // mid-size batches: operand image, gate_up, GeGLU + Q8_0, down (mid.cuh)
-        const size_t smem_gu = (size_t)md_layout(0, d, a.nff).total, smem_dn = (size_t)md_layout(1, d, a.nff).total;
+    // gate_up and down each run the mid-size kernels (mid.cuh) or the tcgen05 kernels; both write the
+    // gate_up rows to hbuf in slot order, so the two choices are independent
+    MdParams m{};
+    m.T = T; m.E = E; m.d = d; m.k = k; m.nff = a.nff;
+    m.tiles = a.tiles; m.n_tiles = a.n_tiles; m.perm = a.perm; m.img = a.bimg;
+    if (a.mid_gu || a.mid_dn) {
         // opt in once at the largest size any layer shape may ask for
         e = smem_optin((const void *)md_kernel<0>, 227 * 1024, optin, 2);
         if (e == cudaSuccess) e = smem_optin((const void *)md_kernel<1>, 227 * 1024, optin, 3);
         if (e != cudaSuccess) return e;
+    }
+    PfParams p{};
+    p.T = T; p.E = E; p.d = d; p.k = k; p.nff = a.nff;
+    p.gu[0] = a.hot_gu; p.gu[1] = a.cold_gu; p.dn[0] = a.hot_dn; p.dn[1] = a.cold_dn;
+    p.perm = a.perm; p.tiles = a.tiles; p.n_tiles = a.n_tiles;
+    p.xq8 = a.xq8; p.xd = a.xd; p.xbs = a.xbs;
+    p.bimg = a.bimg; p.dxt = a.dxt; p.hbuf = a.hbuf; p.dimg = a.dimg; p.h = a.h; p.y = a.y;
+    void *pargs[] = {&p};
+    if (a.mid_gu) {
         {
             const PfTile *tl = a.tiles;
             const int32_t *nt = a.n_tiles, *perm = a.perm;
@@ -2035,16 +2047,23 @@ cudaError_t launch_prefill(const PrefillArgs &a, cudaStream_t s, int n_sms) {
             if (e != cudaSuccess) return e;
             if ((e = prof_mark(s, mark++)) != cudaSuccess) return e;
         }
-        MdParams m{};
-        m.T = T; m.E = E; m.d = d; m.k = k; m.nff = a.nff;
-        m.tiles = a.tiles; m.n_tiles = a.n_tiles; m.perm = a.perm; m.img = a.bimg;
         m.pv[0] = a.hot_gu; m.pv[1] = a.cold_gu; m.out = a.hbuf;
-        {
-            void *args[] = {&m};
-            e = pf_launch("md_kernel<0>", (const void *)md_kernel<0>, dim3(n_sms), dim3(kMdThreads), smem_gu, s, true, args);
-            if (e != cudaSuccess) return e;
-            if ((e = prof_mark(s, mark++)) != cudaSuccess) return e;
-        }
+        void *args[] = {&m};
+        e = pf_launch("md_kernel<0>", (const void *)md_kernel<0>, dim3(n_sms), dim3(kMdThreads),
+                      (size_t)md_layout(0, d, a.nff).total, s, true, args);
+        if (e != cudaSuccess) return e;
+        if ((e = prof_mark(s, mark++)) != cudaSuccess) return e;
+    } else {
+        e = pf_launch("pf_gather_kernel", (const void *)pf_gather_kernel, dim3(a.max_tiles, d / QK_K), dim3(256), 0, s,
+                      true, pargs);
+        if (e != cudaSuccess) return e;
+        if ((e = prof_mark(s, mark++)) != cudaSuccess) return e;
+        e = pf_launch("pf_gate_up_kernel", (const void *)pf_gate_up_kernel, dim3(n_sms), dim3(kPfThreads), sizeof(GuSmem), s,
+                      true, pargs);
+        if (e != cudaSuccess) return e;
+        if ((e = prof_mark(s, mark++)) != cudaSuccess) return e;
+    }
+    if (a.mid_dn) {
         {
             const PfTile *tl = a.tiles;
             const int32_t *nt = a.n_tiles, *perm = a.perm;
@@ -2059,39 +2078,20 @@ cudaError_t launch_prefill(const PrefillArgs &a, cudaStream_t s, int n_sms) {
             if ((e = prof_mark(s, mark++)) != cudaSuccess) return e;
         }
         m.pv[0] = a.hot_dn; m.pv[1] = a.cold_dn; m.out = a.y;
-        {
-            void *args[] = {&m};
-            e = pf_launch("md_kernel<1>", (const void *)md_kernel<1>, dim3(n_sms), dim3(kMdThreads), smem_dn, s, true, args);
-            if (e != cudaSuccess) return e;
-            if ((e = prof_mark(s, mark++)) != cudaSuccess) return e;
-        }
+        void *args[] = {&m};
+        e = pf_launch("md_kernel<1>", (const void *)md_kernel<1>, dim3(n_sms), dim3(kMdThreads),
+                      (size_t)md_layout(1, d, a.nff).total, s, true, args);
+        if (e != cudaSuccess) return e;
+        if ((e = prof_mark(s, mark++)) != cudaSuccess) return e;
     } else {
-        PfParams p{};
-        p.T = T; p.E = E; p.d = d; p.k = k; p.nff = a.nff;
-        p.gu[0] = a.hot_gu; p.gu[1] = a.cold_gu; p.dn[0] = a.hot_dn; p.dn[1] = a.cold_dn;
-        p.perm = a.perm; p.tiles = a.tiles; p.n_tiles = a.n_tiles;
-        p.xq8 = a.xq8; p.xd = a.xd; p.xbs = a.xbs;
-        p.bimg = a.bimg; p.dxt = a.dxt; p.hbuf = a.hbuf; p.dimg = a.dimg; p.h = a.h; p.y = a.y;
-        {
-            void *args[] = {&p};
-            e = pf_launch("pf_gather_kernel", (const void *)pf_gather_kernel, dim3(a.max_tiles, d / QK_K), dim3(256), 0, s,
-                          true, args);
-            if (e != cudaSuccess) return e;
-            if ((e = prof_mark(s, mark++)) != cudaSuccess) return e;
-        }
-        {
-            void *args[] = {&p};
-            e = pf_launch("pf_gate_up_kernel", (const void *)pf_gate_up_kernel, dim3(n_sms), dim3(kPfThreads), sizeof(GuSmem), s, true, args);
-            if (e != cudaSuccess) return e;
-            if ((e = prof_mark(s, mark++)) != cudaSuccess) return e;
-            e = pf_launch("pf_geglu_kernel", (const void *)pf_geglu_kernel, dim3(a.max_tiles, a.nff / 32), dim3(256), 0, s,
-                          true, args);
-            if (e != cudaSuccess) return e;
-            if ((e = prof_mark(s, mark++)) != cudaSuccess) return e;
-            e = pf_launch("pf_down_kernel", (const void *)pf_down_kernel, dim3(n_sms), dim3(kDnThreads), sizeof(DnSmem), s, true, args);
-            if (e != cudaSuccess) return e;
-            if ((e = prof_mark(s, mark++)) != cudaSuccess) return e;
-        }
+        e = pf_launch("pf_geglu_kernel", (const void *)pf_geglu_kernel, dim3(a.max_tiles, a.nff / 32), dim3(256), 0, s,
+                      true, pargs);
+        if (e != cudaSuccess) return e;
+        if ((e = prof_mark(s, mark++)) != cudaSuccess) return e;
+        e = pf_launch("pf_down_kernel", (const void *)pf_down_kernel, dim3(n_sms), dim3(kDnThreads), sizeof(DnSmem), s, true,
+                      pargs);
+        if (e != cudaSuccess) return e;
+        if ((e = prof_mark(s, mark++)) != cudaSuccess) return e;
     }
     {
         const float *y = a.y, *w = a.w;

@@ -163,7 +163,8 @@ struct PrefillArgs {
     float *out;                 // [T][d]
     float *y_pairs;             // optional [P][d] down outputs, pair order
     int32_t routed;             // 1: ids / w are given (the router and top-k kernels are skipped)
-    int32_t mid;                // 1: mid-size path (int8 MMAs on the weight codes; bimg holds its operand images)
+    int32_t mid_gu, mid_dn;     // 1: that projection runs the mid-size kernels (int8 MMAs on the weight codes;
+                                // bimg holds their operand images), 0: the tcgen05 kernels
     int32_t md_max_cb;          // mid path: bound on the column blocks (P / 8 + max_tiles)
 };
 // K parts of the prefill router GEMM: the smallest divisor s >= 4 of d / 32 (32-wide K chunks) that
@@ -188,8 +189,9 @@ MOEB_HD inline size_t md_image_bytes(int P, int E, int d, int nff) {
 cudaError_t launch_route(const float *w_router, const float *b_router, const float *x, int T, int E, int d, int k,
                          float *part, float *logits, int32_t *ids, float *w, cudaStream_t s);
 cudaError_t launch_prefill(const PrefillArgs &a, cudaStream_t s, int n_sms);
-// whether the mid-size kernels cover this shape (shared memory, tile count) for P routed pairs
-bool mid_shape_ok(int d, int nff, int P, int E);
+// whether the mid-size kernel of a projection (0 gate_up, 1 down) covers this shape (shared
+// memory, tile and unit counts) for P routed pairs
+bool mid_shape_ok(int kind, int d, int nff, int P, int E);
 // router, top-k, dispatch, activation quantisation, gather, gate_up, GeGLU, down, combine
 constexpr int kPrefillKernels = 9;
 void prefill_profile_enable(bool on);

@@ -113,15 +113,19 @@ class MoELayer:
         shape_ok = h.n_ff % 64 == 0 and h.d_model % 128 == 0 and h.d_model // 256 <= 16 and h.n_ff // 32 <= 32
         return shape_ok and n_tokens >= int(capi.lib().moeb_set_prefill_min_tokens(0))
 
-    def mid_path(self, n_tokens: int) -> bool:
-        """Whether a prefill-path forward of n_tokens runs the mid-size kernels (int8 MMAs on the
-        weight codes) rather than the tcgen05 GEMMs: fewer routed pairs per expert than the
-        library's bound (moeb_set_mid_max_pairs) and a covered shape."""
+    def mid_path(self, n_tokens: int, kind: int = 0) -> bool:
+        """Whether a prefill-path forward of n_tokens runs projection `kind` (0 gate_up, 1 down) on the
+        mid-size kernels (int8 MMAs on the weight codes) rather than the tcgen05 GEMM: fewer routed
+        pairs per expert than the library's bound (moeb_set_mid_max_pairs / _down) and a covered
+        shape (tile and work-unit counts, mirrored from the library)."""
         h = self.host
         P = n_tokens * h.top_k
-        m = int(capi.lib().moeb_set_mid_max_pairs(0))   # 1: off
-        return (self.prefill_path(n_tokens) and m > 1 and P < m * h.n_expert
-                and h.d_model % 256 == 0 and h.n_ff % 32 == 0 and P // 128 + h.n_expert + 1 <= 512)
+        lib = capi.lib()
+        m = int(lib.moeb_set_mid_max_pairs(0) if kind == 0 else lib.moeb_set_mid_max_pairs_down(0))   # 1: off
+        tiles = P // 128 + h.n_expert + 1
+        chunk = 2 if kind == 0 else 4
+        return (self.prefill_path(n_tokens) and m > 1 and P < m * h.n_expert and h.d_model % 256 == 0
+                and h.n_ff % 32 == 0 and tiles <= 512 and P // (8 * chunk) + tiles <= 1024)
 
     def launches(self, n_tokens: int) -> int:
         """Kernels one forward of n_tokens launches: nine on the prefill path, else one cooperative

@@ -25,9 +25,14 @@ def gemm():
     """Selects the prefill path's GEMMs for one test ("mid": int8 MMAs on the weight codes;
     "tcgen05": the converted-operand tensor-core GEMMs) and restores the threshold afterwards."""
     lib = capi.lib()
-    prev = lib.moeb_set_mid_max_pairs(0)
-    yield lambda kind: lib.moeb_set_mid_max_pairs(1 << 30 if kind == "mid" else 1)
-    lib.moeb_set_mid_max_pairs(prev)
+    prev = lib.moeb_set_mid_max_pairs(0), lib.moeb_set_mid_max_pairs_down(0)
+
+    def select(kind):
+        lib.moeb_set_mid_max_pairs(1 << 30 if kind in ("mid", "mid_gate_up") else 1)
+        lib.moeb_set_mid_max_pairs_down(1 << 30 if kind in ("mid", "mid_down") else 1)
+    yield select
+    lib.moeb_set_mid_max_pairs(prev[0])
+    lib.moeb_set_mid_max_pairs_down(prev[1])
 
 
 @pytest.mark.parametrize("kind", ["tcgen05", "mid"])
@@ -52,8 +57,9 @@ def test_prefill_mini_vs_reference_fixture(golden, prefill_from, gemm, kind):
 
 
 def host_layer_mid(host, T):
-    m = int(capi.lib().moeb_set_mid_max_pairs(0))
-    return m > 1 and T * host.top_k < m * host.n_expert
+    lib = capi.lib()
+    return any(m > 1 and T * host.top_k < m * host.n_expert
+               for m in (int(lib.moeb_set_mid_max_pairs(0)), int(lib.moeb_set_mid_max_pairs_down(0))))
 
 
 def q80_flips(port, want_act, cond_act):
@@ -117,10 +123,25 @@ def test_layer_paths_vs_port_oracle(port, prefill_from, gemm, path, name, T):
     x = workload.make_input(workload.CONFIGS[name], n_tokens=T, stream=T + 1)
     out, aux, layer = run_layer(host, x, aux_names=("logits", "ids", "gate_up", "down", "counts", "perm"))
     assert layer.prefill_path(T) == (path != "decode")
-    assert layer.mid_path(T) == (path == "mid")
+    assert layer.mid_path(T, 0) == (path == "mid") and layer.mid_path(T, 1) == (path == "mid")
     tokens = np.arange(0, T, 4) if T >= 256 else None
     rel, nt, nf = check_stages(port, host, x, out, aux, tokens=tokens, dispatch=path != "decode" or T <= 8)
     print(f"{path} {name} T={T}: max-abs / rms = {rel:.2e}; near-tie tokens {nt}, Q8_0-flip tokens {nf}")
+
+
+@pytest.mark.parametrize("mix", ["mid_gate_up", "mid_down"])
+@pytest.mark.parametrize("name,T", [("prefill_t2048_q4k", 160), ("stack30_t256_mixed", 256)])
+def test_mixed_gemm_paths(port, prefill_from, gemm, mix, name, T):
+    """One projection on the mid-size kernels, the other on tcgen05: the two hand over the gate_up
+    rows in the same slot-order buffer (and share the operand-image buffer in turn)."""
+    prefill_from(1)
+    gemm(mix)
+    host = host_layer(name)
+    x = workload.make_input(workload.CONFIGS[name], n_tokens=T, stream=T + 3)
+    out, aux, layer = run_layer(host, x, aux_names=("logits", "ids", "gate_up", "down", "counts", "perm"))
+    assert layer.mid_path(T, 0) == (mix == "mid_gate_up") and layer.mid_path(T, 1) == (mix == "mid_down")
+    rel, nt, nf = check_stages(port, host, x, out, aux, tokens=np.arange(0, T, 4))
+    print(f"{mix} {name} T={T}: max-abs / rms = {rel:.2e}; near-tie tokens {nt}, Q8_0-flip tokens {nf}")
 
 
 def test_prefill_full_size(port, prefill_from):
