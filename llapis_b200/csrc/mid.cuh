@@ -387,6 +387,17 @@ __device__ __forceinline__ void md_down(const uint8_t *stage, int rb, int nb, in
     }
 }
 
+#ifdef MOEB_TRACE
+// per CTA (first 64), per stage of group 0: claimed, data ready, computed, reduced; per unit: start, chunk ready
+__device__ unsigned long long g_mdtrace[2][64][64][4];
+__device__ unsigned long long g_mdutrace[2][64][8][2];
+#define MDTRACE(it, f) do { if (blockIdx.x < 64 && (it) < 64 && lane == 0 && warp == 0) g_mdtrace[KIND][blockIdx.x][it][f] = clock64(); } while (0)
+#define MDUTRACE(u, f) do { if (blockIdx.x < 64 && (u) < 8 && lane == 0 && warp == 0) g_mdutrace[KIND][blockIdx.x][u][f] = clock64(); } while (0)
+#else
+#define MDTRACE(it, f) do { } while (0)
+#define MDUTRACE(u, f) do { } while (0)
+#endif
+
 template <int KIND>
 __global__ void __launch_bounds__(kMdThreads, 1) md_kernel(MdParams p) {
     constexpr int CH = MdCfg<KIND>::kChunk, PS = 8 * CH + 1;
@@ -467,7 +478,9 @@ __global__ void __launch_bounds__(kMdThreads, 1) md_kernel(MdParams p) {
             __syncwarp();   // the whole warp reaches the next unit's CTA barrier together
             continue;
         }
+        MDUTRACE(u - u_lo, 0);
         if (ok && !mbar_wait(bfull, (uint32_t)((u - u_lo) & 1))) ok = false;
+        MDUTRACE(u - u_lo, 1);
         const PoolView &pv = p.pv[sh.cls[t] == 0 ? 0 : 1];
         const int rb = (int)row_bytes(pv.type, d_in), n = sh.n[t];
         const float post = (KIND == 1 && pv.scale) ? pv.scale[sh.widx[t]] : 1.f;
@@ -476,8 +489,10 @@ __global__ void __launch_bounds__(kMdThreads, 1) md_kernel(MdParams p) {
             group_sync(grp);
             const int it = sh.claim[grp][m & 1];
             if (it >= su1) break;
+            MDTRACE(it, 0);
             const int slot = it % L.n_slots;
             if (ok && !mbar_wait(&full[slot], (uint32_t)((it / L.n_slots) & 1))) ok = false;
+            MDTRACE(it, 1);
             const StagePlan st = stage_plan(S0 + it, g0, g1, gpe, spe, sg);
             const uint8_t *stage = slots + slot * L.slot_cap;
             float acc[CH][4];
@@ -493,6 +508,7 @@ __global__ void __launch_bounds__(kMdThreads, 1) md_kernel(MdParams p) {
                     md_down<CH>(stage, rb, d_in / QK32, wg, pv.type, kv, atile, bchunk, cbb, nc, acc);
                 }
             }
+            MDTRACE(it, 2);
             // this warp's partial tile: [row][col] with col = 8 q + (column within the block)
             const int g = lane >> 2, c = lane & 3;
 #pragma unroll
@@ -518,6 +534,7 @@ __global__ void __launch_bounds__(kMdThreads, 1) md_kernel(MdParams p) {
                 }
             }
             group_sync(grp);   // the partial tiles are free again
+            MDTRACE(it, 3);
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
         }

@@ -1009,8 +1009,15 @@ __global__ void __launch_bounds__(256) pf_topk_kernel(const float *part, const f
             // the router's K parts added in order, then the bias (ggml_add after the mul_mat)
             const size_t o = (size_t)t * E + lane + 32 * i;
             float l = part[o];
+            // eight parts' loads in flight before they are added (in order)
+            for (int sp0 = 1; sp0 < nsplit; sp0 += 8) {
+                float pv[8];
 #pragma unroll
-            for (int sp = 1; sp < nsplit; ++sp) l = __fadd_rn(l, part[(size_t)sp * T * E + o]);
+                for (int q = 0; q < 8; ++q) pv[q] = sp0 + q < nsplit ? part[(size_t)(sp0 + q) * T * E + o] : 0.f;
+#pragma unroll
+                for (int q = 0; q < 8; ++q)
+                    if (sp0 + q < nsplit) l = __fadd_rn(l, pv[q]);
+            }
             if (bias) l = __fadd_rn(l, bias[lane + 32 * i]);
             logits[o] = l;
             v[i] = l;
