@@ -385,7 +385,7 @@ def run_stack(args, cfg):
         "config": {"workload": cfg.name, "n_tokens": T, "layers": cfg.n_layers, "d_model": cfg.d_model,
                    "n_expert": cfg.n_expert, "top_k": cfg.top_k, "hot_experts": len(cfg.hot), "parallelism": "single",
                    "l2": f"inputs larger than L2 ({cfg.n_layers} layers of weights streamed per step)",
-                   "path": "prefill (tcgen05 grouped GEMMs)" if layers[0].prefill_path(T) else "decode (fused)",
+                   "path": path_label(layers[0], T),
                    "ms_per_layer": avg_ms / cfg.n_layers},
         "e2e": {"value": T * args.steps / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": int(x_host.nbytes),
                 "d2h_bytes_per_step": int(x_host.nbytes)},
@@ -400,6 +400,14 @@ def run_stack(args, cfg):
     }
     print(json.dumps(line))
     return 0
+
+
+def path_label(layer, T):
+    """Which kernels a forward of T tokens runs (decode, or the prefill path's per-projection GEMMs)."""
+    if not layer.prefill_path(T):
+        return "decode (fused kernel)"
+    kinds = ["mid-size int8 MMAs" if layer.mid_path(T, kind) else "tcgen05" for kind in (0, 1)]
+    return f"prefill path: gate_up {kinds[0]}, down {kinds[1]}"
 
 
 def _free_port():
@@ -585,7 +593,7 @@ def main():
                        "n_expert": cfg.n_expert, "top_k": cfg.top_k, "hot_experts": len(cfg.hot),
                        "parallelism": f"replicas{world}" if world > 1 else "single",
                        "l2": "flushed between steps (256 MiB write, not timed)",
-                       "path": "prefill (tcgen05 grouped GEMMs)" if prefill else "decode (fused GEMV kernel)",
+                       "path": path_label(layer, T),
                        "cuda_graph": graph is not None, "unique_experts": int(np.unique(ids.cpu().numpy()).size)},
             "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": int(x_host.nbytes),
                     "d2h_bytes_per_step": int(x_host.nbytes)},
