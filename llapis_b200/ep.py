@@ -16,8 +16,9 @@ This mirrors the reference's single-GPU arithmetic except for the final order of
 reference adds all k weighted outputs in slot order, here the slot-ordered partial sums of each
 rank are added in rank order (a difference of float rounding only).
 
-The data path is four collectives (counts, rows + metadata out, partials back); the bookkeeping
-between them (which rows go where) is a handful of device-side index operations.
+The data path is three collectives (counts, rows with their ids and weights out, partials back)
+with one host synchronisation (the split sizes); the bookkeeping between them (which rows go where)
+is a handful of device-side index operations.
 """
 from __future__ import annotations
 
@@ -41,15 +42,26 @@ def _a2a(out: torch.Tensor, inp: torch.Tensor, out_splits, in_splits, group):
     return out
 
 
-def dispatch_plan(ids: torch.Tensor, n_expert: int, world: int):
-    """For local routing ids [T, k]: the (rank, token) pairs to send, rank-major then token order,
-    the per-rank counts, and each sent row's ids with experts of other ranks masked to -1."""
+def presence(ids: torch.Tensor, n_expert: int, world: int):
+    """[world, T] bool: whether token t has at least one of its top-k experts on rank r, and the
+    per-rank counts (device tensors: no host synchronisation)."""
     T, k = ids.shape
     dest = owner(ids.long(), n_expert, world)                                  # [T, k]
     present = torch.zeros((world, T), dtype=torch.bool, device=ids.device)
     present[dest.t().reshape(-1), torch.arange(T, device=ids.device).repeat(k)] = True
-    r_idx, t_idx = present.nonzero(as_tuple=True)                              # rank-major, tokens ascending
-    counts = present.sum(dim=1)
+    return dest, present, present.sum(dim=1)
+
+
+def dispatch_plan(ids: torch.Tensor, n_expert: int, world: int, n_sent: int | None = None):
+    """For local routing ids [T, k]: the (rank, token) pairs to send, rank-major then token order,
+    the per-rank counts, and each sent row's ids with experts of other ranks masked to -1. With
+    n_sent (the total, already known on the host) the compaction needs no host synchronisation."""
+    dest, present, counts = presence(ids, n_expert, world)
+    if n_sent is None:
+        r_idx, t_idx = present.nonzero(as_tuple=True)                          # rank-major, tokens ascending
+    else:
+        nz = torch.nonzero_static(present, size=n_sent)
+        r_idx, t_idx = nz[:, 0], nz[:, 1]
     sent_ids = torch.where(dest[t_idx] == r_idx[:, None], ids[t_idx], torch.full_like(ids[t_idx], -1))
     return r_idx, t_idx, counts, sent_ids
 
@@ -75,22 +87,24 @@ class EPMoE:
                    lambda rows, ids, w: layer.forward_routed(rows, ids, w), group)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        G, d, dev = self.world, x.shape[1], x.device
+        G, d, k, dev = self.world, x.shape[1], self.k, x.device
         ids, w = self.route_fn(x)
-        r_idx, t_idx, counts, sent_ids = dispatch_plan(ids, self.E, G)
-        sent_w = torch.where(sent_ids >= 0, w[t_idx], torch.zeros_like(w[t_idx]))
-        sent_x = x[t_idx].contiguous()
-        # counts, then rows + metadata
+        _, _, counts = presence(ids, self.E, G)
+        # counts, then the one host synchronisation of the step: both sides' split sizes
         recv_counts = torch.empty_like(counts)
         _a2a(recv_counts, counts, None, None, self.group)
-        in_splits, out_splits = counts.tolist(), recv_counts.tolist()
+        both = torch.stack([counts, recv_counts]).tolist()
+        in_splits, out_splits = both[0], both[1]
         n_recv = int(sum(out_splits))
-        recv_x = torch.empty((n_recv, d), dtype=x.dtype, device=dev)
-        recv_ids = torch.empty((n_recv, self.k), dtype=torch.int32, device=dev)
-        recv_w = torch.empty((n_recv, self.k), dtype=torch.float32, device=dev)
-        _a2a(recv_x, sent_x, out_splits, in_splits, self.group)
-        _a2a(recv_ids, sent_ids.to(torch.int32).contiguous(), out_splits, in_splits, self.group)
-        _a2a(recv_w, sent_w.contiguous(), out_splits, in_splits, self.group)
+        r_idx, t_idx, _, sent_ids = dispatch_plan(ids, self.E, G, n_sent=int(sum(in_splits)))
+        sent_w = torch.where(sent_ids >= 0, w[t_idx], torch.zeros_like(w[t_idx]))
+        # one message per row: the f32 row, its k ids (bit-cast) and its k weights
+        sent = torch.cat([x[t_idx].float(), sent_ids.to(torch.int32).view(torch.float32), sent_w.float()], dim=1)
+        recv = torch.empty((n_recv, d + 2 * k), dtype=torch.float32, device=dev)
+        _a2a(recv, sent.contiguous(), out_splits, in_splits, self.group)
+        recv_x = recv[:, :d].to(x.dtype).contiguous()
+        recv_ids = recv[:, d:d + k].contiguous().view(torch.int32)
+        recv_w = recv[:, d + k:].contiguous()
         # the local experts' weighted sums per received row
         partial = self.experts_fn(recv_x, recv_ids, recv_w) if n_recv else torch.empty((0, d), dtype=x.dtype,
                                                                                           device=dev)
