@@ -1097,6 +1097,7 @@ __global__ void __launch_bounds__(1024, 1) pf_dispatch_kernel(PfDispatchParams p
             if (e >= E) { atomicOr(&g_error, ERR_BAD_EXPERT); e = 0; }
             const bool v = e >= 0;        // a negative id is an absent pair (expert-parallel partial routing)
             const unsigned act = __ballot_sync(0xffffffffu, v);
+            if (act == 0u) continue;      // a step of absent pairs only (warp-uniform)
             const unsigned peers = __match_any_sync(0xffffffffu, e) & act;
             if (v && (peers & lt) == 0) wcnt[warp][e] += __popc(peers);
             __syncwarp();
@@ -1174,6 +1175,10 @@ __global__ void __launch_bounds__(1024, 1) pf_dispatch_kernel(PfDispatchParams p
             if (e >= E) e = 0;
             const bool v = e >= 0;
             const unsigned act = __ballot_sync(0xffffffffu, v);
+            if (act == 0u) {              // a step of absent pairs only (warp-uniform)
+                if (pi < hi) p.pos[pi] = -1;
+                continue;
+            }
             const unsigned peers = __match_any_sync(0xffffffffu, e) & act;
             const int b0 = v ? wcnt[warp][e] : 0;
             __syncwarp();

@@ -6,7 +6,7 @@ shard of the batch. One forward:
   1. route the local tokens (replicated router: moeb_layer_route);
   2. dispatch: for every (token, rank) pair with at least one of the token's top-k experts on that
      rank, send the token's row once, with its k expert ids (-1 where the expert lives elsewhere)
-     and routing weights -- all-to-all-v of the counts, then of rows, ids and weights;
+     and routing weights -- one all-to-all of fixed-size blocks;
   3. each rank runs the expert half on what it received (moeb_layer_forward_routed), which sums
      its own experts' weighted outputs per row in slot order;
   4. combine: all-to-all-v of those partial rows back to their source rank, which adds them in
@@ -16,9 +16,10 @@ This mirrors the reference's single-GPU arithmetic except for the final order of
 reference adds all k weighted outputs in slot order, here the slot-ordered partial sums of each
 rank are added in rank order (a difference of float rounding only).
 
-The data path is three collectives (counts, rows with their ids and weights out, partials back)
-with one host synchronisation (the split sizes); the bookkeeping between them (which rows go where)
-is a handful of device-side index operations.
+The data path is two collectives of fixed size (rows with their ids and weights out, partial rows
+back): each rank sends every rank a block of T rows, its own rows first and absent rows (ids all -1)
+after them, so no split sizes cross to the host and a step needs no host synchronisation. The
+bookkeeping (which rows go where) is a handful of device-side index operations.
 """
 from __future__ import annotations
 
@@ -88,36 +89,39 @@ class EPMoE:
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         G, d, k, dev = self.world, x.shape[1], self.k, x.device
+        T = x.shape[0]
         ids, w = self.route_fn(x)
-        _, _, counts = presence(ids, self.E, G)
-        # counts, then the one host synchronisation of the step: both sides' split sizes
-        recv_counts = torch.empty_like(counts)
-        _a2a(recv_counts, counts, None, None, self.group)
-        both = torch.stack([counts, recv_counts]).tolist()
-        in_splits, out_splits = both[0], both[1]
-        n_recv = int(sum(out_splits))
-        r_idx, t_idx, _, sent_ids = dispatch_plan(ids, self.E, G, n_sent=int(sum(in_splits)))
-        sent_w = torch.where(sent_ids >= 0, w[t_idx], torch.zeros_like(w[t_idx]))
-        # one message per row: the f32 row, its k ids (bit-cast) and its k weights
-        sent = torch.cat([x[t_idx].float(), sent_ids.to(torch.int32).view(torch.float32), sent_w.float()], dim=1)
-        recv = torch.empty((n_recv, d + 2 * k), dtype=torch.float32, device=dev)
-        _a2a(recv, sent.contiguous(), out_splits, in_splits, self.group)
+        dest, present, _ = presence(ids, self.E, G)                        # [T, k], [G, T]
+        # Fixed-capacity messages: each rank gets a block of T rows (its rows first, in token order,
+        # then absent rows with every id -1), so the exchange needs no split sizes on the host and
+        # the step runs without any host synchronisation.
+        pos = torch.cumsum(present.to(torch.int32), dim=1) - 1             # slot of token t in rank r's block
+        base = torch.arange(G, device=dev, dtype=torch.int64)[:, None] * T
+        dump = G * T                                                       # one spare row takes the absent pairs
+        idx = torch.where(present, base + pos.long(), torch.full_like(base + pos.long(), dump)).reshape(-1)
+        mine = dest.t()[:, :, None] == torch.arange(G, device=dev)[None, None, :]   # [k, T, G]
+        mine = mine.permute(2, 1, 0)                                                 # [G, T, k]
+        sids = torch.where(mine, ids[None].expand(G, T, k), torch.full((G, T, k), -1, dtype=ids.dtype, device=dev))
+        sw = torch.where(mine, w[None].expand(G, T, k), torch.zeros((G, T, k), dtype=w.dtype, device=dev))
+        rows = torch.cat([x.float()[None].expand(G, T, d), sids.to(torch.int32).view(torch.float32), sw.float()],
+                         dim=2).reshape(G * T, d + 2 * k)
+        sent = torch.empty((G * T + 1, d + 2 * k), dtype=torch.float32, device=dev)
+        sent[:G * T, d:d + k] = torch.full((), -1, dtype=torch.int32, device=dev).view(torch.float32)  # absent ids
+        sent.index_put_((idx,), rows)   # absent pairs all land in the spare row
+        recv = torch.empty((G * T, d + 2 * k), dtype=torch.float32, device=dev)
+        _a2a(recv, sent[:G * T], None, None, self.group)
         recv_x = recv[:, :d].to(x.dtype).contiguous()
         recv_ids = recv[:, d:d + k].contiguous().view(torch.int32)
         recv_w = recv[:, d + k:].contiguous()
-        # the local experts' weighted sums per received row
-        partial = self.experts_fn(recv_x, recv_ids, recv_w) if n_recv else torch.empty((0, d), dtype=x.dtype,
-                                                                                          device=dev)
-        back = torch.empty((int(sum(in_splits)), d), dtype=x.dtype, device=dev)
-        _a2a(back, partial.contiguous(), in_splits, out_splits, self.group)
-        # combine in rank order (the sent rows are rank-major)
+        # the local experts' weighted sums per received row (absent rows give zeros)
+        partial = self.experts_fn(recv_x, recv_ids, recv_w)
+        back = torch.empty((G * T, d), dtype=x.dtype, device=dev)
+        _a2a(back, partial.contiguous(), None, None, self.group)
+        # combine in rank order
         out = torch.zeros_like(x)
-        start = 0
         for r in range(G):
-            n = in_splits[r]
-            if n:
-                out.index_add_(0, t_idx[start:start + n], back[start:start + n])
-            start += n
+            got = back[(r * T + pos[r].clamp(min=0)).long()]
+            out += torch.where(present[r][:, None], got, torch.zeros_like(got))
         return out
 
     __call__ = forward

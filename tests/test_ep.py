@@ -57,8 +57,13 @@ def _worker(rank, world, port, skew):
 
         def experts_fn(rows, ids, w):
             assert all(int(e) in mine for e in ids.reshape(-1).tolist() if e >= 0), "row routed to a foreign expert"
-            assert bool((ids >= 0).any(dim=1).all()), "a row with no local expert was sent here"
-            seen.append(rows.shape[0])
+            # fixed-size blocks: each source sends T_LOCAL rows, its present rows first, then absent ones
+            assert rows.shape[0] == world * T_LOCAL
+            has = (ids >= 0).any(dim=1).reshape(world, T_LOCAL)
+            for blk in has:
+                n = int(blk.sum())
+                assert bool(blk[:n].all()) and not bool(blk[n:].any()), "present rows must lead their block"
+            seen.append(int(has.sum()))
             out = torch.zeros_like(rows)
             for j in range(K):
                 for r in range(rows.shape[0]):
@@ -72,7 +77,7 @@ def _worker(rank, world, port, skew):
         want = _dense(x, ids, w)
         torch.testing.assert_close(out, want, rtol=1e-5, atol=1e-6)
         if skew and rank == 1:
-            assert not seen, "rank 1 owns no routed expert and must receive no rows"
+            assert seen == [0], "rank 1 owns no routed expert and must receive only absent rows"
     finally:
         dist.destroy_process_group()
 
