@@ -16,9 +16,10 @@ This mirrors the reference's single-GPU arithmetic except for the final order of
 reference adds all k weighted outputs in slot order, here the slot-ordered partial sums of each
 rank are added in rank order (a difference of float rounding only).
 
-The data path is two collectives of fixed size (rows with their ids and weights out, partial rows
-back): each rank sends every rank a block of T rows, its own rows first and absent rows (ids all -1)
-after them, so no split sizes cross to the host and a step needs no host synchronisation. The
+The data path is collectives of fixed size (rows out, with a small message of their ids and
+weights, and partial rows back): each rank sends every rank a block of T rows, its own rows first
+and absent rows (ids all -1) after them, so no split sizes cross to the host and a step needs no
+host synchronisation. The
 bookkeeping (which rows go where) is a handful of device-side index operations.
 """
 from __future__ import annotations
@@ -103,16 +104,20 @@ class EPMoE:
         mine = mine.permute(2, 1, 0)                                                 # [G, T, k]
         sids = torch.where(mine, ids[None].expand(G, T, k), torch.full((G, T, k), -1, dtype=ids.dtype, device=dev))
         sw = torch.where(mine, w[None].expand(G, T, k), torch.zeros((G, T, k), dtype=w.dtype, device=dev))
-        rows = torch.cat([x.float()[None].expand(G, T, d), sids.to(torch.int32).view(torch.float32), sw.float()],
-                         dim=2).reshape(G * T, d + 2 * k)
-        sent = torch.empty((G * T + 1, d + 2 * k), dtype=torch.float32, device=dev)
-        sent[:G * T, d:d + k] = torch.full((), -1, dtype=torch.int32, device=dev).view(torch.float32)  # absent ids
-        sent.index_put_((idx,), rows)   # absent pairs all land in the spare row
-        recv = torch.empty((G * T, d + 2 * k), dtype=torch.float32, device=dev)
-        _a2a(recv, sent[:G * T], None, None, self.group)
-        recv_x = recv[:, :d].to(x.dtype).contiguous()
-        recv_ids = recv[:, d:d + k].contiguous().view(torch.int32)
-        recv_w = recv[:, d + k:].contiguous()
+        # rows: gathered straight into the send buffer through the inverse of idx (absent rows repeat
+        # token 0; their ids are all -1, so nothing reads them); ids and weights: a small second message
+        inv = torch.zeros(G * T + 1, dtype=torch.int64, device=dev)
+        inv.index_put_((idx,), torch.arange(T, device=dev).repeat(G))
+        sent_x = x.index_select(0, inv[:G * T])
+        meta = torch.empty((G * T + 1, 2 * k), dtype=torch.float32, device=dev)
+        meta[:G * T, :k] = torch.full((), -1, dtype=torch.int32, device=dev).view(torch.float32)   # absent ids
+        meta.index_put_((idx,), torch.cat([sids.to(torch.int32).view(torch.float32), sw.float()], dim=2).reshape(G * T, 2 * k))
+        recv_x = torch.empty((G * T, d), dtype=x.dtype, device=dev)
+        recv_meta = torch.empty((G * T, 2 * k), dtype=torch.float32, device=dev)
+        _a2a(recv_x, sent_x, None, None, self.group)
+        _a2a(recv_meta, meta[:G * T], None, None, self.group)
+        recv_ids = recv_meta[:, :k].contiguous().view(torch.int32)
+        recv_w = recv_meta[:, k:].contiguous()
         # the local experts' weighted sums per received row (absent rows give zeros)
         partial = self.experts_fn(recv_x, recv_ids, recv_w)
         back = torch.empty((G * T, d), dtype=x.dtype, device=dev)
