@@ -183,7 +183,7 @@ __device__ __forceinline__ void md_q4k(const uint8_t *stage, uint32_t stage_s, i
     const uint32_t a_row = stage_s + (uint32_t)(((lane & 7) + 8 * (am & 1)) * rb + 16 * (am >> 1) + 16);
     const uint8_t *r0 = stage + (size_t)g * rb, *r1 = stage + (size_t)(g + 8) * rb;
     const uint32_t M = 0x0f0f0f0fu;
-#pragma unroll 2
+#pragma unroll 1
     for (int sb = wg; sb < nsb; sb += 4) {
         const uint4 h0 = *reinterpret_cast<const uint4 *>(r0 + sb * B_Q4_K);
         const uint4 h1 = *reinterpret_cast<const uint4 *>(r1 + sb * B_Q4_K);

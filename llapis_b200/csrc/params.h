@@ -168,11 +168,12 @@ struct PrefillArgs {
     int32_t md_max_cb;          // mid path: bound on the column blocks (P / 8 + max_tiles)
 };
 // K parts of the prefill router GEMM: the smallest divisor s >= 4 of d / 32 (32-wide K chunks) that
-// gives at least one wave of 64-token x 128-expert CTAs on 148 SMs, at most d / 64 (two chunks per CTA)
+// gives at least one wave of 64-token x 128-expert CTAs on 148 SMs, at most d / 128 (four chunks per
+// CTA: the top-k kernel adds the parts in order, so more parts cost more there)
 MOEB_HD inline int router_splits(int T, int E, int d) {
     const int nch = d / 32, tiles = ((T + 63) / 64) * ((E + 127) / 128);
     int best = 4;
-    for (int s = 4; s <= nch / 2; ++s) {
+    for (int s = 4; s <= nch / 4; ++s) {
         if (nch % s) continue;
         best = s;
         if (tiles * s >= 148) break;

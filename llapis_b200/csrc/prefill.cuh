@@ -926,7 +926,9 @@ __global__ void __launch_bounds__(256) pf_router_kernel(const float *W, const fl
     pdl_launch_dependents();
     const int t0 = blockIdx.x * kRtTok, e0 = blockIdx.z * kRtExp, split = blockIdx.y, tid = threadIdx.x;
     const int kq = d / nsplit, kbeg = split * kq, nch = kq / kRtK;
-    const int eg = tid & 15, tg = tid >> 4;           // experts 8eg..8eg+7, tokens 4tg..4tg+3
+    // experts 8eg..8eg+7, tokens 4tg..4tg+3; tokens vary along a half-warp, so a warp's reads of
+    // the expert rows are broadcasts and its reads of the token rows are 256 contiguous bytes
+    const int tg = tid & 15, eg = tid >> 4;
     float acc[8][4];
 #pragma unroll
     for (int i = 0; i < 8; ++i)
@@ -984,10 +986,11 @@ __global__ void __launch_bounds__(256) pf_router_kernel(const float *W, const fl
     for (int j = 0; j < 4; ++j) {
         const int t = t0 + 4 * tg + j;
         if (t >= T) continue;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const int e = e0 + 8 * eg + i;
-            if (e < E) pp[(size_t)t * E + e] = acc[i][j];
+        const int e = e0 + 8 * eg;   // E is a multiple of 32: the 8 experts are all present or all absent
+        if (e < E) {
+            float4 *dst = reinterpret_cast<float4 *>(pp + (size_t)t * E + e);
+            dst[0] = make_float4(acc[0][j], acc[1][j], acc[2][j], acc[3][j]);
+            dst[1] = make_float4(acc[4][j], acc[5][j], acc[6][j], acc[7][j]);
         }
     }
 }
@@ -1009,15 +1012,8 @@ __global__ void __launch_bounds__(256) pf_topk_kernel(const float *part, const f
             // the router's K parts added in order, then the bias (ggml_add after the mul_mat)
             const size_t o = (size_t)t * E + lane + 32 * i;
             float l = part[o];
-            // eight parts' loads in flight before they are added (in order)
-            for (int sp0 = 1; sp0 < nsplit; sp0 += 8) {
-                float pv[8];
 #pragma unroll
-                for (int q = 0; q < 8; ++q) pv[q] = sp0 + q < nsplit ? part[(size_t)(sp0 + q) * T * E + o] : 0.f;
-#pragma unroll
-                for (int q = 0; q < 8; ++q)
-                    if (sp0 + q < nsplit) l = __fadd_rn(l, pv[q]);
-            }
+            for (int sp = 1; sp < nsplit; ++sp) l = __fadd_rn(l, part[(size_t)sp * T * E + o]);
             if (bias) l = __fadd_rn(l, bias[lane + 32 * i]);
             logits[o] = l;
             v[i] = l;
