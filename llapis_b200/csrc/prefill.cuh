@@ -1069,6 +1069,20 @@ struct PfDispatchParams {
 
 // One CTA of 1024 threads. Warp w owns the contiguous pair range [w*per, (w+1)*per); counting
 // and placement walk it 32 pairs at a time in pair order, so the permutation is stable.
+// Lanes of the warp holding the same value as this lane (0 <= e < 256 for every lane that counts):
+// the AND over the value's 8 bits of that bit's ballot or its complement. Equivalent to
+// __match_any_sync, which runs far slower on this part (it dominated the dispatch kernel's time).
+__device__ __forceinline__ unsigned same_lanes(int e) {
+    unsigned m = 0xffffffffu;
+#pragma unroll
+    for (int b = 0; b < 8; ++b) {
+        const bool on = (e >> b) & 1;
+        const unsigned bb = __ballot_sync(0xffffffffu, on);
+        m &= on ? bb : ~bb;
+    }
+    return m;
+}
+
 __global__ void __launch_bounds__(1024, 1) pf_dispatch_kernel(PfDispatchParams p) {
     __shared__ int32_t wcnt[32][kMaxE];
     __shared__ int32_t cnt[kMaxE], off[kMaxE + 1], tpre[kMaxE + 1], cls[kMaxE], widx[kMaxE];
@@ -1094,7 +1108,7 @@ __global__ void __launch_bounds__(1024, 1) pf_dispatch_kernel(PfDispatchParams p
             const bool v = e >= 0;        // a negative id is an absent pair (expert-parallel partial routing)
             const unsigned act = __ballot_sync(0xffffffffu, v);
             if (act == 0u) continue;      // a step of absent pairs only (warp-uniform)
-            const unsigned peers = __match_any_sync(0xffffffffu, e) & act;
+            const unsigned peers = same_lanes(e) & act;
             if (v && (peers & lt) == 0) wcnt[warp][e] += __popc(peers);
             __syncwarp();
         }
@@ -1175,7 +1189,7 @@ __global__ void __launch_bounds__(1024, 1) pf_dispatch_kernel(PfDispatchParams p
                 if (pi < hi) p.pos[pi] = -1;
                 continue;
             }
-            const unsigned peers = __match_any_sync(0xffffffffu, e) & act;
+            const unsigned peers = same_lanes(e) & act;
             const int b0 = v ? wcnt[warp][e] : 0;
             __syncwarp();
             if (v) {
