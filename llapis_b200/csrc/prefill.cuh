@@ -792,7 +792,6 @@ __global__ void __launch_bounds__(kDnThreads, 1) pf_down_kernel(PfParams p) {
 // semantics), written as fp16 into the tile's down operand image, the scale into the tile's
 // per-row table. A kernel of its own: the table lookups are random, and here the table stays
 // in L2 instead of being evicted by the weight stream of the GEMMs.
-constexpr int kGegluRows = 4;   // pairs a warp keeps in flight
 __global__ void __launch_bounds__(256) pf_geglu_kernel(PfParams p) {
     pdl_wait();
     pdl_launch_dependents();
@@ -800,51 +799,58 @@ __global__ void __launch_bounds__(256) pf_geglu_kernel(PfParams p) {
     if (ti >= *p.n_tiles) return;
     const PfTile tl = p.tiles[ti];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nff = p.nff;
-    const int st = blk >> 1, kcol = 4 * (blk & 1) + (lane >> 3);
+    // lane (row rr, quarter qk): 8 consecutive values K = 32 blk + 8 qk .. + 7 of the block for pair
+    // row rr of the warp's 8 rows; the block's Q8_0 amax is a max over the 4 lanes of the row, and
+    // every lane writes whole 16-byte core-matrix rows of the hi and lo operand images
+    const int rr = lane >> 2, qk = lane & 3;
+    const int st = blk >> 1, kcol = 4 * (blk & 1) + qk;
     uint8_t *dimg = p.dimg + ((size_t)ti * (nff / 64) + st) * 2 * kPfDnImageBytes;
-    for (int c0 = warp * kGegluRows; c0 < tl.n; c0 += 8 * kGegluRows) {
-        float g[kGegluRows], u[kGegluRows];
-        uint16_t tv[kGegluRows];
+    for (int c = warp * 8 + rr; c - rr < tl.n; c += 64) {   // warp-uniform bound: the row block starts in the tile
+        const bool valid = c < tl.n;
+        float g[8], u[8];
+        const float *hr = p.hbuf + (size_t)(tl.slot0 + (valid ? c : 0)) * 2 * nff + 32 * blk + 8 * qk;
+        const float4 g0 = *reinterpret_cast<const float4 *>(hr), g1 = *reinterpret_cast<const float4 *>(hr + 4);
+        const float4 u0 = *reinterpret_cast<const float4 *>(hr + nff), u1 = *reinterpret_cast<const float4 *>(hr + nff + 4);
+        g[0] = g0.x; g[1] = g0.y; g[2] = g0.z; g[3] = g0.w; g[4] = g1.x; g[5] = g1.y; g[6] = g1.z; g[7] = g1.w;
+        u[0] = u0.x; u[1] = u0.y; u[2] = u0.z; u[3] = u0.w; u[4] = u1.x; u[5] = u1.y; u[6] = u1.z; u[7] = u1.w;
+        uint16_t tv[8];
 #pragma unroll
-        for (int j = 0; j < kGegluRows; ++j) {
-            const int c = min(c0 + j, tl.n - 1);
-            const float *hr = p.hbuf + (size_t)(tl.slot0 + c) * 2 * nff + 32 * blk + lane;
-            g[j] = hr[0];
-            u[j] = hr[nff];
-        }
+        for (int j = 0; j < 8; ++j) tv[j] = g_gelu_f16[f2h_rn(g[j])];
+        float a[8], m = 0.f;
 #pragma unroll
-        for (int j = 0; j < kGegluRows; ++j) tv[j] = g_gelu_f16[f2h_rn(g[j])];
-        float a[kGegluRows], m[kGegluRows];
-#pragma unroll
-        for (int j = 0; j < kGegluRows; ++j) {
+        for (int j = 0; j < 8; ++j) {
             a[j] = g[j] <= -10.0f ? 0.0f : (g[j] >= 10.0f ? __fmul_rn(g[j], u[j]) : __fmul_rn(h2f(tv[j]), u[j]));
-            m[j] = fabsf(a[j]);
+            m = fmaxf(m, fabsf(a[j]));
         }
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+        if (!valid) continue;
+        const float dd = h2f(f2h_rn(__fdiv_rn(m, 127.f)));
+        const float id = m != 0.f ? __fdiv_rn(127.f, m) : 0.f;
+        // the down operand is dx * q8 (exact in f32: an fp16 scale times a 7-bit integer), split into
+        // fp16 hi + lo, both exact: the value and its parts are multiples of 2^-24 with at most 18
+        // significant bits
+        uint32_t hw[4], lw[4];
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-            for (int j = 0; j < kGegluRows; ++j) m[j] = fmaxf(m[j], __shfl_xor_sync(0xffffffffu, m[j], o));
-#pragma unroll
-        for (int j = 0; j < kGegluRows; ++j) {
-            const int c = c0 + j;
-            if (c >= tl.n) break;   // warp-uniform
-            const float dd = h2f(f2h_rn(__fdiv_rn(m[j], 127.f)));
-            const float id = m[j] != 0.f ? __fdiv_rn(127.f, m[j]) : 0.f;
-            // the down operand is dx * q8 (exact in f32: an fp16 scale times a 7-bit integer), split
-            // into fp16 hi + lo, both exact: the value and its parts are multiples of 2^-24 with at
-            // most 18 significant bits
-            const float v = __fmul_rn(dd, (float)__float2int_rn(__fmul_rn(a[j], id)));
-            if (fabsf(v) > 65504.f) atomicOr(&g_error, ERR_RANGE);
-            const __half hi = __float2half_rn(v);
-            const __half lo = __float2half_rn(__fsub_rn(v, __half2float(hi)));
-            const uint32_t off = canon_off(c, kcol, kDnKc) + 2 * (lane & 7);
-            *reinterpret_cast<__half *>(dimg + off) = hi;
-            *reinterpret_cast<__half *>(dimg + kPfDnImageBytes + off) = lo;
-            if (p.h) {
-                float *hp = p.h + (size_t)p.perm[tl.slot0 + c] * 2 * nff + 32 * blk + lane;
-                hp[0] = g[j];
-                hp[nff] = u[j];
-            }
+        for (int j = 0; j < 8; j += 2) {
+            const float v0 = __fmul_rn(dd, (float)__float2int_rn(__fmul_rn(a[j], id)));
+            const float v1 = __fmul_rn(dd, (float)__float2int_rn(__fmul_rn(a[j + 1], id)));
+            if (fabsf(v0) > 65504.f || fabsf(v1) > 65504.f) atomicOr(&g_error, ERR_RANGE);
+            const __half h0 = __float2half_rn(v0), h1 = __float2half_rn(v1);
+            const __half l0 = __float2half_rn(__fsub_rn(v0, __half2float(h0)));
+            const __half l1 = __float2half_rn(__fsub_rn(v1, __half2float(h1)));
+            hw[j / 2] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
+            lw[j / 2] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
+        }
+        const uint32_t off = canon_off(c, kcol, kDnKc);
+        *reinterpret_cast<uint4 *>(dimg + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        *reinterpret_cast<uint4 *>(dimg + kPfDnImageBytes + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+        if (p.h) {
+            float *hp = p.h + (size_t)p.perm[tl.slot0 + c] * 2 * nff + 32 * blk + 8 * qk;
+            *reinterpret_cast<float4 *>(hp) = g0;
+            *reinterpret_cast<float4 *>(hp + 4) = g1;
+            *reinterpret_cast<float4 *>(hp + nff) = u0;
+            *reinterpret_cast<float4 *>(hp + nff + 4) = u1;
         }
     }
 }
