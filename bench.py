@@ -42,6 +42,9 @@ def parse():
     p.add_argument("--no-graph", action="store_true", help="launch eagerly instead of replaying a CUDA graph")
     p.add_argument("--cpu-sample-s", type=float, default=15.0, help="CPU baseline budget (seconds)")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--block-norms", action="store_true",
+                   help="the whole Gemma-4 MoE block: pre / router-input / output rms_norms fused into the layer "
+                        "(moeb_layer_forward_gemma4); input is the block input (attn_out)")
     return p.parse_args()
 
 
@@ -133,22 +136,29 @@ def reference_spec(host, x):
                      s_cold=host.s_cold)
 
 
-def time_reference(host, x, warmup, steps, budget_s, n_threads=None):
-    """The reference CPU path (oracle/_ref: the ggml-cpu MUL_MAT_ID graph of build_moe_ffn) on this
-    host's cores: `warmup` untimed forwards, then up to `steps` timed ones within `budget_s`."""
+def time_reference(host, x, warmup, steps, budget_s, n_threads=None, norms=None):
+    """The reference CPU path (oracle/_ref: the ggml-cpu MUL_MAT_ID graph of build_moe_ffn; with
+    norms, also the block's rms_norm / scale / mul nodes) on this host's cores: `warmup` untimed
+    forwards, then up to `steps` timed ones within `budget_s`."""
     from oracle import Ref, ref_available
     if not ref_available():
         return None
     r = Ref()
     spec = reference_spec(host, x)
     nt = n_threads or os.cpu_count() or 1
+
+    def fwd():
+        if norms is not None:
+            r.gemma4_block(spec, norms, n_threads=nt, want=())
+        else:
+            r.moe_layer(spec, n_threads=nt, want=())
     for _ in range(max(1, warmup)):
-        r.moe_layer(spec, n_threads=nt, want=())
+        fwd()
     times = []
     t_end = time.perf_counter() + budget_s
     while len(times) < max(1, steps) and (len(times) < 2 or time.perf_counter() < t_end):
         t0 = time.perf_counter()
-        r.moe_layer(spec, n_threads=nt, want=())
+        fwd()
         times.append(time.perf_counter() - t0)
     value = x.shape[0] * len(times) / sum(times)
     return {"value": value, "unit": "tokens/s", "cores": nt, "kind": "reference",
@@ -163,8 +173,10 @@ def run_reference(args):
     from llapis_b200 import workload
     cfg = workload.CONFIGS[args.config]
     host = workload.build_layer(cfg)
-    x = workload.make_input(cfg)[:256]   # bounded sample: at most 256 tokens per step (tokens/s is per token)
-    cb = time_reference(host, x, args.warmup, args.steps, budget_s=120.0)
+    norms = workload.block_norms(cfg) if args.block_norms else None
+    # bounded sample: at most 256 tokens per step (tokens/s is per token)
+    x = (workload.make_block_input(cfg) if norms else workload.make_input(cfg))[:256]
+    cb = time_reference(host, x, args.warmup, args.steps, budget_s=120.0, norms=norms)
     if cb is None:
         print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref (reference ggml-cpu build) missing"}))
         return 0
@@ -173,7 +185,7 @@ def run_reference(args):
             "warmup": args.warmup, "ms_per_step": cb["ms_per_forward"], "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "q8 int dot / f32", "data": "synthetic (seeded)",
             "config": {"workload": cfg.name, "n_tokens": cfg.n_tokens, "layers": 1,
-                       "sample_tokens_per_step": int(x.shape[0])},
+                       "sample_tokens_per_step": int(x.shape[0]), "block_norms": norms is not None},
             "impl": "reference", "cpu_baseline": cb,
             "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line))
@@ -422,6 +434,8 @@ def main():
     if args.impl == "reference":
         return run_reference(args)
     from llapis_b200 import workload as _wl
+    if args.block_norms and (args.config.startswith("ep_") or _wl.CONFIGS[args.config].n_layers > 1):
+        raise SystemExit("--block-norms covers the single-layer configs")
     if args.config.startswith("ep_"):
         return run_ep(args, _wl.CONFIGS[args.config])
     if _wl.CONFIGS[args.config].n_layers > 1:
@@ -442,8 +456,9 @@ def main():
 
     cfg = workload.CONFIGS[args.config]
     host = workload.build_layer(cfg)
-    layer = MoELayer(host, dev)
-    x_host = workload.make_input(cfg)
+    norms = workload.block_norms(cfg) if args.block_norms else None
+    layer = MoELayer(host, dev, norms=norms)
+    x_host = workload.make_block_input(cfg) if norms else workload.make_input(cfg)
     T = x_host.shape[0]
     x = torch.from_numpy(x_host).to(dev)
     out = torch.empty_like(x)
@@ -581,7 +596,7 @@ def main():
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         # a bounded sample: at most 256 tokens of the batch (the CPU cost per token is flat in T)
-        cpu = time_reference(host, x_host[:256], 1, 1000, args.cpu_sample_s)
+        cpu = time_reference(host, x_host[:256], 1, 1000, args.cpu_sample_s, norms=norms)
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
@@ -593,7 +608,7 @@ def main():
                        "n_expert": cfg.n_expert, "top_k": cfg.top_k, "hot_experts": len(cfg.hot),
                        "parallelism": f"replicas{world}" if world > 1 else "single",
                        "l2": "flushed between steps (256 MiB write, not timed)",
-                       "path": path_label(layer, T),
+                       "path": path_label(layer, T), "block_norms": norms is not None,
                        "cuda_graph": graph is not None, "unique_experts": int(np.unique(ids.cpu().numpy()).size)},
             "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": int(x_host.nbytes),
                     "d2h_bytes_per_step": int(x_host.nbytes)},

@@ -103,6 +103,30 @@ size_t moeb_layer_workspace_size(const moeb_layer *L, int32_t n_tokens);
 int moeb_layer_forward(const moeb_layer *L, const float *x, int32_t n_tokens, float *out,
                        const moeb_layer_aux *aux, void *workspace, size_t workspace_bytes, void *stream);
 
+/* The norms around the Gemma-4 MoE block (third_party/llama/src/models/gemma4.cpp:394-427), device
+ * pointers to f32 [d_model] vectors, 16-byte aligned:
+ *   expert input = rms_norm(x) * pre_norm                      (ffn_pre_norm_2, gemma4.cpp:394-396)
+ *   router input = rms_norm(x) * (1 / sqrtf(d_model)) * router_scale   (ffn_gate_inp_s, :399-402)
+ *   out          = rms_norm(moe(expert input)) * post_norm    (ffn_post_norm_2, :423-425)
+ * rms_norm(v) = v * (1 / sqrt(mean(v^2) + eps)) with ggml_rms_norm's arithmetic. */
+typedef struct moeb_norms {
+    const float *pre_norm;
+    const float *router_scale;
+    const float *post_norm;
+    float        eps;          /* f_norm_rms_eps, >= 0 */
+    int32_t      _pad;
+} moeb_norms;
+
+/* moeb_layer_forward with the Gemma-4 block norms fused in (new; the reference runs them as separate
+ * graph nodes around build_moe_ffn): x is the block input (attn_out), out the normed MoE output
+ * that the host adds to the dense MLP branch. Same paths, workspace size and aux outputs as
+ * moeb_layer_forward (aux->logits are the logits of the router input, aux->gate_up and
+ * aux->down are computed from the expert input; out is after the output norm). The norms add no
+ * launch on the decode path; the prefill path adds one small kernel (the rows' norm scales). */
+int moeb_layer_forward_gemma4(const moeb_layer *L, const moeb_norms *norms, const float *x, int32_t n_tokens,
+                              float *out, const moeb_layer_aux *aux, void *workspace, size_t workspace_bytes,
+                              void *stream);
+
 /* The two halves of the layer, for expert-parallel hosts (new; the reference runs the router and
  * the expert matmuls as separate graph nodes, llama-graph.cpp:1530-1613 and :1689-1848).
  *  moeb_layer_route: router logits (f32 [n_tokens][n_expert], caller memory), top-k ids

@@ -37,6 +37,12 @@ class LayerAux(C.Structure):
     _fields_ = [(n, C.c_void_p) for n in ("logits", "ids", "weights", "counts", "offsets", "perm", "gate_up", "down")]
 
 
+class Norms(C.Structure):
+    """moeb_norms: the Gemma-4 MoE block norms (device pointers to f32 [d_model])."""
+    _fields_ = [("pre_norm", C.c_void_p), ("router_scale", C.c_void_p), ("post_norm", C.c_void_p),
+                ("eps", C.c_float), ("_pad", C.c_int32)]
+
+
 _lib = None
 
 # name -> (restype, argtypes); every symbol include/*.h declares
@@ -48,6 +54,8 @@ SIGNATURES = {
     "moeb_layer_workspace_size": (C.c_size_t, [C.POINTER(Layer), C.c_int32]),
     "moeb_layer_forward": (C.c_int, [C.POINTER(Layer), C.c_void_p, C.c_int32, C.c_void_p, C.POINTER(LayerAux),
                                      C.c_void_p, C.c_size_t, C.c_void_p]),
+    "moeb_layer_forward_gemma4": (C.c_int, [C.POINTER(Layer), C.POINTER(Norms), C.c_void_p, C.c_int32, C.c_void_p,
+                                            C.POINTER(LayerAux), C.c_void_p, C.c_size_t, C.c_void_p]),
     "moeb_layer_forward_static": (C.c_int, [C.POINTER(Layer), C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p]),
     "moeb_set_prefill_min_tokens": (C.c_int32, [C.c_int32]),
     "moeb_set_mid_max_pairs": (C.c_int32, [C.c_int32]),

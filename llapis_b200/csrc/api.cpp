@@ -139,6 +139,7 @@ struct LayerWs {
     float *w;
     uint8_t *qa;
     uint32_t *sync;
+    double *nsum;
     size_t bytes;
 };
 
@@ -158,13 +159,14 @@ LayerWs carve(const moeb_layer *L, int T, uint8_t *base) {
     w.perm = (int32_t *)take(sizeof(int32_t) * P);
     w.qa = take((size_t)P * fused_qa_stride(L->n_ff));
     w.sync = (uint32_t *)take(sizeof(uint32_t) * fused_sync_words(T, L->d_model, L->n_ff));
+    w.nsum = (double *)take(sizeof(double) * T * ((L->d_model + 63) / 64));
     w.bytes = o;
     return w;
 }
 
 // prefill path workspace (whole call at once)
 struct PrefillWs {
-    float *logits, *rpart, *w, *xd, *ad, *y;
+    float *logits, *rpart, *w, *xd, *ad, *y, *nscale;
     int32_t *ids, *cnt, *off, *perm, *pos, *n_tiles;
     PfTile *tiles;
     int8_t *xq8;
@@ -202,6 +204,7 @@ PrefillWs carve_prefill(const moeb_layer *L, int T, uint8_t *base) {
     w.hbuf = (float *)take(sizeof(float) * P * 2 * nff);
     w.dimg = (uint8_t *)take(mt * (nff / 64) * 2 * kPfDnImageBytes);
     w.y = (float *)take(sizeof(float) * P * d);
+    w.nscale = (float *)take(sizeof(float) * T);
     w.bytes = o;
     return w;
 }
@@ -310,7 +313,8 @@ extern "C" int32_t moeb_set_prefill_min_tokens(int32_t n_tokens) {
 }
 
 static int forward_chunks(const moeb_layer *L, const float *x, int32_t n_tokens, float *out,
-                          const moeb_layer_aux *aux, void *workspace, cudaStream_t s, int n_sms);
+                          const moeb_layer_aux *aux, void *workspace, cudaStream_t s, int n_sms,
+                          const NormArgs &nrm = NormArgs{});
 
 // argument checks shared by both paths of the layer forward
 static int check_forward(const moeb_layer *L, const float *x, int32_t n_tokens, float *out, void *workspace,
@@ -332,13 +336,15 @@ static int check_forward(const moeb_layer *L, const float *x, int32_t n_tokens, 
 
 // The prefill path: nine PDL-chained kernels, the expert matmuls on tcgen05 tensor cores.
 static int forward_prefill(const moeb_layer *L, const float *x, int32_t T, float *out, const moeb_layer_aux *aux,
-                           void *workspace, cudaStream_t s, int n_sms) {
+                           void *workspace, cudaStream_t s, int n_sms, const NormArgs &nrm = NormArgs{}) {
     const int d = L->d_model, k = L->top_k, E = L->n_expert, P = T * k;
     PrefillWs w = carve_prefill(L, T, (uint8_t *)workspace);
     PrefillArgs a{};
     a.w_router = L->w_router;
     a.b_router = L->b_router;
     a.x = x;
+    a.nrm = nrm;
+    a.nscale = w.nscale;
     a.T = T; a.E = E; a.d = d; a.k = k; a.nff = L->n_ff;
     a.res = {L->hot.n, L->exp_slot, L->slot_exp, L->slot_state};
     a.hot_gu = pool_view(L->hot, true);
@@ -463,6 +469,24 @@ extern "C" int moeb_layer_forward(const moeb_layer *L, const float *x, int32_t n
     return forward_chunks(L, x, n_tokens, out, aux, workspace, (cudaStream_t)stream, n_sms);
 }
 
+extern "C" int moeb_layer_forward_gemma4(const moeb_layer *L, const moeb_norms *norms, const float *x,
+                                         int32_t n_tokens, float *out, const moeb_layer_aux *aux, void *workspace,
+                                         size_t workspace_bytes, void *stream) {
+    int n_sms = 0;
+    int rc = check_forward(L, x, n_tokens, out, workspace, workspace_bytes,
+                           L ? moeb_layer_workspace_size(L, n_tokens) : 0, &n_sms);
+    if (rc || n_tokens == 0) return rc;
+    if (!norms || !norms->pre_norm || !norms->router_scale || !norms->post_norm)
+        return fail(MOEB_EINVAL, "moeb_layer_forward_gemma4: null norms / pre_norm / router_scale / post_norm");
+    if (!aligned16(norms->pre_norm) || !aligned16(norms->router_scale) || !aligned16(norms->post_norm))
+        return fail(MOEB_EINVAL, "moeb_layer_forward_gemma4: norm vectors must be 16-byte aligned");
+    if (!(norms->eps >= 0.f)) return fail(MOEB_EINVAL, "moeb_layer_forward_gemma4: eps must be >= 0");
+    const NormArgs nrm = {norms->pre_norm, norms->router_scale, norms->post_norm, norms->eps};
+    if (use_prefill(L, n_tokens))
+        return forward_prefill(L, x, n_tokens, out, aux, workspace, (cudaStream_t)stream, n_sms, nrm);
+    return forward_chunks(L, x, n_tokens, out, aux, workspace, (cudaStream_t)stream, n_sms, nrm);
+}
+
 int moeb::layer_forward_chunked(const moeb_layer *L, const float *x, int32_t n_tokens, float *out, void *workspace,
                                 size_t workspace_bytes, void *stream) {
     int n_sms = 0;
@@ -473,7 +497,7 @@ int moeb::layer_forward_chunked(const moeb_layer *L, const float *x, int32_t n_t
 
 // The decode path: one fused cooperative kernel per chunk of up to kFusedTokens tokens.
 static int forward_chunks(const moeb_layer *L, const float *x, int32_t n_tokens, float *out, const moeb_layer_aux *aux,
-                          void *workspace, cudaStream_t s, int n_sms) {
+                          void *workspace, cudaStream_t s, int n_sms, const NormArgs &nrm) {
     const int d = L->d_model, k = L->top_k, E = L->n_expert;
     const Residency res = {L->hot.n, L->exp_slot, L->slot_exp, L->slot_state};
 
@@ -486,6 +510,8 @@ static int forward_chunks(const moeb_layer *L, const float *x, int32_t n_tokens,
         f.w_router = L->w_router;
         f.b_router = L->b_router;
         f.x = x + (size_t)t0 * d;
+        f.nrm = nrm;
+        f.nsum = w.nsum;
         f.T = T;
         f.E = E;
         f.d = d;

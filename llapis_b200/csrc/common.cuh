@@ -138,5 +138,37 @@ __device__ __forceinline__ float warp_max(float v) {
     for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
     return v;
 }
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// ---------------------------------------------------------------- rms_norm (Gemma-4 block norms)
+// ggml_rms_norm (ggml-cpu/ops.cpp:3813-3820): every square rounded to f32, the squares summed in
+// double, mean = sum / n rounded to f32, scale = 1 / sqrt(mean + eps) with the correctly rounded f32
+// square root and division. The double sum's order differs from the reference's sequential one;
+// the f32 mean is the same unless the two sums straddle an f32 rounding boundary (their difference
+// is a few units of 2^-53 relative).
+__device__ __forceinline__ double sq_sum4(float4 v) {
+    return ((double)__fmul_rn(v.x, v.x) + (double)__fmul_rn(v.y, v.y)) +
+           ((double)__fmul_rn(v.z, v.z) + (double)__fmul_rn(v.w, v.w));
+}
+__device__ __forceinline__ float rms_row_scale(double sumsq, int n, float eps) {
+    const float mean = (float)(sumsq / (double)n);
+    return __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(mean, eps)));
+}
+// 1 / sqrtf((float) n_embd) of the router input (gemma4.cpp:400)
+__device__ __forceinline__ float router_input_scale(int d) { return __fdiv_rn(1.f, __fsqrt_rn((float)d)); }
+// router input (x * s) * c * r and expert input (x * s) * w, each product rounded to f32 as the
+// reference's separate rms_norm, scale and mul nodes round them (gemma4.cpp:394-402)
+__device__ __forceinline__ float4 router_input4(float4 x, float s, float c, float4 r) {
+    return make_float4(__fmul_rn(__fmul_rn(__fmul_rn(x.x, s), c), r.x), __fmul_rn(__fmul_rn(__fmul_rn(x.y, s), c), r.y),
+                       __fmul_rn(__fmul_rn(__fmul_rn(x.z, s), c), r.z), __fmul_rn(__fmul_rn(__fmul_rn(x.w, s), c), r.w));
+}
+__device__ __forceinline__ float4 norm_weight4(float4 x, float s, float4 w) {
+    return make_float4(__fmul_rn(__fmul_rn(x.x, s), w.x), __fmul_rn(__fmul_rn(x.y, s), w.y),
+                       __fmul_rn(__fmul_rn(x.z, s), w.z), __fmul_rn(__fmul_rn(x.w, s), w.w));
+}
 
 }  // namespace moeb

@@ -38,10 +38,16 @@ __device__ __forceinline__ Q8KView q8k_view(const uint8_t *row, int nsb) {
 // Q8_K quantisation of one 256-value super-block by one warp (quantize_row_q8_K_ref,
 // ggml-quants.c:2696): the signed value of largest magnitude (first one on ties) sets
 // iscale = -127/max; q = min(127, rne(iscale*x)); d = 1/iscale; bsums over 16 values.
-__device__ void q8k_superblock_warp(const float *x, int8_t *qs, float *d_out, int16_t *bs, int lane) {
+// With w given, the values quantised are the normed (x * s) * w (the Gemma-4 expert input).
+__device__ void q8k_superblock_warp(const float *x, int8_t *qs, float *d_out, int16_t *bs, int lane,
+                                    float nscale = 1.f, const float *w = nullptr) {
     float v[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) v[i] = x[lane * 8 + i];
+    if (w) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(__fmul_rn(v[i], nscale), w[lane * 8 + i]);
+    }
     float amax = 0.f;
     int aidx = 0x7fffffff;
 #pragma unroll
@@ -958,6 +964,8 @@ __device__ __forceinline__ bool grid_barrier_thread(unsigned nblocks) {
 struct FusedParams {
     const float *w_router, *b_router, *x;
     int32_t T, E, d, k, nff;
+    NormArgs nrm;   // Gemma-4 block norms (nrm.pre == nullptr: none)
+    double *nsum;   // [T][ceil(d / 64)] sums of squares of the combined output blocks (norms only)
     Residency res;
     PoolView hot_gu, cold_gu, hot_dn, cold_dn;
     float *logits;
@@ -968,8 +976,8 @@ struct FusedParams {
     float *w_out;
     uint8_t *qa;   // down activations (Q8_0 rows of n_ff) in expert-sorted slot order
     // completion counters, zeroed in phase A: gate_up rows done per (unique expert, 32-row ff block)
-    // [kFusedMaxP][n_ff / 32], finished ff blocks per unique expert [kFusedMaxP], then down rows
-    // done per (token, 64-row block) [T][ceil(d / 64)]
+    // [kFusedMaxP][n_ff / 32], finished ff blocks per unique expert [kFusedMaxP], down rows done per
+    // (token, 64-row block) [T][ceil(d / 64)], then combined output blocks per token [T]
     uint32_t *sync;
 };
 
@@ -989,6 +997,8 @@ struct FusedRoute {
     int32_t claim_gu, claim_dn;      // next unclaimed gate_up / down stage of this CTA
     int32_t claim[kGroups][2];       // each group's current claim (double-buffered by iteration)
     float red[kFusedMaxT][kConsumerWarps + 1];
+    double dred[kFusedMaxT][kConsumerWarps + 1];
+    float nscale[kFusedMaxT];        // rms_norm row scales of the tokens (Gemma-4 block norms)
 };
 
 struct FusedSmem {
@@ -1206,7 +1216,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) fused_decode_kernel(FusedPara
     if (warp == 0) FTRACE(0);
     const int nrb = (d + 63) / 64;
     if (blockIdx.x == 0)
-        for (int i = tid; i < kFusedMaxP * (nff / QK32 + 1) + T * nrb; i += kGemvThreads) p.sync[i] = 0u;
+        for (int i = tid; i < fused_sync_words(T, d, nff); i += kGemvThreads) p.sync[i] = 0u;
     {
         // the GELU table (128 KB) into L2 ahead of the GeGLU step: CTA b takes lines b, b + G, ...
         const char *gt = reinterpret_cast<const char *>(g_gelu_f16);
@@ -1256,21 +1266,57 @@ __global__ void __launch_bounds__(kGemvThreads, 1) fused_decode_kernel(FusedPara
 #pragma unroll
         for (int i = 0; i < MOE_IQ2S_GRID_ROWS / 32; ++i) grid[lane + 32 * i] = g[i];
     }
+    const bool nrm = p.nrm.pre != nullptr;
+    if (nrm) {
+        // Gemma-4 block norms: the rms_norm scales of all T tokens, in every CTA (a logits unit
+        // needs every token's); the same code and summation order everywhere, so all CTAs agree
+        const int n4 = d / 4;
+        double sq[kFusedMaxT];
+#pragma unroll
+        for (int t = 0; t < kFusedMaxT; ++t) sq[t] = 0.0;
+        for (int i = tid; i < n4; i += kGemvThreads) {
+#pragma unroll
+            for (int t = 0; t < kFusedMaxT; ++t)
+                if (t < T) sq[t] += sq_sum4(__ldg(reinterpret_cast<const float4 *>(p.x + (size_t)t * d) + i));
+        }
+#pragma unroll
+        for (int t = 0; t < kFusedMaxT; ++t) {
+            if (t < T) {
+                const double v = warp_sum_d(sq[t]);
+                if (lane == 0) rs.dred[t][warp] = v;
+            }
+        }
+        __syncthreads();
+        if (tid < T) {
+            double v = 0.0;
+            for (int w = 0; w < kConsumerWarps + 1; ++w) v += rs.dred[tid][w];
+            rs.nscale[tid] = rms_row_scale(v, d, p.nrm.eps);
+        }
+        __syncthreads();
+    }
     for (int unit = blockIdx.x; unit < E + T; unit += G) {
         if (unit < E) {
             // logits[t][unit] = W[unit] . x[t] (+ bias): every thread a strided share, then warp and
-            // CTA reductions in a fixed order
+            // CTA reductions in a fixed order. With the block norms, x[t] is the router input
+            // rms_norm(x[t]) / sqrt(d) * router_scale, formed value by value as the loads arrive.
             const int n4 = d / 4;
             const float4 *w4 = reinterpret_cast<const float4 *>(p.w_router + (size_t)unit * d);
-            float part[kFusedMaxT];
+            const float4 *r4 = reinterpret_cast<const float4 *>(p.nrm.router);
+            const float rc = nrm ? router_input_scale(d) : 1.f;
+            float part[kFusedMaxT], ns[kFusedMaxT];
 #pragma unroll
-            for (int t = 0; t < kFusedMaxT; ++t) part[t] = 0.f;
+            for (int t = 0; t < kFusedMaxT; ++t) {
+                part[t] = 0.f;
+                ns[t] = nrm && t < T ? rs.nscale[t] : 1.f;
+            }
             for (int i = tid; i < n4; i += kGemvThreads) {
                 const float4 w = __ldg(w4 + i);
+                const float4 r = nrm ? __ldg(r4 + i) : make_float4(1.f, 1.f, 1.f, 1.f);
 #pragma unroll
                 for (int t = 0; t < kFusedMaxT; ++t) {
                     if (t < T) {
-                        const float4 xv = __ldg(reinterpret_cast<const float4 *>(p.x + (size_t)t * d) + i);
+                        float4 xv = __ldg(reinterpret_cast<const float4 *>(p.x + (size_t)t * d) + i);
+                        if (nrm) xv = router_input4(xv, ns[t], rc, r);
                         part[t] = fmaf(w.x, xv.x, part[t]);
                         part[t] = fmaf(w.y, xv.y, part[t]);
                         part[t] = fmaf(w.z, xv.z, part[t]);
@@ -1299,7 +1345,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) fused_decode_kernel(FusedPara
             for (int sb = warp; sb < nsb; sb += kGemvThreads / 32)
                 q8k_superblock_warp(p.x + (size_t)t * d + sb * 256, reinterpret_cast<int8_t *>(row) + sb * 256,
                                     reinterpret_cast<float *>(row + nsb * 256) + sb,
-                                    reinterpret_cast<int16_t *>(row + nsb * 256 + nsb * 4) + sb * 16, lane);
+                                    reinterpret_cast<int16_t *>(row + nsb * 256 + nsb * 4) + sb * 16, lane,
+                                    nrm ? rs.nscale[t] : 1.f, nrm ? p.nrm.pre + sb * 256 : nullptr);
         }
     }
     __syncthreads();
@@ -1392,6 +1439,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) fused_decode_kernel(FusedPara
         const size_t hpart = (size_t)T * k * 2 * nff;   // stride of the four gate_up partial-sum parts
         const int qas = fused_qa_stride(nff);
         uint32_t *blk_cnt = p.sync, *act_cnt = p.sync + kFusedMaxP * nb, *dn_cnt = act_cnt + kFusedMaxP;
+        uint32_t *tok_cnt = dn_cnt + T * nrb;
         const int grp = warp / kWarpsPerGroup, wg = warp % kWarpsPerGroup;
         uint32_t kv[4];
 #pragma unroll
@@ -1663,12 +1711,34 @@ __global__ void __launch_bounds__(kGemvThreads, 1) fused_decode_kernel(FusedPara
             consumer_sync();
             for (int q = warp; q < n_todo; q += kConsumerWarps) {
                 const int t = todo[1 + 2 * q], rb = todo[2 + 2 * q];
+                double sq = 0.0;
                 for (int rr = lane; rr < min(64, d - rb * 64); rr += 32) {
                     const int row = rb * 64 + rr;
                     float acc = __fmul_rn(__ldcg(p.y + (size_t)(t * k) * d + row), rs.w[t * k]);
                     for (int j = 1; j < k; ++j)
                         acc = __fadd_rn(acc, __fmul_rn(__ldcg(p.y + (size_t)(t * k + j) * d + row), rs.w[t * k + j]));
                     p.out[(size_t)t * d + row] = acc;
+                    sq += (double)__fmul_rn(acc, acc);
+                }
+                if (nrm) {
+                    // the output norm (ffn_post_norm_2): the block's sum of squares, then a count
+                    // per token; the warp that combines the token's last block scales its row
+                    sq = warp_sum_d(sq);
+                    if (lane == 0) p.nsum[t * nrb + rb] = sq;
+                    __threadfence();
+                    __syncwarp();
+                    uint32_t done = 0;
+                    if (lane == 0) done = atomicAdd(&tok_cnt[t], 1u) + 1u;
+                    done = __shfl_sync(0xffffffffu, done, 0);
+                    if (done == (uint32_t)nrb) {
+                        __threadfence();
+                        double tot = 0.0;   // the blocks' sums in block order
+                        for (int b = 0; b < nrb; ++b) tot += __ldcg(p.nsum + t * nrb + b);
+                        const float sc = rms_row_scale(tot, d, p.nrm.eps);
+                        float4 *o4 = reinterpret_cast<float4 *>(p.out + (size_t)t * d);
+                        const float4 *w4 = reinterpret_cast<const float4 *>(p.nrm.post);
+                        for (int i = lane; i < d / 4; i += 32) o4[i] = norm_weight4(__ldcg(o4 + i), sc, __ldg(w4 + i));
+                    }
                 }
             }
         }
@@ -1851,6 +1921,7 @@ size_t fused_smem_bytes(int d, int nff) { return (size_t)fused_layout(d, nff).to
 cudaError_t launch_fused(const FusedArgs &a, cudaStream_t s, int n_sms) {
     FusedParams p{};
     p.w_router = a.w_router; p.b_router = a.b_router; p.x = a.x;
+    p.nrm = a.nrm; p.nsum = a.nsum;
     p.T = a.T; p.E = a.E; p.d = a.d; p.k = a.k; p.nff = a.nff;
     p.res = a.res;
     p.hot_gu = a.hot_gu; p.cold_gu = a.cold_gu; p.hot_dn = a.hot_dn; p.cold_dn = a.cold_dn;
@@ -1964,12 +2035,23 @@ cudaError_t launch_prefill(const PrefillArgs &a, cudaStream_t s, int n_sms) {
     const int T = a.T, E = a.E, d = a.d, k = a.k;
     int mark = 0;
     if ((e = prof_mark(s, mark++)) != cudaSuccess) return e;
+    const bool nrm = a.nrm.pre != nullptr;
+    if (nrm) {   // the Gemma-4 block norms' row scales (timed with the router in the profile)
+        const float *x = a.x;
+        float *ns = a.nscale;
+        int t = T, dd = d;
+        float eps = a.nrm.eps;
+        void *args[] = {&x, &ns, &t, &dd, &eps};
+        e = pf_launch("pf_norm_kernel", (const void *)pf_norm_kernel, dim3((T + 7) / 8), dim3(256), 0, s, true, args);
+        if (e != cudaSuccess) return e;
+    }
     if (!a.routed) {
         {
             const float *W = a.w_router, *x = a.x;
             float *part = a.rpart;
             int t = T, ne = E, dd = d, ns = router_splits(T, E, d);
-            void *args[] = {&W, &x, &part, &t, &ne, &dd, &ns};
+            const float *nsc = nrm ? a.nscale : nullptr, *rsc = a.nrm.router;
+            void *args[] = {&W, &x, &part, &t, &ne, &dd, &ns, &nsc, &rsc};
             e = pf_launch("pf_router_kernel", (const void *)pf_router_kernel,
                           dim3((T + kRtTok - 1) / kRtTok, ns, (E + kRtExp - 1) / kRtExp), dim3(256), 0, s, true, args);
             if (e != cudaSuccess) return e;
@@ -2009,7 +2091,8 @@ cudaError_t launch_prefill(const PrefillArgs &a, cudaStream_t s, int n_sms) {
         float *xd = a.xd;
         int16_t *bs = a.xbs;
         int t = T, dd = d;
-        void *args[] = {&x, &q, &xd, &bs, &t, &dd};
+        const float *nsc = nrm ? a.nscale : nullptr, *pre = a.nrm.pre;
+        void *args[] = {&x, &q, &xd, &bs, &t, &dd, &nsc, &pre};
         e = pf_launch("pf_actq_kernel", (const void *)pf_actq_kernel, dim3((T * (d / QK_K) + 7) / 8), dim3(256), 0, s, true, args);
         if (e != cudaSuccess) return e;
         if ((e = prof_mark(s, mark++)) != cudaSuccess) return e;
@@ -2098,8 +2181,10 @@ cudaError_t launch_prefill(const PrefillArgs &a, cudaStream_t s, int n_sms) {
         const int32_t *pos = a.pos;
         float *out = a.out, *yp = a.y_pairs;
         int t = T, kk = k, dd = d;
-        void *args[] = {&y, &pos, &w, &out, &yp, &t, &kk, &dd};
-        e = pf_launch("pf_combine_kernel", (const void *)pf_combine_kernel, dim3(T), dim3(256), 0, s, true, args);
+        const float *post = nrm ? a.nrm.post : nullptr;
+        float eps = a.nrm.eps;
+        void *args[] = {&y, &pos, &w, &out, &yp, &t, &kk, &dd, &post, &eps};
+        e = pf_launch("pf_combine_kernel", (const void *)pf_combine_kernel, dim3(T), dim3(kCbThreads), 0, s, true, args);
         if (e != cudaSuccess) return e;
     }
     return prof_mark(s, mark++);
@@ -2111,7 +2196,8 @@ cudaError_t launch_route(const float *w_router, const float *b_router, const flo
     // buffer, which the top-k kernel completes in place (bias)
     int t = T, ne = E, dd = d, kk = k, ns = part ? kRtSplit : 1;
     float *dst = part ? part : logits;
-    void *a1[] = {&w_router, &x, &dst, &t, &ne, &dd, &ns};
+    const float *no_norm = nullptr;
+    void *a1[] = {&w_router, &x, &dst, &t, &ne, &dd, &ns, &no_norm, &no_norm};
     cudaError_t e = pf_launch("pf_router_kernel", (const void *)pf_router_kernel,
                               dim3((T + kRtTok - 1) / kRtTok, ns, (E + kRtExp - 1) / kRtExp), dim3(256), 0, s, true, a1);
     if (e != cudaSuccess) return e;

@@ -98,11 +98,23 @@ struct GemvParams {
     int32_t *rc_counts, *rc_hits;
 };
 
+// The norms around the Gemma-4 MoE block (gemma4.cpp:394-427), device pointers to f32 [d]:
+//   expert input  = rms_norm(x) * pre            (ffn_pre_norm_2)
+//   router input  = rms_norm(x) / sqrt(d) * router  (ffn_gate_inp_s)
+//   output        = rms_norm(moe) * post         (ffn_post_norm_2)
+// pre == nullptr: the plain layer (x feeds both the router and the experts, no output norm).
+struct NormArgs {
+    const float *pre, *router, *post;
+    float eps;
+};
+
 // the fused decode layer (one cooperative launch per chunk of <= kFusedTokens tokens)
 constexpr int kFusedTokens = 8;
 struct FusedArgs {
     const float *w_router, *b_router, *x;
     int32_t T, E, d, k, nff;
+    NormArgs nrm;
+    double *nsum;            // [kFusedTokens][ceil(d / 64)] output sums of squares per 64-row block (norms only)
     Residency res;
     PoolView hot_gu, cold_gu, hot_dn, cold_dn;
     float *logits;
@@ -115,9 +127,9 @@ struct FusedArgs {
     uint32_t *sync;          // fused_sync_words(T, d, nff) zero-initialised-by-the-kernel counters
 };
 // counters: gate_up rows per (unique expert, 32-row ff block), finished blocks per unique expert,
-// down rows per (token, 64-row output block)
+// down rows per (token, 64-row output block), combined output blocks per token
 MOEB_HD inline int fused_sync_words(int T, int d, int nff) {
-    return kFusedTokens * kMaxTopK * (nff / 32 + 1) + T * ((d + 63) / 64);
+    return kFusedTokens * kMaxTopK * (nff / 32 + 1) + T * ((d + 63) / 64) + T;
 }
 
 // the prefill path (tcgen05 grouped GEMMs; prefill.cuh)
@@ -140,6 +152,8 @@ constexpr int kPfDnImageBytes = kPrefillTile * 8 * 16;
 struct PrefillArgs {
     const float *w_router, *b_router, *x;
     int32_t T, E, d, k, nff;
+    NormArgs nrm;
+    float *nscale;              // [T] rms_norm row scales of x (norms only)
     Residency res;
     PoolView hot_gu, cold_gu, hot_dn, cold_dn;
     float *logits;              // [T][E]

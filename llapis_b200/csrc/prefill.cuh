@@ -924,8 +924,10 @@ __global__ void __launch_bounds__(256) pf_gather_kernel(PfParams p) {
 // the top-k kernel adds them in order (deterministic); with nsplit = 1, part may be the logits
 // buffer itself (the top-k kernel completes it in place).
 constexpr int kRtTok = 64, kRtExp = 128, kRtK = 32, kRtSplit = 4;
+// With the Gemma-4 block norms (nscale given) the x values become the router input
+// rms_norm(x) / sqrt(d) * router_scale as they are staged.
 __global__ void __launch_bounds__(256) pf_router_kernel(const float *W, const float *x, float *part, int T, int E,
-                                                        int d, int nsplit) {
+                                                        int d, int nsplit, const float *nscale, const float *rscale) {
     __shared__ __align__(16) float ws[kRtK][kRtExp];
     __shared__ __align__(16) float xs[kRtK][kRtTok];
     pdl_wait();
@@ -942,6 +944,13 @@ __global__ void __launch_bounds__(256) pf_router_kernel(const float *W, const fl
         for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
     // global -> register staging: W rows (e fastest across threads) and x rows
     float4 wr[4], xr[2];
+    const float rc = router_input_scale(d);
+    float ns[2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const int t = (tid + 256 * i) & 63;
+        ns[i] = nscale && t0 + t < T ? nscale[t0 + t] : 1.f;
+    }
     auto load = [&](int k0) {
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
@@ -954,6 +963,7 @@ __global__ void __launch_bounds__(256) pf_router_kernel(const float *W, const fl
             const int idx = tid + 256 * i, t = idx & 63, qd = idx >> 6;
             xr[i] = t0 + t < T ? __ldg(reinterpret_cast<const float4 *>(x + (size_t)(t0 + t) * d + k0 + 4 * qd))
                                : make_float4(0.f, 0.f, 0.f, 0.f);
+            if (nscale) xr[i] = router_input4(xr[i], ns[i], rc, __ldg(reinterpret_cast<const float4 *>(rscale + k0 + 4 * qd)));
         }
     };
     auto store = [&]() {
@@ -1212,8 +1222,10 @@ __global__ void __launch_bounds__(1024, 1) pf_dispatch_kernel(PfDispatchParams p
 }
 
 // Q8_K quantisation of every token: one warp per (token, super-block)
+// With the Gemma-4 block norms (nscale given) the values quantised are the expert input
+// rms_norm(x) * pre_norm.
 __global__ void __launch_bounds__(256) pf_actq_kernel(const float *x, int8_t *xq8, float *xd, int16_t *xbs, int T,
-                                                      int d) {
+                                                      int d, const float *nscale, const float *pre) {
     pdl_wait();
     pdl_launch_dependents();
     const int nsb = d / QK_K;
@@ -1221,17 +1233,40 @@ __global__ void __launch_bounds__(256) pf_actq_kernel(const float *x, int8_t *xq
     if (item >= T * nsb) return;
     const int t = item / nsb, sb = item - t * nsb;
     q8k_superblock_warp(x + (size_t)t * d + sb * QK_K, xq8 + (size_t)t * d + sb * QK_K, xd + item, xbs + (size_t)item * 16,
-                        lane);
+                        lane, nscale ? nscale[t] : 1.f, nscale ? pre + sb * QK_K : nullptr);
+}
+
+// rms_norm row scales of x for the Gemma-4 block norms, one warp per token
+__global__ void __launch_bounds__(256) pf_norm_kernel(const float *x, float *nscale, int T, int d, float eps) {
+    pdl_wait();
+    pdl_launch_dependents();
+    const int t = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (t >= T) return;
+    const float4 *x4 = reinterpret_cast<const float4 *>(x + (size_t)t * d);
+    double sq = 0.0;
+#pragma unroll 4
+    for (int i = lane; i < d / 4; i += 32) sq += sq_sum4(__ldg(x4 + i));
+    sq = warp_sum_d(sq);
+    if (lane == 0) nscale[t] = rms_row_scale(sq, d, eps);
 }
 
 // out[t] = ((w0 y0 + w1 y1) + w2 y2) + ...: products rounded, then added in slot order, as the
-// reference's mul + add chain does; optionally copies y to pair order.
-__global__ void __launch_bounds__(256) pf_combine_kernel(const float *y, const int32_t *pos, const float *w, float *out,
-                                                         float *y_pairs, int T, int k, int d) {
+// reference's mul + add chain does; optionally copies y to pair order. With post given (the
+// Gemma-4 ffn_post_norm_2) the row is then rms-normed and multiplied by post.
+constexpr int kCbThreads = 256, kCbPer = kPrefillMaxSb * QK_K / (4 * kCbThreads);
+__global__ void __launch_bounds__(kCbThreads) pf_combine_kernel(const float *y, const int32_t *pos, const float *w,
+                                                                float *out, float *y_pairs, int T, int k, int d,
+                                                                const float *post, float eps) {
+    __shared__ double red[kCbThreads / 32];
     pdl_wait();
     pdl_launch_dependents();
     const int t = blockIdx.x;
-    for (int c = 4 * threadIdx.x; c < d; c += 4 * blockDim.x) {
+    float4 row[kCbPer];
+    double sq = 0.0;
+#pragma unroll
+    for (int it = 0; it < kCbPer; ++it) {
+        const int c = 4 * (threadIdx.x + it * kCbThreads);
+        if (c >= d) break;
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
         for (int j = 0; j < k; ++j) {
             const int sl = pos[(size_t)t * k + j];
@@ -1243,7 +1278,24 @@ __global__ void __launch_bounds__(256) pf_combine_kernel(const float *y, const i
             else acc = make_float4(__fadd_rn(acc.x, pr.x), __fadd_rn(acc.y, pr.y), __fadd_rn(acc.z, pr.z), __fadd_rn(acc.w, pr.w));
             if (y_pairs) *reinterpret_cast<float4 *>(y_pairs + ((size_t)t * k + j) * d + c) = v;
         }
-        *reinterpret_cast<float4 *>(out + (size_t)t * d + c) = acc;
+        row[it] = acc;
+        sq += sq_sum4(acc);
+        if (!post) *reinterpret_cast<float4 *>(out + (size_t)t * d + c) = acc;
+    }
+    if (!post) return;
+    sq = warp_sum_d(sq);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sq;
+    __syncthreads();
+    double tot = 0.0;   // the warps' sums in warp order
+#pragma unroll
+    for (int i = 0; i < kCbThreads / 32; ++i) tot += red[i];
+    const float sc = rms_row_scale(tot, d, eps);
+#pragma unroll
+    for (int it = 0; it < kCbPer; ++it) {
+        const int c = 4 * (threadIdx.x + it * kCbThreads);
+        if (c >= d) break;
+        *reinterpret_cast<float4 *>(out + (size_t)t * d + c) =
+            norm_weight4(row[it], sc, __ldg(reinterpret_cast<const float4 *>(post + c)));
     }
 }
 

@@ -63,6 +63,18 @@ class HostLayer:
                 + self.d_model * capi.row_size(self.cold_type_down, self.n_ff))
 
 
+@dataclass
+class BlockNorms:
+    """The norms around a Gemma-4 MoE block (third_party/llama/src/models/gemma4.cpp:394-427), f32
+    [d_model] each: the experts see rms_norm(x) * pre_norm (ffn_pre_norm_2), the router
+    rms_norm(x) / sqrt(d_model) * router_scale (ffn_gate_inp_s), and the block output is
+    rms_norm(moe) * post_norm (ffn_post_norm_2)."""
+    pre_norm: np.ndarray
+    router_scale: np.ndarray
+    post_norm: np.ndarray
+    eps: float = 1e-6
+
+
 def _dev(a, device):
     return None if a is None else torch.from_numpy(np.ascontiguousarray(a)).to(device)
 
@@ -72,10 +84,12 @@ def _ptr(t):
 
 
 class MoELayer:
-    """One MoE layer resident on a CUDA device."""
+    """One MoE layer resident on a CUDA device. With `norms` the forward is the whole Gemma-4 MoE
+    block (moeb_layer_forward_gemma4): x is the block input and the output is normed."""
 
-    def __init__(self, host: HostLayer, device: str | torch.device = "cuda"):
+    def __init__(self, host: HostLayer, device: str | torch.device = "cuda", norms: BlockNorms | None = None):
         self.host = host
+        self.norms = norms
         self.device = torch.device(device)
         if self.device.index is None:
             self.device = torch.device(self.device.type, torch.cuda.current_device())
@@ -104,6 +118,11 @@ class MoELayer:
                            _ptr(t["cold_gu"]), _ptr(t["cold_down"]), _ptr(t["s_cold"]))
         L.exp_slot, L.slot_exp, L.slot_state = _ptr(t["exp_slot"]), _ptr(t["slot_exp"]), _ptr(t["slot_state"])
         self.c = L
+        self.cn = None
+        if norms is not None:
+            for n in ("pre_norm", "router_scale", "post_norm"):
+                t[n] = _dev(np.asarray(getattr(norms, n), np.float32).reshape(h.d_model), self.device)
+            self.cn = capi.Norms(_ptr(t["pre_norm"]), _ptr(t["router_scale"]), _ptr(t["post_norm"]), float(norms.eps), 0)
         self._ws = None
         self._rws = None
 
@@ -128,11 +147,13 @@ class MoELayer:
                 and h.n_ff % 32 == 0 and tiles <= 512 and P // (8 * chunk) + tiles <= 1024)
 
     def launches(self, n_tokens: int) -> int:
-        """Kernels one forward of n_tokens launches: nine on the prefill path, else one cooperative
-        fused kernel per 8-token chunk."""
+        """Kernels one forward of n_tokens launches: nine on the prefill path (ten with the block
+        norms: their row scales), else one cooperative fused kernel per 8-token chunk."""
         if n_tokens <= 0:
             return 0
-        return 9 if self.prefill_path(n_tokens) else (n_tokens + 7) // 8
+        if self.prefill_path(n_tokens):
+            return 9 + (self.norms is not None)
+        return (n_tokens + 7) // 8
 
     def workspace_bytes(self, n_tokens: int) -> int:
         return int(capi.lib().moeb_layer_workspace_size(C.byref(self.c), n_tokens))
@@ -157,9 +178,13 @@ class MoELayer:
         a = None
         if aux:
             a = capi.LayerAux(*[_ptr(aux.get(n)) for n, _ in capi.LayerAux._fields_])
-        rc = capi.lib().moeb_layer_forward(C.byref(self.c), x.data_ptr(), T, out.data_ptr(),
-                                           C.byref(a) if a is not None else None, ws.data_ptr(), ws.numel(),
-                                           s.cuda_stream)
+        ap = C.byref(a) if a is not None else None
+        if self.cn is not None:
+            rc = capi.lib().moeb_layer_forward_gemma4(C.byref(self.c), C.byref(self.cn), x.data_ptr(), T,
+                                                      out.data_ptr(), ap, ws.data_ptr(), ws.numel(), s.cuda_stream)
+        else:
+            rc = capi.lib().moeb_layer_forward(C.byref(self.c), x.data_ptr(), T, out.data_ptr(), ap, ws.data_ptr(),
+                                               ws.numel(), s.cuda_stream)
         capi.check(rc)
         return out
 

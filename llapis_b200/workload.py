@@ -162,6 +162,27 @@ def make_input(cfg: LayerConfig, n_tokens: int | None = None, stream: int = 0) -
     return x
 
 
+NORM_EPS = 1e-6   # Gemma-4 f_norm_rms_eps
+
+
+def block_norms(cfg: LayerConfig, layer: int = 0):
+    """Seeded Gemma-4 block norm vectors for layer `layer` of cfg: ffn_pre_norm_2, ffn_gate_inp_s and
+    ffn_post_norm_2 as 1 + N(0, 0.1) each (f32 [d_model]), eps 1e-6."""
+    from .layer import BlockNorms
+    d = cfg.d_model
+    v = [np.float32(1.0) + _normal((cfg.seed, layer, 1 << 21, i), (d,), 0.1) for i in range(3)]
+    return BlockNorms(pre_norm=v[0], router_scale=v[1], post_norm=v[2], eps=NORM_EPS)
+
+
+def make_block_input(cfg: LayerConfig, n_tokens: int | None = None, stream: int = 0) -> np.ndarray:
+    """Block input (attn_out, the residual stream) [T, d]: make_input's rows times a per-token
+    magnitude 2^u, u uniform in [0, 4), so the norms' row scales vary over tokens."""
+    x = make_input(cfg, n_tokens, stream)
+    rng = np.random.Generator(np.random.PCG64(np.random.SeedSequence([cfg.seed, 9191, stream])))
+    mag = np.exp2(rng.uniform(0.0, 4.0, (x.shape[0], 1))).astype(np.float32)
+    return (x * mag).astype(np.float32)
+
+
 def algorithmic_bytes(host: HostLayer, ids: np.ndarray, n_tokens: int) -> int:
     """Unique routed experts' weight bytes + router + activations in and out (f32)."""
     uniq = np.unique(ids.reshape(-1))

@@ -416,11 +416,12 @@ int oracle_moe_layer(const oracle_layer *L, oracle_layer_out *o) {
 
     for (int t = 0; t < T; ++t) {
         const float *xt = L->x + (size_t)t * d;
+        const float *xr = L->x_router ? L->x_router + (size_t)t * d : xt;
         /* router logits (mul_mat f32; summed in double here) + optional bias (llama-graph.cpp:1530-1540) */
         for (int e = 0; e < E; ++e) {
             double s = 0.0;
             const float *wr = L->w_router + (size_t)e * d;
-            for (int i = 0; i < d; ++i) s += (double)wr[i] * (double)xt[i];
+            for (int i = 0; i < d; ++i) s += (double)wr[i] * (double)xr[i];
             logit[e] = (float)s;
             if (L->b_router) logit[e] += L->b_router[e];
         }
@@ -484,4 +485,24 @@ int oracle_moe_layer(const oracle_layer *L, oracle_layer_out *o) {
     }
     free(logit); free(prob); free(h); free(a); free(y); free(acc); free(ids); free(w); free(xq); free(aq);
     return 1;
+}
+
+/* ggml_rms_norm, row by row (ggml-cpu/ops.cpp:3808-3838, ggml_compute_forward_rms_norm_f32): sum
+ * of x*x (each product in float) accumulated in double, mean = sum / n, scale = 1.0f / sqrtf(mean +
+ * eps), y = x * scale; then the ggml_scale node (ops.cpp:4522-4529: y * s) and the ggml_mul node
+ * with a broadcast [n] weight (y * w[i]) when the caller's graph has them */
+void oracle_rms_norm(const float *x, const float *w, float s, float *y, int64_t rows, int64_t n, float eps) {
+    for (int64_t r = 0; r < rows; ++r) {
+        const float *xr = x + r * n;
+        double sum = 0.0;
+        for (int64_t i = 0; i < n; ++i) sum += (double)(xr[i] * xr[i]);
+        const float mean = (float)(sum / (double)n);
+        const float scale = 1.0f / sqrtf(mean + eps);
+        for (int64_t i = 0; i < n; ++i) {
+            float v = xr[i] * scale;
+            if (s != 1.0f) v = v * s;
+            if (w) v = v * w[i];
+            y[r * n + i] = v;
+        }
+    }
 }

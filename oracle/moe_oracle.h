@@ -57,6 +57,10 @@ typedef struct oracle_layer {
      * implementation fed them. */
     const int32_t *ids_in;
     const float   *gate_up_in;
+    /* Router input when it differs from the experts' input x ([n_tokens][d_model], or NULL = x):
+     * Gemma-4 routes on rms_norm(attn_out) / sqrt(d) * ffn_gate_inp_s and feeds the experts
+     * rms_norm(attn_out) * ffn_pre_norm_2 (third_party/llama/src/models/gemma4.cpp:394-403). */
+    const float   *x_router;
 } oracle_layer;
 
 typedef struct oracle_layer_out {
@@ -85,6 +89,12 @@ uint16_t oracle_gelu_table(uint16_t h);
 /* top-k in (value desc, index asc) order over one row */
 void    oracle_topk(const float *v, int32_t n, int32_t k, int32_t *ids);
 int     oracle_moe_layer(const oracle_layer *L, oracle_layer_out *o);
+/* ggml_rms_norm over rows of n (ggml-cpu/ops.cpp, ggml_compute_forward_rms_norm_f32): the sum of
+ * squares in double, scale = 1 / sqrtf(mean + eps) in float, y = x * scale; then y * s (ggml_scale)
+ * and y * w[i] (ggml_mul with a [n] weight, w may be NULL), each an f32 product. The Gemma-4 block
+ * norms: expert input s = 1, w = ffn_pre_norm_2; router input s = 1 / sqrtf(n), w = ffn_gate_inp_s;
+ * output s = 1, w = ffn_post_norm_2 (third_party/llama/src/models/gemma4.cpp:394-427). */
+void    oracle_rms_norm(const float *x, const float *w, float s, float *y, int64_t rows, int64_t n, float eps);
 /* iq2s grid table used by the restatement (1024 packed 8-byte rows) */
 const uint64_t *oracle_iq2s_grid(void);
 const int8_t   *oracle_iq4nl_values(void);
@@ -99,6 +109,7 @@ int32_t ref_vec_dot_type(int32_t wtype);
 float   ref_vec_dot(int32_t wtype, int64_t n, const void *w_row, const void *x_q);
 uint16_t ref_gelu_table(uint16_t h);
 int     ref_moe_layer(const oracle_layer *L, oracle_layer_out *o);
+void    ref_rms_norm(const float *x, const float *w, float s, float *y, int64_t rows, int64_t n, float eps);
 
 #ifdef __cplusplus
 }

@@ -28,6 +28,7 @@ class _Layer(C.Structure):
         ("cold_gu", C.c_void_p), ("cold_down", C.c_void_p), ("s_cold", C.c_void_p),
         ("n_threads", C.c_int32),
         ("ids_in", C.c_void_p), ("gate_up_in", C.c_void_p),
+        ("x_router", C.c_void_p),
     ]
 
 
@@ -65,6 +66,7 @@ class LayerSpec:
     s_cold: np.ndarray | None = None
     ids_in: np.ndarray | None = None      # i32 [T, k]: routing taken as given (port oracle only)
     gate_up_in: np.ndarray | None = None  # f32 [T*k, 2*n_ff]: gate_up taken as given (port oracle only)
+    x_router: np.ndarray | None = None    # f32 [T, d_model]: router input when it differs from x
     keep: list = field(default_factory=list)
 
     @property
@@ -90,6 +92,7 @@ class LayerSpec:
             s_cold=None if self.s_cold is None else np.ascontiguousarray(self.s_cold, np.float32),
             ids_in=None if self.ids_in is None else np.ascontiguousarray(self.ids_in, np.int32),
             gate_up_in=None if self.gate_up_in is None else np.ascontiguousarray(self.gate_up_in, np.float32),
+            x_router=None if self.x_router is None else np.ascontiguousarray(self.x_router, np.float32),
         )
         self.keep = list(arrs.values())
         for k, v in arrs.items():
@@ -99,6 +102,15 @@ class LayerSpec:
         L.cold_type_gu, L.cold_type_down = self.cold_type_gu, self.cold_type_down
         L.n_threads = n_threads
         return L
+
+
+@dataclass
+class BlockNorms:
+    """The Gemma-4 MoE block norms (f32 [d_model] each) and the rms_norm epsilon."""
+    pre_norm: np.ndarray       # ffn_pre_norm_2
+    router_scale: np.ndarray   # ffn_gate_inp_s
+    post_norm: np.ndarray      # ffn_post_norm_2
+    eps: float = 1e-6
 
 
 class _Oracle:
@@ -114,6 +126,8 @@ class _Oracle:
         self._vdt = f(p + "vec_dot_type", C.c_int32, [C.c_int32])
         self._vdot = f(p + "vec_dot", C.c_float, [C.c_int32, C.c_int64, C.c_void_p, C.c_void_p])
         self._layer = f(p + "moe_layer", C.c_int, [C.POINTER(_Layer), C.POINTER(_LayerOut)])
+        self._rms = f(p + "rms_norm", None, [C.c_void_p, C.c_void_p, C.c_float, C.c_void_p, C.c_int64, C.c_int64,
+                                             C.c_float])
 
     def _fn(self, name, res, args):
         fn = getattr(self.lib, name)
@@ -142,6 +156,36 @@ class _Oracle:
     def vec_dot(self, wtype: int, n: int, w_row: np.ndarray, xq: np.ndarray) -> float:
         return float(self._vdot(wtype, n, np.ascontiguousarray(w_row).ctypes.data,
                                 np.ascontiguousarray(xq).ctypes.data))
+
+    def rms_norm(self, x: np.ndarray, eps: float, w: np.ndarray | None = None, s: float = 1.0) -> np.ndarray:
+        """Row-wise ((x / sqrt(mean(x^2) + eps)) * s) * w of a 2-D f32 array (ggml_rms_norm, then
+        ggml_scale when s != 1 and ggml_mul when w is given)."""
+        x = np.ascontiguousarray(x, np.float32)
+        out = np.empty_like(x)
+        wp = None if w is None else np.ascontiguousarray(w, np.float32)
+        self._rms(x.ctypes.data, None if wp is None else wp.ctypes.data, s, out.ctypes.data, x.shape[0], x.shape[1],
+                  eps)
+        return out
+
+    def gemma4_block(self, spec: LayerSpec, norms: "BlockNorms", n_threads: int = 1,
+                     want=("logits", "ids", "weights", "gate_up", "act", "down")) -> dict:
+        """The Gemma-4 MoE block around the layer (third_party/llama/src/models/gemma4.cpp:394-427):
+        spec.x is the block input (attn_out); the experts see rms_norm(x) * pre_norm (:394-396),
+        the router rms_norm(x) * (1 / sqrtf(d)) * router_scale (:399-402), and the output is
+        rms_norm(moe) * post_norm (:423-425). Result keys as moe_layer plus "moe" (before the output
+        norm), "x_expert" and "x_router". Each norm is one call of this oracle's rms_norm (the reference
+        build runs the reference's own rms_norm, scale and mul nodes)."""
+        eps = float(np.float32(norms.eps))
+        c = float(np.float32(1.0) / np.sqrt(np.float32(spec.d_model)))   # 1.0f / sqrtf((float) n_embd)
+        x_expert = self.rms_norm(spec.x, eps, norms.pre_norm)
+        x_router = self.rms_norm(spec.x, eps, norms.router_scale, c)
+        inner = LayerSpec(**{f: getattr(spec, f) for f in spec.__dataclass_fields__ if f != "keep"})
+        inner.x, inner.x_router = x_expert, x_router
+        res = self.moe_layer(inner, n_threads=n_threads, want=want)
+        res["moe"] = res["out"]
+        res["out"] = self.rms_norm(res["out"], eps, norms.post_norm)
+        res["x_expert"], res["x_router"] = x_expert, x_router
+        return res
 
     def moe_layer(self, spec: LayerSpec, n_threads: int = 1, want=("logits", "probs", "ids", "weights",
                                                                      "gate_up", "act", "down")) -> dict:

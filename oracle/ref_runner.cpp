@@ -152,7 +152,7 @@ extern "C" int ref_moe_layer(const oracle_layer * L, oracle_layer_out * o) {
     std::vector<float>   wts((size_t) T * k);
     {
         Ctx c((size_t) T * E * 4 * 8 + (size_t) T * d * 4 + (16u << 20));
-        ggml_tensor * x  = wrap(c.meta, GGML_TYPE_F32, d, T, 1, L->x);
+        ggml_tensor * x  = wrap(c.meta, GGML_TYPE_F32, d, T, 1, L->x_router ? L->x_router : L->x);
         ggml_tensor * wr = wrap(c.meta, GGML_TYPE_F32, d, E, 1, L->w_router);
         x  = ggml_reshape_2d(c.meta, x, d, T);
         wr = ggml_reshape_2d(c.meta, wr, d, E);
@@ -221,4 +221,21 @@ extern "C" int ref_moe_layer(const oracle_layer * L, oracle_layer_out * o) {
             memcpy(o->out + (size_t) t * d, (const char *) acc->data + t * acc->nb[1], sizeof(float) * d);
     }
     return 1;
+}
+
+// ggml_rms_norm over `rows` rows of n values, then ggml_scale by s (when s != 1) and ggml_mul by the
+// [n] weight w (when given): the reference's own nodes, as the Gemma-4 block builds them
+extern "C" void ref_rms_norm(const float * x, const float * w, float s, float * y, int64_t rows, int64_t n, float eps) {
+    ref_init();
+    Ctx c((size_t) rows * n * 4 * 4 + (4u << 20));
+    ggml_tensor * xt = wrap(c.meta, GGML_TYPE_F32, n, rows, 1, x);
+    xt = ggml_reshape_2d(c.meta, xt, n, rows);
+    ggml_tensor * yt = ggml_rms_norm(c.work, xt, eps);
+    if (s != 1.0f) yt = ggml_scale(c.work, yt, s);
+    if (w) yt = ggml_mul(c.work, yt, wrap(c.meta, GGML_TYPE_F32, n, 1, 1, w));
+    ggml_cgraph * gf = ggml_new_graph(c.work);
+    ggml_build_forward_expand(gf, yt);
+    ggml_graph_compute_with_ctx(c.work, gf, 1);
+    for (int64_t r = 0; r < rows; ++r)
+        memcpy(y + r * n, (const char *) yt->data + r * yt->nb[1], sizeof(float) * n);
 }

@@ -9,6 +9,7 @@ if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
 GOLDEN = os.path.join(ROOT, "tests", "golden", "golden.npz")
+GOLDEN_BLOCK = os.path.join(ROOT, "tests", "golden", "golden_block.npz")
 
 
 def pytest_configure(config):
@@ -18,6 +19,12 @@ def pytest_configure(config):
 @pytest.fixture(scope="session")
 def golden():
     return dict(np.load(GOLDEN, allow_pickle=False))
+
+
+@pytest.fixture(scope="session")
+def golden_block():
+    """Reference outputs of the Gemma-4 block norms (tests/golden/make_golden.py --block)."""
+    return dict(np.load(GOLDEN_BLOCK, allow_pickle=False))
 
 
 @pytest.fixture(scope="session")

@@ -55,6 +55,8 @@ def test_python_struct_mirrors_match_c(lib):
     assert C.sizeof(capi.Pool) == 16 + 3 * 8
     assert C.sizeof(capi.Layer) == 16 + 2 * 8 + 2 * C.sizeof(capi.Pool) + 3 * 8
     assert C.sizeof(capi.LayerAux) == 8 * 8
+    # moeb_norms: 3 pointers, f32 eps, i32 pad
+    assert C.sizeof(capi.Norms) == 3 * 8 + 8 and capi.Norms.eps.offset == 24
 
 
 def test_row_sizes(lib):

@@ -114,8 +114,10 @@ def test_dispatch_bit_exact():
     assert np.array_equal(perm.cpu().numpy(), want_perm)
 
 
-def run_layer(host, x, aux_names=("logits", "ids", "weights", "counts", "offsets", "perm", "gate_up", "down")):
-    layer = MoELayer(host)
+def run_layer(host, x, aux_names=("logits", "ids", "weights", "counts", "offsets", "perm", "gate_up", "down"),
+              norms=None):
+    """One forward through the C-ABI (moeb_layer_forward, or moeb_layer_forward_gemma4 with norms)."""
+    layer = MoELayer(host, norms=norms)
     T, E, k = x.shape[0], host.n_expert, host.top_k
     shapes = dict(logits=((T, E), torch.float32), ids=((T, k), torch.int32), weights=((T, k), torch.float32),
                   counts=((E,), torch.int32), offsets=((E + 1,), torch.int32), perm=((T * k,), torch.int32),

@@ -99,3 +99,57 @@ def test_port_vs_reference_random_layers(ref, port):
     a, b = ref.moe_layer(spec, n_threads=4), port.moe_layer(spec)
     assert np.array_equal(a["ids"], b["ids"])
     assert_layer_close(b["out"], a["out"], tol=1e-4)
+
+
+def block_norms_of(gb_cfg):
+    from llapis_b200 import workload
+    return workload.block_norms(workload.CONFIGS[gb_cfg])
+
+
+def test_rms_norm_matches_reference_fixture(golden_block, port):
+    """ggml_rms_norm rows (zero row, 1e-3 .. 1e3 magnitudes) plain, with a weight (ggml_mul) and with
+    the router's scale and weight: bit-exact against the reference's nodes."""
+    from llapis_b200.workload import NORM_EPS
+    x, w, c = golden_block["rms_x"], golden_block["rms_w"], float(golden_block["rms_c"])
+    for got, want in ((port.rms_norm(x, NORM_EPS), golden_block["rms_plain"]),
+                      (port.rms_norm(x, NORM_EPS, w), golden_block["rms_weight"]),
+                      (port.rms_norm(x, NORM_EPS, w, c), golden_block["rms_router"])):
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    assert not golden_block["rms_plain"][4].any()
+
+
+@pytest.mark.parametrize("name", ["mini_mixed", "decode_t4_mixed"])
+def test_gemma4_block_matches_reference_fixture(golden_block, port, name):
+    """The Gemma-4 block (pre / router norms, the MoE layer, the output norm) against the reference
+    run through its own rms_norm, scale and mul nodes: both norm inputs bit-exact, routing exact off
+    near ties, outputs to the layer's parity bar."""
+    host = host_layer(name)
+    for n in ("hot_gu", "hot_down", "cold_gu", "cold_down"):
+        got = sha(getattr(host, n)) if getattr(host, n) is not None else ""
+        assert got == str(golden_block[f"{name}_sha_{n}"])
+    x = golden_block[f"{name}_x"]
+    res = port.gemma4_block(spec_of(host, x), block_norms_of(name))
+    for k in ("x_expert", "x_router"):
+        assert np.array_equal(res[k].view(np.uint32), golden_block[f"{name}_{k}"].view(np.uint32)), k
+    ties = set(near_tie_tokens(golden_block[f"{name}_logits"], host.top_k).tolist())
+    same = [t for t in range(x.shape[0]) if t not in ties]
+    assert np.array_equal(res["ids"][same], golden_block[f"{name}_ids"][same])
+    np.testing.assert_allclose(res["logits"], golden_block[f"{name}_logits"], rtol=1e-5, atol=1e-6)
+    if name == "mini_mixed":
+        assert_layer_close(res["gate_up"], golden_block[f"{name}_gate_up"], tol=1e-5)
+        assert_layer_close(res["down"], golden_block[f"{name}_down"], tol=1e-4)
+    assert_layer_close(res["moe"], golden_block[f"{name}_moe"], tol=1e-4)
+    assert_layer_close(res["out"], golden_block[f"{name}_out"], tol=1e-4)
+
+
+def test_rms_norm_port_vs_reference_live(ref, port):
+    """Fresh rows through both builds (needs oracle/_ref): the squares' double sum and the f32
+    scale agree bit for bit at the model width and at an odd width."""
+    rng = np.random.default_rng(9)
+    for n in (2816, 7, 4096):
+        x = (rng.standard_normal((9, n)) * np.exp2(rng.uniform(-12, 12, (9, 1)))).astype(np.float32)
+        w = rng.uniform(0.5, 1.5, n).astype(np.float32)
+        c = float(np.float32(1.0) / np.sqrt(np.float32(n)))
+        for args in ((None, 1.0), (w, 1.0), (w, c)):
+            a, b = ref.rms_norm(x, 1e-6, *args), port.rms_norm(x, 1e-6, *args)
+            assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
