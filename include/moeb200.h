@@ -122,7 +122,10 @@ typedef struct moeb_norms {
  * that the host adds to the dense MLP branch. Same paths, workspace size and aux outputs as
  * moeb_layer_forward (aux->logits are the logits of the router input, aux->gate_up and
  * aux->down are computed from the expert input; out is after the output norm). The norms add no
- * launch on the decode path; the prefill path adds one small kernel (the rows' norm scales). */
+ * launch: the decode kernel forms both inputs as it loads x and norms each token's output row
+ * after its last block is combined; the prefill path's first kernel computes the row scales and
+ * the expert input's Q8_K rows, the router applies the router-input scaling as it stages x, and
+ * the combine kernel applies the output norm. */
 int moeb_layer_forward_gemma4(const moeb_layer *L, const moeb_norms *norms, const float *x, int32_t n_tokens,
                               float *out, const moeb_layer_aux *aux, void *workspace, size_t workspace_bytes,
                               void *stream);

@@ -1222,10 +1222,8 @@ __global__ void __launch_bounds__(1024, 1) pf_dispatch_kernel(PfDispatchParams p
 }
 
 // Q8_K quantisation of every token: one warp per (token, super-block)
-// With the Gemma-4 block norms (nscale given) the values quantised are the expert input
-// rms_norm(x) * pre_norm.
 __global__ void __launch_bounds__(256) pf_actq_kernel(const float *x, int8_t *xq8, float *xd, int16_t *xbs, int T,
-                                                      int d, const float *nscale, const float *pre) {
+                                                      int d) {
     pdl_wait();
     pdl_launch_dependents();
     const int nsb = d / QK_K;
@@ -1233,21 +1231,39 @@ __global__ void __launch_bounds__(256) pf_actq_kernel(const float *x, int8_t *xq
     if (item >= T * nsb) return;
     const int t = item / nsb, sb = item - t * nsb;
     q8k_superblock_warp(x + (size_t)t * d + sb * QK_K, xq8 + (size_t)t * d + sb * QK_K, xd + item, xbs + (size_t)item * 16,
-                        lane, nscale ? nscale[t] : 1.f, nscale ? pre + sb * QK_K : nullptr);
+                        lane);
 }
 
-// rms_norm row scales of x for the Gemma-4 block norms, one warp per token
-__global__ void __launch_bounds__(256) pf_norm_kernel(const float *x, float *nscale, int T, int d, float eps) {
+// The Gemma-4 block norms' first kernel (in place of pf_actq_kernel, ahead of the router): per
+// token its rms_norm scale (written for the router) and the Q8_K rows of the expert input
+// rms_norm(x) * pre. One CTA per token, one warp per 256-value super-block: the squares of the
+// warp's values summed in double, the warps' sums added in warp order.
+__global__ void __launch_bounds__(kPrefillMaxSb * 32) pf_actq_norm_kernel(const float *x, int8_t *xq8, float *xd,
+                                                                         int16_t *xbs, float *nscale, const float *pre,
+                                                                         int T, int d, float eps) {
+    __shared__ double red[kPrefillMaxSb];
+    __shared__ float sc;
     pdl_wait();
     pdl_launch_dependents();
-    const int t = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-    if (t >= T) return;
-    const float4 *x4 = reinterpret_cast<const float4 *>(x + (size_t)t * d);
-    double sq = 0.0;
-#pragma unroll 4
-    for (int i = lane; i < d / 4; i += 32) sq += sq_sum4(__ldg(x4 + i));
-    sq = warp_sum_d(sq);
-    if (lane == 0) nscale[t] = rms_row_scale(sq, d, eps);
+    const int t = blockIdx.x, sb = threadIdx.x >> 5, lane = threadIdx.x & 31, nsb = d / QK_K;
+    const float4 *x4 = reinterpret_cast<const float4 *>(x + (size_t)t * d + sb * QK_K);
+    const float4 a = __ldg(x4 + 2 * lane), b = __ldg(x4 + 2 * lane + 1);
+    const double sq = warp_sum_d(sq_sum4(a) + sq_sum4(b));
+    if (lane == 0) red[sb] = sq;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double tot = 0.0;
+        for (int i = 0; i < nsb; ++i) tot += red[i];
+        sc = rms_row_scale(tot, d, eps);
+        nscale[t] = sc;
+    }
+    __syncthreads();
+    const float s = sc;
+    const float4 *w4 = reinterpret_cast<const float4 *>(pre + sb * QK_K);
+    const float4 na = norm_weight4(a, s, __ldg(w4 + 2 * lane)), nb = norm_weight4(b, s, __ldg(w4 + 2 * lane + 1));
+    float v[8] = {na.x, na.y, na.z, na.w, nb.x, nb.y, nb.z, nb.w};
+    const int item = t * nsb + sb;
+    q8k_quantize_warp(v, xq8 + (size_t)t * d + sb * QK_K, xd + item, xbs + (size_t)item * 16, lane);
 }
 
 // out[t] = ((w0 y0 + w1 y1) + w2 y2) + ...: products rounded, then added in slot order, as the

@@ -147,13 +147,12 @@ class MoELayer:
                 and h.n_ff % 32 == 0 and tiles <= 512 and P // (8 * chunk) + tiles <= 1024)
 
     def launches(self, n_tokens: int) -> int:
-        """Kernels one forward of n_tokens launches: nine on the prefill path (ten with the block
-        norms: their row scales), else one cooperative fused kernel per 8-token chunk."""
+        """Kernels one forward of n_tokens launches: nine on the prefill path (with the block norms
+        too: their kernel takes the activation quantiser's place), else one cooperative fused kernel
+        per 8-token chunk."""
         if n_tokens <= 0:
             return 0
-        if self.prefill_path(n_tokens):
-            return 9 + (self.norms is not None)
-        return (n_tokens + 7) // 8
+        return 9 if self.prefill_path(n_tokens) else (n_tokens + 7) // 8
 
     def workspace_bytes(self, n_tokens: int) -> int:
         return int(capi.lib().moeb_layer_workspace_size(C.byref(self.c), n_tokens))

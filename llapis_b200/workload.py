@@ -166,11 +166,14 @@ NORM_EPS = 1e-6   # Gemma-4 f_norm_rms_eps
 
 
 def block_norms(cfg: LayerConfig, layer: int = 0):
-    """Seeded Gemma-4 block norm vectors for layer `layer` of cfg: ffn_pre_norm_2, ffn_gate_inp_s and
-    ffn_post_norm_2 as 1 + N(0, 0.1) each (f32 [d_model]), eps 1e-6."""
+    """Seeded Gemma-4 block norm vectors for layer `layer` of cfg (f32 [d_model]), eps 1e-6:
+    ffn_pre_norm_2 and ffn_post_norm_2 1 + N(0, 0.1); ffn_gate_inp_s sqrt(d) * (1 + N(0, 0.1)), so
+    that the router input rms_norm(x) / sqrt(d) * ffn_gate_inp_s has unit scale and the N(0, 0.02)
+    router weights give logits of the same spread as the plain layer's N(0, 1) input does."""
     from .layer import BlockNorms
     d = cfg.d_model
     v = [np.float32(1.0) + _normal((cfg.seed, layer, 1 << 21, i), (d,), 0.1) for i in range(3)]
+    v[1] = (v[1] * np.sqrt(np.float32(d))).astype(np.float32)
     return BlockNorms(pre_norm=v[0], router_scale=v[1], post_norm=v[2], eps=NORM_EPS)
 
 
