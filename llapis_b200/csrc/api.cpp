@@ -481,6 +481,7 @@ extern "C" int moeb_layer_forward_gemma4(const moeb_layer *L, const moeb_norms *
     if (!aligned16(norms->pre_norm) || !aligned16(norms->router_scale) || !aligned16(norms->post_norm))
         return fail(MOEB_EINVAL, "moeb_layer_forward_gemma4: norm vectors must be 16-byte aligned");
     if (!(norms->eps >= 0.f)) return fail(MOEB_EINVAL, "moeb_layer_forward_gemma4: eps must be >= 0");
+    if (L->d_model > 4096) return fail(MOEB_EINVAL, "moeb_layer_forward_gemma4: d_model %d > 4096", L->d_model);
     const NormArgs nrm = {norms->pre_norm, norms->router_scale, norms->post_norm, norms->eps};
     if (use_prefill(L, n_tokens))
         return forward_prefill(L, x, n_tokens, out, aux, workspace, (cudaStream_t)stream, n_sms, nrm);

@@ -40,7 +40,7 @@ __device__ __forceinline__ Q8KView q8k_view(const uint8_t *row, int nsb) {
 // iscale = -127/max; q = min(127, rne(iscale*x)); d = 1/iscale; bsums over 16 values.
 // q8k_quantize_warp takes the lane's 8 values (lane * 8 .. lane * 8 + 7) in registers;
 // q8k_superblock_warp loads them, with w given as the normed (x * s) * w (the Gemma-4 expert input).
-__device__ void q8k_quantize_warp(float (&v)[8], int8_t *qs, float *d_out, int16_t *bs, int lane);
+__device__ __forceinline__ void q8k_quantize_warp(float (&v)[8], int8_t *qs, float *d_out, int16_t *bs, int lane);
 __device__ void q8k_superblock_warp(const float *x, int8_t *qs, float *d_out, int16_t *bs, int lane,
                                     float nscale = 1.f, const float *w = nullptr) {
     float v[8];
@@ -52,7 +52,7 @@ __device__ void q8k_superblock_warp(const float *x, int8_t *qs, float *d_out, in
     }
     q8k_quantize_warp(v, qs, d_out, bs, lane);
 }
-__device__ void q8k_quantize_warp(float (&v)[8], int8_t *qs, float *d_out, int16_t *bs, int lane) {
+__device__ __forceinline__ void q8k_quantize_warp(float (&v)[8], int8_t *qs, float *d_out, int16_t *bs, int lane) {
     float amax = 0.f;
     int aidx = 0x7fffffff;
 #pragma unroll
@@ -1004,6 +1004,7 @@ struct FusedRoute {
     float red[kFusedMaxT][kConsumerWarps + 1];
     double dred[kFusedMaxT][kConsumerWarps + 1];
     float nscale[kFusedMaxT];        // rms_norm row scales of the tokens (Gemma-4 block norms)
+    int32_t fin_n, fin[kFusedMaxT];  // tokens whose last output block this CTA combined (output norm)
 };
 
 struct FusedSmem {
@@ -1203,6 +1204,9 @@ __device__ __forceinline__ int group_at_pre_warp(const uint32_t *pre, int U, uin
     return u * gpe + (int)((pos - pre[u]) / unit);
 }
 
+// NRM: with the Gemma-4 block norms (p.nrm); a separate instance, so the plain layer's code is the
+// same as without them
+template <bool NRM>
 __global__ void __launch_bounds__(kGemvThreads, 1) fused_decode_kernel(FusedParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -1271,48 +1275,25 @@ __global__ void __launch_bounds__(kGemvThreads, 1) fused_decode_kernel(FusedPara
 #pragma unroll
         for (int i = 0; i < MOE_IQ2S_GRID_ROWS / 32; ++i) grid[lane + 32 * i] = g[i];
     }
-    const bool nrm = p.nrm.pre != nullptr;
-    if (nrm) {
-        // Gemma-4 block norms: the rms_norm scales of all T tokens, in every CTA (a logits unit
-        // needs every token's); the same code and summation order everywhere, so all CTAs agree
-        const int n4 = d / 4;
-        double sq[kFusedMaxT];
-#pragma unroll
-        for (int t = 0; t < kFusedMaxT; ++t) sq[t] = 0.0;
-        for (int i = tid; i < n4; i += kGemvThreads) {
-#pragma unroll
-            for (int t = 0; t < kFusedMaxT; ++t)
-                if (t < T) sq[t] += sq_sum4(__ldg(reinterpret_cast<const float4 *>(p.x + (size_t)t * d) + i));
-        }
-#pragma unroll
-        for (int t = 0; t < kFusedMaxT; ++t) {
-            if (t < T) {
-                const double v = warp_sum_d(sq[t]);
-                if (lane == 0) rs.dred[t][warp] = v;
-            }
-        }
-        __syncthreads();
-        if (tid < T) {
-            double v = 0.0;
-            for (int w = 0; w < kConsumerWarps + 1; ++w) v += rs.dred[tid][w];
-            rs.nscale[tid] = rms_row_scale(v, d, p.nrm.eps);
-        }
-        __syncthreads();
-    }
+    constexpr bool nrm = NRM;
     for (int unit = blockIdx.x; unit < E + T; unit += G) {
         if (unit < E) {
             // logits[t][unit] = W[unit] . x[t] (+ bias): every thread a strided share, then warp and
-            // CTA reductions in a fixed order. With the block norms, x[t] is the router input
-            // rms_norm(x[t]) / sqrt(d) * router_scale, formed value by value as the loads arrive.
+            // CTA reductions in a fixed order. With the Gemma-4 block norms the router input is
+            // rms_norm(x[t]) / sqrt(d) * router_scale; its row scale s_t is factored out of the dot
+            // (logit = s_t * (W . ((x / sqrt(d)) * router_scale)), equal to the dot of the per-value
+            // rounded input to f32 rounding, like the summation order) and s_t comes from the
+            // squares of the same x loads, so the logits need no pass over x ahead of them.
             const int n4 = d / 4;
             const float4 *w4 = reinterpret_cast<const float4 *>(p.w_router + (size_t)unit * d);
             const float4 *r4 = reinterpret_cast<const float4 *>(p.nrm.router);
             const float rc = nrm ? router_input_scale(d) : 1.f;
-            float part[kFusedMaxT], ns[kFusedMaxT];
+            float part[kFusedMaxT];
+            double sq[kFusedMaxT];
 #pragma unroll
             for (int t = 0; t < kFusedMaxT; ++t) {
                 part[t] = 0.f;
-                ns[t] = nrm && t < T ? rs.nscale[t] : 1.f;
+                sq[t] = 0.0;
             }
             for (int i = tid; i < n4; i += kGemvThreads) {
                 const float4 w = __ldg(w4 + i);
@@ -1321,7 +1302,10 @@ __global__ void __launch_bounds__(kGemvThreads, 1) fused_decode_kernel(FusedPara
                 for (int t = 0; t < kFusedMaxT; ++t) {
                     if (t < T) {
                         float4 xv = __ldg(reinterpret_cast<const float4 *>(p.x + (size_t)t * d) + i);
-                        if (nrm) xv = router_input4(xv, ns[t], rc, r);
+                        if (nrm) {
+                            sq[t] += sq_sum4(xv);
+                            xv = router_input4(xv, 1.f, rc, r);
+                        }
                         part[t] = fmaf(w.x, xv.x, part[t]);
                         part[t] = fmaf(w.y, xv.y, part[t]);
                         part[t] = fmaf(w.z, xv.z, part[t]);
@@ -1332,16 +1316,63 @@ __global__ void __launch_bounds__(kGemvThreads, 1) fused_decode_kernel(FusedPara
 #pragma unroll
             for (int t = 0; t < kFusedMaxT; ++t) {
                 if (t < T) {
-                    const float s = warp_sum(part[t]);
-                    if (lane == 0) rs.red[t][warp] = s;
+                    const float v = warp_sum(part[t]);
+                    if (lane == 0) rs.red[t][warp] = v;
+                }
+            }
+            if (nrm) {   // all tokens' squares reduced together (absent tokens reduce zeros)
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+                    for (int t = 0; t < kFusedMaxT; ++t) sq[t] += __shfl_xor_sync(0xffffffffu, sq[t], o);
+                }
+                if (lane == 0) {
+#pragma unroll
+                    for (int t = 0; t < kFusedMaxT; ++t)
+                        if (t < T) rs.dred[t][warp] = sq[t];
                 }
             }
             __syncthreads();
             if (tid < T) {
-                float s = 0.f;
-                for (int w = 0; w < kConsumerWarps + 1; ++w) s += rs.red[tid][w];
-                if (p.b_router) s = __fadd_rn(s, p.b_router[unit]);
-                p.logits[(size_t)tid * E + unit] = s;
+                float v = 0.f;
+                for (int w = 0; w < kConsumerWarps + 1; ++w) v += rs.red[tid][w];
+                if (nrm) {
+                    double q = 0.0;
+                    for (int w = 0; w < kConsumerWarps + 1; ++w) q += rs.dred[tid][w];
+                    v = __fmul_rn(v, rms_row_scale(q, d, p.nrm.eps));
+                }
+                if (p.b_router) v = __fadd_rn(v, p.b_router[unit]);
+                p.logits[(size_t)tid * E + unit] = v;
+            }
+            __syncthreads();
+        } else if (nrm) {
+            // token t's Q8_K row of the expert input rms_norm(x[t]) * pre_norm: one warp per
+            // super-block (d <= 4096 for the block norms), the row scale from the warps' squares
+            const int t = unit - E, nsb = d / QK_K;
+            uint8_t *row = p.xq + (size_t)t * p.xq_stride;
+            float4 xa = make_float4(0.f, 0.f, 0.f, 0.f), xb = xa;
+            if (warp < nsb) {
+                const float4 *x4 = reinterpret_cast<const float4 *>(p.x + (size_t)t * d + warp * QK_K);
+                xa = __ldg(x4 + 2 * lane);
+                xb = __ldg(x4 + 2 * lane + 1);
+            }
+            const double q = warp_sum_d(sq_sum4(xa) + sq_sum4(xb));
+            if (lane == 0) rs.dred[0][warp] = q;
+            __syncthreads();
+            if (tid == 0) {
+                double tot = 0.0;
+                for (int w = 0; w < nsb; ++w) tot += rs.dred[0][w];
+                rs.nscale[0] = rms_row_scale(tot, d, p.nrm.eps);
+            }
+            __syncthreads();
+            if (warp < nsb) {
+                const float sc = rs.nscale[0];
+                const float4 *pw = reinterpret_cast<const float4 *>(p.nrm.pre + warp * QK_K);
+                const float4 na = norm_weight4(xa, sc, __ldg(pw + 2 * lane)), nb = norm_weight4(xb, sc, __ldg(pw + 2 * lane + 1));
+                float v[8] = {na.x, na.y, na.z, na.w, nb.x, nb.y, nb.z, nb.w};
+                q8k_quantize_warp(v, reinterpret_cast<int8_t *>(row) + warp * 256,
+                                  reinterpret_cast<float *>(row + nsb * 256) + warp,
+                                  reinterpret_cast<int16_t *>(row + nsb * 256 + nsb * 4) + warp * 16, lane);
             }
             __syncthreads();
         } else {
@@ -1350,8 +1381,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) fused_decode_kernel(FusedPara
             for (int sb = warp; sb < nsb; sb += kGemvThreads / 32)
                 q8k_superblock_warp(p.x + (size_t)t * d + sb * 256, reinterpret_cast<int8_t *>(row) + sb * 256,
                                     reinterpret_cast<float *>(row + nsb * 256) + sb,
-                                    reinterpret_cast<int16_t *>(row + nsb * 256 + nsb * 4) + sb * 16, lane,
-                                    nrm ? rs.nscale[t] : 1.f, nrm ? p.nrm.pre + sb * 256 : nullptr);
+                                    reinterpret_cast<int16_t *>(row + nsb * 256 + nsb * 4) + sb * 16, lane);
         }
     }
     __syncthreads();
@@ -1681,6 +1711,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) fused_decode_kernel(FusedPara
         int *todo = reinterpret_cast<int *>(dact);   // the activations are no longer needed
         if (tid == 0) {
             todo[0] = 0;
+            rs.fin_n = 0;
             __threadfence();
         }
         consumer_sync();
@@ -1727,23 +1758,39 @@ __global__ void __launch_bounds__(kGemvThreads, 1) fused_decode_kernel(FusedPara
                 }
                 if (nrm) {
                     // the output norm (ffn_post_norm_2): the block's sum of squares, then a count
-                    // per token; the warp that combines the token's last block scales its row
+                    // per token; the CTA that combines the token's last block scales its row below
                     sq = warp_sum_d(sq);
                     if (lane == 0) p.nsum[t * nrb + rb] = sq;
-                    __threadfence();
+                    asm volatile("fence.acq_rel.gpu;" ::: "memory");   // this lane's out rows (and sum) first
                     __syncwarp();
-                    uint32_t done = 0;
-                    if (lane == 0) done = atomicAdd(&tok_cnt[t], 1u) + 1u;
-                    done = __shfl_sync(0xffffffffu, done, 0);
-                    if (done == (uint32_t)nrb) {
-                        __threadfence();
-                        double tot = 0.0;   // the blocks' sums in block order
-                        for (int b = 0; b < nrb; ++b) tot += __ldcg(p.nsum + t * nrb + b);
-                        const float sc = rms_row_scale(tot, d, p.nrm.eps);
-                        float4 *o4 = reinterpret_cast<float4 *>(p.out + (size_t)t * d);
-                        const float4 *w4 = reinterpret_cast<const float4 *>(p.nrm.post);
-                        for (int i = lane; i < d / 4; i += 32) o4[i] = norm_weight4(__ldcg(o4 + i), sc, __ldg(w4 + i));
+                    if (lane == 0 && atomicAdd(&tok_cnt[t], 1u) + 1u == (uint32_t)nrb) {
+                        asm volatile("fence.acq_rel.gpu;" ::: "memory");
+                        rs.fin[atomicAdd(&rs.fin_n, 1)] = t;
                     }
+                }
+            }
+        }
+        if (nrm) {
+            consumer_sync();
+            const int nf = rs.fin_n;
+            if (nf > 0) {
+                asm volatile("fence.acq_rel.gpu;" ::: "memory");
+                const int n4 = d / 4, i0 = tid, i1 = tid + kConsumerWarps * 32;   // d <= 4096: two per thread
+                const float4 *w4 = reinterpret_cast<const float4 *>(p.nrm.post);
+                for (int f = 0; f < nf; ++f) {
+                    const int t = rs.fin[f];
+                    float4 *o4 = reinterpret_cast<float4 *>(p.out + (size_t)t * d);
+                    // this thread's share of the row and the blocks' sums, loaded together; every warp
+                    // sums the blocks lane-strided then by the xor tree (one fixed order, so all warps,
+                    // in whichever CTA finishes the token, form the same scale)
+                    float4 v0 = make_float4(0.f, 0.f, 0.f, 0.f), v1 = v0, w0 = v0, w1 = v0;
+                    if (i0 < n4) { v0 = __ldcg(o4 + i0); w0 = __ldg(w4 + i0); }
+                    if (i1 < n4) { v1 = __ldcg(o4 + i1); w1 = __ldg(w4 + i1); }
+                    double part = 0.0;
+                    for (int b = lane; b < nrb; b += 32) part += __ldcg(p.nsum + t * nrb + b);
+                    const float sc = rms_row_scale(warp_sum_d(part), d, p.nrm.eps);
+                    if (i0 < n4) o4[i0] = norm_weight4(v0, sc, w0);
+                    if (i1 < n4) o4[i1] = norm_weight4(v1, sc, w1);
                 }
             }
         }
@@ -1936,12 +1983,12 @@ cudaError_t launch_fused(const FusedArgs &a, cudaStream_t s, int n_sms) {
     p.qa = a.qa;
     p.sync = a.sync;
     const size_t smem = fused_smem_bytes(a.d, a.nff);
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute((const void *)fused_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             227 * 1024);
+    const void *fn = a.nrm.pre ? (const void *)fused_decode_kernel<true> : (const void *)fused_decode_kernel<false>;
+    static bool attr_set[2] = {false, false};
+    if (!attr_set[a.nrm.pre ? 1 : 0]) {
+        cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
         if (e != cudaSuccess) return e;
-        attr_set = true;
+        attr_set[a.nrm.pre ? 1 : 0] = true;
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(n_sms);
@@ -1954,7 +2001,7 @@ cudaError_t launch_fused(const FusedArgs &a, cudaStream_t s, int n_sms) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     void *args[] = {&p};
-    return cudaLaunchKernelExC(&cfg, (const void *)fused_decode_kernel, args);
+    return cudaLaunchKernelExC(&cfg, fn, args);
 }
 
 // Opt-in to more than 48 KB of dynamic shared memory, once per device and kernel.
