@@ -122,10 +122,12 @@ typedef struct moeb_norms {
  * that the host adds to the dense MLP branch. Same paths, workspace size and aux outputs as
  * moeb_layer_forward (aux->logits are the logits of the router input, aux->gate_up and
  * aux->down are computed from the expert input; out is after the output norm). The norms add no
- * launch: the decode kernel forms both inputs as it loads x and norms each token's output row
- * after its last block is combined; the prefill path's first kernel computes the row scales and
- * the expert input's Q8_K rows, the router applies the router-input scaling as it stages x, and
- * the combine kernel applies the output norm. */
+ * launch: the decode kernel takes the row scales from the squares of its own loads of x (the
+ * router's row scale factored out of its dot product: the logits equal the reference's to f32
+ * rounding, as their summation order already makes them) and norms each token's output row after
+ * its last block is combined; the prefill path's first kernel computes the row scales and the
+ * expert input's Q8_K rows, the router forms its input value by value as it stages x, and the
+ * combine kernel applies the output norm. d_model <= 4096. */
 int moeb_layer_forward_gemma4(const moeb_layer *L, const moeb_norms *norms, const float *x, int32_t n_tokens,
                               float *out, const moeb_layer_aux *aux, void *workspace, size_t workspace_bytes,
                               void *stream);
