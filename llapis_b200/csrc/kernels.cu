@@ -1711,7 +1711,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) fused_decode_kernel(FusedPara
         int *todo = reinterpret_cast<int *>(dact);   // the activations are no longer needed
         if (tid == 0) {
             todo[0] = 0;
-            rs.fin_n = 0;
+            if (nrm) rs.fin_n = 0;
             __threadfence();
         }
         consumer_sync();
@@ -1754,7 +1754,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) fused_decode_kernel(FusedPara
                     for (int j = 1; j < k; ++j)
                         acc = __fadd_rn(acc, __fmul_rn(__ldcg(p.y + (size_t)(t * k + j) * d + row), rs.w[t * k + j]));
                     p.out[(size_t)t * d + row] = acc;
-                    sq += (double)__fmul_rn(acc, acc);
+                    if (nrm) sq += (double)__fmul_rn(acc, acc);
                 }
                 if (nrm) {
                     // the output norm (ffn_post_norm_2): the block's sum of squares, then a count
