@@ -234,6 +234,47 @@ size_t moeb_quantize_weights(int32_t type, const float *src, void *dst, int64_t 
                              int32_t n_threads);
 size_t moeb_row_size(int32_t type, int64_t n_per_row);
 
+/* ---- Expert loading from files into the class pools (new; the reference's host loads the same
+ * tensors through ggml's GGUF reader, third_party/llama/ggml/src/gguf.cpp, and the hot class's
+ * pages through its expert store and memory manager, moert/include/moert/store.h and memmgr.h).
+ * A Gemma-4 layer's stacked expert tensors in a GGUF (blk.<il>.ffn_gate_up_exps.weight
+ * [n_embd, 2*n_ff, E], blk.<il>.ffn_down_exps.weight [n_ff, n_embd, E]) are laid out exactly as a
+ * cold pool ([E][rows][row bytes]); the hot pool's slots are filled page by page from a store
+ * (include/moert_store.h). Host functions; the copies run on `stream` and have completed when a
+ * loader returns. */
+
+/* GGUF tensor directory: header, key/values (arrays skipped) and tensor infos of a v2/v3 file. */
+typedef struct moeb_gguf moeb_gguf;
+typedef struct moeb_gguf_tensor {
+    int32_t  type;       /* ggml type id */
+    int32_t  n_dims;
+    int64_t  ne[4];      /* trailing 1s */
+    uint64_t offset;     /* absolute byte offset of the data in the file */
+    uint64_t nbytes;
+} moeb_gguf_tensor;
+moeb_gguf *moeb_gguf_open(const char *path);              /* NULL on error (moeb_last_error) */
+void       moeb_gguf_close(moeb_gguf *g);
+int        moeb_gguf_find_tensor(const moeb_gguf *g, const char *name, moeb_gguf_tensor *out);
+int        moeb_gguf_get_u32(const moeb_gguf *g, const char *key, uint32_t *out);
+int        moeb_gguf_get_f32(const moeb_gguf *g, const char *key, float *out);
+int        moeb_gguf_get_str(const moeb_gguf *g, const char *key, char *out, size_t cap);
+
+/* Copies nbytes of a file from `offset` to device memory `dst`: eight reader threads, each with two
+ * 8 MiB pinned staging buffers (128 MiB, allocated on the first load and kept for the process)
+ * and its own copy stream, ordered after the work already on `stream`. Loads from several host
+ * threads run one at a time. Returns the bytes copied or a negative MOEB_E* code. */
+int64_t moeb_load_file_range(const char *path, uint64_t offset, uint64_t nbytes, void *dst, void *stream);
+
+/* Copies the store pages (layer, kind, is_scale, experts[i]) to dst + i * dst_stride, i < n: the
+ * hot pool's slots in slot order (kind 0 gate_up, 1 down; is_scale 1: the per-expert down scale,
+ * stride 4), with the staging of moeb_load_file_range (pages of at most 8 MiB). verify != 0
+ * re-checks each page's checksum. Returns the bytes copied or a negative MOEB_E* code (a missing
+ * page, or one longer than dst_stride or 8 MiB: MOEB_EINVAL). */
+struct moert_store_reader;
+int64_t moeb_load_store_pages(struct moert_store_reader *r, int32_t layer, int32_t kind, int32_t is_scale,
+                              const int32_t *experts, int32_t n, void *dst, uint64_t dst_stride, int32_t verify,
+                              void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -21,9 +21,9 @@ LIBDIR = os.path.join(PKG, "lib")
 LIB = os.path.join(LIBDIR, "libmoeb200.so")
 INCLUDE = os.path.join(ROOT, "include")
 
-SOURCES = ["kernels.cu", "api.cpp", "quant.cpp"]
+SOURCES = ["kernels.cu", "api.cpp", "quant.cpp", "store.cpp", "load.cpp"]
 HEADERS = ["common.cuh", "params.h", "ggml_tables.inc", "prefill.cuh", "mid.cuh"]
-PUBLIC_HEADERS = ["moeb200.h", "moert_cuda.h"]
+PUBLIC_HEADERS = ["moeb200.h", "moert_cuda.h", "moert_store.h"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 HOST_FLAGS = "-fPIC,-O2,-ffp-contract=off,-mf16c,-mavx2,-mfma,-pthread"

@@ -43,6 +43,19 @@ class Norms(C.Structure):
                 ("eps", C.c_float), ("_pad", C.c_int32)]
 
 
+class StoreInfo(C.Structure):
+    """moert_store_info (include/moert_store.h)."""
+    _fields_ = [("format_version", C.c_uint32), ("source_uuid", C.c_uint64), ("arch", C.c_char * 16),
+                ("n_layers", C.c_int32), ("n_expert", C.c_int32), ("n_embd", C.c_uint64), ("n_ff_exp", C.c_uint64),
+                ("pack_uuid", C.c_uint64), ("record_count", C.c_uint64)]
+
+
+class GgufTensor(C.Structure):
+    """moeb_gguf_tensor (include/moeb200.h)."""
+    _fields_ = [("type", C.c_int32), ("n_dims", C.c_int32), ("ne", C.c_int64 * 4), ("offset", C.c_uint64),
+                ("nbytes", C.c_uint64)]
+
+
 _lib = None
 
 # name -> (restype, argtypes); every symbol include/*.h declares
@@ -77,6 +90,31 @@ SIGNATURES = {
     "moeb_quantize_act": (C.c_int, [C.c_int32, C.c_void_p, C.c_void_p, C.c_int64, C.c_int64, C.c_void_p]),
     "moeb_quantize_weights": (C.c_size_t, [C.c_int32, C.c_void_p, C.c_void_p, C.c_int64, C.c_int64, C.c_int32]),
     "moeb_row_size": (C.c_size_t, [C.c_int32, C.c_int64]),
+    "moeb_gguf_open": (C.c_void_p, [C.c_char_p]),
+    "moeb_gguf_close": (None, [C.c_void_p]),
+    "moeb_gguf_find_tensor": (C.c_int, [C.c_void_p, C.c_char_p, C.POINTER(GgufTensor)]),
+    "moeb_gguf_get_u32": (C.c_int, [C.c_void_p, C.c_char_p, C.POINTER(C.c_uint32)]),
+    "moeb_gguf_get_f32": (C.c_int, [C.c_void_p, C.c_char_p, C.POINTER(C.c_float)]),
+    "moeb_gguf_get_str": (C.c_int, [C.c_void_p, C.c_char_p, C.c_char_p, C.c_size_t]),
+    "moeb_load_file_range": (C.c_int64, [C.c_char_p, C.c_uint64, C.c_uint64, C.c_void_p, C.c_void_p]),
+    "moeb_load_store_pages": (C.c_int64, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_void_p, C.c_int32,
+                                          C.c_void_p, C.c_uint64, C.c_int32, C.c_void_p]),
+    "moert_store_probe": (C.c_int32, [C.c_char_p, C.POINTER(StoreInfo)]),
+    "moert_store_verify": (C.c_int64, [C.c_char_p]),
+    "moert_store_writer_open": (C.c_void_p, [C.c_char_p, C.c_char_p, C.POINTER(StoreInfo)]),
+    "moert_store_writer_add_page": (C.c_int32, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
+                                                C.c_int32, C.c_uint32, C.POINTER(C.c_int64), C.c_int32, C.c_void_p,
+                                                C.c_uint64]),
+    "moert_store_writer_close": (C.c_int32, [C.c_void_p]),
+    "moert_store_fnv1a64": (C.c_uint64, [C.c_void_p, C.c_uint64, C.c_uint64]),
+    "moert_store_reader_open": (C.c_void_p, [C.c_char_p, C.c_uint64]),
+    "moert_store_reader_free": (None, [C.c_void_p]),
+    "moert_store_reader_geometry": (C.c_int32, [C.c_void_p, C.POINTER(C.c_int32), C.POINTER(C.c_int32)]),
+    "moert_store_reader_page_nbytes": (C.c_uint64, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_int32]),
+    "moert_store_reader_page_info": (C.c_int32, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
+                                                 C.POINTER(C.c_int32), C.POINTER(C.c_uint64), C.POINTER(C.c_int64)]),
+    "moert_store_reader_read": (C.c_uint64, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_void_p,
+                                             C.c_uint64, C.c_int32]),
     "moert_cuda_configure": (None, [C.c_void_p]),
     "moert_ffn_moe": (None, [C.c_void_p, C.c_void_p]),
     "moert_cuda_route_counts_enable": (C.c_int32, [C.c_int32, C.c_int32]),

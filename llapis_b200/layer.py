@@ -87,7 +87,11 @@ class MoELayer:
     """One MoE layer resident on a CUDA device. With `norms` the forward is the whole Gemma-4 MoE
     block (moeb_layer_forward_gemma4): x is the block input and the output is normed."""
 
-    def __init__(self, host: HostLayer, device: str | torch.device = "cuda", norms: BlockNorms | None = None):
+    def __init__(self, host: HostLayer, device: str | torch.device = "cuda", norms: BlockNorms | None = None,
+                 pools: dict | None = None):
+        """pools: device tensors already holding the weights (hot_gu, hot_down, cold_gu, cold_down,
+        s_hot, s_cold; llapis_b200.loader fills them from files); the host arrays of those names
+        are then not uploaded."""
         self.host = host
         self.norms = norms
         self.device = torch.device(device)
@@ -98,12 +102,11 @@ class MoELayer:
             capi.check(capi.lib().moeb_init())
         h = host
         exp_slot, slot_exp, slot_state = h.residency()
+        weights = ("hot_gu", "hot_down", "cold_gu", "cold_down", "s_hot", "s_cold")
         self.t = dict(
             w_router=_dev(h.w_router.astype(np.float32), self.device),
             b_router=_dev(None if h.b_router is None else h.b_router.astype(np.float32), self.device),
-            hot_gu=_dev(h.hot_gu, self.device), hot_down=_dev(h.hot_down, self.device),
-            cold_gu=_dev(h.cold_gu, self.device), cold_down=_dev(h.cold_down, self.device),
-            s_hot=_dev(h.s_hot, self.device), s_cold=_dev(h.s_cold, self.device),
+            **{n: (pools.get(n) if pools is not None else _dev(getattr(h, n), self.device)) for n in weights},
             exp_slot=_dev(exp_slot, self.device) if h.n_slots else None,
             slot_exp=_dev(slot_exp, self.device) if h.n_slots else None,
             slot_state=_dev(slot_state, self.device) if h.n_slots else None,
@@ -112,9 +115,9 @@ class MoELayer:
         L = capi.Layer()
         L.d_model, L.n_ff, L.n_expert, L.top_k = h.d_model, h.n_ff, h.n_expert, h.top_k
         L.w_router, L.b_router = _ptr(t["w_router"]), _ptr(t["b_router"])
-        L.hot = capi.Pool(h.hot_type_gu, h.hot_type_down, h.n_slots if h.hot_gu is not None else 0, 0,
+        L.hot = capi.Pool(h.hot_type_gu, h.hot_type_down, h.n_slots if t["hot_gu"] is not None else 0, 0,
                           _ptr(t["hot_gu"]), _ptr(t["hot_down"]), _ptr(t["s_hot"]))
-        L.cold = capi.Pool(h.cold_type_gu, h.cold_type_down, h.n_expert if h.cold_gu is not None else 0, 0,
+        L.cold = capi.Pool(h.cold_type_gu, h.cold_type_down, h.n_expert if t["cold_gu"] is not None else 0, 0,
                            _ptr(t["cold_gu"]), _ptr(t["cold_down"]), _ptr(t["s_cold"]))
         L.exp_slot, L.slot_exp, L.slot_state = _ptr(t["exp_slot"]), _ptr(t["slot_exp"]), _ptr(t["slot_state"])
         self.c = L

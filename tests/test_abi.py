@@ -15,7 +15,7 @@ from conftest import ROOT
 sys.path.insert(0, os.path.join(ROOT, "tests", "golden"))
 import abi_layout  # noqa: E402
 
-HEADERS = [os.path.join(ROOT, "include", h) for h in ("moeb200.h", "moert_cuda.h")]
+HEADERS = [os.path.join(ROOT, "include", h) for h in ("moeb200.h", "moert_cuda.h", "moert_store.h")]
 
 
 def declared_functions():
