@@ -254,3 +254,54 @@ def test_layer_round_trip(tmp_path, split):
     assert gn.eps == np.float32(1e-6)
     with pytest.raises(Exception):
         load_host_layer(gp, 2, sp, host.hot_ids)   # no such layer in the file
+
+
+def test_gguf_rejects_malformed_files(tmp_path):
+    """Truncated headers, an unknown tensor type, a row that is not whole blocks and data past the
+    end of the file all fail to open with a message, and never read past the file."""
+    from llapis_b200 import capi
+    from llapis_b200.loader import Gguf
+    lib = capi.lib()
+    kvs, tensors = small_gguf_content()
+    good = str(tmp_path / "good.gguf")
+    write_gguf(good, kvs, tensors)
+    raw = open(good, "rb").read()
+    cases = {
+        "truncated_header": raw[:20],
+        "truncated_infos": raw[:200],
+        "data_past_end": raw[:-64],
+        "bad_version": raw[:4] + (7).to_bytes(4, "little") + raw[8:],
+    }
+    for name, data in cases.items():
+        p = str(tmp_path / f"{name}.gguf")
+        open(p, "wb").write(data)
+        assert not lib.moeb_gguf_open(p.encode()), name
+        assert lib.moeb_last_error().decode(), name
+    for typ, ne in ((99, (8, 1)), (12, (100, 1))):   # unknown type; 100 values of a 256-value block type
+        p = str(tmp_path / f"t{typ}.gguf")
+        write_gguf(p, [], [("x", typ, ne, bytes(4096))])
+        with pytest.raises(Exception):
+            Gguf(p)
+    g = Gguf(good)
+    assert g.str("gemma4.expert_count") is None          # wrong type asked for
+    assert g.u32("general.architecture") is None
+
+
+def test_loaders_fail_cleanly(tmp_path):
+    """Bad arguments, missing pages, pages longer than the slot stride and unreadable files are
+    refused before any copy is issued."""
+    from llapis_b200 import capi
+    from llapis_b200.loader import Store
+    lib = capi.lib()
+    idx = str(tmp_path / "s.experts.index")
+    write_with(lib, idx, idx.replace("index", "pack"), pages())
+    st = Store(idx)
+    ids = np.array([0, 1], np.int32)            # expert 1 has no page
+    dst = C.c_void_p(16)                        # never dereferenced: the page check fails first
+    assert lib.moeb_load_store_pages(st.h, 0, 0, 0, ids.ctypes.data, 2, dst, 1 << 20, 0, None) == -1
+    assert b"no page" in lib.moeb_last_error()
+    ids = np.array([0, 2], np.int32)
+    assert lib.moeb_load_store_pages(st.h, 0, 0, 0, ids.ctypes.data, 2, dst, 100, 0, None) == -1   # stride too small
+    assert lib.moeb_load_file_range(b"/nonexistent/file", 0, 10, dst, None) == -1
+    assert lib.moeb_load_file_range(None, 0, 10, dst, None) == -1
+    st.close()
