@@ -46,7 +46,11 @@ class Gguf:
             _lib().moeb_gguf_close(self.h)
             self.h = None
 
-    __del__ = close
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:   # interpreter shutdown: the library binding may already be gone
+            pass
 
     def tensor(self, name: str) -> capi.GgufTensor | None:
         t = capi.GgufTensor()
@@ -85,7 +89,11 @@ class Store:
             _lib().moert_store_reader_free(self.h)
             self.h = None
 
-    __del__ = close
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:   # interpreter shutdown: the library binding may already be gone
+            pass
 
     def info(self, layer: int, kind: int, is_scale: int, expert: int):
         """(quant_type, nbytes, shape) of a page, or None when absent."""
