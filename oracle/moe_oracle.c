@@ -21,6 +21,8 @@
 
 static const uint64_t k_iq2s_grid[MOE_IQ2S_GRID_ROWS] = MOE_IQ2S_GRID_INIT;
 static const int8_t   k_iq4nl[16] = MOE_IQ4NL_VALUES_INIT;
+static const uint64_t k_iq2xxs_grid[256] = MOE_IQ2XXS_GRID_INIT;
+static const uint8_t  k_iq2xxs_signs[128] = MOE_IQ2XXS_SIGNS_INIT;
 
 const uint64_t *oracle_iq2s_grid(void) { return k_iq2s_grid; }
 const int8_t   *oracle_iq4nl_values(void) { return k_iq4nl; }
@@ -79,6 +81,7 @@ size_t oracle_row_size(int32_t type, int64_t n) {
         case ORACLE_T_Q8_K:   return (size_t)(n / 256) * 292;
         case ORACLE_T_IQ4_NL: return (size_t)(n / 32) * 18;
         case ORACLE_T_IQ2_S:  return (size_t)(n / 256) * 82;
+        case ORACLE_T_IQ2_XXS: return (size_t)(n / 256) * 66;
         default:              return 0;
     }
 }
@@ -86,7 +89,7 @@ size_t oracle_row_size(int32_t type, int64_t n) {
 int32_t oracle_vec_dot_type(int32_t wtype) {
     /* ggml-cpu/ggml-cpu.c type_traits_cpu: K-quants and IQ2_S pair with Q8_K, the 32-blocks with Q8_0 */
     switch (wtype) {
-        case ORACLE_T_Q4_K: case ORACLE_T_IQ2_S: return ORACLE_T_Q8_K;
+        case ORACLE_T_Q4_K: case ORACLE_T_IQ2_S: case ORACLE_T_IQ2_XXS: return ORACLE_T_Q8_K;
         case ORACLE_T_Q5_0: case ORACLE_T_IQ4_NL: return ORACLE_T_Q8_0;
         default: return wtype;
     }
@@ -99,6 +102,8 @@ int32_t oracle_vec_dot_type(int32_t wtype) {
  * block_iq4_nl (ggml-common.h):        d f16 | qs[16]                                    18 B / 32
  * block_q8_K  (ggml-common.h:361):     d f32 | qs[256] | bsums[16] i16                   292 B
  * block_q8_0:                          d f16 | qs[32]                                    34 B
+ * block_iq2_xxs (ggml-common.h:371):   d f16 | 8 x (4 codebook indices u8 | 4 x 7-bit sign index
+ *                                      + 4-bit sub-scale, one u32)                        66 B / 256
  */
 static uint16_t rd16(const uint8_t *p) { return (uint16_t)(p[0] | (p[1] << 8)); }
 
@@ -153,6 +158,22 @@ void oracle_dequantize_row(int32_t type, const void *src, float *y, int64_t n) {
                         const float mag = (float)((row >> (8 * j)) & 0xff);
                         y[j] = dl * mag * ((signs[g] >> j) & 1 ? -1.f : 1.f);
                     }
+                    y += 8;
+                }
+            }
+        }
+    } else if (type == ORACLE_T_IQ2_XXS) {     /* dequantize_row_iq2_xxs, ggml-quants.c:2416 */
+        for (int64_t i = 0; i < n / 256; ++i, b += 66) {
+            const float d = h2f(rd16(b));
+            for (int ib = 0; ib < 8; ++ib) {
+                const uint8_t *g8 = b + 2 + 8 * ib;
+                const uint32_t hi = (uint32_t)g8[4] | ((uint32_t)g8[5] << 8) | ((uint32_t)g8[6] << 16) | ((uint32_t)g8[7] << 24);
+                const float db = d * (0.5f + (float)(hi >> 28)) * 0.25f;
+                for (int l = 0; l < 4; ++l) {
+                    const uint64_t row = k_iq2xxs_grid[g8[l]];
+                    const uint8_t sg = k_iq2xxs_signs[(hi >> (7 * l)) & 127];
+                    for (int j = 0; j < 8; ++j)
+                        y[j] = db * (float)((row >> (8 * j)) & 0xff) * ((sg >> j) & 1 ? -1.f : 1.f);
                     y += 8;
                 }
             }
@@ -336,8 +357,48 @@ static float dot_iq4nl(int64_t n, const uint8_t *w, const uint8_t *x) {
     return acc;
 }
 
+/* ggml_vec_dot_iq2_xxs_q8_K (ggml-cpu/quants.c:855): per 32-block the signed integer dot times
+ * (2 * sub-scale + 1), summed per super-block, scaled by d_w * d_x; the total times 1/8 */
+static float dot_iq2xxs(int64_t n, const uint8_t *w, const uint8_t *x) {
+    float acc = 0.f;
+    for (int64_t i = 0; i < n / 256; ++i, w += 66, x += 292) {
+        float dx; memcpy(&dx, x, 4);
+        const int8_t *q8 = (const int8_t *)(x + 4);
+        int bsum = 0;
+        for (int ib = 0; ib < 8; ++ib) {
+            const uint8_t *g8 = w + 2 + 8 * ib;
+            const uint32_t hi = (uint32_t)g8[4] | ((uint32_t)g8[5] << 8) | ((uint32_t)g8[6] << 16) | ((uint32_t)g8[7] << 24);
+            int s = 0;
+            for (int l = 0; l < 4; ++l) {
+                const uint64_t row = k_iq2xxs_grid[g8[l]];
+                const uint8_t sg = k_iq2xxs_signs[(hi >> (7 * l)) & 127];
+                for (int j = 0; j < 8; ++j) {
+                    const int mag = (int)((row >> (8 * j)) & 0xff);
+                    s += ((sg >> j) & 1 ? -mag : mag) * q8[32 * ib + 8 * l + j];
+                }
+            }
+            bsum += s * (int)(2 * (hi >> 28) + 1);
+        }
+        acc += (h2f(rd16(w)) * dx) * (float)bsum;
+    }
+    return 0.125f * acc;
+}
+
+/* ggml_vec_dot_q8_0_q8_0 (ggml-cpu/quants.c:400): integer dot per 32-block times d_w * d_x */
+static float dot_q8_0(int64_t n, const uint8_t *w, const uint8_t *x) {
+    float acc = 0.f;
+    for (int64_t i = 0; i < n / 32; ++i, w += 34, x += 34) {
+        int s = 0;
+        for (int j = 0; j < 32; ++j) s += (int8_t)w[2 + j] * (int8_t)x[2 + j];
+        acc += (float)s * (h2f(rd16(w)) * h2f(rd16(x)));
+    }
+    return acc;
+}
+
 float oracle_vec_dot(int32_t wtype, int64_t n, const void *w, const void *xq) {
     switch (wtype) {
+        case ORACLE_T_IQ2_XXS: return dot_iq2xxs(n, (const uint8_t *)w, (const uint8_t *)xq);
+        case ORACLE_T_Q8_0:   return dot_q8_0(n, (const uint8_t *)w, (const uint8_t *)xq);
         case ORACLE_T_Q4_K:   return dot_q4k(n, (const uint8_t *)w, (const uint8_t *)xq);
         case ORACLE_T_IQ2_S:  return dot_iq2s(n, (const uint8_t *)w, (const uint8_t *)xq);
         case ORACLE_T_Q5_0:   return dot_q5_0(n, (const uint8_t *)w, (const uint8_t *)xq);

@@ -29,7 +29,7 @@ extern "C" {
 /* ggml type ids (third_party/llama/ggml/include/ggml.h:390-432) */
 enum {
     ORACLE_T_F32 = 0, ORACLE_T_F16 = 1, ORACLE_T_Q5_0 = 6, ORACLE_T_Q8_0 = 8, ORACLE_T_Q4_K = 12,
-    ORACLE_T_Q8_K = 15, ORACLE_T_IQ4_NL = 20, ORACLE_T_IQ2_S = 22,
+    ORACLE_T_Q8_K = 15, ORACLE_T_IQ2_XXS = 16, ORACLE_T_IQ4_NL = 20, ORACLE_T_IQ2_S = 22,
 };
 
 typedef struct oracle_layer {
@@ -109,6 +109,8 @@ int32_t ref_vec_dot_type(int32_t wtype);
 float   ref_vec_dot(int32_t wtype, int64_t n, const void *w_row, const void *x_q);
 uint16_t ref_gelu_table(uint16_t h);
 int     ref_moe_layer(const oracle_layer *L, oracle_layer_out *o);
+size_t  ref_quantize_imatrix(int32_t type, const float *src, void *dst, int64_t nrow, int64_t n_per_row,
+                             const float *imatrix);
 void    ref_rms_norm(const float *x, const float *w, float s, float *y, int64_t rows, int64_t n, float eps);
 
 #ifdef __cplusplus

@@ -13,7 +13,7 @@ REF_SO = os.path.join(HERE, "_ref", "libref_runner.so")
 PORT_SO = os.path.join(HERE, "_build", "libmoe_oracle.so")
 
 # ggml type ids (third_party/llama/ggml/include/ggml.h:390-432)
-F32, F16, Q5_0, Q8_0, Q4_K, Q8_K, IQ4_NL, IQ2_S = 0, 1, 6, 8, 12, 15, 20, 22
+F32, F16, Q5_0, Q8_0, Q4_K, Q8_K, IQ2_XXS, IQ4_NL, IQ2_S = 0, 1, 6, 8, 12, 15, 16, 20, 22
 
 
 class _Layer(C.Structure):
@@ -211,16 +211,25 @@ class Ref(_Oracle):
     def __init__(self):
         super().__init__(REF_SO)
         self._quant = self._fn("ref_quantize", C.c_size_t, [C.c_int32, C.c_void_p, C.c_void_p, C.c_int64, C.c_int64])
+        self._quant_im = self._fn("ref_quantize_imatrix", C.c_size_t,
+                                  [C.c_int32, C.c_void_p, C.c_void_p, C.c_int64, C.c_int64, C.c_void_p])
         self._gelu = self._fn("ref_gelu_table", C.c_uint16, [C.c_uint16])
         self.lib.ref_init()
 
-    def quantize(self, t: int, w: np.ndarray) -> np.ndarray:
-        """Reference quantiser ggml_quantize_chunk (ggml.c:7761) over rows of ``w`` (f32 [..., n])."""
+    def quantize(self, t: int, w: np.ndarray, imatrix: np.ndarray | None = None) -> np.ndarray:
+        """Reference quantiser ggml_quantize_chunk (ggml.c:7761) over rows of ``w`` (f32 [..., n]).
+        IQ2_XXS needs an importance matrix; without one given, a uniform one is used."""
         w = np.ascontiguousarray(w, np.float32)
         n = w.shape[-1]
         nrow = w.size // n
         out = np.zeros(nrow * self.row_size(t, n), np.uint8)
-        self._quant(t, w.ctypes.data, out.ctypes.data, nrow, n)
+        if imatrix is None and t == IQ2_XXS:
+            imatrix = np.ones(n, np.float32)
+        if imatrix is None:
+            self._quant(t, w.ctypes.data, out.ctypes.data, nrow, n)
+        else:
+            im = np.ascontiguousarray(imatrix, np.float32)
+            self._quant_im(t, w.ctypes.data, out.ctypes.data, nrow, n, im.ctypes.data)
         return out.reshape(*w.shape[:-1], self.row_size(t, n))
 
     def gelu_table(self) -> np.ndarray:

@@ -73,6 +73,14 @@ extern "C" size_t ref_quantize(int32_t type, const float * src, void * dst, int6
     return ggml_quantize_chunk((ggml_type) type, src, dst, 0, nrow, n_per_row, nullptr);
 }
 
+// the same with an importance matrix (f32 [n_per_row]); the types ggml quantises only with one
+// (IQ2_XXS, IQ2_XS, IQ1_S: ggml.c:7753-7772) need it
+extern "C" size_t ref_quantize_imatrix(int32_t type, const float * src, void * dst, int64_t nrow, int64_t n_per_row,
+                                       const float * imatrix) {
+    ref_init();
+    return ggml_quantize_chunk((ggml_type) type, src, dst, 0, nrow, n_per_row, imatrix);
+}
+
 extern "C" void ref_dequantize_row(int32_t type, const void * src, float * dst, int64_t n) {
     ref_init();
     ggml_get_type_traits((ggml_type) type)->to_float(src, dst, n);

@@ -3,6 +3,7 @@
     make -C oracle ref          # builds oracle/_ref from the reference sources
     python tests/golden/make_golden.py           # golden.npz
     python tests/golden/make_golden.py --block   # golden_block.npz (the Gemma-4 block norms)
+    python tests/golden/make_golden.py --types   # golden_types.npz + the IQ2_XXS tables (IQ2_XXS / Q8_0 weights)
 
 Everything in the fixtures comes out of the reference's own code (ggml-base + ggml-cpu of the
 vendored llama.cpp, compiled into oracle/_ref): quantised bytes from ggml_quantize_chunk, dequantised
@@ -27,7 +28,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, ROOT)
 
-from oracle.oracle import IQ2_S, IQ4_NL, Q4_K, Q5_0, Q8_0, Q8_K, LayerSpec, Ref  # noqa: E402
+from oracle.oracle import IQ2_S, IQ2_XXS, IQ4_NL, Q4_K, Q5_0, Q8_0, Q8_K, LayerSpec, Ref  # noqa: E402
 from llapis_b200 import workload  # noqa: E402
 
 
@@ -62,7 +63,34 @@ def extract_tables(r: Ref):
     return grid, kv
 
 
-def write_tables(grid, kv):
+def extract_iq2xxs_tables(r: Ref):
+    """The IQ2_XXS codebook (256 rows) and its 128 sign patterns, through the reference dequantiser
+    (dequantize_row_iq2_xxs, ggml-quants.c:2416): with d = 8 and a zero sub-scale a group's
+    multiplier is exactly 1, so sign index 0 returns codebook rows verbatim, and codebook row 0
+    (no zero magnitude) shows each sign pattern as the negative entries."""
+    def block(idx, sgn):   # 32 groups: codebook indices and sign indices, sub-scale 0
+        blk = np.zeros(66, np.uint8)
+        blk[0:2] = np.frombuffer(np.float16(8.0).tobytes(), np.uint8)
+        for ib in range(8):
+            w0 = sum(int(idx[4 * ib + l]) << (8 * l) for l in range(4))
+            w1 = sum(int(sgn[4 * ib + l]) << (7 * l) for l in range(4))
+            blk[2 + 8 * ib:2 + 8 * ib + 8] = np.frombuffer(np.array([w0, w1], np.uint32).tobytes(), np.uint8)
+        return blk
+    grid = np.zeros(256, np.uint64)
+    for b in range(8):
+        y = r.dequantize(IQ2_XXS, block(range(32 * b, 32 * b + 32), [0] * 32), 256)
+        for g in range(32):
+            grid[32 * b + g] = np.frombuffer(y[8 * g:8 * g + 8].astype(np.uint8).tobytes(), np.uint64)[0]
+    assert all(((int(grid[0]) >> (8 * j)) & 0xff) for j in range(8))
+    signs = np.zeros(128, np.uint8)
+    for b in range(4):
+        y = r.dequantize(IQ2_XXS, block([0] * 32, range(32 * b, 32 * b + 32)), 256)
+        for g in range(32):
+            signs[32 * b + g] = sum(1 << j for j in range(8) if y[8 * g + j] < 0)
+    return grid, signs
+
+
+def write_tables(grid, kv, xxs_grid=None, xxs_signs=None):
     body = ("/* IQ2_S codebook: 1024 rows of 8 unsigned magnitudes in {8, 25, 43}, packed little-endian\n"
             " * into one 64-bit word per row. Format constant of ggml's block_iq2_s; the values were\n"
             " * recovered by dequantising crafted blocks through the reference dequantiser\n"
@@ -74,6 +102,14 @@ def write_tables(grid, kv):
     body += "}\n\n/* IQ4_NL non-linear 4-bit levels (block_iq4_nl format constant), recovered the same way through\n" \
             " * dequantize_row_iq4_nl (ggml-quants.c:2653) with d = 1. */\n"
     body += "#define MOE_IQ4NL_VALUES_INIT { " + ", ".join(str(int(v)) for v in kv) + " }\n"
+    if xxs_grid is not None:
+        body += ("\n/* IQ2_XXS codebook (256 rows of 8 magnitudes, one 64-bit word per row) and its 128 sign\n"
+                 " * patterns (bit j set: value j negative), format constants of ggml's block_iq2_xxs, recovered\n"
+                 " * through dequantize_row_iq2_xxs (ggml-quants.c:2416) with d = 8 and a zero sub-scale. */\n"
+                 "#define MOE_IQ2XXS_GRID_INIT { \\\n")
+        for i in range(0, 256, 4):
+            body += "    " + ", ".join("0x%016xull" % int(v) for v in xxs_grid[i:i + 4]) + (", \\\n" if i + 4 < 256 else " \\\n")
+        body += "}\n#define MOE_IQ2XXS_SIGNS_INIT { " + ", ".join(str(int(v)) for v in xxs_signs) + " }\n"
     with open(os.path.join(ROOT, "llapis_b200", "csrc", "ggml_tables.inc"), "w") as f:
         f.write("/* Generated by tests/golden/make_golden.py — do not edit. */\n" + body)
     with open(os.path.join(ROOT, "oracle", "ggml_tables.inc"), "w") as f:
@@ -241,8 +277,56 @@ def main_block():
     print("wrote", path, os.path.getsize(path), "bytes")
 
 
+def main_types():
+    """IQ2_XXS and Q8_0 expert weights (the other types the product files use): the tables, reference
+    dequantised rows, and a mini layer whose cold class is IQ2_XXS gate_up / IQ4_NL down and whose
+    hot class is Q8_0 gate_up and down, through the reference's MUL_MAT_ID graph."""
+    r = Ref()
+    write_tables(*extract_tables(r), *extract_iq2xxs_tables(r))
+    rng = np.random.default_rng(20261203)
+    fx = {}
+    for t, n in ((IQ2_XXS, 512), (Q8_0, 64)):
+        w = rng.normal(0, 0.02, (6, n)).astype(np.float32)
+        w[1] *= 1e-3
+        w[2, 3] = 0.5
+        q = r.quantize(t, w)
+        fx[f"deq_{t}_src"] = q
+        fx[f"deq_{t}_f32"] = np.stack([r.dequantize(t, q[i], n) for i in range(len(q))])
+    cfg = workload.CONFIGS["mini_mixed"]
+    E, d, nff, hot = cfg.n_expert, cfg.d_model, cfg.n_ff, list(cfg.hot)
+    cold_gu, cold_dn, hot_gu, hot_dn = [], [], [], []
+    for e in range(E):
+        gu, dn = workload.expert_f32(cfg, 0, e)
+        cold_gu.append(r.quantize(IQ2_XXS, gu))
+        cold_dn.append(r.quantize(IQ4_NL, dn))
+        if e in hot:
+            hot_gu.append(r.quantize(Q8_0, gu))
+            hot_dn.append(r.quantize(Q8_0, dn))
+    x = workload.make_input(cfg, n_tokens=12, stream=5)
+    K = len(hot)
+    exp_slot = np.full(E, -1, np.int32)
+    exp_slot[hot] = np.arange(K, dtype=np.int32)
+    spec = LayerSpec(d, nff, E, cfg.top_k, x=x, w_router=workload._normal((cfg.seed, 0, 1 << 20), (E, d), 0.02),
+                     n_slots=K, exp_slot=exp_slot, slot_exp=np.array(hot, np.int32),
+                     slot_state=np.full(K, 2, np.int32), hot_type_gu=Q8_0, hot_type_down=Q8_0,
+                     hot_gu=np.stack(hot_gu), hot_down=np.stack(hot_dn), s_hot=np.ones(K, np.float32),
+                     cold_type_gu=IQ2_XXS, cold_type_down=IQ4_NL, cold_gu=np.stack(cold_gu),
+                     cold_down=np.stack(cold_dn), s_cold=np.ones(E, np.float32))
+    res = r.moe_layer(spec, n_threads=4)
+    for k, v in res.items():
+        fx[f"types_{k}"] = v
+    fx["types_x"] = x
+    for n in ("hot_gu", "hot_down", "cold_gu", "cold_down"):   # the pools are regenerated by the tests
+        fx[f"types_sha_{n}"] = np.array(sha(getattr(spec, n)))
+    path = os.path.join(HERE, "golden_types.npz")
+    np.savez_compressed(path, **fx)
+    print("wrote", path, os.path.getsize(path), "bytes")
+
+
 if __name__ == "__main__":
-    if "--block" in sys.argv:
+    if "--types" in sys.argv:
+        main_types()
+    elif "--block" in sys.argv:
         main_block()
     else:
         main()

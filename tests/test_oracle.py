@@ -153,3 +153,56 @@ def test_rms_norm_port_vs_reference_live(ref, port):
         for args in ((None, 1.0), (w, 1.0), (w, c)):
             a, b = ref.rms_norm(x, 1e-6, *args), port.rms_norm(x, 1e-6, *args)
             assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+
+
+@pytest.fixture(scope="module")
+def golden_types():
+    """Reference outputs for IQ2_XXS / Q8_0 expert weights (tests/golden/make_golden.py --types)."""
+    import os
+    from conftest import ROOT
+    return dict(np.load(os.path.join(ROOT, "tests", "golden", "golden_types.npz"), allow_pickle=False))
+
+
+@pytest.mark.parametrize("t,n", [(16, 512), (Q8_0, 64)])
+def test_iq2xxs_q8_0_dequant_bit_exact(golden_types, port, t, n):
+    """IQ2_XXS (codebook + sign-pattern tables recovered from the reference) and Q8_0 weight rows
+    dequantise bit for bit as the reference's dequantize_row_iq2_xxs / _q8_0."""
+    src, want = golden_types[f"deq_{t}_src"], golden_types[f"deq_{t}_f32"]
+    for i in range(len(src)):
+        assert np.array_equal(port.dequantize(t, src[i], n).view(np.uint32), want[i].view(np.uint32)), f"row {i}"
+
+
+def test_iq2xxs_q8_0_layer_matches_reference_fixture(golden_types, port, ref):
+    """A mini layer whose cold class is IQ2_XXS gate_up / IQ4_NL down and whose hot class is Q8_0
+    gate_up and down: the pools from the reference quantiser (digests pinned), then the port's
+    layer against the reference's MUL_MAT_ID graph."""
+    from llapis_b200 import workload
+    from oracle import LayerSpec
+    from oracle.oracle import IQ2_XXS
+    cfg = workload.CONFIGS["mini_mixed"]
+    E, d, nff, hot = cfg.n_expert, cfg.d_model, cfg.n_ff, list(cfg.hot)
+    pools = {n: [] for n in ("cold_gu", "cold_down", "hot_gu", "hot_down")}
+    for e in range(E):
+        gu, dn = workload.expert_f32(cfg, 0, e)
+        pools["cold_gu"].append(ref.quantize(IQ2_XXS, gu))
+        pools["cold_down"].append(ref.quantize(IQ4_NL, dn))
+        if e in hot:
+            pools["hot_gu"].append(ref.quantize(Q8_0, gu))
+            pools["hot_down"].append(ref.quantize(Q8_0, dn))
+    pools = {n: np.stack(v) for n, v in pools.items()}
+    for n, v in pools.items():
+        assert sha(v) == str(golden_types[f"types_sha_{n}"]), n
+    K = len(hot)
+    exp_slot = np.full(E, -1, np.int32)
+    exp_slot[hot] = np.arange(K, dtype=np.int32)
+    spec = LayerSpec(d, nff, E, cfg.top_k, x=golden_types["types_x"],
+                     w_router=workload._normal((cfg.seed, 0, 1 << 20), (E, d), 0.02), n_slots=K, exp_slot=exp_slot,
+                     slot_exp=np.array(hot, np.int32), slot_state=np.full(K, 2, np.int32), hot_type_gu=Q8_0,
+                     hot_type_down=Q8_0, s_hot=np.ones(K, np.float32), cold_type_gu=IQ2_XXS, cold_type_down=IQ4_NL,
+                     s_cold=np.ones(E, np.float32), **pools)
+    res = port.moe_layer(spec)
+    assert np.array_equal(res["ids"], golden_types["types_ids"])
+    np.testing.assert_allclose(res["logits"], golden_types["types_logits"], rtol=1e-5, atol=1e-6)
+    assert_layer_close(res["gate_up"], golden_types["types_gate_up"], tol=1e-5)
+    assert_layer_close(res["down"], golden_types["types_down"], tol=1e-4)
+    assert_layer_close(res["out"], golden_types["types_out"], tol=1e-4)
