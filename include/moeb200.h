@@ -41,6 +41,8 @@ enum {
 
 /* ggml type ids accepted as weight types (third_party/llama/ggml/include/ggml.h:390-432) */
 enum { MOEB_T_Q5_0 = 6, MOEB_T_Q4_K = 12, MOEB_T_IQ4_NL = 20, MOEB_T_IQ2_S = 22 };
+/* further expert types the product files use; so far moeb_dequantize and moeb_row_size only */
+enum { MOEB_T_Q8_0 = 8, MOEB_T_IQ2_XXS = 16 };
 
 /* One HBM-resident precision class: merged gate_up [n][2*n_ff rows][row(d_model)] and
  * down [n][d_model rows][row(n_ff)], each in ggml block layout. */
@@ -218,7 +220,8 @@ int moeb_router_topk(const float *logits, int32_t n_tokens, int32_t n_expert, in
 int moeb_dispatch(const int32_t *ids, int32_t n_tokens, int32_t top_k, int32_t n_expert,
                   int32_t *counts, int32_t *offsets, int32_t *perm, void *stream);
 
-/* Weight dequantisation to f32 rows (bit-exact with ggml's dequantize_row_*). */
+/* Weight dequantisation to f32 rows (bit-exact with ggml's dequantize_row_*): Q4_K, IQ2_S, Q5_0,
+ * IQ4_NL, IQ2_XXS, Q8_0. */
 int moeb_dequantize(int32_t type, const void *src, float *dst, int64_t n_rows, int64_t n_per_row, void *stream);
 
 /* Activation quantisation of f32 rows to the vec_dot type of `wtype` (Q8_K for Q4_K/IQ2_S, Q8_0

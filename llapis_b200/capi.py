@@ -11,7 +11,7 @@ import os
 from . import build as _build
 
 # ggml type ids (third_party/llama/ggml/include/ggml.h:390-432)
-Q5_0, Q4_K, IQ4_NL, IQ2_S, Q8_0, Q8_K = 6, 12, 20, 22, 8, 15
+Q5_0, Q4_K, IQ4_NL, IQ2_S, Q8_0, Q8_K, IQ2_XXS = 6, 12, 20, 22, 8, 15, 16
 
 ERRORS = {0: "OK", -1: "EINVAL", -2: "ENODEV", -3: "ECUDA", -4: "ESPACE", -5: "EDEVICE", -6: "ETYPE"}
 

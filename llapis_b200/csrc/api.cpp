@@ -604,9 +604,10 @@ extern "C" int moeb_dispatch(const int32_t *ids, int32_t n_tokens, int32_t top_k
 }
 
 extern "C" int moeb_dequantize(int32_t type, const void *src, float *dst, int64_t n_rows, int64_t n_per_row, void *stream) {
-    if (type != MOEB_T_Q4_K && type != MOEB_T_IQ2_S && type != MOEB_T_Q5_0 && type != MOEB_T_IQ4_NL)
+    if (type != MOEB_T_Q4_K && type != MOEB_T_IQ2_S && type != MOEB_T_Q5_0 && type != MOEB_T_IQ4_NL &&
+        type != MOEB_T_IQ2_XXS && type != MOEB_T_Q8_0)
         return fail(MOEB_ETYPE, "moeb_dequantize: type %d unsupported", type);
-    const int blk = (type == MOEB_T_Q4_K || type == MOEB_T_IQ2_S) ? QK_K : QK32;
+    const int blk = (type == MOEB_T_Q4_K || type == MOEB_T_IQ2_S || type == MOEB_T_IQ2_XXS) ? QK_K : QK32;
     if (!src || !dst || n_rows <= 0 || n_per_row <= 0 || n_per_row % blk)
         return fail(MOEB_EINVAL, "moeb_dequantize: bad shape");
     int rc = ensure_device();

@@ -15,9 +15,12 @@ namespace moeb {
 // ---------------------------------------------------------------- format tables (device copies)
 // All device code of the library is one translation unit (kernels.cu includes the kernel
 // headers), so these module-scope variables are defined here, once.
-// IQ2_S codebook (1024 rows x 8 magnitudes) and IQ4_NL levels: format constants of ggml's blocks.
+// IQ2_S codebook (1024 rows x 8 magnitudes), IQ4_NL levels, IQ2_XXS codebook (256 rows) and sign
+// patterns: format constants of ggml's blocks.
 __device__ uint64_t g_iq2s_grid[MOE_IQ2S_GRID_ROWS] = MOE_IQ2S_GRID_INIT;
 __device__ int8_t g_iq4nl[16] = MOE_IQ4NL_VALUES_INIT;
+__device__ uint64_t g_iq2xxs_grid[256] = MOE_IQ2XXS_GRID_INIT;
+__device__ uint8_t g_iq2xxs_signs[128] = MOE_IQ2XXS_SIGNS_INIT;
 // ggml-cpu's fp16 GELU table (gelu_tanh rounded to f16, indexed by the f16 bit pattern of the
 // gate value); filled from the host once per device.
 __device__ uint16_t g_gelu_f16[1 << 16];

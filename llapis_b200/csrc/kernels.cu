@@ -1840,7 +1840,7 @@ __global__ void __launch_bounds__(kThreads, 1) route_only_kernel(RouteSrc r, int
 
 // ------------------------------------------------------------------ dequantisation (bit-exact)
 // One thread per 32 output values. Products are rounded exactly as the ggml dequantisers write
-// them (ggml-quants.c:442,1471,2471,2653): no fused multiply-add.
+// them (ggml-quants.c:442,1471,2416,2471,2653; Q8_0 as dequantize_row_q8_0): no fused multiply-add.
 __global__ void dequant_kernel(int32_t type, const uint8_t *src, float *dst, int64_t rows, int64_t n) {
     const int64_t nchunk = n / 32;
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -1880,6 +1880,23 @@ __global__ void dequant_kernel(int32_t type, const uint8_t *src, float *dst, int
                 y[8 * l + jj] = __fmul_rn(__fmul_rn(dl, mag), ((sg >> jj) & 1) ? -1.f : 1.f);
             }
         }
+    } else if (type == T_IQ2_XXS) {
+        // 32-value group ib: four codebook rows, four sign patterns, one sub-scale
+        const uint8_t *blk = row + (c / 8) * B_IQ2_XXS;
+        const uint8_t *g8 = blk + 2 + 8 * (c % 8);
+        const float d = h2f(ld_u16(blk));
+        const uint32_t hi = (uint32_t)g8[4] | ((uint32_t)g8[5] << 8) | ((uint32_t)g8[6] << 16) | ((uint32_t)g8[7] << 24);
+        const float db = __fmul_rn(__fmul_rn(d, __fadd_rn(0.5f, (float)(hi >> 28))), 0.25f);
+        for (int l = 0; l < 4; ++l) {
+            const uint64_t gv = g_iq2xxs_grid[g8[l]];
+            const uint8_t sg = g_iq2xxs_signs[(hi >> (7 * l)) & 127];
+            for (int jj = 0; jj < 8; ++jj)
+                y[8 * l + jj] = __fmul_rn(__fmul_rn(db, (float)((gv >> (8 * jj)) & 0xff)), ((sg >> jj) & 1) ? -1.f : 1.f);
+        }
+    } else if (type == T_Q8_0) {
+        const uint8_t *blk = row + c * B_Q8_0;
+        const float d = h2f(ld_u16(blk));
+        for (int jj = 0; jj < 32; ++jj) y[jj] = __fmul_rn((float)(int8_t)blk[2 + jj], d);
     } else if (type == T_Q5_0) {
         const uint8_t *blk = row + c * B_Q5_0;
         const float d = h2f(ld_u16(blk));

@@ -17,13 +17,14 @@ namespace moeb {
 // ggml type ids (third_party/llama/ggml/include/ggml.h:390-432); they travel through the moert
 // ABI as opaque "type tags".
 enum : int32_t {
-    T_F32 = 0, T_F16 = 1, T_Q5_0 = 6, T_Q8_0 = 8, T_Q4_K = 12, T_Q8_K = 15, T_IQ4_NL = 20, T_IQ2_S = 22,
+    T_F32 = 0, T_F16 = 1, T_Q5_0 = 6, T_Q8_0 = 8, T_Q4_K = 12, T_Q8_K = 15, T_IQ2_XXS = 16, T_IQ4_NL = 20, T_IQ2_S = 22,
 };
 
 constexpr int QK_K = 256;
 constexpr int QK32 = 32;
 constexpr int B_Q4_K = 144;    // d f16 | dmin f16 | scales[12] | qs[128]
 constexpr int B_IQ2_S = 82;    // d f16 | qs[32] | signs[32] | qh[8] | scales[8]
+constexpr int B_IQ2_XXS = 66;  // d f16 | 8 x (4 codebook indices u8 | u32: 4 x 7-bit sign index, 4-bit sub-scale)
 constexpr int B_Q5_0 = 22;     // d f16 | qh[4] | qs[16]
 constexpr int B_IQ4_NL = 18;   // d f16 | qs[16]
 constexpr int B_Q8_K = 292;    // d f32 | qs[256] | bsums[16] i16
@@ -35,6 +36,7 @@ MOEB_HD inline int64_t row_bytes(int32_t type, int64_t n) {
         case T_F16:    return n * 2;
         case T_Q4_K:   return n / QK_K * B_Q4_K;
         case T_IQ2_S:  return n / QK_K * B_IQ2_S;
+        case T_IQ2_XXS: return n / QK_K * B_IQ2_XXS;
         case T_Q5_0:   return n / QK32 * B_Q5_0;
         case T_IQ4_NL: return n / QK32 * B_IQ4_NL;
         case T_Q8_K:   return n / QK_K * B_Q8_K;

@@ -43,6 +43,20 @@ def test_dequant_bit_exact(golden, t, n):
     assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
 
 
+@pytest.mark.parametrize("t,n", [(16, 512), (8, 64)])
+def test_dequant_iq2xxs_q8_0_bit_exact(t, n):
+    """IQ2_XXS and Q8_0 expert weights (the other types the product files use) dequantise bit for
+    bit as the reference's dequantize_row_iq2_xxs / _q8_0 (rows from tests/golden/golden_types.npz)."""
+    import os
+    from conftest import ROOT
+    g = np.load(os.path.join(ROOT, "tests", "golden", "golden_types.npz"))
+    src, want = g[f"deq_{t}_src"], g[f"deq_{t}_f32"]
+    out = torch.empty(want.shape, dtype=torch.float32, device="cuda")
+    capi.check(capi.lib().moeb_dequantize(t, dev(src).data_ptr(), out.data_ptr(), src.shape[0], n, stream()))
+    assert np.array_equal(out.cpu().numpy().view(np.uint32), want.view(np.uint32))
+    assert capi.lib().moeb_row_size(t, n) == src.shape[1]
+
+
 @pytest.mark.parametrize("wt,vdt", [(Q4_K, Q8_K), (Q5_0, Q8_0)])
 def test_activation_quant_bit_exact(golden, wt, vdt):
     x, want = golden[f"act_{vdt}_x"], golden[f"act_{vdt}_q"]
