@@ -1,10 +1,11 @@
-// Host-side expert-weight quantiser (moeb_quantize_weights): the four ggml formats the MoE path
-// serves, restated from the reference quantiser without an importance matrix
-// (ggml_quantize_chunk, third_party/llama/ggml/src/ggml.c:7761):
+// Host-side expert-weight quantiser (moeb_quantize_weights): the ggml formats the MoE path serves,
+// restated from the reference quantiser without an importance matrix (IQ2_XXS, which ggml
+// quantises only with one, with a uniform one) (ggml_quantize_chunk, ggml/src/ggml.c:7761):
 //   Q4_K   quantize_row_q4_K_ref + make_qkx2_quants  (ggml-quants.c:1399, :741)
 //   Q5_0   quantize_row_q5_0_ref                      (ggml-quants.c:149)
 //   IQ4_NL quantize_row_iq4_nl_impl, 7 scale trials    (ggml-quants.c:4894, :5005)
 //   IQ2_S  quantize_row_iq2_s_impl + the codebook map  (ggml-quants.c:5070, :2781, :3198)
+//   IQ2_XXS quantize_row_iq2_xxs_impl + make_qp_quants (ggml-quants.c:3222, :1018)
 // Every float expression keeps the reference's evaluation order and this file is compiled with
 // -ffp-contract=off, so the output bytes equal the reference quantiser's (checked by the tests).
 // Rows are independent and are spread over host threads.
@@ -264,59 +265,84 @@ void iq4_nl_row(const float *x, uint8_t *y, int64_t n) {
     }
 }
 
-// ---------------------------------------------------------------- IQ2_S
-// The quantiser works on the codebook in its search form: each of the 1024 rows is 8 levels
-// l in {0,1,2} (value 2l+1), packed as u = sum l_i << 2i. `map[u]` is the codebook row of u, or
-// -(offset+1) into `nbr` where the rows at the smallest squared distance from u are listed
-// (count first, then rows in (distance, row) order) — the layout of iq2xs_init_impl.
+// ---------------------------------------------------------------- IQ2_S / IQ2_XXS codebook search
+// The quantisers work on a codebook in its search form: each row is 8 levels l in {0,1,2} (value
+// 2l+1), packed as u = sum l_i << 2i. `map[u]` is the codebook row of u, or -(offset+1) into `nbr`
+// where the rows at the `nwant` smallest squared distances from u are listed (count first, then
+// rows in (distance, row) order) — the layout of iq2xs_init_impl (ggml-quants.c:2781-3190; nwant
+// is 1 for IQ2_S and 2 for IQ2_XXS).
 struct Iq2sSearch {
-    uint64_t grid[1024];       // rows as int8 levels 1/3/5
-    std::vector<int> map;      // 43692 entries
+    std::vector<uint64_t> grid;   // rows as int8 levels 1/3/5
+    std::vector<int> map;         // 43692 entries
     std::vector<uint16_t> nbr;
 };
+
+// dq: the dequantisation rows (magnitudes 8, 25, 43 per byte)
+void build_search(Iq2sSearch &S, const uint64_t *dq, int rows, int nwant) {
+    S.grid.resize(rows);
+    for (int r = 0; r < rows; ++r) {
+        uint64_t g = 0;
+        for (int i = 0; i < 8; ++i) {
+            const int mag = (int)((dq[r] >> (8 * i)) & 0xff);
+            const int l = mag == 8 ? 0 : mag == 25 ? 1 : 2;
+            g |= (uint64_t)(2 * l + 1) << (8 * i);
+        }
+        S.grid[r] = g;
+    }
+    const int kmap = 43692;
+    S.map.assign(kmap, -1);
+    for (int r = 0; r < rows; ++r) {
+        int u = 0;
+        for (int i = 0; i < 8; ++i) u |= ((int)(((S.grid[r] >> (8 * i)) & 0xff) - 1) / 2) << (2 * i);
+        S.map[u] = r;
+    }
+    std::vector<std::pair<int, int>> dist(rows);
+    for (int u = 0; u < kmap; ++u) {
+        if (S.map[u] >= 0) continue;
+        int pos[8];
+        for (int i = 0; i < 8; ++i) pos[i] = 2 * ((u >> (2 * i)) & 3) + 1;
+        for (int r = 0; r < rows; ++r) {
+            int d2 = 0;
+            for (int i = 0; i < 8; ++i) {
+                const int q = (int)((S.grid[r] >> (8 * i)) & 0xff) - pos[i];
+                d2 += q * q;
+            }
+            dist[r] = {d2, r};
+        }
+        std::sort(dist.begin(), dist.end());
+        S.map[u] = -((int)S.nbr.size() + 1);
+        const size_t at = S.nbr.size();
+        S.nbr.push_back(0);
+        int n = 0, have = 1, d2 = dist[0].first;
+        for (int r = 0; r < rows; ++r) {
+            if (dist[r].first > d2) {   // the next distinct distance
+                if (have == nwant) break;
+                d2 = dist[r].first;
+                ++have;
+            }
+            S.nbr.push_back((uint16_t)dist[r].second);
+            ++n;
+        }
+        S.nbr[at] = (uint16_t)n;
+    }
+}
 
 const Iq2sSearch &iq2s_search() {
     static Iq2sSearch S;
     static std::once_flag once;
     std::call_once(once, [] {
-        static const uint64_t dq[1024] = MOE_IQ2S_GRID_INIT;   // dequantisation rows: 8, 25, 43
-        for (int r = 0; r < 1024; ++r) {
-            uint64_t g = 0;
-            for (int i = 0; i < 8; ++i) {
-                const int mag = (int)((dq[r] >> (8 * i)) & 0xff);
-                const int l = mag == 8 ? 0 : mag == 25 ? 1 : 2;
-                g |= (uint64_t)(2 * l + 1) << (8 * i);
-            }
-            S.grid[r] = g;
-        }
-        const int kmap = 43692;
-        S.map.assign(kmap, -1);
-        for (int r = 0; r < 1024; ++r) {
-            int u = 0;
-            for (int i = 0; i < 8; ++i) u |= ((int)(((S.grid[r] >> (8 * i)) & 0xff) - 1) / 2) << (2 * i);
-            S.map[u] = r;
-        }
-        std::vector<std::pair<int, int>> dist(1024);
-        for (int u = 0; u < kmap; ++u) {
-            if (S.map[u] >= 0) continue;
-            int pos[8];
-            for (int i = 0; i < 8; ++i) pos[i] = 2 * ((u >> (2 * i)) & 3) + 1;
-            for (int r = 0; r < 1024; ++r) {
-                int d2 = 0;
-                for (int i = 0; i < 8; ++i) {
-                    const int q = (int)((S.grid[r] >> (8 * i)) & 0xff) - pos[i];
-                    d2 += q * q;
-                }
-                dist[r] = {d2, r};
-            }
-            std::sort(dist.begin(), dist.end());
-            S.map[u] = -((int)S.nbr.size() + 1);
-            const size_t at = S.nbr.size();
-            S.nbr.push_back(0);
-            int n = 0;
-            for (int r = 0; r < 1024 && dist[r].first == dist[0].first; ++r, ++n) S.nbr.push_back((uint16_t)dist[r].second);
-            S.nbr[at] = (uint16_t)n;
-        }
+        static const uint64_t dq[1024] = MOE_IQ2S_GRID_INIT;
+        build_search(S, dq, 1024, 1);
+    });
+    return S;
+}
+
+const Iq2sSearch &iq2xxs_search() {
+    static Iq2sSearch S;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        static const uint64_t dq[256] = MOE_IQ2XXS_GRID_INIT;
+        build_search(S, dq, 256, 2);
     });
     return S;
 }
@@ -461,6 +487,194 @@ void iq2_s_row(const float *x, uint8_t *y, int64_t n) {
     }
 }
 
+// make_qp_quants (ggml-quants.c:1018-1089): levels 0..nmax for non-negative x with weights w,
+// a scale search over nine candidates, then up to five rounds of single-level improvements
+float make_qp_quants(int n, int nmax, const float *x, uint8_t *L, const float *w) {
+    float max = 0;
+    for (int i = 0; i < n; ++i) max = std::max(max, x[i]);
+    if (max < 1e-15f) {
+        for (int i = 0; i < n; ++i) L[i] = 0;
+        return 0.f;
+    }
+    float iscale = nmax / max;
+    for (int i = 0; i < n; ++i) L[i] = (uint8_t)rne(iscale * x[i]);
+    const float scale = 1 / iscale;
+    float best_mse = 0;
+    for (int i = 0; i < n; ++i) {
+        const float diff = x[i] - scale * L[i];
+        best_mse += w[i] * diff * diff;
+    }
+    for (int is = -4; is <= 4; ++is) {
+        if (is == 0) continue;
+        const float iscale_is = (0.1f * is + nmax) / max;
+        const float scale_is = 1 / iscale_is;
+        float mse = 0;
+        for (int i = 0; i < n; ++i) {
+            const int l = std::min(nmax, rne(iscale_is * x[i]));
+            const float diff = x[i] - scale_is * l;
+            mse += w[i] * diff * diff;
+        }
+        if (mse < best_mse) {
+            best_mse = mse;
+            iscale = iscale_is;
+        }
+    }
+    float sumlx = 0, suml2 = 0;
+    for (int i = 0; i < n; ++i) {
+        const int l = std::min(nmax, rne(iscale * x[i]));
+        L[i] = (uint8_t)l;
+        sumlx += w[i] * x[i] * l;
+        suml2 += w[i] * l * l;
+    }
+    for (int itry = 0; itry < 5; ++itry) {
+        int changed = 0;
+        for (int i = 0; i < n; ++i) {
+            float slx = sumlx - w[i] * x[i] * L[i];
+            float sl2 = suml2 - w[i] * L[i] * L[i];
+            if (slx > 0 && sl2 > 0) {
+                const int nl = std::min(nmax, rne(x[i] * sl2 / slx));
+                if (nl != L[i]) {
+                    slx += w[i] * x[i] * nl;
+                    sl2 += w[i] * nl * nl;
+                    if (slx * slx * suml2 > sumlx * sumlx * sl2) {
+                        L[i] = (uint8_t)nl;
+                        sumlx = slx;
+                        suml2 = sl2;
+                        ++changed;
+                    }
+                }
+            }
+        }
+        if (!changed) break;
+    }
+    return suml2 > 0.0f ? sumlx / suml2 : 0.0f;
+}
+
+// IQ2_XXS (quantize_row_iq2_xxs_impl, ggml-quants.c:3222-3397) with a uniform importance matrix
+// (the reference quantises this type only with one): per 32-block a weighted fit of four codebook
+// rows and one scale, each 8-group's signs made even in number (the cheapest value flipped), the
+// scales coded in 4 bits against max_scale / 31.
+void iq2_xxs_row(const float *x, uint8_t *y, int64_t n) {
+    const Iq2sSearch &S = iq2xxs_search();
+    const int kMaxQ = 3;
+    for (int64_t b = 0; b < n / 256; ++b, x += 256, y += B_IQ2_XXS) {
+        uint32_t q2[16] = {};
+        float scales[8], weight[32], xval[32], waux[32];
+        int8_t L[32], Laux[32];
+        uint8_t block_signs[4];
+        float max_scale = 0;
+        float sumx2 = 0;
+        for (int i = 0; i < 256; ++i) sumx2 += x[i] * x[i];
+        const float sigma2 = sumx2 / 256;
+        for (int ib = 0; ib < 8; ++ib) {
+            const float *xb = x + 32 * ib;
+            for (int i = 0; i < 32; ++i) weight[i] = 1.0f * sqrtf(sigma2 + xb[i] * xb[i]);
+            for (int i = 0; i < 32; ++i) waux[i] = sqrtf(weight[i]);
+            for (int k = 0; k < 4; ++k) {
+                int nflip = 0;
+                uint8_t sg = 0;
+                for (int i = 0; i < 8; ++i) {
+                    if (xb[8 * k + i] >= 0) xval[8 * k + i] = xb[8 * k + i];
+                    else { xval[8 * k + i] = -xb[8 * k + i]; ++nflip; sg |= (uint8_t)(1 << i); }
+                }
+                if (nflip % 2) {
+                    int imin = 0;
+                    float mn = weight[8 * k] * xb[8 * k] * xb[8 * k];
+                    for (int i = 1; i < 8; ++i) {
+                        const float ax = weight[8 * k + i] * xb[8 * k + i] * xb[8 * k + i];
+                        if (ax < mn) { mn = ax; imin = i; }
+                    }
+                    xval[8 * k + imin] = -xval[8 * k + imin];
+                    sg ^= (uint8_t)(1 << imin);
+                }
+                block_signs[k] = sg & 127;
+            }
+            float mx = xval[0];
+            for (int i = 1; i < 32; ++i) mx = std::max(mx, xval[i]);
+            if (mx < 1e-15f) {
+                scales[ib] = 0;
+                continue;
+            }
+            float scale = make_qp_quants(32, kMaxQ + 1, xval, reinterpret_cast<uint8_t *>(L), weight);
+            const float eff_max = scale * kMaxQ;
+            if (eff_max <= 0) {
+                scales[ib] = 0;
+                continue;
+            }
+            float best = 0;
+            for (int is = -6; is <= 6; ++is) {
+                const float id = (2 * kMaxQ - 1 + is * 0.1f) / eff_max;
+                const float this_scale = 1 / id;
+                for (int k = 0; k < 4; ++k) {
+                    for (int i = 0; i < 8; ++i) {
+                        const int l = rne(0.5f * (id * xval[8 * k + i] - 1));
+                        Laux[8 * k + i] = (int8_t)std::max(0, std::min(kMaxQ - 1, l));
+                    }
+                    int u = 0;
+                    for (int i = 0; i < 8; ++i) u |= Laux[8 * k + i] << (2 * i);
+                    if (S.map[u] < 0)
+                        best_neighbour(S, S.nbr.data() - S.map[u] - 1, xval + 8 * k, waux + 8 * k, this_scale, Laux + 8 * k);
+                }
+                float sqx = 0, sq2 = 0;
+                for (int i = 0; i < 32; ++i) {
+                    const float q = 2 * Laux[i] + 1;
+                    sqx += weight[i] * xval[i] * q;
+                    sq2 += weight[i] * q * q;
+                }
+                if (sq2 > 0 && sqx * sqx > best * sq2) {
+                    scale = sqx / sq2;
+                    best = scale * sqx;
+                    memcpy(L, Laux, 32);
+                }
+            }
+            if (scale > 0) {
+                const float id = 1 / scale;
+                for (int k = 0; k < 4; ++k) {
+                    int u = 0;
+                    for (int i = 0; i < 8; ++i) {
+                        const int l = std::max(0, std::min(kMaxQ - 1, rne(0.5f * (id * xval[8 * k + i] - 1))));
+                        u |= l << (2 * i);
+                    }
+                    int row = S.map[u];
+                    if (row < 0) row = best_neighbour(S, S.nbr.data() - S.map[u] - 1, xval + 8 * k, waux + 8 * k, scale, L + 8 * k);
+                    for (int i = 0; i < 8; ++i) L[8 * k + i] = (int8_t)(((int)((S.grid[row] >> (8 * i)) & 0xff) - 1) / 2);
+                }
+                float sqx = 0, sq2 = 0;
+                for (int i = 0; i < 32; ++i) {
+                    const float q = 2 * L[i] + 1;
+                    sqx += weight[i] * xval[i] * q;
+                    sq2 += weight[i] * q * q;
+                }
+                if (sq2 > 0) scale = sqx / sq2;
+            }
+            if (scale < 0) {
+                scale = -scale;
+                for (int k = 0; k < 4; ++k) block_signs[k] = (uint8_t)((~block_signs[k]) & 127);
+            }
+            for (int k = 0; k < 4; ++k) {
+                int u = 0;
+                for (int i = 0; i < 8; ++i) u |= L[8 * k + i] << (2 * i);
+                const int row = S.map[u];   // on the codebook by construction
+                q2[2 * ib] |= (uint32_t)row << (8 * k);
+                q2[2 * ib + 1] |= (uint32_t)block_signs[k] << (7 * k);
+            }
+            scales[ib] = scale;
+            max_scale = std::max(max_scale, scale);
+        }
+        memset(y, 0, B_IQ2_XXS);
+        if (!max_scale) continue;
+        const float d = max_scale / 31;
+        const uint16_t dh = to_f16(d);
+        memcpy(y, &dh, 2);
+        const float id = 1 / d;
+        for (int ib = 0; ib < 8; ++ib) {
+            const int l = std::max(0, std::min(15, rne(0.5f * (id * scales[ib] - 1))));
+            q2[2 * ib + 1] |= (uint32_t)l << 28;
+        }
+        memcpy(y + 2, q2, 64);
+    }
+}
+
 }  // namespace
 
 extern "C" size_t moeb_quantize_weights(int32_t type, const float *src, void *dst, int64_t nrow, int64_t n_per_row,
@@ -472,10 +686,12 @@ extern "C" size_t moeb_quantize_weights(int32_t type, const float *src, void *ds
         case MOEB_T_IQ2_S:  row_fn = iq2_s_row;  blk = 256; break;
         case MOEB_T_Q5_0:   row_fn = q5_0_row;   blk = 32;  break;
         case MOEB_T_IQ4_NL: row_fn = iq4_nl_row; blk = 32;  break;
+        case MOEB_T_IQ2_XXS: row_fn = iq2_xxs_row; blk = 256; break;
         default: return 0;
     }
     if (!src || !dst || nrow <= 0 || n_per_row <= 0 || n_per_row % blk) return 0;
     if (type == MOEB_T_IQ2_S) iq2s_search();
+    if (type == MOEB_T_IQ2_XXS) iq2xxs_search();
     const int64_t rb = row_bytes(type, n_per_row);
     int nt = n_threads > 0 ? n_threads : (int)std::thread::hardware_concurrency();
     nt = (int)std::max<int64_t>(1, std::min<int64_t>(nt, nrow));

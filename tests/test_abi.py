@@ -116,3 +116,26 @@ def test_host_quantiser_matches_reference_quantiser(ref):
         got = capi.lib().moeb_quantize_weights(t, w.ctypes.data, ours.ctypes.data, 4, n, 1)
         assert got == 4 * rs
         assert np.array_equal(ours, ref.quantize(t, w).reshape(-1)), t
+
+
+def test_host_iq2xxs_quantiser_matches_reference(ref):
+    """IQ2_XXS through moeb_quantize_weights equals ggml_quantize_chunk given a uniform importance
+    matrix (the reference quantises this type only with one), byte for byte: ordinary rows, a zero
+    row, tiny values, a dominant value, sign patterns of odd parity and the workload's scale."""
+    from llapis_b200 import capi
+    rng = np.random.default_rng(17)
+    n = 1024
+    w = (rng.standard_normal((12, n)) * 0.02).astype(np.float32)
+    w[1] = 0.0
+    w[2] *= 1e-6
+    w[3, 100] = 3.0
+    w[4, :8] = [-1, 2, 3, 4, 5, 6, 7, 8]
+    w[5] = np.abs(w[5])
+    w[6] = -np.abs(w[6])
+    rs = capi.row_size(capi.IQ2_XXS, n)
+    assert rs == n // 256 * 66
+    ours = np.zeros(12 * rs, np.uint8)
+    assert capi.lib().moeb_quantize_weights(capi.IQ2_XXS, w.ctypes.data, ours.ctypes.data, 12, n, 3) == 12 * rs
+    want = ref.quantize(16, w).reshape(-1)
+    bad = [r for r in range(12) if not np.array_equal(ours[r * rs:(r + 1) * rs], want[r * rs:(r + 1) * rs])]
+    assert not bad, f"rows {bad} differ"
