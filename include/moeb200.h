@@ -230,7 +230,7 @@ int moeb_quantize_act(int32_t wtype, const float *x, void *dst, int64_t n_rows, 
 
 /* ---- host-side weight quantiser (CPU, multi-threaded) ----
  * Restates ggml_quantize_chunk without an importance matrix (third_party/llama/ggml/src/ggml.c:7761)
- * for the four expert types, and for IQ2_XXS with a uniform one (ggml requires one for that type);
+ * for the four expert types and Q8_0, and for IQ2_XXS with a uniform one (ggml requires one there);
  * output bytes are identical to the reference quantiser's. src: host
  * f32 [nrow][n_per_row]; dst: host. n_threads <= 0 uses every online CPU. Returns bytes written,
  * or 0 on a bad type/shape. */

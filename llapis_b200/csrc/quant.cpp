@@ -6,6 +6,7 @@
 //   IQ4_NL quantize_row_iq4_nl_impl, 7 scale trials    (ggml-quants.c:4894, :5005)
 //   IQ2_S  quantize_row_iq2_s_impl + the codebook map  (ggml-quants.c:5070, :2781, :3198)
 //   IQ2_XXS quantize_row_iq2_xxs_impl + make_qp_quants (ggml-quants.c:3222, :1018)
+//   Q8_0   quantize_row_q8_0_ref                      (ggml-quants.c:238)
 // Every float expression keeps the reference's evaluation order and this file is compiled with
 // -ffp-contract=off, so the output bytes equal the reference quantiser's (checked by the tests).
 // Rows are independent and are spread over host threads.
@@ -487,6 +488,20 @@ void iq2_s_row(const float *x, uint8_t *y, int64_t n) {
     }
 }
 
+// Q8_0 weights (quantize_row_q8_0_ref, ggml-quants.c:238-261): d = amax / 127, q = roundf(x / d)
+// (half away from zero)
+void q8_0_row(const float *x, uint8_t *y, int64_t n) {
+    for (int64_t b = 0; b < n / 32; ++b, x += 32, y += B_Q8_0) {
+        float amax = 0.0f;
+        for (int j = 0; j < 32; ++j) amax = std::max(amax, fabsf(x[j]));
+        const float d = amax / 127;
+        const float id = d ? 1.0f / d : 0.0f;
+        const uint16_t dh = to_f16(d);
+        memcpy(y, &dh, 2);
+        for (int j = 0; j < 32; ++j) y[2 + j] = (uint8_t)(int8_t)roundf(x[j] * id);
+    }
+}
+
 // make_qp_quants (ggml-quants.c:1018-1089): levels 0..nmax for non-negative x with weights w,
 // a scale search over nine candidates, then up to five rounds of single-level improvements
 float make_qp_quants(int n, int nmax, const float *x, uint8_t *L, const float *w) {
@@ -687,6 +702,7 @@ extern "C" size_t moeb_quantize_weights(int32_t type, const float *src, void *ds
         case MOEB_T_Q5_0:   row_fn = q5_0_row;   blk = 32;  break;
         case MOEB_T_IQ4_NL: row_fn = iq4_nl_row; blk = 32;  break;
         case MOEB_T_IQ2_XXS: row_fn = iq2_xxs_row; blk = 256; break;
+        case MOEB_T_Q8_0:   row_fn = q8_0_row;   blk = 32;  break;
         default: return 0;
     }
     if (!src || !dst || nrow <= 0 || n_per_row <= 0 || n_per_row % blk) return 0;

@@ -139,3 +139,18 @@ def test_host_iq2xxs_quantiser_matches_reference(ref):
     want = ref.quantize(16, w).reshape(-1)
     bad = [r for r in range(12) if not np.array_equal(ours[r * rs:(r + 1) * rs], want[r * rs:(r + 1) * rs])]
     assert not bad, f"rows {bad} differ"
+
+
+def test_host_q8_0_weight_quantiser_matches_reference(ref):
+    """Q8_0 weights through moeb_quantize_weights equal ggml_quantize_chunk (quantize_row_q8_0_ref:
+    round half away from zero), including a zero block and exact .5 ties."""
+    from llapis_b200 import capi
+    rng = np.random.default_rng(5)
+    w = (rng.standard_normal((5, 128)) * 0.02).astype(np.float32)
+    w[1, :32] = 0.0
+    w[2, :32] = np.arange(32, dtype=np.float32) - 15.5      # amax 16.5 ... ties after scaling
+    w[3, :4] = [127.0, 0.5, -0.5, 1.5]
+    rs = capi.row_size(capi.Q8_0, 128)
+    ours = np.zeros(5 * rs, np.uint8)
+    assert capi.lib().moeb_quantize_weights(capi.Q8_0, w.ctypes.data, ours.ctypes.data, 5, 128, 1) == 5 * rs
+    assert np.array_equal(ours, ref.quantize(capi.Q8_0, w).reshape(-1))
