@@ -1971,15 +1971,25 @@ static cudaError_t launch_ex(const void *fn, dim3 grid, dim3 block, size_t smem,
 
 size_t gemv_smem_bytes(int kind, int d_in, int T) { return (size_t)gemv_layout(kind == 0 ? 0 : 1, d_in, T).total; }
 
+// Opt-in to more than 48 KB of dynamic shared memory, once per device and kernel.
+static cudaError_t smem_optin(const void *fn, size_t bytes, unsigned *done_mask, int bit) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 32) return cudaErrorInvalidDevice;
+    static std::mutex mu;
+    std::lock_guard<std::mutex> lk(mu);
+    if (done_mask[dev] & (1u << bit)) return cudaSuccess;
+    e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    if (e == cudaSuccess) done_mask[dev] |= 1u << bit;
+    return e;
+}
+
 cudaError_t launch_gemv(const GemvParams &p, cudaStream_t s, bool pdl, int n_sms) {
     const size_t smem = gemv_smem_bytes(p.kind, p.d_in, p.route.T);
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute((const void *)gemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             227 * 1024);
-        if (e != cudaSuccess) return e;
-        attr_set = true;
-    }
+    static unsigned optin[32];
+    const cudaError_t e = smem_optin((const void *)gemv_kernel, 227 * 1024, optin, 0);
+    if (e != cudaSuccess) return e;
     GemvParams q = p;
     void *args[] = {&q};
     return launch_ex((const void *)gemv_kernel, dim3(n_sms), dim3(kGemvThreads), smem, s, pdl, args);
@@ -2001,12 +2011,9 @@ cudaError_t launch_fused(const FusedArgs &a, cudaStream_t s, int n_sms) {
     p.sync = a.sync;
     const size_t smem = fused_smem_bytes(a.d, a.nff);
     const void *fn = a.nrm.pre ? (const void *)fused_decode_kernel<true> : (const void *)fused_decode_kernel<false>;
-    static bool attr_set[2] = {false, false};
-    if (!attr_set[a.nrm.pre ? 1 : 0]) {
-        cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-        if (e != cudaSuccess) return e;
-        attr_set[a.nrm.pre ? 1 : 0] = true;
-    }
+    static unsigned optin[32];   // per device: the attribute belongs to each device's context
+    const cudaError_t e = smem_optin(fn, 227 * 1024, optin, a.nrm.pre ? 1 : 0);
+    if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(n_sms);
     cfg.blockDim = dim3(kGemvThreads);
@@ -2019,20 +2026,6 @@ cudaError_t launch_fused(const FusedArgs &a, cudaStream_t s, int n_sms) {
     cfg.numAttrs = 1;
     void *args[] = {&p};
     return cudaLaunchKernelExC(&cfg, fn, args);
-}
-
-// Opt-in to more than 48 KB of dynamic shared memory, once per device and kernel.
-static cudaError_t smem_optin(const void *fn, size_t bytes, unsigned *done_mask, int bit) {
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return e;
-    if (dev < 0 || dev >= 32) return cudaErrorInvalidDevice;
-    static std::mutex mu;
-    std::lock_guard<std::mutex> lk(mu);
-    if (done_mask[dev] & (1u << bit)) return cudaSuccess;
-    e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
-    if (e == cudaSuccess) done_mask[dev] |= 1u << bit;
-    return e;
 }
 
 // Optional per-kernel CUDA events around the nine prefill launches (moeb_prefill_profile).
