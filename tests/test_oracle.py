@@ -206,3 +206,30 @@ def test_iq2xxs_q8_0_layer_matches_reference_fixture(golden_types, port, ref):
     assert_layer_close(res["gate_up"], golden_types["types_gate_up"], tol=1e-5)
     assert_layer_close(res["down"], golden_types["types_down"], tol=1e-4)
     assert_layer_close(res["out"], golden_types["types_out"], tol=1e-4)
+
+
+@pytest.mark.parametrize("t,n", [(16, 2816), (IQ4_NL, 704)])
+def test_vec_dot_matches_reference_on_random_blocks(port, ref, t, n):
+    """The reference's own known-answer test for these expert types (tests/test_sidecar_kernels.cpp:
+    random IQ2_XXS gate_up rows at d_in 2816 and IQ4_NL down rows at d_in 704 -- random bytes with
+    an fp16 scale in [0x1C00, 0x2C00] at every block head -- against ggml's vec_dot on N(0, 1)
+    activations quantised by the reference): the oracle's dots against the reference build's
+    vec_dot. Each block's integer sum is exact; the reference build's AVX2 kernels add the blocks'
+    float products in another order, so the bar is 1e-6 of the sum of the blocks' magnitudes."""
+    rng = np.random.default_rng(1234)
+    rows = 64
+    wrow = port.row_size(t, n)
+    bsz = 66 if t == 16 else 18
+    w = rng.integers(0, 256, (rows, wrow), dtype=np.uint8)
+    for off in range(0, wrow, bsz):
+        w[:, off:off + 2] = rng.integers(0x1C00, 0x2C01, rows).astype(np.uint16).view(np.uint8).reshape(rows, 2)
+    vdt = port.vec_dot_type(t)
+    xs = rng.standard_normal((4, n)).astype(np.float32)
+    xq = [ref.quantize_act(vdt, xs[k]) for k in range(4)]
+    assert all(np.array_equal(xq[k], port.quantize_act(vdt, xs[k])) for k in range(4))
+    deq = np.stack([ref.dequantize(t, w[r], n) for r in range(rows)])
+    for r in range(rows):
+        for k in range(4):
+            a, b = port.vec_dot(t, n, w[r], xq[k]), ref.vec_dot(t, n, w[r], xq[k])
+            scale = float(np.abs(deq[r]).sum() * np.abs(xs[k]).max()) + 1e-30
+            assert abs(a - b) <= 1e-6 * scale, (r, k, a, b)
