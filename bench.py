@@ -166,6 +166,36 @@ def time_reference(host, x, warmup, steps, budget_s, n_threads=None, norms=None)
                       f"reference sources, {nt} threads", "ms_per_forward": 1e3 * sum(times) / len(times)}
 
 
+def time_sidecar(host, x, budget_s, n_threads=None):
+    """The reference's CPU sidecar (O2: src/moe_sidecar.cpp, oracle/_ref/libsidecar_ref.so) for a
+    decode batch (at most 4 tokens, 32 pairs a job): each routed pair's gate_up -> tanh GeGLU ->
+    down on the host cores, then scale, weight and slot-order add. Routing is O1's, computed once
+    outside the timed region. A second CPU baseline beside O1; never raises."""
+    try:
+        from oracle import Ref, Sidecar, ref_available, sidecar_available
+        if not (ref_available() and sidecar_available()) or x.shape[0] > 4:
+            return None
+        nt = min(16, n_threads or os.cpu_count() or 1)
+        spec = reference_spec(host, x)
+        o1 = Ref().moe_layer(spec, n_threads=nt, want=("ids", "weights"))
+        sc = Sidecar(nt)
+        sc.layer(spec, o1["ids"], o1["weights"])   # warm
+        times = []
+        t_end = time.perf_counter() + budget_s
+        while len(times) < 3 or (time.perf_counter() < t_end and len(times) < 1000):
+            t0 = time.perf_counter()
+            sc.layer(spec, o1["ids"], o1["weights"])
+            times.append(time.perf_counter() - t0)
+        times.sort()
+        med = times[len(times) // 2]
+        return {"value": x.shape[0] / med, "unit": "tokens/s", "cores": nt, "kind": "reference",
+                "sample": f"{len(times)} forwards of {x.shape[0]} tokens (median), the reference's moe_sidecar on "
+                          f"{nt} threads; routing (O1) outside the timed region; tanh GeGLU",
+                "ms_per_forward": 1e3 * med}
+    except Exception as exc:   # a baseline must not take the bench line down with it
+        return {"unavailable": f"{type(exc).__name__}: {exc}"[:200]}
+
+
 def run_reference(args):
     rank, _, world = dist_env()
     if rank != 0:
@@ -597,6 +627,8 @@ def main():
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         # a bounded sample: at most 256 tokens of the batch (the CPU cost per token is flat in T)
         cpu = time_reference(host, x_host[:256], 1, 1000, args.cpu_sample_s, norms=norms)
+        if cpu is not None and norms is None and T <= 4:
+            cpu["o2_sidecar"] = time_sidecar(host, x_host, min(5.0, args.cpu_sample_s))
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,

@@ -10,4 +10,4 @@ Two oracles share one layer description (``oracle/moe_oracle.h``):
 * ``Port`` — this repository's plain-C restatement (``oracle/moe_oracle.c``), pinned against
   ``Ref`` and the golden fixtures under ``tests/golden/``.
 """
-from .oracle import Port, Ref, LayerSpec, build_port, ref_available, port_available  # noqa: F401
+from .oracle import Port, Ref, LayerSpec, Sidecar, build_port, ref_available, port_available, sidecar_available  # noqa: F401

@@ -526,7 +526,11 @@ int oracle_moe_layer(const oracle_layer *L, oracle_layer_out *o) {
                 oracle_quantize_act(oracle_vec_dot_type(tgu), xt, xq, d);
                 for (int r = 0; r < 2 * nff; ++r) h[r] = oracle_vec_dot(tgu, d, wgu + (size_t)r * rgu, xq);
             }
-            oracle_geglu(nff, a, h, h + nff);
+            if (L->gelu_tanh) {
+                for (int i = 0; i < nff; ++i) a[i] = gelu_tanh(h[i]) * h[nff + i];
+            } else {
+                oracle_geglu(nff, a, h, h + nff);
+            }
             oracle_quantize_act(oracle_vec_dot_type(tdn), a, aq, nff);
             const float sc = hot ? (L->s_hot ? L->s_hot[slot] : 1.f) : (L->s_cold ? L->s_cold[e] : 1.f);
             for (int r = 0; r < d; ++r) {

@@ -61,6 +61,9 @@ typedef struct oracle_layer {
      * Gemma-4 routes on rms_norm(attn_out) / sqrt(d) * ffn_gate_inp_s and feeds the experts
      * rms_norm(attn_out) * ffn_pre_norm_2 (third_party/llama/src/models/gemma4.cpp:394-403). */
     const float   *x_router;
+    /* 1: the GeGLU's GELU in tanh form evaluated in f32 (the CPU sidecar's, src/moe_sidecar.cpp:622-626)
+     * instead of ggml-cpu's fp16 table; for attributing differences to that choice */
+    int32_t        gelu_tanh;
 } oracle_layer;
 
 typedef struct oracle_layer_out {

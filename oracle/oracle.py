@@ -10,6 +10,7 @@ import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REF_SO = os.path.join(HERE, "_ref", "libref_runner.so")
+SIDECAR_SO = os.path.join(HERE, "_ref", "libsidecar_ref.so")
 PORT_SO = os.path.join(HERE, "_build", "libmoe_oracle.so")
 
 # ggml type ids (third_party/llama/ggml/include/ggml.h:390-432)
@@ -28,7 +29,7 @@ class _Layer(C.Structure):
         ("cold_gu", C.c_void_p), ("cold_down", C.c_void_p), ("s_cold", C.c_void_p),
         ("n_threads", C.c_int32),
         ("ids_in", C.c_void_p), ("gate_up_in", C.c_void_p),
-        ("x_router", C.c_void_p),
+        ("x_router", C.c_void_p), ("gelu_tanh", C.c_int32),
     ]
 
 
@@ -67,6 +68,7 @@ class LayerSpec:
     ids_in: np.ndarray | None = None      # i32 [T, k]: routing taken as given (port oracle only)
     gate_up_in: np.ndarray | None = None  # f32 [T*k, 2*n_ff]: gate_up taken as given (port oracle only)
     x_router: np.ndarray | None = None    # f32 [T, d_model]: router input when it differs from x
+    gelu_tanh: bool = False               # port oracle: tanh-form GELU instead of the fp16 table
     keep: list = field(default_factory=list)
 
     @property
@@ -97,6 +99,7 @@ class LayerSpec:
         self.keep = list(arrs.values())
         for k, v in arrs.items():
             setattr(L, k, _ptr(v))
+        L.gelu_tanh = int(self.gelu_tanh)
         L.n_slots = self.n_slots
         L.hot_type_gu, L.hot_type_down = self.hot_type_gu, self.hot_type_down
         L.cold_type_gu, L.cold_type_down = self.cold_type_gu, self.cold_type_down
@@ -263,6 +266,79 @@ class Port(_Oracle):
         out = np.empty_like(gate)
         self._geglu(gate.size, out.ctypes.data, gate.ctypes.data, up.ctypes.data)
         return out
+
+
+class Sidecar:
+    """The reference's CPU sidecar (src/moe_sidecar.cpp, O2), built into oracle/_ref with
+    oracle/sidecar_runner.cpp: per routed pair gate_up -> tanh GeGLU -> down on the host cores
+    (ggml-cpu's vec_dot, the sidecar's own kernels for IQ2_XXS / IQ4_NL), at most 32 pairs a job."""
+
+    def __init__(self, n_workers: int = 8):
+        self.lib = C.CDLL(SIDECAR_SO)
+        self.lib.sidecar_init.restype = C.c_int
+        self.lib.sidecar_init.argtypes = [C.c_int]
+        self.lib.sidecar_ffn.restype = C.c_int
+        self.lib.sidecar_ffn.argtypes = [C.c_int32, C.c_int32, C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_void_p,
+                                         C.c_void_p, C.c_uint64, C.c_int32, C.c_int32, C.c_int32, C.c_void_p, C.c_uint64,
+                                         C.c_int32, C.c_void_p, C.c_void_p]
+        if not self.lib.sidecar_init(n_workers):
+            raise RuntimeError("sidecar init failed")
+        self.n_workers = n_workers
+
+    def ffn(self, x, pool_ids, pairs, k, gu, gu_type, dn, dn_type, d, nff):
+        """Raw down outputs [len(pairs), d] of pairs p (token p // k) on pool entries pool_ids."""
+        x = np.ascontiguousarray(x, np.float32)
+        gu, dn = np.ascontiguousarray(gu), np.ascontiguousarray(dn)
+        out = np.zeros((len(pairs), d), np.float32)
+        for s in range(0, len(pairs), 32):
+            ids = np.ascontiguousarray(pool_ids[s:s + 32], np.int32)
+            cd = np.ascontiguousarray(pairs[s:s + 32], np.int32)
+            # the job writes pair i's row at y[i * d]; its error path clears 4096 floats per pair
+            y = np.zeros((len(ids), max(d, 4096)), np.float32)
+            ns = C.c_int64()
+            got = self.lib.sidecar_ffn(0, len(ids), ids.ctypes.data, cd.ctypes.data, k, x.shape[0], x.ctypes.data,
+                                       gu.ctypes.data, gu[0].nbytes, gu_type, d, nff, dn.ctypes.data, dn[0].nbytes,
+                                       dn_type, y.ctypes.data, C.byref(ns))
+            if got != len(ids):
+                raise RuntimeError(f"sidecar job computed {got} of {len(ids)} pairs")
+            out[s:s + len(ids)] = y.reshape(-1)[:len(ids) * d].reshape(len(ids), d)
+        return out
+
+    def layer(self, spec: LayerSpec, ids: np.ndarray, weights: np.ndarray) -> np.ndarray:
+        """The layer output with the given routing (O1's): each pair through the sidecar on its class's
+        pool, then the down scale, the routing weight and the slot-order add, each product rounded
+        (the reference's mul / mul / add-chain nodes)."""
+        T, k, d = spec.n_tokens, spec.top_k, spec.d_model
+        flat = ids.reshape(-1)
+        hot = np.zeros(len(flat), bool)
+        widx = flat.copy()
+        if spec.n_slots and spec.exp_slot is not None:
+            for p, e in enumerate(flat):
+                s = int(spec.exp_slot[e])
+                if 0 <= s < spec.n_slots and spec.slot_state[s] == 2 and spec.slot_exp[s] == e:
+                    hot[p], widx[p] = True, s
+        y = np.zeros((len(flat), d), np.float32)
+        for cls in (True, False):
+            sel = np.nonzero(hot == cls)[0]
+            if not len(sel):
+                continue
+            gu, dn = (spec.hot_gu, spec.hot_down) if cls else (spec.cold_gu, spec.cold_down)
+            tg, td = (spec.hot_type_gu, spec.hot_type_down) if cls else (spec.cold_type_gu, spec.cold_type_down)
+            sc = spec.s_hot if cls else spec.s_cold
+            yy = self.ffn(spec.x, widx[sel], sel, k, gu, tg, dn, td, d, spec.n_ff)
+            if sc is not None:
+                yy = (yy * sc[widx[sel]][:, None].astype(np.float32)).astype(np.float32)
+            y[sel] = yy
+        w = weights.reshape(-1).astype(np.float32)
+        prod = (y * w[:, None]).astype(np.float32).reshape(T, k, d)
+        out = prod[:, 0].copy()
+        for j in range(1, k):
+            out = (out + prod[:, j]).astype(np.float32)
+        return out
+
+
+def sidecar_available() -> bool:
+    return os.path.exists(SIDECAR_SO)
 
 
 def ref_available() -> bool:

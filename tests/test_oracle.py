@@ -233,3 +233,24 @@ def test_vec_dot_matches_reference_on_random_blocks(port, ref, t, n):
             a, b = port.vec_dot(t, n, w[r], xq[k]), ref.vec_dot(t, n, w[r], xq[k])
             scale = float(np.abs(deq[r]).sum() * np.abs(xs[k]).max()) + 1e-30
             assert abs(a - b) <= 1e-6 * scale, (r, k, a, b)
+
+
+@pytest.mark.parametrize("name,T", [("decode_t1_iq2s", 1), ("decode_t4_mixed", 4), ("mini_mixed", 3)])
+def test_cpu_sidecar_matches_port_with_tanh_gelu(name, T, port, ref):
+    """The reference's CPU sidecar (O2: src/moe_sidecar.cpp over ggml-cpu, built into oracle/_ref)
+    on O1's routing equals the port oracle run with the sidecar's tanh-form GELU (to 1e-3 x RMS:
+    the sidecar's 8-wide tanh uses its own exp, which moves a few Q8_0 roundings of the down
+    input). Its distance to O1 is the fp16-table GELU's doing, measured here, not bounded."""
+    from llapis_b200 import workload
+    from oracle import Sidecar, sidecar_available
+    if not sidecar_available():
+        pytest.skip("oracle/_ref/libsidecar_ref.so not built")
+    host = host_layer(name)
+    spec = spec_of(host, workload.make_input(workload.CONFIGS[name], n_tokens=T))
+    o1 = ref.moe_layer(spec, n_threads=8, want=("ids", "weights"))
+    side = Sidecar(8).layer(spec, o1["ids"], o1["weights"])
+    spec.gelu_tanh, spec.ids_in = True, o1["ids"]
+    tanh_port = port.moe_layer(spec, want=())["out"]
+    assert_layer_close(side, tanh_port, tol=1e-3)
+    rms = float(np.sqrt(np.mean(np.square(o1["out"], dtype=np.float64))))
+    print(f"{name}: sidecar vs O1 (fp16-table GELU) max-abs / rms = {np.abs(side - o1['out']).max() / rms:.2e}")
