@@ -18,7 +18,7 @@ from dataclasses import dataclass
 import numpy as np
 
 from . import capi
-from .capi import IQ2_S, IQ4_NL, Q4_K, Q5_0
+from .capi import IQ2_S, IQ2_XXS, IQ4_NL, Q4_K, Q5_0
 from .layer import HostLayer
 
 
@@ -35,6 +35,7 @@ class LayerConfig:
     top_k: int = 8
     seed: int = 0
     n_layers: int = 1
+    cold_gu_type: int = IQ2_S   # the cold class's gate_up type (IQ2_XXS: the product files' type)
 
 
 CONFIGS = {
@@ -47,6 +48,10 @@ CONFIGS = {
     # reduced shapes for tests (same structure, seconds to build)
     "mini_mixed": LayerConfig("mini_mixed", 3, tuple(range(8)), 1.1, False, d_model=512, n_ff=64, n_expert=32,
                               top_k=4, seed=11),
+    # decode_t4_mixed's experts with the product files' cold class, IQ2_XXS gate_up / IQ4_NL down, and
+    # no router skew, so both classes are routed (the oracle, the host quantiser and the dequantiser
+    # serve it; the layer kernels do not yet)
+    "decode_t4_iq2xxs": LayerConfig("decode_t4_iq2xxs", 4, tuple(range(48)), None, False, cold_gu_type=IQ2_XXS),
 }
 
 
@@ -110,28 +115,31 @@ def build_layer(cfg: LayerConfig, layer: int = 0, n_threads: int = 0) -> HostLay
     is_hot = np.zeros(E, bool)
     is_hot[hot] = True
 
+    ct = cfg.cold_gu_type
+
     def one(e):
         def make():
             gu, dn = expert_f32(cfg, layer, e)
             if is_hot[e]:
                 a, b = quantize(Q4_K, gu, 1), quantize(Q5_0, dn, 1)
             else:
-                a, b = quantize(IQ2_S, gu, 1), quantize(IQ4_NL, dn, 1)
+                a, b = quantize(ct, gu, 1), quantize(IQ4_NL, dn, 1)
             return np.concatenate([a.reshape(-1), b.reshape(-1)])
-        return _cached(f"v1|{cfg.seed}|{layer}|{e}|{d}|{nff}|{int(is_hot[e])}", make)
+        tag = "" if is_hot[e] or ct == IQ2_S else f"|{ct}"
+        return _cached(f"v1|{cfg.seed}|{layer}|{e}|{d}|{nff}|{int(is_hot[e])}{tag}", make)
 
     nt = n_threads or os.cpu_count() or 1
-    capi.lib().moeb_quantize_weights(IQ2_S, np.zeros(256, np.float32).ctypes.data,
-                                     np.zeros(82, np.uint8).ctypes.data, 1, 256, 1)   # build the IQ2_S search tables once
+    capi.lib().moeb_quantize_weights(ct, np.zeros(256, np.float32).ctypes.data, np.zeros(128, np.uint8).ctypes.data, 1,
+                                     256, 1)   # build the codebook search tables once
     with ThreadPoolExecutor(max_workers=nt) as ex:
         blobs = list(ex.map(one, range(E)))
     hgu, hdn = 2 * nff * capi.row_size(Q4_K, d), d * capi.row_size(Q5_0, nff)
-    cgu, cdn = 2 * nff * capi.row_size(IQ2_S, d), d * capi.row_size(IQ4_NL, nff)
+    cgu, cdn = 2 * nff * capi.row_size(ct, d), d * capi.row_size(IQ4_NL, nff)
     K = len(hot)
     hot_gu = np.zeros((K, 2 * nff, capi.row_size(Q4_K, d)), np.uint8) if K else None
     hot_dn = np.zeros((K, d, capi.row_size(Q5_0, nff)), np.uint8) if K else None
     n_cold = int((~is_hot).sum())
-    cold_gu = np.zeros((E, 2 * nff, capi.row_size(IQ2_S, d)), np.uint8) if n_cold else None
+    cold_gu = np.zeros((E, 2 * nff, capi.row_size(ct, d)), np.uint8) if n_cold else None
     cold_dn = np.zeros((E, d, capi.row_size(IQ4_NL, nff)), np.uint8) if n_cold else None
     slot = {int(e): s for s, e in enumerate(hot)}
     for e in range(E):
@@ -147,7 +155,7 @@ def build_layer(cfg: LayerConfig, layer: int = 0, n_threads: int = 0) -> HostLay
     if cfg.bias_s is not None:
         b_router = (-cfg.bias_s * np.log1p(np.arange(E, dtype=np.float64))).astype(np.float32)
     return HostLayer(d_model=d, n_ff=nff, n_expert=E, top_k=cfg.top_k, w_router=w_router, b_router=b_router,
-                     hot_ids=hot, hot_gu=hot_gu, hot_down=hot_dn, cold_gu=cold_gu, cold_down=cold_dn,
+                     hot_ids=hot, hot_gu=hot_gu, hot_down=hot_dn, cold_gu=cold_gu, cold_down=cold_dn, cold_type_gu=ct,
                      s_hot=np.ones(K, np.float32) if K else None, s_cold=np.ones(E, np.float32) if n_cold else None)
 
 

@@ -318,6 +318,33 @@ def main_types():
     fx["types_x"] = x
     for n in ("hot_gu", "hot_down", "cold_gu", "cold_down"):   # the pools are regenerated by the tests
         fx[f"types_sha_{n}"] = np.array(sha(getattr(spec, n)))
+    # real shape, the product files' cold class: decode_t4_iq2xxs (cold gate_up IQ2_XXS from the
+    # reference quantiser, digest pinned; the other pools are digest-pinned by golden.npz)
+    cfg = workload.CONFIGS["decode_t4_iq2xxs"]
+    host = workload.build_layer(cfg)
+    hot_set = set(cfg.hot)
+    r.quantize(IQ2_XXS, np.zeros((1, 256), np.float32))   # the reference's IQ2_XXS tables, once
+
+    def cold_row(e):
+        return e, (None if e in hot_set else r.quantize(IQ2_XXS, workload.expert_f32(cfg, 0, e)[0]))
+    with ThreadPoolExecutor(8) as ex:
+        cold = dict(ex.map(cold_row, range(cfg.n_expert)))
+    cold_gu = np.zeros_like(host.cold_gu)
+    for e, q in cold.items():
+        if q is not None:
+            cold_gu[e] = q
+    fx["real_sha_cold_gu"] = np.array(sha(cold_gu))
+    x = workload.make_input(cfg)
+    from oracle import LayerSpec as _LS
+    exp_slot, slot_exp, slot_state = host.residency()
+    spec = _LS(host.d_model, host.n_ff, host.n_expert, host.top_k, x=x, w_router=host.w_router, b_router=host.b_router,
+               n_slots=host.n_slots, exp_slot=exp_slot, slot_exp=slot_exp, slot_state=slot_state, hot_gu=host.hot_gu,
+               hot_down=host.hot_down, s_hot=host.s_hot, cold_type_gu=IQ2_XXS, cold_gu=cold_gu,
+               cold_down=host.cold_down, s_cold=host.s_cold)
+    res = r.moe_layer(spec, n_threads=8, want=("logits", "ids", "weights"))
+    for k in ("logits", "ids", "weights", "out"):
+        fx[f"real_{k}"] = res[k]
+    fx["real_x"] = x
     path = os.path.join(HERE, "golden_types.npz")
     np.savez_compressed(path, **fx)
     print("wrote", path, os.path.getsize(path), "bytes")

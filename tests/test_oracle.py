@@ -254,3 +254,24 @@ def test_cpu_sidecar_matches_port_with_tanh_gelu(name, T, port, ref):
     assert_layer_close(side, tanh_port, tol=1e-3)
     rms = float(np.sqrt(np.mean(np.square(o1["out"], dtype=np.float64))))
     print(f"{name}: sidecar vs O1 (fp16-table GELU) max-abs / rms = {np.abs(side - o1['out']).max() / rms:.2e}")
+
+
+def test_iq2xxs_real_shape_layer_matches_reference_fixture(golden_types, port):
+    """decode_t4_iq2xxs (d_model 2816, 128 experts, top-8; cold class IQ2_XXS gate_up / IQ4_NL down,
+    the product files' types; 20 of the 32 pairs cold): the host quantiser's IQ2_XXS pool equals
+    the reference quantiser's (digest), and the oracle's layer equals the reference graph's:
+    routing exact off near ties, outputs to the parity bar 2e-3 x RMS (the IQ2_XXS gate_up dots
+    agree with the reference build's AVX2 vec_dot up to float summation order, and a last-bit
+    difference there can move a Q8_0 rounding of the down input: a few 1e-3 of RMS at n_ff 704)."""
+    host = host_layer("decode_t4_iq2xxs")
+    assert host.cold_type_gu == 16
+    assert sha(host.cold_gu) == str(golden_types["real_sha_cold_gu"])
+    x = golden_types["real_x"]
+    res = port.moe_layer(spec_of(host, x), want=("logits", "ids", "weights"))
+    ties = set(near_tie_tokens(golden_types["real_logits"], host.top_k).tolist())
+    same = [t for t in range(x.shape[0]) if t not in ties]
+    assert np.array_equal(res["ids"][same], golden_types["real_ids"][same])
+    np.testing.assert_allclose(res["logits"], golden_types["real_logits"], rtol=1e-5, atol=1e-5)
+    rel = assert_layer_close(res["out"], golden_types["real_out"], tol=2e-3)
+    print(f"decode_t4_iq2xxs oracle vs reference: max-abs / rms = {rel:.2e}")
+    assert (golden_types["real_ids"] >= 48).sum() >= 8   # the IQ2_XXS class is exercised
