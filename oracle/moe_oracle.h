@@ -112,6 +112,8 @@ int32_t ref_vec_dot_type(int32_t wtype);
 float   ref_vec_dot(int32_t wtype, int64_t n, const void *w_row, const void *x_q);
 uint16_t ref_gelu_table(uint16_t h);
 int     ref_moe_layer(const oracle_layer *L, oracle_layer_out *o);
+int     ref_dense_ffn(const float *x, int64_t T, int64_t d, int64_t nff, int32_t gu_type, const void *w_gate,
+                      const void *w_up, int32_t dn_type, const void *w_down, float *out, int n_threads);
 size_t  ref_quantize_imatrix(int32_t type, const float *src, void *dst, int64_t nrow, int64_t n_per_row,
                              const float *imatrix);
 void    ref_rms_norm(const float *x, const float *w, float s, float *y, int64_t rows, int64_t n, float eps);

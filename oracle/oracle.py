@@ -238,6 +238,36 @@ class Ref(_Oracle):
     def gelu_table(self) -> np.ndarray:
         return np.array([self._gelu(h) for h in range(1 << 16)], np.uint16)
 
+    def dense_ffn(self, x, gu_type, w_gate, w_up, dn_type, w_down, n_threads: int = 4) -> np.ndarray:
+        """The Gemma-4 dense MLP's FFN nodes (build_ffn, GELU / PAR): W_down geglu(W_gate x, W_up x)."""
+        x = np.ascontiguousarray(x, np.float32)
+        T, d = x.shape
+        nff = w_gate.shape[0]
+        fn = self._fn("ref_dense_ffn", C.c_int, [C.c_void_p, C.c_int64, C.c_int64, C.c_int64, C.c_int32, C.c_void_p,
+                                                 C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p, C.c_int])
+        out = np.zeros((T, d), np.float32)
+        ws = [np.ascontiguousarray(w) for w in (w_gate, w_up, w_down)]
+        assert fn(x.ctypes.data, T, d, nff, gu_type, ws[0].ctypes.data, ws[1].ctypes.data, dn_type, ws[2].ctypes.data,
+                  out.ctypes.data, n_threads) == 1
+        return out
+
+
+def dense_as_expert_spec(x, gu_type, w_gate, w_up, dn_type, w_down, n_expert: int = 32) -> LayerSpec:
+    """A dense GeGLU MLP as a one-expert MoE layer: a single hot slot holding [gate rows; up rows] and
+    the down matrix, zero router weights with a bias that puts every token on expert 0, top-1 (its
+    normalised weight is then exactly 1.0) and scale 1, so the layer output is the MLP's output."""
+    T, d = x.shape
+    nff = w_gate.shape[0]
+    bias = np.full(n_expert, -1e4, np.float32)
+    bias[0] = 0.0
+    exp_slot = np.full(n_expert, -1, np.int32)
+    exp_slot[0] = 0
+    return LayerSpec(d, nff, n_expert, 1, x=x, w_router=np.zeros((n_expert, d), np.float32), b_router=bias, n_slots=1,
+                     exp_slot=exp_slot, slot_exp=np.zeros(1, np.int32), slot_state=np.full(1, 2, np.int32),
+                     hot_type_gu=gu_type, hot_type_down=dn_type,
+                     hot_gu=np.concatenate([w_gate, w_up])[None], hot_down=np.asarray(w_down)[None],
+                     s_hot=np.ones(1, np.float32))
+
 
 class Port(_Oracle):
     """This repository's plain-C restatement of the path (oracle/moe_oracle.c)."""

@@ -231,6 +231,28 @@ extern "C" int ref_moe_layer(const oracle_layer * L, oracle_layer_out * o) {
     return 1;
 }
 
+// The Gemma-4 dense MLP's FFN nodes as build_ffn adds them with GELU / PAR and no biases or scales
+// (llama-graph.cpp:1316-1390, gemma4.cpp:382-387): gate = W_gate x, up = W_up x, a = geglu_split(gate,
+// up), out = W_down a. Weights in ggml layout ([rows][row bytes]); x and out f32 [T][d].
+extern "C" int ref_dense_ffn(const float * x, int64_t T, int64_t d, int64_t nff, int32_t gu_type, const void * w_gate,
+                             const void * w_up, int32_t dn_type, const void * w_down, float * out, int n_threads) {
+    ref_init();
+    Ctx c((size_t) T * (3 * nff + 2 * d) * 4 * 4 + (64u << 20));
+    ggml_tensor * xt = ggml_reshape_2d(c.meta, wrap(c.meta, GGML_TYPE_F32, d, T, 1, x), d, T);
+    ggml_tensor * wg = ggml_reshape_2d(c.meta, wrap(c.meta, (ggml_type) gu_type, d, nff, 1, w_gate), d, nff);
+    ggml_tensor * wu = ggml_reshape_2d(c.meta, wrap(c.meta, (ggml_type) gu_type, d, nff, 1, w_up), d, nff);
+    ggml_tensor * wd = ggml_reshape_2d(c.meta, wrap(c.meta, (ggml_type) dn_type, nff, d, 1, w_down), nff, d);
+    ggml_tensor * up = ggml_mul_mat(c.work, wu, xt);
+    ggml_tensor * gate = ggml_mul_mat(c.work, wg, xt);
+    ggml_tensor * a = ggml_geglu_split(c.work, gate, up);
+    ggml_tensor * y = ggml_mul_mat(c.work, wd, a);
+    ggml_cgraph * gf = ggml_new_graph(c.work);
+    ggml_build_forward_expand(gf, y);
+    ggml_graph_compute_with_ctx(c.work, gf, n_threads);
+    for (int64_t t = 0; t < T; ++t) memcpy(out + t * d, (const char *) y->data + t * y->nb[1], sizeof(float) * d);
+    return 1;
+}
+
 // ggml_rms_norm over `rows` rows of n values, then ggml_scale by s (when s != 1) and ggml_mul by the
 // [n] weight w (when given): the reference's own nodes, as the Gemma-4 block builds them
 extern "C" void ref_rms_norm(const float * x, const float * w, float s, float * y, int64_t rows, int64_t n, float eps) {

@@ -275,3 +275,24 @@ def test_iq2xxs_real_shape_layer_matches_reference_fixture(golden_types, port):
     rel = assert_layer_close(res["out"], golden_types["real_out"], tol=2e-3)
     print(f"decode_t4_iq2xxs oracle vs reference: max-abs / rms = {rel:.2e}")
     assert (golden_types["real_ids"] >= 48).sum() >= 8   # the IQ2_XXS class is exercised
+
+
+def test_dense_mlp_is_a_one_expert_layer(port, ref):
+    """Gemma-4's dense shared MLP (build_ffn with GELU / PAR: W_down geglu(W_gate x, W_up x),
+    gemma4.cpp:382-387) is this path's layer with one expert: a hot slot holding [gate; up] and
+    down, routing forced to it at top-1 (weight exactly 1.0), scale 1. The reference's own graphs
+    agree bit for bit; the oracle's one-expert layer agrees with them to the dots' summation order.
+    Real Gemma-4 widths: d_model 2816, a dense inner width of 2112."""
+    from oracle.oracle import dense_as_expert_spec
+    rng = np.random.default_rng(7)
+    d, nff, T = 2816, 2112, 6
+    wg = ref.quantize(Q4_K, (rng.standard_normal((nff, d)) * 0.02).astype(np.float32))
+    wu = ref.quantize(Q4_K, (rng.standard_normal((nff, d)) * 0.02).astype(np.float32))
+    wd = ref.quantize(Q5_0, (rng.standard_normal((d, nff)) * 0.02).astype(np.float32))
+    x = rng.standard_normal((T, d)).astype(np.float32)
+    dense = ref.dense_ffn(x, Q4_K, wg, wu, Q5_0, wd)
+    spec = dense_as_expert_spec(x, Q4_K, wg, wu, Q5_0, wd)
+    as_layer = ref.moe_layer(spec, n_threads=4, want=("ids", "weights"))
+    assert (as_layer["ids"] == 0).all() and (as_layer["weights"] == 1.0).all()
+    assert np.array_equal(as_layer["out"].view(np.uint32), dense.view(np.uint32))
+    assert_layer_close(port.moe_layer(spec, want=())["out"], dense, tol=1e-4)
