@@ -4,9 +4,11 @@
  * Plain-C restatement of the reference's CPU path for the Gemma-4 MoE FFN layer, written from the
  * reference's documented algorithm. It is the checker for the CUDA path; it is pinned against the
  * reference itself (oracle/_ref, built from the reference sources) and against the committed
- * golden fixtures in tests/golden/. Single-threaded, no SIMD: float sums run in plain block order,
- * so layer outputs match the reference within float reordering, while every integer step
- * (quantised activations, integer block dot products, routing indices) matches bit for bit.
+ * golden fixtures in tests/golden/. Single-threaded, no SIMD. The quantised dot products restate the
+ * float order of the reference's x86 kernels (8 lanes, fused multiply-add per block, the fixed
+ * horizontal sum), so they are bit-equal to the reference's; every integer step (quantised
+ * activations, routing indices) matches bit for bit. The f32 router logits are summed in double
+ * here (the reference's f32 dot differs in the last bits; routing is compared off near ties).
  *
  * Each function cites the reference function it restates (paths relative to third_party/llama/ggml
  * unless stated).
@@ -274,125 +276,194 @@ void oracle_quantize_act(int32_t vdt, const float *x, void *y, int64_t n) {
 }
 
 /* ------------------------------------------------------------------ block dot products
- * Integer work per block is exact; the per-block float scale products and their running sum
- * follow the generic kernels' formulas (ggml-cpu/quants.c:314,645,947,1203). */
+ * The reference build runs the x86 AVX2 kernels of these dots (ggml-cpu/arch/x86/quants.c; the
+ * AVX-512 VNNI and AVX-VNNI forms of the same kernels produce the same integer lanes). Their float
+ * result depends on one fixed structure, restated here exactly:
+ *   - 8 integer lanes per 32 values: lane L sums the 4 consecutive products at positions
+ *     4L..4L+3 of every 32-value group (maddubs pairs, then madd_epi16 adding neighbouring pairs;
+ *     the sub-block scales multiply inside the integer lanes);
+ *   - per super-block (or 32-block) each lane converts to float and is fused-multiply-added into
+ *     its own f32 accumulator with that block's scale (_mm256_fmadd_ps);
+ *   - the 8 accumulators are reduced as hsum_float_8 (x86/quants.c:43-49):
+ *     ((a0 + a4) + (a2 + a6)) + ((a1 + a5) + (a3 + a7)).
+ * Integer lane sums are exact (no int16 saturation is reachable with these formats), so every
+ * rounding of the reference is reproduced and the dots are bit-equal to the reference's. */
 
+static float hsum8(const float a[8]) {
+    return ((a[0] + a[4]) + (a[2] + a[6])) + ((a[1] + a[5]) + (a[3] + a[7]));
+}
+
+/* ggml_vec_dot_q4_K_q8_K, AVX2 branch (x86/quants.c:1900-1982). Lane L of super-block i:
+ * sum over the four 64-value chunks c of sc[2c] * sum_e q4lo[32c+4L+e] * q8[64c+4L+e] +
+ * sc[2c+1] * sum_e q4hi[32c+4L+e] * q8[64c+32+4L+e]; d = y.d * x.d. The min term: four lanes
+ * m = mins[2m] * q8s[2m] + mins[2m+1] * q8s[2m+1] with q8s[j] = bsums[2j] + bsums[2j+1] (the
+ * 32-value sub-block sums), each fused into its own accumulator with dmin = -y.d * x.dmin, reduced
+ * as (m0 + m2) + (m1 + m3) and added last. */
 static float dot_q4k(int64_t n, const uint8_t *w, const uint8_t *x) {
-    float acc = 0.f;
+    float acc[8] = {0}, accm[4] = {0};
     for (int64_t i = 0; i < n / 256; ++i, w += 144, x += 292) {
-        float dx; memcpy(&dx, x, 4);
+        float yd; memcpy(&yd, x, 4);
         const int8_t *q8 = (const int8_t *)(x + 4);
         int16_t bs[16]; memcpy(bs, x + 260, 32);
         const uint8_t *sc = w + 4, *q4 = w + 16;
-        int main_sum = 0, min_sum = 0;
-        for (int c = 0; c < 4; ++c) {
-            int s0, m0, s1, m1;
-            q4k_scale_min(sc, 2 * c, &s0, &m0);
-            q4k_scale_min(sc, 2 * c + 1, &s1, &m1);
-            int a0 = 0, a1 = 0;
-            for (int l = 0; l < 32; ++l) {
-                a0 += (q4[32 * c + l] & 0xf) * q8[64 * c + l];
-                a1 += (q4[32 * c + l] >> 4) * q8[64 * c + 32 + l];
-            }
-            main_sum += s0 * a0 + s1 * a1;
-            min_sum += m0 * (bs[4 * c] + bs[4 * c + 1]) + m1 * (bs[4 * c + 2] + bs[4 * c + 3]);
+        const float d = yd * h2f(rd16(w));
+        const float dmin = -yd * h2f(rd16(w + 2));
+        int scv[8], mnv[8];
+        for (int j = 0; j < 8; ++j) q4k_scale_min(sc, j, &scv[j], &mnv[j]);
+        for (int m = 0; m < 4; ++m) {
+            const int prod = mnv[2 * m] * (bs[4 * m] + bs[4 * m + 1]) + mnv[2 * m + 1] * (bs[4 * m + 2] + bs[4 * m + 3]);
+            accm[m] = fmaf(dmin, (float)prod, accm[m]);
         }
-        const float d = h2f(rd16(w)) * dx, dm = h2f(rd16(w + 2)) * dx;
-        acc += d * (float)main_sum;
-        acc -= dm * (float)min_sum;
+        for (int L = 0; L < 8; ++L) {
+            int lane = 0;
+            for (int c = 0; c < 4; ++c) {
+                int lo = 0, hi = 0;
+                for (int e = 0; e < 4; ++e) {
+                    const int b = 32 * c + 4 * L + e;
+                    lo += (q4[b] & 0xf) * q8[64 * c + 4 * L + e];
+                    hi += (q4[b] >> 4) * q8[64 * c + 32 + 4 * L + e];
+                }
+                lane += scv[2 * c] * lo + scv[2 * c + 1] * hi;
+            }
+            acc[L] = fmaf(d, (float)lane, acc[L]);
+        }
     }
-    return acc;
+    const float summ = (accm[0] + accm[2]) + (accm[1] + accm[3]);
+    return hsum8(acc) + summ;
 }
 
+/* ggml_vec_dot_iq2_s_q8_K, AVX2 branch (x86/quants.c:2937-3025). Lane L of super-block i: sum over
+ * the eight 32-blocks b of ls(b, half) * sum_e grid * sign * q8 at 32b+4L+e, where the half is the
+ * block's first 16 values for L < 4 (low scale nibble) and its second 16 for L >= 4, ls = 2 * nibble
+ * + 1; d = x.d * y.d; the total times 1/8. */
 static float dot_iq2s(int64_t n, const uint8_t *w, const uint8_t *x) {
-    float acc = 0.f;
+    float acc[8] = {0};
     for (int64_t i = 0; i < n / 256; ++i, w += 82, x += 292) {
-        float dx; memcpy(&dx, x, 4);
+        float yd; memcpy(&yd, x, 4);
         const int8_t *q8 = (const int8_t *)(x + 4);
         const uint8_t *signs = w + 34, *scales = w + 74;
-        int bsum = 0;
-        for (int ib = 0; ib < 8; ++ib) {
-            int s[2] = {0, 0};
-            for (int l = 0; l < 4; ++l) {
-                const int g = 4 * ib + l;
-                const uint64_t row = k_iq2s_grid[iq2s_index(w, g)];
-                for (int j = 0; j < 8; ++j) {
-                    const int mag = (int)((row >> (8 * j)) & 0xff);
+        const float d = h2f(rd16(w)) * yd;
+        int lane[8] = {0};
+        for (int b = 0; b < 8; ++b) {
+            for (int L = 0; L < 8; ++L) {
+                int s = 0;
+                for (int e = 0; e < 4; ++e) {
+                    const int pos = 4 * L + e, g = 4 * b + pos / 8, j = pos % 8;
+                    const int mag = (int)((k_iq2s_grid[iq2s_index(w, g)] >> (8 * j)) & 0xff);
                     const int v = (signs[g] >> j) & 1 ? -mag : mag;
-                    s[l >> 1] += v * q8[8 * g + j];
+                    s += v * q8[32 * b + pos];
                 }
+                const int ls = 2 * (L < 4 ? (scales[b] & 0xf) : (scales[b] >> 4)) + 1;
+                lane[L] += ls * s;
             }
-            bsum += (1 + 2 * (scales[ib] & 0xf)) * s[0] + (1 + 2 * (scales[ib] >> 4)) * s[1];
         }
-        acc += (h2f(rd16(w)) * dx) * (float)bsum;
+        for (int L = 0; L < 8; ++L) acc[L] = fmaf(d, (float)lane[L], acc[L]);
     }
-    return 0.125f * acc;
+    return 0.125f * hsum8(acc);
 }
 
+/* ggml_vec_dot_q5_0_q8_0, AVX2 branch (x86/quants.c:1004-1043): values (q | qh bit << 4) - 16 in
+ * element order; one accumulator, d = x.d * y.d per 32-block. */
 static float dot_q5_0(int64_t n, const uint8_t *w, const uint8_t *x) {
-    float acc = 0.f;
+    float acc[8] = {0};
     for (int64_t i = 0; i < n / 32; ++i, w += 22, x += 34) {
         const uint32_t qh = (uint32_t)w[2] | ((uint32_t)w[3] << 8) | ((uint32_t)w[4] << 16) | ((uint32_t)w[5] << 24);
         const int8_t *q8 = (const int8_t *)(x + 2);
-        int s = 0;
-        for (int j = 0; j < 16; ++j) {
-            const int v0 = (int)((w[6 + j] & 0xf) | (((qh >> j) & 1) << 4)) - 16;
-            const int v1 = (int)((w[6 + j] >> 4) | (((qh >> (j + 16)) & 1) << 4)) - 16;
-            s += v0 * q8[j] + v1 * q8[j + 16];
-        }
-        acc += (h2f(rd16(w)) * h2f(rd16(x))) * (float)s;
-    }
-    return acc;
-}
-
-static float dot_iq4nl(int64_t n, const uint8_t *w, const uint8_t *x) {
-    float acc = 0.f;
-    for (int64_t i = 0; i < n / 32; ++i, w += 18, x += 34) {
-        const int8_t *q8 = (const int8_t *)(x + 2);
-        int s = 0;
-        for (int j = 0; j < 16; ++j)
-            s += q8[j] * k_iq4nl[w[2 + j] & 0xf] + q8[j + 16] * k_iq4nl[w[2 + j] >> 4];
-        acc += (h2f(rd16(x)) * h2f(rd16(w))) * (float)s;
-    }
-    return acc;
-}
-
-/* ggml_vec_dot_iq2_xxs_q8_K (ggml-cpu/quants.c:855): per 32-block the signed integer dot times
- * (2 * sub-scale + 1), summed per super-block, scaled by d_w * d_x; the total times 1/8 */
-static float dot_iq2xxs(int64_t n, const uint8_t *w, const uint8_t *x) {
-    float acc = 0.f;
-    for (int64_t i = 0; i < n / 256; ++i, w += 66, x += 292) {
-        float dx; memcpy(&dx, x, 4);
-        const int8_t *q8 = (const int8_t *)(x + 4);
-        int bsum = 0;
-        for (int ib = 0; ib < 8; ++ib) {
-            const uint8_t *g8 = w + 2 + 8 * ib;
-            const uint32_t hi = (uint32_t)g8[4] | ((uint32_t)g8[5] << 8) | ((uint32_t)g8[6] << 16) | ((uint32_t)g8[7] << 24);
+        const float d = h2f(rd16(w)) * h2f(rd16(x));
+        for (int L = 0; L < 8; ++L) {
             int s = 0;
-            for (int l = 0; l < 4; ++l) {
-                const uint64_t row = k_iq2xxs_grid[g8[l]];
-                const uint8_t sg = k_iq2xxs_signs[(hi >> (7 * l)) & 127];
-                for (int j = 0; j < 8; ++j) {
-                    const int mag = (int)((row >> (8 * j)) & 0xff);
-                    s += ((sg >> j) & 1 ? -mag : mag) * q8[32 * ib + 8 * l + j];
-                }
+            for (int e = 0; e < 4; ++e) {
+                const int j = 4 * L + e;
+                const int nib = j < 16 ? (w[6 + j] & 0xf) : (w[6 + j - 16] >> 4);
+                s += ((int)(nib | (((qh >> j) & 1) << 4)) - 16) * q8[j];
             }
-            bsum += s * (int)(2 * (hi >> 28) + 1);
+            acc[L] = fmaf(d, (float)s, acc[L]);
         }
-        acc += (h2f(rd16(w)) * dx) * (float)bsum;
     }
-    return 0.125f * acc;
+    return hsum8(acc);
 }
 
-/* ggml_vec_dot_q8_0_q8_0 (ggml-cpu/quants.c:400): integer dot per 32-block times d_w * d_x */
-static float dot_q8_0(int64_t n, const uint8_t *w, const uint8_t *x) {
-    float acc = 0.f;
-    for (int64_t i = 0; i < n / 32; ++i, w += 34, x += 34) {
-        int s = 0;
-        for (int j = 0; j < 32; ++j) s += (int8_t)w[2 + j] * (int8_t)x[2 + j];
-        acc += (float)s * (h2f(rd16(w)) * h2f(rd16(x)));
+/* ggml_vec_dot_iq4_nl_q8_0, AVX2 branch (x86/quants.c:3782-3815) and its scalar tail (:3854-3862):
+ * even 32-blocks into one set of lane accumulators and odd blocks into another (d = y.d * x.d),
+ * the two added lane by lane before the reduction; a last unpaired block is added in scalar. */
+static float dot_iq4nl(int64_t n, const uint8_t *w, const uint8_t *x) {
+    float acc[2][8] = {{0}};
+    const int64_t nb = n / 32;
+    int64_t ib = 0;
+    for (; ib + 1 < nb; ib += 2) {
+        for (int h = 0; h < 2; ++h) {
+            const uint8_t *wb = w + (ib + h) * 18, *xb = x + (ib + h) * 34;
+            const int8_t *q8 = (const int8_t *)(xb + 2);
+            const float d = h2f(rd16(xb)) * h2f(rd16(wb));
+            for (int L = 0; L < 8; ++L) {
+                int s = 0;
+                for (int e = 0; e < 4; ++e) {
+                    const int j = 4 * L + e;
+                    s += k_iq4nl[j < 16 ? (wb[2 + j] & 0xf) : (wb[2 + j - 16] >> 4)] * q8[j];
+                }
+                acc[h][L] = fmaf(d, (float)s, acc[h][L]);
+            }
+        }
     }
-    return acc;
+    float a[8];
+    for (int L = 0; L < 8; ++L) a[L] = acc[0][L] + acc[1][L];
+    float sumf = nb >= 2 ? hsum8(a) : 0.f;
+    for (; ib < nb; ++ib) {
+        const uint8_t *wb = w + ib * 18, *xb = x + ib * 34;
+        const int8_t *q8 = (const int8_t *)(xb + 2);
+        const float d = h2f(rd16(xb)) * h2f(rd16(wb));
+        int s1 = 0, s2 = 0;
+        for (int j = 0; j < 16; ++j) {
+            s1 += q8[j] * k_iq4nl[wb[2 + j] & 0xf];
+            s2 += q8[j + 16] * k_iq4nl[wb[2 + j] >> 4];
+        }
+        sumf += d * (float)(s1 + s2);
+    }
+    return sumf;
+}
+
+/* ggml_vec_dot_iq2_xxs_q8_K, AVX2 branch (x86/quants.c:2522-2563): lane L of super-block i sums,
+ * over the eight 32-blocks b, (2 * ls_b + 1) * sum_e grid * sign * q8 at 32b+4L+e (the sign pattern
+ * of each 8-group from the 7-bit index); d = x.d * y.d; the total times 1/8. */
+static float dot_iq2xxs(int64_t n, const uint8_t *w, const uint8_t *x) {
+    float acc[8] = {0};
+    for (int64_t i = 0; i < n / 256; ++i, w += 66, x += 292) {
+        float yd; memcpy(&yd, x, 4);
+        const int8_t *q8 = (const int8_t *)(x + 4);
+        const float d = h2f(rd16(w)) * yd;
+        int lane[8] = {0};
+        for (int b = 0; b < 8; ++b) {
+            const uint8_t *g8 = w + 2 + 8 * b;
+            const uint32_t hi = (uint32_t)g8[4] | ((uint32_t)g8[5] << 8) | ((uint32_t)g8[6] << 16) | ((uint32_t)g8[7] << 24);
+            const int ls = (int)(2 * (hi >> 28) + 1);
+            for (int L = 0; L < 8; ++L) {
+                int s = 0;
+                for (int e = 0; e < 4; ++e) {
+                    const int pos = 4 * L + e, l = pos / 8, j = pos % 8;
+                    const int mag = (int)((k_iq2xxs_grid[g8[l]] >> (8 * j)) & 0xff);
+                    const uint8_t sg = k_iq2xxs_signs[(hi >> (7 * l)) & 127];
+                    s += ((sg >> j) & 1 ? -mag : mag) * q8[32 * b + pos];
+                }
+                lane[L] += ls * s;
+            }
+        }
+        for (int L = 0; L < 8; ++L) acc[L] = fmaf(d, (float)lane[L], acc[L]);
+    }
+    return 0.125f * hsum8(acc);
+}
+
+/* ggml_vec_dot_q8_0_q8_0, AVX2 branch (x86/quants.c:1170-1204): one accumulator, d = x.d * y.d */
+static float dot_q8_0(int64_t n, const uint8_t *w, const uint8_t *x) {
+    float acc[8] = {0};
+    for (int64_t i = 0; i < n / 32; ++i, w += 34, x += 34) {
+        const float d = h2f(rd16(w)) * h2f(rd16(x));
+        for (int L = 0; L < 8; ++L) {
+            int s = 0;
+            for (int e = 0; e < 4; ++e) s += (int8_t)w[2 + 4 * L + e] * (int8_t)x[2 + 4 * L + e];
+            acc[L] = fmaf(d, (float)s, acc[L]);
+        }
+    }
+    return hsum8(acc);
 }
 
 float oracle_vec_dot(int32_t wtype, int64_t n, const void *w, const void *xq) {
