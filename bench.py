@@ -7,9 +7,16 @@ One JSON line on rank 0. A "step" is one layer forward over the config's tokens.
 layer-tokens/s summed over ranks, device-timed with CUDA events on the launching stream (inputs
 resident in HBM, L2 flushed between steps with a 256 MiB write that is not timed). `e2e` is the
 same metric through the public API with the step's input copied from pinned host memory and the
-output read back inside the timed region. Decode configs do not shard: at N > 1 every rank runs
-an independent replica (weak scaling). `--impl reference` times the reference's own CPU
-implementation (ggml-cpu built from the reference sources, oracle/_ref) on this host's cores.
+output read back inside the timed region.
+
+The metric is quoted at T=2048 and T=1: the default line is the T=2048 prefill layer
+(prefill_t2048_q4k) and carries the T=1 decode layer (decode_t1_iq2s) as `secondary`. At N > 1
+the default layer runs expert-parallel (experts sharded over the ranks, NCCL all-to-all dispatch
+and combine) with 2048 tokens per rank (weak scaling; at N = 4 that is the T=8192 expert-parallel
+config). Other decode configs do not shard: at N > 1 every rank runs an independent replica.
+`--impl reference` times the reference's own CPU implementation (ggml-cpu built from the
+reference sources, oracle/_ref) on this host's cores, with weights from the reference's own
+quantiser; it never loads this repository's library.
 """
 from __future__ import annotations
 
@@ -28,7 +35,8 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-DEFAULT_CONFIG = "decode_t4_mixed"
+DEFAULT_CONFIG = "prefill_t2048_q4k"
+SECONDARY_CONFIG = "decode_t1_iq2s"   # the metric's T=1 point, reported beside the default line
 METRIC = "moe_layer_tokens_per_s"
 
 
@@ -42,6 +50,7 @@ def parse():
     p.add_argument("--no-graph", action="store_true", help="launch eagerly instead of replaying a CUDA graph")
     p.add_argument("--cpu-sample-s", type=float, default=15.0, help="CPU baseline budget (seconds)")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-secondary", action="store_true", help="skip the T=1 decode line of the default run")
     p.add_argument("--block-norms", action="store_true",
                    help="the whole Gemma-4 MoE block: pre / router-input / output rms_norms fused into the layer "
                         "(moeb_layer_forward_gemma4); input is the block input (attn_out)")
@@ -196,22 +205,99 @@ def time_sidecar(host, x, budget_s, n_threads=None):
         return {"unavailable": f"{type(exc).__name__}: {exc}"[:200]}
 
 
+def reference_layer_spec(cfg, x):
+    """The config's layer for the reference arm, built without this repository's library: the same
+    seeded f32 weights (llapis_b200.workload, numpy only) quantised by the reference's own
+    ggml_quantize_chunk (oracle/_ref), in parallel over the host cores (ctypes releases the GIL),
+    cached per expert on disk under its own key."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    from llapis_b200 import workload
+    from oracle import LayerSpec, Ref
+    from oracle.oracle import IQ4_NL, Q4_K, Q5_0
+    ref = Ref()
+    E, d, nff = cfg.n_expert, cfg.d_model, cfg.n_ff
+    hot = [int(e) for e in cfg.hot]
+    is_hot = np.zeros(E, bool)
+    is_hot[hot] = True
+    ct = cfg.cold_gu_type
+
+    def one(e):
+        def make():
+            gu, dn = workload.expert_f32(cfg, 0, e)
+            ta, tb = (Q4_K, Q5_0) if is_hot[e] else (ct, IQ4_NL)
+            return np.concatenate([ref.quantize(ta, gu).reshape(-1), ref.quantize(tb, dn).reshape(-1)])
+        return workload._cached(f"ref-v1|{cfg.seed}|0|{e}|{d}|{nff}|{int(is_hot[e])}|{ct}", make)
+
+    with ThreadPoolExecutor(max_workers=os.cpu_count() or 1) as ex:
+        blobs = list(ex.map(one, range(E)))
+    hgu, hdn = 2 * nff * ref.row_size(Q4_K, d), d * ref.row_size(Q5_0, nff)
+    cgu, cdn = 2 * nff * ref.row_size(ct, d), d * ref.row_size(IQ4_NL, nff)
+    K = len(hot)
+    pools = {"hot_gu": [], "hot_down": [], "cold_gu": np.zeros((E, 2 * nff, cgu // (2 * nff)), np.uint8),
+             "cold_down": np.zeros((E, d, cdn // d), np.uint8)}
+    for e in hot:
+        pools["hot_gu"].append(blobs[e][:hgu].reshape(2 * nff, -1))
+        pools["hot_down"].append(blobs[e][hgu:hgu + hdn].reshape(d, -1))
+    for e in range(E):
+        if not is_hot[e]:
+            pools["cold_gu"][e] = blobs[e][:cgu].reshape(2 * nff, -1)
+            pools["cold_down"][e] = blobs[e][cgu:cgu + cdn].reshape(d, -1)
+    n_cold = E - K
+    exp_slot = np.full(E, -1, np.int32)
+    exp_slot[hot] = np.arange(K, dtype=np.int32)
+    b_router = None
+    if cfg.bias_s is not None:
+        b_router = (-cfg.bias_s * np.log1p(np.arange(E, dtype=np.float64))).astype(np.float32)
+    return LayerSpec(d, nff, E, cfg.top_k, x=x, w_router=workload._normal((cfg.seed, 0, 1 << 20), (E, d), 0.02),
+                     b_router=b_router, n_slots=K, exp_slot=exp_slot if K else None,
+                     slot_exp=np.array(hot, np.int32) if K else None,
+                     slot_state=np.full(K, 2, np.int32) if K else None,
+                     hot_gu=np.stack(pools["hot_gu"]) if K else None,
+                     hot_down=np.stack(pools["hot_down"]) if K else None,
+                     s_hot=np.ones(K, np.float32) if K else None, cold_type_gu=ct,
+                     cold_gu=pools["cold_gu"] if n_cold else None, cold_down=pools["cold_down"] if n_cold else None,
+                     s_cold=np.ones(E, np.float32) if n_cold else None)
+
+
 def run_reference(args):
+    """--impl reference: the reference's CPU implementation of the path (oracle/_ref: ggml-cpu's
+    MUL_MAT_ID graph of build_moe_ffn, built from the reference sources) on all host threads, each
+    step a bounded sample (<= 256 tokens) of the config's batch. Rank 0 only under torchrun."""
     rank, _, world = dist_env()
     if rank != 0:
         return 0
-    from llapis_b200 import workload
-    cfg = workload.CONFIGS[args.config]
-    host = workload.build_layer(cfg)
-    norms = workload.block_norms(cfg) if args.block_norms else None
-    # bounded sample: at most 256 tokens per step (tokens/s is per token)
-    x = (workload.make_block_input(cfg) if norms else workload.make_input(cfg))[:256]
-    cb = time_reference(host, x, args.warmup, args.steps, budget_s=120.0, norms=norms)
-    if cb is None:
+    from oracle import Ref, ref_available
+    if not ref_available():
         print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref (reference ggml-cpu build) missing"}))
         return 0
-    v = cb["value"]
-    line = {"metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
+    from llapis_b200 import workload
+    cfg = workload.CONFIGS[args.config]
+    norms = workload.block_norms(cfg) if args.block_norms else None
+    x = (workload.make_block_input(cfg) if norms else workload.make_input(cfg))[:256]
+    spec = reference_layer_spec(cfg, x)
+    r = Ref()
+    nt = os.cpu_count() or 1
+
+    def fwd():
+        if norms is not None:
+            r.gemma4_block(spec, norms, n_threads=nt, want=())
+        else:
+            r.moe_layer(spec, n_threads=nt, want=())
+    for _ in range(max(1, args.warmup)):
+        fwd()
+    times = []
+    t_end = time.perf_counter() + 120.0
+    while len(times) < max(1, args.steps) and (len(times) < 2 or time.perf_counter() < t_end):
+        t0 = time.perf_counter()
+        fwd()
+        times.append(time.perf_counter() - t0)
+    v = x.shape[0] * len(times) / sum(times)
+    cb = {"value": v, "unit": "tokens/s", "cores": nt, "kind": "reference",
+          "sample": f"{len(times)} layer forwards of {x.shape[0]} tokens each (a bounded sample of the {cfg.n_tokens}-token "
+                    f"batch), ggml-cpu O1 graph built from the reference sources, weights from the reference "
+                    f"quantiser, {nt} threads", "ms_per_forward": 1e3 * sum(times) / len(times)}
+    line = {"metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus, "steps": len(times),
             "warmup": args.warmup, "ms_per_step": cb["ms_per_forward"], "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "q8 int dot / f32", "data": "synthetic (seeded)",
             "config": {"workload": cfg.name, "n_tokens": cfg.n_tokens, "layers": 1,
@@ -232,9 +318,11 @@ def local_shard(host, rank, world):
                                s_hot=host.s_hot[mine], cold_gu=None, cold_down=None, s_cold=None)
 
 
-def run_ep(args, cfg):
-    """Expert-parallel prefill: experts sharded over the ranks, tokens split
-    T/G per rank, NCCL all-to-all dispatch and combine (llapis_b200/ep.py); strong scaling."""
+def run_ep(args, cfg, tokens_per_rank=None):
+    """Expert-parallel prefill: experts sharded over the ranks, tokens split T/G per rank, NCCL
+    all-to-all dispatch and combine (llapis_b200/ep.py). With tokens_per_rank the batch grows with
+    the ranks (T = tokens_per_rank x G, weak scaling: the default T=2048 layer at N > 1); without,
+    the config's T is split (strong scaling: the T=8192 expert-parallel config)."""
     import torch
     import torch.distributed as dist
     from datetime import timedelta
@@ -253,7 +341,7 @@ def run_ep(args, cfg):
                                 timeout=timedelta(seconds=300), device_id=dev)
     host = workload.build_layer(cfg)
     layer = MoELayer(local_shard(host, rank, world), dev)
-    x_all = workload.make_input(cfg)
+    x_all = workload.make_input(cfg, n_tokens=tokens_per_rank * world if tokens_per_rank else None)
     T = x_all.shape[0]
     assert T % world == 0
     x_host = x_all[rank * (T // world):(rank + 1) * (T // world)]
@@ -326,7 +414,7 @@ def run_ep(args, cfg):
         line = {
             "metric": METRIC, "value": T * args.steps / (dev_ms / 1e3), "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": avg_ms, "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None,
+            "scaling": "weak" if tokens_per_rank else "strong", "vs_baseline": None,
             "dtype": "int8 x q4/q5 integer dots on fp16-exact tcgen05 MMAs / f32",
             "data": "synthetic (seeded N(0,0.02) weights quantised to ggml formats, bf16-valued N(0,1) activations)",
             "config": {"workload": cfg.name, "n_tokens": T, "layers": 1, "d_model": cfg.d_model,
@@ -474,17 +562,42 @@ def main():
     import torch
     import torch.distributed as dist
 
-    from llapis_b200 import capi, workload
-    from llapis_b200.layer import MoELayer
+    from llapis_b200 import workload
 
     rank, local, world = dist_env()
+    cfg = workload.CONFIGS[args.config]
+    if world > 1 and cfg.name == DEFAULT_CONFIG:
+        # the default layer at N > 1: expert-parallel, 2048 tokens per rank (weak scaling)
+        return run_ep(args, cfg, tokens_per_rank=cfg.n_tokens)
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    line = measure_layer(args, cfg, dev, rank, world, cpu_sample=not args.no_cpu_baseline)
+    if cfg.name == DEFAULT_CONFIG and world == 1 and not args.no_secondary and not args.block_norms:
+        sec = measure_layer(args, workload.CONFIGS[SECONDARY_CONFIG], dev, rank, world,
+                            cpu_sample=not args.no_cpu_baseline)
+        line["secondary"] = {k: sec[k] for k in ("metric", "value", "unit", "ms_per_step", "dtype", "config", "e2e",
+                                                 "gpu_launches", "roofline", "cpu_baseline", "clocks", "device_error")}
+    if rank == 0:
+        print(json.dumps(line))
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
 
-    cfg = workload.CONFIGS[args.config]
+
+def measure_layer(args, cfg, dev, rank, world, cpu_sample=True):
+    """One single-GPU layer config (or one replica of it per rank): device-timed steps (CUDA-graph
+    replay, L2 flushed between steps), the end-to-end steps through the public API, the roofline of
+    the dominant kernel and the reference CPU baseline (rank 0, N=1). Returns the JSON line."""
+    import torch
+    import torch.distributed as dist
+
+    from llapis_b200 import capi, workload
+    from llapis_b200.layer import MoELayer
+
+    local = dev.index
     host = workload.build_layer(cfg)
     norms = workload.block_norms(cfg) if args.block_norms else None
     layer = MoELayer(host, dev, norms=norms)
@@ -624,7 +737,8 @@ def main():
                              f"algorithmic bytes {alg_bytes} per step"}
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    line = None
+    if rank == 0 and world == 1 and cpu_sample:
         # a bounded sample: at most 256 tokens of the batch (the CPU cost per token is flat in T)
         cpu = time_reference(host, x_host[:256], 1, 1000, args.cpu_sample_s, norms=norms)
         if cpu is not None and norms is None and T <= 4:
@@ -650,11 +764,8 @@ def main():
             "clocks": clk.summary(),
             "device_error": err,
         }
-        print(json.dumps(line))
-    if world > 1:
-        del graph
-        dist.destroy_process_group()
-    return 0
+    del graph
+    return line
 
 
 if __name__ == "__main__":

@@ -198,6 +198,9 @@ int moeb_prefill_profile_read(float *ms, int32_t n);
  *    rejected with MOEB_ESPACE (the Gemma-4 26B-A4B layer needs about 2.2 MB);
  *  - the first call on a device does one-time set-up there (format tables, the device address of
  *    the static array); make that first call before any stream capture on that device;
+ *  - the device address is kept for the life of the process: do not use this entry on a device
+ *    after cudaDeviceReset (or any other re-creation of its primary context), which reloads the
+ *    library's module there and leaves the kept address pointing at freed memory;
  *  - all calls share the one array per device and it keeps the last call's contents: calls that
  *    overlap on the GPU (different streams, or different host threads, on the same device) race.
  *    Nothing in it needs clearing between calls; every byte a forward reads it writes first. */

@@ -67,11 +67,15 @@ TypeSize type_size(int32_t t) {
     }
 }
 
-// buffered little-endian reader over a FILE
+// buffered little-endian reader over a FILE of `size` bytes; every length read from the file is
+// checked against the bytes left before it is used, so a corrupt header ends the parse instead of
+// seeking backwards or allocating what the file cannot hold
 struct In {
     FILE *f;
+    uint64_t size = 0;
     uint64_t pos = 0;
     bool ok = true;
+    uint64_t left() const { return pos <= size ? size - pos : 0; }
     template <class T> T get() {
         T v{};
         if (ok && std::fread(&v, sizeof(T), 1, f) == 1) pos += sizeof(T);
@@ -80,14 +84,14 @@ struct In {
     }
     std::string str() {
         const uint64_t n = get<uint64_t>();
-        if (!ok || n > (1u << 24)) return ok = false, std::string();
+        if (!ok || n > (1u << 24) || n > left()) return ok = false, std::string();
         std::string s(n, '\0');
         if (n && std::fread(&s[0], 1, n, f) != n) ok = false;
         pos += n;
         return s;
     }
     void skip(uint64_t n) {
-        if (ok && std::fseek(f, (long)n, SEEK_CUR) == 0) pos += n;
+        if (ok && n <= left() && std::fseek(f, (long)n, SEEK_CUR) == 0) pos += n;
         else ok = false;
     }
 };
@@ -124,7 +128,10 @@ extern "C" moeb_gguf *moeb_gguf_open(const char *path) {
     if (!path) return set_last_error(MOEB_EINVAL, "moeb_gguf_open: null path"), nullptr;
     FILE *f = std::fopen(path, "rb");
     if (!f) return set_last_error(MOEB_EINVAL, "moeb_gguf_open: cannot open %s", path), nullptr;
-    In in{f};
+    std::fseek(f, 0, SEEK_END);
+    const long fsize = std::ftell(f);
+    std::fseek(f, 0, SEEK_SET);
+    In in{f, fsize > 0 ? (uint64_t)fsize : 0};
     auto *g = new moeb_gguf();
     g->path = path;
     const uint32_t magic = in.get<uint32_t>(), version = in.get<uint32_t>();
@@ -142,9 +149,11 @@ extern "C" moeb_gguf *moeb_gguf_open(const char *path) {
             const uint32_t et = in.get<uint32_t>();
             const uint64_t n = in.get<uint64_t>();
             if (et == kStr) {
-                for (uint64_t j = 0; j < n && in.ok; ++j) in.str();
+                if (n > in.left() / 8) err = "array longer than the file";   // every string has an 8-byte length
+                for (uint64_t j = 0; !err && j < n && in.ok; ++j) in.str();
             } else if (scalar_bytes(et)) {
-                in.skip(n * (uint64_t)scalar_bytes(et));
+                if (n > in.left() / (uint64_t)scalar_bytes(et)) err = "array longer than the file";
+                else in.skip(n * (uint64_t)scalar_bytes(et));
             } else {
                 err = "bad array element type";
             }
@@ -185,16 +194,23 @@ extern "C" moeb_gguf *moeb_gguf_open(const char *path) {
             err = "tensor of an unknown type or a row that is not whole blocks";
             break;
         }
-        t.nbytes = (uint64_t)(t.ne[0] / ts.blck) * ts.bytes * (uint64_t)t.ne[1] * (uint64_t)t.ne[2] * (uint64_t)t.ne[3];
+        uint64_t nb = (uint64_t)(t.ne[0] / ts.blck);
+        bool ovf = __builtin_mul_overflow(nb, (uint64_t)ts.bytes, &nb);
+        for (int d = 1; d < 4; ++d) ovf = ovf || __builtin_mul_overflow(nb, (uint64_t)t.ne[d], &nb);
+        if (ovf) { err = "tensor size overflows"; break; }
+        t.nbytes = nb;
         infos.emplace_back(name, t);
     }
     if (!err) {
         g->data_offset = n_tensors ? (in.pos + g->alignment - 1) / g->alignment * g->alignment : in.pos;
-        std::fseek(f, 0, SEEK_END);
-        const uint64_t size = (uint64_t)std::ftell(f);
+        const uint64_t size = in.size;
         for (auto &nt : infos) {
-            nt.second.offset += g->data_offset;   // absolute
-            if (nt.second.offset + nt.second.nbytes > size) { err = "tensor data past the end of the file"; break; }
+            uint64_t end = 0;
+            if (__builtin_add_overflow(nt.second.offset, g->data_offset, &nt.second.offset) ||   // absolute
+                __builtin_add_overflow(nt.second.offset, nt.second.nbytes, &end) || end > size) {
+                err = "tensor data past the end of the file";
+                break;
+            }
             g->tensors[nt.first] = nt.second;
         }
     }

@@ -7,6 +7,7 @@
 #include "moert_store.h"
 
 #include <fcntl.h>
+#include <sys/stat.h>
 #include <unistd.h>
 
 #include <chrono>
@@ -99,6 +100,12 @@ struct Store {
     IndexHeader hdr{};
     std::vector<IndexRecord> recs;
     int pack_fd = -1;
+    uint64_t pack_bytes = 0;
+    // whether record r's page lies inside the pack (offset + nbytes without overflow)
+    bool in_pack(const IndexRecord &r) const {
+        uint64_t end = 0;
+        return !__builtin_add_overflow(r.offset, r.nbytes, &end) && end <= pack_bytes;
+    }
 };
 
 bool load_store(const char *index_path, Store &s) {
@@ -107,6 +114,17 @@ bool load_store(const char *index_path, Store &s) {
     bool ok = std::fread(&s.hdr, 1, sizeof(s.hdr), f) == sizeof(s.hdr);
     if (!ok) say("expert store: %s: truncated header\n", index_path);
     ok = ok && header_ok(s.hdr, index_path);
+    if (ok) {
+        // the record list must fit in the file before anything is sized from the header's count
+        std::fseek(f, 0, SEEK_END);
+        const long fsz = std::ftell(f);
+        uint64_t need = 0;
+        if (fsz < 0 || __builtin_mul_overflow(s.hdr.record_count, (uint64_t)s.hdr.record_stride, &need) ||
+            __builtin_add_overflow(need, (uint64_t)s.hdr.header_bytes, &need) || need > (uint64_t)fsz) {
+            say("expert store: %s: record list longer than the file\n", index_path);
+            ok = false;
+        }
+    }
     if (ok && std::fseek(f, (long)s.hdr.header_bytes, SEEK_SET) != 0) ok = false;
     if (ok) {
         s.recs.resize(s.hdr.record_count);
@@ -125,6 +143,8 @@ bool load_store(const char *index_path, Store &s) {
     const std::string pp = pack_path_of(index_path);
     s.pack_fd = ::open(pp.c_str(), O_RDONLY | O_CLOEXEC);
     if (s.pack_fd < 0) return say("expert store: cannot open pack %s\n", pp.c_str()), false;
+    struct stat st{};
+    s.pack_bytes = ::fstat(s.pack_fd, &st) == 0 ? (uint64_t)st.st_size : 0;
     PackHeader ph{};
     if (!pread_all(s.pack_fd, &ph, sizeof(ph), 0) || std::memcmp(ph.magic, kPackMagic, 8) != 0 ||
         ph.format_version != kVersion) {
@@ -192,8 +212,9 @@ extern "C" int64_t moert_store_verify(const char *index_path) {
     int64_t bad = 0;
     for (size_t i = 0; i < s.recs.size(); ++i) {
         const IndexRecord &r = s.recs[i];
-        buf.resize(r.nbytes);
-        const bool read = pread_all(s.pack_fd, buf.data(), r.nbytes, r.offset);
+        const bool inside = s.in_pack(r);
+        if (inside) buf.resize(r.nbytes);
+        const bool read = inside && pread_all(s.pack_fd, buf.data(), r.nbytes, r.offset);
         if (!read || moert_store_fnv1a64(buf.data(), r.nbytes, MOERT_STORE_FNV_SEED) != r.checksum) {
             std::fprintf(stderr, "expert store: page %zu (layer %u, expert %u, kind %u%s): %s\n", i, r.layer, r.expert_id,
                          r.matrix_kind, (r.flags & MOERT_PAGE_SCALE) ? ", scale" : "",
@@ -277,7 +298,7 @@ extern "C" uint64_t moert_store_reader_read(moert_store_reader *r, int32_t layer
                      rec->nbytes, dst_cap, layer, expert);
         return 0;
     }
-    if (!pread_all(r->s.pack_fd, dst, rec->nbytes, rec->offset)) {
+    if (!r->s.in_pack(*rec) || !pread_all(r->s.pack_fd, dst, rec->nbytes, rec->offset)) {
         std::fprintf(stderr, "expert store: page read failed (layer %d, expert %d, kind %d)\n", layer, expert, kind);
         return 0;
     }

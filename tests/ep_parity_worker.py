@@ -1,9 +1,11 @@
-"""Multi-GPU parity check of the expert-parallel forward (run under torchrun, one rank per GPU):
-every rank computes its token shard with experts sharded over the ranks; rank 0 gathers the
-outputs and compares them with the whole layer on one GPU (moeb_layer_forward, same kernels).
-Prints one JSON line; exits non-zero on a mismatch.
+"""TEST WORKER — the multi-GPU parity check of the expert-parallel forward, one rank per GPU
+(tests/test_gpu_ep_multi.py launches it under torchrun): every rank computes its token shard with
+the experts sharded over the ranks; rank 0 gathers the outputs and compares them with the whole
+layer on one GPU (moeb_layer_forward, same kernels). Prints one JSON line; exits non-zero on a
+mismatch.
 
-    torchrun --nproc-per-node 2 --master-addr 127.0.0.1 -m llapis_b200.ep_parity [config] [n_tokens]
+    python -m torch.distributed.run --nproc-per-node 2 --master-addr 127.0.0.1 tests/ep_parity_worker.py \
+        [config] [n_tokens]
 """
 from __future__ import annotations
 
@@ -18,6 +20,7 @@ import torch.distributed as dist
 
 
 def main() -> int:
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
     from llapis_b200 import workload
     from llapis_b200.ep import EPMoE, local_experts
     from llapis_b200.layer import MoELayer
@@ -27,7 +30,7 @@ def main() -> int:
     rank, local, world = int(os.environ["RANK"]), int(os.environ["LOCAL_RANK"]), int(os.environ["WORLD_SIZE"])
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
     cfg = workload.CONFIGS[name]
     T = int(sys.argv[2]) if len(sys.argv) > 2 else cfg.n_tokens
     host = workload.build_layer(cfg)

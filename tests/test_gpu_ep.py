@@ -1,6 +1,6 @@
 """The expert half on given routing (moeb_layer_forward_routed) and the expert-parallel forward at
 world size 1 over NCCL, on a B200 (-m gpu). Multi-rank runs: bench.py --config
-ep_prefill_t8192_q4k under torchrun, and ep_parity.py for the 2-GPU parity check."""
+ep_prefill_t8192_q4k under torchrun; tests/test_gpu_ep_multi.py runs the 2-GPU parity check."""
 import socket
 from datetime import timedelta
 

@@ -282,6 +282,21 @@ def test_gguf_rejects_malformed_files(tmp_path):
         write_gguf(p, [], [("x", typ, ne, bytes(4096))])
         with pytest.raises(Exception):
             Gguf(p)
+    # sizes from the file that would wrap or run past its end: a u8 array of 2^62 elements (its
+    # byte count must not seek backwards), a string array longer than the file, and a tensor whose
+    # element count overflows 64 bits (its offset + size must not wrap below the file size)
+    import struct
+    hdr = b"GGUF" + struct.pack("<IQQ", 3, 0, 1)
+    arrays = {"huge_u8_array": struct.pack("<IQ", 0, 1 << 62), "huge_str_array": struct.pack("<IQ", 8, 1 << 40)}
+    for name, body in arrays.items():
+        p = str(tmp_path / f"{name}.gguf")
+        open(p, "wb").write(hdr + struct.pack("<Q", 1) + b"a" + struct.pack("<I", 9) + body + bytes(64))
+        assert not lib.moeb_gguf_open(p.encode()), name
+        assert b"array" in lib.moeb_last_error() or b"truncated" in lib.moeb_last_error(), name
+    p = str(tmp_path / "overflow.gguf")
+    write_gguf(p, [], [("x", 0, (1 << 31, 1 << 31, 1 << 31, 8), bytes(64))])   # f32: 2^96 x 8 x 4 bytes
+    assert not lib.moeb_gguf_open(p.encode())
+    assert b"overflow" in lib.moeb_last_error()
     g = Gguf(good)
     assert g.str("gemma4.expert_count") is None          # wrong type asked for
     assert g.u32("general.architecture") is None
@@ -305,3 +320,19 @@ def test_loaders_fail_cleanly(tmp_path):
     assert lib.moeb_load_file_range(b"/nonexistent/file", 0, 10, dst, None) == -1
     assert lib.moeb_load_file_range(None, 0, 10, dst, None) == -1
     st.close()
+    # a corrupt index: a record count the file cannot hold fails the open (nothing is sized from
+    # it), and a page whose offset + size runs past the pack is a bad page, never a huge read
+    raw = bytearray(open(idx, "rb").read())
+    bad = str(tmp_path / "bad.experts.index")
+    import shutil
+    shutil.copy(idx.replace("index", "pack"), bad.replace("index", "pack"))
+    raw_count = bytearray(raw)
+    raw_count[72:80] = (1 << 60).to_bytes(8, "little")                   # record_count
+    open(bad, "wb").write(raw_count)
+    assert lib.moert_store_verify(bad.encode()) == -1
+    assert not lib.moert_store_reader_open(bad.encode(), 0)
+    raw_page = bytearray(raw)
+    hb = int.from_bytes(raw[12:16], "little")                             # header_bytes
+    raw_page[hb + 16:hb + 24] = ((1 << 64) - 8).to_bytes(8, "little")     # record 0: nbytes
+    open(bad, "wb").write(raw_page)
+    assert lib.moert_store_verify(bad.encode()) == 1

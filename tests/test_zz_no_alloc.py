@@ -12,12 +12,11 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import assert_layer_close, host_layer
+from conftest import host_layer
 from llapis_b200 import capi, workload
 from llapis_b200.layer import MoELayer
 
 pytestmark = pytest.mark.gpu
-TOL = 2e-3   # max-abs / RMS, as in the other layer parity tests
 
 
 def _forward_static(layer, x):
@@ -29,6 +28,8 @@ def _forward_static(layer, x):
 
 
 def test_static_scratch_entry_matches_workspace_entry():
+    """Both entries run the same decode kernel on the same 8-token chunks (every reduction in a
+    fixed order), so their outputs must be identical bit for bit."""
     host = host_layer("decode_t4_mixed")
     layer = MoELayer(host)
     cfg = workload.CONFIGS["decode_t4_mixed"]
@@ -38,7 +39,7 @@ def test_static_scratch_entry_matches_workspace_entry():
         got = _forward_static(layer, x)
         want = layer(x)
         torch.cuda.synchronize()
-        assert_layer_close(got.cpu().numpy(), want.cpu().numpy().astype(np.float64), tol=TOL)
+        assert np.array_equal(got.cpu().numpy().view(np.uint32), want.cpu().numpy().view(np.uint32)), f"T={T}"
     assert layer.device_error() == 0
 
 
