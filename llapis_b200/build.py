@@ -22,7 +22,7 @@ LIB = os.path.join(LIBDIR, "libmoeb200.so")
 INCLUDE = os.path.join(ROOT, "include")
 
 SOURCES = ["kernels.cu", "api.cpp", "quant.cpp", "store.cpp", "load.cpp"]
-HEADERS = ["common.cuh", "params.h", "ggml_tables.inc", "prefill.cuh", "mid.cuh"]
+HEADERS = ["common.cuh", "params.h", "ggml_tables.inc", "prefill.cuh", "gateup_lx.cuh", "mid.cuh"]
 PUBLIC_HEADERS = ["moeb200.h", "moert_cuda.h", "moert_store.h"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -96,8 +96,8 @@ size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 int check_pool(const moeb_pool &pl, int d_model, int n_ff, const char *name) {
     if (pl.n <= 0) return MOEB_OK;
-    if (pl.type_gu != MOEB_T_Q4_K && pl.type_gu != MOEB_T_IQ2_S)
-        return fail(MOEB_ETYPE, "%s pool: gate_up type %d unsupported (Q4_K=12, IQ2_S=22)", name, pl.type_gu);
+    if (pl.type_gu != MOEB_T_Q4_K && pl.type_gu != MOEB_T_IQ2_S && pl.type_gu != MOEB_T_IQ2_XXS)
+        return fail(MOEB_ETYPE, "%s pool: gate_up type %d unsupported (Q4_K=12, IQ2_S=22, IQ2_XXS=16)", name, pl.type_gu);
     if (pl.type_down != MOEB_T_Q5_0 && pl.type_down != MOEB_T_IQ4_NL)
         return fail(MOEB_ETYPE, "%s pool: down type %d unsupported (Q5_0=6, IQ4_NL=20)", name, pl.type_down);
     if (!pl.w_gu || !pl.w_down) return fail(MOEB_EINVAL, "%s pool: null weight pointer", name);
@@ -198,7 +198,7 @@ PrefillWs carve_prefill(const moeb_layer *L, int T, uint8_t *base) {
     w.xbs = (int16_t *)take(sizeof(int16_t) * T * nsb * 16);
     const size_t mt = (size_t)w.max_tiles;
     // the tcgen05 path's gate_up images, or the mid-size path's operand images
-    const size_t pf_img = mt * nsb * 2 * kPfGuImageBytes, md_img = md_image_bytes((int)P, (int)E, (int)d, (int)nff);
+    const size_t pf_img = mt * lx_tile_bytes((int)nsb), md_img = md_image_bytes((int)P, (int)E, (int)d, (int)nff);
     w.bimg = (uint8_t *)take(pf_img > md_img ? pf_img : md_img);
     w.dxt = (float *)take(sizeof(float) * mt * nsb * kPrefillTile);
     w.hbuf = (float *)take(sizeof(float) * P * 2 * nff);
@@ -222,10 +222,11 @@ bool use_prefill(const moeb_layer *L, int32_t n_tokens) {
 }
 
 // Prefill-path batches with fewer routed pairs per expert than these run a projection on the
-// mid-size kernels (gate_up, down). Measured: gate_up on the mid-size kernel wins up to ~48 pairs
-// per expert; the down kernel re-streams a tile's weight rows once per 4-block chunk, which loses
-// to the tcgen05 down on skewed routing already at 16 (one stack layer: 178 vs 152 us).
-std::atomic<int32_t> g_mid_max[2] = {{48}, {16}};
+// mid-size kernels (gate_up, down). gate_up: off by default (1) -- the lane-exact tcgen05 kernel
+// reproduces the reference's float order, the mid-size kernel only its integer sums; down: the
+// down kernel re-streams a tile's weight rows once per 4-block chunk, which loses to the tcgen05
+// down on skewed routing already at 16 (one stack layer: 178 vs 152 us).
+std::atomic<int32_t> g_mid_max[2] = {{1}, {16}};
 
 bool use_mid(const moeb_layer *L, int32_t n_rows, int kind) {
     const long long P = (long long)n_rows * L->top_k;
@@ -619,7 +620,7 @@ extern "C" int moeb_dequantize(int32_t type, const void *src, float *dst, int64_
 extern "C" int moeb_quantize_act(int32_t wtype, const float *x, void *dst, int64_t n_rows, int64_t n_per_row,
                                  void *stream) {
     int32_t vdt;
-    if (wtype == MOEB_T_Q4_K || wtype == MOEB_T_IQ2_S) vdt = T_Q8_K;
+    if (wtype == MOEB_T_Q4_K || wtype == MOEB_T_IQ2_S || wtype == MOEB_T_IQ2_XXS) vdt = T_Q8_K;
     else if (wtype == MOEB_T_Q5_0 || wtype == MOEB_T_IQ4_NL) vdt = T_Q8_0;
     else return fail(MOEB_ETYPE, "moeb_quantize_act: weight type %d unsupported", wtype);
     if (!x || !dst || n_rows <= 0 || n_per_row <= 0 || n_per_row % (vdt == T_Q8_K ? QK_K : QK32))

@@ -70,6 +70,17 @@ __device__ __forceinline__ uint32_t ld_u32_a2(const uint8_t *p) {
 
 __device__ __forceinline__ int dp4a(int a, int b, int c) { return __dp4a(a, b, c); }
 
+// 6-bit scale and min of sub-block j of a Q4_K super-block (get_scale_min_k4, ggml-quants.c:822)
+__device__ __forceinline__ void q4k_scale_min(int j, const uint8_t *q, int &sc, int &m) {
+    if (j < 4) {
+        sc = q[j] & 63;
+        m = q[j + 4] & 63;
+    } else {
+        sc = (q[j + 4] & 0xF) | ((q[j - 4] >> 6) << 4);
+        m = (q[j + 4] >> 4) | ((q[j] >> 6) << 4);
+    }
+}
+
 // byte-wise mask 0xff for each set bit of the low 4 bits of s
 __device__ __forceinline__ uint32_t sign_bytes4(uint32_t s) {
     return ((s * 0x00204081u) & 0x01010101u) * 0xffu;

@@ -1,0 +1,637 @@
+// gate_up grouped GEMM of the prefill path, bit-exact with the reference's CPU dots.
+//
+// ggml-cpu's x86 kernels for the gate_up types (ggml_vec_dot_q4_K_q8_K, x86/quants.c:1900;
+// _iq2_s_q8_K :2937; _iq2_xxs_q8_K :2522) fix the float order of every dot: per 256-value
+// super-block, eight integer lanes (lane L sums the products at positions 4L..4L+3 of each 32-value
+// group, the sub-block scale inside the integer), each lane fused-multiply-added into its own f32
+// accumulator with the super-block's scale d = d_x * d_w, and at the end the horizontal sum
+// ((a0 + a4) + (a2 + a6)) + ((a1 + a5) + (a3 + a7)) (hsum_float_8, :43). Q4_K adds a min term of
+// four lanes (mins[2m] * q8s[2m] + mins[2m+1] * q8s[2m+1], q8s the 32-value sub-block sums), fused
+// into its own four accumulators with dmin = -d_x * dmin_w, reduced as (m0 + m2) + (m1 + m3) and
+// added last. A last-bit difference here moves the Q8_0 and fp16-GELU roundings of the down input,
+// so this kernel reproduces that order exactly:
+//
+//   - the tensor cores compute each lane's exact integer sum (kind::f16 with small-integer fp16
+//     operands, fp32 accumulation of integers below 2^24), one accumulator per lane;
+//   - a "pass" runs two lanes over all super-blocks of the row: (0,4), (2,6), (1,5), (3,7), then for
+//     Q4_K the min lanes (0,2), (1,3); the epilogue keeps the two lanes' f32 chains in registers
+//     (fma.rn.f32x2 per column pair) and folds finished passes into two held partial sums in the
+//     reference's reduction order;
+//   - operands: A = the weight rows (M = 128: 64 gate + 64 up rows), converted by four warps (thread
+//     = row = TMEM lane) and stored straight into tensor memory with tcgen05.st (no shared-memory
+//     round trip); B = the pairs' Q8_K values as fp16, in a per-(tile, pass, super-block) image that
+//     pf_gather_lx_kernel lays out in the same lane order, bulk-copied into shared memory by a
+//     producer warp up to four steps ahead; N = up to 64 pairs per work unit.
+//
+// TMEM (512 columns): three accumulator buffers of 2 lanes x 64 columns [0, 384) and four A buffers
+// of 32 columns [384, 512); the two held partial sums live in shared memory.
+#pragma once
+
+namespace moeb {
+
+constexpr int kLxN = 64;                    // pairs per work unit (MMA N <= 64)
+constexpr int kLxMainCores = 8;             // K = 64 per main pass step (2 lanes x 32), in 8-value cores
+constexpr int kLxMinCores = 4;              // K = 32 per min pass step (2 lanes x 16)
+constexpr int kLxBStageBytes = (kLxN / 8) * kLxMainCores * 128;   // 8 KB: one unit's half of a main image
+constexpr int kLxEpiWarps = 16;             // four per TMEM lane quadrant, 16 columns each
+constexpr int kLxEpiCols = kLxN / (kLxEpiWarps / 4);
+constexpr int kLxProdWarp = kPfConvWarps + 1;
+constexpr int kLxEpiWarp0 = kLxProdWarp + 1;
+constexpr int kLxThreads = (kLxEpiWarp0 + kLxEpiWarps) * 32;
+// TMEM: three accumulator buffers of 2 lanes x 64 columns, then four A buffers of 32 columns; the
+// A buffers and the B stages share one ring index (step % kLxRing) and one "operands free" barrier
+constexpr int kLxDBufs = 3, kLxRing = 4;
+constexpr uint32_t kLxColD = 0, kLxColA = 128 * kLxDBufs, kLxTmemCols = 512;
+static_assert(kLxColA + 32 * kLxRing <= kLxTmemCols, "TMEM budget");
+static_assert(kLxImgMain == (kPrefillTile / 8) * kLxMainCores * 128 && kLxImgMin == (kPrefillTile / 8) * kLxMinCores * 128,
+              "image sizes in params.h");
+
+// the two reference lanes of main pass p: (0,4), (2,6), (1,5), (3,7)
+MOEB_HD constexpr int lx_first_lane(int pass) { return pass == 0 ? 0 : pass == 1 ? 2 : pass == 2 ? 1 : 3; }
+template <int PASS>
+__device__ constexpr int lx_lane_c(int second) { return lx_first_lane(PASS) + 4 * second; }
+
+// Q4_K raw row blocks of a step, staged by two 2D tensor-map copies (64 gate rows, 64 up rows) of
+// 144 bytes (one super-block) per row
+constexpr int kLxRawBytes = kPfM * B_Q4_K;
+struct LxMaps {
+    CUtensorMap gu[2];   // [hot, cold] gate_up pools as 2D byte arrays (row bytes x rows); Q4_K pools only
+};
+struct LxSmem {
+    uint8_t b[kLxRing][kLxBStageBytes];
+    uint8_t raw[kLxRing][kLxRawBytes];       // Q4_K units: the step's super-block of the unit's 128 rows
+    float held[2][kLxN][kPfM];               // the two held partial sums of each (row, column), column-major
+    float dxs[kPrefillMaxSb][kLxN];          // Q8_K scale of each unit column, per super-block
+    float2 xdt[kPrefillMaxSb][kPfM];         // (d, -dmin) of each unit row, per super-block
+    uint64_t bfull[kLxRing], afull[kLxRing], opfree[kLxRing], dfull[kLxDBufs], dempty[kLxDBufs], done, epibar;
+    uint32_t tmem;
+    int32_t abort;
+};
+
+// ---------------------------------------------------------------- TMEM stores / loads of 32-bit columns
+#define MOEB_R32(a) MOEB_R16(a), "=r"(a[16]), "=r"(a[17]), "=r"(a[18]), "=r"(a[19]), "=r"(a[20]), "=r"(a[21]), \
+    "=r"(a[22]), "=r"(a[23]), "=r"(a[24]), "=r"(a[25]), "=r"(a[26]), "=r"(a[27]), "=r"(a[28]), "=r"(a[29]), "=r"(a[30]), \
+    "=r"(a[31])
+#define MOEB_I16(a) "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(a[4]), "r"(a[5]), "r"(a[6]), "r"(a[7]), "r"(a[8]), \
+    "r"(a[9]), "r"(a[10]), "r"(a[11]), "r"(a[12]), "r"(a[13]), "r"(a[14]), "r"(a[15])
+#define MOEB_I32(a) MOEB_I16(a), "r"(a[16]), "r"(a[17]), "r"(a[18]), "r"(a[19]), "r"(a[20]), "r"(a[21]), "r"(a[22]), \
+    "r"(a[23]), "r"(a[24]), "r"(a[25]), "r"(a[26]), "r"(a[27]), "r"(a[28]), "r"(a[29]), "r"(a[30]), "r"(a[31])
+
+__device__ __forceinline__ void tmem_st16(uint32_t ta, const uint32_t (&v)[16]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+                 ::"r"(ta), MOEB_I16(v) : "memory");
+}
+__device__ __forceinline__ void tmem_st32(uint32_t ta, const uint32_t (&v)[32]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+                 "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};"
+                 ::"r"(ta), MOEB_I32(v) : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_ld32(uint32_t ta, uint32_t (&v)[32]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+                 "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+                 : MOEB_R32(v) : "r"(ta));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" : MOEB_RW16(v), "+r"(v[16]), "+r"(v[17]), "+r"(v[18]), "+r"(v[19]),
+                 "+r"(v[20]), "+r"(v[21]), "+r"(v[22]), "+r"(v[23]), "+r"(v[24]), "+r"(v[25]), "+r"(v[26]), "+r"(v[27]),
+                 "+r"(v[28]), "+r"(v[29]), "+r"(v[30]), "+r"(v[31])::"memory");
+}
+// 16 columns of two accumulators (lane a and lane b of a pass) in one wait
+__device__ __forceinline__ void tmem_ld16x2u(uint32_t ta, uint32_t tb, uint32_t (&a)[16], uint32_t (&b)[16]) {
+    asm volatile(MOEB_LD16 : MOEB_R16(a) : "r"(ta));
+    asm volatile(MOEB_LD16 : MOEB_R16(b) : "r"(tb));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" : MOEB_RW16(a), MOEB_RW16(b)::"memory");
+}
+
+// MMA with the A operand in tensor memory (M = 128 rows in the 128 TMEM lanes, K along the
+// columns, two fp16 values per 32-bit column) and B from shared memory
+__device__ __forceinline__ void umma_f16_ts(uint32_t dtmem, uint32_t atmem, uint64_t b, uint32_t idesc, uint32_t accum) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(dtmem),
+        "r"(atmem), "l"(b), "r"(idesc), "r"(accum)
+        : "memory");
+}
+
+// ---------------------------------------------------------------- packed f32 pairs (IEEE, round to nearest)
+__device__ __forceinline__ uint64_t f2pack(float x, float y) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(x), "f"(y));
+    return r;
+}
+__device__ __forceinline__ float2 f2unpack(uint64_t v) {
+    float2 r;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+    return r;
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+
+// ---------------------------------------------------------------- 2D tensor-map copy (no multicast)
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_addr(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
+        : "memory");
+}
+
+// ---------------------------------------------------------------- A operands (weight rows, one thread per row)
+// Lane L's 32 values of a super-block in K order 4j + e <-> value 32j + 4L + e (j = 32-value
+// group, e < 4): 16 columns of fp16 pairs.
+
+// Q4_K (block: d, dmin, scales[12], qs[128]; byte 32c + b holds value b of sub-block 2c in its low
+// nibble and of sub-block 2c + 1 in its high nibble): A = sc_j * q, exact in fp16
+__device__ __forceinline__ void lx_a_q4k_lane(const uint32_t (&qw)[4], const int (&sc)[8], uint32_t *o) {
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        const __half2 sl = __float2half2_rn((float)sc[2 * c]), nsl = __float2half2_rn(-1024.f * sc[2 * c]);
+        const __half2 sh = __float2half2_rn((float)sc[2 * c + 1]), nsh = __float2half2_rn(-1024.f * sc[2 * c + 1]);
+        scale4(qw[c] & 0x0f0f0f0fu, sl, nsl, o[4 * c], o[4 * c + 1]);
+        scale4((qw[c] >> 4) & 0x0f0f0f0fu, sh, nsh, o[4 * c + 2], o[4 * c + 3]);
+    }
+}
+
+// IQ2_S (block: d, qs[32] grid low bytes, signs[32], qh[8], scales[8]): value 32b + 4L + e is byte
+// 4(L & 1) + e of grid entry g = 4b + L/2 (index qs[g] | 2 bits of qh[b]), sign bit of signs[g],
+// times ls = 2 * (L < 4 ? low : high scale nibble of block b) + 1
+__device__ __forceinline__ void lx_a_iq2s_lane(const uint8_t *blk, int L, uint32_t *o) {
+    const uint8_t *qs = blk + 2, *sg = blk + 34, *qh = blk + 66, *scl = blk + 74;
+#pragma unroll
+    for (int b = 0; b < 8; ++b) {
+        const int g = 4 * b + (L >> 1);
+        const uint32_t idx = (uint32_t)__ldg(qs + g) | ((((uint32_t)__ldg(qh + b) >> (2 * (g & 3))) & 3u) << 8);
+        const uint64_t grid = g_iq2s_grid[idx];
+        const uint32_t mag = (uint32_t)(grid >> (32 * (L & 1)));
+        const uint32_t sv = __ldg(scl + b);
+        const int ls = 2 * (int)(L < 4 ? (sv & 0xfu) : (sv >> 4)) + 1;
+        const __half2 s2 = __float2half2_rn((float)ls), ns2 = __float2half2_rn(-1024.f * ls);
+        uint32_t o0, o1;
+        scale4(mag, s2, ns2, o0, o1);
+        const uint32_t s4 = ((uint32_t)__ldg(sg + g) >> (4 * (L & 1))) & 0xfu;
+        o0 ^= ((s4 & 1u) << 15) | ((s4 & 2u) << 30);
+        o1 ^= ((s4 & 4u) << 13) | ((s4 & 8u) << 28);
+        o[2 * b] = o0;
+        o[2 * b + 1] = o1;
+    }
+}
+
+// IQ2_XXS (block: d, then per 32-block 4 grid indices and a u32 of four 7-bit sign indices + a 4-bit
+// scale): value 32b + 4L + e is byte 4(L & 1) + e of grid entry aux[L/2], the sign from the 7-bit
+// index's pattern, times 2 * ls + 1
+__device__ __forceinline__ void lx_a_iq2xxs_lane(const uint8_t *blk, int L, uint32_t *o) {
+#pragma unroll
+    for (int b = 0; b < 8; ++b) {
+        const uint8_t *g8 = blk + 2 + 8 * b;
+        const uint32_t hi = (uint32_t)__ldg(g8 + 4) | ((uint32_t)__ldg(g8 + 5) << 8) | ((uint32_t)__ldg(g8 + 6) << 16) |
+                            ((uint32_t)__ldg(g8 + 7) << 24);
+        const int l = L >> 1;
+        const uint64_t grid = g_iq2xxs_grid[__ldg(g8 + l)];
+        const uint32_t mag = (uint32_t)(grid >> (32 * (L & 1)));
+        const int ls = 2 * (int)(hi >> 28) + 1;
+        const __half2 s2 = __float2half2_rn((float)ls), ns2 = __float2half2_rn(-1024.f * ls);
+        uint32_t o0, o1;
+        scale4(mag, s2, ns2, o0, o1);
+        const uint32_t s4 = ((uint32_t)g_iq2xxs_signs[(hi >> (7 * l)) & 127u] >> (4 * (L & 1))) & 0xfu;
+        o0 ^= ((s4 & 1u) << 15) | ((s4 & 2u) << 30);
+        o1 ^= ((s4 & 4u) << 13) | ((s4 & 8u) << 28);
+        o[2 * b] = o0;
+        o[2 * b + 1] = o1;
+    }
+}
+
+// ---------------------------------------------------------------- B operand images
+// One CTA per (tile, super-block), thread = (tile row c, half h). Half 0 writes main passes 0, 1
+// (lanes (0,4), (2,6)) and min pass 4 (lanes 0, 2); half 1 writes main passes 2, 3 and min pass 5.
+// A main image row holds lane a's 32 values (cores 0-3) then lane b's (cores 4-7), each in K order
+// 4j + e; a min image row holds [bsums 4m..4m+3, 0 x 12] for its two lanes m (cores 0-1, 2-3).
+// Rows n..N-1 (padding up to a multiple of 16) are zero. Half 0 also writes the row's Q8_K scale.
+template <int PASS>
+__device__ __forceinline__ void lx_b_main_row(const uint4 (&v)[16], uint8_t *img, int c) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const int L = j < 4 ? lx_lane_c<PASS>(0) : lx_lane_c<PASS>(1);
+        const int g0 = 2 * (j & 3);   // 32-value groups g0, g0 + 1 in this core
+        uint32_t w[2];
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+            const int wi = 8 * (g0 + q) + L;   // word index of values 32(g0+q) + 4L .. + 3
+            const uint4 &u = v[wi >> 2];
+            w[q] = (wi & 3) == 0 ? u.x : (wi & 3) == 1 ? u.y : (wi & 3) == 2 ? u.z : u.w;
+        }
+        uint32_t o0, o1, o2, o3;
+        s8x4_h(w[0], o0, o1);
+        s8x4_h(w[1], o2, o3);
+        *reinterpret_cast<uint4 *>(img + canon_off(c, j, kLxMainCores)) = make_uint4(o0, o1, o2, o3);
+    }
+}
+
+__global__ void __launch_bounds__(256) pf_gather_lx_kernel(PfParams p) {
+    pdl_wait();
+    pdl_launch_dependents();
+    const int ti = blockIdx.x, sb = blockIdx.y;
+    if (ti >= *p.n_tiles) return;
+    const PfTile tl = p.tiles[ti];
+    const int N = (tl.n + 15) & ~15, nsb = p.d / QK_K;
+    const int c = threadIdx.x >> 1, h = threadIdx.x & 1;
+    if (c >= N) return;
+    uint8_t *base = p.bimg + (size_t)ti * lx_tile_bytes(nsb);
+    uint8_t *im0 = base + lx_image_off(nsb, 2 * h, sb), *im1 = base + lx_image_off(nsb, 2 * h + 1, sb);
+    uint8_t *imm = base + lx_image_off(nsb, 4 + h, sb);
+    float *dxt = p.dxt + ((size_t)ti * nsb + sb) * kPfN;
+    const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+    if (c >= tl.n) {
+#pragma unroll
+        for (int j = 0; j < kLxMainCores; ++j) {
+            *reinterpret_cast<uint4 *>(im0 + canon_off(c, j, kLxMainCores)) = z;
+            *reinterpret_cast<uint4 *>(im1 + canon_off(c, j, kLxMainCores)) = z;
+        }
+#pragma unroll
+        for (int j = 0; j < kLxMinCores; ++j) *reinterpret_cast<uint4 *>(imm + canon_off(c, j, kLxMinCores)) = z;
+        if (h == 0) dxt[c] = 0.f;
+        return;
+    }
+    const int t = p.perm[tl.slot0 + c] / p.k;
+    const int8_t *q8 = p.xq8 + (size_t)t * p.d + sb * QK_K;
+    uint4 v[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __ldg(reinterpret_cast<const uint4 *>(q8 + 16 * i));
+    if (h == 0) {
+        lx_b_main_row<0>(v, im0, c);
+        lx_b_main_row<1>(v, im1, c);
+        dxt[c] = p.xd[(size_t)t * nsb + sb];
+    } else {
+        lx_b_main_row<2>(v, im0, c);
+        lx_b_main_row<3>(v, im1, c);
+    }
+    // min pass 4 + h: lanes m = h and m = h + 2, each [bsums 4m .. 4m + 3, 0 x 12] (exact in fp16:
+    // |bsum| <= 16 x 127)
+    const int16_t *bs16 = p.xbs + ((size_t)t * nsb + sb) * 16;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const int m = h + 2 * i;
+        const uint2 b = __ldg(reinterpret_cast<const uint2 *>(bs16 + 4 * m));
+        const uint32_t w0 = pack_h2i((int)(int16_t)(b.x & 0xffffu), (int)(int16_t)(b.x >> 16));
+        const uint32_t w1 = pack_h2i((int)(int16_t)(b.y & 0xffffu), (int)(int16_t)(b.y >> 16));
+        *reinterpret_cast<uint4 *>(imm + canon_off(c, 2 * i, kLxMinCores)) = make_uint4(w0, w1, 0u, 0u);
+        *reinterpret_cast<uint4 *>(imm + canon_off(c, 2 * i + 1, kLxMinCores)) = z;
+    }
+}
+
+// ---------------------------------------------------------------- the grouped GEMM
+// Work unit (tile, mb, nh): 64 gate rows [64 mb, 64 mb + 64) and the matching 64 up rows against
+// pairs [64 nh, 64 nh + 64) of an expert tile (units of an empty half are skipped by every role
+// alike). Persistent: CTA b takes units b, b + grid, ...; a step is (unit, pass, super-block), and
+// every role walks the same step sequence with an LxIter.
+__device__ __forceinline__ bool lx_unit(const PfParams &p, int u, int n_mb, int &ti, int &mb, int &nh, PfTile &tl) {
+    ti = u / (2 * n_mb);
+    const int rem = u - ti * 2 * n_mb;
+    mb = rem >> 1;
+    nh = rem & 1;
+    tl = p.tiles[ti];
+    return 64 * nh < tl.n;
+}
+__device__ __forceinline__ int lx_passes(int type) { return type == T_Q4_K ? 6 : 4; }
+
+struct LxIter {
+    int u, ti, mb, nh, pass, sb, np, nc, N, type;
+    PfTile tl;
+    const uint8_t *arow;   // this thread's weight row of the unit (rows 0..63 gate, 64..127 the matching up rows)
+    bool ok;
+    // from u (inclusive): the first unit with pairs in it; r: this thread's row (< 0: no row)
+    __device__ __forceinline__ void seek(const PfParams &p, int units, int n_mb, int r) {
+        for (; u < units; u += gridDim.x)
+            if (lx_unit(p, u, n_mb, ti, mb, nh, tl)) break;
+        ok = u < units;
+        if (ok) {
+            // field by field, not p.gu[tl.cls]: a runtime index into the parameter block copies it to
+            // local memory
+            const bool c1 = tl.cls != 0;
+            PoolView pv;
+            pv.w = c1 ? p.gu[1].w : p.gu[0].w;
+            pv.type = c1 ? p.gu[1].type : p.gu[0].type;
+            pv.ptrs = c1 ? p.gu[1].ptrs : p.gu[0].ptrs;
+            type = pv.type;
+            np = lx_passes(type);
+            nc = min(kLxN, tl.n - 64 * nh);
+            N = (nc + 15) & ~15;
+            pass = 0;
+            sb = 0;
+            if (r >= 0) {
+                const int wr = r < 64 ? 64 * mb + r : p.nff + 64 * mb + (r - 64);
+                arow = tile_rows(pv, tl.widx, 2 * p.nff, p.d) + (size_t)wr * row_bytes(type, p.d);
+            }
+        }
+    }
+    __device__ __forceinline__ void start(const PfParams &p, int units, int n_mb, int r) {
+        u = blockIdx.x;
+        seek(p, units, n_mb, r);
+    }
+    __device__ __forceinline__ void advance(const PfParams &p, int units, int n_mb, int nsb, int r) {
+        if (++sb < nsb) return;
+        sb = 0;
+        if (++pass < np) return;
+        u += gridDim.x;
+        seek(p, units, n_mb, r);
+    }
+};
+
+__global__ void __launch_bounds__(kLxThreads, 1) pf_gate_up_lx_kernel(PfParams p, const __grid_constant__ LxMaps maps) {
+    extern __shared__ __align__(1024) uint8_t pf_smem[];
+    LxSmem &S = *reinterpret_cast<LxSmem *>(pf_smem);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (tid == 0) {
+        for (int i = 0; i < kLxRing; ++i) {
+            mbar_init(&S.bfull[i], 1);
+            mbar_init(&S.afull[i], kPfConvWarps);
+            mbar_init(&S.opfree[i], 1);
+        }
+        for (int b = 0; b < kLxDBufs; ++b) {
+            mbar_init(&S.dfull[b], 1);
+            mbar_init(&S.dempty[b], kLxEpiWarps);
+        }
+        mbar_init(&S.done, 1);
+        mbar_init(&S.epibar, kLxEpiWarps);
+        S.abort = 0;
+        fence_mbar_init();
+    }
+    if (warp == kPfMmaWarp) tmem_alloc_warp(&S.tmem, kLxTmemCols);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = S.tmem;
+    volatile int32_t *abort = &S.abort;
+    pdl_wait();
+    const int nsb = p.d / QK_K, n_mb = p.nff / 64, gu_rows = 2 * p.nff;
+    const int units = *p.n_tiles * n_mb * 2;
+
+    if (warp < kPfConvWarps) {
+        // ------------------------------------------------ converters: thread r = weight row r = TMEM lane r
+        const int r = tid;
+        const uint32_t ta = tmem + ((uint32_t)(32 * warp) << 16) + kLxColA;
+        LxIter cur;
+        cur.start(p, units, n_mb, r);
+        for (int it = 0; cur.ok && !warp_aborted(abort); ++it) {
+            const int ab = it % kLxRing;
+            if (tid == 0) PTRACE(0, 0, it, 0);
+            if (it >= kLxRing && !pf_wait_warp(&S.opfree[ab], ((it / kLxRing) - 1) & 1, abort)) break;
+            if (tid == 0) PTRACE(0, 0, it, 1);
+            tc_fence_after();
+            const bool mn = cur.pass >= 4;
+            uint32_t o[32];
+            if (cur.type == T_Q4_K) {
+                // the step's raw blocks (and B image) have landed in ring slot ab
+                if (!pf_wait_warp(&S.bfull[ab], (it / kLxRing) & 1, abort)) break;
+                const uint32_t *w = reinterpret_cast<const uint32_t *>(S.raw[ab] + r * B_Q4_K);
+                uint8_t sc12[12];
+                *reinterpret_cast<uint32_t *>(sc12 + 0) = w[1];
+                *reinterpret_cast<uint32_t *>(sc12 + 4) = w[2];
+                *reinterpret_cast<uint32_t *>(sc12 + 8) = w[3];
+                int sc[8], mn8[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) q4k_scale_min(j, sc12, sc[j], mn8[j]);
+                if (!mn) {
+#pragma unroll
+                    for (int li = 0; li < 2; ++li) {
+                        const int L = lx_first_lane(cur.pass) + 4 * li;   // qs word of chunk c: 4 + 8c + L
+                        const uint32_t qw[4] = {w[4 + L], w[12 + L], w[20 + L], w[28 + L]};
+                        lx_a_q4k_lane(qw, sc, o + 16 * li);
+                    }
+                } else {
+                    // min lanes m = pass - 4 and m + 2: [mins[2m] x 2, mins[2m+1] x 2, 0 x 12]
+#pragma unroll
+                    for (int li = 0; li < 2; ++li) {
+                        const int m = (cur.pass - 4) + 2 * li;
+                        o[8 * li] = pack_h2i(mn8[2 * m], mn8[2 * m]);
+                        o[8 * li + 1] = pack_h2i(mn8[2 * m + 1], mn8[2 * m + 1]);
+#pragma unroll
+                        for (int i = 2; i < 8; ++i) o[8 * li + i] = 0u;
+                    }
+                }
+            } else if (cur.type == T_IQ2_S) {
+                const uint8_t *blk = cur.arow + (size_t)cur.sb * B_IQ2_S;
+                lx_a_iq2s_lane(blk, lx_first_lane(cur.pass), o);
+                lx_a_iq2s_lane(blk, lx_first_lane(cur.pass) + 4, o + 16);
+            } else {
+                const uint8_t *blk = cur.arow + (size_t)cur.sb * B_IQ2_XXS;
+                lx_a_iq2xxs_lane(blk, lx_first_lane(cur.pass), o);
+                lx_a_iq2xxs_lane(blk, lx_first_lane(cur.pass) + 4, o + 16);
+            }
+            if (mn) {
+                uint32_t o16[16];
+#pragma unroll
+                for (int i = 0; i < 16; ++i) o16[i] = o[i];
+                tmem_st16(ta + 32 * ab, o16);
+            } else {
+                tmem_st32(ta + 32 * ab, o);
+            }
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&S.afull[ab]);
+            if (tid == 0) PTRACE(0, 0, it, 2);
+            cur.advance(p, units, n_mb, nsb, r);
+        }
+    } else if (warp == kPfMmaWarp) {
+        // ------------------------------------------------ MMA issue (one thread)
+        if (lane == 0) {
+            LxIter s;
+            s.start(p, units, n_mb, -1);
+            for (int it = 0; s.ok && !*abort; ++it) {
+                const int ab = it % kLxRing, db = it % kLxDBufs;
+                PTRACE(0, 1, it, 0);
+                if (!pf_wait(&S.afull[ab], (it / kLxRing) & 1, abort) || !pf_wait(&S.bfull[ab], (it / kLxRing) & 1, abort) ||
+                    (it >= kLxDBufs && !pf_wait(&S.dempty[db], ((it / kLxDBufs) - 1) & 1, abort)))
+                    break;
+                PTRACE(0, 1, it, 1);
+                tc_fence_after();
+                const uint32_t idesc = umma_idesc_f16(kPfM, s.N);
+                const uint32_t a0 = tmem + kLxColA + 32 * ab, d0 = tmem + kLxColD + 128 * db;
+                const uint32_t b0 = smem_addr(S.b[ab]);
+                if (s.pass < 4) {   // lane a: K = 32 into d0, lane b: K = 32 into d0 + 64
+                    const uint32_t sbo = kLxMainCores * 128;
+                    umma_f16_ts(d0, a0, umma_sdesc(b0, 128, sbo), idesc, 0);
+                    umma_f16_ts(d0, a0 + 8, umma_sdesc(b0 + 256, 128, sbo), idesc, 1);
+                    umma_f16_ts(d0 + 64, a0 + 16, umma_sdesc(b0 + 512, 128, sbo), idesc, 0);
+                    umma_f16_ts(d0 + 64, a0 + 24, umma_sdesc(b0 + 768, 128, sbo), idesc, 1);
+                } else {            // the two min lanes, K = 16 each
+                    const uint32_t sbo = kLxMinCores * 128;
+                    umma_f16_ts(d0, a0, umma_sdesc(b0, 128, sbo), idesc, 0);
+                    umma_f16_ts(d0 + 64, a0 + 8, umma_sdesc(b0 + 256, 128, sbo), idesc, 0);
+                }
+                umma_commit(&S.opfree[ab]);
+                umma_commit(&S.dfull[db]);
+                PTRACE(0, 1, it, 2);
+                s.advance(p, units, n_mb, nsb, -1);
+            }
+            umma_commit(&S.done);
+            mbar_wait(&S.done, 0);   // issued MMAs always complete; TMEM is freed only after them
+        }
+        __syncwarp();
+    } else if (warp == kLxProdWarp) {
+        // ------------------------------------------------ B operand images, bulk-copied up to kLxRing steps ahead
+        if (lane == 0) {
+            LxIter s;
+            s.start(p, units, n_mb, -1);
+            for (int it = 0; s.ok && !*abort; ++it) {
+                const int bs = it % kLxRing;
+                if (it >= kLxRing && !pf_wait(&S.opfree[bs], ((it / kLxRing) - 1) & 1, abort)) break;
+                const int ncores = s.pass >= 4 ? kLxMinCores : kLxMainCores;
+                const uint32_t bytes = (uint32_t)(s.N / 8) * ncores * 128;
+                const bool q4 = s.type == T_Q4_K;
+                mbar_expect_tx(&S.bfull[bs], bytes + (q4 ? (uint32_t)kLxRawBytes : 0u));
+                bulk_g2s(S.b[bs],
+                         p.bimg + (size_t)s.ti * lx_tile_bytes(nsb) + lx_image_off(nsb, s.pass, s.sb) +
+                             (size_t)(8 * s.nh) * ncores * 128,
+                         bytes, &S.bfull[bs]);
+                if (q4) {   // rows [64 mb, +64) and [n_ff + 64 mb, +64) of the entry, bytes [144 sb, +144)
+                    const CUtensorMap *map = s.tl.cls ? &maps.gu[1] : &maps.gu[0];
+                    const int y0 = s.tl.widx * gu_rows + 64 * s.mb;
+                    tma_load_2d(S.raw[bs], map, s.sb * B_Q4_K, y0, &S.bfull[bs]);
+                    tma_load_2d(S.raw[bs] + 64 * B_Q4_K, map, s.sb * B_Q4_K, y0 + p.nff, &S.bfull[bs]);
+                }
+                s.advance(p, units, n_mb, nsb, -1);
+            }
+        }
+        __syncwarp();
+    } else {
+        // ------------------------------------------------ epilogue: the lanes' f32 chains
+        const int ew = warp - kLxEpiWarp0, et = tid - kLxEpiWarp0 * 32;
+        const int q = warp & 3, ch = ew >> 2;
+        const int r = 32 * q + lane, col0 = kLxEpiCols * ch;
+        const uint32_t tl_lane = tmem + ((uint32_t)(32 * q) << 16);
+        int it = 0;
+        uint32_t eph = 0;
+        LxIter s;
+        s.start(p, units, n_mb, r);
+        while (s.ok && !warp_aborted(abort)) {
+            const int ti = s.ti, nh = s.nh, np = s.np, nc = s.nc, type = s.type;
+            const PfTile tl = s.tl;
+            const uint8_t *arow = s.arow;
+            const int wr = r < 64 ? 64 * s.mb + r : p.nff + 64 * s.mb + (r - 64);
+            for (int i = et; i < nsb * kLxN; i += kLxEpiWarps * 32) {
+                const int sb = i / kLxN, j = i - sb * kLxN;
+                S.dxs[sb][j] = p.dxt[((size_t)ti * nsb + sb) * kPfN + 64 * nh + j];
+            }
+            if (ch == 0) {
+                for (int sb = 0; sb < nsb; ++sb) {
+                    float2 v;
+                    if (type == T_Q4_K) {
+                        const uint32_t hd = __ldg(reinterpret_cast<const uint32_t *>(arow + (size_t)sb * B_Q4_K));
+                        v = make_float2(h2f((uint16_t)(hd & 0xffffu)), -h2f((uint16_t)(hd >> 16)));
+                    } else {
+                        const int bsz = type == T_IQ2_S ? B_IQ2_S : B_IQ2_XXS;
+                        v = make_float2(h2f(__ldg(reinterpret_cast<const uint16_t *>(arow + (size_t)sb * bsz))), 0.f);
+                    }
+                    S.xdt[sb][r] = v;
+                }
+            }
+            if (!epi_barrier(&S.epibar, eph, abort)) break;
+            const bool live = col0 < s.N;   // this warp's columns hold MMA output
+            bool ok = true;
+            for (int pass = 0; pass < np && ok; ++pass) {
+                const bool mn = pass >= 4;
+                uint64_t accA[kLxEpiCols / 2], accB[kLxEpiCols / 2];
+#pragma unroll
+                for (int i = 0; i < kLxEpiCols / 2; ++i) { accA[i] = 0ull; accB[i] = 0ull; }
+                for (int sb = 0; sb < nsb; ++sb, ++it) {
+                    const int db = it % kLxDBufs;
+                    if (et == 0) PTRACE(0, 2, it, 0);
+                    if (!pf_wait_warp(&S.dfull[db], (it / kLxDBufs) & 1, abort)) { ok = false; break; }
+                    if (et == 0) PTRACE(0, 2, it, 1);
+                    tc_fence_after();
+                    if (live) {
+                        const float2 xw = S.xdt[sb][r];
+                        const float xs = mn ? xw.y : xw.x;   // d_w, or -dmin_w for the min lanes
+                        const uint64_t xs2 = f2pack(xs, xs);
+                        const uint32_t dcol = tl_lane + kLxColD + 128 * db + col0;
+                        uint32_t sa[16], sbv[16];
+                        tmem_ld16x2u(dcol, dcol + 64, sa, sbv);
+                        const float4 *yd = reinterpret_cast<const float4 *>(&S.dxs[sb][col0]);
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const float4 y4 = yd[i];
+                            // d = d_x * d_w rounded to f32 (for the min lanes -d_x * dmin_w)
+                            const uint64_t d01 = mul2(f2pack(y4.x, y4.y), xs2), d23 = mul2(f2pack(y4.z, y4.w), xs2);
+                            accA[2 * i] = fma2(d01, f2pack(__uint_as_float(sa[4 * i]), __uint_as_float(sa[4 * i + 1])), accA[2 * i]);
+                            accB[2 * i] = fma2(d01, f2pack(__uint_as_float(sbv[4 * i]), __uint_as_float(sbv[4 * i + 1])), accB[2 * i]);
+                            accA[2 * i + 1] = fma2(d23, f2pack(__uint_as_float(sa[4 * i + 2]), __uint_as_float(sa[4 * i + 3])),
+                                                   accA[2 * i + 1]);
+                            accB[2 * i + 1] = fma2(d23, f2pack(__uint_as_float(sbv[4 * i + 2]), __uint_as_float(sbv[4 * i + 3])),
+                                                   accB[2 * i + 1]);
+                        }
+                    }
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&S.dempty[db]);
+                    if (et == 0) PTRACE(0, 2, it, 2);
+                }
+                if (!ok || !live) continue;
+                // fold the finished pass in the reference's reduction order:
+                //   pass 0 (0,4): Ha = a0;  1 (2,6): Ha = a0 + a2 = c0;  2 (1,5): Hb = a1;
+                //   3 (3,7): Ha = c0 + (a1 + a3);  4 (m0,m2): Hb = m0 + m2;  5 (m1,m3): h = Ha + (Hb + (m1 + m3))
+                float t[kLxEpiCols];
+#pragma unroll
+                for (int i = 0; i < kLxEpiCols / 2; ++i) {
+                    const float2 v = f2unpack(add2(accA[i], accB[i]));
+                    t[2 * i] = v.x;
+                    t[2 * i + 1] = v.y;
+                }
+                float(*ha)[kPfM] = S.held[0] + col0;
+                float(*hb)[kPfM] = S.held[1] + col0;
+                if (pass == 0 || pass == 2 || pass == 4) {
+#pragma unroll
+                    for (int i = 0; i < kLxEpiCols; ++i) (pass == 0 ? ha : hb)[i][r] = t[i];
+                    continue;
+                }
+#pragma unroll
+                for (int i = 0; i < kLxEpiCols; ++i) t[i] = __fadd_rn((pass == 1 ? ha : hb)[i][r], t[i]);
+                if (pass == 1) {
+#pragma unroll
+                    for (int i = 0; i < kLxEpiCols; ++i) ha[i][r] = t[i];
+                    continue;
+                }
+                // pass 3: Ha = c0, t = c1;  pass 5: Ha = the lanes' sum, t = M
+#pragma unroll
+                for (int i = 0; i < kLxEpiCols; ++i) t[i] = __fadd_rn(ha[i][r], t[i]);
+                if (pass == 3 && np == 6) {
+#pragma unroll
+                    for (int i = 0; i < kLxEpiCols; ++i) ha[i][r] = t[i];
+                    continue;
+                }
+                if (pass == 3) {   // IQ2_S, IQ2_XXS: the sum times 1/8
+#pragma unroll
+                    for (int i = 0; i < kLxEpiCols; ++i) t[i] = __fmul_rn(0.125f, t[i]);
+                }
+                // the unit's rows for this warp's pairs, f32, slot order ([slot][2 n_ff])
+                float *hbp = p.hbuf + (size_t)(tl.slot0 + 64 * nh + col0) * gu_rows + wr;
+#pragma unroll
+                for (int i = 0; i < kLxEpiCols; ++i)
+                    if (col0 + i < nc) hbp[(size_t)i * gu_rows] = t[i];
+            }
+            if (!ok || !epi_barrier(&S.epibar, eph, abort)) break;
+            s.u += gridDim.x;
+            s.seek(p, units, n_mb, r);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == kPfMmaWarp) {
+        tc_fence_after();
+        tmem_dealloc_warp(tmem, kLxTmemCols);
+    }
+}
+
+}  // namespace moeb

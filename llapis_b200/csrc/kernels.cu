@@ -9,9 +9,12 @@
 //   gemv_kernel         : one projection of the moert per-kind ABI (moert_ffn_moe): the same
 //                         grouped GEMV with routes given by the caller.
 //   route_only / dequant / quant_act kernels : the inspection entry points of moeb200.h.
+#include <cuda.h>
+
 #include "common.cuh"
 
 #include <algorithm>
+#include <cstring>
 #include <atomic>
 #include <mutex>
 
@@ -254,7 +257,6 @@ __device__ __forceinline__ void lds_words_a2(const uint8_t *p, uint32_t (&w)[N])
     for (int i = 0; i < N; ++i) w[i] = __funnelshift_r(raw[i], raw[i + 1], sh);
 }
 
-__device__ __forceinline__ uint32_t byte_of(uint32_t w, int i) { return (w >> (8 * i)) & 0xffu; }
 
 // per-token activation rows in shared memory (pointers hoisted out of the block loops)
 struct ActQ8K {           // Q8_K row split as qs[nsb][256] | d[nsb] f32 | bsums[nsb][16] i16
@@ -268,94 +270,117 @@ struct ActQ80 {           // Q8_0 row split as qs[nb][32] | d[nb] f32 | qsum[nb]
     const int *qsum;
 };
 
-// ------------------------------------------------------------------ per-format row dot products
-// Each lane accumulates its share of a row's dot products with NT activation columns; the lanes
-// sharing a row are summed by the caller. Integer work per block equals ggml-cpu's vec_dot kernels
-// (ggml-cpu/quants.c:314, :645, :947, :1203); only the float summation order differs.
+// ------------------------------------------------------------------ gate_up row dot products
+// Eight threads share a row; thread L computes the reference's lane L of the x86 kernels
+// (ggml_vec_dot_q4_K_q8_K, x86/quants.c:1900; _iq2_s_q8_K :2937; _iq2_xxs_q8_K :2522): the integer
+// sum of the products at positions 4L..4L+3 of each 32-value group of a super-block (one dp4a per
+// group, the group's scale inside the integer), fused-multiply-added into its own f32 chain with
+// the super-block's d_x * d_w. gu_rows then adds the eight chains in the reference's order. Q4_K's
+// min term: thread L also runs min lane m = L & 3, mins[2m] * q8s[2m] + mins[2m+1] * q8s[2m+1]
+// (q8s = the 32-value sub-block sums), in a chain scaled by -d_x * dmin_w.
 
-// IQ2_S x Q8_K, lane = 32-value sub-block j of every super-block (8 lanes per row):
-// sum over the 4 groups of 8 of (signed codebook magnitude * q8), scaled ls0 / ls1 = 1 + 2*nibble,
-// times d_w * d_x per super-block; the caller multiplies the total by 0.125.
+// Q4_K (rows 16-byte aligned): byte 32c + b of qs holds value b of sub-block 2c (low nibble) and of
+// sub-block 2c + 1 (high nibble), so lane L's values of chunk c are the nibbles of one word
 template <int NT>
-__device__ __forceinline__ void iq2s_lane(const uint8_t *row, int nsb, int j, const uint64_t *grid,
-                                          const ActQ8K (&x)[NT], float (&acc)[NT]) {
-#pragma unroll 1
-    for (int sb = 0; sb < nsb; ++sb) {
-        const uint8_t *blk = row + sb * B_IQ2_S;
-        const float dw = h2f(*reinterpret_cast<const uint16_t *>(blk));
-        uint32_t qs4[1], sg4[1];
-        lds_words_a2<1>(blk + 2 + 4 * j, qs4);
-        lds_words_a2<1>(blk + 34 + 4 * j, sg4);
-        const uint32_t qh = blk[66 + j], sc = blk[74 + j];
-        int wv[8];
-#pragma unroll
-        for (int l = 0; l < 4; ++l) {
-            const uint32_t gi = byte_of(qs4[0], l) | (((qh >> (2 * l)) & 3u) << 8);
-            const uint64_t g = grid[gi];
-            const uint32_t s = byte_of(sg4[0], l);
-            const uint32_t c0 = ((s & 15u) * 0x00204081u) & 0x01010101u;
-            const uint32_t c1 = ((s >> 4) * 0x00204081u) & 0x01010101u;
-            // negate flagged bytes: (w ^ 0xff) + 1 == -w; magnitudes are >= 8, so nothing carries
-            wv[2 * l] = (int)(((uint32_t)g ^ (c0 * 0xffu)) + c0);
-            wv[2 * l + 1] = (int)(((uint32_t)(g >> 32) ^ (c1 * 0xffu)) + c1);
-        }
-        const int ls0 = 1 + 2 * (int)(sc & 15u), ls1 = 1 + 2 * (int)(sc >> 4);
-#pragma unroll
-        for (int t = 0; t < NT; ++t) {
-            const int4 *q = reinterpret_cast<const int4 *>(x[t].qs + sb * 256 + 32 * j);
-            const int4 qa = q[0], qb = q[1];
-            int s0 = dp4a(wv[0], qa.x, 0);
-            s0 = dp4a(wv[1], qa.y, s0);
-            s0 = dp4a(wv[2], qa.z, s0);
-            s0 = dp4a(wv[3], qa.w, s0);
-            int s1 = dp4a(wv[4], qb.x, 0);
-            s1 = dp4a(wv[5], qb.y, s1);
-            s1 = dp4a(wv[6], qb.z, s1);
-            s1 = dp4a(wv[7], qb.w, s1);
-            acc[t] = fmaf(dw * x[t].d[sb], (float)(ls0 * s0 + ls1 * s1), acc[t]);
-        }
-    }
-}
-
-// Q4_K x Q8_K, lane = sub-block j (8 lanes per row): s_j * sum(q4 * q8) and m_j * (bsum pair),
-// combined as (d_w d_x) main - (dmin_w d_x) min per super-block. Q4_K rows are 16-byte aligned.
-template <int NT>
-__device__ __forceinline__ void q4k_lane(const uint8_t *row, int nsb, int j, const ActQ8K (&x)[NT],
-                                         float (&acc)[NT]) {
-    const int jj = 8 * (j & 3), hi = j >> 2, sh = 4 * (j & 1), qoff = 16 + 32 * (j >> 1);
+__device__ __forceinline__ void q4k_lane(const uint8_t *row, int nsb, int L, const ActQ8K (&x)[NT], float (&acc)[NT],
+                                         float (&macc)[NT]) {
+    const int m = L & 3;
+    const uint32_t M = 0x0f0f0f0fu;
 #pragma unroll 1
     for (int sb = 0; sb < nsb; ++sb) {
         const uint8_t *blk = row + sb * B_Q4_K;
         const uint4 hdr = *reinterpret_cast<const uint4 *>(blk);   // d, dmin | scales[12]
         const float dw = h2f((uint16_t)(hdr.x & 0xffffu)), dmin = h2f((uint16_t)(hdr.x >> 16));
-        // 6-bit scale and min of sub-block j (get_scale_min_k4, ggml-quants.c:822)
-        const int s = hi ? (int)(((hdr.w >> jj) & 0xfu) | (((hdr.y >> (jj + 6)) & 3u) << 4)) : (int)((hdr.y >> jj) & 63u);
-        const int m = hi ? (int)(((hdr.w >> (jj + 4)) & 0xfu) | (((hdr.z >> (jj + 6)) & 3u) << 4))
-                         : (int)((hdr.z >> jj) & 63u);
-        const int4 *qp = reinterpret_cast<const int4 *>(blk + qoff);
-        const int4 qa = qp[0], qb = qp[1];
-        int wv[8];
-        wv[0] = (qa.x >> sh) & 0x0f0f0f0f; wv[1] = (qa.y >> sh) & 0x0f0f0f0f;
-        wv[2] = (qa.z >> sh) & 0x0f0f0f0f; wv[3] = (qa.w >> sh) & 0x0f0f0f0f;
-        wv[4] = (qb.x >> sh) & 0x0f0f0f0f; wv[5] = (qb.y >> sh) & 0x0f0f0f0f;
-        wv[6] = (qb.z >> sh) & 0x0f0f0f0f; wv[7] = (qb.w >> sh) & 0x0f0f0f0f;
+        uint8_t sc12[12];
+        *reinterpret_cast<uint32_t *>(sc12) = hdr.y;
+        *reinterpret_cast<uint32_t *>(sc12 + 4) = hdr.z;
+        *reinterpret_cast<uint32_t *>(sc12 + 8) = hdr.w;
+        int sc[8], mn[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) q4k_scale_min(j, sc12, sc[j], mn[j]);
+        uint32_t qw[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) qw[c] = *reinterpret_cast<const uint32_t *>(blk + 16 + 32 * c + 4 * L);
 #pragma unroll
         for (int t = 0; t < NT; ++t) {
-            const int4 *q = reinterpret_cast<const int4 *>(x[t].qs + sb * 256 + 32 * j);
-            const int4 xa = q[0], xb = q[1];
-            int d = dp4a(wv[0], xa.x, 0);
-            d = dp4a(wv[1], xa.y, d);
-            d = dp4a(wv[2], xa.z, d);
-            d = dp4a(wv[3], xa.w, d);
-            d = dp4a(wv[4], xb.x, d);
-            d = dp4a(wv[5], xb.y, d);
-            d = dp4a(wv[6], xb.z, d);
-            d = dp4a(wv[7], xb.w, d);
-            const uint32_t bp = *reinterpret_cast<const uint32_t *>(x[t].bs + sb * 16 + 2 * j);
-            const int bsum = (int)(int16_t)(bp & 0xffffu) + (int)(int16_t)(bp >> 16);
-            const float dx = x[t].d[sb];
-            acc[t] = fmaf(dw * dx, (float)(s * d), acc[t]);
-            acc[t] = fmaf(-(dmin * dx), (float)(m * bsum), acc[t]);
+            const int *q8 = reinterpret_cast<const int *>(x[t].qs + sb * 256);
+            int sum = 0;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                sum += sc[2 * c] * dp4a((int)(qw[c] & M), q8[16 * c + L], 0);
+                sum += sc[2 * c + 1] * dp4a((int)((qw[c] >> 4) & M), q8[16 * c + 8 + L], 0);
+            }
+            const float yd = x[t].d[sb];
+            acc[t] = fmaf(__fmul_rn(yd, dw), (float)sum, acc[t]);
+            const int16_t *bs = x[t].bs + sb * 16 + 4 * m;
+            const int msum = mn[2 * m] * ((int)bs[0] + (int)bs[1]) + mn[2 * m + 1] * ((int)bs[2] + (int)bs[3]);
+            macc[t] = fmaf(-__fmul_rn(yd, dmin), (float)msum, macc[t]);
+        }
+    }
+}
+
+// IQ2_S (82-byte blocks, 2-byte aligned): value 32b + 4L + e is byte 4(L & 1) + e of grid entry
+// g = 4b + L/2, negated where bit 4(L & 1) + e of signs[g] is set, times 2 * (L < 4 ? low : high
+// scale nibble of block b) + 1; the caller scales the total by 1/8
+template <int NT>
+__device__ __forceinline__ void iq2s_lane(const uint8_t *row, int nsb, int L, const uint64_t *grid,
+                                          const ActQ8K (&x)[NT], float (&acc)[NT]) {
+#pragma unroll 1
+    for (int sb = 0; sb < nsb; ++sb) {
+        const uint8_t *blk = row + sb * B_IQ2_S;
+        const float dw = h2f(*reinterpret_cast<const uint16_t *>(blk));
+        int wv[8], ls[8];
+#pragma unroll
+        for (int b = 0; b < 8; ++b) {
+            const int g = 4 * b + (L >> 1);
+            const uint32_t gi = (uint32_t)blk[2 + g] | ((((uint32_t)blk[66 + b] >> (2 * (g & 3))) & 3u) << 8);
+            const uint32_t mag = (uint32_t)(grid[gi] >> (32 * (L & 1)));
+            const uint32_t c = ((((uint32_t)blk[34 + g] >> (4 * (L & 1))) & 15u) * 0x00204081u) & 0x01010101u;
+            // negate flagged bytes: (w ^ 0xff) + 1 == -w; magnitudes are >= 8, so nothing carries
+            wv[b] = (int)((mag ^ (c * 0xffu)) + c);
+            const uint32_t sv = blk[74 + b];
+            ls[b] = 2 * (int)(L < 4 ? (sv & 15u) : (sv >> 4)) + 1;
+        }
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+            const int *q8 = reinterpret_cast<const int *>(x[t].qs + sb * 256);
+            int sum = 0;
+#pragma unroll
+            for (int b = 0; b < 8; ++b) sum += ls[b] * dp4a(wv[b], q8[8 * b + L], 0);
+            acc[t] = fmaf(__fmul_rn(dw, x[t].d[sb]), (float)sum, acc[t]);
+        }
+    }
+}
+
+// IQ2_XXS (66-byte blocks, 2-byte aligned): per 32-block b, 4 grid indices then a word of four 7-bit
+// sign-pattern indices and a 4-bit scale; value 32b + 4L + e is byte 4(L & 1) + e of grid entry
+// aux[L/2], signed by that pattern, times 2 * ls + 1; the caller scales the total by 1/8
+template <int NT>
+__device__ __forceinline__ void iq2xxs_lane(const uint8_t *row, int nsb, int L, const ActQ8K (&x)[NT], float (&acc)[NT]) {
+    const int l = L >> 1;
+#pragma unroll 1
+    for (int sb = 0; sb < nsb; ++sb) {
+        const uint8_t *blk = row + sb * B_IQ2_XXS;
+        const float dw = h2f(*reinterpret_cast<const uint16_t *>(blk));
+        int wv[8], ls[8];
+#pragma unroll
+        for (int b = 0; b < 8; ++b) {
+            const uint8_t *g8 = blk + 2 + 8 * b;
+            const uint32_t hi = (uint32_t)*reinterpret_cast<const uint16_t *>(g8 + 4) |
+                                ((uint32_t)*reinterpret_cast<const uint16_t *>(g8 + 6) << 16);
+            const uint32_t mag = (uint32_t)(g_iq2xxs_grid[g8[l]] >> (32 * (L & 1)));
+            const uint32_t c = ((((uint32_t)g_iq2xxs_signs[(hi >> (7 * l)) & 127u] >> (4 * (L & 1))) & 15u) * 0x00204081u) &
+                               0x01010101u;
+            wv[b] = (int)((mag ^ (c * 0xffu)) + c);
+            ls[b] = 2 * (int)(hi >> 28) + 1;
+        }
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+            const int *q8 = reinterpret_cast<const int *>(x[t].qs + sb * 256);
+            int sum = 0;
+#pragma unroll
+            for (int b = 0; b < 8; ++b) sum += ls[b] * dp4a(wv[b], q8[8 * b + L], 0);
+            acc[t] = fmaf(__fmul_rn(dw, x[t].d[sb]), (float)sum, acc[t]);
         }
     }
 }
@@ -366,9 +391,6 @@ __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &d0, uint32_t &d
                  : "=r"(d0), "=r"(d1), "=r"(d2), "=r"(d3)
                  : "r"(addr)
                  : "memory");
-}
-__device__ __forceinline__ void ldsm_x2(uint32_t addr, uint32_t &d0, uint32_t &d1) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];" : "=r"(d0), "=r"(d1) : "r"(addr) : "memory");
 }
 // D = A (16x32 s8, row) * B (32x8 s8, col), exact int32
 __device__ __forceinline__ void mma_s8_k32(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
@@ -387,80 +409,6 @@ __device__ __forceinline__ void mma_s8_k16(int (&d)[4], uint32_t a0, uint32_t a1
 __device__ __forceinline__ int sbyte(uint32_t w, int i) { return (int)((w >> (8 * i)) & 0xffu); }
 __device__ __forceinline__ uint32_t pack_s8x4(int a, int b, int c, int d) {
     return (uint32_t)(a & 0xff) | ((uint32_t)(b & 0xff) << 8) | ((uint32_t)(c & 0xff) << 16) | ((uint32_t)(d & 0xff) << 24);
-}
-
-// One 16-row x (up to 8) column tile of a Q4_K gate_up stage against the Q8_K activation rows of
-// its pairs, over super-blocks sb0, sb0 + 4, ... (the four warps of a group split a stage's
-// super-blocks). Integer work of ggml_vec_dot_q4_K_q8_K (x86/quants.c:1900) on warp-level int8
-// MMAs: per sub-block j an m16n8k32 gives sum_i q_i * q8_i exactly, scaled by the 6-bit sc_j in
-// int32; the min term sum_j m_j * bsum_j runs as two m16n8k16 (bsum = 64 hi + lo); d_w * d_x and
-// dmin_w * d_x per super-block in f32. Lane (g, c) owns rows g, g + 8 and columns 2c, 2c + 1.
-// stage/_s: the stage's rows (generic / shared address); tok_*: the activation rows of columns
-// lane & 7, g, 2c and 2c + 1.
-__device__ __forceinline__ void q4k_tile_mma(const uint8_t *stage, uint32_t stage_s, int rb, int sb0, int nsb,
-                                             const uint8_t *xact, uint32_t xact_s, int xs, int tok_l7, int tok_g,
-                                             int tok_a, int tok_b, int n, float (&out)[4]) {
-    const int lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
-    const int am = lane >> 3;   // ldmatrix.x4 matrix this lane addresses: rows +8 for odd, bytes +16 for 2, 3
-    const uint32_t a_row = stage_s + (uint32_t)(((lane & 7) + 8 * (am & 1)) * rb + 16 * (am >> 1) + 16);
-    const uint32_t b_row = xact_s + (uint32_t)(tok_l7 * xs + 16 * ((lane >> 3) & 1));
-    const bool colv = g < n;
-    const uint8_t *r0 = stage + (size_t)g * rb, *r1 = stage + (size_t)(g + 8) * rb;
-    const uint8_t *xg = xact + (size_t)tok_g * xs;
-    const float *dxa = reinterpret_cast<const float *>(xact + (size_t)tok_a * xs + nsb * 256);
-    const float *dxb = reinterpret_cast<const float *>(xact + (size_t)tok_b * xs + nsb * 256);
-    const int16_t *bsg = reinterpret_cast<const int16_t *>(xg + nsb * 256 + nsb * 4);
-    const uint32_t M = 0x0f0f0f0fu;
-#pragma unroll 1
-    for (int sb = sb0; sb < nsb; sb += 4) {
-        const uint4 h0 = *reinterpret_cast<const uint4 *>(r0 + sb * B_Q4_K);
-        const uint4 h1 = *reinterpret_cast<const uint4 *>(r1 + sb * B_Q4_K);
-        // 6-bit scales / mins of sub-blocks 0-3 and 4-7, four per word (get_scale_min_k4, ggml-quants.c:822)
-        const uint32_t s0l = h0.y & 0x3f3f3f3fu, s0h = (h0.w & M) | ((h0.y >> 2) & 0x30303030u);
-        const uint32_t m0l = h0.z & 0x3f3f3f3fu, m0h = ((h0.w >> 4) & M) | ((h0.z >> 2) & 0x30303030u);
-        const uint32_t s1l = h1.y & 0x3f3f3f3fu, s1h = (h1.w & M) | ((h1.y >> 2) & 0x30303030u);
-        const uint32_t m1l = h1.z & 0x3f3f3f3fu, m1h = ((h1.w >> 4) & M) | ((h1.z >> 2) & 0x30303030u);
-        int as[4] = {0, 0, 0, 0};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {   // 32-byte qs chunk i: sub-block 2i (low nibbles), 2i + 1 (high)
-            uint32_t w0, w1, w2, w3, b0l, b1l, b0h, b1h;
-            ldsm_x4(a_row + (uint32_t)(sb * B_Q4_K + 32 * i), w0, w1, w2, w3);
-            ldsm_x2(b_row + (uint32_t)(sb * 256 + 64 * i), b0l, b1l);
-            ldsm_x2(b_row + (uint32_t)(sb * 256 + 64 * i + 32), b0h, b1h);
-            if (!colv) b0l = b1l = b0h = b1h = 0u;
-            int dl[4], dh[4];
-            mma_s8_k32(dl, w0 & M, w1 & M, w2 & M, w3 & M, b0l, b1l);
-            mma_s8_k32(dh, (w0 >> 4) & M, (w1 >> 4) & M, (w2 >> 4) & M, (w3 >> 4) & M, b0h, b1h);
-            const int jl = 2 * i, jh = 2 * i + 1;
-            const int sl0 = sbyte(jl < 4 ? s0l : s0h, jl & 3), sh0 = sbyte(jh < 4 ? s0l : s0h, jh & 3);
-            const int sl1 = sbyte(jl < 4 ? s1l : s1h, jl & 3), sh1 = sbyte(jh < 4 ? s1l : s1h, jh & 3);
-            as[0] += sl0 * dl[0] + sh0 * dh[0];
-            as[1] += sl0 * dl[1] + sh0 * dh[1];
-            as[2] += sl1 * dl[2] + sh1 * dh[2];
-            as[3] += sl1 * dl[3] + sh1 * dh[3];
-        }
-        // min term: A = [m_0..7 | m_0..7] (rows g, g + 8), B = [bsum_j >> 6 | 0] and [0 | bsum_j & 63]
-        const uint32_t am0 = (c & 1) ? m0h : m0l, am1 = (c & 1) ? m1h : m1l;
-        const int16_t *bq = bsg + sb * 16 + 8 * (c & 1);
-        const uint32_t q01 = *reinterpret_cast<const uint32_t *>(bq), q23 = *reinterpret_cast<const uint32_t *>(bq + 2);
-        const uint32_t q45 = *reinterpret_cast<const uint32_t *>(bq + 4), q67 = *reinterpret_cast<const uint32_t *>(bq + 6);
-        const int p0 = (int)(int16_t)(q01 & 0xffffu) + (int)(int16_t)(q01 >> 16);
-        const int p1 = (int)(int16_t)(q23 & 0xffffu) + (int)(int16_t)(q23 >> 16);
-        const int p2 = (int)(int16_t)(q45 & 0xffffu) + (int)(int16_t)(q45 >> 16);
-        const int p3 = (int)(int16_t)(q67 & 0xffffu) + (int)(int16_t)(q67 >> 16);
-        uint32_t bw = c < 2 ? pack_s8x4(p0 >> 6, p1 >> 6, p2 >> 6, p3 >> 6) : pack_s8x4(p0 & 63, p1 & 63, p2 & 63, p3 & 63);
-        if (!colv) bw = 0u;
-        int d1[4], d2[4];
-        mma_s8_k16(d1, am0, am1, c < 2 ? bw : 0u);
-        mma_s8_k16(d2, am0, am1, c < 2 ? 0u : bw);
-        const float dw0 = h2f((uint16_t)(h0.x & 0xffffu)), dm0 = h2f((uint16_t)(h0.x >> 16));
-        const float dw1 = h2f((uint16_t)(h1.x & 0xffffu)), dm1 = h2f((uint16_t)(h1.x >> 16));
-        const float dxa_ = dxa[sb], dxb_ = dxb[sb];
-        out[0] = fmaf(dxa_, fmaf(-dm0, (float)(64 * d1[0] + d2[0]), dw0 * (float)as[0]), out[0]);
-        out[1] = fmaf(dxb_, fmaf(-dm0, (float)(64 * d1[1] + d2[1]), dw0 * (float)as[1]), out[1]);
-        out[2] = fmaf(dxa_, fmaf(-dm1, (float)(64 * d1[2] + d2[2]), dw1 * (float)as[2]), out[2]);
-        out[3] = fmaf(dxb_, fmaf(-dm1, (float)(64 * d1[3] + d2[3]), dw1 * (float)as[3]), out[3]);
-    }
 }
 
 // Q5_0 x Q8_0, lane = half of a row's 32-blocks: value = (nibble | hbit << 4) - 16, so
@@ -657,18 +605,30 @@ __device__ __forceinline__ void gu_rows(const uint8_t *row, int nsb, int j, int 
         x[t].d = reinterpret_cast<const float *>(a + nsb * 256);
         x[t].bs = reinterpret_cast<const int16_t *>(a + nsb * 256 + nsb * 4);
     }
-    float acc[NT];
+    float acc[NT], macc[NT];
 #pragma unroll
-    for (int t = 0; t < NT; ++t) acc[t] = 0.f;
-    if (type == T_IQ2_S) {
-        iq2s_lane<NT>(row, nsb, j, grid, x, acc);
+    for (int t = 0; t < NT; ++t) acc[t] = macc[t] = 0.f;
+    if (type == T_IQ2_S) iq2s_lane<NT>(row, nsb, j, grid, x, acc);
+    else if (type == T_IQ2_XXS) iq2xxs_lane<NT>(row, nsb, j, x, acc);
+    else q4k_lane<NT>(row, nsb, j, x, acc, macc);
+    // the reference's reductions (hsum_float_8: ((a0 + a4) + (a2 + a6)) + ((a1 + a5) + (a3 + a7)); the
+    // min lanes (m0 + m2) + (m1 + m3), added last); every thread of the row ends with the same value
 #pragma unroll
-        for (int t = 0; t < NT; ++t) acc[t] *= 0.125f;
-    } else {
-        q4k_lane<NT>(row, nsb, j, x, acc);
+    for (int t = 0; t < NT; ++t) {
+        float s = acc[t];
+        s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, 4));
+        s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, 2));
+        s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, 1));
+        if (type == T_Q4_K) {
+            float m = macc[t];
+            m = __fadd_rn(m, __shfl_xor_sync(0xffffffffu, m, 2));
+            m = __fadd_rn(m, __shfl_xor_sync(0xffffffffu, m, 1));
+            s = __fadd_rn(s, m);
+        } else {
+            s = __fmul_rn(0.125f, s);
+        }
+        out[t] = s;
     }
-#pragma unroll
-    for (int t = 0; t < NT; ++t) out[t] = acc[t];
 }
 
 template <int NT>
@@ -865,13 +825,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(GemvParams p) {
                     if (nt == 1) gu_rows<1>(row, nsb, j, pv.type, grid, act, xs, tok, v);
                     else gu_rows<4>(row, nsb, j, pv.type, grid, act, xs, tok, v);
 #pragma unroll
-                    for (int c = 0; c < kTokChunk; ++c) {
-                        float s = v[c];
-                        s += __shfl_xor_sync(0xffffffffu, s, 1);
-                        s += __shfl_xor_sync(0xffffffffu, s, 2);
-                        s += __shfl_xor_sync(0xffffffffu, s, 4);
-                        if (j == 0 && c < nt) p.y[(size_t)pair[c] * p.d_out + st.row0 + r] = s;
-                    }
+                    for (int c = 0; c < kTokChunk; ++c)
+                        if (j == 0 && c < nt) p.y[(size_t)pair[c] * p.d_out + st.row0 + r] = v[c];
                 }
             }
         } else {
@@ -1100,8 +1055,8 @@ __device__ void fused_route(const FusedParams &p, FusedRoute &rs, int tid) {
 __device__ __forceinline__ uint32_t fused_cost(const FusedParams &p, bool gu, int type, int n) {
     uint32_t bytes, instr;
     if (gu) {
-        const uint32_t dec = type == T_IQ2_S ? 70u : 24u;
-        bytes = 8u * (uint32_t)(p.d / QK_K) * (type == T_IQ2_S ? (uint32_t)B_IQ2_S : (uint32_t)B_Q4_K);
+        const uint32_t dec = type == T_Q4_K ? 24u : 70u;
+        bytes = 8u * (uint32_t)row_bytes(type, p.d);
         instr = 8u * 8u * (uint32_t)(p.d / QK_K) * (dec + 16u * (uint32_t)n);
     } else {
         const uint32_t dec = type == T_IQ4_NL ? 45u : 25u;
@@ -1502,24 +1457,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) fused_decode_kernel(FusedPara
             const int rb = (int)row_bytes(type, d);
             const int po = rs.off[e], n = rs.cnt[e];
             const int j = lane & 7, r = wg * 4 + (lane >> 3);
-            if (ok && type == T_Q4_K) {
-                // warp-level int8 MMAs: warp wg takes super-blocks wg, wg + 4, ... of all 16 rows and
-                // writes its partial sums to gate_up part wg (the GeGLU step adds the four in order)
-                // pair of column c (missing columns repeat column 0)
-                auto pair_of = [&](int c) { return rs.perm[po + (c < n ? c : 0)]; };
-                const int g = lane >> 2, cc = lane & 3;
-                const int pa = pair_of(2 * cc), pb = pair_of(2 * cc + 1);
-                float v[4] = {0.f, 0.f, 0.f, 0.f};
-                const uint8_t *stage = slots + slot * L.slot_cap;
-                q4k_tile_mma(stage, smem_addr(stage), rb, wg, nsb, xact, smem_addr(xact), xs, pair_of(lane & 7) / k,
-                             pair_of(g) / k, pa / k, pb / k, n, v);
-                float *hp = p.h + (size_t)wg * hpart;
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const int row = g + 8 * (q >> 1), col = 2 * cc + (q & 1);
-                    if (row < st.nrows && col < n) hp[(size_t)((q & 1) ? pb : pa) * 2 * nff + st.row0 + row] = v[q];
-                }
-            } else if (ok && wg * 4 < st.nrows) {
+            if (ok && wg * 4 < st.nrows) {
                 const uint8_t *row = slots + slot * L.slot_cap + (size_t)r * rb;
                 for (int c0 = 0; c0 < n; c0 += kTokChunk) {
                     const int nt = min(kTokChunk, n - c0);
@@ -1535,13 +1473,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) fused_decode_kernel(FusedPara
                     else gu_rows<4>(row, nsb, j, type, grid, xact, xs, tok, v);
 #pragma unroll
                     for (int c = 0; c < kTokChunk; ++c) {
-                        float s = v[c];
-                        s += __shfl_xor_sync(0xffffffffu, s, 1);
-                        s += __shfl_xor_sync(0xffffffffu, s, 2);
-                        s += __shfl_xor_sync(0xffffffffu, s, 4);
                         if (j == 0 && c < nt) {
                             float *hp = p.h + (size_t)pair[c] * 2 * nff + st.row0 + r;
-                            hp[0] = s;
+                            hp[0] = v[c];
                             hp[hpart] = 0.f;   // rows not split over the four parts
                             hp[2 * hpart] = 0.f;
                             hp[3 * hpart] = 0.f;
@@ -1801,6 +1735,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) fused_decode_kernel(FusedPara
 }  // namespace moeb
 
 #include "prefill.cuh"
+#include "gateup_lx.cuh"
 #include "mid.cuh"
 
 namespace moeb {
@@ -2089,9 +2024,36 @@ bool mid_shape_ok(int kind, int d, int nff, int P, int E) {
            P / (8 * md_chunk(kind)) + tiles <= kMdMaxUnits && md_layout(kind, d, nff).n_slots >= 2;
 }
 
+// 2D tensor map of a Q4_K gate_up pool (row bytes x rows, one super-block x 64 rows per box) for the
+// lane-exact gate_up kernel's raw-row staging; other pool types leave the map zero (unused)
+static cudaError_t lx_encode_map(CUtensorMap *map, const PoolView &pv, int d, int nff) {
+    std::memset(map, 0, sizeof(*map));
+    if (!pv.w || pv.type != T_Q4_K || pv.n <= 0) return cudaSuccess;
+    using Encode = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+    static Encode encode = nullptr;
+    if (!encode) {
+        void *fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        const cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+        if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn) return e != cudaSuccess ? e : cudaErrorNotSupported;
+        encode = reinterpret_cast<Encode>(fn);
+    }
+    const cuuint64_t rb = (cuuint64_t)row_bytes(T_Q4_K, d);
+    const cuuint64_t dims[2] = {rb, (cuuint64_t)pv.n * 2 * nff};
+    const cuuint64_t strides[1] = {rb};
+    const cuuint32_t box[2] = {(cuuint32_t)B_Q4_K, 64u};
+    const cuuint32_t estr[2] = {1u, 1u};
+    const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t *>(pv.w), dims, strides, box, estr,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
 cudaError_t launch_prefill(const PrefillArgs &a, cudaStream_t s, int n_sms) {
     static unsigned optin[32];
-    cudaError_t e = smem_optin((const void *)pf_gate_up_kernel, sizeof(GuSmem), optin, 0);
+    cudaError_t e = smem_optin((const void *)pf_gate_up_lx_kernel, sizeof(LxSmem), optin, 0);
     if (e == cudaSuccess) e = smem_optin((const void *)pf_down_kernel, sizeof(DnSmem), optin, 1);
     if (e != cudaSuccess) return e;
     const int T = a.T, E = a.E, d = a.d, k = a.k;
@@ -2203,12 +2165,16 @@ cudaError_t launch_prefill(const PrefillArgs &a, cudaStream_t s, int n_sms) {
         if (e != cudaSuccess) return e;
         if ((e = prof_mark(s, mark++)) != cudaSuccess) return e;
     } else {
-        e = pf_launch("pf_gather_kernel", (const void *)pf_gather_kernel, dim3(a.max_tiles, d / QK_K), dim3(256), 0, s,
-                      true, pargs);
+        e = pf_launch("pf_gather_lx_kernel", (const void *)pf_gather_lx_kernel, dim3(a.max_tiles, d / QK_K), dim3(256), 0,
+                      s, true, pargs);
         if (e != cudaSuccess) return e;
         if ((e = prof_mark(s, mark++)) != cudaSuccess) return e;
-        e = pf_launch("pf_gate_up_kernel", (const void *)pf_gate_up_kernel, dim3(n_sms), dim3(kPfThreads), sizeof(GuSmem), s,
-                      true, pargs);
+        LxMaps maps;
+        if ((e = lx_encode_map(&maps.gu[0], a.hot_gu, d, a.nff)) != cudaSuccess) return e;
+        if ((e = lx_encode_map(&maps.gu[1], a.cold_gu, d, a.nff)) != cudaSuccess) return e;
+        void *largs[] = {&p, &maps};
+        e = pf_launch("pf_gate_up_lx_kernel", (const void *)pf_gate_up_lx_kernel, dim3(n_sms), dim3(kLxThreads),
+                      sizeof(LxSmem), s, true, largs);
         if (e != cudaSuccess) return e;
         if ((e = prof_mark(s, mark++)) != cudaSuccess) return e;
     }

@@ -103,10 +103,10 @@ __device__ __forceinline__ void tmem_ld16x2(uint32_t ta, uint32_t tb, float (&va
 // Instrumented builds only (-DMOEB_TRACE): SM-clock stamps of CTA 0's converter warp 0, MMA thread
 // and first epilogue warp, per pipeline step.
 #ifdef MOEB_TRACE
-__device__ unsigned long long g_ptrace[2][3][96][3];
+__device__ unsigned long long g_ptrace[2][3][256][3];
 __device__ unsigned long long g_utrace[32][16];
 #define PTRACE(k, role, idx, f) \
-    if (blockIdx.x == 0 && (idx) < 96) g_ptrace[k][role][idx][f] = clock64();
+    if (blockIdx.x == 0 && (idx) < 256) g_ptrace[k][role][idx][f] = clock64();
 #define UTRACE(u, f) \
     if (blockIdx.x == 0 && (u) < 32) g_utrace[u][f] = clock64();
 #else
@@ -219,16 +219,6 @@ __device__ __forceinline__ void sts128(uint8_t *p, uint32_t a, uint32_t b, uint3
     *reinterpret_cast<uint4 *>(p) = make_uint4(a, b, c, d);
 }
 
-// 6-bit scale and min of sub-block j of a Q4_K super-block (get_scale_min_k4, ggml-quants.c:822)
-__device__ __forceinline__ void q4k_scale_min(int j, const uint8_t *q, int &sc, int &m) {
-    if (j < 4) {
-        sc = q[j] & 63;
-        m = q[j + 4] & 63;
-    } else {
-        sc = (q[j + 4] & 0xF) | ((q[j - 4] >> 6) << 4);
-        m = (q[j + 4] >> 4) | ((q[j] >> 6) << 4);
-    }
-}
 
 // Raw bytes of one gate_up stage, loaded into registers ahead of their conversion (read-only
 // global loads, so they may be issued before the shared-memory stores of the previous step).

@@ -49,8 +49,7 @@ CONFIGS = {
     "mini_mixed": LayerConfig("mini_mixed", 3, tuple(range(8)), 1.1, False, d_model=512, n_ff=64, n_expert=32,
                               top_k=4, seed=11),
     # decode_t4_mixed's experts with the product files' cold class, IQ2_XXS gate_up / IQ4_NL down, and
-    # no router skew, so both classes are routed (the oracle, the host quantiser and the dequantiser
-    # serve it; the layer kernels do not yet)
+    # no router skew, so both classes are routed
     "decode_t4_iq2xxs": LayerConfig("decode_t4_iq2xxs", 4, tuple(range(48)), None, False, cold_gu_type=IQ2_XXS),
 }
 

@@ -34,7 +34,7 @@ def test_block_mini_vs_reference_fixture(golden_block, prefill_from, gemm, path)
     x = golden_block[f"{name}_x"]
     out, aux, layer = run_layer(host, x, aux_names=AUX, norms=norms_of(name))
     assert layer.prefill_path(x.shape[0]) == (path != "decode")
-    assert layer.mid_path(x.shape[0]) == (path == "mid")
+    assert layer.mid_path(x.shape[0], 1) == (path == "mid")
     ties = set(near_tie_tokens(golden_block[f"{name}_logits"], host.top_k).tolist())
     same = [t for t in range(x.shape[0]) if t not in ties]
     assert np.array_equal(aux["ids"][same], golden_block[f"{name}_ids"][same])
