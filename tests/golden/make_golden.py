@@ -4,6 +4,7 @@
     python tests/golden/make_golden.py           # golden.npz
     python tests/golden/make_golden.py --block   # golden_block.npz (the Gemma-4 block norms)
     python tests/golden/make_golden.py --types   # golden_types.npz + the IQ2_XXS tables (IQ2_XXS / Q8_0 weights)
+    python tests/golden/make_golden.py --prefill # golden_prefill.npz (T=2048 prefill layer, stack layer 0)
 
 Everything in the fixtures comes out of the reference's own code (ggml-base + ggml-cpu of the
 vendored llama.cpp, compiled into oracle/_ref): quantised bytes from ggml_quantize_chunk, dequantised
@@ -350,8 +351,45 @@ def main_types():
     print("wrote", path, os.path.getsize(path), "bytes")
 
 
+def token_digests(a: np.ndarray, T: int) -> np.ndarray:
+    """Per-token 64-bit digests (leading 8 bytes of SHA-256) of a [T * k, n] f32 array in pair order."""
+    rows = a.reshape(T, -1)
+    return np.array([np.frombuffer(hashlib.sha256(np.ascontiguousarray(rows[t]).tobytes()).digest()[:8], np.uint64)[0]
+                     for t in range(T)], np.uint64)
+
+
+def main_prefill():
+    """The prefill workloads at their full token counts through the reference graph: routing, per-token
+    digests of gate_up and of the GeGLU output (both bit-exact targets), and the outputs of every
+    `step`-th token with the whole output's RMS (the parity bar's scale)."""
+    r = Ref()
+    fx = {}
+    for name, step in (("prefill_t2048_q4k", 32), ("stack30_t256_mixed", 8)):
+        cfg = workload.CONFIGS[name]
+        pools = ref_pools(r, cfg)
+        x = workload.make_input(cfg)
+        T = x.shape[0]
+        spec = layer_spec(cfg, pools, x)
+        res = r.moe_layer(spec, n_threads=8, want=("logits", "ids", "weights", "gate_up", "act"))
+        fx[f"{name}_ids"] = res["ids"]
+        fx[f"{name}_logits_sha"] = np.array(sha(res["logits"]))
+        fx[f"{name}_gate_up_digest"] = token_digests(res["gate_up"], T)
+        fx[f"{name}_act_digest"] = token_digests(res["act"], T)
+        fx[f"{name}_out_rows"] = np.arange(0, T, step, dtype=np.int32)
+        fx[f"{name}_out"] = res["out"][::step]
+        fx[f"{name}_out_rms"] = np.array(np.sqrt(np.mean(res["out"].astype(np.float64) ** 2)))
+        for k, v in pool_digests(spec).items():
+            fx[f"{name}_sha_{k}"] = np.array(v)
+        print(name, "done")
+    path = os.path.join(HERE, "golden_prefill.npz")
+    np.savez_compressed(path, **fx)
+    print("wrote", path, os.path.getsize(path), "bytes")
+
+
 if __name__ == "__main__":
-    if "--types" in sys.argv:
+    if "--prefill" in sys.argv:
+        main_prefill()
+    elif "--types" in sys.argv:
         main_types()
     elif "--block" in sys.argv:
         main_block()

@@ -330,3 +330,27 @@ def test_dense_mlp_is_a_one_expert_layer(port, ref):
     assert (as_layer["ids"] == 0).all() and (as_layer["weights"] == 1.0).all()
     assert np.array_equal(as_layer["out"].view(np.uint32), dense.view(np.uint32))
     assert_layer_close(port.moe_layer(spec, want=())["out"], dense, tol=1e-5)
+
+
+@pytest.mark.parametrize("name,rows", [("prefill_t2048_q4k", [0, 1, 777, 2047]), ("stack30_t256_mixed", [0, 5, 128, 255])])
+def test_prefill_fixture_digests_match_port(port, name, rows):
+    """The reference's prefill-shape fixtures (tests/golden/golden_prefill.npz, per-token digests of
+    gate_up and of the GeGLU output) are reproduced by the oracle bit for bit on sampled tokens, and
+    the quantised pools are the reference quantiser's."""
+    import hashlib
+    import os
+    from conftest import ROOT
+    g = dict(np.load(os.path.join(ROOT, "tests", "golden", "golden_prefill.npz"), allow_pickle=False))
+    host = host_layer(name)
+    for n in ("hot_gu", "hot_down", "cold_gu", "cold_down"):
+        got = sha(getattr(host, n)) if getattr(host, n) is not None else ""
+        assert got == str(g[f"{name}_sha_{n}"]), n
+    x = workload.make_input(workload.CONFIGS[name])[rows]
+    res = port.moe_layer(spec_of(host, x), n_threads=4, want=("ids", "gate_up", "act"))
+    k = host.top_k
+    for i, t in enumerate(rows):
+        assert np.array_equal(res["ids"][i], g[f"{name}_ids"][t]), t
+        for key in ("gate_up", "act"):
+            rowbits = np.ascontiguousarray(res[key][i * k:(i + 1) * k]).tobytes()
+            d = np.frombuffer(hashlib.sha256(rowbits).digest()[:8], np.uint64)[0]
+            assert d == g[f"{name}_{key}_digest"][t], (key, t)
