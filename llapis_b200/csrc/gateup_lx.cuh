@@ -33,9 +33,11 @@ constexpr int kLxN = 64;                    // pairs per work unit (MMA N <= 64)
 constexpr int kLxMainCores = 8;             // K = 64 per main pass step (2 lanes x 32), in 8-value cores
 constexpr int kLxMinCores = 4;              // K = 32 per min pass step (2 lanes x 16)
 constexpr int kLxBStageBytes = (kLxN / 8) * kLxMainCores * 128;   // 8 KB: one unit's half of a main image
-constexpr int kLxEpiWarps = 16;             // four per TMEM lane quadrant, 16 columns each
+constexpr int kLxEpiWarps = 8;              // two per TMEM lane quadrant, 32 columns each
 constexpr int kLxEpiCols = kLxN / (kLxEpiWarps / 4);
-constexpr int kLxProdWarp = kPfConvWarps + 1;
+constexpr int kLxConvWarps = 8;             // two per TMEM lane quadrant, on alternate steps
+constexpr int kLxMmaWarp = kLxConvWarps;
+constexpr int kLxProdWarp = kLxMmaWarp + 1;
 constexpr int kLxEpiWarp0 = kLxProdWarp + 1;
 constexpr int kLxThreads = (kLxEpiWarp0 + kLxEpiWarps) * 32;
 // TMEM: three accumulator buffers of 2 lanes x 64 columns, then four A buffers of 32 columns; the
@@ -102,6 +104,18 @@ __device__ __forceinline__ void tmem_ld16x2u(uint32_t ta, uint32_t tb, uint32_t 
     asm volatile("tcgen05.wait::ld.sync.aligned;" : MOEB_RW16(a), MOEB_RW16(b)::"memory");
 }
 
+// 8 columns of two accumulators in one wait
+#define MOEB_LD8 "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+__device__ __forceinline__ void tmem_ld8x2u(uint32_t ta, uint32_t tb, uint32_t (&a)[8], uint32_t (&b)[8]) {
+    asm volatile(MOEB_LD8 : "=r"(a[0]), "=r"(a[1]), "=r"(a[2]), "=r"(a[3]), "=r"(a[4]), "=r"(a[5]), "=r"(a[6]), "=r"(a[7])
+                 : "r"(ta));
+    asm volatile(MOEB_LD8 : "=r"(b[0]), "=r"(b[1]), "=r"(b[2]), "=r"(b[3]), "=r"(b[4]), "=r"(b[5]), "=r"(b[6]), "=r"(b[7])
+                 : "r"(tb));
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(a[0]), "+r"(a[1]), "+r"(a[2]), "+r"(a[3]), "+r"(a[4]), "+r"(a[5]), "+r"(a[6]), "+r"(a[7]), "+r"(b[0]),
+                   "+r"(b[1]), "+r"(b[2]), "+r"(b[3]), "+r"(b[4]), "+r"(b[5]), "+r"(b[6]), "+r"(b[7])::"memory");
+}
+
 // MMA with the A operand in tensor memory (M = 128 rows in the 128 TMEM lanes, K along the
 // columns, two fp16 values per 32-bit column) and B from shared memory
 __device__ __forceinline__ void umma_f16_ts(uint32_t dtmem, uint32_t atmem, uint64_t b, uint32_t idesc, uint32_t accum) {
@@ -139,6 +153,34 @@ __device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
     return r;
 }
 
+// ---------------------------------------------------------------- waits that sleep
+// mbarrier.try_wait with a suspend-time hint: a waiting thread is suspended until the phase completes
+// (or the hint of ~1 us runs out) instead of spinning, so waiting warps leave the issue slots to the
+// converters, the MMA thread and the epilogue. Bounded like pf_wait: after kLxWaitLimit tries (about
+// a second) the wait records ERR_MBAR_TIMEOUT, raises the CTA's abort flag and gives up.
+constexpr uint32_t kLxWaitLimit = 1u << 20;
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity), "r"(1000u)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ bool lx_wait(uint64_t *bar, uint32_t parity, volatile int32_t *abort) {
+    for (uint32_t i = 0; i < kLxWaitLimit; ++i) {
+        if (mbar_try_wait_sleep(bar, parity)) return true;
+        if ((i & 15u) == 15u && *abort) return false;
+    }
+    atomicOr(&g_error, ERR_MBAR_TIMEOUT);
+    *abort = 1;
+    return false;
+}
+__device__ __forceinline__ bool lx_wait_warp(uint64_t *bar, uint32_t parity, volatile int32_t *abort) {
+    return __all_sync(0xffffffffu, lx_wait(bar, parity, abort));
+}
+
 // ---------------------------------------------------------------- 2D tensor-map copy (no multicast)
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
     asm volatile(
@@ -154,14 +196,27 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, i
 
 // Q4_K (block: d, dmin, scales[12], qs[128]; byte 32c + b holds value b of sub-block 2c in its low
 // nibble and of sub-block 2c + 1 in its high nibble): A = sc_j * q, exact in fp16
-__device__ __forceinline__ void lx_a_q4k_lane(const uint32_t (&qw)[4], const int (&sc)[8], uint32_t *o) {
+__device__ __forceinline__ void lx_a_q4k_lane(const uint32_t (&qw)[4], const __half2 (&s2)[8], const __half2 (&ns2)[8],
+                                              uint32_t *o) {
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
-        const __half2 sl = __float2half2_rn((float)sc[2 * c]), nsl = __float2half2_rn(-1024.f * sc[2 * c]);
-        const __half2 sh = __float2half2_rn((float)sc[2 * c + 1]), nsh = __float2half2_rn(-1024.f * sc[2 * c + 1]);
-        scale4(qw[c] & 0x0f0f0f0fu, sl, nsl, o[4 * c], o[4 * c + 1]);
-        scale4((qw[c] >> 4) & 0x0f0f0f0fu, sh, nsh, o[4 * c + 2], o[4 * c + 3]);
+        scale4(qw[c] & 0x0f0f0f0fu, s2[2 * c], ns2[2 * c], o[4 * c], o[4 * c + 1]);
+        scale4((qw[c] >> 4) & 0x0f0f0f0fu, s2[2 * c + 1], ns2[2 * c + 1], o[4 * c + 2], o[4 * c + 3]);
     }
+}
+
+// The eight 6-bit scales (mins) of a Q4_K super-block as bytes of two words (get_scale_min_k4,
+// ggml-quants.c:822), from the scale words w1, w2, w3 (bytes 4..15 of the block)
+__device__ __forceinline__ void q4k_scale_words(uint32_t w1, uint32_t w2, uint32_t w3, uint32_t (&sc)[2], uint32_t (&mn)[2]) {
+    sc[0] = w1 & 0x3f3f3f3fu;
+    sc[1] = (w3 & 0x0f0f0f0fu) | ((w1 >> 2) & 0x30303030u);
+    mn[0] = w2 & 0x3f3f3f3fu;
+    mn[1] = ((w3 >> 4) & 0x0f0f0f0fu) | ((w2 >> 2) & 0x30303030u);
+}
+// byte j of two words as an exact fp16 pair (v, v): bytes [v, 0x64, v, 0x64] are (1024 + v) twice
+__device__ __forceinline__ __half2 byte_h2(const uint32_t (&w)[2], int j) {
+    const uint32_t b = (uint32_t)(j & 3);
+    return __hsub2(u2h(__byte_perm(w[j >> 2], 0x64646464u, 0x4040u | b | (b << 8))), u2h(0x64006400u));
 }
 
 // IQ2_S (block: d, qs[32] grid low bytes, signs[32], qh[8], scales[8]): value 32b + 4L + e is byte
@@ -367,7 +422,7 @@ __global__ void __launch_bounds__(kLxThreads, 1) pf_gate_up_lx_kernel(PfParams p
         S.abort = 0;
         fence_mbar_init();
     }
-    if (warp == kPfMmaWarp) tmem_alloc_warp(&S.tmem, kLxTmemCols);
+    if (warp == kLxMmaWarp) tmem_alloc_warp(&S.tmem, kLxTmemCols);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -377,45 +432,51 @@ __global__ void __launch_bounds__(kLxThreads, 1) pf_gate_up_lx_kernel(PfParams p
     const int nsb = p.d / QK_K, n_mb = p.nff / 64, gu_rows = 2 * p.nff;
     const int units = *p.n_tiles * n_mb * 2;
 
-    if (warp < kPfConvWarps) {
-        // ------------------------------------------------ converters: thread r = weight row r = TMEM lane r
-        const int r = tid;
-        const uint32_t ta = tmem + ((uint32_t)(32 * warp) << 16) + kLxColA;
+    if (warp < kLxConvWarps) {
+        // ------------------------------------------------ converters: thread r = weight row r = TMEM lane r;
+        // group 0 (warps 0-3) takes the even steps, group 1 (warps 4-7) the odd ones
+        const int grp = warp >> 2, qd = warp & 3;
+        const int r = 32 * qd + lane;
+        const uint32_t ta = tmem + ((uint32_t)(32 * qd) << 16) + kLxColA;
         LxIter cur;
         cur.start(p, units, n_mb, r);
-        for (int it = 0; cur.ok && !warp_aborted(abort); ++it) {
+        if (grp == 1 && cur.ok) cur.advance(p, units, n_mb, nsb, r);
+        for (int it = grp; cur.ok && !warp_aborted(abort); it += 2) {
             const int ab = it % kLxRing;
             if (tid == 0) PTRACE(0, 0, it, 0);
-            if (it >= kLxRing && !pf_wait_warp(&S.opfree[ab], ((it / kLxRing) - 1) & 1, abort)) break;
+            if (it >= kLxRing && !lx_wait_warp(&S.opfree[ab], ((it / kLxRing) - 1) & 1, abort)) break;
             if (tid == 0) PTRACE(0, 0, it, 1);
             tc_fence_after();
             const bool mn = cur.pass >= 4;
             uint32_t o[32];
             if (cur.type == T_Q4_K) {
                 // the step's raw blocks (and B image) have landed in ring slot ab
-                if (!pf_wait_warp(&S.bfull[ab], (it / kLxRing) & 1, abort)) break;
+                if (!lx_wait_warp(&S.bfull[ab], (it / kLxRing) & 1, abort)) break;
+                if (lane == 0 && grp == 0) XTRACE(it, 4 + qd);
                 const uint32_t *w = reinterpret_cast<const uint32_t *>(S.raw[ab] + r * B_Q4_K);
-                uint8_t sc12[12];
-                *reinterpret_cast<uint32_t *>(sc12 + 0) = w[1];
-                *reinterpret_cast<uint32_t *>(sc12 + 4) = w[2];
-                *reinterpret_cast<uint32_t *>(sc12 + 8) = w[3];
-                int sc[8], mn8[8];
-#pragma unroll
-                for (int j = 0; j < 8; ++j) q4k_scale_min(j, sc12, sc[j], mn8[j]);
+                uint32_t scw[2], mnw[2];
+                q4k_scale_words(w[1], w[2], w[3], scw, mnw);
                 if (!mn) {
+                    // per sub-block j: (sc_j, sc_j) and (-1024 sc_j, -1024 sc_j) for scale4, shared by both lanes
+                    __half2 s2[8], ns2[8];
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        s2[j] = byte_h2(scw, j);
+                        ns2[j] = __hmul2(s2[j], u2h(0xe400e400u));   // x -1024, exact
+                    }
 #pragma unroll
                     for (int li = 0; li < 2; ++li) {
                         const int L = lx_first_lane(cur.pass) + 4 * li;   // qs word of chunk c: 4 + 8c + L
                         const uint32_t qw[4] = {w[4 + L], w[12 + L], w[20 + L], w[28 + L]};
-                        lx_a_q4k_lane(qw, sc, o + 16 * li);
+                        lx_a_q4k_lane(qw, s2, ns2, o + 16 * li);
                     }
                 } else {
                     // min lanes m = pass - 4 and m + 2: [mins[2m] x 2, mins[2m+1] x 2, 0 x 12]
 #pragma unroll
                     for (int li = 0; li < 2; ++li) {
                         const int m = (cur.pass - 4) + 2 * li;
-                        o[8 * li] = pack_h2i(mn8[2 * m], mn8[2 * m]);
-                        o[8 * li + 1] = pack_h2i(mn8[2 * m + 1], mn8[2 * m + 1]);
+                        o[8 * li] = h2u(byte_h2(mnw, 2 * m));
+                        o[8 * li + 1] = h2u(byte_h2(mnw, 2 * m + 1));
 #pragma unroll
                         for (int i = 2; i < 8; ++i) o[8 * li + i] = 0u;
                     }
@@ -429,6 +490,7 @@ __global__ void __launch_bounds__(kLxThreads, 1) pf_gate_up_lx_kernel(PfParams p
                 lx_a_iq2xxs_lane(blk, lx_first_lane(cur.pass), o);
                 lx_a_iq2xxs_lane(blk, lx_first_lane(cur.pass) + 4, o + 16);
             }
+            if (lane == 0 && grp == 0) XTRACE(it, 8 + qd);
             if (mn) {
                 uint32_t o16[16];
 #pragma unroll
@@ -441,10 +503,12 @@ __global__ void __launch_bounds__(kLxThreads, 1) pf_gate_up_lx_kernel(PfParams p
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&S.afull[ab]);
+            if (lane == 0 && grp == 0 && qd > 0) XTRACE(it, qd);
             if (tid == 0) PTRACE(0, 0, it, 2);
             cur.advance(p, units, n_mb, nsb, r);
+            if (cur.ok) cur.advance(p, units, n_mb, nsb, r);
         }
-    } else if (warp == kPfMmaWarp) {
+    } else if (warp == kLxMmaWarp) {
         // ------------------------------------------------ MMA issue (one thread)
         if (lane == 0) {
             LxIter s;
@@ -452,8 +516,8 @@ __global__ void __launch_bounds__(kLxThreads, 1) pf_gate_up_lx_kernel(PfParams p
             for (int it = 0; s.ok && !*abort; ++it) {
                 const int ab = it % kLxRing, db = it % kLxDBufs;
                 PTRACE(0, 1, it, 0);
-                if (!pf_wait(&S.afull[ab], (it / kLxRing) & 1, abort) || !pf_wait(&S.bfull[ab], (it / kLxRing) & 1, abort) ||
-                    (it >= kLxDBufs && !pf_wait(&S.dempty[db], ((it / kLxDBufs) - 1) & 1, abort)))
+                if (!lx_wait(&S.afull[ab], (it / kLxRing) & 1, abort) || !lx_wait(&S.bfull[ab], (it / kLxRing) & 1, abort) ||
+                    (it >= kLxDBufs && !lx_wait(&S.dempty[db], ((it / kLxDBufs) - 1) & 1, abort)))
                     break;
                 PTRACE(0, 1, it, 1);
                 tc_fence_after();
@@ -463,9 +527,11 @@ __global__ void __launch_bounds__(kLxThreads, 1) pf_gate_up_lx_kernel(PfParams p
                 if (s.pass < 4) {   // lane a: K = 32 into d0, lane b: K = 32 into d0 + 64
                     const uint32_t sbo = kLxMainCores * 128;
                     umma_f16_ts(d0, a0, umma_sdesc(b0, 128, sbo), idesc, 0);
+                    XTRACE(it, 12);
                     umma_f16_ts(d0, a0 + 8, umma_sdesc(b0 + 256, 128, sbo), idesc, 1);
                     umma_f16_ts(d0 + 64, a0 + 16, umma_sdesc(b0 + 512, 128, sbo), idesc, 0);
                     umma_f16_ts(d0 + 64, a0 + 24, umma_sdesc(b0 + 768, 128, sbo), idesc, 1);
+                    XTRACE(it, 13);
                 } else {            // the two min lanes, K = 16 each
                     const uint32_t sbo = kLxMinCores * 128;
                     umma_f16_ts(d0, a0, umma_sdesc(b0, 128, sbo), idesc, 0);
@@ -473,6 +539,7 @@ __global__ void __launch_bounds__(kLxThreads, 1) pf_gate_up_lx_kernel(PfParams p
                 }
                 umma_commit(&S.opfree[ab]);
                 umma_commit(&S.dfull[db]);
+                XTRACE(it, 14);
                 PTRACE(0, 1, it, 2);
                 s.advance(p, units, n_mb, nsb, -1);
             }
@@ -487,7 +554,7 @@ __global__ void __launch_bounds__(kLxThreads, 1) pf_gate_up_lx_kernel(PfParams p
             s.start(p, units, n_mb, -1);
             for (int it = 0; s.ok && !*abort; ++it) {
                 const int bs = it % kLxRing;
-                if (it >= kLxRing && !pf_wait(&S.opfree[bs], ((it / kLxRing) - 1) & 1, abort)) break;
+                if (it >= kLxRing && !lx_wait(&S.opfree[bs], ((it / kLxRing) - 1) & 1, abort)) break;
                 const int ncores = s.pass >= 4 ? kLxMinCores : kLxMainCores;
                 const uint32_t bytes = (uint32_t)(s.N / 8) * ncores * 128;
                 const bool q4 = s.type == T_Q4_K;
@@ -502,6 +569,7 @@ __global__ void __launch_bounds__(kLxThreads, 1) pf_gate_up_lx_kernel(PfParams p
                     tma_load_2d(S.raw[bs], map, s.sb * B_Q4_K, y0, &S.bfull[bs]);
                     tma_load_2d(S.raw[bs] + 64 * B_Q4_K, map, s.sb * B_Q4_K, y0 + p.nff, &S.bfull[bs]);
                 }
+                XTRACE(it, 0);
                 s.advance(p, units, n_mb, nsb, -1);
             }
         }
@@ -549,7 +617,7 @@ __global__ void __launch_bounds__(kLxThreads, 1) pf_gate_up_lx_kernel(PfParams p
                 for (int sb = 0; sb < nsb; ++sb, ++it) {
                     const int db = it % kLxDBufs;
                     if (et == 0) PTRACE(0, 2, it, 0);
-                    if (!pf_wait_warp(&S.dfull[db], (it / kLxDBufs) & 1, abort)) { ok = false; break; }
+                    if (!lx_wait_warp(&S.dfull[db], (it / kLxDBufs) & 1, abort)) { ok = false; break; }
                     if (et == 0) PTRACE(0, 2, it, 1);
                     tc_fence_after();
                     if (live) {
@@ -557,20 +625,25 @@ __global__ void __launch_bounds__(kLxThreads, 1) pf_gate_up_lx_kernel(PfParams p
                         const float xs = mn ? xw.y : xw.x;   // d_w, or -dmin_w for the min lanes
                         const uint64_t xs2 = f2pack(xs, xs);
                         const uint32_t dcol = tl_lane + kLxColD + 128 * db + col0;
-                        uint32_t sa[16], sbv[16];
-                        tmem_ld16x2u(dcol, dcol + 64, sa, sbv);
                         const float4 *yd = reinterpret_cast<const float4 *>(&S.dxs[sb][col0]);
 #pragma unroll
-                        for (int i = 0; i < 4; ++i) {
-                            const float4 y4 = yd[i];
-                            // d = d_x * d_w rounded to f32 (for the min lanes -d_x * dmin_w)
-                            const uint64_t d01 = mul2(f2pack(y4.x, y4.y), xs2), d23 = mul2(f2pack(y4.z, y4.w), xs2);
-                            accA[2 * i] = fma2(d01, f2pack(__uint_as_float(sa[4 * i]), __uint_as_float(sa[4 * i + 1])), accA[2 * i]);
-                            accB[2 * i] = fma2(d01, f2pack(__uint_as_float(sbv[4 * i]), __uint_as_float(sbv[4 * i + 1])), accB[2 * i]);
-                            accA[2 * i + 1] = fma2(d23, f2pack(__uint_as_float(sa[4 * i + 2]), __uint_as_float(sa[4 * i + 3])),
-                                                   accA[2 * i + 1]);
-                            accB[2 * i + 1] = fma2(d23, f2pack(__uint_as_float(sbv[4 * i + 2]), __uint_as_float(sbv[4 * i + 3])),
-                                                   accB[2 * i + 1]);
+                        for (int hh = 0; hh < kLxEpiCols / 8; ++hh) {
+                            uint32_t sa[8], sbv[8];
+                            tmem_ld8x2u(dcol + 8 * hh, dcol + 64 + 8 * hh, sa, sbv);
+                            if (et == 0 && hh == 0) XTRACE(it, 15);
+#pragma unroll
+                            for (int i = 0; i < 2; ++i) {
+                                const float4 y4 = yd[2 * hh + i];
+                                // d = d_x * d_w rounded to f32 (for the min lanes -d_x * dmin_w)
+                                const uint64_t d01 = mul2(f2pack(y4.x, y4.y), xs2), d23 = mul2(f2pack(y4.z, y4.w), xs2);
+                                const int k0 = 4 * hh + 2 * i;
+                                accA[k0] = fma2(d01, f2pack(__uint_as_float(sa[4 * i]), __uint_as_float(sa[4 * i + 1])), accA[k0]);
+                                accB[k0] = fma2(d01, f2pack(__uint_as_float(sbv[4 * i]), __uint_as_float(sbv[4 * i + 1])), accB[k0]);
+                                accA[k0 + 1] = fma2(d23, f2pack(__uint_as_float(sa[4 * i + 2]), __uint_as_float(sa[4 * i + 3])),
+                                                    accA[k0 + 1]);
+                                accB[k0 + 1] = fma2(d23, f2pack(__uint_as_float(sbv[4 * i + 2]), __uint_as_float(sbv[4 * i + 3])),
+                                                    accB[k0 + 1]);
+                            }
                         }
                     }
                     tc_fence_before();
@@ -628,7 +701,7 @@ __global__ void __launch_bounds__(kLxThreads, 1) pf_gate_up_lx_kernel(PfParams p
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == kPfMmaWarp) {
+    if (warp == kLxMmaWarp) {
         tc_fence_after();
         tmem_dealloc_warp(tmem, kLxTmemCols);
     }

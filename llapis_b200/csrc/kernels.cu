@@ -2320,6 +2320,9 @@ extern "C" int moeb_mdtrace_read(void *host, size_t bytes, void *host_u, size_t 
     if (cudaMemcpyFromSymbol(host, moeb::g_mdtrace, bytes) != cudaSuccess) return -3;
     return cudaMemcpyFromSymbol(host_u, moeb::g_mdutrace, bytes_u) == cudaSuccess ? 0 : -3;
 }
+extern "C" int moeb_xtrace_read(void *host, size_t bytes) {
+    return cudaMemcpyFromSymbol(host, moeb::g_xtrace, bytes) == cudaSuccess ? 0 : -3;
+}
 extern "C" int moeb_utrace_read(void *host, size_t bytes) {
     return cudaMemcpyFromSymbol(host, moeb::g_utrace, bytes) == cudaSuccess ? 0 : -3;
 }

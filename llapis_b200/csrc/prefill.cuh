@@ -105,6 +105,9 @@ __device__ __forceinline__ void tmem_ld16x2(uint32_t ta, uint32_t tb, float (&va
 #ifdef MOEB_TRACE
 __device__ unsigned long long g_ptrace[2][3][256][3];
 __device__ unsigned long long g_utrace[32][16];
+__device__ unsigned long long g_xtrace[256][16];
+#define XTRACE(idx, f) \
+    if (blockIdx.x == 0 && (idx) < 256) g_xtrace[idx][f] = clock64();
 #define PTRACE(k, role, idx, f) \
     if (blockIdx.x == 0 && (idx) < 256) g_ptrace[k][role][idx][f] = clock64();
 #define UTRACE(u, f) \
@@ -112,6 +115,7 @@ __device__ unsigned long long g_utrace[32][16];
 #else
 #define PTRACE(k, role, idx, f)
 #define UTRACE(u, f)
+#define XTRACE(idx, f)
 #endif
 
 // ---------------------------------------------------------------- shapes of the tensor-core kernels
