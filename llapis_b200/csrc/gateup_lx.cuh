@@ -35,7 +35,8 @@ constexpr int kLxMinCores = 4;              // K = 32 per min pass step (2 lanes
 constexpr int kLxBStageBytes = (kLxN / 8) * kLxMainCores * 128;   // 8 KB: one unit's half of a main image
 constexpr int kLxEpiWarps = 8;              // two per TMEM lane quadrant, 32 columns each
 constexpr int kLxEpiCols = kLxN / (kLxEpiWarps / 4);
-constexpr int kLxConvWarps = 8;             // two per TMEM lane quadrant, on alternate steps
+constexpr int kLxConvGroups = 2;            // converter groups of four warps (one per TMEM lane quadrant),
+constexpr int kLxConvWarps = 4 * kLxConvGroups;   // group g converting steps g, g + groups, ...
 constexpr int kLxMmaWarp = kLxConvWarps;
 constexpr int kLxProdWarp = kLxMmaWarp + 1;
 constexpr int kLxEpiWarp0 = kLxProdWarp + 1;
@@ -179,6 +180,13 @@ __device__ __forceinline__ bool lx_wait(uint64_t *bar, uint32_t parity, volatile
 }
 __device__ __forceinline__ bool lx_wait_warp(uint64_t *bar, uint32_t parity, volatile int32_t *abort) {
     return __all_sync(0xffffffffu, lx_wait(bar, parity, abort));
+}
+// One lane of a converged warp (elect.sync): the single-thread issue points (MMA, commit, bulk copy)
+// sit inside warp-uniform loops, so their operands stay in uniform registers.
+__device__ __forceinline__ bool elect_one() {
+    uint32_t pred;
+    asm volatile("{\n .reg .b32 r;\n .reg .pred p;\n elect.sync r|p, 0xffffffff;\n selp.u32 %0, 1, 0, p;\n}\n" : "=r"(pred));
+    return pred != 0;
 }
 
 // ---------------------------------------------------------------- 2D tensor-map copy (no multicast)
@@ -410,7 +418,7 @@ __global__ void __launch_bounds__(kLxThreads, 1) pf_gate_up_lx_kernel(PfParams p
     if (tid == 0) {
         for (int i = 0; i < kLxRing; ++i) {
             mbar_init(&S.bfull[i], 1);
-            mbar_init(&S.afull[i], kPfConvWarps);
+            mbar_init(&S.afull[i], 4);
             mbar_init(&S.opfree[i], 1);
         }
         for (int b = 0; b < kLxDBufs; ++b) {
@@ -440,8 +448,8 @@ __global__ void __launch_bounds__(kLxThreads, 1) pf_gate_up_lx_kernel(PfParams p
         const uint32_t ta = tmem + ((uint32_t)(32 * qd) << 16) + kLxColA;
         LxIter cur;
         cur.start(p, units, n_mb, r);
-        if (grp == 1 && cur.ok) cur.advance(p, units, n_mb, nsb, r);
-        for (int it = grp; cur.ok && !warp_aborted(abort); it += 2) {
+        for (int g = 0; g < grp && cur.ok; ++g) cur.advance(p, units, n_mb, nsb, r);
+        for (int it = grp; cur.ok && !warp_aborted(abort); it += kLxConvGroups) {
             const int ab = it % kLxRing;
             if (tid == 0) PTRACE(0, 0, it, 0);
             if (it >= kLxRing && !lx_wait_warp(&S.opfree[ab], ((it / kLxRing) - 1) & 1, abort)) break;
@@ -491,6 +499,8 @@ __global__ void __launch_bounds__(kLxThreads, 1) pf_gate_up_lx_kernel(PfParams p
                 lx_a_iq2xxs_lane(blk, lx_first_lane(cur.pass) + 4, o + 16);
             }
             if (lane == 0 && grp == 0) XTRACE(it, 8 + qd);
+            // the MMA thread waits on afull only: every converter sees the step's B image land first
+            if (cur.type != T_Q4_K && !lx_wait_warp(&S.bfull[ab], (it / kLxRing) & 1, abort)) break;
             if (mn) {
                 uint32_t o16[16];
 #pragma unroll
@@ -505,33 +515,33 @@ __global__ void __launch_bounds__(kLxThreads, 1) pf_gate_up_lx_kernel(PfParams p
             if (lane == 0) mbar_arrive(&S.afull[ab]);
             if (lane == 0 && grp == 0 && qd > 0) XTRACE(it, qd);
             if (tid == 0) PTRACE(0, 0, it, 2);
-            cur.advance(p, units, n_mb, nsb, r);
-            if (cur.ok) cur.advance(p, units, n_mb, nsb, r);
+            for (int g = 0; g < kLxConvGroups && cur.ok; ++g) cur.advance(p, units, n_mb, nsb, r);
         }
     } else if (warp == kLxMmaWarp) {
-        // ------------------------------------------------ MMA issue (one thread)
-        if (lane == 0) {
-            LxIter s;
-            s.start(p, units, n_mb, -1);
-            for (int it = 0; s.ok && !*abort; ++it) {
-                const int ab = it % kLxRing, db = it % kLxDBufs;
-                PTRACE(0, 1, it, 0);
-                if (!lx_wait(&S.afull[ab], (it / kLxRing) & 1, abort) || !lx_wait(&S.bfull[ab], (it / kLxRing) & 1, abort) ||
-                    (it >= kLxDBufs && !lx_wait(&S.dempty[db], ((it / kLxDBufs) - 1) & 1, abort)))
-                    break;
-                PTRACE(0, 1, it, 1);
-                tc_fence_after();
-                const uint32_t idesc = umma_idesc_f16(kPfM, s.N);
-                const uint32_t a0 = tmem + kLxColA + 32 * ab, d0 = tmem + kLxColD + 128 * db;
-                const uint32_t b0 = smem_addr(S.b[ab]);
+        // ------------------------------------------------ MMA issue: a warp-uniform loop, one elected
+        // lane issues. The converters arrive on afull only after they saw the step's bfull, so afull
+        // alone says that both operands are in place.
+        LxIter s;
+        s.start(p, units, n_mb, -1);
+        int it = 0;
+        for (; s.ok && !warp_aborted(abort); ++it) {
+            const int ab = it % kLxRing, db = it % kLxDBufs;
+            if (lane == 0) PTRACE(0, 1, it, 0);
+            if (!lx_wait_warp(&S.afull[ab], (it / kLxRing) & 1, abort) ||
+                (it >= kLxDBufs && !lx_wait_warp(&S.dempty[db], ((it / kLxDBufs) - 1) & 1, abort)))
+                break;
+            if (lane == 0) PTRACE(0, 1, it, 1);
+            tc_fence_after();
+            const uint32_t idesc = umma_idesc_f16(kPfM, s.N);
+            const uint32_t a0 = tmem + kLxColA + 32 * ab, d0 = tmem + kLxColD + 128 * db;
+            const uint32_t b0 = smem_addr(S.b[ab]);
+            if (elect_one()) {
                 if (s.pass < 4) {   // lane a: K = 32 into d0, lane b: K = 32 into d0 + 64
                     const uint32_t sbo = kLxMainCores * 128;
                     umma_f16_ts(d0, a0, umma_sdesc(b0, 128, sbo), idesc, 0);
-                    XTRACE(it, 12);
                     umma_f16_ts(d0, a0 + 8, umma_sdesc(b0 + 256, 128, sbo), idesc, 1);
                     umma_f16_ts(d0 + 64, a0 + 16, umma_sdesc(b0 + 512, 128, sbo), idesc, 0);
                     umma_f16_ts(d0 + 64, a0 + 24, umma_sdesc(b0 + 768, 128, sbo), idesc, 1);
-                    XTRACE(it, 13);
                 } else {            // the two min lanes, K = 16 each
                     const uint32_t sbo = kLxMinCores * 128;
                     umma_f16_ts(d0, a0, umma_sdesc(b0, 128, sbo), idesc, 0);
@@ -539,25 +549,27 @@ __global__ void __launch_bounds__(kLxThreads, 1) pf_gate_up_lx_kernel(PfParams p
                 }
                 umma_commit(&S.opfree[ab]);
                 umma_commit(&S.dfull[db]);
-                XTRACE(it, 14);
-                PTRACE(0, 1, it, 2);
-                s.advance(p, units, n_mb, nsb, -1);
             }
-            umma_commit(&S.done);
-            mbar_wait(&S.done, 0);   // issued MMAs always complete; TMEM is freed only after them
+            __syncwarp();
+            if (lane == 0) PTRACE(0, 1, it, 2);
+            s.advance(p, units, n_mb, nsb, -1);
         }
+        // issued MMAs always complete; TMEM is freed only after them
+        if (elect_one()) umma_commit(&S.done);
         __syncwarp();
+        mbar_wait(&S.done, 0);
     } else if (warp == kLxProdWarp) {
-        // ------------------------------------------------ B operand images, bulk-copied up to kLxRing steps ahead
-        if (lane == 0) {
-            LxIter s;
-            s.start(p, units, n_mb, -1);
-            for (int it = 0; s.ok && !*abort; ++it) {
-                const int bs = it % kLxRing;
-                if (it >= kLxRing && !lx_wait(&S.opfree[bs], ((it / kLxRing) - 1) & 1, abort)) break;
-                const int ncores = s.pass >= 4 ? kLxMinCores : kLxMainCores;
-                const uint32_t bytes = (uint32_t)(s.N / 8) * ncores * 128;
-                const bool q4 = s.type == T_Q4_K;
+        // ------------------------------------------------ B operand images (and Q4_K raw rows), bulk-copied
+        // up to kLxRing steps ahead by one elected lane of a warp-uniform loop
+        LxIter s;
+        s.start(p, units, n_mb, -1);
+        for (int it = 0; s.ok && !warp_aborted(abort); ++it) {
+            const int bs = it % kLxRing;
+            if (it >= kLxRing && !lx_wait_warp(&S.opfree[bs], ((it / kLxRing) - 1) & 1, abort)) break;
+            const int ncores = s.pass >= 4 ? kLxMinCores : kLxMainCores;
+            const uint32_t bytes = (uint32_t)(s.N / 8) * ncores * 128;
+            const bool q4 = s.type == T_Q4_K;
+            if (elect_one()) {
                 mbar_expect_tx(&S.bfull[bs], bytes + (q4 ? (uint32_t)kLxRawBytes : 0u));
                 bulk_g2s(S.b[bs],
                          p.bimg + (size_t)s.ti * lx_tile_bytes(nsb) + lx_image_off(nsb, s.pass, s.sb) +
@@ -570,10 +582,10 @@ __global__ void __launch_bounds__(kLxThreads, 1) pf_gate_up_lx_kernel(PfParams p
                     tma_load_2d(S.raw[bs] + 64 * B_Q4_K, map, s.sb * B_Q4_K, y0 + p.nff, &S.bfull[bs]);
                 }
                 XTRACE(it, 0);
-                s.advance(p, units, n_mb, nsb, -1);
             }
+            __syncwarp();
+            s.advance(p, units, n_mb, nsb, -1);
         }
-        __syncwarp();
     } else {
         // ------------------------------------------------ epilogue: the lanes' f32 chains
         const int ew = warp - kLxEpiWarp0, et = tid - kLxEpiWarp0 * 32;
