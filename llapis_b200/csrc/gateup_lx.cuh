@@ -37,10 +37,13 @@ constexpr int kLxEpiWarps = 8;              // two per TMEM lane quadrant, 32 co
 constexpr int kLxEpiCols = kLxN / (kLxEpiWarps / 4);
 constexpr int kLxConvGroups = 2;            // converter groups of four warps (one per TMEM lane quadrant),
 constexpr int kLxConvWarps = 4 * kLxConvGroups;   // group g converting steps g, g + groups, ...
-constexpr int kLxMmaWarp = kLxConvWarps;
-constexpr int kLxProdWarp = kLxMmaWarp + 1;
-constexpr int kLxEpiWarp0 = kLxProdWarp + 1;
-constexpr int kLxThreads = (kLxEpiWarp0 + kLxEpiWarps) * 32;
+constexpr int kLxEpiWarp0 = kLxConvWarps;
+// MMA issue and operand copies: kLxIssue warps each, taking alternate steps, so that their issue
+// work is spread over the four SM sub-partitions instead of slowing the epilogue warps of two
+constexpr int kLxIssue = 2;
+constexpr int kLxMmaWarp = kLxEpiWarp0 + kLxEpiWarps;
+constexpr int kLxProdWarp = kLxMmaWarp + kLxIssue;
+constexpr int kLxThreads = (kLxProdWarp + kLxIssue) * 32;
 // TMEM: three accumulator buffers of 2 lanes x 64 columns, then four A buffers of 32 columns; the
 // A buffers and the B stages share one ring index (step % kLxRing) and one "operands free" barrier
 constexpr int kLxDBufs = 3, kLxRing = 4;
@@ -425,7 +428,7 @@ __global__ void __launch_bounds__(kLxThreads, 1) pf_gate_up_lx_kernel(PfParams p
             mbar_init(&S.dfull[b], 1);
             mbar_init(&S.dempty[b], kLxEpiWarps);
         }
-        mbar_init(&S.done, 1);
+        mbar_init(&S.done, kLxIssue);
         mbar_init(&S.epibar, kLxEpiWarps);
         S.abort = 0;
         fence_mbar_init();
@@ -460,7 +463,6 @@ __global__ void __launch_bounds__(kLxThreads, 1) pf_gate_up_lx_kernel(PfParams p
             if (cur.type == T_Q4_K) {
                 // the step's raw blocks (and B image) have landed in ring slot ab
                 if (!lx_wait_warp(&S.bfull[ab], (it / kLxRing) & 1, abort)) break;
-                if (lane == 0 && grp == 0) XTRACE(it, 4 + qd);
                 const uint32_t *w = reinterpret_cast<const uint32_t *>(S.raw[ab] + r * B_Q4_K);
                 uint32_t scw[2], mnw[2];
                 q4k_scale_words(w[1], w[2], w[3], scw, mnw);
@@ -498,7 +500,6 @@ __global__ void __launch_bounds__(kLxThreads, 1) pf_gate_up_lx_kernel(PfParams p
                 lx_a_iq2xxs_lane(blk, lx_first_lane(cur.pass), o);
                 lx_a_iq2xxs_lane(blk, lx_first_lane(cur.pass) + 4, o + 16);
             }
-            if (lane == 0 && grp == 0) XTRACE(it, 8 + qd);
             // the MMA thread waits on afull only: every converter sees the step's B image land first
             if (cur.type != T_Q4_K && !lx_wait_warp(&S.bfull[ab], (it / kLxRing) & 1, abort)) break;
             if (mn) {
@@ -517,19 +518,22 @@ __global__ void __launch_bounds__(kLxThreads, 1) pf_gate_up_lx_kernel(PfParams p
             if (tid == 0) PTRACE(0, 0, it, 2);
             for (int g = 0; g < kLxConvGroups && cur.ok; ++g) cur.advance(p, units, n_mb, nsb, r);
         }
-    } else if (warp == kLxMmaWarp) {
-        // ------------------------------------------------ MMA issue: a warp-uniform loop, one elected
-        // lane issues. The converters arrive on afull only after they saw the step's bfull, so afull
-        // alone says that both operands are in place.
+    } else if (warp >= kLxMmaWarp && warp < kLxProdWarp) {
+        // ------------------------------------------------ MMA issue: warp m takes steps m, m + kLxIssue, ...
+        // in a warp-uniform loop, one elected lane issues (and commits its own MMAs). The converters
+        // arrive on afull only after they saw the step's bfull, so afull alone says that both operands
+        // are in place.
+        const int m = warp - kLxMmaWarp;
         LxIter s;
         s.start(p, units, n_mb, -1);
-        int it = 0;
-        for (; s.ok && !warp_aborted(abort); ++it) {
+        for (int g = 0; g < m && s.ok; ++g) s.advance(p, units, n_mb, nsb, -1);
+        for (int it = m; s.ok && !warp_aborted(abort); it += kLxIssue) {
             const int ab = it % kLxRing, db = it % kLxDBufs;
             if (lane == 0) PTRACE(0, 1, it, 0);
-            if (!lx_wait_warp(&S.afull[ab], (it / kLxRing) & 1, abort) ||
-                (it >= kLxDBufs && !lx_wait_warp(&S.dempty[db], ((it / kLxDBufs) - 1) & 1, abort)))
-                break;
+            if (!lx_wait_warp(&S.afull[ab], (it / kLxRing) & 1, abort)) break;
+            if (lane == 0) XTRACE(it, 12);
+            if (it >= kLxDBufs && !lx_wait_warp(&S.dempty[db], ((it / kLxDBufs) - 1) & 1, abort)) break;
+            if (lane == 0) XTRACE(it, 13);
             if (lane == 0) PTRACE(0, 1, it, 1);
             tc_fence_after();
             const uint32_t idesc = umma_idesc_f16(kPfM, s.N);
@@ -552,18 +556,20 @@ __global__ void __launch_bounds__(kLxThreads, 1) pf_gate_up_lx_kernel(PfParams p
             }
             __syncwarp();
             if (lane == 0) PTRACE(0, 1, it, 2);
-            s.advance(p, units, n_mb, nsb, -1);
+            for (int g = 0; g < kLxIssue && s.ok; ++g) s.advance(p, units, n_mb, nsb, -1);
         }
-        // issued MMAs always complete; TMEM is freed only after them
+        // issued MMAs always complete; TMEM is freed only after them (both issuers' commits)
         if (elect_one()) umma_commit(&S.done);
         __syncwarp();
         mbar_wait(&S.done, 0);
-    } else if (warp == kLxProdWarp) {
+    } else if (warp >= kLxProdWarp) {
         // ------------------------------------------------ B operand images (and Q4_K raw rows), bulk-copied
-        // up to kLxRing steps ahead by one elected lane of a warp-uniform loop
+        // up to kLxRing steps ahead; warp m takes steps m, m + kLxIssue, ..., one elected lane issuing
+        const int m = warp - kLxProdWarp;
         LxIter s;
         s.start(p, units, n_mb, -1);
-        for (int it = 0; s.ok && !warp_aborted(abort); ++it) {
+        for (int g = 0; g < m && s.ok; ++g) s.advance(p, units, n_mb, nsb, -1);
+        for (int it = m; s.ok && !warp_aborted(abort); it += kLxIssue) {
             const int bs = it % kLxRing;
             if (it >= kLxRing && !lx_wait_warp(&S.opfree[bs], ((it / kLxRing) - 1) & 1, abort)) break;
             const int ncores = s.pass >= 4 ? kLxMinCores : kLxMainCores;
@@ -584,7 +590,7 @@ __global__ void __launch_bounds__(kLxThreads, 1) pf_gate_up_lx_kernel(PfParams p
                 XTRACE(it, 0);
             }
             __syncwarp();
-            s.advance(p, units, n_mb, nsb, -1);
+            for (int g = 0; g < kLxIssue && s.ok; ++g) s.advance(p, units, n_mb, nsb, -1);
         }
     } else {
         // ------------------------------------------------ epilogue: the lanes' f32 chains
@@ -661,6 +667,7 @@ __global__ void __launch_bounds__(kLxThreads, 1) pf_gate_up_lx_kernel(PfParams p
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&S.dempty[db]);
+                    if (lane == 0) XTRACE(it, 4 + ew);
                     if (et == 0) PTRACE(0, 2, it, 2);
                 }
                 if (!ok || !live) continue;
