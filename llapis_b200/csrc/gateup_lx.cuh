@@ -31,7 +31,6 @@ namespace moeb {
 
 constexpr int kLxN = 64;                    // pairs per work unit (MMA N <= 64)
 constexpr int kLxMainCores = 8;             // K = 64 per main pass step (2 lanes x 32), in 8-value cores
-constexpr int kLxMinCores = 4;              // K = 32 per min pass step (2 lanes x 16)
 constexpr int kLxBStageBytes = (kLxN / 8) * kLxMainCores * 128;   // 8 KB: one unit's half of a main image
 constexpr int kLxEpiWarps = 8;              // two per TMEM lane quadrant, 32 columns each
 constexpr int kLxEpiCols = kLxN / (kLxEpiWarps / 4);
@@ -49,8 +48,7 @@ constexpr int kLxThreads = (kLxProdWarp + kLxIssue) * 32;
 constexpr int kLxDBufs = 3, kLxRing = 4;
 constexpr uint32_t kLxColD = 0, kLxColA = 128 * kLxDBufs, kLxTmemCols = 512;
 static_assert(kLxColA + 32 * kLxRing <= kLxTmemCols, "TMEM budget");
-static_assert(kLxImgMain == (kPrefillTile / 8) * kLxMainCores * 128 && kLxImgMin == (kPrefillTile / 8) * kLxMinCores * 128,
-              "image sizes in params.h");
+static_assert(kLxImgMain == (kPrefillTile / 8) * kLxMainCores * 128, "image size in params.h");
 
 // the two reference lanes of main pass p: (0,4), (2,6), (1,5), (3,7)
 MOEB_HD constexpr int lx_first_lane(int pass) { return pass == 0 ? 0 : pass == 1 ? 2 : pass == 2 ? 1 : 3; }
@@ -68,7 +66,7 @@ struct LxSmem {
     uint8_t raw[kLxRing][kLxRawBytes];       // Q4_K units: the step's super-block of the unit's 128 rows
     float held[2][kLxN][kPfM];               // the two held partial sums of each (row, column), column-major
     float dxs[kPrefillMaxSb][kLxN];          // Q8_K scale of each unit column, per super-block
-    float2 xdt[kPrefillMaxSb][kPfM];         // (d, -dmin) of each unit row, per super-block
+    float xdt[kPrefillMaxSb][kPfM];          // d_w of each unit row, per super-block
     uint64_t bfull[kLxRing], afull[kLxRing], opfree[kLxRing], dfull[kLxDBufs], dempty[kLxDBufs], done, epibar;
     uint32_t tmem;
     int32_t abort;
@@ -279,11 +277,10 @@ __device__ __forceinline__ void lx_a_iq2xxs_lane(const uint8_t *blk, int L, uint
 }
 
 // ---------------------------------------------------------------- B operand images
-// One CTA per (tile, super-block), thread = (tile row c, half h). Half 0 writes main passes 0, 1
-// (lanes (0,4), (2,6)) and min pass 4 (lanes 0, 2); half 1 writes main passes 2, 3 and min pass 5.
-// A main image row holds lane a's 32 values (cores 0-3) then lane b's (cores 4-7), each in K order
-// 4j + e; a min image row holds [bsums 4m..4m+3, 0 x 12] for its two lanes m (cores 0-1, 2-3).
-// Rows n..N-1 (padding up to a multiple of 16) are zero. Half 0 also writes the row's Q8_K scale.
+// One CTA per (tile, super-block), thread = (tile row c, half h): half 0 writes main passes 0, 1
+// (lanes (0,4), (2,6)), half 1 passes 2, 3 ((1,5), (3,7)). An image row holds lane a's 32 values
+// (cores 0-3) then lane b's (cores 4-7), each in K order 4j + e. Rows n..N-1 (padding up to a
+// multiple of 16) are zero. Half 0 also writes the row's Q8_K scale.
 template <int PASS>
 __device__ __forceinline__ void lx_b_main_row(const uint4 (&v)[16], uint8_t *img, int c) {
 #pragma unroll
@@ -315,7 +312,6 @@ __global__ void __launch_bounds__(256) pf_gather_lx_kernel(PfParams p) {
     if (c >= N) return;
     uint8_t *base = p.bimg + (size_t)ti * lx_tile_bytes(nsb);
     uint8_t *im0 = base + lx_image_off(nsb, 2 * h, sb), *im1 = base + lx_image_off(nsb, 2 * h + 1, sb);
-    uint8_t *imm = base + lx_image_off(nsb, 4 + h, sb);
     float *dxt = p.dxt + ((size_t)ti * nsb + sb) * kPfN;
     const uint4 z = make_uint4(0u, 0u, 0u, 0u);
     if (c >= tl.n) {
@@ -324,8 +320,6 @@ __global__ void __launch_bounds__(256) pf_gather_lx_kernel(PfParams p) {
             *reinterpret_cast<uint4 *>(im0 + canon_off(c, j, kLxMainCores)) = z;
             *reinterpret_cast<uint4 *>(im1 + canon_off(c, j, kLxMainCores)) = z;
         }
-#pragma unroll
-        for (int j = 0; j < kLxMinCores; ++j) *reinterpret_cast<uint4 *>(imm + canon_off(c, j, kLxMinCores)) = z;
         if (h == 0) dxt[c] = 0.f;
         return;
     }
@@ -342,17 +336,123 @@ __global__ void __launch_bounds__(256) pf_gather_lx_kernel(PfParams p) {
         lx_b_main_row<2>(v, im0, c);
         lx_b_main_row<3>(v, im1, c);
     }
-    // min pass 4 + h: lanes m = h and m = h + 2, each [bsums 4m .. 4m + 3, 0 x 12] (exact in fp16:
-    // |bsum| <= 16 x 127)
-    const int16_t *bs16 = p.xbs + ((size_t)t * nsb + sb) * 16;
+}
+
+// ---------------------------------------------------------------- Q4_K min term, M = (m0 + m2) + (m1 + m3)
+// The four min lanes of ggml_vec_dot_q4_K_q8_K (x86/quants.c:1900): per super-block, lane m is the
+// integer mins[2m] * q8s[2m] + mins[2m+1] * q8s[2m+1] (q8s[j] = bsums[2j] + bsums[2j+1]), fused into
+// its own f32 chain with dmin = -d_x * dmin_w; the four chains reduce as (m0 + m2) + (m1 + m3), which
+// the dot adds last. This kernel computes M for every (row, pair) of the Q4_K tiles and stores it in
+// hbuf, where the grouped GEMM's epilogue adds the main lanes' sum to it.
+//
+// The integers come from mma.sync m16n8k16 (fp16 operands, f32 accumulators, all exact): A row r holds
+// mins[j] twice at K = 2j, 2j + 1 (j < 8), B column c of group m holds bsums 4m..4m+3 at K = 4m..4m+3 and
+// zeros elsewhere, so one MMA per group gives lane m's integer for a 16 x 8 block, and the chains stay
+// in registers. CTA = (tile, 64 rows), four warps of 16 rows, 32 pairs per chunk (four n-blocks).
+constexpr int kMinRows = 64, kMinCols = 32;
+__device__ __forceinline__ void mma_f16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                              uint32_t b0, uint32_t b1) {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                 "{%10,%10,%10,%10};"
+                 : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.f));
+}
+
+__global__ void __launch_bounds__(128) pf_q4k_min_kernel(PfParams p) {
+    __shared__ uint2 s_mins[kPrefillMaxSb][kMinRows];             // the row's 8 mins (bytes)
+    __shared__ float s_ndmin[kPrefillMaxSb][kMinRows];            // -dmin_w
+    __shared__ uint32_t s_bs[kPrefillMaxSb][kMinCols][8];         // the pair's 16 bsums as fp16 pairs
+    __shared__ float s_dx[kPrefillMaxSb][kMinCols];               // the pair's Q8_K scale
+    pdl_wait();
+    pdl_launch_dependents();
+    const int ti = blockIdx.x, rb = blockIdx.y;
+    if (ti >= *p.n_tiles) return;
+    const PfTile tl = p.tiles[ti];
+    const bool c1 = tl.cls != 0;
+    PoolView pv;
+    pv.w = c1 ? p.gu[1].w : p.gu[0].w;
+    pv.type = c1 ? p.gu[1].type : p.gu[0].type;
+    pv.ptrs = c1 ? p.gu[1].ptrs : p.gu[0].ptrs;
+    if (pv.type != T_Q4_K) return;
+    const int nsb = p.d / QK_K, gu_rows = 2 * p.nff, row0 = rb * kMinRows;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t4 = lane & 3;
+    const uint8_t *base = tile_rows(pv, tl.widx, gu_rows, p.d);
+    const size_t rbytes = row_bytes(T_Q4_K, p.d);
+    for (int i = tid; i < nsb * kMinRows; i += blockDim.x) {
+        const int sb = i / kMinRows, r = i - sb * kMinRows;
+        const uint4 h = __ldg(reinterpret_cast<const uint4 *>(base + (size_t)(row0 + r) * rbytes + (size_t)sb * B_Q4_K));
+        uint32_t sc[2], mn[2];
+        q4k_scale_words(h.y, h.z, h.w, sc, mn);
+        s_mins[sb][r] = make_uint2(mn[0], mn[1]);
+        s_ndmin[sb][r] = -h2f((uint16_t)(h.x >> 16));
+    }
+    const int ra = 16 * warp + g, rbw = ra + 8;   // this thread's two rows (of the CTA's 64)
+    for (int c0 = 0; c0 < tl.n; c0 += kMinCols) {
+        __syncthreads();   // the row table is written; the previous chunk's column table is consumed
+        for (int i = tid; i < nsb * kMinCols; i += blockDim.x) {
+            const int sb = i / kMinCols, c = i - sb * kMinCols;
+            uint32_t w[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+            float dx = 0.f;
+            if (c0 + c < tl.n) {
+                const int t = p.perm[tl.slot0 + c0 + c] / p.k;
+                const uint4 *bs = reinterpret_cast<const uint4 *>(p.xbs + ((size_t)t * nsb + sb) * 16);
+                const uint4 u0 = __ldg(bs), u1 = __ldg(bs + 1);
+                const uint32_t raw[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
 #pragma unroll
-    for (int i = 0; i < 2; ++i) {
-        const int m = h + 2 * i;
-        const uint2 b = __ldg(reinterpret_cast<const uint2 *>(bs16 + 4 * m));
-        const uint32_t w0 = pack_h2i((int)(int16_t)(b.x & 0xffffu), (int)(int16_t)(b.x >> 16));
-        const uint32_t w1 = pack_h2i((int)(int16_t)(b.y & 0xffffu), (int)(int16_t)(b.y >> 16));
-        *reinterpret_cast<uint4 *>(imm + canon_off(c, 2 * i, kLxMinCores)) = make_uint4(w0, w1, 0u, 0u);
-        *reinterpret_cast<uint4 *>(imm + canon_off(c, 2 * i + 1, kLxMinCores)) = z;
+                for (int j = 0; j < 8; ++j)   // |bsum| <= 16 x 127: exact in fp16
+                    w[j] = pack_h2i((int)(int16_t)(raw[j] & 0xffffu), (int)(int16_t)(raw[j] >> 16));
+                dx = p.xd[(size_t)t * nsb + sb];
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) s_bs[sb][c][j] = w[j];
+            s_dx[sb][c] = dx;
+        }
+        __syncthreads();
+        float acc[4][4][4];   // [n-block][lane m][fragment element]
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+            for (int m = 0; m < 4; ++m)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) acc[j][m][e] = 0.f;
+        for (int sb = 0; sb < nsb; ++sb) {
+            const uint2 ma = s_mins[sb][ra], mb = s_mins[sb][rbw];
+            const uint32_t wa[2] = {ma.x, ma.y}, wb[2] = {mb.x, mb.y};
+            // A: row g K 2t4, 2t4+1 = mins[t4]; K 2t4+8, 2t4+9 = mins[t4+4] (rows g + 8 likewise)
+            const uint32_t a0 = h2u(byte_h2(wa, t4)), a1 = h2u(byte_h2(wb, t4));
+            const uint32_t a2 = h2u(byte_h2(wa, t4 + 4)), a3 = h2u(byte_h2(wb, t4 + 4));
+            const float nda = s_ndmin[sb][ra], ndb = s_ndmin[sb][rbw];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                // B: column g of n-block j, K 2t4, 2t4+1 (bsums 2t4, 2t4+1) and K 2t4+8, 2t4+9; group m
+                // keeps only its K range 4m..4m+3
+                const uint32_t p0 = s_bs[sb][8 * j + g][t4], p1 = s_bs[sb][8 * j + g][t4 + 4];
+                const float dx0 = s_dx[sb][8 * j + 2 * t4], dx1 = s_dx[sb][8 * j + 2 * t4 + 1];
+                // dmin = -d_x * dmin_w per (row, pair), rounded to f32
+                const float dm[4] = {__fmul_rn(dx0, nda), __fmul_rn(dx1, nda), __fmul_rn(dx0, ndb), __fmul_rn(dx1, ndb)};
+                const bool lo = t4 < 2;
+#pragma unroll
+                for (int m = 0; m < 4; ++m) {
+                    const uint32_t b0 = m < 2 && (lo == (m == 0)) ? p0 : 0u;
+                    const uint32_t b1 = m >= 2 && (lo == (m == 2)) ? p1 : 0u;
+                    float dd[4];
+                    mma_f16_16816(dd, a0, a1, a2, a3, b0, b1);
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) acc[j][m][e] = __fmaf_rn(dm[e], dd[e], acc[j][m][e]);
+                }
+            }
+        }
+        // fragment element e: row (e < 2 ? g : g + 8), pair 2 t4 + (e & 1) of the n-block
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int c = c0 + 8 * j + 2 * t4 + (e & 1);
+                if (c >= tl.n) continue;
+                const float M = __fadd_rn(__fadd_rn(acc[j][0][e], acc[j][2][e]), __fadd_rn(acc[j][1][e], acc[j][3][e]));
+                const int wr = row0 + (e < 2 ? ra : rbw);
+                p.hbuf[(size_t)(tl.slot0 + c) * gu_rows + wr] = M;
+            }
     }
 }
 
@@ -369,7 +469,7 @@ __device__ __forceinline__ bool lx_unit(const PfParams &p, int u, int n_mb, int 
     tl = p.tiles[ti];
     return 64 * nh < tl.n;
 }
-__device__ __forceinline__ int lx_passes(int type) { return type == T_Q4_K ? 6 : 4; }
+__device__ __forceinline__ int lx_passes(int) { return 4; }
 
 struct LxIter {
     int u, ti, mb, nh, pass, sb, np, nc, N, type;
@@ -458,7 +558,6 @@ __global__ void __launch_bounds__(kLxThreads, 1) pf_gate_up_lx_kernel(PfParams p
             if (it >= kLxRing && !lx_wait_warp(&S.opfree[ab], ((it / kLxRing) - 1) & 1, abort)) break;
             if (tid == 0) PTRACE(0, 0, it, 1);
             tc_fence_after();
-            const bool mn = cur.pass >= 4;
             uint32_t o[32];
             if (cur.type == T_Q4_K) {
                 // the step's raw blocks (and B image) have landed in ring slot ab
@@ -466,30 +565,18 @@ __global__ void __launch_bounds__(kLxThreads, 1) pf_gate_up_lx_kernel(PfParams p
                 const uint32_t *w = reinterpret_cast<const uint32_t *>(S.raw[ab] + r * B_Q4_K);
                 uint32_t scw[2], mnw[2];
                 q4k_scale_words(w[1], w[2], w[3], scw, mnw);
-                if (!mn) {
-                    // per sub-block j: (sc_j, sc_j) and (-1024 sc_j, -1024 sc_j) for scale4, shared by both lanes
-                    __half2 s2[8], ns2[8];
+                // per sub-block j: (sc_j, sc_j) and (-1024 sc_j, -1024 sc_j) for scale4, shared by both lanes
+                __half2 s2[8], ns2[8];
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        s2[j] = byte_h2(scw, j);
-                        ns2[j] = __hmul2(s2[j], u2h(0xe400e400u));   // x -1024, exact
-                    }
+                for (int j = 0; j < 8; ++j) {
+                    s2[j] = byte_h2(scw, j);
+                    ns2[j] = __hmul2(s2[j], u2h(0xe400e400u));   // x -1024, exact
+                }
 #pragma unroll
-                    for (int li = 0; li < 2; ++li) {
-                        const int L = lx_first_lane(cur.pass) + 4 * li;   // qs word of chunk c: 4 + 8c + L
-                        const uint32_t qw[4] = {w[4 + L], w[12 + L], w[20 + L], w[28 + L]};
-                        lx_a_q4k_lane(qw, s2, ns2, o + 16 * li);
-                    }
-                } else {
-                    // min lanes m = pass - 4 and m + 2: [mins[2m] x 2, mins[2m+1] x 2, 0 x 12]
-#pragma unroll
-                    for (int li = 0; li < 2; ++li) {
-                        const int m = (cur.pass - 4) + 2 * li;
-                        o[8 * li] = h2u(byte_h2(mnw, 2 * m));
-                        o[8 * li + 1] = h2u(byte_h2(mnw, 2 * m + 1));
-#pragma unroll
-                        for (int i = 2; i < 8; ++i) o[8 * li + i] = 0u;
-                    }
+                for (int li = 0; li < 2; ++li) {
+                    const int L = lx_first_lane(cur.pass) + 4 * li;   // qs word of chunk c: 4 + 8c + L
+                    const uint32_t qw[4] = {w[4 + L], w[12 + L], w[20 + L], w[28 + L]};
+                    lx_a_q4k_lane(qw, s2, ns2, o + 16 * li);
                 }
             } else if (cur.type == T_IQ2_S) {
                 const uint8_t *blk = cur.arow + (size_t)cur.sb * B_IQ2_S;
@@ -502,14 +589,7 @@ __global__ void __launch_bounds__(kLxThreads, 1) pf_gate_up_lx_kernel(PfParams p
             }
             // the MMA thread waits on afull only: every converter sees the step's B image land first
             if (cur.type != T_Q4_K && !lx_wait_warp(&S.bfull[ab], (it / kLxRing) & 1, abort)) break;
-            if (mn) {
-                uint32_t o16[16];
-#pragma unroll
-                for (int i = 0; i < 16; ++i) o16[i] = o[i];
-                tmem_st16(ta + 32 * ab, o16);
-            } else {
-                tmem_st32(ta + 32 * ab, o);
-            }
+            tmem_st32(ta + 32 * ab, o);
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
@@ -540,17 +620,12 @@ __global__ void __launch_bounds__(kLxThreads, 1) pf_gate_up_lx_kernel(PfParams p
             const uint32_t a0 = tmem + kLxColA + 32 * ab, d0 = tmem + kLxColD + 128 * db;
             const uint32_t b0 = smem_addr(S.b[ab]);
             if (elect_one()) {
-                if (s.pass < 4) {   // lane a: K = 32 into d0, lane b: K = 32 into d0 + 64
-                    const uint32_t sbo = kLxMainCores * 128;
-                    umma_f16_ts(d0, a0, umma_sdesc(b0, 128, sbo), idesc, 0);
-                    umma_f16_ts(d0, a0 + 8, umma_sdesc(b0 + 256, 128, sbo), idesc, 1);
-                    umma_f16_ts(d0 + 64, a0 + 16, umma_sdesc(b0 + 512, 128, sbo), idesc, 0);
-                    umma_f16_ts(d0 + 64, a0 + 24, umma_sdesc(b0 + 768, 128, sbo), idesc, 1);
-                } else {            // the two min lanes, K = 16 each
-                    const uint32_t sbo = kLxMinCores * 128;
-                    umma_f16_ts(d0, a0, umma_sdesc(b0, 128, sbo), idesc, 0);
-                    umma_f16_ts(d0 + 64, a0 + 8, umma_sdesc(b0 + 256, 128, sbo), idesc, 0);
-                }
+                // lane a: K = 32 into d0, lane b: K = 32 into d0 + 64
+                const uint32_t sbo = kLxMainCores * 128;
+                umma_f16_ts(d0, a0, umma_sdesc(b0, 128, sbo), idesc, 0);
+                umma_f16_ts(d0, a0 + 8, umma_sdesc(b0 + 256, 128, sbo), idesc, 1);
+                umma_f16_ts(d0 + 64, a0 + 16, umma_sdesc(b0 + 512, 128, sbo), idesc, 0);
+                umma_f16_ts(d0 + 64, a0 + 24, umma_sdesc(b0 + 768, 128, sbo), idesc, 1);
                 umma_commit(&S.opfree[ab]);
                 umma_commit(&S.dfull[db]);
             }
@@ -572,14 +647,13 @@ __global__ void __launch_bounds__(kLxThreads, 1) pf_gate_up_lx_kernel(PfParams p
         for (int it = m; s.ok && !warp_aborted(abort); it += kLxIssue) {
             const int bs = it % kLxRing;
             if (it >= kLxRing && !lx_wait_warp(&S.opfree[bs], ((it / kLxRing) - 1) & 1, abort)) break;
-            const int ncores = s.pass >= 4 ? kLxMinCores : kLxMainCores;
-            const uint32_t bytes = (uint32_t)(s.N / 8) * ncores * 128;
+            const uint32_t bytes = (uint32_t)(s.N / 8) * kLxMainCores * 128;
             const bool q4 = s.type == T_Q4_K;
             if (elect_one()) {
                 mbar_expect_tx(&S.bfull[bs], bytes + (q4 ? (uint32_t)kLxRawBytes : 0u));
                 bulk_g2s(S.b[bs],
                          p.bimg + (size_t)s.ti * lx_tile_bytes(nsb) + lx_image_off(nsb, s.pass, s.sb) +
-                             (size_t)(8 * s.nh) * ncores * 128,
+                             (size_t)(8 * s.nh) * kLxMainCores * 128,
                          bytes, &S.bfull[bs]);
                 if (q4) {   // rows [64 mb, +64) and [n_ff + 64 mb, +64) of the entry, bytes [144 sb, +144)
                     const CUtensorMap *map = s.tl.cls ? &maps.gu[1] : &maps.gu[0];
@@ -611,24 +685,15 @@ __global__ void __launch_bounds__(kLxThreads, 1) pf_gate_up_lx_kernel(PfParams p
                 const int sb = i / kLxN, j = i - sb * kLxN;
                 S.dxs[sb][j] = p.dxt[((size_t)ti * nsb + sb) * kPfN + 64 * nh + j];
             }
-            if (ch == 0) {
-                for (int sb = 0; sb < nsb; ++sb) {
-                    float2 v;
-                    if (type == T_Q4_K) {
-                        const uint32_t hd = __ldg(reinterpret_cast<const uint32_t *>(arow + (size_t)sb * B_Q4_K));
-                        v = make_float2(h2f((uint16_t)(hd & 0xffffu)), -h2f((uint16_t)(hd >> 16)));
-                    } else {
-                        const int bsz = type == T_IQ2_S ? B_IQ2_S : B_IQ2_XXS;
-                        v = make_float2(h2f(__ldg(reinterpret_cast<const uint16_t *>(arow + (size_t)sb * bsz))), 0.f);
-                    }
-                    S.xdt[sb][r] = v;
-                }
+            if (ch == 0) {   // the row's d_w per super-block (the first fp16 of every block type here)
+                const int bsz = type == T_Q4_K ? B_Q4_K : type == T_IQ2_S ? B_IQ2_S : B_IQ2_XXS;
+                for (int sb = 0; sb < nsb; ++sb)
+                    S.xdt[sb][r] = h2f(__ldg(reinterpret_cast<const uint16_t *>(arow + (size_t)sb * bsz)));
             }
             if (!epi_barrier(&S.epibar, eph, abort)) break;
             const bool live = col0 < s.N;   // this warp's columns hold MMA output
             bool ok = true;
             for (int pass = 0; pass < np && ok; ++pass) {
-                const bool mn = pass >= 4;
                 uint64_t accA[kLxEpiCols / 2], accB[kLxEpiCols / 2];
 #pragma unroll
                 for (int i = 0; i < kLxEpiCols / 2; ++i) { accA[i] = 0ull; accB[i] = 0ull; }
@@ -639,8 +704,7 @@ __global__ void __launch_bounds__(kLxThreads, 1) pf_gate_up_lx_kernel(PfParams p
                     if (et == 0) PTRACE(0, 2, it, 1);
                     tc_fence_after();
                     if (live) {
-                        const float2 xw = S.xdt[sb][r];
-                        const float xs = mn ? xw.y : xw.x;   // d_w, or -dmin_w for the min lanes
+                        const float xs = S.xdt[sb][r];   // d_w
                         const uint64_t xs2 = f2pack(xs, xs);
                         const uint32_t dcol = tl_lane + kLxColD + 128 * db + col0;
                         const float4 *yd = reinterpret_cast<const float4 *>(&S.dxs[sb][col0]);
@@ -671,9 +735,10 @@ __global__ void __launch_bounds__(kLxThreads, 1) pf_gate_up_lx_kernel(PfParams p
                     if (et == 0) PTRACE(0, 2, it, 2);
                 }
                 if (!ok || !live) continue;
-                // fold the finished pass in the reference's reduction order:
-                //   pass 0 (0,4): Ha = a0;  1 (2,6): Ha = a0 + a2 = c0;  2 (1,5): Hb = a1;
-                //   3 (3,7): Ha = c0 + (a1 + a3);  4 (m0,m2): Hb = m0 + m2;  5 (m1,m3): h = Ha + (Hb + (m1 + m3))
+                // fold the finished pass in the reference's reduction order (aL = the pass's lane pair
+                // sum a_L + a_{L+4}):  pass 0: Ha = a0;  1: Ha = a0 + a2 = c0;  2: Hb = a1;
+                // 3: h = c0 + (a1 + a3), then Q4_K: h + M (M from pf_q4k_min_kernel, already in hbuf),
+                // IQ2_S / IQ2_XXS: h x 1/8
                 float t[kLxEpiCols];
 #pragma unroll
                 for (int i = 0; i < kLxEpiCols / 2; ++i) {
@@ -683,7 +748,7 @@ __global__ void __launch_bounds__(kLxThreads, 1) pf_gate_up_lx_kernel(PfParams p
                 }
                 float(*ha)[kPfM] = S.held[0] + col0;
                 float(*hb)[kPfM] = S.held[1] + col0;
-                if (pass == 0 || pass == 2 || pass == 4) {
+                if (pass == 0 || pass == 2) {
 #pragma unroll
                     for (int i = 0; i < kLxEpiCols; ++i) (pass == 0 ? ha : hb)[i][r] = t[i];
                     continue;
@@ -695,20 +760,19 @@ __global__ void __launch_bounds__(kLxThreads, 1) pf_gate_up_lx_kernel(PfParams p
                     for (int i = 0; i < kLxEpiCols; ++i) ha[i][r] = t[i];
                     continue;
                 }
-                // pass 3: Ha = c0, t = c1;  pass 5: Ha = the lanes' sum, t = M
+                // pass 3: Ha = c0, t = c1
 #pragma unroll
                 for (int i = 0; i < kLxEpiCols; ++i) t[i] = __fadd_rn(ha[i][r], t[i]);
-                if (pass == 3 && np == 6) {
+                // the unit's rows for this warp's pairs, f32, slot order ([slot][2 n_ff])
+                float *hbp = p.hbuf + (size_t)(tl.slot0 + 64 * nh + col0) * gu_rows + wr;
+                if (type == T_Q4_K) {
 #pragma unroll
-                    for (int i = 0; i < kLxEpiCols; ++i) ha[i][r] = t[i];
-                    continue;
-                }
-                if (pass == 3) {   // IQ2_S, IQ2_XXS: the sum times 1/8
+                    for (int i = 0; i < kLxEpiCols; ++i)
+                        if (col0 + i < nc) t[i] = __fadd_rn(t[i], hbp[(size_t)i * gu_rows]);
+                } else {
 #pragma unroll
                     for (int i = 0; i < kLxEpiCols; ++i) t[i] = __fmul_rn(0.125f, t[i]);
                 }
-                // the unit's rows for this warp's pairs, f32, slot order ([slot][2 n_ff])
-                float *hbp = p.hbuf + (size_t)(tl.slot0 + 64 * nh + col0) * gu_rows + wr;
 #pragma unroll
                 for (int i = 0; i < kLxEpiCols; ++i)
                     if (col0 + i < nc) hbp[(size_t)i * gu_rows] = t[i];

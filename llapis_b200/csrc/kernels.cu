@@ -2169,6 +2169,11 @@ cudaError_t launch_prefill(const PrefillArgs &a, cudaStream_t s, int n_sms) {
                       s, true, pargs);
         if (e != cudaSuccess) return e;
         if ((e = prof_mark(s, mark++)) != cudaSuccess) return e;
+        // the Q4_K min term of every (row, pair) into hbuf, which the grouped GEMM's epilogue completes
+        // (both run inside the gate_up profile slot)
+        e = pf_launch("pf_q4k_min_kernel", (const void *)pf_q4k_min_kernel,
+                      dim3(a.max_tiles, 2 * a.nff / kMinRows), dim3(128), 0, s, true, pargs);
+        if (e != cudaSuccess) return e;
         LxMaps maps;
         if ((e = lx_encode_map(&maps.gu[0], a.hot_gu, d, a.nff)) != cudaSuccess) return e;
         if ((e = lx_encode_map(&maps.gu[1], a.cold_gu, d, a.nff)) != cudaSuccess) return e;

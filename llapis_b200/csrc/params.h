@@ -150,15 +150,11 @@ MOEB_HD inline int prefill_max_tiles(int P, int E) { return P / kPrefillTile + E
 // columns (128 values + 16 min-term columns) per half super-block for gate_up, 128 rows x 8 core
 // columns (two 32-blocks) per down stage; 16 bytes per core row
 constexpr int kPfGuImageBytes = kPrefillTile * 18 * 16;
-// B operand images of the lane-exact gate_up GEMM (gateup_lx.cuh), per tile and super-block: two
-// min-pass images (16 row groups x 4 cores x 128 B) and four main-pass images (16 x 8 x 128 B); per
-// tile the min passes come first (pass 4, 5: 2 x nsb images), then the main passes 0..3
-constexpr int kLxImgMain = (kPrefillTile / 8) * 8 * 128, kLxImgMin = (kPrefillTile / 8) * 4 * 128;
-MOEB_HD inline size_t lx_tile_bytes(int nsb) { return (size_t)nsb * (2 * kLxImgMin + 4 * kLxImgMain); }
-MOEB_HD inline size_t lx_image_off(int nsb, int pass, int sb) {
-    return pass >= 4 ? (size_t)((pass - 4) * nsb + sb) * kLxImgMin
-                     : (size_t)2 * nsb * kLxImgMin + (size_t)(pass * nsb + sb) * kLxImgMain;
-}
+// B operand images of the lane-exact gate_up GEMM (gateup_lx.cuh): per tile, pass (0..3) and
+// super-block one image of 16 row groups x 8 cores x 128 B, pass-major
+constexpr int kLxImgMain = (kPrefillTile / 8) * 8 * 128;
+MOEB_HD inline size_t lx_tile_bytes(int nsb) { return (size_t)nsb * 4 * kLxImgMain; }
+MOEB_HD inline size_t lx_image_off(int nsb, int pass, int sb) { return (size_t)(pass * nsb + sb) * kLxImgMain; }
 constexpr int kPfDnImageBytes = kPrefillTile * 8 * 16;
 struct PrefillArgs {
     const float *w_router, *b_router, *x;
