@@ -173,6 +173,7 @@ struct PrefillWs {
     int16_t *xbs;
     uint8_t *bimg, *dimg;
     float *dxt, *hbuf;
+    uint32_t *bst;
     int max_tiles;
     size_t bytes;
 };
@@ -201,6 +202,7 @@ PrefillWs carve_prefill(const moeb_layer *L, int T, uint8_t *base) {
     const size_t pf_img = mt * lx_tile_bytes((int)nsb), md_img = md_image_bytes((int)P, (int)E, (int)d, (int)nff);
     w.bimg = (uint8_t *)take(pf_img > md_img ? pf_img : md_img);
     w.dxt = (float *)take(sizeof(float) * mt * nsb * kPrefillTile);
+    w.bst = (uint32_t *)take(sizeof(uint32_t) * 8 * mt * nsb * kPrefillTile);
     w.hbuf = (float *)take(sizeof(float) * P * 2 * nff);
     w.dimg = (uint8_t *)take(mt * (nff / 64) * 2 * kPfDnImageBytes);
     w.y = (float *)take(sizeof(float) * P * d);
@@ -356,7 +358,7 @@ static int forward_prefill(const moeb_layer *L, const float *x, int32_t T, float
     a.cnt = w.cnt; a.off = w.off; a.perm = w.perm; a.pos = w.pos;
     a.tiles = w.tiles; a.n_tiles = w.n_tiles;
     a.xq8 = w.xq8; a.xd = w.xd; a.xbs = w.xbs;
-    a.bimg = w.bimg; a.dxt = w.dxt; a.hbuf = w.hbuf; a.dimg = w.dimg; a.max_tiles = w.max_tiles;
+    a.bimg = w.bimg; a.dxt = w.dxt; a.bst = w.bst; a.hbuf = w.hbuf; a.dimg = w.dimg; a.max_tiles = w.max_tiles;
     a.h = aux ? aux->gate_up : nullptr;
     a.y = w.y;
     a.out = out;
@@ -447,7 +449,7 @@ extern "C" int moeb_layer_forward_routed(const moeb_layer *L, const float *x, in
     a.cnt = w.cnt; a.off = w.off; a.perm = w.perm; a.pos = w.pos;
     a.tiles = w.tiles; a.n_tiles = w.n_tiles;
     a.xq8 = w.xq8; a.xd = w.xd; a.xbs = w.xbs;
-    a.bimg = w.bimg; a.dxt = w.dxt; a.hbuf = w.hbuf; a.dimg = w.dimg; a.max_tiles = w.max_tiles;
+    a.bimg = w.bimg; a.dxt = w.dxt; a.bst = w.bst; a.hbuf = w.hbuf; a.dimg = w.dimg; a.max_tiles = w.max_tiles;
     a.y = w.y;
     a.out = out;
     a.routed = 1;

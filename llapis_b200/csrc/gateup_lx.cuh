@@ -280,7 +280,8 @@ __device__ __forceinline__ void lx_a_iq2xxs_lane(const uint8_t *blk, int L, uint
 // One CTA per (tile, super-block), thread = (tile row c, half h): half 0 writes main passes 0, 1
 // (lanes (0,4), (2,6)), half 1 passes 2, 3 ((1,5), (3,7)). An image row holds lane a's 32 values
 // (cores 0-3) then lane b's (cores 4-7), each in K order 4j + e. Rows n..N-1 (padding up to a
-// multiple of 16) are zero. Half 0 also writes the row's Q8_K scale.
+// multiple of 16) are zero. Half 0 also writes the row's Q8_K scale, half 1 its 16 bsums as fp16
+// pairs (exact: |bsum| <= 16 x 127) for pf_q4k_min_kernel.
 template <int PASS>
 __device__ __forceinline__ void lx_b_main_row(const uint4 (&v)[16], uint8_t *img, int c) {
 #pragma unroll
@@ -323,6 +324,7 @@ __global__ void __launch_bounds__(256) pf_gather_lx_kernel(PfParams p) {
         if (h == 0) dxt[c] = 0.f;
         return;
     }
+    uint4 *bst = reinterpret_cast<uint4 *>(p.bst + (((size_t)ti * nsb + sb) * kPfN + c) * 8);
     const int t = p.perm[tl.slot0 + c] / p.k;
     const int8_t *q8 = p.xq8 + (size_t)t * p.d + sb * QK_K;
     uint4 v[16];
@@ -335,6 +337,16 @@ __global__ void __launch_bounds__(256) pf_gather_lx_kernel(PfParams p) {
     } else {
         lx_b_main_row<2>(v, im0, c);
         lx_b_main_row<3>(v, im1, c);
+        const uint4 *bs = reinterpret_cast<const uint4 *>(p.xbs + ((size_t)t * nsb + sb) * 16);
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const uint4 u = __ldg(bs + i);
+            const uint32_t raw[4] = {u.x, u.y, u.z, u.w};
+            uint32_t o[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) o[j] = pack_h2i((int)(int16_t)(raw[j] & 0xffffu), (int)(int16_t)(raw[j] >> 16));
+            bst[i] = make_uint4(o[0], o[1], o[2], o[3]);
+        }
     }
 }
 
@@ -348,8 +360,14 @@ __global__ void __launch_bounds__(256) pf_gather_lx_kernel(PfParams p) {
 // The integers come from mma.sync m16n8k16 (fp16 operands, f32 accumulators, all exact): A row r holds
 // mins[j] twice at K = 2j, 2j + 1 (j < 8), B column c of group m holds bsums 4m..4m+3 at K = 4m..4m+3 and
 // zeros elsewhere, so one MMA per group gives lane m's integer for a 16 x 8 block, and the chains stay
-// in registers. CTA = (tile, 64 rows), four warps of 16 rows, 32 pairs per chunk (four n-blocks).
-constexpr int kMinRows = 64, kMinCols = 32;
+// in registers. CTA = (tile, 128 rows), eight warps of 16 rows; the tile's bsums (fp16 pairs, written
+// by pf_gather_lx_kernel) and scales are staged once, then 32-pair chunks (four n-blocks) run.
+// (A packed-f32 CUDA-core formulation of the same integers measured slower here: its operand tables
+// make it shared-memory bound.)
+constexpr int kMinRows = 128, kMinCols = 32, kMinThreads = 256;
+// dynamic shared memory: per super-block the tile's bsums [128][8] + scales [128] and the CTA rows'
+// mins [128] (uint2) + -dmin_w [128]
+MOEB_HD constexpr size_t min_smem_bytes(int nsb) { return (size_t)nsb * (kPfN * 36 + kMinRows * 12); }
 __device__ __forceinline__ void mma_f16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                               uint32_t b0, uint32_t b1) {
     asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
@@ -358,11 +376,8 @@ __device__ __forceinline__ void mma_f16_16816(float (&d)[4], uint32_t a0, uint32
                  : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.f));
 }
 
-__global__ void __launch_bounds__(128) pf_q4k_min_kernel(PfParams p) {
-    __shared__ uint2 s_mins[kPrefillMaxSb][kMinRows];             // the row's 8 mins (bytes)
-    __shared__ float s_ndmin[kPrefillMaxSb][kMinRows];            // -dmin_w
-    __shared__ uint32_t s_bs[kPrefillMaxSb][kMinCols][8];         // the pair's 16 bsums as fp16 pairs
-    __shared__ float s_dx[kPrefillMaxSb][kMinCols];               // the pair's Q8_K scale
+__global__ void __launch_bounds__(kMinThreads) pf_q4k_min_kernel(PfParams p) {
+    extern __shared__ __align__(16) uint8_t mn_smem[];
     pdl_wait();
     pdl_launch_dependents();
     const int ti = blockIdx.x, rb = blockIdx.y;
@@ -375,10 +390,26 @@ __global__ void __launch_bounds__(128) pf_q4k_min_kernel(PfParams p) {
     pv.ptrs = c1 ? p.gu[1].ptrs : p.gu[0].ptrs;
     if (pv.type != T_Q4_K) return;
     const int nsb = p.d / QK_K, gu_rows = 2 * p.nff, row0 = rb * kMinRows;
+    const int N = (tl.n + kMinCols - 1) / kMinCols * kMinCols;
+    uint32_t(*s_bs)[kPfN][8] = reinterpret_cast<uint32_t(*)[kPfN][8]>(mn_smem);
+    float(*s_dx)[kPfN] = reinterpret_cast<float(*)[kPfN]>(mn_smem + (size_t)nsb * kPfN * 32);
+    uint2(*s_mins)[kMinRows] = reinterpret_cast<uint2(*)[kMinRows]>(mn_smem + (size_t)nsb * kPfN * 36);
+    float(*s_ndmin)[kMinRows] = reinterpret_cast<float(*)[kMinRows]>(mn_smem + (size_t)nsb * (kPfN * 36 + kMinRows * 8));
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t4 = lane & 3;
+    // the tile's bsums and scales, columns [0, N) (those at or past the tile's n are never stored)
+    for (int i = tid; i < nsb * N * 2; i += kMinThreads) {
+        const int sb = i / (N * 2), rem = i - sb * N * 2;
+        reinterpret_cast<uint4 *>(&s_bs[sb][0][0])[rem] =
+            reinterpret_cast<const uint4 *>(p.bst + ((size_t)ti * nsb + sb) * kPfN * 8)[rem];
+    }
+    for (int i = tid; i < nsb * N; i += kMinThreads) {
+        const int sb = i / N, c = i - sb * N;
+        s_dx[sb][c] = p.dxt[((size_t)ti * nsb + sb) * kPfN + c];
+    }
+    // the CTA rows' block headers: mins and -dmin_w
     const uint8_t *base = tile_rows(pv, tl.widx, gu_rows, p.d);
     const size_t rbytes = row_bytes(T_Q4_K, p.d);
-    for (int i = tid; i < nsb * kMinRows; i += blockDim.x) {
+    for (int i = tid; i < nsb * kMinRows; i += kMinThreads) {
         const int sb = i / kMinRows, r = i - sb * kMinRows;
         const uint4 h = __ldg(reinterpret_cast<const uint4 *>(base + (size_t)(row0 + r) * rbytes + (size_t)sb * B_Q4_K));
         uint32_t sc[2], mn[2];
@@ -386,28 +417,10 @@ __global__ void __launch_bounds__(128) pf_q4k_min_kernel(PfParams p) {
         s_mins[sb][r] = make_uint2(mn[0], mn[1]);
         s_ndmin[sb][r] = -h2f((uint16_t)(h.x >> 16));
     }
-    const int ra = 16 * warp + g, rbw = ra + 8;   // this thread's two rows (of the CTA's 64)
-    for (int c0 = 0; c0 < tl.n; c0 += kMinCols) {
-        __syncthreads();   // the row table is written; the previous chunk's column table is consumed
-        for (int i = tid; i < nsb * kMinCols; i += blockDim.x) {
-            const int sb = i / kMinCols, c = i - sb * kMinCols;
-            uint32_t w[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
-            float dx = 0.f;
-            if (c0 + c < tl.n) {
-                const int t = p.perm[tl.slot0 + c0 + c] / p.k;
-                const uint4 *bs = reinterpret_cast<const uint4 *>(p.xbs + ((size_t)t * nsb + sb) * 16);
-                const uint4 u0 = __ldg(bs), u1 = __ldg(bs + 1);
-                const uint32_t raw[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
-#pragma unroll
-                for (int j = 0; j < 8; ++j)   // |bsum| <= 16 x 127: exact in fp16
-                    w[j] = pack_h2i((int)(int16_t)(raw[j] & 0xffffu), (int)(int16_t)(raw[j] >> 16));
-                dx = p.xd[(size_t)t * nsb + sb];
-            }
-#pragma unroll
-            for (int j = 0; j < 8; ++j) s_bs[sb][c][j] = w[j];
-            s_dx[sb][c] = dx;
-        }
-        __syncthreads();
+    __syncthreads();
+    const int ra = 16 * warp + g, rbw = ra + 8;   // this thread's two rows (of the CTA's 128)
+    const bool lo = t4 < 2;
+    for (int c0 = 0; c0 < N; c0 += kMinCols) {
         float acc[4][4][4];   // [n-block][lane m][fragment element]
 #pragma unroll
         for (int j = 0; j < 4; ++j)
@@ -424,13 +437,13 @@ __global__ void __launch_bounds__(128) pf_q4k_min_kernel(PfParams p) {
             const float nda = s_ndmin[sb][ra], ndb = s_ndmin[sb][rbw];
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
+                const int cb = c0 + 8 * j;
                 // B: column g of n-block j, K 2t4, 2t4+1 (bsums 2t4, 2t4+1) and K 2t4+8, 2t4+9; group m
                 // keeps only its K range 4m..4m+3
-                const uint32_t p0 = s_bs[sb][8 * j + g][t4], p1 = s_bs[sb][8 * j + g][t4 + 4];
-                const float dx0 = s_dx[sb][8 * j + 2 * t4], dx1 = s_dx[sb][8 * j + 2 * t4 + 1];
+                const uint32_t p0 = s_bs[sb][cb + g][t4], p1 = s_bs[sb][cb + g][t4 + 4];
+                const float2 dx = *reinterpret_cast<const float2 *>(&s_dx[sb][cb + 2 * t4]);
                 // dmin = -d_x * dmin_w per (row, pair), rounded to f32
-                const float dm[4] = {__fmul_rn(dx0, nda), __fmul_rn(dx1, nda), __fmul_rn(dx0, ndb), __fmul_rn(dx1, ndb)};
-                const bool lo = t4 < 2;
+                const float dm[4] = {__fmul_rn(dx.x, nda), __fmul_rn(dx.y, nda), __fmul_rn(dx.x, ndb), __fmul_rn(dx.y, ndb)};
 #pragma unroll
                 for (int m = 0; m < 4; ++m) {
                     const uint32_t b0 = m < 2 && (lo == (m == 0)) ? p0 : 0u;

@@ -2055,6 +2055,7 @@ cudaError_t launch_prefill(const PrefillArgs &a, cudaStream_t s, int n_sms) {
     static unsigned optin[32];
     cudaError_t e = smem_optin((const void *)pf_gate_up_lx_kernel, sizeof(LxSmem), optin, 0);
     if (e == cudaSuccess) e = smem_optin((const void *)pf_down_kernel, sizeof(DnSmem), optin, 1);
+    if (e == cudaSuccess) e = smem_optin((const void *)pf_q4k_min_kernel, min_smem_bytes(kPrefillMaxSb), optin, 4);
     if (e != cudaSuccess) return e;
     const int T = a.T, E = a.E, d = a.d, k = a.k;
     int mark = 0;
@@ -2141,7 +2142,7 @@ cudaError_t launch_prefill(const PrefillArgs &a, cudaStream_t s, int n_sms) {
     p.gu[0] = a.hot_gu; p.gu[1] = a.cold_gu; p.dn[0] = a.hot_dn; p.dn[1] = a.cold_dn;
     p.perm = a.perm; p.tiles = a.tiles; p.n_tiles = a.n_tiles;
     p.xq8 = a.xq8; p.xd = a.xd; p.xbs = a.xbs;
-    p.bimg = a.bimg; p.dxt = a.dxt; p.hbuf = a.hbuf; p.dimg = a.dimg; p.h = a.h; p.y = a.y;
+    p.bimg = a.bimg; p.dxt = a.dxt; p.bst = a.bst; p.hbuf = a.hbuf; p.dimg = a.dimg; p.h = a.h; p.y = a.y;
     void *pargs[] = {&p};
     if (a.mid_gu) {
         {
@@ -2172,7 +2173,8 @@ cudaError_t launch_prefill(const PrefillArgs &a, cudaStream_t s, int n_sms) {
         // the Q4_K min term of every (row, pair) into hbuf, which the grouped GEMM's epilogue completes
         // (both run inside the gate_up profile slot)
         e = pf_launch("pf_q4k_min_kernel", (const void *)pf_q4k_min_kernel,
-                      dim3(a.max_tiles, 2 * a.nff / kMinRows), dim3(128), 0, s, true, pargs);
+                      dim3(a.max_tiles, 2 * a.nff / kMinRows), dim3(kMinThreads), min_smem_bytes(d / QK_K), s, true,
+                      pargs);
         if (e != cudaSuccess) return e;
         LxMaps maps;
         if ((e = lx_encode_map(&maps.gu[0], a.hot_gu, d, a.nff)) != cudaSuccess) return e;

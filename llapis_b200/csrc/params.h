@@ -174,8 +174,9 @@ struct PrefillArgs {
     int8_t *xq8;                // [T][d]
     float *xd;                  // [T][d / 256]
     int16_t *xbs;               // [T][d / 256][16]
-    uint8_t *bimg;              // [max_tiles][d / 256][2][kPfGuImageBytes] gate_up B operand images
+    uint8_t *bimg;              // [max_tiles][lx_tile_bytes] gate_up B operand images (or the mid path's)
     float *dxt;                 // [max_tiles][d / 256][kPrefillTile] Q8_K scales per tile row
+    uint32_t *bst;              // [max_tiles][d / 256][kPrefillTile][8] Q8_K bsums per tile row, fp16 pairs
     float *hbuf;                // [P][2 nff] gate_up outputs, slot order
     uint8_t *dimg;              // [max_tiles][nff / 64][2][kPfDnImageBytes] down B operand images (hi, lo)
     int32_t max_tiles;

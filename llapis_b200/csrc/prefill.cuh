@@ -400,6 +400,7 @@ struct PfParams {
     const int16_t *xbs;               // [T][d/256][16] Q8_K bsums
     uint8_t *bimg;                    // gate_up B operand images, [tile][sb][half][kPfGuImageBytes]
     float *dxt;                       // [tile][sb][128] Q8_K scale of each tile row
+    uint32_t *bst;                    // [tile][sb][128][8] Q8_K bsums of each tile row, fp16 pairs
     float *hbuf;                      // [slot][2 n_ff] gate_up outputs, f32
     uint8_t *dimg;                    // down B operand images, [tile][stage][kPfDnImageBytes]
 
