@@ -54,6 +54,10 @@ def parse():
     p.add_argument("--block-norms", action="store_true",
                    help="the whole Gemma-4 MoE block: pre / router-input / output rms_norms fused into the layer "
                         "(moeb_layer_forward_gemma4); input is the block input (attn_out)")
+    p.add_argument("--ffn-block", action="store_true",
+                   help="the Gemma-4 feed-forward block: the MoE block plus the dense MLP branch (d_model 2816, "
+                        "inner width 2112) on a side stream (moeb_ffn_block_gemma4), against each branch alone "
+                        "and both in turn")
     return p.parse_args()
 
 
@@ -559,6 +563,8 @@ def main():
     from llapis_b200 import workload as _wl
     if args.block_norms and (args.config.startswith("ep_") or _wl.CONFIGS[args.config].n_layers > 1):
         raise SystemExit("--block-norms covers the single-layer configs")
+    if args.ffn_block:
+        return run_ffn_block(args, _wl.CONFIGS[args.config])
     if args.config.startswith("ep_"):
         return run_ep(args, _wl.CONFIGS[args.config])
     if _wl.CONFIGS[args.config].n_layers > 1:
@@ -589,6 +595,59 @@ def main():
         print(json.dumps(line))
     if world > 1:
         dist.destroy_process_group()
+    return 0
+
+
+def run_ffn_block(args, cfg):
+    """The Gemma-4 feed-forward block at the config's T on one GPU: the MoE block (with its norms),
+    the dense MLP branch alone, the block with both branches in turn on one stream, and the block
+    with the dense branch on a side stream (concurrent with the MoE kernels). Device time per step
+    (CUDA events on the launching stream, L2 flushed between steps, eager launches)."""
+    import torch
+
+    from llapis_b200 import workload
+    from llapis_b200.layer import FfnBlock, MoELayer
+
+    if cfg.n_layers > 1 or cfg.name.startswith("ep_"):
+        raise SystemExit("--ffn-block covers the single-layer configs")
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    moe = MoELayer(workload.build_layer(cfg), dev, norms=workload.block_norms(cfg))
+    mlp = MoELayer(workload.build_dense_layer(), dev, norms=workload.dense_block_norms())
+    blk = FfnBlock(moe, mlp)
+    x = torch.from_numpy(workload.make_block_input(cfg)).to(dev)
+    T = x.shape[0]
+    out = torch.empty_like(x)
+    s, side = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    variants = {"moe_block": lambda: moe(x, out, stream=s), "dense_mlp": lambda: mlp(x, out, stream=s),
+                "sequential": lambda: blk(x, out, stream=s), "overlapped": lambda: blk(x, out, stream=s, side_stream=side)}
+    res = {}
+    with Clocks(0) as clk:
+        for name, fn in variants.items():
+            ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+            with torch.cuda.stream(s):
+                for _ in range(max(3, args.warmup)):
+                    flush.zero_()
+                    fn()
+                for i in range(args.steps):
+                    flush.zero_()
+                    ev[i][0].record(s)
+                    fn()
+                    ev[i][1].record(s)
+            torch.cuda.synchronize()
+            res[name] = float(np.mean([a.elapsed_time(b) for a, b in ev]))
+    line = {"metric": "ffn_block_ms", "value": res["overlapped"], "unit": "ms", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "higher_is_better": False, "dtype": "as the layer path",
+            "data": "synthetic (seeded weights quantised to ggml formats, N(0,1) block input)",
+            "config": {"workload": cfg.name, "n_tokens": T, "dense_n_ff": mlp.host.n_ff, "moe_path": path_label(moe, T),
+                       "dense_path": path_label(mlp, T), "l2": "flushed between steps (256 MiB write, not timed)",
+                       "cuda_graph": False},
+            "ms": {k: round(v, 4) for k, v in res.items()},
+            "overlap_saving_ms": round(res["sequential"] - res["overlapped"], 4),
+            "tokens_per_s_overlapped": T / (res["overlapped"] * 1e-3), "clocks": clk.summary(),
+            "device_error": moe.device_error()}
+    print(json.dumps(line))
     return 0
 
 

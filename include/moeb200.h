@@ -95,6 +95,13 @@ int32_t     moeb_device_error(void *stream);
  * outputs of every routed pair: n_tokens * top_k * d_model * 4 bytes). */
 size_t moeb_layer_workspace_size(const moeb_layer *L, int32_t n_tokens);
 
+/* The path moeb_layer_forward takes for n_tokens tokens of this layer (new, an inspection entry):
+ * 0 the fused decode kernel (8-token chunks), 1 the prefill kernels; a negative MOEB_E* code for a
+ * layer moeb_layer_forward would refuse. Layers whose decode kernel does not fit in an SM's shared
+ * memory (n_ff above ~1.5K at d_model 2816, e.g. the Gemma-4 dense MLP's 2112) take the prefill
+ * path at every batch size. */
+int32_t moeb_layer_path(const moeb_layer *L, int32_t n_tokens);
+
 /* One whole MoE layer, router to combine (new; the graph-level unit the benchmark measures).
  * x: f32 [n_tokens][d_model]; out: f32 [n_tokens][d_model]. The workspace must stay untouched
  * until the stream reaches the end of the call. Kernels are chained with programmatic dependent
@@ -133,6 +140,32 @@ typedef struct moeb_norms {
 int moeb_layer_forward_gemma4(const moeb_layer *L, const moeb_norms *norms, const float *x, int32_t n_tokens,
                               float *out, const moeb_layer_aux *aux, void *workspace, size_t workspace_bytes,
                               void *stream);
+
+/* The feed-forward part of a Gemma-4 MoE block (new; third_party/llama/src/models/gemma4.cpp:376-431):
+ *   mlp = rms_norm(x) * ffn_norm -> build_ffn (GELU, PAR) -> rms_norm * ffn_post_norm_1   (dense branch)
+ *   moe = moeb_layer_forward_gemma4(moe, moe_norms, x)                                     (MoE branch)
+ *   out = moe + mlp                                                                        (ggml_add)
+ * The dense MLP is passed as a one-expert layer (top_k 1, one hot slot holding [gate rows; up rows]
+ * and down, zero router weights with a bias putting every token on expert 0: its softmax weight is
+ * then exactly 1.0) with mlp_norms = {ffn_norm, any non-null router_scale (unused: the router weights
+ * are zero), ffn_post_norm_1}. With a side_stream the dense branch runs there, concurrently with the
+ * MoE branch on stream (fork / join through events, capturable in a CUDA graph); with side_stream
+ * NULL both run on stream in turn. Calls on one device issued from several host threads at once are
+ * serialised on the host while they enqueue. The workspace (moeb_ffn_block_workspace_size) holds
+ * both branches' workspaces and the dense branch's output. */
+/* Row-wise rms_norm followed by the reference's optional scale and mul nodes (new; ggml_rms_norm
+ * then ggml_scale and ggml_mul, as the Gemma-4 block applies them, gemma4.cpp:394-402, :423-425):
+ * out = ((x * s) * scale) * w per row, s = 1 / sqrt(mean(x^2) + eps), each product rounded to f32;
+ * scale 1 skips the scale node, w NULL the mul node. x, out: f32 [rows][d], 16-byte aligned, d a
+ * multiple of 4; out may equal x. The expert-parallel layer norms its tokens with it before the
+ * dispatch and after the cross-rank combine. */
+int moeb_rms_norm(const float *x, int32_t rows, int32_t d, const float *w, float scale, float eps, float *out,
+                  void *stream);
+
+size_t moeb_ffn_block_workspace_size(const moeb_layer *moe, const moeb_layer *mlp, int32_t n_tokens);
+int moeb_ffn_block_gemma4(const moeb_layer *moe, const moeb_norms *moe_norms, const moeb_layer *mlp,
+                          const moeb_norms *mlp_norms, const float *x, int32_t n_tokens, float *out,
+                          void *workspace, size_t workspace_bytes, void *stream, void *side_stream);
 
 /* The two halves of the layer, for expert-parallel hosts (new; the reference runs the router and
  * the expert matmuls as separate graph nodes, llama-graph.cpp:1530-1613 and :1689-1848).

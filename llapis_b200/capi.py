@@ -65,10 +65,17 @@ SIGNATURES = {
     "moeb_version": (C.c_char_p, []),
     "moeb_device_error": (C.c_int32, [C.c_void_p]),
     "moeb_layer_workspace_size": (C.c_size_t, [C.POINTER(Layer), C.c_int32]),
+    "moeb_layer_path": (C.c_int32, [C.POINTER(Layer), C.c_int32]),
     "moeb_layer_forward": (C.c_int, [C.POINTER(Layer), C.c_void_p, C.c_int32, C.c_void_p, C.POINTER(LayerAux),
                                      C.c_void_p, C.c_size_t, C.c_void_p]),
     "moeb_layer_forward_gemma4": (C.c_int, [C.POINTER(Layer), C.POINTER(Norms), C.c_void_p, C.c_int32, C.c_void_p,
                                             C.POINTER(LayerAux), C.c_void_p, C.c_size_t, C.c_void_p]),
+    "moeb_rms_norm": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_void_p, C.c_float, C.c_float, C.c_void_p,
+                                C.c_void_p]),
+    "moeb_ffn_block_workspace_size": (C.c_size_t, [C.POINTER(Layer), C.POINTER(Layer), C.c_int32]),
+    "moeb_ffn_block_gemma4": (C.c_int, [C.POINTER(Layer), C.POINTER(Norms), C.POINTER(Layer), C.POINTER(Norms),
+                                        C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p,
+                                        C.c_void_p]),
     "moeb_layer_forward_static": (C.c_int, [C.POINTER(Layer), C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p]),
     "moeb_set_prefill_min_tokens": (C.c_int32, [C.c_int32]),
     "moeb_set_mid_max_pairs": (C.c_int32, [C.c_int32]),

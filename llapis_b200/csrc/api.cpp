@@ -108,6 +108,13 @@ int check_pool(const moeb_pool &pl, int d_model, int n_ff, const char *name) {
     return MOEB_OK;
 }
 
+bool prefill_shape_ok(const moeb_layer *L);
+
+// The fused decode kernel keeps a stage ring of whole weight rows and the chunk's activations in
+// shared memory; wider layers (the dense MLP's 2112-wide inner dimension) run every batch size on
+// the prefill kernels instead.
+bool fused_fits(const moeb_layer *L) { return fused_smem_bytes(L->d_model, L->n_ff) <= 227 * 1024; }
+
 int check_layer(const moeb_layer *L) {
     if (!L) return fail(MOEB_EINVAL, "null layer");
     if (L->d_model <= 0 || L->d_model % QK_K) return fail(MOEB_EINVAL, "d_model %d must be a multiple of 256", L->d_model);
@@ -122,9 +129,9 @@ int check_layer(const moeb_layer *L) {
     if (L->hot.n <= 0 && L->cold.n <= 0) return fail(MOEB_EINVAL, "no expert pool");
     if (L->cold.n > 0 && L->cold.n < L->n_expert)
         return fail(MOEB_EINVAL, "cold pool holds %d experts, layer has %d", L->cold.n, L->n_expert);
-    if (fused_smem_bytes(L->d_model, L->n_ff) > 227 * 1024)
-        return fail(MOEB_EINVAL, "layer shape d_model=%d n_ff=%d needs more shared memory than an SM has", L->d_model,
-                    L->n_ff);
+    if (!fused_fits(L) && !prefill_shape_ok(L))
+        return fail(MOEB_EINVAL, "layer shape d_model=%d n_ff=%d: the decode kernel needs more shared memory than an SM "
+                                 "has and the prefill kernels do not cover it", L->d_model, L->n_ff);
     int rc = check_pool(L->hot, L->d_model, L->n_ff, "hot");
     if (rc) return rc;
     return check_pool(L->cold, L->d_model, L->n_ff, "cold");
@@ -220,7 +227,7 @@ bool prefill_shape_ok(const moeb_layer *L) {
 }
 
 bool use_prefill(const moeb_layer *L, int32_t n_tokens) {
-    return n_tokens >= g_prefill_min.load() && prefill_shape_ok(L);
+    return prefill_shape_ok(L) && (n_tokens >= g_prefill_min.load() || !fused_fits(L));
 }
 
 // Prefill-path batches with fewer routed pairs per expert than these run a projection on the
@@ -283,6 +290,12 @@ extern "C" size_t moeb_layer_workspace_size(const moeb_layer *L, int32_t n_token
     if (!L || n_tokens <= 0) return 0;
     if (use_prefill(L, n_tokens)) return carve_prefill(L, n_tokens, nullptr).bytes;
     return chunk_workspace_size(L, n_tokens);
+}
+
+extern "C" int32_t moeb_layer_path(const moeb_layer *L, int32_t n_tokens) {
+    const int rc = check_layer(L);
+    if (rc) return rc;
+    return use_prefill(L, n_tokens) ? 1 : 0;
 }
 
 extern "C" int moeb_prefill_profile(int32_t enable) {
@@ -429,7 +442,7 @@ extern "C" int moeb_layer_forward_routed(const moeb_layer *L, const float *x, in
     if (rc || n_rows == 0) return rc;
     if (!prefill_shape_ok(L))
         return fail(MOEB_EINVAL, "moeb_layer_forward_routed: n_ff must be a multiple of 64, d_model of 128, d_model <= "
-                                 "4096 and n_ff <= 1024");
+                                 "4096 and n_ff <= %d", kPrefillMaxBlk * 32);
     if (!ids || !weights) return fail(MOEB_EINVAL, "moeb_layer_forward_routed: null ids / weights");
     const int d = L->d_model, k = L->top_k, E = L->n_expert;
     PrefillWs w = carve_prefill(L, n_rows, (uint8_t *)workspace);
@@ -491,11 +504,90 @@ extern "C" int moeb_layer_forward_gemma4(const moeb_layer *L, const moeb_norms *
     return forward_chunks(L, x, n_tokens, out, aux, workspace, (cudaStream_t)stream, n_sms, nrm);
 }
 
+extern "C" int moeb_rms_norm(const float *x, int32_t rows, int32_t d, const float *w, float scale, float eps,
+                             float *out, void *stream) {
+    if (rows < 0 || d <= 0 || d % 4) return fail(MOEB_EINVAL, "moeb_rms_norm: rows %d / d %d (d a multiple of 4)", rows, d);
+    if (rows == 0) return MOEB_OK;
+    if (!x || !out || !aligned16(x) || !aligned16(out) || (w && !aligned16(w)))
+        return fail(MOEB_EINVAL, "moeb_rms_norm: null or unaligned x / out / w (16-byte alignment)");
+    if (!(eps >= 0.f)) return fail(MOEB_EINVAL, "moeb_rms_norm: eps must be >= 0");
+    int rc = ensure_device();
+    if (rc != MOEB_OK) return rc;
+    cudaError_t e = launch_rms_norm(x, rows, d, w, scale, eps, out, (cudaStream_t)stream);
+    return e == cudaSuccess ? MOEB_OK : cuda_fail(e, "rms_norm launch");
+}
+
+// ---------------------------------------------------------------- the Gemma-4 feed-forward block
+namespace {
+std::mutex g_block_mu;
+cudaEvent_t g_block_ev[64][2];   // fork / join events per device, created on first use
+}  // namespace
+
+extern "C" size_t moeb_ffn_block_workspace_size(const moeb_layer *moe, const moeb_layer *mlp, int32_t n_tokens) {
+    if (!moe || !mlp || n_tokens <= 0) return 0;
+    return align_up(moeb_layer_workspace_size(moe, n_tokens), 256) + align_up(moeb_layer_workspace_size(mlp, n_tokens), 256) +
+           align_up((size_t)n_tokens * mlp->d_model * sizeof(float), 256);
+}
+
+extern "C" int moeb_ffn_block_gemma4(const moeb_layer *moe, const moeb_norms *moe_norms, const moeb_layer *mlp,
+                                     const moeb_norms *mlp_norms, const float *x, int32_t n_tokens, float *out,
+                                     void *workspace, size_t workspace_bytes, void *stream, void *side_stream) {
+    if (!moe || !mlp) return fail(MOEB_EINVAL, "moeb_ffn_block_gemma4: null moe / mlp layer");
+    if (moe->d_model != mlp->d_model)
+        return fail(MOEB_EINVAL, "moeb_ffn_block_gemma4: d_model %d (moe) != %d (mlp)", moe->d_model, mlp->d_model);
+    if (mlp->top_k != 1 || mlp->hot.n != 1 || mlp->cold.n > 0)
+        return fail(MOEB_EINVAL, "moeb_ffn_block_gemma4: the dense MLP must be a one-expert layer (top_k 1, one hot "
+                                 "slot, no cold pool)");
+    if (n_tokens < 0) return fail(MOEB_EINVAL, "n_tokens %d < 0", n_tokens);
+    const size_t need = moeb_ffn_block_workspace_size(moe, mlp, n_tokens);
+    if (n_tokens > 0 && (!workspace || workspace_bytes < need || !aligned16(workspace)))
+        return fail(MOEB_EINVAL, "moeb_ffn_block_gemma4: workspace of %zu bytes (16-byte aligned) needed, %zu given", need,
+                    workspace_bytes);
+    int rc = check_layer(moe);
+    if (!rc) rc = check_layer(mlp);
+    if (rc || n_tokens == 0) return rc;
+    int n_sms = 0;
+    if ((rc = ensure_device(&n_sms)) != MOEB_OK) return rc;
+    const size_t w_moe = align_up(moeb_layer_workspace_size(moe, n_tokens), 256);
+    const size_t w_mlp = align_up(moeb_layer_workspace_size(mlp, n_tokens), 256);
+    uint8_t *ws = (uint8_t *)workspace;
+    float *tmp = (float *)(ws + w_moe + w_mlp);
+    cudaStream_t s = (cudaStream_t)stream, s2 = side_stream ? (cudaStream_t)side_stream : s;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess || dev < 0 || dev >= 64) return fail(MOEB_ENODEV, "moeb_ffn_block_gemma4: no usable device");
+    std::lock_guard<std::mutex> lk(g_block_mu);   // record -> wait pairs of one call stay together
+    if (s2 != s) {
+        for (int i = 0; i < 2; ++i)
+            if (!g_block_ev[dev][i] && (e = cudaEventCreateWithFlags(&g_block_ev[dev][i], cudaEventDisableTiming)) != cudaSuccess)
+                return cuda_fail(e, "create the block's fork / join events");
+        if ((e = cudaEventRecord(g_block_ev[dev][0], s)) != cudaSuccess ||
+            (e = cudaStreamWaitEvent(s2, g_block_ev[dev][0], 0)) != cudaSuccess)
+            return cuda_fail(e, "fork the dense branch onto the side stream");
+    }
+    // the dense branch on the side stream, the MoE branch on the main stream, then out = moe + mlp
+    int rc2 = moeb_layer_forward_gemma4(mlp, mlp_norms, x, n_tokens, tmp, nullptr, ws + w_moe, w_mlp, s2);
+    rc = rc2 ? rc2 : moeb_layer_forward_gemma4(moe, moe_norms, x, n_tokens, out, nullptr, ws, w_moe, s);
+    if (s2 != s) {
+        // joined on every path, so the side stream never runs past the call
+        if ((e = cudaEventRecord(g_block_ev[dev][1], s2)) != cudaSuccess ||
+            (e = cudaStreamWaitEvent(s, g_block_ev[dev][1], 0)) != cudaSuccess)
+            return cuda_fail(e, "join the dense branch");
+    }
+    if (rc) return rc;
+    if ((e = launch_add_f32(out, tmp, (size_t)n_tokens * moe->d_model, n_sms, s)) != cudaSuccess)
+        return cuda_fail(e, "add the block's branches");
+    return MOEB_OK;
+}
+
 int moeb::layer_forward_chunked(const moeb_layer *L, const float *x, int32_t n_tokens, float *out, void *workspace,
                                 size_t workspace_bytes, void *stream) {
     int n_sms = 0;
     int rc = check_forward(L, x, n_tokens, out, workspace, workspace_bytes, chunk_workspace_size(L, n_tokens), &n_sms);
     if (rc || n_tokens == 0) return rc;
+    if (!fused_fits(L))
+        return fail(MOEB_EINVAL, "layer shape d_model=%d n_ff=%d runs on the prefill kernels only (the decode kernel "
+                                 "does not fit in shared memory); use moeb_layer_forward", L->d_model, L->n_ff);
     return forward_chunks(L, x, n_tokens, out, nullptr, workspace, (cudaStream_t)stream, n_sms);
 }
 

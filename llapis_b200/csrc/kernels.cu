@@ -2020,7 +2020,8 @@ static cudaError_t pf_launch(const char *name, const void *fn, dim3 grid, dim3 b
 
 bool mid_shape_ok(int kind, int d, int nff, int P, int E) {
     const int tiles = prefill_max_tiles(P, E);
-    return d % QK_K == 0 && nff % QK32 == 0 && tiles <= kMdMaxTiles &&
+    // n_ff <= 1024: the widths the mid-size kernels are tested at (wider layers take the tcgen05 GEMMs)
+    return d % QK_K == 0 && nff % QK32 == 0 && nff <= 1024 && tiles <= kMdMaxTiles &&
            P / (8 * md_chunk(kind)) + tiles <= kMdMaxUnits && md_layout(kind, d, nff).n_slots >= 2;
 }
 
@@ -2252,6 +2253,65 @@ __global__ void sum4_kernel(const float *h, size_t stride, float *dst, size_t n)
 
 cudaError_t launch_sum4(const float *h, size_t stride, float *dst, size_t n, cudaStream_t s) {
     sum4_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(h, stride, dst, n);
+    return cudaGetLastError();
+}
+
+// Row-wise rms_norm with the reference nodes that follow it (gemma4.cpp:394-402, :423-425):
+// out = ((x * s) * c) * w, s = 1 / sqrt(mean(x^2) + eps), each product rounded to f32 as the separate
+// rms_norm, scale (when c != 1) and mul (when w is given) nodes round it. One CTA per row; the squares
+// are rounded to f32 and summed in double, as in the layer kernels' fused norms.
+__global__ void __launch_bounds__(256) rms_norm_kernel(const float *x, const float *w, float c, float eps, float *out,
+                                                       int d) {
+    __shared__ double red[8];
+    const int row = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, n4 = d / 4;
+    const float4 *x4 = reinterpret_cast<const float4 *>(x + (size_t)row * d);
+    double q = 0.0;
+    for (int i = tid; i < n4; i += 256) q += sq_sum4(__ldg(x4 + i));
+    q = warp_sum_d(q);
+    if (lane == 0) red[warp] = q;
+    __syncthreads();
+    double tot = 0.0;
+    for (int i = 0; i < 8; ++i) tot += red[i];   // one fixed order, every thread the same scale
+    const float sc = rms_row_scale(tot, d, eps);
+    float4 *o4 = reinterpret_cast<float4 *>(out + (size_t)row * d);
+    const float4 *w4 = reinterpret_cast<const float4 *>(w);
+    for (int i = tid; i < n4; i += 256) {
+        const float4 v = __ldg(x4 + i);
+        float4 r = make_float4(__fmul_rn(v.x, sc), __fmul_rn(v.y, sc), __fmul_rn(v.z, sc), __fmul_rn(v.w, sc));
+        if (c != 1.f) r = make_float4(__fmul_rn(r.x, c), __fmul_rn(r.y, c), __fmul_rn(r.z, c), __fmul_rn(r.w, c));
+        if (w) {
+            const float4 g = __ldg(w4 + i);
+            r = make_float4(__fmul_rn(r.x, g.x), __fmul_rn(r.y, g.y), __fmul_rn(r.z, g.z), __fmul_rn(r.w, g.w));
+        }
+        o4[i] = r;
+    }
+}
+
+cudaError_t launch_rms_norm(const float *x, int rows, int d, const float *w, float c, float eps, float *out,
+                            cudaStream_t s) {
+    rms_norm_kernel<<<rows, 256, 0, s>>>(x, w, c, eps, out, d);
+    return cudaGetLastError();
+}
+
+// out += a (f32, n a multiple of 4, 16-byte aligned): the Gemma-4 block's ggml_add of the MoE and
+// dense-MLP branches (gemma4.cpp:429), one rounding per element like the reference's
+__global__ void add_f32_kernel(float4 *out, const float4 *a, size_t n4) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
+        float4 o = out[i];
+        const float4 v = __ldg(a + i);
+        o.x = __fadd_rn(o.x, v.x);
+        o.y = __fadd_rn(o.y, v.y);
+        o.z = __fadd_rn(o.z, v.z);
+        o.w = __fadd_rn(o.w, v.w);
+        out[i] = o;
+    }
+}
+
+cudaError_t launch_add_f32(float *out, const float *a, size_t n, int n_sms, cudaStream_t s) {
+    const size_t n4 = n / 4;
+    const size_t want = (n4 + 255) / 256, cap = (size_t)(n_sms > 0 ? n_sms : 148) * 8;
+    add_f32_kernel<<<(unsigned)(want < cap ? want : cap), 256, 0, s>>>(reinterpret_cast<float4 *>(out),
+                                                                        reinterpret_cast<const float4 *>(a), n4);
     return cudaGetLastError();
 }
 

@@ -137,7 +137,7 @@ MOEB_HD inline int fused_sync_words(int T, int d, int nff) {
 // the prefill path (tcgen05 grouped GEMMs; prefill.cuh)
 constexpr int kPrefillTile = 128;        // routed pairs per expert tile (MMA N)
 constexpr int kPrefillMaxSb = 16;        // d_model <= 4096
-constexpr int kPrefillMaxBlk = 32;       // n_ff <= 1024
+constexpr int kPrefillMaxBlk = 128;      // n_ff <= 4096
 // One expert tile: up to kPrefillTile consecutive slots of the expert-sorted pair order.
 struct PfTile {
     int32_t cls;     // 0 hot pool, 1 cold pool
@@ -235,6 +235,9 @@ cudaError_t launch_fused(const FusedArgs &a, cudaStream_t s, int n_sms);
 // dst[i] = ((h[i] + h[i + stride]) + h[i + 2 stride]) + h[i + 3 stride]: the fused kernel's gate_up
 // rows are four partial sums (super-block quarters); this adds them for the aux output
 cudaError_t launch_sum4(const float *h, size_t stride, float *dst, size_t n, cudaStream_t s);
+cudaError_t launch_add_f32(float *out, const float *a, size_t n, int n_sms, cudaStream_t s);
+cudaError_t launch_rms_norm(const float *x, int rows, int d, const float *w, float c, float eps, float *out,
+                            cudaStream_t s);
 size_t fused_smem_bytes(int d, int nff);
 // standalone pieces behind the moeb_* inspection entry points
 cudaError_t launch_route_only(const RouteSrc &r, int32_t *ids, float *w, int32_t *cnt, int32_t *off, int32_t *perm,

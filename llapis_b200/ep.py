@@ -16,6 +16,17 @@ This mirrors the reference's single-GPU arithmetic except for the final order of
 reference adds all k weighted outputs in slot order, here the slot-ordered partial sums of each
 rank are added in rank order (a difference of float rounding only).
 
+Inside a Gemma-4 block (norms given), the source rank norms its tokens before step 1 (the router
+input rms_norm(x) / sqrt(d) * ffn_gate_inp_s, the expert input rms_norm(x) * ffn_pre_norm_2) and the
+combined rows after step 4 (rms_norm(out) * ffn_post_norm_2, gemma4.cpp:394-427): the output norm
+needs every rank's partial rows, so it cannot run inside the experts' kernels as on one GPU.
+
+Failure handling: with a Heartbeat, every rank announces each step in the process group's store
+before it launches anything, and waits (bounded) for the others' announcements; a rank that left
+(announced through Heartbeat.leave, or silent past the deadline) raises RankFailure on the others
+before their next collective, so no rank blocks in a collective that can never complete. A
+collective that fails anyway (the process group's own timeout) is reported as RankFailure too.
+
 The data path is collectives of fixed size (rows out, with a small message of their ids and
 weights, and partial rows back): each rank sends every rank a block of T rows, its own rows first
 and absent rows (ids all -1) after them, so no split sizes cross to the host and a step needs no
@@ -24,9 +35,56 @@ bookkeeping (which rows go where) is a handful of device-side index operations.
 """
 from __future__ import annotations
 
+import time
+from datetime import timedelta
+
 import numpy as np
 import torch
 import torch.distributed as dist
+
+
+class RankFailure(RuntimeError):
+    """A peer rank left or stopped answering; raised before this rank's next collective."""
+
+
+class Heartbeat:
+    """Per-step liveness through a torch.distributed Store (the process group's TCP store).
+
+    beat(step) records this rank at `step`, then waits until every other rank has recorded it too,
+    polling the store (a few ms apart) for at most deadline_s; a rank that called leave() fails the
+    wait at once. Keys older than two steps are deleted, so the store stays small."""
+
+    def __init__(self, store, rank: int, world: int, deadline_s: float = 30.0, prefix: str = "ep"):
+        self.store, self.rank, self.world, self.deadline_s, self.prefix = store, rank, world, deadline_s, prefix
+
+    def _key(self, step: int, r: int) -> str:
+        return f"{self.prefix}/s{step}/r{r}"
+
+    def _left(self, r: int) -> str:
+        return f"{self.prefix}/left/r{r}"
+
+    def beat(self, step: int) -> None:
+        self.store.set(self._key(step, self.rank), b"1")
+        others = [r for r in range(self.world) if r != self.rank]
+        t_end = time.monotonic() + self.deadline_s
+        pause = 1e-4
+        while True:
+            gone = [r for r in others if self.store.check([self._left(r)])]
+            if gone:
+                raise RankFailure(f"rank(s) {gone} left the expert-parallel group before step {step}")
+            missing = [r for r in others if not self.store.check([self._key(step, r)])]
+            if not missing:
+                break
+            if time.monotonic() > t_end:
+                raise RankFailure(f"rank(s) {missing} did not reach step {step} within {self.deadline_s:.1f} s")
+            time.sleep(pause)
+            pause = min(2 * pause, 5e-3)
+        if step >= 2:
+            self.store.delete_key(self._key(step - 2, self.rank))
+
+    def leave(self) -> None:
+        """Announce that this rank takes no further steps (call between steps)."""
+        self.store.set(self._left(self.rank), b"1")
 
 
 def owner(e: torch.Tensor, n_expert: int, world: int) -> torch.Tensor:
@@ -75,23 +133,68 @@ class EPMoE:
     the local compute; by default they are a MoELayer's route / forward_routed (sm_100a kernels).
     Tests on CPU pass host functions instead, over a gloo group."""
 
-    def __init__(self, n_expert: int, top_k: int, route_fn, experts_fn, group=None):
+    def __init__(self, n_expert: int, top_k: int, route_fn, experts_fn, group=None, norm_in=None, norm_out=None,
+                 heartbeat: Heartbeat | None = None):
+        """norm_in(x) -> (router input, expert input) and norm_out(rows) -> rows: the Gemma-4 block
+        norms (None: the plain layer). heartbeat: per-step liveness checks (None: none)."""
         self.E, self.k = n_expert, top_k
         self.route_fn, self.experts_fn = route_fn, experts_fn
+        self.norm_in, self.norm_out = norm_in, norm_out
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
+        self.heartbeat = heartbeat
+        self.step = 0
         self.timing = {}
 
     @classmethod
-    def from_layer(cls, layer, group=None):
+    def from_layer(cls, layer, group=None, norms=None, heartbeat: Heartbeat | None = None):
+        """From a plain MoELayer (no norms of its own); with `norms` (BlockNorms) the forward is the
+        Gemma-4 MoE block, its norms computed by moeb_rms_norm on the source rank."""
+        norm_in = norm_out = None
+        if norms is not None:
+            from . import capi
+
+            dev, d = layer.device, layer.host.d_model
+            pre, rsc, post = (torch.from_numpy(np.asarray(getattr(norms, n), np.float32).reshape(d)).to(dev)
+                              for n in ("pre_norm", "router_scale", "post_norm"))
+            eps = float(norms.eps)
+            c = float(np.float32(1.0) / np.sqrt(np.float32(d)))   # 1.0f / sqrtf((float) n_embd)
+
+            def rms(v, w, scale):
+                out = torch.empty_like(v)
+                capi.check(capi.lib().moeb_rms_norm(v.data_ptr(), v.shape[0], d, w.data_ptr(), scale, eps,
+                                                    out.data_ptr(), torch.cuda.current_stream(dev).cuda_stream))
+                return out
+
+            def norm_in(x):
+                return rms(x, rsc, c), rms(x, pre, 1.0)
+
+            def norm_out(rows):
+                return rms(rows, post, 1.0)
         return cls(layer.host.n_expert, layer.host.top_k, lambda x: layer.route(x)[1:],
-                   lambda rows, ids, w: layer.forward_routed(rows, ids, w), group)
+                   lambda rows, ids, w: layer.forward_routed(rows, ids, w), group, norm_in, norm_out, heartbeat)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        step = self.step
+        self.step += 1
+        if self.heartbeat is not None:
+            self.heartbeat.beat(step)
+        try:
+            return self._forward(x)
+        except RuntimeError as e:   # a collective that failed (peer gone, process-group timeout)
+            if isinstance(e, RankFailure):
+                raise
+            raise RankFailure(f"expert-parallel step {step} failed: {e}") from e
+
+    def _forward(self, x: torch.Tensor) -> torch.Tensor:
         G, d, k, dev = self.world, x.shape[1], self.k, x.device
         T = x.shape[0]
-        ids, w = self.route_fn(x)
+        if self.norm_in is not None:
+            x_router, x = self.norm_in(x)
+        else:
+            x_router = x
+        ids, w = self.route_fn(x_router)
         dest, present, _ = presence(ids, self.E, G)                        # [T, k], [G, T]
         # Fixed-capacity messages: each rank gets a block of T rows (its rows first, in token order,
         # then absent rows with every id -1), so the exchange needs no split sizes on the host and
@@ -127,6 +230,8 @@ class EPMoE:
         for r in range(G):
             got = back[(r * T + pos[r].clamp(min=0)).long()]
             out += torch.where(present[r][:, None], got, torch.zeros_like(got))
+        if self.norm_out is not None:
+            out = self.norm_out(out)
         return out
 
     __call__ = forward

@@ -131,9 +131,7 @@ class MoELayer:
 
     def prefill_path(self, n_tokens: int) -> bool:
         """Whether moeb_layer_forward runs n_tokens on the prefill (tensor-core GEMM) path."""
-        h = self.host
-        shape_ok = h.n_ff % 64 == 0 and h.d_model % 128 == 0 and h.d_model // 256 <= 16 and h.n_ff // 32 <= 32
-        return shape_ok and n_tokens >= int(capi.lib().moeb_set_prefill_min_tokens(0))
+        return int(capi.lib().moeb_layer_path(C.byref(self.c), max(int(n_tokens), 1))) == 1
 
     def mid_path(self, n_tokens: int, kind: int = 0) -> bool:
         """Whether a prefill-path forward of n_tokens runs projection `kind` (0 gate_up, 1 down) on the
@@ -147,7 +145,7 @@ class MoELayer:
         tiles = P // 128 + h.n_expert + 1
         chunk = 2 if kind == 0 else 4
         return (self.prefill_path(n_tokens) and m > 1 and P < m * h.n_expert and h.d_model % 256 == 0
-                and h.n_ff % 32 == 0 and tiles <= 512 and P // (8 * chunk) + tiles <= 1024)
+                and h.n_ff % 32 == 0 and h.n_ff <= 1024 and tiles <= 512 and P // (8 * chunk) + tiles <= 1024)
 
     def launches(self, n_tokens: int) -> int:
         """Kernels one forward of n_tokens launches: nine on the prefill path (with the block norms
@@ -231,3 +229,37 @@ class MoELayer:
     def device_error(self) -> int:
         s = torch.cuda.current_stream(self.device)
         return int(capi.lib().moeb_device_error(s.cuda_stream))
+
+
+class FfnBlock:
+    """The feed-forward part of a Gemma-4 MoE block (moeb_ffn_block_gemma4): out = the MoE block
+    (`moe`, a MoELayer with its norms) + the dense MLP branch (`mlp`, a one-expert MoELayer with the
+    dense norms ffn_norm / ffn_post_norm_1), the dense branch on a side stream when one is given."""
+
+    def __init__(self, moe: MoELayer, mlp: MoELayer):
+        assert moe.cn is not None and mlp.cn is not None, "both branches need their block norms"
+        assert moe.device == mlp.device
+        self.moe, self.mlp, self.device = moe, mlp, moe.device
+        self._ws = None
+
+    def workspace(self, n_tokens: int) -> torch.Tensor:
+        need = int(capi.lib().moeb_ffn_block_workspace_size(C.byref(self.moe.c), C.byref(self.mlp.c), n_tokens))
+        if self._ws is None or self._ws.numel() < need:
+            self._ws = torch.empty(need, dtype=torch.uint8, device=self.device)
+        return self._ws
+
+    def forward(self, x: torch.Tensor, out: torch.Tensor | None = None, stream: torch.cuda.Stream | None = None,
+                side_stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+        assert x.dtype == torch.float32 and x.is_contiguous() and x.device == self.device
+        T = x.shape[0]
+        if out is None:
+            out = torch.empty_like(x)
+        ws = self.workspace(T)
+        s = stream if stream is not None else torch.cuda.current_stream(self.device)
+        capi.check(capi.lib().moeb_ffn_block_gemma4(C.byref(self.moe.c), C.byref(self.moe.cn), C.byref(self.mlp.c),
+                                                    C.byref(self.mlp.cn), x.data_ptr(), T, out.data_ptr(),
+                                                    ws.data_ptr(), ws.numel(), s.cuda_stream,
+                                                    side_stream.cuda_stream if side_stream is not None else None))
+        return out
+
+    __call__ = forward

@@ -203,3 +203,55 @@ def algorithmic_bytes(host: HostLayer, ids: np.ndarray, n_tokens: int) -> int:
 def layer_flops(host: HostLayer, n_tokens: int) -> int:
     per_pair = 2 * (2 * host.n_ff) * host.d_model + 2 * host.d_model * host.n_ff
     return int(n_tokens * host.top_k * per_pair + n_tokens * 2 * host.d_model * host.n_expert)
+
+
+# ---------------------------------------------------------------- Gemma-4 dense (shared) MLP
+# The dense MLP beside the MoE in every Gemma-4 MoE block (third_party/llama/src/models/gemma4.cpp:
+# 376-391: build_ffn with GELU / PAR, gate and up [n_ff_dense x d], down [d x n_ff_dense]) is this
+# path's layer with one expert: a hot slot holding [gate rows; up rows] and down, zero router weights
+# with a bias that puts every token on expert 0 at top-1 (softmax weight exactly 1.0), scale 1.
+DENSE_D, DENSE_NFF, DENSE_E, DENSE_SEED = 2816, 2112, 32, 3
+
+
+def dense_mlp_f32(d: int = DENSE_D, nff: int = DENSE_NFF, seed: int = DENSE_SEED):
+    """f32 gate [nff, d], up [nff, d] and down [d, nff] of the dense MLP (N(0, 0.02))."""
+    return (_normal((seed, 5151, 0), (nff, d), 0.02), _normal((seed, 5151, 1), (nff, d), 0.02),
+            _normal((seed, 5151, 2), (d, nff), 0.02))
+
+
+def dense_as_layer(w_gate_q: np.ndarray, w_up_q: np.ndarray, w_down_q: np.ndarray, d: int, nff: int,
+                   gu_type: int = Q4_K, dn_type: int = Q5_0, n_expert: int = DENSE_E) -> HostLayer:
+    """A quantised dense GeGLU MLP as a one-expert MoE layer (see the block comment above)."""
+    b = np.full(n_expert, -1e4, np.float32)
+    b[0] = 0.0
+    return HostLayer(d_model=d, n_ff=nff, n_expert=n_expert, top_k=1, w_router=np.zeros((n_expert, d), np.float32),
+                     b_router=b, hot_ids=np.zeros(1, np.int32), hot_gu=np.concatenate([w_gate_q, w_up_q])[None],
+                     hot_down=np.asarray(w_down_q)[None], cold_gu=None, cold_down=None, hot_type_gu=gu_type,
+                     hot_type_down=dn_type, s_hot=np.ones(1, np.float32))
+
+
+def build_dense_layer(d: int = DENSE_D, nff: int = DENSE_NFF, seed: int = DENSE_SEED) -> HostLayer:
+    """The seeded dense MLP (Q4_K gate / up, Q5_0 down), quantised with this library's quantiser."""
+    def make():
+        g, u, w = dense_mlp_f32(d, nff, seed)
+        return np.concatenate([quantize(Q4_K, g).reshape(-1), quantize(Q4_K, u).reshape(-1),
+                               quantize(Q5_0, w).reshape(-1)])
+    blob = _cached(f"dense-v1|{seed}|{d}|{nff}", make)
+    ng = nff * capi.row_size(Q4_K, d)
+    g = blob[:ng].reshape(nff, -1)
+    u = blob[ng:2 * ng].reshape(nff, -1)
+    w = blob[2 * ng:].reshape(d, -1)
+    return dense_as_layer(g, u, w, d, nff)
+
+
+def make_dense_input(n_tokens: int, seed: int = DENSE_SEED) -> np.ndarray:
+    """Dense-MLP input rows [T, d] N(0, 1)."""
+    return _normal((seed, 7777, 0), (n_tokens, DENSE_D), 1.0)
+
+
+def dense_block_norms(d: int = DENSE_D, seed: int = DENSE_SEED):
+    """Seeded norms of the dense branch (f32 [d], eps 1e-6): ffn_norm and ffn_post_norm_1
+    1 + N(0, 0.1); router_scale ones (unused: the one-expert layer's router weights are zero)."""
+    from .layer import BlockNorms
+    v = [np.float32(1.0) + _normal((seed, 6161, i), (d,), 0.1) for i in range(2)]
+    return BlockNorms(pre_norm=v[0], router_scale=np.ones(d, np.float32), post_norm=v[1], eps=NORM_EPS)

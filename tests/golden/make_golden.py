@@ -5,6 +5,7 @@
     python tests/golden/make_golden.py --block   # golden_block.npz (the Gemma-4 block norms)
     python tests/golden/make_golden.py --types   # golden_types.npz + the IQ2_XXS tables (IQ2_XXS / Q8_0 weights)
     python tests/golden/make_golden.py --prefill # golden_prefill.npz (T=2048 prefill layer, stack layer 0)
+    python tests/golden/make_golden.py --dense   # golden_dense.npz (the Gemma-4 dense MLP, 2112 wide)
 
 Everything in the fixtures comes out of the reference's own code (ggml-base + ggml-cpu of the
 vendored llama.cpp, compiled into oracle/_ref): quantised bytes from ggml_quantize_chunk, dequantised
@@ -386,8 +387,34 @@ def main_prefill():
     print("wrote", path, os.path.getsize(path), "bytes")
 
 
+def main_dense():
+    """Gemma-4's dense MLP (d_model 2816, inner width 2112, Q4_K gate / up, Q5_0 down) through the
+    reference's own build_ffn nodes (ref_dense_ffn) and, as a one-expert layer, through its MoE graph:
+    the pools' digests, per-token digests of gate_up and of the GeGLU output, sampled output rows and
+    the output's RMS."""
+    from oracle.oracle import dense_as_expert_spec
+    r = Ref()
+    g, u, w = workload.dense_mlp_f32()
+    gq, uq, wq = r.quantize(Q4_K, g), r.quantize(Q4_K, u), r.quantize(Q5_0, w)
+    T, step = 64, 4
+    x = workload.make_dense_input(T)
+    dense = r.dense_ffn(x, Q4_K, gq, uq, Q5_0, wq, n_threads=8)
+    res = r.moe_layer(dense_as_expert_spec(x, Q4_K, gq, uq, Q5_0, wq), n_threads=8,
+                      want=("ids", "weights", "gate_up", "act"))
+    assert np.array_equal(res["out"].view(np.uint32), dense.view(np.uint32))
+    fx = {"sha_gate": np.array(sha(gq)), "sha_up": np.array(sha(uq)), "sha_down": np.array(sha(wq)),
+          "gate_up_digest": token_digests(res["gate_up"], T), "act_digest": token_digests(res["act"], T),
+          "out_digest": token_digests(dense, T), "out_rows": np.arange(0, T, step, dtype=np.int32),
+          "out": dense[::step], "out_rms": np.array(np.sqrt(np.mean(dense.astype(np.float64) ** 2)))}
+    path = os.path.join(HERE, "golden_dense.npz")
+    np.savez_compressed(path, **fx)
+    print("wrote", path, os.path.getsize(path), "bytes")
+
+
 if __name__ == "__main__":
-    if "--prefill" in sys.argv:
+    if "--dense" in sys.argv:
+        main_dense()
+    elif "--prefill" in sys.argv:
         main_prefill()
     elif "--types" in sys.argv:
         main_types()

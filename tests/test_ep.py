@@ -94,3 +94,97 @@ def test_dispatch_plan_dedups_per_rank():
     assert list(zip(r_idx.tolist(), t_idx.tolist())) == [(0, 0), (0, 2), (1, 0), (1, 1)]
     assert sent_ids.tolist() == [[0, 1, -1], [2, 3, 1], [-1, -1, 5], [4, 6, 7]]
     assert owner(torch.tensor([0, 3, 4, 7]), 8, 2).tolist() == [0, 0, 1, 1]
+
+
+def _norm_rows(v, w, scale=1.0, eps=1e-6):
+    s = 1.0 / torch.sqrt(torch.mean(v.double() ** 2, dim=1, keepdim=True) + eps)
+    return (v * s.float() * scale) * w
+
+
+def _norm_worker(rank, world, port):
+    """The Gemma-4 block around the expert-parallel layer: norms on the source rank before the
+    dispatch (router and expert inputs) and after the combine (output norm)."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        g = torch.Generator().manual_seed(9)
+        w_r = torch.randn((E, D), generator=g)
+        pre, rsc, post = (1 + 0.1 * torch.randn(D, generator=g) for _ in range(3))
+        x_all = torch.randn((world * T_LOCAL, D), generator=g) * 3
+        x = x_all[rank * T_LOCAL:(rank + 1) * T_LOCAL]
+
+        def experts_fn(rows, ids, w):
+            out = torch.zeros_like(rows)
+            for j in range(K):
+                for r in range(rows.shape[0]):
+                    if ids[r, j] >= 0:
+                        out[r] += w[r, j] * _expert(int(ids[r, j]), rows[r])
+            return out
+
+        ep = EPMoE(E, K, lambda xx: _route(xx, w_r, torch.zeros(E)), experts_fn,
+                   norm_in=lambda v: (_norm_rows(v, rsc, D ** -0.5), _norm_rows(v, pre)),
+                   norm_out=lambda v: _norm_rows(v, post))
+        out = ep(x)
+        ids, w = _route(_norm_rows(x, rsc, D ** -0.5), w_r, torch.zeros(E))
+        want = _norm_rows(_dense(_norm_rows(x, pre), ids, w), post)
+        torch.testing.assert_close(out, want, rtol=1e-5, atol=1e-5)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_ep_block_norms_world2():
+    mp.spawn(_norm_worker, args=(2, _free_port()), nprocs=2, join=True)
+
+
+def _leave_worker(rank, world, port, announce, q):
+    """Rank 1 takes one step and leaves between steps (announced, or silently); rank 0's next step
+    must fail with RankFailure on the host, before any collective, within the heartbeat deadline."""
+    import time
+    from datetime import timedelta
+
+    from llapis_b200.ep import Heartbeat, RankFailure
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    g = torch.Generator().manual_seed(5)
+    w_r = torch.randn((E, D), generator=g)
+    x = torch.randn((T_LOCAL, D), generator=g)
+    hb = Heartbeat(dist.distributed_c10d._get_default_store(), rank, world, deadline_s=2.0)
+    ep = EPMoE(E, K, lambda xx: _route(xx, w_r, torch.zeros(E)), lambda rows, ids, w: torch.zeros_like(rows),
+               heartbeat=hb)
+    ep(x)
+    if rank == 1:
+        if announce:
+            hb.leave()
+        q.put(("rank1", "left"))
+        q.close()
+        q.join_thread()   # the message is flushed before the process leaves
+        os._exit(0)       # between steps: none of its collectives in flight
+    t0 = time.monotonic()
+    try:
+        ep(x)
+        q.put(("rank0", "no failure raised"))
+    except RankFailure as e:
+        q.put(("rank0", f"ok {time.monotonic() - t0:.2f} {e}"))
+    q.close()
+    q.join_thread()
+    os._exit(0)       # the departed peer never joins a teardown
+
+
+@pytest.mark.parametrize("announce", [True, False])
+def test_ep_departed_rank_detected_on_host(announce):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_leave_worker, args=(r, 2, port, announce, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    msgs = dict(q.get(timeout=120) for _ in range(2))
+    for p in procs:
+        p.join(timeout=60)
+    status = msgs["rank0"]
+    assert status.startswith("ok"), status
+    elapsed = float(status.split()[1])
+    assert elapsed < (1.0 if announce else 10.0), status
+    assert ("left" in status) if announce else ("did not reach step 1" in status), status

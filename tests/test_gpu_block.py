@@ -113,3 +113,24 @@ def test_block_norm_invariance(prefill_from):
         a, _, _ = run_layer(host, x, aux_names=(), norms=norms)
         b, _, _ = run_layer(host, (x * np.float32(8.0)).astype(np.float32), aux_names=(), norms=norms)
         assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+
+
+def test_rms_norm_entry_vs_reference_fixture(golden_block):
+    """moeb_rms_norm (the norms the expert-parallel block applies around its exchange) against the
+    reference's rms_norm / scale / mul nodes: zero row and 1e-3 .. 1e3 magnitudes, bit for bit (the
+    double sum of the squares can differ from the reference's order only across an f32 rounding
+    boundary of the mean, which these rows do not meet)."""
+    import torch
+
+    from llapis_b200 import capi
+    from llapis_b200.workload import NORM_EPS
+    x = torch.from_numpy(golden_block["rms_x"]).cuda()
+    w = torch.from_numpy(golden_block["rms_w"]).cuda()
+    c = float(golden_block["rms_c"])
+    s = torch.cuda.current_stream().cuda_stream
+    for wt, scale, key in ((None, 1.0, "rms_plain"), (w, 1.0, "rms_weight"), (w, c, "rms_router")):
+        out = torch.empty_like(x)
+        capi.check(capi.lib().moeb_rms_norm(x.data_ptr(), x.shape[0], x.shape[1], None if wt is None else wt.data_ptr(),
+                                            scale, NORM_EPS, out.data_ptr(), s))
+        torch.cuda.synchronize()
+        assert np.array_equal(out.cpu().numpy().view(np.uint32), golden_block[key].view(np.uint32)), key

@@ -1,5 +1,6 @@
 """CPU: the restated oracle is pinned against the reference's golden fixtures (and against the
 reference build itself when oracle/_ref is present)."""
+import hashlib
 import numpy as np
 import pytest
 
@@ -354,3 +355,26 @@ def test_prefill_fixture_digests_match_port(port, name, rows):
             rowbits = np.ascontiguousarray(res[key][i * k:(i + 1) * k]).tobytes()
             d = np.frombuffer(hashlib.sha256(rowbits).digest()[:8], np.uint64)[0]
             assert d == g[f"{name}_{key}_digest"][t], (key, t)
+
+
+def test_dense_fixture_pins_port_and_quantiser(port):
+    """The dense MLP fixture (the reference's build_ffn at d_model 2816, inner width 2112): this
+    library's quantiser reproduces the reference's bytes, and the oracle's one-expert layer its
+    gate_up, GeGLU activations and outputs bit for bit."""
+    import os
+    from conftest import ROOT
+    g = dict(np.load(os.path.join(ROOT, "tests", "golden", "golden_dense.npz"), allow_pickle=False))
+    host = workload.build_dense_layer()
+    nff = host.n_ff
+    assert sha(host.hot_gu[0][:nff]) == str(g["sha_gate"]) and sha(host.hot_gu[0][nff:]) == str(g["sha_up"])
+    assert sha(host.hot_down[0]) == str(g["sha_down"])
+    T = 16
+    x = workload.make_dense_input(64)[:T]
+    res = port.moe_layer(spec_of(host, x), n_threads=4, want=("ids", "gate_up", "act"))
+    assert (res["ids"] == 0).all()
+    for key, fx in (("gate_up", "gate_up_digest"), ("act", "act_digest")):
+        rows = res[key].reshape(T, -1)
+        for t in range(T):
+            d = np.frombuffer(hashlib.sha256(np.ascontiguousarray(rows[t]).tobytes()).digest()[:8], np.uint64)[0]
+            assert d == g[fx][t], (key, t)
+    np.testing.assert_array_equal(res["out"][::4].view(np.uint32), g["out"][:T // 4].view(np.uint32))
