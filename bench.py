@@ -379,15 +379,17 @@ def run_ep(args, cfg, tokens_per_rank=None):
     # compute-only: the same local expert work on the rows this rank received, without communication
     recv_probe = {}
 
-    def experts_only():
-        layer.forward_routed(recv_probe["x"], recv_probe["ids"], recv_probe["w"])
-
     orig = ep.experts_fn
+
+    def experts_only():
+        orig(recv_probe["x"], recv_probe["ids"], recv_probe["w"])
+
     ep.experts_fn = lambda rx, ri, rw: (recv_probe.update(x=rx, ids=ri, w=rw), orig(rx, ri, rw))[1]
     ep(x)
     torch.cuda.synchronize()
     ep.experts_fn = orig
-    comp_ms = timed(experts_only, args.steps) if recv_probe["x"].shape[0] else 0.0
+    recv_rows = int(recv_probe["x"].shape[0])
+    comp_ms = timed(experts_only, args.steps) if recv_rows else 0.0
     # kernel profile of this rank's expert half
     lib = capi.lib()
     names = ("router", "topk", "dispatch", "actq", "gather", "gate_up", "geglu", "down", "combine")
@@ -427,8 +429,8 @@ def run_ep(args, cfg, tokens_per_rank=None):
                        "l2": "flushed between steps (256 MiB write, not timed)", "cuda_graph": False},
             "e2e": {"value": T * args.steps / (e2e_ms / 1e3), "unit": "tokens/s",
                     "h2d_bytes_per_step": int(x_host.nbytes) * world, "d2h_bytes_per_step": int(x_host.nbytes) * world},
-            # per step: router + top-k, then the seven kernels of the routed expert half
-            "gpu_launches": 9 * args.steps,
+            # per step: router + top-k, the Q8_K quantisation of the sent rows, then the routed expert half
+            "gpu_launches": (2 + 1 + layer.routed_launches(recv_rows)) * args.steps,
             "roofline": {"bound": "tensor", "achieved": ach, "peak": tflops_peak * world, "unit": "TFLOP/s",
                          "frac": ach / (tflops_peak * world), "traffic": None,
                          "peak_kind": f"{peak_kind} dense bf16 (burst) x {world} GPUs",

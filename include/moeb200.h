@@ -184,12 +184,21 @@ size_t moeb_routed_workspace_size(const moeb_layer *L, int32_t n_rows);
 int    moeb_layer_forward_routed(const moeb_layer *L, const float *x, int32_t n_rows, const int32_t *ids,
                                  const float *weights, float *out, void *workspace, size_t workspace_bytes,
                                  void *stream);
+/* The same expert half on rows already quantised to Q8_K (new): xq is [n_rows][d_model / 256] ggml
+ * block_q8_K (d f32 | qs[256] | bsums[16] i16, 292 bytes a block), as moeb_quantize_act(MOEB_T_Q8_K)
+ * writes it, 16-byte aligned. The experts consume exactly these bytes, so an expert-parallel host can
+ * send them in place of f32 rows (3,212 bytes a 2816-wide row instead of 11,264) with identical
+ * results. */
+int    moeb_layer_forward_routed_q8k(const moeb_layer *L, const void *xq, int32_t n_rows, const int32_t *ids,
+                                     const float *weights, float *out, void *workspace, size_t workspace_bytes,
+                                     void *stream);
 
 /* Sets the smallest batch that moeb_layer_forward runs on the prefill path (default 64; values
  * <= 0 leave it unchanged) and returns the previous value. Process-wide. No counterpart in the
  * reference (its ggml-cuda backend picks mul_mat_vec_q or mul_mat_q by batch size internally,
  * ggml-cuda.cu). Layers whose shape the prefill kernels do not cover (n_ff not a multiple of 64,
- * d_model not a multiple of 128, d_model > 4096 or n_ff > 1024) always take the decode path. */
+ * d_model not a multiple of 128, d_model > 4096 or n_ff > 4096) always take the decode path; layers
+ * whose decode kernel does not fit in shared memory always take the prefill path. */
 int32_t moeb_set_prefill_min_tokens(int32_t n_tokens);
 
 /* Sets the bound on the mean routed pairs per expert (top_k x n_tokens / n_expert) below which a

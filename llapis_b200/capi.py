@@ -86,6 +86,8 @@ SIGNATURES = {
     "moeb_routed_workspace_size": (C.c_size_t, [C.POINTER(Layer), C.c_int32]),
     "moeb_layer_forward_routed": (C.c_int, [C.POINTER(Layer), C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p,
                                             C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p]),
+    "moeb_layer_forward_routed_q8k": (C.c_int, [C.POINTER(Layer), C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p,
+                                                C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p]),
     "moeb_prefill_profile": (C.c_int, [C.c_int32]),
     "moeb_prefill_profile_read": (C.c_int, [C.POINTER(C.c_float), C.c_int32]),
     "moeb_bind_pools": (C.c_int, [C.c_int32, C.c_int32, C.c_void_p, C.c_int32, C.c_int32, C.c_void_p, C.c_int32,

@@ -433,11 +433,13 @@ extern "C" size_t moeb_routed_workspace_size(const moeb_layer *L, int32_t n_rows
     return carve_prefill(L, n_rows, nullptr).bytes;
 }
 
-extern "C" int moeb_layer_forward_routed(const moeb_layer *L, const float *x, int32_t n_rows, const int32_t *ids,
-                                         const float *weights, float *out, void *workspace, size_t workspace_bytes,
-                                         void *stream) {
+static int forward_routed(const moeb_layer *L, const float *x, const uint8_t *xq_rows, int32_t n_rows,
+                          const int32_t *ids, const float *weights, float *out, void *workspace, size_t workspace_bytes,
+                          void *stream) {
     int n_sms = 0;
-    int rc = check_forward(L, x, n_rows, out, workspace, workspace_bytes, L ? moeb_routed_workspace_size(L, n_rows) : 0,
+    // x or the Q8_K rows, whichever is given, stands for the input in the shared checks
+    const float *xin = x ? x : reinterpret_cast<const float *>(xq_rows);
+    int rc = check_forward(L, xin, n_rows, out, workspace, workspace_bytes, L ? moeb_routed_workspace_size(L, n_rows) : 0,
                            &n_sms);
     if (rc || n_rows == 0) return rc;
     if (!prefill_shape_ok(L))
@@ -466,12 +468,26 @@ extern "C" int moeb_layer_forward_routed(const moeb_layer *L, const float *x, in
     a.y = w.y;
     a.out = out;
     a.routed = 1;
+    a.xq_rows = xq_rows;
     a.mid_gu = use_mid(L, n_rows, 0) ? 1 : 0;
     a.mid_dn = use_mid(L, n_rows, 1) ? 1 : 0;
     a.md_max_cb = n_rows * k / 8 + w.max_tiles;
     cudaError_t e = launch_prefill(a, (cudaStream_t)stream, n_sms);
     if (e != cudaSuccess) return MOEB_ECUDA;
     return MOEB_OK;
+}
+
+extern "C" int moeb_layer_forward_routed(const moeb_layer *L, const float *x, int32_t n_rows, const int32_t *ids,
+                                         const float *weights, float *out, void *workspace, size_t workspace_bytes,
+                                         void *stream) {
+    return forward_routed(L, x, nullptr, n_rows, ids, weights, out, workspace, workspace_bytes, stream);
+}
+
+extern "C" int moeb_layer_forward_routed_q8k(const moeb_layer *L, const void *xq, int32_t n_rows, const int32_t *ids,
+                                             const float *weights, float *out, void *workspace, size_t workspace_bytes,
+                                             void *stream) {
+    if (n_rows > 0 && !xq) return fail(MOEB_EINVAL, "moeb_layer_forward_routed_q8k: null Q8_K rows");
+    return forward_routed(L, nullptr, (const uint8_t *)xq, n_rows, ids, weights, out, workspace, workspace_bytes, stream);
 }
 
 extern "C" int moeb_layer_forward(const moeb_layer *L, const float *x, int32_t n_tokens, float *out,

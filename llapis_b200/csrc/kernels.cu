@@ -2116,7 +2116,17 @@ cudaError_t launch_prefill(const PrefillArgs &a, cudaStream_t s, int n_sms) {
         if (e != cudaSuccess) return e;
         if ((e = prof_mark(s, mark++)) != cudaSuccess) return e;
     }
-    if (!nrm) {
+    if (!nrm && a.xq_rows) {
+        const uint8_t *rows = a.xq_rows;
+        int8_t *q = a.xq8;
+        float *xd = a.xd;
+        int16_t *bs = a.xbs;
+        int t = T, dd = d;
+        void *args[] = {&rows, &q, &xd, &bs, &t, &dd};
+        e = pf_launch("pf_unpack_q8k_kernel", (const void *)pf_unpack_q8k_kernel, dim3((T * (d / QK_K) + 7) / 8), dim3(256),
+                      0, s, true, args);
+        if (e != cudaSuccess) return e;
+    } else if (!nrm) {
         const float *x = a.x;
         int8_t *q = a.xq8;
         float *xd = a.xd;

@@ -185,6 +185,8 @@ struct PrefillArgs {
     float *out;                 // [T][d]
     float *y_pairs;             // optional [P][d] down outputs, pair order
     int32_t routed;             // 1: ids / w are given (the router and top-k kernels are skipped)
+    const uint8_t *xq_rows;     // routed only, optional: the tokens' Q8_K rows in ggml layout ([T][d / 256]
+                                // blocks of d f32 | qs[256] | bsums[16] i16), unpacked in place of quantising x
     int32_t mid_gu, mid_dn;     // 1: that projection runs the mid-size kernels (int8 MMAs on the weight codes;
                                 // bimg holds their operand images), 0: the tcgen05 kernels
     int32_t md_max_cb;          // mid path: bound on the column blocks (P / 8 + max_tiles)

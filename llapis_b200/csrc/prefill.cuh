@@ -1229,6 +1229,28 @@ __global__ void __launch_bounds__(256) pf_actq_kernel(const float *x, int8_t *xq
                         lane);
 }
 
+// Q8_K rows already quantised by the sender (the expert-parallel exchange carries them instead of
+// f32 rows), ggml layout per super-block: d f32 | qs[256] | bsums[16] i16 (292 bytes), split into the
+// xq8 / xd / xbs arrays pf_actq_kernel writes. One warp per (token, super-block), 73 words.
+__global__ void __launch_bounds__(256) pf_unpack_q8k_kernel(const uint8_t *rows, int8_t *xq8, float *xd, int16_t *xbs,
+                                                            int T, int d) {
+    pdl_wait();
+    pdl_launch_dependents();
+    const int nsb = d / QK_K;
+    const int item = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (item >= T * nsb) return;
+    const int t = item / nsb, sb = item - t * nsb;
+    const uint32_t *src = reinterpret_cast<const uint32_t *>(rows + (size_t)item * B_Q8_K);
+    uint32_t *qs = reinterpret_cast<uint32_t *>(xq8 + (size_t)t * d + sb * QK_K);
+    uint32_t *bs = reinterpret_cast<uint32_t *>(xbs + (size_t)item * 16);
+    for (int i = lane; i < B_Q8_K / 4; i += 32) {
+        const uint32_t v = __ldg(src + i);
+        if (i == 0) xd[item] = __uint_as_float(v);
+        else if (i <= QK_K / 4) qs[i - 1] = v;
+        else bs[i - 1 - QK_K / 4] = v;
+    }
+}
+
 // The Gemma-4 block norms' first kernel (in place of pf_actq_kernel, ahead of the router): per
 // token its rms_norm scale (written for the router) and the Q8_K rows of the expert input
 // rms_norm(x) * pre. One CTA per token, one warp per 256-value super-block: the squares of the

@@ -134,11 +134,14 @@ class EPMoE:
     Tests on CPU pass host functions instead, over a gloo group."""
 
     def __init__(self, n_expert: int, top_k: int, route_fn, experts_fn, group=None, norm_in=None, norm_out=None,
-                 heartbeat: Heartbeat | None = None):
+                 heartbeat: Heartbeat | None = None, encode_fn=None):
         """norm_in(x) -> (router input, expert input) and norm_out(rows) -> rows: the Gemma-4 block
-        norms (None: the plain layer). heartbeat: per-step liveness checks (None: none)."""
+        norms (None: the plain layer). heartbeat: per-step liveness checks (None: none).
+        encode_fn(x) -> wire rows: what the dispatch sends for each expert-input row (None: the f32
+        row); experts_fn then receives those rows."""
         self.E, self.k = n_expert, top_k
         self.route_fn, self.experts_fn = route_fn, experts_fn
+        self.encode_fn = encode_fn
         self.norm_in, self.norm_out = norm_in, norm_out
         self.group = group
         self.world = dist.get_world_size(group)
@@ -148,9 +151,11 @@ class EPMoE:
         self.timing = {}
 
     @classmethod
-    def from_layer(cls, layer, group=None, norms=None, heartbeat: Heartbeat | None = None):
+    def from_layer(cls, layer, group=None, norms=None, heartbeat: Heartbeat | None = None, wire: str = "q8k"):
         """From a plain MoELayer (no norms of its own); with `norms` (BlockNorms) the forward is the
-        Gemma-4 MoE block, its norms computed by moeb_rms_norm on the source rank."""
+        Gemma-4 MoE block, its norms computed by moeb_rms_norm on the source rank. wire "q8k": the
+        dispatch carries each row's Q8_K bytes (quantised once on the source rank: the bytes the
+        experts consume, 3.5x smaller than f32 at d_model 2816, identical results); "f32": f32 rows."""
         norm_in = norm_out = None
         if norms is not None:
             from . import capi
@@ -172,6 +177,11 @@ class EPMoE:
 
             def norm_out(rows):
                 return rms(rows, post, 1.0)
+        if wire == "q8k":
+            return cls(layer.host.n_expert, layer.host.top_k, lambda x: layer.route(x)[1:],
+                       lambda rows, ids, w: layer.forward_routed_q8k(rows, ids, w), group, norm_in, norm_out, heartbeat,
+                       encode_fn=layer.quantize_q8k)
+        assert wire == "f32", wire
         return cls(layer.host.n_expert, layer.host.top_k, lambda x: layer.route(x)[1:],
                    lambda rows, ids, w: layer.forward_routed(rows, ids, w), group, norm_in, norm_out, heartbeat)
 
@@ -211,11 +221,12 @@ class EPMoE:
         # token 0; their ids are all -1, so nothing reads them); ids and weights: a small second message
         inv = torch.zeros(G * T + 1, dtype=torch.int64, device=dev)
         inv.index_put_((idx,), torch.arange(T, device=dev).repeat(G))
-        sent_x = x.index_select(0, inv[:G * T])
+        wire = self.encode_fn(x) if self.encode_fn is not None else x
+        sent_x = wire.index_select(0, inv[:G * T])
         meta = torch.empty((G * T + 1, 2 * k), dtype=torch.float32, device=dev)
         meta[:G * T, :k] = torch.full((), -1, dtype=torch.int32, device=dev).view(torch.float32)   # absent ids
         meta.index_put_((idx,), torch.cat([sids.to(torch.int32).view(torch.float32), sw.float()], dim=2).reshape(G * T, 2 * k))
-        recv_x = torch.empty((G * T, d), dtype=x.dtype, device=dev)
+        recv_x = torch.empty((G * T, wire.shape[1]), dtype=wire.dtype, device=dev)
         recv_meta = torch.empty((G * T, 2 * k), dtype=torch.float32, device=dev)
         _a2a(recv_x, sent_x, None, None, self.group)
         _a2a(recv_meta, meta[:G * T], None, None, self.group)

@@ -148,12 +148,21 @@ class MoELayer:
                 and h.n_ff % 32 == 0 and h.n_ff <= 1024 and tiles <= 512 and P // (8 * chunk) + tiles <= 1024)
 
     def launches(self, n_tokens: int) -> int:
-        """Kernels one forward of n_tokens launches: nine on the prefill path (with the block norms
-        too: their kernel takes the activation quantiser's place), else one cooperative fused kernel
-        per 8-token chunk."""
+        """Kernels one forward of n_tokens launches. Prefill path: router, top-k, then the routed half
+        (routed_launches; with the block norms their kernel takes the activation quantiser's place).
+        Decode path: one cooperative fused kernel per 8-token chunk."""
         if n_tokens <= 0:
             return 0
-        return 9 if self.prefill_path(n_tokens) else (n_tokens + 7) // 8
+        return 2 + self.routed_launches(n_tokens) if self.prefill_path(n_tokens) else (n_tokens + 7) // 8
+
+    def routed_launches(self, n_rows: int) -> int:
+        """Kernels of the routed expert half (moeb_layer_forward_routed[_q8k]): dispatch, activation
+        quantisation (or the Q8_K rows' unpacking), gate_up (tcgen05: B-image gather, Q4_K min-term
+        kernel, GEMM; mid-size: operand images, GEMM), down (GeGLU images + GEMM on either path),
+        combine."""
+        if n_rows <= 0:
+            return 0
+        return 1 + 1 + (2 if self.mid_path(n_rows, 0) else 3) + 2 + 1
 
     def workspace_bytes(self, n_tokens: int) -> int:
         return int(capi.lib().moeb_layer_workspace_size(C.byref(self.c), n_tokens))
@@ -224,6 +233,35 @@ class MoELayer:
         capi.check(capi.lib().moeb_layer_forward_routed(C.byref(self.c), x.data_ptr(), n, ids.data_ptr(), w.data_ptr(),
                                                         out.data_ptr(), self._ws.data_ptr(), self._ws.numel(),
                                                         s.cuda_stream))
+        return out
+
+    def quantize_q8k(self, x: torch.Tensor, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+        """x's Q8_K rows (uint8 [T, d / 256 * 292], ggml block_q8_K), the bytes the experts consume."""
+        assert x.dtype == torch.float32 and x.is_contiguous() and x.device == self.device
+        T, d = x.shape
+        out = torch.empty((T, capi.row_size(capi.Q8_K, d)), dtype=torch.uint8, device=self.device)
+        if T:
+            s = stream if stream is not None else torch.cuda.current_stream(self.device)
+            capi.check(capi.lib().moeb_quantize_act(capi.Q4_K, x.data_ptr(), out.data_ptr(), T, d, s.cuda_stream))
+        return out
+
+    def forward_routed_q8k(self, xq: torch.Tensor, ids: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None,
+                           stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+        """forward_routed on rows already quantised to Q8_K (moeb_layer_forward_routed_q8k)."""
+        assert xq.dtype == torch.uint8 and xq.is_contiguous() and xq.device == self.device
+        assert ids.dtype == torch.int32 and w.dtype == torch.float32 and ids.is_contiguous() and w.is_contiguous()
+        n = xq.shape[0]
+        if out is None:
+            out = torch.empty((n, self.host.d_model), dtype=torch.float32, device=self.device)
+        if n == 0:
+            return out
+        need = int(capi.lib().moeb_routed_workspace_size(C.byref(self.c), n))
+        if self._ws is None or self._ws.numel() < need:
+            self._ws = torch.empty(need, dtype=torch.uint8, device=self.device)
+        s = stream if stream is not None else torch.cuda.current_stream(self.device)
+        capi.check(capi.lib().moeb_layer_forward_routed_q8k(C.byref(self.c), xq.data_ptr(), n, ids.data_ptr(),
+                                                            w.data_ptr(), out.data_ptr(), self._ws.data_ptr(),
+                                                            self._ws.numel(), s.cuda_stream))
         return out
 
     def device_error(self) -> int:

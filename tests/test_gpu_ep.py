@@ -37,6 +37,22 @@ def test_routed_halves_sum_to_full():
     assert torch.count_nonzero(none).item() == 0
 
 
+def test_routed_q8k_rows_equal_f32_rows():
+    """The expert half on Q8_K rows quantised by moeb_quantize_act gives the same bits as on the f32
+    rows it quantises itself (the expert-parallel exchange sends the Q8_K rows)."""
+    host = host_layer("decode_t4_mixed")
+    layer = MoELayer(host)
+    x = torch.from_numpy(workload.make_input(workload.CONFIGS["decode_t4_mixed"], n_tokens=150, stream=4)).cuda()
+    _, ids, w = layer.route(x)
+    a = layer.forward_routed(x, ids, w).clone()
+    xq = layer.quantize_q8k(x)
+    assert xq.shape == (150, 11 * 292)
+    b = layer.forward_routed_q8k(xq, ids, w).clone()
+    torch.cuda.synchronize()
+    assert torch.equal(a.view(torch.int32), b.view(torch.int32))
+    assert layer.device_error() == 0
+
+
 def test_ep_world1_matches_layer():
     from llapis_b200.ep import EPMoE
     with socket.socket() as s:
@@ -49,6 +65,8 @@ def test_ep_world1_matches_layer():
         layer = MoELayer(host)
         x = torch.from_numpy(workload.make_input(workload.CONFIGS["mini_mixed"], n_tokens=300, stream=8)).cuda()
         out = EPMoE.from_layer(layer)(x)
+        out_f32 = EPMoE.from_layer(layer, wire="f32")(x)
+        assert torch.equal(out.view(torch.int32), out_f32.view(torch.int32))   # Q8_K rows on the wire: same bits
         want = layer(x)
         assert_layer_close(out.cpu().numpy(), want.cpu().numpy(), tol=5e-5 if layer.prefill_path(300) else 5e-4)
     finally:
