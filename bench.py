@@ -368,13 +368,35 @@ def run_ep(args, cfg, tokens_per_rank=None):
         ep(x)
     torch.cuda.synchronize()
     dist.barrier()
+    # one step as a CUDA graph (router, the exchange's bookkeeping, the three all-to-alls and both
+    # expert halves): the fixed-size exchange needs no host synchronisation, so the whole step
+    # captures; every rank captures at the same point (NCCL calls are recorded, not run)
+    graph, graph_note = None, "eager launches"
+    if not args.no_graph:
+        try:
+            cap = torch.cuda.Stream(dev)
+            cap.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(cap):
+                for _ in range(3):
+                    ep(x)
+            torch.cuda.current_stream(dev).wait_stream(cap)
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                ep(x)
+            torch.cuda.synchronize()
+            graph, graph_note = g, "one CUDA graph per step (NCCL all-to-alls captured)"
+        except RuntimeError as e:   # capture refused: time the eager step instead
+            graph_note = f"eager launches (graph capture failed: {str(e)[:120]})"
+        dist.barrier()
+    step = graph.replay if graph is not None else (lambda: ep(x))
     with Clocks(local) as clk:
         # keep the GPU loaded while the sampler takes its first readings: a FIXED number of steps,
         # the same on every rank (each step holds collectives, so ranks must take the same count)
         for _ in range(160):
-            ep(x)
+            step()
         torch.cuda.synchronize()
-        dev_ms = timed(lambda: ep(x), args.steps)
+        dev_ms = timed(step, args.steps)
     dist.barrier()
     # compute-only: the same local expert work on the rows this rank received, without communication
     recv_probe = {}
@@ -411,6 +433,7 @@ def run_ep(args, cfg, tokens_per_rank=None):
     tot = torch.tensor([dev_ms, comp_ms, e2e_ms], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(tot, op=dist.ReduceOp.MAX)
+    del step, graph   # a graph holding NCCL calls is released before the process group goes
     dev_ms, comp_ms, e2e_ms = tot.tolist()
     hbm, tflops_peak, peak_kind = measured_peaks()
     avg_ms = dev_ms / args.steps
@@ -426,7 +449,8 @@ def run_ep(args, cfg, tokens_per_rank=None):
             "config": {"workload": cfg.name, "n_tokens": T, "layers": 1, "d_model": cfg.d_model,
                        "n_expert": cfg.n_expert, "top_k": cfg.top_k, "parallelism": f"ep{world}",
                        "experts_per_gpu": cfg.n_expert // world, "tokens_per_gpu": T // world,
-                       "l2": "flushed between steps (256 MiB write, not timed)", "cuda_graph": False},
+                       "l2": "flushed between steps (256 MiB write, not timed)", "cuda_graph": graph_note,
+                       "wire": "Q8_K rows out, f32 partial rows back"},
             "e2e": {"value": T * args.steps / (e2e_ms / 1e3), "unit": "tokens/s",
                     "h2d_bytes_per_step": int(x_host.nbytes) * world, "d2h_bytes_per_step": int(x_host.nbytes) * world},
             # per step: router + top-k, the Q8_K quantisation of the sent rows, then the routed expert half

@@ -146,12 +146,9 @@ struct PfTile {
     int32_t n;       // pairs
 };
 MOEB_HD inline int prefill_max_tiles(int P, int E) { return P / kPrefillTile + E + 1; }
-// fp16 operand images of one tile in the tensor cores' canonical layout: 128 rows x 18 core
-// columns (128 values + 16 min-term columns) per half super-block for gate_up, 128 rows x 8 core
-// columns (two 32-blocks) per down stage; 16 bytes per core row
-constexpr int kPfGuImageBytes = kPrefillTile * 18 * 16;
-// B operand images of the lane-exact gate_up GEMM (gateup_lx.cuh): per tile, pass (0..3) and
-// super-block one image of 16 row groups x 8 cores x 128 B, pass-major
+// fp16 operand images of one tile in the tensor cores' canonical layout (16 bytes per core row).
+// gate_up (gateup_lx.cuh): per tile, pass (0..3) and super-block one image of 16 row groups x 8
+// cores x 128 B, pass-major; down: 128 rows x 8 core columns (two 32-blocks) per stage
 constexpr int kLxImgMain = (kPrefillTile / 8) * 8 * 128;
 MOEB_HD inline size_t lx_tile_bytes(int nsb) { return (size_t)nsb * 4 * kLxImgMain; }
 MOEB_HD inline size_t lx_image_off(int nsb, int pass, int sb) { return (size_t)(pass * nsb + sb) * kLxImgMain; }

@@ -1,40 +1,41 @@
 // Prefill path of the MoE-FFN layer: the same layer as the fused decode kernel, for batches large
-// enough that every routed expert sees many tokens. Seven kernels chained with programmatic
+// enough that every routed expert sees many tokens. Ten kernels chained with programmatic
 // dependent launch:
 //
-//   pf_router_kernel   : router logits, f32 GEMM (ggml mul_mat of ffn_gate_inp, gemma4.cpp:403)
-//   pf_topk_kernel     : softmax -> top-k (value desc, index asc) -> normalised weights
-//                        (llama-graph.cpp:1553-1648), one warp per token
-//   pf_dispatch_kernel : histogram, exclusive scan and stable permutation of the routed pairs
-//                        (ggml-cpu.c:1613-1626 grouping; mmid.cu:28 on the GPU) plus the per-expert
-//                        tile list the grouped GEMMs walk
-//   pf_actq_kernel     : Q8_K quantisation of every token (quantize_row_q8_K, x86/quants.c:505)
-//   pf_gather_kernel   : per expert tile, the tokens' Q8_K values as fp16 operand images
-//   pf_gate_up_kernel  : tcgen05 grouped GEMM, gate_up of every tile (f32 rows, slot order)
-//   pf_geglu_kernel    : GeGLU (fp16-table GELU, vec.h:1414) and Q8_0 quantisation of its output
-//                        (x86/quants.c:302) into the down kernel's fp16 operand images
-//   pf_down_kernel     : tcgen05 grouped GEMM, down projection, per-expert down scale
-//   pf_combine_kernel  : out[t] = sum_j w[t,j] * y[t,j] in j order (llama-graph.cpp:1814-1848)
+//   pf_router_kernel     : router logits, f32 GEMM (ggml mul_mat of ffn_gate_inp, gemma4.cpp:403)
+//   pf_topk_kernel       : softmax -> top-k (value desc, index asc) -> normalised weights
+//                          (llama-graph.cpp:1553-1648), one warp per token
+//   pf_dispatch_kernel   : histogram, exclusive scan and stable permutation of the routed pairs
+//                          (ggml-cpu.c:1613-1626 grouping; mmid.cu:28 on the GPU) plus the per-expert
+//                          tile list the grouped GEMMs walk
+//   pf_actq_kernel       : Q8_K quantisation of every token (quantize_row_q8_K, x86/quants.c:505);
+//                          pf_actq_norm_kernel with the block norms, pf_unpack_q8k_kernel for rows
+//                          that arrive already quantised
+//   pf_gather_lx_kernel  : per expert tile, the tokens' Q8_K values as fp16 operand images in the
+//                          reference's lane order (gateup_lx.cuh)
+//   pf_q4k_min_kernel    : the Q4_K min term of every (row, pair) (gateup_lx.cuh)
+//   pf_gate_up_lx_kernel : tcgen05 grouped GEMM, gate_up of every tile in the reference's float
+//                          order (gateup_lx.cuh), f32 rows in slot order
+//   pf_geglu_kernel      : GeGLU (fp16-table GELU, vec.h:1414) and Q8_0 quantisation of its output
+//                          (x86/quants.c:302) into the down kernel's fp16 operand images
+//   pf_down_kernel       : tcgen05 grouped GEMM, down projection, per-expert down scale
+//   pf_combine_kernel    : out[t] = sum_j w[t,j] * y[t,j] in j order (llama-graph.cpp:1814-1848)
 //
 // Integer-exact tensor-core formulation. ggml-cpu computes the expert matmuls as integer block
 // dot products scaled per block (ggml_vec_dot_q4_K_q8_K, x86/quants.c:1900; _iq2_s_q8_K :2937;
 // _q5_0_q8_0; _iq4_nl_q8_0). The MMAs here reproduce the integer sums exactly with kind::f16
 // operands that are small integers (exactly representable in fp16) and fp32 accumulation, and
 // apply the per-block float scales in the epilogue ("promotion"):
-//   gate_up Q4_K : A = sc_j * q (<= 945), B = q8; one accumulator per 256-value super-block,
-//                  promoted with d_w * d_x. The min term sum_j m_j * bsum_j goes through one extra
-//                  K=16 MMA into a second accumulator: A = [64 m_j | m_j], B = [bsum_j >> 6 |
-//                  bsum_j & 63], promoted with dmin_w * d_x.
-//   gate_up IQ2_S: A = ls * (+-grid) (<= 1333), B = q8, promoted with d_w * d_x / 8.
+//   gate_up      : gateup_lx.cuh (one accumulator per reference lane, the lanes' f32 chains in the
+//                  reference's order).
 //   down Q5_0    : A = q - 16; B = d_x * q8 (the Q8_0 GeGLU output, dequantised) split exactly
 //                  into fp16 hi + lo, two MMAs per K step; promoted per 32-block with d_w.
 //   down IQ4_NL  : A = kvalues_iq4nl[q], B as for Q5_0.
 // Converter warps build the fp16 weight (A) tiles in shared memory; the activation (B) tiles are
-// fp16 images in HBM (written by pf_gather_kernel for gate_up, by the gate_up epilogue for down)
-// fetched with one bulk copy per stage. Converter warps build the A tiles (canonical no-swizzle K-major
-// layout: 8-row x 16-byte core matrices), one thread issues the MMAs, accumulators live in TMEM
-// (double- or quadruple-buffered so the MMAs of the next block overlap the promotion of the last),
-// and epilogue warps read them back with tcgen05.ld.
+// fp16 images in HBM (written by pf_geglu_kernel) fetched with one bulk copy per stage. The A tiles
+// use the canonical no-swizzle K-major layout (8-row x 16-byte core matrices), one thread issues
+// the MMAs, accumulators live in TMEM (quadruple-buffered so the MMAs of the next block overlap the
+// promotion of the last), and epilogue warps read them back with tcgen05.ld.
 #pragma once
 
 namespace moeb {
@@ -124,16 +125,6 @@ constexpr int kPfM = 128;             // weight rows per work unit = MMA M (TMEM
 constexpr int kPfConvWarps = 4;       // thread i builds A row i (a weight row) and B row i (a pair)
 constexpr int kPfMmaWarp = kPfConvWarps;
 constexpr int kPfEpiWarp0 = kPfConvWarps + 1;
-constexpr int kPfEpiWarps = 8;        // two per TMEM lane quadrant, one per half of the columns
-// 13 warps: at most 4 share an SM sub-partition's 16K registers, so a thread may hold 128
-constexpr int kPfThreads = (kPfConvWarps + 1 + kPfEpiWarps) * 32;
-// gate_up: a stage is half a super-block, 128 values (+ 16 min-term columns in the first half of
-// a Q4_K super-block): 18 core columns of 8 values
-constexpr int kGuKc = 18;
-constexpr int kGuTileBytes = kPfM * kGuKc * 16;
-constexpr int kGuStages = 3;
-constexpr int kGegluBatch = 8;        // GeGLU items a warp reduces together
-constexpr int kGegluItems = 2 * kPrefillTile / 8;   // items per epilogue warp: 2 blocks x 128 pairs / 8 warps
 // down: a stage is two 32-blocks (8 core columns); four accumulator buffers of 128 columns
 constexpr int kDnKc = 8;
 constexpr int kDnTileBytes = kPfM * kDnKc * 16;
@@ -150,14 +141,6 @@ __device__ __forceinline__ uint32_t canon_off(int r, int c, int kc) {
     return (uint32_t)((((r >> 3) * kc + c) << 7) + ((r & 7) << 4));
 }
 
-struct GuSmem {
-    uint8_t a[kGuStages][kGuTileBytes];
-    uint8_t b[kGuStages][kGuTileBytes];
-    float dxs[kPrefillMaxSb][kPfN];     // Q8_K scale of each tile column, per super-block
-    uint64_t full[kGuStages], empty[kGuStages], accfull[2], accempty[2], done, epibar;
-    uint32_t tmem;
-    int32_t abort;
-};
 struct DnSmem {
     uint8_t a[kDnStages][kDnTileBytes];
     uint8_t b[kDnStages][2 * kDnTileBytes];   // hi and lo halves of dx * q8
@@ -183,7 +166,7 @@ __device__ __forceinline__ bool warp_aborted(volatile int32_t *abort) { return _
 __device__ __forceinline__ bool pf_wait_warp(uint64_t *bar, uint32_t parity, volatile int32_t *abort) {
     return __all_sync(0xffffffffu, pf_wait(bar, parity, abort));
 }
-// Barrier of the epilogue warps on an mbarrier (count kPfEpiWarps): bounded, unlike bar.sync, so a
+// Barrier of the epilogue warps on an mbarrier (count: the epilogue warps): bounded, unlike bar.sync, so a
 // warp that gave up cannot leave the others waiting for good.
 __device__ __forceinline__ bool epi_barrier(uint64_t *bar, uint32_t &phase, volatile int32_t *abort) {
     __syncwarp();
@@ -221,107 +204,6 @@ __device__ __forceinline__ uint32_t pack_h2i(int a, int b) {
 }
 __device__ __forceinline__ void sts128(uint8_t *p, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
     *reinterpret_cast<uint4 *>(p) = make_uint4(a, b, c, d);
-}
-
-
-// Raw bytes of one gate_up stage, loaded into registers ahead of their conversion (read-only
-// global loads, so they may be issued before the shared-memory stores of the previous step).
-struct GuARaw {
-    uint4 v[5];   // Q4_K: header (d, dmin, scales) + the 64 qs bytes of this half;
-                  // IQ2_S: grid bytes, sign bytes, qh and scale words of this half (11 words)
-};
-
-__device__ __forceinline__ void gu_a_load(const uint8_t *blk, int h, bool q4, GuARaw &a) {
-    if (q4) {
-        a.v[0] = __ldg(reinterpret_cast<const uint4 *>(blk));
-#pragma unroll
-        for (int i = 0; i < 4; ++i) a.v[1 + i] = __ldg(reinterpret_cast<const uint4 *>(blk + 16 + 64 * h + 16 * i));
-    } else {   // 2-byte aligned block: 16-bit loads
-        const unsigned short *b16 = reinterpret_cast<const unsigned short *>(blk);
-        uint32_t w[11];
-#pragma unroll
-        for (int ii = 0; ii < 4; ++ii) {
-            w[ii] = (uint32_t)__ldg(b16 + 1 + 8 * h + 2 * ii) | ((uint32_t)__ldg(b16 + 2 + 8 * h + 2 * ii) << 16);
-            w[4 + ii] = (uint32_t)__ldg(b16 + 17 + 8 * h + 2 * ii) | ((uint32_t)__ldg(b16 + 18 + 8 * h + 2 * ii) << 16);
-        }
-        w[8] = (uint32_t)__ldg(b16 + 33 + 2 * h) | ((uint32_t)__ldg(b16 + 34 + 2 * h) << 16);
-        w[9] = (uint32_t)__ldg(b16 + 37 + 2 * h) | ((uint32_t)__ldg(b16 + 38 + 2 * h) << 16);
-        w[10] = 0;
-        a.v[0] = make_uint4(w[0], w[1], w[2], w[3]);
-        a.v[1] = make_uint4(w[4], w[5], w[6], w[7]);
-        a.v[2] = make_uint4(w[8], w[9], w[10], 0u);
-    }
-}
-
-// A rows of one gate_up stage (half `h` of a super-block), Q4_K: sc_j * q, then (h == 0) the
-// min-term columns [64 m_0..7 | m_0..7]
-__device__ __forceinline__ void gu_a_q4k(const GuARaw &a, int h, uint8_t *tile, int r) {
-    const uint4 hdr = a.v[0];
-    uint8_t sc12[12];
-    *reinterpret_cast<uint32_t *>(sc12 + 0) = hdr.y;
-    *reinterpret_cast<uint32_t *>(sc12 + 4) = hdr.z;
-    *reinterpret_cast<uint32_t *>(sc12 + 8) = hdr.w;
-    uint32_t W[16];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        W[4 * i] = a.v[1 + i].x; W[4 * i + 1] = a.v[1 + i].y; W[4 * i + 2] = a.v[1 + i].z; W[4 * i + 3] = a.v[1 + i].w;
-    }
-#pragma unroll
-    for (int ii = 0; ii < 2; ++ii) {
-        int slo, mlo, shi, mhi;
-        q4k_scale_min(4 * h + 2 * ii, sc12, slo, mlo);
-        q4k_scale_min(4 * h + 2 * ii + 1, sc12, shi, mhi);
-        const __half2 s2l = __float2half2_rn((float)slo), ns2l = __float2half2_rn(-1024.f * slo);
-        const __half2 s2h = __float2half2_rn((float)shi), ns2h = __float2half2_rn(-1024.f * shi);
-#pragma unroll
-        for (int cq = 0; cq < 4; ++cq) {
-            const uint32_t w0 = W[8 * ii + 2 * cq], w1 = W[8 * ii + 2 * cq + 1];
-            uint32_t o0, o1, o2, o3;
-            scale4(w0 & 0x0f0f0f0fu, s2l, ns2l, o0, o1);
-            scale4(w1 & 0x0f0f0f0fu, s2l, ns2l, o2, o3);
-            sts128(tile + canon_off(r, 8 * ii + cq, kGuKc), o0, o1, o2, o3);
-            scale4((w0 >> 4) & 0x0f0f0f0fu, s2h, ns2h, o0, o1);
-            scale4((w1 >> 4) & 0x0f0f0f0fu, s2h, ns2h, o2, o3);
-            sts128(tile + canon_off(r, 8 * ii + 4 + cq, kGuKc), o0, o1, o2, o3);
-        }
-    }
-    if (h == 0) {
-        int m[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) { int sc; q4k_scale_min(j, sc12, sc, m[j]); }
-        sts128(tile + canon_off(r, 16, kGuKc), pack_h2i(64 * m[0], 64 * m[1]), pack_h2i(64 * m[2], 64 * m[3]),
-               pack_h2i(64 * m[4], 64 * m[5]), pack_h2i(64 * m[6], 64 * m[7]));
-        sts128(tile + canon_off(r, 17, kGuKc), pack_h2i(m[0], m[1]), pack_h2i(m[2], m[3]), pack_h2i(m[4], m[5]),
-               pack_h2i(m[6], m[7]));
-    }
-}
-
-// A rows of one gate_up stage, IQ2_S (dequantize_row_iq2_s, ggml-quants.c:2471): ls * (+-grid)
-// with ls = 2 * scale_nibble + 1; the d / 8 factor goes to the epilogue.
-__device__ __forceinline__ void gu_a_iq2s(const GuARaw &a, uint8_t *tile, int r) {
-    const uint32_t g[4] = {a.v[0].x, a.v[0].y, a.v[0].z, a.v[0].w};
-    const uint32_t sg[4] = {a.v[1].x, a.v[1].y, a.v[1].z, a.v[1].w};
-    const uint32_t qh = a.v[2].x, scb = a.v[2].y;
-#pragma unroll
-    for (int ii = 0; ii < 4; ++ii) {
-        const uint32_t qhb = (qh >> (8 * ii)) & 0xffu, sc = (scb >> (8 * ii)) & 0xffu;
-#pragma unroll
-        for (int l = 0; l < 4; ++l) {
-            const uint32_t idx = ((g[ii] >> (8 * l)) & 0xffu) | (((qhb >> (2 * l)) & 3u) << 8);
-            const uint64_t grid = g_iq2s_grid[idx];
-            const int ls = 2 * (int)((sc >> (4 * (l >> 1))) & 0xfu) + 1;
-            const __half2 s2 = __float2half2_rn((float)ls), ns2 = __float2half2_rn(-1024.f * ls);
-            uint32_t o0, o1, o2, o3;
-            scale4((uint32_t)grid, s2, ns2, o0, o1);
-            scale4((uint32_t)(grid >> 32), s2, ns2, o2, o3);
-            const uint32_t s8 = (sg[ii] >> (8 * l)) & 0xffu;
-            o0 ^= ((s8 & 1u) << 15) | ((s8 & 2u) << 30);
-            o1 ^= ((s8 & 4u) << 13) | ((s8 & 8u) << 28);
-            o2 ^= ((s8 & 16u) << 11) | ((s8 & 32u) << 26);
-            o3 ^= ((s8 & 64u) << 9) | ((s8 & 128u) << 24);
-            sts128(tile + canon_off(r, 4 * ii + l, kGuKc), o0, o1, o2, o3);
-        }
-    }
 }
 
 
@@ -398,7 +280,7 @@ struct PfParams {
     const int8_t *xq8;                // [T][d] Q8_K values
     const float *xd;                  // [T][d/256] Q8_K scales
     const int16_t *xbs;               // [T][d/256][16] Q8_K bsums
-    uint8_t *bimg;                    // gate_up B operand images, [tile][sb][half][kPfGuImageBytes]
+    uint8_t *bimg;                    // gate_up B operand images, [tile][pass][sb][kLxImgMain] (or the mid path's)
     float *dxt;                       // [tile][sb][128] Q8_K scale of each tile row
     uint32_t *bst;                    // [tile][sb][128][8] Q8_K bsums of each tile row, fp16 pairs
     float *hbuf;                      // [slot][2 n_ff] gate_up outputs, f32
@@ -410,201 +292,6 @@ struct PfParams {
 
 __device__ __forceinline__ const uint8_t *tile_rows(const PoolView &pv, int widx, int rows, int d_in) {
     return pool_entry(pv, widx, rows, d_in);
-}
-
-// ---------------------------------------------------------------- gate_up grouped GEMM
-// Work unit (tile, mb): the pairs of one expert tile against 64 gate rows [64 mb, 64 mb + 64) and
-// the matching 64 up rows, so GeGLU pairs sit in the same CTA. Persistent: CTA b takes units
-// b, b + grid, ...; the 11 units of a tile run side by side, sharing its activations in L2.
-__global__ void __launch_bounds__(kPfThreads, 1) pf_gate_up_kernel(PfParams p) {
-    extern __shared__ __align__(1024) uint8_t pf_smem[];
-    GuSmem &S = *reinterpret_cast<GuSmem *>(pf_smem);
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    if (tid == 0) {
-        for (int s = 0; s < kGuStages; ++s) { mbar_init(&S.full[s], kPfConvWarps + 1); mbar_init(&S.empty[s], 1); }
-        for (int b = 0; b < 2; ++b) { mbar_init(&S.accfull[b], 1); mbar_init(&S.accempty[b], kPfEpiWarps); }
-        mbar_init(&S.done, 1);
-        mbar_init(&S.epibar, kPfEpiWarps);
-        S.abort = 0;
-        fence_mbar_init();
-    }
-    if (warp == kPfMmaWarp) tmem_alloc_warp(&S.tmem, 512);
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t tmem = S.tmem;
-    volatile int32_t *abort = &S.abort;
-    pdl_wait();
-    const int nsb = p.d / QK_K, n_mb = p.nff / 64;
-    const int units = *p.n_tiles * n_mb;
-    const int gu_rows = 2 * p.nff;
-
-    if (warp < kPfConvWarps) {
-        // ------------------------------------------------ converters
-        // Thread i expands weight row i; thread 0 also fetches the stage's B operand image (built by
-        // pf_gather_kernel) with one bulk copy. Software-pipelined: the raw rows of a stage are
-        // loaded two stages ahead (one register buffer per half super-block).
-        int it = 0;
-        GuARaw ar0, ar1;
-        for (int u = blockIdx.x; u < units && !warp_aborted(abort); u += gridDim.x) {
-            const int ti = u / n_mb, mb = u - ti * n_mb;
-            const PfTile tl = p.tiles[ti];
-            const PoolView &pv = p.gu[tl.cls];
-            const bool q4 = pv.type == T_Q4_K;
-            const int bsz = q4 ? B_Q4_K : B_IQ2_S;
-            const int rb = (int)row_bytes(pv.type, p.d);
-            const uint32_t bbytes = (uint32_t)(((tl.n + 15) & ~15) / 8) * (kGuKc * 128);
-            const uint8_t *bsrc = p.bimg + (size_t)ti * nsb * 2 * kPfGuImageBytes;
-            const int r = tid;
-            const int wr = r < 64 ? 64 * mb + r : p.nff + 64 * mb + (r - 64);
-            const uint8_t *arow = tile_rows(pv, tl.widx, gu_rows, p.d) + (size_t)wr * rb;
-            gu_a_load(arow, 0, q4, ar0);
-            gu_a_load(arow, 1, q4, ar1);
-            bool ok = true;
-            for (int sb = 0; sb < nsb && ok; ++sb) {
-#pragma unroll
-                for (int h = 0; h < 2; ++h, ++it) {
-                    const int s = it % kGuStages;
-                    if (tid == 0) PTRACE(0, 0, it, 0);
-                    if (it >= kGuStages && !pf_wait_warp(&S.empty[s], ((it / kGuStages) - 1) & 1, abort)) { ok = false; break; }
-                    if (tid == 0) {
-                        PTRACE(0, 0, it, 1);
-                        mbar_expect_tx(&S.full[s], bbytes);
-                        bulk_g2s(S.b[s], bsrc + (size_t)(2 * sb + h) * kPfGuImageBytes, bbytes, &S.full[s]);
-                    }
-                    GuARaw &ar = h == 0 ? ar0 : ar1;
-                    if (q4) gu_a_q4k(ar, h, S.a[s], r);
-                    else gu_a_iq2s(ar, S.a[s], r);
-                    if (sb + 1 < nsb) gu_a_load(arow + (sb + 1) * bsz, h, q4, ar);   // two stages ahead
-                    if (tid == 0) PTRACE(0, 0, it, 2);
-                    fence_async_smem();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&S.full[s]);
-                }
-            }
-            if (!ok) break;
-        }
-    } else if (warp == kPfMmaWarp) {
-        // ------------------------------------------------ MMA issue (one thread)
-        if (lane == 0) {
-            int it = 0, sbc = 0;
-            const uint32_t sbo = kGuKc * 128;
-            for (int u = blockIdx.x; u < units && !*abort; u += gridDim.x) {
-                const PfTile tl = p.tiles[u / n_mb];
-                const bool q4 = p.gu[tl.cls].type == T_Q4_K;
-                const int N = (tl.n + 15) & ~15;
-                const uint32_t idesc = umma_idesc_f16(kPfM, N);
-                for (int sb = 0; sb < nsb && !*abort; ++sb, ++sbc) {
-                    const int b = sbc & 1;
-                    if (sbc >= 2 && !pf_wait(&S.accempty[b], ((sbc >> 1) & 1) ^ 1, abort)) break;
-                    tc_fence_after();
-                    const uint32_t dmain = tmem + (uint32_t)(b * 256), dmin = dmain + 128;
-                    for (int h = 0; h < 2; ++h, ++it) {
-                        const int s = it % kGuStages;
-                        PTRACE(0, 1, it, 0);
-                        if (!pf_wait(&S.full[s], (it / kGuStages) & 1, abort)) break;
-                        PTRACE(0, 1, it, 1);
-                        tc_fence_after();
-                        const uint32_t a0 = smem_addr(S.a[s]), b0 = smem_addr(S.b[s]);
-#pragma unroll
-                        for (int ks = 0; ks < 8; ++ks)
-                            umma_f16(dmain, umma_sdesc(a0 + ks * 256, 128, sbo), umma_sdesc(b0 + ks * 256, 128, sbo), idesc,
-                                     (h | ks) != 0);
-                        if (h == 0 && q4)
-                            umma_f16(dmin, umma_sdesc(a0 + 8 * 256, 128, sbo), umma_sdesc(b0 + 8 * 256, 128, sbo), idesc, 0);
-                        umma_commit(&S.empty[s]);
-                        PTRACE(0, 1, it, 2);
-                    }
-                    umma_commit(&S.accfull[b]);
-                }
-            }
-            umma_commit(&S.done);
-            mbar_wait(&S.done, 0);   // issued MMAs always complete; TMEM is freed only after them
-        }
-        __syncwarp();
-    } else {
-        // ------------------------------------------------ epilogue: promotion, GeGLU, Q8_0
-        const int ew = warp - kPfEpiWarp0, et = tid - kPfEpiWarp0 * 32;
-        const int q = warp & 3, ch = ew >> 2;
-        const int r = 32 * q + lane;
-        int sbc = 0, ucount = 0;
-        uint32_t eph = 0;
-        for (int u = blockIdx.x; u < units && !warp_aborted(abort); u += gridDim.x, ++ucount) {
-            const int ti = u / n_mb, mb = u - ti * n_mb;
-            const PfTile tl = p.tiles[ti];
-            const PoolView &pv = p.gu[tl.cls];
-            const bool q4 = pv.type == T_Q4_K;
-            const int rb = (int)row_bytes(pv.type, p.d);
-            const int N = (tl.n + 15) & ~15;
-            const int wr = r < 64 ? 64 * mb + r : p.nff + 64 * mb + (r - 64);
-            const uint8_t *arow = tile_rows(pv, tl.widx, gu_rows, p.d) + (size_t)wr * rb;
-            for (int i = et; i < nsb * kPfN; i += kPfEpiWarps * 32)
-                (&S.dxs[0][0])[i] = p.dxt[(size_t)ti * nsb * kPfN + i];
-            if (!epi_barrier(&S.epibar, eph, abort)) break;
-            if (et == 0) UTRACE(ucount, 0);
-            float acc[64];
-#pragma unroll
-            for (int i = 0; i < 64; ++i) acc[i] = 0.f;
-            for (int sb = 0; sb < nsb; ++sb, ++sbc) {
-                float dw, dmn = 0.f;
-                if (q4) {
-                    const uint32_t hd = *reinterpret_cast<const uint32_t *>(arow + sb * B_Q4_K);
-                    dw = h2f((uint16_t)(hd & 0xffffu));
-                    dmn = h2f((uint16_t)(hd >> 16));
-                } else {
-                    dw = 0.125f * h2f(*reinterpret_cast<const uint16_t *>(arow + sb * B_IQ2_S));
-                }
-                const int b = sbc & 1;
-                if (et == 0) PTRACE(0, 2, sbc, 0);
-                if (!pf_wait_warp(&S.accfull[b], (sbc >> 1) & 1, abort)) break;
-                if (et == 0) PTRACE(0, 2, sbc, 1);
-                tc_fence_after();
-                const uint32_t tb = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(b * 256);
-#pragma unroll
-                for (int cc = 0; cc < 4; ++cc) {
-                    const int col = 64 * ch + 16 * cc;
-                    if (col < N) {
-                        float vm[16], vn[16];
-                        if (q4) {
-                            tmem_ld16x2(tb + col, tb + 128 + col, vm, vn);
-#pragma unroll
-                            for (int i = 0; i < 16; ++i)
-                                acc[16 * cc + i] = fmaf(S.dxs[sb][col + i], fmaf(-dmn, vn[i], dw * vm[i]), acc[16 * cc + i]);
-                        } else {
-                            tmem_ld16(tb + col, vm);
-#pragma unroll
-                            for (int i = 0; i < 16; ++i)
-                                acc[16 * cc + i] = fmaf(S.dxs[sb][col + i], dw * vm[i], acc[16 * cc + i]);
-                        }
-                    }
-                }
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&S.accempty[b]);
-                if (et == 0) PTRACE(0, 2, sbc, 2);
-            }
-            if (warp_aborted(abort)) break;
-            if (et == 0) UTRACE(ucount, 1);
-            // the unit's 64 gate and 64 up rows for every pair of the tile, f32, slot order
-            // ([slot][2 n_ff]); lanes write consecutive rows
-            {
-                const int wr = r < 64 ? 64 * mb + r : p.nff + 64 * mb + (r - 64);
-                float *hb = p.hbuf + (size_t)tl.slot0 * 2 * p.nff + wr;
-#pragma unroll
-                for (int i = 0; i < 64; ++i)
-                    if (64 * ch + i < tl.n) hb[(size_t)(64 * ch + i) * 2 * p.nff] = acc[i];
-            }
-            if (et == 0) UTRACE(ucount, 3);
-            if (!epi_barrier(&S.epibar, eph, abort)) break;
-            if (et == 0) UTRACE(ucount, 4);
-        }
-    }
-    tc_fence_before();
-    __syncthreads();
-    if (warp == kPfMmaWarp) {
-        tc_fence_after();
-        tmem_dealloc_warp(tmem, 512);
-    }
 }
 
 // ---------------------------------------------------------------- down grouped GEMM
@@ -847,67 +534,6 @@ __global__ void __launch_bounds__(256) pf_geglu_kernel(PfParams p) {
             *reinterpret_cast<float4 *>(hp + nff) = u0;
             *reinterpret_cast<float4 *>(hp + nff + 4) = u1;
         }
-    }
-}
-
-// ---------------------------------------------------------------- gate_up B operand images
-// One CTA per (tile, super-block), thread = (tile row c, half h): the q8 values of the row's token
-// as fp16 in the canonical layout of a gate_up stage, the min-term columns [bsum_j >> 6 |
-// bsum_j & 63] in the first half, and the row's Q8_K scale. Rows n..N-1 (padding up to the
-// MMA's N) are zero. Each image is read by the tile's n_ff / 64 gate_up work units.
-__global__ void __launch_bounds__(256) pf_gather_kernel(PfParams p) {
-    pdl_wait();
-    pdl_launch_dependents();
-    const int ti = blockIdx.x, sb = blockIdx.y;
-    if (ti >= *p.n_tiles) return;
-    const PfTile tl = p.tiles[ti];
-    const int N = (tl.n + 15) & ~15, nsb = p.d / QK_K;
-    const int c = threadIdx.x >> 1, h = threadIdx.x & 1;
-    if (c >= N) return;
-    uint8_t *img = p.bimg + ((size_t)(ti * nsb + sb) * 2 + h) * kPfGuImageBytes;
-    float *dxt = p.dxt + ((size_t)ti * nsb + sb) * kPfN;
-    if (c >= tl.n) {
-        const uint4 z = make_uint4(0u, 0u, 0u, 0u);
-#pragma unroll
-        for (int col = 0; col < kGuKc; ++col) *reinterpret_cast<uint4 *>(img + canon_off(c, col, kGuKc)) = z;
-        if (h == 0) dxt[c] = 0.f;
-        return;
-    }
-    const int t = p.perm[tl.slot0 + c] / p.k;
-    const int8_t *q8 = p.xq8 + (size_t)t * p.d + sb * QK_K + h * 128;
-    uint4 v[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = __ldg(reinterpret_cast<const uint4 *>(q8 + 16 * i));
-    uint4 b0 = make_uint4(0u, 0u, 0u, 0u), b1 = b0;
-    const int16_t *bs16 = p.xbs + ((size_t)t * nsb + sb) * 16;
-    if (h == 0) {
-        b0 = __ldg(reinterpret_cast<const uint4 *>(bs16));
-        b1 = __ldg(reinterpret_cast<const uint4 *>(bs16 + 8));
-        dxt[c] = p.xd[(size_t)t * nsb + sb];
-    }
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        uint32_t o0, o1, o2, o3;
-        s8x4_h(v[i].x, o0, o1);
-        s8x4_h(v[i].y, o2, o3);
-        *reinterpret_cast<uint4 *>(img + canon_off(c, 2 * i, kGuKc)) = make_uint4(o0, o1, o2, o3);
-        s8x4_h(v[i].z, o0, o1);
-        s8x4_h(v[i].w, o2, o3);
-        *reinterpret_cast<uint4 *>(img + canon_off(c, 2 * i + 1, kGuKc)) = make_uint4(o0, o1, o2, o3);
-    }
-    if (h == 0) {
-        const uint32_t w[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
-        int hi[8], lo[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const int sm = (int)(int16_t)(w[j] & 0xffffu) + (int)(int16_t)(w[j] >> 16);   // bsums 2j, 2j+1
-            hi[j] = sm >> 6;     // floor division: sm = 64 * hi + lo, lo in [0, 63]
-            lo[j] = sm & 63;
-        }
-        *reinterpret_cast<uint4 *>(img + canon_off(c, 16, kGuKc)) =
-            make_uint4(pack_h2i(hi[0], hi[1]), pack_h2i(hi[2], hi[3]), pack_h2i(hi[4], hi[5]), pack_h2i(hi[6], hi[7]));
-        *reinterpret_cast<uint4 *>(img + canon_off(c, 17, kGuKc)) =
-            make_uint4(pack_h2i(lo[0], lo[1]), pack_h2i(lo[2], lo[3]), pack_h2i(lo[4], lo[5]), pack_h2i(lo[6], lo[7]));
     }
 }
 
