@@ -32,7 +32,7 @@ namespace moeb {
 constexpr int kLxN = 64;                    // pairs per work unit (MMA N <= 64)
 constexpr int kLxMainCores = 8;             // K = 64 per main pass step (2 lanes x 32), in 8-value cores
 constexpr int kLxBStageBytes = (kLxN / 8) * kLxMainCores * 128;   // 8 KB: one unit's half of a main image
-constexpr int kLxEpiWarps = 8;              // two per TMEM lane quadrant, 32 columns each
+constexpr int kLxEpiWarps = 16;             // four per TMEM lane quadrant, 16 columns each
 constexpr int kLxEpiCols = kLxN / (kLxEpiWarps / 4);
 constexpr int kLxConvGroups = 2;            // converter groups of four warps (one per TMEM lane quadrant),
 constexpr int kLxConvWarps = 4 * kLxConvGroups;   // group g converting steps g, g + groups, ...
@@ -721,24 +721,23 @@ __global__ void __launch_bounds__(kLxThreads, 1) pf_gate_up_lx_kernel(PfParams p
                         const uint64_t xs2 = f2pack(xs, xs);
                         const uint32_t dcol = tl_lane + kLxColD + 128 * db + col0;
                         const float4 *yd = reinterpret_cast<const float4 *>(&S.dxs[sb][col0]);
+                        // the warp's 16 columns of both lanes in one TMEM round trip
+                        static_assert(kLxEpiCols == 16, "one x16 load per lane");
+                        uint32_t sa[16], sbv[16];
+                        tmem_ld16x2u(dcol, dcol + 64, sa, sbv);
+                        if (et == 0) XTRACE(it, 15);
 #pragma unroll
-                        for (int hh = 0; hh < kLxEpiCols / 8; ++hh) {
-                            uint32_t sa[8], sbv[8];
-                            tmem_ld8x2u(dcol + 8 * hh, dcol + 64 + 8 * hh, sa, sbv);
-                            if (et == 0 && hh == 0) XTRACE(it, 15);
-#pragma unroll
-                            for (int i = 0; i < 2; ++i) {
-                                const float4 y4 = yd[2 * hh + i];
-                                // d = d_x * d_w rounded to f32 (for the min lanes -d_x * dmin_w)
-                                const uint64_t d01 = mul2(f2pack(y4.x, y4.y), xs2), d23 = mul2(f2pack(y4.z, y4.w), xs2);
-                                const int k0 = 4 * hh + 2 * i;
-                                accA[k0] = fma2(d01, f2pack(__uint_as_float(sa[4 * i]), __uint_as_float(sa[4 * i + 1])), accA[k0]);
-                                accB[k0] = fma2(d01, f2pack(__uint_as_float(sbv[4 * i]), __uint_as_float(sbv[4 * i + 1])), accB[k0]);
-                                accA[k0 + 1] = fma2(d23, f2pack(__uint_as_float(sa[4 * i + 2]), __uint_as_float(sa[4 * i + 3])),
-                                                    accA[k0 + 1]);
-                                accB[k0 + 1] = fma2(d23, f2pack(__uint_as_float(sbv[4 * i + 2]), __uint_as_float(sbv[4 * i + 3])),
-                                                    accB[k0 + 1]);
-                            }
+                        for (int i = 0; i < 4; ++i) {
+                            const float4 y4 = yd[i];
+                            // d = d_x * d_w rounded to f32
+                            const uint64_t d01 = mul2(f2pack(y4.x, y4.y), xs2), d23 = mul2(f2pack(y4.z, y4.w), xs2);
+                            const int k0 = 2 * i;
+                            accA[k0] = fma2(d01, f2pack(__uint_as_float(sa[4 * i]), __uint_as_float(sa[4 * i + 1])), accA[k0]);
+                            accB[k0] = fma2(d01, f2pack(__uint_as_float(sbv[4 * i]), __uint_as_float(sbv[4 * i + 1])), accB[k0]);
+                            accA[k0 + 1] = fma2(d23, f2pack(__uint_as_float(sa[4 * i + 2]), __uint_as_float(sa[4 * i + 3])),
+                                                accA[k0 + 1]);
+                            accB[k0 + 1] = fma2(d23, f2pack(__uint_as_float(sbv[4 * i + 2]), __uint_as_float(sbv[4 * i + 3])),
+                                                accB[k0 + 1]);
                         }
                     }
                     tc_fence_before();
