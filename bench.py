@@ -381,12 +381,13 @@ def run_ep(args, cfg, tokens_per_rank=None):
                     ep(x)
             torch.cuda.current_stream(dev).wait_stream(cap)
             torch.cuda.synchronize()
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g):
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
                 ep(x)
             torch.cuda.synchronize()
-            graph, graph_note = g, "one CUDA graph per step (NCCL all-to-alls captured)"
+            graph_note = "one CUDA graph per step (NCCL all-to-alls captured)"
         except RuntimeError as e:   # capture refused: time the eager step instead
+            graph = None            # (the only reference: a graph holding NCCL calls must not outlive the group)
             graph_note = f"eager launches (graph capture failed: {str(e)[:120]})"
         dist.barrier()
     step = graph.replay if graph is not None else (lambda: ep(x))
@@ -433,7 +434,10 @@ def run_ep(args, cfg, tokens_per_rank=None):
     tot = torch.tensor([dev_ms, comp_ms, e2e_ms], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(tot, op=dist.ReduceOp.MAX)
-    del step, graph   # a graph holding NCCL calls is released before the process group goes
+    # every reference to a graph holding NCCL calls goes before the process group does (else the exit
+    # waits for good)
+    del step, graph
+    torch.cuda.synchronize()
     dev_ms, comp_ms, e2e_ms = tot.tolist()
     hbm, tflops_peak, peak_kind = measured_peaks()
     avg_ms = dev_ms / args.steps

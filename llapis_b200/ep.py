@@ -108,7 +108,9 @@ def presence(ids: torch.Tensor, n_expert: int, world: int):
     T, k = ids.shape
     dest = owner(ids.long(), n_expert, world)                                  # [T, k]
     present = torch.zeros((world, T), dtype=torch.bool, device=ids.device)
-    present[dest.t().reshape(-1), torch.arange(T, device=ids.device).repeat(k)] = True
+    # the value as a device tensor: a Python scalar would be copied from the host (not capturable)
+    present.index_put_((dest.t().reshape(-1), torch.arange(T, device=ids.device).repeat(k)),
+                       torch.ones((), dtype=torch.bool, device=ids.device))
     return dest, present, present.sum(dim=1)
 
 
