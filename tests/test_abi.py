@@ -154,3 +154,45 @@ def test_host_q8_0_weight_quantiser_matches_reference(ref):
     ours = np.zeros(5 * rs, np.uint8)
     assert capi.lib().moeb_quantize_weights(capi.Q8_0, w.ctypes.data, ours.ctypes.data, 5, 128, 1) == 5 * rs
     assert np.array_equal(ours, ref.quantize(capi.Q8_0, w).reshape(-1))
+
+
+def test_layer_path_and_new_entries_validate_without_device(lib):
+    """moeb_layer_path picks the prefill kernels for every batch size of a layer whose decode kernel
+    does not fit (the dense MLP's 2112-wide inner dimension) and refuses bad layers; the block,
+    rms_norm and Q8_K routed entries reject bad arguments before any device work."""
+    from llapis_b200 import capi, workload
+    dense = workload.build_dense_layer()
+    L = capi.Layer()
+    L.d_model, L.n_ff, L.n_expert, L.top_k = dense.d_model, dense.n_ff, dense.n_expert, dense.top_k
+    dummy = C.c_void_p(256)   # never dereferenced: the path query reads only the shape and pointers' presence
+    L.w_router = dummy
+    L.hot = capi.Pool(capi.Q4_K, capi.Q5_0, 1, 0, dummy, dummy, None)
+    L.exp_slot = L.slot_exp = L.slot_state = dummy
+    assert lib.moeb_layer_path(C.byref(L), 1) == 1 and lib.moeb_layer_path(C.byref(L), 4096) == 1
+    M = capi.Layer.from_buffer_copy(L)
+    M.n_ff = 704
+    prev = lib.moeb_set_prefill_min_tokens(0)
+    assert lib.moeb_layer_path(C.byref(M), 1) == 0 and lib.moeb_layer_path(C.byref(M), max(prev, 1)) == 1
+    M.n_ff = 8192                          # neither kernel family covers it
+    assert lib.moeb_layer_path(C.byref(M), 1) == -1
+    assert lib.moeb_layer_path(None, 1) == -1
+    # the feed-forward block: shapes must agree and the dense MLP must be a one-expert layer
+    B = capi.Layer.from_buffer_copy(L)
+    B.d_model = 512
+    ws = C.c_void_p(4096)
+    assert lib.moeb_ffn_block_gemma4(C.byref(L), None, C.byref(B), None, None, 4, None, ws, 1 << 30, None, None) == -1
+    assert "d_model" in lib.moeb_last_error().decode()
+    assert lib.moeb_ffn_block_gemma4(C.byref(L), None, C.byref(L), None, None, 4, None, None, 0, None, None) == -1
+    assert "workspace" in lib.moeb_last_error().decode()
+    E = capi.Layer.from_buffer_copy(L)
+    E.top_k = 2
+    assert lib.moeb_ffn_block_gemma4(C.byref(L), None, C.byref(E), None, None, 4, None, ws, 1 << 30, None, None) == -1
+    assert "one-expert" in lib.moeb_last_error().decode()
+    assert lib.moeb_ffn_block_workspace_size(C.byref(L), C.byref(L), 64) > 64 * 2816 * 4
+    # rms_norm: row width a multiple of 4, aligned pointers, eps >= 0
+    assert lib.moeb_rms_norm(None, 2, 6, None, 1.0, 1e-6, None, None) == -1
+    assert lib.moeb_rms_norm(C.c_void_p(17), 2, 8, None, 1.0, 1e-6, C.c_void_p(32), None) == -1
+    assert lib.moeb_rms_norm(C.c_void_p(16), 2, 8, None, 1.0, -1.0, C.c_void_p(32), None) == -1
+    assert lib.moeb_rms_norm(None, 0, 8, None, 1.0, 1e-6, None, None) == 0      # nothing to do
+    # Q8_K routed half: null rows refused
+    assert lib.moeb_layer_forward_routed_q8k(C.byref(L), None, 4, None, None, None, None, 0, None) == -1
