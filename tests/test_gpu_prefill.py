@@ -199,3 +199,30 @@ def test_prefill_zero_and_small_batches(prefill_from, gemm, port, kind):
         out, _, _ = run_layer(host, x, aux_names=())
         assert_layer_close(out, port.moe_layer(spec_of(host, x))["out"], tol=TOL)
     torch.cuda.synchronize()
+
+
+@pytest.mark.parametrize("path", ["decode", "tcgen05", "mid"])
+def test_per_expert_down_scales_both_classes(port, prefill_from, gemm, path):
+    """Non-unit per-expert down scales in BOTH precision classes (ffn_down_exps.scale of the hot
+    slots and of the cold experts), on every path: applied once to each pair's down row before the
+    weighted combine, as the reference's ggml_mul by the scale does."""
+    import dataclasses
+    prefill_from(1 << 30 if path == "decode" else 1)
+    gemm("mid" if path == "mid" else "tcgen05")
+    base = host_layer("mini_mixed")
+    rng = np.random.default_rng(31)
+    h = dataclasses.replace(base, s_hot=rng.uniform(0.5, 2.0, base.n_slots).astype(np.float32),
+                            s_cold=rng.uniform(0.5, 2.0, base.n_expert).astype(np.float32))
+    x = workload.make_input(workload.CONFIGS["mini_mixed"], n_tokens=96, stream=41)
+    out, aux, layer = run_layer(h, x, aux_names=("ids", "gate_up"))
+    assert layer.prefill_path(96) == (path != "decode")
+    want = port.moe_layer(spec_of(h, x), n_threads=8, want=("ids", "gate_up"))
+    same = np.all(aux["ids"] == want["ids"], axis=1)
+    assert same.mean() > 0.95
+    k = h.top_k
+    pairs = (np.nonzero(same)[0][:, None] * k + np.arange(k)[None, :]).reshape(-1)
+    assert np.array_equal(aux["gate_up"][pairs].view(np.uint32), want["gate_up"][pairs].view(np.uint32))
+    cold_routed = ~np.isin(aux["ids"], h.hot_ids)
+    assert cold_routed.any() and (~cold_routed).any(), "both classes must be routed"
+    rel = assert_layer_close(out[same], want["out"][same], tol=TOL)
+    print(f"{path}: down scales in both classes, max-abs / rms {rel:.2e}")
