@@ -357,10 +357,11 @@ __global__ void __launch_bounds__(256) pf_gather_lx_kernel(PfParams p) {
 // the dot adds last. This kernel computes M for every (row, pair) of the Q4_K tiles and stores it in
 // hbuf, where the grouped GEMM's epilogue adds the main lanes' sum to it.
 //
-// The integers come from mma.sync m16n8k16 (fp16 operands, f32 accumulators, all exact): A row r holds
-// mins[j] twice at K = 2j, 2j + 1 (j < 8), B column c of group m holds bsums 4m..4m+3 at K = 4m..4m+3 and
-// zeros elsewhere, so one MMA per group gives lane m's integer for a 16 x 8 block, and the chains stay
-// in registers. CTA = (tile, 128 rows), eight warps of 16 rows; the tile's bsums (fp16 pairs, written
+// The integers come from mma.sync m16n8k8 (fp16 operands, f32 accumulators, all exact) with the
+// lanes in M: for a weight row, M-row g holds lane 0 (2) and M-row g + 8 lane 1 (3) of the low (high)
+// half of the 16 bsums; lane m's two mins sit twice each at the K of its four bsums and zeros
+// elsewhere, B column c is the pair's eight bsums of that half, so two MMAs give all four lane
+// integers of 8 rows x 8 pairs and every (row, pair) chain stays in one thread's registers. CTA = (tile, 128 rows), eight warps of 16 rows; the tile's bsums (fp16 pairs, written
 // by pf_gather_lx_kernel) and scales are staged once, then 32-pair chunks (four n-blocks) run.
 // (A packed-f32 CUDA-core formulation of the same integers measured slower here: its operand tables
 // make it shared-memory bound.)
@@ -368,12 +369,10 @@ constexpr int kMinRows = 128, kMinCols = 32, kMinThreads = 256;
 // dynamic shared memory: per super-block the tile's bsums [128][8] + scales [128] and the CTA rows'
 // mins [128] (uint2) + -dmin_w [128]
 MOEB_HD constexpr size_t min_smem_bytes(int nsb) { return (size_t)nsb * (kPfN * 36 + kMinRows * 12); }
-__device__ __forceinline__ void mma_f16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                              uint32_t b0, uint32_t b1) {
-    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-                 "{%10,%10,%10,%10};"
+__device__ __forceinline__ void mma_f16_1688(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
+    asm volatile("mma.sync.aligned.m16n8k8.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%7,%7,%7,%7};"
                  : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
-                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.f));
+                 : "r"(a0), "r"(a1), "r"(b0), "f"(0.f));
 }
 
 __global__ void __launch_bounds__(kMinThreads) pf_q4k_min_kernel(PfParams p) {
@@ -431,27 +430,42 @@ __global__ void __launch_bounds__(kMinThreads) pf_q4k_min_kernel(PfParams p) {
         for (int sb = 0; sb < nsb; ++sb) {
             const uint2 ma = s_mins[sb][ra], mb = s_mins[sb][rbw];
             const uint32_t wa[2] = {ma.x, ma.y}, wb[2] = {mb.x, mb.y};
-            // A: row g K 2t4, 2t4+1 = mins[t4]; K 2t4+8, 2t4+9 = mins[t4+4] (rows g + 8 likewise)
-            const uint32_t a0 = h2u(byte_h2(wa, t4)), a1 = h2u(byte_h2(wb, t4));
-            const uint32_t a2 = h2u(byte_h2(wa, t4 + 4)), a3 = h2u(byte_h2(wb, t4 + 4));
+            // m16n8k8 with the lanes in M: for weight row r, M-row g holds lane 2h (low MMA, bsums 0..7)
+            // or lane 2h + 2 (high MMA, bsums 8..15) and M-row g + 8 the next lane; lane m's two mins
+            // sit at the K of its four bsums (each min twice), zeros elsewhere, so B needs no mask
+            const uint32_t vla = h2u(byte_h2(wa, t4)), vha = h2u(byte_h2(wa, t4 + 4));
+            const uint32_t vlb = h2u(byte_h2(wb, t4)), vhb = h2u(byte_h2(wb, t4 + 4));
+            const uint32_t la0 = lo ? vla : 0u, la1 = lo ? 0u : vla, ha0 = lo ? vha : 0u, ha1 = lo ? 0u : vha;
+            const uint32_t lb0 = lo ? vlb : 0u, lb1 = lo ? 0u : vlb, hb0 = lo ? vhb : 0u, hb1 = lo ? 0u : vhb;
             const float nda = s_ndmin[sb][ra], ndb = s_ndmin[sb][rbw];
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
                 const int cb = c0 + 8 * j;
-                // B: column g of n-block j, K 2t4, 2t4+1 (bsums 2t4, 2t4+1) and K 2t4+8, 2t4+9; group m
-                // keeps only its K range 4m..4m+3
+                // B: column g of n-block j, K 2t4, 2t4+1 = bsums 2t4, 2t4+1 (low) or 8 + 2t4, 9 + 2t4 (high)
                 const uint32_t p0 = s_bs[sb][cb + g][t4], p1 = s_bs[sb][cb + g][t4 + 4];
                 const float2 dx = *reinterpret_cast<const float2 *>(&s_dx[sb][cb + 2 * t4]);
                 // dmin = -d_x * dmin_w per (row, pair), rounded to f32
                 const float dm[4] = {__fmul_rn(dx.x, nda), __fmul_rn(dx.y, nda), __fmul_rn(dx.x, ndb), __fmul_rn(dx.y, ndb)};
+                float dl[4], dh[4];
+                // row ra: lanes 0, 1 (low) and 2, 3 (high); fragment rows g / g + 8 = the two lanes
+                mma_f16_1688(dl, la0, la1, p0);
+                mma_f16_1688(dh, ha0, ha1, p1);
 #pragma unroll
-                for (int m = 0; m < 4; ++m) {
-                    const uint32_t b0 = m < 2 && (lo == (m == 0)) ? p0 : 0u;
-                    const uint32_t b1 = m >= 2 && (lo == (m == 2)) ? p1 : 0u;
-                    float dd[4];
-                    mma_f16_16816(dd, a0, a1, a2, a3, b0, b1);
+                for (int q = 0; q < 2; ++q) {
+                    acc[j][0][q] = __fmaf_rn(dm[q], dl[q], acc[j][0][q]);
+                    acc[j][1][q] = __fmaf_rn(dm[q], dl[2 + q], acc[j][1][q]);
+                    acc[j][2][q] = __fmaf_rn(dm[q], dh[q], acc[j][2][q]);
+                    acc[j][3][q] = __fmaf_rn(dm[q], dh[2 + q], acc[j][3][q]);
+                }
+                // row rbw
+                mma_f16_1688(dl, lb0, lb1, p0);
+                mma_f16_1688(dh, hb0, hb1, p1);
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) acc[j][m][e] = __fmaf_rn(dm[e], dd[e], acc[j][m][e]);
+                for (int q = 0; q < 2; ++q) {
+                    acc[j][0][2 + q] = __fmaf_rn(dm[2 + q], dl[q], acc[j][0][2 + q]);
+                    acc[j][1][2 + q] = __fmaf_rn(dm[2 + q], dl[2 + q], acc[j][1][2 + q]);
+                    acc[j][2][2 + q] = __fmaf_rn(dm[2 + q], dh[q], acc[j][2][2 + q]);
+                    acc[j][3][2 + q] = __fmaf_rn(dm[2 + q], dh[2 + q], acc[j][3][2 + q]);
                 }
             }
         }
