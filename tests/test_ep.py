@@ -188,3 +188,37 @@ def test_ep_departed_rank_detected_on_host(announce):
     elapsed = float(status.split()[1])
     assert elapsed < (1.0 if announce else 10.0), status
     assert ("left" in status) if announce else ("did not reach step 1" in status), status
+
+
+def _hb_worker(rank, world, port, q):
+    """Five heartbeats on both ranks: every step's records exist while it runs, and each rank
+    deletes its records older than two steps (the store does not grow with the step count)."""
+    from datetime import timedelta
+
+    from llapis_b200.ep import Heartbeat
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    store = dist.distributed_c10d._get_default_store()
+    hb = Heartbeat(store, rank, world, deadline_s=10.0, prefix="hbtest")
+    for step in range(5):
+        hb.beat(step)
+    dist.barrier()
+    kept = [s for s in range(5) if store.check([f"hbtest/s{s}/r{rank}"])]
+    q.put((rank, kept))
+    q.close()
+    q.join_thread()
+    dist.destroy_process_group()
+
+
+def test_heartbeat_keeps_the_store_bounded():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_hb_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in range(2))
+    for p in procs:
+        p.join(timeout=60)
+    assert res[0] == [3, 4] and res[1] == [3, 4], res
